@@ -1,0 +1,348 @@
+"""Benchmark of the fast-memory path at the 110M shape.
+
+One step = the fast-memory operator forward + backward (unified_memory, kernel.py:199-238 of the
+reference) for every one of the 12 UnifiedBlocks, on 16 sequences x 1024 tokens per GPU
+(dim D=768, slots M=2048), followed at N>1 by the data-parallel all-reduce of the operator's
+parameter gradients (dw, dg of every block) over NCCL. Inputs are seeded synthetic relu^2-normalised
+addresses r and Gaussian values v, resident in HBM and larger than L2 (r alone is 134 MB), so no L2
+flush is needed between steps. Metric: tokens per second through all 12 blocks, whole job.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--precision bf16|fp32]
+
+Under torchrun each rank drives one GPU; the step time is the max over ranks of the CUDA-event time.
+`--impl reference` times the reference's CPU algorithm (the chunked pure-PyTorch form of
+test_all.py:28-51, restated in oracle/memory.py) on this host's cores.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from __graft_entry__ import load_package  # noqa: E402
+
+WORKLOAD = dict(B=16, T=1024, M=2048, D=768, L=12, lam=0.95, prior=4.0)
+METRIC = "fast-memory fwd+bwd tokens/s (110M shape)"
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def peaks():
+    try:
+        p = json.load(open(PEAKS_FILE))
+        return {"bf16_tflops": p["bf16_tflops"], "hbm_gbs": p["hbm_gbs"], "source": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def make_inputs(B, T, M, D, lam, prior, device, seed=0):
+    gen = torch.Generator(device=device).manual_seed(seed)
+    a = torch.randn(B, T, M, device=device, generator=gen) + 0.3
+    a.relu_().square_()
+    r = a / (1.0 + a.sum(-1, keepdim=True))
+    del a
+    v = torch.randn(B, T, D, device=device, generator=gen)
+    g = torch.tensor(float(torch.log(torch.tensor(lam))), device=device)
+    w = torch.full((M,), prior, device=device)
+    dq_out = torch.randn(B, T, M, device=device, generator=gen) * 1e-3
+    dfast = torch.randn(B, T, D, device=device, generator=gen) * 1e-3
+    return r, v, g, w, dq_out, dfast
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(parts)
+            except Exception:
+                pass
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(p[1]) for p in rows if p[1].replace(".", "").isdigit()]
+        mx = [float(p[2]) for p in rows if p[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for p in rows for n, val in zip(names, p[5:9]) if val.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_seconds(T, M, D, lam, prior, reps, threads):
+    """Seconds for one sequence x one block of the reference's chunked CPU form, fwd + bwd, fp32."""
+    from oracle import memory as O
+    torch.set_num_threads(threads)
+    g_ = torch.Generator().manual_seed(0)
+    a = torch.randn(1, T, M, generator=g_) + 0.3
+    z = torch.relu(a).square()
+    r = z / (1.0 + z.sum(-1, keepdim=True))
+    v = torch.randn(1, T, D, generator=g_)
+    g = torch.tensor(float(torch.log(torch.tensor(lam))))
+    w = torch.full((M,), prior)
+    dq_out = torch.randn(1, T, M, generator=g_)
+    dfast = torch.randn(1, T, D, generator=g_)
+    O.memory_grads(r, v, g, w, dq_out, dfast, form="chunked", chunk=64)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.memory_grads(r, v, g, w, dq_out, dfast, form="chunked", chunk=64)
+    return (time.perf_counter() - t0) / reps
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    W = WORKLOAD
+    threads = os.cpu_count() or 1
+    reps = 1
+    # warm-up W samples, then K timed samples; one sample = 1 sequence through 1 block
+    for _ in range(max(args.warmup, 0)):
+        cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 1, threads)
+    secs = [cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], reps, threads)
+            for _ in range(args.steps)]
+    per_sample = statistics.median(secs)
+    value = W["T"] / (W["L"] * per_sample)
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per_sample * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "unified_memory fwd+bwd, 1 sequence x 1 block per sample, scaled to 12 blocks",
+                       "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"]},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, "
+                                       "chunked pure-PyTorch form (test_all.py:28-51 restated), fp32"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def timed_products(ulm_lib, L_, tensors, W, prec):
+    """CUDA-event time of each tensor-core product launch of one block's fwd+bwd (the dominant
+    kernel family), with its algorithmic flops. Returns (flops, seconds) summed over launches."""
+    B, T, M, D = W["B"], W["T"], W["M"], W["D"]
+    qop, kop, vop, P, doop, dS, dqf, dk, dv, fast, g = tensors
+    ldm, ldd, ldt = L_.lib().ulm_operand_ld(M), L_.lib().ulm_operand_ld(D), L_.lib().ulm_operand_ld(T)
+    st = torch.cuda.current_stream()
+    sp = L_.stream_of(qop)
+    pairs = T * (T + 1) // 2  # (t, s) pairs with s <= t
+    lib = L_.lib()
+    calls = [
+        (2 * B * pairs * M, lambda: lib.ulm_decayed_scores(L_.ptr(qop), ldm, L_.ptr(kop), ldm, L_.ptr(P), ldt,
+                                                           L_.ptr(g), B, T, M, prec, sp)),
+        (2 * B * pairs * D, lambda: lib.ulm_causal_apply(L_.ptr(P), ldt, L_.ptr(vop), ldd, L_.ptr(fast), D,
+                                                         L_.ULM_F32, 0, B, T, D, prec, sp)),
+        (2 * B * pairs * D, lambda: lib.ulm_decayed_scores(L_.ptr(doop), ldd, L_.ptr(vop), ldd, L_.ptr(dS), ldt,
+                                                           L_.ptr(g), B, T, D, prec, sp)),
+        (2 * B * pairs * M, lambda: lib.ulm_causal_apply(L_.ptr(dS), ldt, L_.ptr(kop), ldm, L_.ptr(dqf), M,
+                                                         L_.ULM_F32, 0, B, T, M, prec, sp)),
+        (2 * B * pairs * M, lambda: lib.ulm_causal_apply(L_.ptr(dS), ldt, L_.ptr(qop), ldm, L_.ptr(dk), M,
+                                                         L_.ULM_F32, 1, B, T, M, prec, sp)),
+        (2 * B * pairs * D, lambda: lib.ulm_causal_apply(L_.ptr(P), ldt, L_.ptr(doop), ldd, L_.ptr(dv), D,
+                                                         L_.ULM_F32, 1, B, T, D, prec, sp)),
+    ]
+    flops, secs = 0, 0.0
+    per = []
+    for fl, fn in calls:
+        L_.check(fn())  # warm
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        reps = 5
+        torch.cuda.synchronize()
+        ev[0].record(st)
+        for _ in range(reps):
+            L_.check(fn())
+        ev[1].record(st)
+        torch.cuda.synchronize()
+        s = ev[0].elapsed_time(ev[1]) / 1e3 / reps
+        per.append((fl, s))
+        flops += fl
+        secs += s
+    return flops, secs, per
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    load_package()
+    import unifiedlm_c_b200._lib as L_
+    from unifiedlm_c_b200.kernel import memory_fwd, memory_bwd, PRECISION
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    W = WORKLOAD
+    prec = PRECISION[args.precision]
+    r, v, g, w, dq_out, dfast = make_inputs(W["B"], W["T"], W["M"], W["D"], W["lam"], W["prior"], dev, seed=rank)
+    grads = torch.zeros(W["L"], W["M"] + 1, device=dev)
+
+    def step(r_, v_, dq_, df_):
+        for layer in range(W["L"]):
+            q, fast, c, qop, kop, vop, P = memory_fwd(r_, v_, g, w, prec)
+            dr, dv, dg, dw = memory_bwd(dq_, df_, r_, g, w, q, c, qop, kop, vop, P, prec)
+            grads[layer, :W["M"]] = dw
+            grads[layer, W["M"]] = dg
+        if world > 1:
+            dist.all_reduce(grads)
+        return grads
+
+    for _ in range(args.warmup):
+        step(r, v, dq_out, dfast)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(args.steps):
+            step(r, v, dq_out, dfast)
+        ev1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    secs = torch.tensor(ev0.elapsed_time(ev1) / 1e3, device=dev)
+    if world > 1:
+        dist.all_reduce(secs, op=dist.ReduceOp.MAX)
+    secs = float(secs)
+    tokens = world * W["B"] * W["T"] * args.steps
+    value = tokens / secs
+    if L_.device_error() != 0:
+        raise RuntimeError("a kernel reported a device-side error during the bench")
+
+    # e2e: inputs copied from pinned host memory every step, parameter gradients read back
+    host = [t.cpu().pin_memory() for t in (r, v, dq_out, dfast)]
+    dev_in = [torch.empty_like(t) for t in (r, v, dq_out, dfast)]
+    host_out = torch.empty(grads.shape, dtype=grads.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host):
+            d_.copy_(h_, non_blocking=True)
+        out = step(*dev_in)
+        host_out.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_secs = torch.tensor(e0.elapsed_time(e1) / 1e3, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_secs, op=dist.ReduceOp.MAX)
+    e2e_value = world * W["B"] * W["T"] * e2e_steps / float(e2e_secs)
+    del dev_in, host
+
+    # roofline of the dominant kernel family (tensor-core products), CUDA events per launch
+    q, fast, c, qop, kop, vop, P = memory_fwd(r, v, g, w, prec)
+    ldd, ldt = L_.lib().ulm_operand_ld(W["D"]), L_.lib().ulm_operand_ld(W["T"])
+    opt = qop.dtype
+    doop = torch.zeros(W["B"], W["T"], ldd, device=dev, dtype=opt)
+    doop[..., :W["D"]] = dfast.to(opt)
+    dS = torch.empty(W["B"], W["T"], ldt, device=dev, dtype=opt)
+    dqf = torch.empty(W["B"], W["T"], W["M"], device=dev)
+    dk = torch.empty_like(dqf)
+    dvb = torch.empty(W["B"], W["T"], W["D"], device=dev)
+    fast32 = torch.empty(W["B"], W["T"], W["D"], device=dev)
+    flops, psecs, per = timed_products(None, L_, (qop, kop, vop, P, doop, dS, dqf, dk, dvb, fast32, g), W, prec)
+    pk = peaks()
+    achieved = flops / psecs / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
+                "kernel": "tc_gemm_kernel (6 causal products per block fwd+bwd)",
+                "peak_source": pk["source"],
+                "per_launch_ms": [round(s * 1e3, 4) for _, s in per],
+                "per_launch_tflops": [round(f / s / 1e12, 1) for f, s in per]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        s = cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 2, threads)
+        cpu = {"value": W["T"] / (W["L"] * s), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd x2, chunked "
+                         "pure-PyTorch form (test_all.py:28-51 restated in oracle/memory.py), fp32, "
+                         "scaled to 12 blocks"}
+
+    # kernels of ours per step: per block fwd 4 (stats, convert, scores, read), bwd 7 (convert,
+    # scores, 3 reads, stats, finalize)
+    launches = args.steps * W["L"] * 11
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+            "config": {"workload": "unified_memory fwd+bwd x 12 blocks (110M shape), 16 seq x 1024 tok per GPU",
+                       "B_per_gpu": W["B"], "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"],
+                       "lam": W["lam"], "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (r is 134 MB), no flush"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

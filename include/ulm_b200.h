@@ -1,0 +1,135 @@
+/*
+ * ulm_b200.h - C ABI of the B200 (sm_100a) fast-memory library for UnifiedLM.
+ *
+ * Every entry point takes plain device pointers, element counts / strides in elements, and a
+ * CUDA stream passed as `void*` (NULL = legacy default stream). Work is enqueued on that stream
+ * and the call returns without synchronising. Outputs are written into caller-owned buffers;
+ * nothing here allocates device memory unless a comment says otherwise. The return value is a
+ * ulm_status; on failure `ulm_last_error()` returns a message for the calling thread.
+ *
+ * Tensors are row-major. "(B,T,M) ld" means element [b][t][m] lives at
+ * base + (b*T + t)*ld + m, with ld >= M. Scalars that the reference keeps on the device (the log
+ * decay g) are passed as device pointers so no call needs a host synchronisation.
+ *
+ * Reference interfaces replaced (file:line in ruhai-lin/unifiedlm.c):
+ *   kernel.py:199-238  UnifiedMemory / unified_memory      -> ulm_memory_fwd, ulm_memory_bwd
+ *   kernel.py:109-136  _fwd_stats_kernel                     -> ulm_memory_stats_fwd
+ *   kernel.py:139-180  _bwd_stats_kernel + shift-add (:232)  -> ulm_memory_stats_bwd
+ *   kernel.py:51-72    _la_attn_kernel (decayed chunk scores) -> ulm_decayed_scores
+ *   kernel.py:23-48,
+ *   kernel.py:75-101   _la_state / _la_out (apply scores)     -> ulm_causal_apply
+ */
+#ifndef ULM_B200_H
+#define ULM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+enum {
+  ULM_OK = 0,
+  ULM_ERR_INVALID = 1,     /* bad argument: shape, stride, alignment, null pointer, dtype */
+  ULM_ERR_CUDA = 2,        /* a CUDA runtime / driver call failed */
+  ULM_ERR_UNSUPPORTED = 3, /* the device is not sm_100 or a required driver entry point is missing */
+  ULM_ERR_DEVICE = 4       /* a kernel recorded a device-side error (see ulm_device_error) */
+};
+
+/* element types */
+enum { ULM_F32 = 0, ULM_BF16 = 1 };
+
+/* contraction precision of the chunk products:
+ *   ULM_PREC_BF16: bf16 operands on the tcgen05 tensor cores, fp32 accumulation (the reference's
+ *                  choice, kernel.py:205, 219);
+ *   ULM_PREC_FP32: fp32 operands and fp32 FMA accumulation (the 1e-5 parity mode). */
+enum { ULM_PREC_BF16 = 0, ULM_PREC_FP32 = 1 };
+
+/* ---- library ------------------------------------------------------------------------------ */
+
+/* Message describing the last failure on the calling thread ("" if none). */
+const char* ulm_last_error(void);
+
+/* ABI version of this library. */
+int ulm_version(void);
+
+/* Synchronises the current device, then reads and clears its device-side error flag: *site = 0
+ * when no kernel gave up a bounded wait, otherwise the site code of the first one. */
+int ulm_device_error(int* site);
+
+/* ---- fast-memory statistics (kernel.py:109-136, 139-180) ----------------------------------- */
+
+/* Forward slot statistics, per batch row b and slot a (lam = exp(*g)):
+ *   k_t = r_{t-1} (k_0 = 0),  c_t = w + sum_{s<=t} lam^(t-s) k_s,  q_t = r_t / c_t.
+ * r, q, c: (B,T,M) fp32 with row stride M. qop, kop: (B,T,M) copies of q and k in `op_dtype`
+ * (ULM_BF16 for the tensor-core products, ULM_F32 for the fp32 mode) with row stride ld_op >= M.
+ * w: (M,) fp32. g: device fp32 scalar. */
+int ulm_memory_stats_fwd(const float* r, const float* w, const float* g, float* q, float* c, void* qop,
+                         void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M,
+                         void* stream);
+
+/* Backward of the statistics, walking time in reverse. Inputs: dqf = gradient reaching q through
+ * the fast read, dq_out = gradient on the q output (may be NULL), dk = gradient reaching k through
+ * the fast read, and the saved q, c, r. Outputs:
+ *   dr  (B,T,M) fp32 : dq/c plus the shifted write-address gradient dk_total[t+1]
+ *   dw  (M,)    fp32 : sum over b,t of dc                          (overwritten, not accumulated)
+ *   dg  (1,)    fp32 : d/dg of the memory terms                    (overwritten)
+ * `partial` is caller-provided scratch of ulm_memory_stats_bwd_scratch(B,T,M) bytes.
+ * The sums over batch rows and positions run in a fixed order: results are deterministic. */
+int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
+                         const float* r, const float* w, const float* g, float* dr, float* dw, float* dg,
+                         void* partial, int64_t B, int64_t T, int64_t M, void* stream);
+
+int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M);
+
+/* ---- the chunk products -------------------------------------------------------------------- */
+
+/* Decayed causal scores over the whole sequence (the reference's intra-chunk matrix A_n,
+ * kernel.py:51-72, extended across chunks):
+ *   P[b][t][s] = lam^(t-s) * sum_k a[b][t][k] * bb[b][s][k]   for s <= t, and 0 for s > t
+ * a, bb: (B,T,K) with row strides lda, ldb; P: (B,T,T) with row stride ldp. Only the tiles on or
+ * below the diagonal are written (128 x 128 granularity in bf16 precision).
+ * prec = ULM_PREC_BF16: a, bb, P are bf16; lda, ldb, ldp multiples of 8; 16-byte aligned bases.
+ * prec = ULM_PREC_FP32: a, bb, P are fp32. */
+int ulm_decayed_scores(const void* a, int64_t lda, const void* bb, int64_t ldb, void* P, int64_t ldp,
+                       const float* g, int64_t B, int64_t T, int64_t K, int prec, void* stream);
+
+/* Apply decayed scores to values (the products of kernel.py:75-101):
+ *   transpose = 0 : o[b][t][v] = sum_{s<=t} P[b][t][s] * c[b][s][v]     (forward read)
+ *   transpose = 1 : o[b][s][v] = sum_{t>=s} P[b][t][s] * c[b][t][v]     (time-reversed read)
+ * P: (B,T,T) ldp; c: (B,T,V) ldc; o: (B,T,V) ldo with element type o_dtype (ULM_F32 / ULM_BF16).
+ * Operand types and alignment follow `prec` as in ulm_decayed_scores. */
+int ulm_causal_apply(const void* P, int64_t ldp, const void* c, int64_t ldc, void* o, int64_t ldo, int o_dtype,
+                     int transpose, int64_t B, int64_t T, int64_t V, int prec, void* stream);
+
+/* ---- the whole operator (kernel.py:199-238) ---------------------------------------------------- */
+
+/* Padded row stride used for the operand copies of a length-n row (multiple of 8 elements). */
+int64_t ulm_operand_ld(int64_t n);
+
+/* Forward of unified_memory(r, v, g, w) -> (q, fast).
+ * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
+ * Outputs: q (B,T,M) fp32; fast (B,T,D) of type v_dtype.
+ * Saved for the backward (caller-owned, element type = ULM_BF16 for ULM_PREC_BF16, ULM_F32 for
+ * ULM_PREC_FP32): c (B,T,M) fp32; qop, kop (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D));
+ * P (B,T,ulm_operand_ld(T)). */
+int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const float* g, const float* w, float* q,
+                   void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
+                   int64_t M, int64_t D, int prec, void* stream);
+
+/* Backward of unified_memory. dq_out may be NULL; dfast (B,T,D) of type do_dtype. Workspace
+ * buffers (caller-owned): doop (B,T,ulm_operand_ld(D)) and dS (B,T,ulm_operand_ld(T)) in the
+ * operand type, dqf and dk (B,T,M) fp32, `partial` of ulm_memory_stats_bwd_scratch bytes.
+ * Outputs: dr (B,T,M) fp32, dv (B,T,D) of type do_dtype, dg (1,) fp32, dw (M,) fp32. */
+int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* g,
+                   const float* w, const float* q, const float* c, const void* qop, const void* kop,
+                   const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
+                   float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T, int64_t M, int64_t D,
+                   int prec, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ULM_B200_H */

@@ -1,0 +1,94 @@
+"""The C ABI without a GPU: the library loads, exports every symbol include/ulm_b200.h declares,
+the Python binding covers them, and argument validation fails with a message before any device
+work. Also the model.bin v1 format round trip."""
+import ctypes
+import os
+import re
+import struct
+
+import pytest
+import torch
+
+import unifiedlm_c_b200._lib as L
+from unifiedlm_c_b200 import export
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ulm_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ulm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_functions():
+    names = declared_functions()
+    assert "ulm_memory_fwd" in names and "ulm_memory_bwd" in names and len(names) >= 10
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(L.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert sorted(L.SIGNATURES) == declared_functions()
+
+
+def test_version_and_helpers():
+    lib = L.lib()
+    assert lib.ulm_version() >= 1
+    assert lib.ulm_operand_ld(13) == 16 and lib.ulm_operand_ld(64) == 64
+    assert lib.ulm_memory_stats_bwd_scratch(2, 100, 70) >= 2 * 70 * 4 + 2 * 3 * 8
+
+
+def test_validation_rejects_bad_arguments_without_device_work():
+    lib = L.lib()
+    dummy = ctypes.c_void_p(16)
+    # bad precision code
+    rc = lib.ulm_decayed_scores(dummy, 64, dummy, 64, dummy, 64, dummy, 1, 64, 64, 7, None)
+    assert rc == L.ULM_ERR_INVALID and b"prec" in lib.ulm_last_error()
+    # row stride shorter than the row
+    rc = lib.ulm_memory_stats_fwd(dummy, dummy, dummy, dummy, dummy, dummy, dummy, L.ULM_BF16, 8, 1, 4, 16, None)
+    assert rc == L.ULM_ERR_INVALID and b"ld_op" in lib.ulm_last_error()
+    # null pointers
+    rc = lib.ulm_memory_fwd(None, None, L.ULM_F32, None, None, None, None, None, None, None, None, None,
+                            1, 4, 8, 8, L.ULM_PREC_BF16, None)
+    assert rc == L.ULM_ERR_INVALID and b"null" in lib.ulm_last_error()
+    # bad dtype
+    rc = lib.ulm_causal_apply(dummy, 64, dummy, 64, dummy, 64, 5, 0, 1, 64, 64, L.ULM_PREC_BF16, None)
+    assert rc == L.ULM_ERR_INVALID
+
+
+def test_check_raises_with_message():
+    lib = L.lib()
+    rc = lib.ulm_decayed_scores(None, 1, None, 1, None, 1, None, 1, 1, 1, 9, None)
+    with pytest.raises(L.UlmError, match="prec"):
+        L.check(rc)
+
+
+def test_cpu_tensors_are_refused():
+    from unifiedlm_c_b200.kernel import unified_memory
+    r = torch.rand(1, 8, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        unified_memory(r, torch.rand(1, 8, 4), torch.tensor(-0.1), torch.ones(4))
+
+
+def test_model_bin_roundtrip(tmp_path, golden_dir):
+    f = torch.load(os.path.join(golden_dir, "runc_tiny.pt"), weights_only=False)
+    sd = f["state_dict"]
+    path = tmp_path / "m.bin"
+    export.write_model_bin(sd, str(path), f["max_seq_len"])
+    raw = open(path, "rb").read()
+    magic, version, dim, nl, hid, vocab, seq, conv, shared = struct.unpack_from("<Ii7i", raw, 0)
+    assert (magic, version, dim, nl, hid, vocab, seq, conv, shared) == (0x554C4D65, 1, 32, 2, 48, 512, 64, 4, 1)
+    cfg, t = export.read_model_bin(str(path))
+    assert cfg["dim"] == 32 and cfg["n_layers"] == 2
+    assert torch.equal(t["layers.1.key.weight"], sd["layers.1.key.weight"].float())
+    assert torch.equal(t["layers.0.conv"], sd["layers.0.conv.weight"][:, 0, :].float())
+    lam = torch.exp(-torch.exp(sd["layers.0.log_rate"])).float()
+    assert torch.equal(t["layers.0.lam"], lam.reshape(1))
+    expect = 256 + 4 * (512 * 32 + 2 * (32 + 32 * 4 + 48 * 32 + 48 + 32 * 48 + 32 * 32 + 48 + 2) + 32)
+    assert len(raw) == expect

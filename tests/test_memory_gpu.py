@@ -1,0 +1,166 @@
+"""Parity of the sm_100a fast-memory operator with the float64 CPU oracle.
+
+bf16 precision (tensor-core products, bf16 operands, fp32 accumulation): relative error of q,
+fast and every gradient below 1e-2, the reference kernel's bar (test_all.py:140-166).
+fp32 precision: below 1e-5, the 1e-5 parity mode.
+Relative error = ||x - x_ref|| / ||x_ref|| over the whole tensor.
+"""
+import ctypes
+import os
+
+import pytest
+import torch
+
+import unifiedlm_c_b200._lib as L
+from oracle import memory as O
+from unifiedlm_c_b200.kernel import unified_memory, operand_ld
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"bf16": 1e-2, "fp32": 1e-5}
+DEV = "cuda:0"
+
+
+def make_inputs(B, T, M, D, lam=0.95, seed=0):
+    g_ = torch.Generator().manual_seed(seed)
+    a = torch.randn(B, T, M, generator=g_, dtype=torch.float64) + 0.3
+    z = torch.relu(a).square()
+    r = z / (1.0 + z.sum(-1, keepdim=True))
+    v = torch.randn(B, T, D, generator=g_, dtype=torch.float64)
+    g = torch.tensor(float(torch.log(torch.tensor(lam))), dtype=torch.float64)
+    w = torch.exp(torch.randn(M, generator=g_, dtype=torch.float64))
+    dq_out = torch.randn(B, T, M, generator=g_, dtype=torch.float64)
+    dfast = torch.randn(B, T, D, generator=g_, dtype=torch.float64)
+    return r, v, g, w, dq_out, dfast
+
+
+def rel(x, ref):
+    ref = ref.double().cpu()
+    return float((x.double().cpu() - ref).norm() / ref.norm().clamp(min=1e-30))
+
+
+def run_gpu(r, v, g, w, dq_out, dfast, precision, v_dtype=torch.float32, use_dq=True):
+    leaves = [r.float().to(DEV), v.to(v_dtype).to(DEV), g.float().to(DEV), w.float().to(DEV)]
+    for t in leaves:
+        t.requires_grad_(True)
+    q, fast = unified_memory(*leaves, precision=precision)
+    loss = (fast.float() * dfast.float().to(DEV)).sum()
+    if use_dq:
+        loss = loss + (q * dq_out.float().to(DEV)).sum()
+    loss.backward()
+    torch.cuda.synchronize()
+    return q, fast, [t.grad for t in leaves]
+
+
+SHAPES = [
+    (1, 40, 48, 32),      # tiny, partial tiles everywhere
+    (2, 200, 140, 64),    # the reference's kernel test shape (T not a multiple of 64, M of 8)
+    (2, 70, 20, 24),      # the golden fixture's shape
+    (8, 512, 256, 64),    # BASELINE config 1 (260K op)
+    (2, 384, 1024, 512),  # 42M op shape, short T
+]
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_memory_matches_oracle(shape, precision):
+    r, v, g, w, dq_out, dfast = make_inputs(*shape)
+    q, fast, grads = run_gpu(r, v, g, w, dq_out, dfast, precision)
+    q_ref, fast_ref = O.memory_dense(r, v, g, w)
+    refs = O.memory_grads(r, v, g, w, dq_out, dfast, form="dense")
+    errs = {"q": rel(q, q_ref), "fast": rel(fast, fast_ref)}
+    errs.update({n: rel(gr, rf) for n, gr, rf in zip(("dr", "dv", "dg", "dw"), grads, refs)})
+    assert max(errs.values()) < TOL[precision], errs
+    assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("lam", [0.9, 0.99, 0.999])
+def test_decay_sweep_bf16(lam):
+    r, v, g, w, dq_out, dfast = make_inputs(2, 512, 512, 128, lam=lam, seed=1)
+    q, fast, grads = run_gpu(r, v, g, w, dq_out, dfast, "bf16")
+    q_ref, fast_ref = O.memory_dense(r, v, g, w)
+    refs = O.memory_grads(r, v, g, w, dq_out, dfast, form="dense")
+    errs = {"q": rel(q, q_ref), "fast": rel(fast, fast_ref)}
+    errs.update({n: rel(gr, rf) for n, gr, rf in zip(("dr", "dv", "dg", "dw"), grads, refs)})
+    assert max(errs.values()) < 1e-2, errs
+
+
+def test_golden_fixture(golden_dir):
+    f = torch.load(os.path.join(golden_dir, "memory_op.pt"), weights_only=False)
+    for precision in ("bf16", "fp32"):
+        q, fast, grads = run_gpu(f["r"], f["v"], f["g"], f["w"], f["dq_out"], f["dfast"], precision)
+        errs = {"q": rel(q, f["q"]), "fast": rel(fast, f["fast"])}
+        errs.update({n: rel(gr, f[n]) for n, gr in zip(("dr", "dv", "dg", "dw"), grads)})
+        assert max(errs.values()) < TOL[precision], (precision, errs)
+
+
+def test_without_q_gradient_and_bf16_values():
+    r, v, g, w, dq_out, dfast = make_inputs(2, 200, 140, 64, seed=3)
+    q, fast, grads = run_gpu(r, v, g, w, dq_out, dfast, "bf16", v_dtype=torch.bfloat16, use_dq=False)
+    assert fast.dtype == torch.bfloat16 and grads[1].dtype == torch.bfloat16
+    refs = O.memory_grads(r, v.bfloat16().double(), g, w, None, dfast, form="dense")
+    _, fast_ref = O.memory_dense(r, v.bfloat16().double(), g, w)
+    assert rel(fast, fast_ref) < 1e-2
+    for n, gr, rf in zip(("dr", "dv", "dg", "dw"), grads, refs):
+        assert rel(gr, rf) < 1e-2, n
+
+
+def test_products_against_torch():
+    """ulm_decayed_scores / ulm_causal_apply through the C ABI against torch fp32 math."""
+    torch.manual_seed(0)
+    B, T, K, V = 3, 300, 200, 96
+    lib = L.lib()
+    a = torch.randn(B, T, K, device=DEV)
+    b = torch.randn(B, T, K, device=DEV)
+    c = torch.randn(B, T, V, device=DEV)
+    g = torch.tensor([-0.03], device=DEV)
+    t = torch.arange(T, device=DEV, dtype=torch.float32)
+    Dm = torch.where(t[:, None] >= t[None, :], torch.exp(g * (t[:, None] - t[None, :])), torch.zeros(()))
+    ld_k, ld_t, ld_v = operand_ld(K), operand_ld(T), operand_ld(V)
+    a16 = torch.zeros(B, T, ld_k, device=DEV, dtype=torch.bfloat16)
+    b16 = torch.zeros_like(a16)
+    c16 = torch.zeros(B, T, ld_v, device=DEV, dtype=torch.bfloat16)
+    a16[..., :K], b16[..., :K], c16[..., :V] = a, b, c
+    P = torch.zeros(B, T, ld_t, device=DEV, dtype=torch.bfloat16)
+    st = L.stream_of(a)
+    L.check(lib.ulm_decayed_scores(L.ptr(a16), ld_k, L.ptr(b16), ld_k, L.ptr(P), ld_t, L.ptr(g), B, T, K,
+                                   L.ULM_PREC_BF16, st))
+    ref_P = (a16[..., :K].float() @ b16[..., :K].float().transpose(1, 2)) * Dm
+    assert rel(P[..., :T].float(), ref_P) < 5e-3
+    for transpose in (0, 1):
+        o = torch.empty(B, T, V, device=DEV)
+        L.check(lib.ulm_causal_apply(L.ptr(P), ld_t, L.ptr(c16), ld_v, L.ptr(o), V, L.ULM_F32, transpose, B, T, V,
+                                     L.ULM_PREC_BF16, st))
+        Pf = P[..., :T].float()
+        ref = (Pf.transpose(1, 2) if transpose else Pf) @ c16[..., :V].float()
+        assert rel(o, ref) < 1e-4, transpose
+    torch.cuda.synchronize()
+    assert L.device_error() == 0
+
+
+def test_full_size_properties():
+    """At the 110M shape (B=16, T=1024, M=2048, D=768): linearity of fast in v, exact causality,
+    determinism, and one batch row against the oracle."""
+    B, T, M, D = 16, 1024, 2048, 768
+    torch.manual_seed(0)
+    a = torch.randn(B, T, M, device=DEV) + 0.3
+    z = torch.relu(a).square()
+    r = z / (1.0 + z.sum(-1, keepdim=True))
+    v1 = torch.randn(B, T, D, device=DEV)
+    v2 = torch.randn(B, T, D, device=DEV)
+    g = torch.tensor(-0.05, device=DEV)
+    w = torch.full((M,), 4.0, device=DEV)
+    q, f1 = unified_memory(r, v1, g, w)
+    _, f2 = unified_memory(r, v2, g, w)
+    _, f12 = unified_memory(r, v1 + v2, g, w)
+    assert rel(f12, f1 + f2) < 1e-2
+    _, f1b = unified_memory(r, v1, g, w)
+    assert torch.equal(f1, f1b)  # deterministic
+    v3 = v1.clone()
+    v3[:, 700:] = torch.randn(B, T - 700, D, device=DEV)
+    _, f3 = unified_memory(r, v3, g, w)
+    assert torch.equal(f3[:, :700], f1[:, :700])  # nothing leaks backwards in time
+    q_ref, fast_ref = O.memory_dense(r[:1].double().cpu(), v1[:1].double().cpu(), g.double().cpu(),
+                                     w.double().cpu())
+    assert rel(q[:1], q_ref) < 1e-5 and rel(f1[:1], fast_ref) < 1e-2
+    assert L.device_error() == 0

@@ -1,0 +1,86 @@
+"""ctypes binding of the C ABI in include/ulm_b200.h (libulm_b200.so, built in-tree).
+
+There is no fallback: if the library is missing or a call fails, the caller gets an exception.
+"""
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libulm_b200.so")
+
+ULM_OK, ULM_ERR_INVALID, ULM_ERR_CUDA, ULM_ERR_UNSUPPORTED, ULM_ERR_DEVICE = range(5)
+ULM_F32, ULM_BF16 = 0, 1
+ULM_PREC_BF16, ULM_PREC_FP32 = 0, 1
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+# name -> (restype, argtypes); kept in the order of include/ulm_b200.h
+SIGNATURES = {
+    "ulm_last_error": (ctypes.c_char_p, []),
+    "ulm_version": (_I, []),
+    "ulm_device_error": (_I, [ctypes.POINTER(_I)]),
+    "ulm_memory_stats_fwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _P]),
+    "ulm_memory_stats_bwd": (_I, [_P] * 12 + [_I64, _I64, _I64, _P]),
+    "ulm_memory_stats_bwd_scratch": (_I64, [_I64, _I64, _I64]),
+    "ulm_decayed_scores": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
+    "ulm_causal_apply": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _P]),
+    "ulm_operand_ld": (_I64, [_I64]),
+    "ulm_memory_fwd": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "ulm_memory_bwd": (_I, [_P, _P, _I] + [_P] * 18 + [_I64, _I64, _I64, _I64, _I, _P]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library with argument types declared. Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; "
+                               f"g.build()'` (nvcc, sm_100a)")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+class UlmError(RuntimeError):
+    pass
+
+
+def check(rc):
+    if rc != ULM_OK:
+        msg = lib().ulm_last_error().decode(errors="replace")
+        raise UlmError(f"libulm_b200 status {rc}: {msg}")
+
+
+def ptr(t):
+    """Device (or host) address of a tensor, or NULL for None."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def dtype_code(dtype):
+    if dtype == torch.float32:
+        return ULM_F32
+    if dtype == torch.bfloat16:
+        return ULM_BF16
+    raise UlmError(f"unsupported element type {dtype}")
+
+
+def device_error():
+    """Synchronise and read/clear the device-side error flag (0 = none)."""
+    site = _I(0)
+    check(lib().ulm_device_error(ctypes.byref(site)))
+    return site.value

@@ -1,0 +1,493 @@
+// The two back ends of the batched GEMM engine (see gemm.cuh).
+//
+// Tensor-core back end (bf16 operands): a persistent, warp-specialised sm_100a kernel.
+//   warp 0        : TMA producer - 128B-swizzled tiles of A (128 x 64) and B (BN x 64) per stage
+//   warp 1        : allocates TMEM, one elected lane issues tcgen05.mma (M=128, N=BN, K=16) into a
+//                   double-buffered fp32 accumulator (2 x BN TMEM columns)
+//   warps 2..5    : epilogue - tcgen05.ld 32 columns at a time, fused decay/mask, vector stores
+// Stage hand-offs use mbarriers; the accumulator is double-buffered so the epilogue of tile i
+// overlaps the MMAs of tile i+1. Every wait is bounded: on timeout the kernel records a device
+// error, drains what it has in flight, frees its TMEM and returns.
+//
+// FMA back end (fp32 operands): 64 x 64 tiles, 16-deep k slices in shared memory, 4 x 4 outputs
+// per thread, same tile decomposition and epilogue semantics.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "gemm.cuh"
+
+namespace ulm {
+
+// ------------------------------------------------------------------------------------------------
+// epilogue: one thread owns one output row segment of 32 columns
+
+__device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const GemmShape& s, float gl2, int b,
+                                                 int row, int col0, float (&v)[32]) {
+  if (row >= s.M || col0 >= s.N) return;
+  if (e.kind == EPI_DECAY) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int lag = row - (col0 + i);
+      v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
+    }
+  }
+  const int ncols = min(32, s.N - col0);
+  const int64_t off = (int64_t)b * e.out_bstride + (int64_t)row * e.ldo + col0;
+  if (e.out_dtype == ULM_F32) {
+    float* o = reinterpret_cast<float*>(e.out) + off;
+    if (ncols == 32 && e.vec_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) o[i] = v[i];
+    }
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out) + off;
+    if (ncols == 32 && e.vec_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 pk;
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+        __nv_bfloat162 p1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+        __nv_bfloat162 p2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+        __nv_bfloat162 p3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+        memcpy(&pk.x, &p0, 4);
+        memcpy(&pk.y, &p1, 4);
+        memcpy(&pk.z, &p2, 4);
+        memcpy(&pk.w, &p3, 4);
+        *reinterpret_cast<uint4*>(o + i) = pk;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) o[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// tensor-core back end
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;
+constexpr int TC_THREADS = 192;
+
+template <int BN>
+struct TcConfig {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
+  static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // stages + 1024 alignment slack + barriers / TMEM slot / flags
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+// Wait on an mbarrier phase unless the CTA is aborting; false on timeout or abort.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > 2000000000ull) {
+        raise_device_error(site);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
+                   const int tiles_per_batch, const int total_tiles) {
+  using Cfg = TcConfig<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_bf16_f32(TC_BM, BN, A_MN, B_MN);
+  // descriptor strides: K-major rows are 128 B, 8-row atoms 1024 B apart; MN-major operands keep
+  // 64-element M/N blocks of 64 K-rows (8 KB) one after the other
+  constexpr uint32_t SBO = 1024;
+  constexpr uint32_t MN_LBO = TC_BK * 128;
+  // per K=16 step: K-major advances 32 B inside the swizzle row, MN-major advances 16 rows
+  constexpr uint32_t A_KSTEP = A_MN ? 16 * 128 : 32;
+  constexpr uint32_t B_KSTEP = B_MN ? 16 * 128 : 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;  // stages issued and possibly not yet consumed (for draining on abort)
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+        const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM_PRODUCER_WAIT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          const int k0 = kb * TC_BK;
+          if (!A_MN) {
+            tma_load_3d(&tma_a, sa, &full[stage], k0, tc.mb * TC_BM, tc.b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < TC_BM / 64; ++j)
+              tma_load_3d(&tma_a, sa + j * MN_LBO, &full[stage], tc.mb * TC_BM + j * 64, k0, tc.b);
+          }
+          if (!B_MN) {
+            tma_load_3d(&tma_b, sb, &full[stage], k0, tc.nb * BN, tc.b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(&tma_b, sb + j * MN_LBO, &full[stage], tc.nb * BN + j * 64, k0, tc.b);
+          }
+          issued = min(issued + 1, STAGES);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded) for the loads still in flight into the last `issued` stages
+        for (int i = 0; i < issued; ++i) {
+          if (--stage < 0) {
+            stage = STAGES - 1;
+            phase ^= 1u;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[stage], phase) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int j = 0;
+      bool ok = true, issued_any = false;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
+        const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+        const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int acc = j & 1;
+        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM_MMA_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM_MMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
+            const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
+            umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+      }
+      if (!ok && issued_any) {
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    const float gl2 = (epi.kind == EPI_DECAY) ? (*epi.g) * 1.4426950408889634f : 0.f;
+    int j = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
+      const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+      const int acc = j & 1;
+      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+      if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, DEVERR_GEMM_EPILOGUE_WAIT)) break;
+      tc_fence_after();
+      const int row = tc.mb * TC_BM + row_in_tile;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld_32x32(taddr + (uint32_t)c, v);
+        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// FMA back end
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(256)
+    simt_gemm_kernel(const float* __restrict__ A, int64_t lda, int64_t bsA, const float* __restrict__ Bm, int64_t ldb,
+                     int64_t bsB, const GemmShape shape, const GemmEpilogue epi, const int m_blocks,
+                     const int n_blocks, const int tiles_per_batch) {
+  constexpr int BM = 64, BN = 64, BK = 16;
+  __shared__ float As[BK][BM + 1];
+  __shared__ float Bs[BK][BN + 1];
+  const TileCoord tc = decode_tile<BM, BN>(blockIdx.x, shape, m_blocks, n_blocks, tiles_per_batch);
+  const float* Ab = A + (int64_t)tc.b * bsA;
+  const float* Bb = Bm + (int64_t)tc.b * bsB;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) acc[i][jj] = 0.f;
+
+  for (int k0 = tc.k_begin; k0 < tc.k_end; k0 += BK) {
+    for (int i = threadIdx.x; i < BM * BK; i += 256) {
+      int mm, kk;
+      if (A_MN) { kk = i / BM; mm = i % BM; } else { mm = i / BK; kk = i % BK; }
+      const int gm = tc.mb * BM + mm, gk = k0 + kk;
+      float val = 0.f;
+      if (gm < shape.M && gk < tc.k_end) val = A_MN ? Ab[(int64_t)gk * lda + gm] : Ab[(int64_t)gm * lda + gk];
+      As[kk][mm] = val;
+    }
+    for (int i = threadIdx.x; i < BN * BK; i += 256) {
+      int nn, kk;
+      if (B_MN) { kk = i / BN; nn = i % BN; } else { nn = i / BK; kk = i % BK; }
+      const int gn = tc.nb * BN + nn, gk = k0 + kk;
+      float val = 0.f;
+      if (gn < shape.N && gk < tc.k_end) val = B_MN ? Bb[(int64_t)gk * ldb + gn] : Bb[(int64_t)gn * ldb + gk];
+      Bs[kk][nn] = val;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) bv[jj] = Bs[kk][tx + 16 * jj];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(a[i], bv[jj], acc[i][jj]);
+    }
+    __syncthreads();
+  }
+  const float g = (epi.kind == EPI_DECAY) ? *epi.g : 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = tc.mb * BM + ty + 16 * i;
+    if (row >= shape.M) continue;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int col = tc.nb * BN + tx + 16 * jj;
+      if (col >= shape.N) continue;
+      float v = acc[i][jj];
+      if (epi.kind == EPI_DECAY) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
+      const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
+      if (epi.out_dtype == ULM_F32)
+        reinterpret_cast<float*>(epi.out)[off] = v;
+      else
+        reinterpret_cast<__nv_bfloat16*>(epi.out)[off] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D tiled map over (inner, rows, batch) of a bf16 operand with a 128-byte swizzle.
+int make_tmap(CUtensorMap* map, const Operand& op, int batches, uint32_t box_inner, uint32_t box_rows) {
+  auto fn = encode_tiled();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return ULM_ERR_UNSUPPORTED;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)op.inner, (cuuint64_t)op.rows, (cuuint64_t)batches};
+  cuuint64_t strides[2] = {(cuuint64_t)op.ld * 2, (cuuint64_t)op.bstride * 2};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(op.ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): inner=%lld rows=%lld ld=%lld", (int)r, (long long)op.inner,
+              (long long)op.rows, (long long)op.ld);
+    return ULM_ERR_CUDA;
+  }
+  return ULM_OK;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+  using Cfg = TcConfig<BN>;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : TC_BM);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : BN);
+  if (rc) return rc;
+  const int dev = current_device();
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range", dev);
+    return ULM_ERR_INVALID;
+  }
+  if (!configured[dev]) {
+    ULM_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel<BN, A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Cfg::SMEM_BYTES));
+    configured[dev] = true;
+  }
+  const int m_blocks = (int)cdiv(s.M, TC_BM), n_blocks = (int)cdiv(s.N, BN);
+  const int tpb = tiles_per_batch_host(s, TC_BM, BN, m_blocks, n_blocks);
+  const int64_t total64 = (int64_t)tpb * s.batches;
+  ULM_REQUIRE(total64 < (1ll << 31), "too many tiles (%lld)", (long long)total64);
+  const int total = (int)total64;
+  if (total == 0) return ULM_OK;
+  const int grid = total < sm_count(dev) ? total : sm_count(dev);
+  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, s, e, m_blocks, n_blocks, tpb,
+                                                                            total);
+  ULM_LAUNCH_CHECK("tc_gemm_kernel");
+  return ULM_OK;
+}
+
+template <int BN>
+int dispatch_tc_major(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+  if (!A.mn_major && !B.mn_major) return launch_tc<BN, false, false>(A, B, s, e, st);
+  if (!A.mn_major && B.mn_major) return launch_tc<BN, false, true>(A, B, s, e, st);
+  if (A.mn_major && !B.mn_major) return launch_tc<BN, true, false>(A, B, s, e, st);
+  return launch_tc<BN, true, true>(A, B, s, e, st);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_simt(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+  const int m_blocks = (int)cdiv(s.M, 64), n_blocks = (int)cdiv(s.N, 64);
+  const int tpb = tiles_per_batch_host(s, 64, 64, m_blocks, n_blocks);
+  const int64_t total = (int64_t)tpb * s.batches;
+  ULM_REQUIRE(total < (1ll << 31), "too many tiles (%lld)", (long long)total);
+  if (total == 0) return ULM_OK;
+  simt_gemm_kernel<A_MN, B_MN><<<(unsigned)total, 256, 0, st>>>(
+      static_cast<const float*>(A.ptr), A.ld, A.bstride, static_cast<const float*>(B.ptr), B.ld, B.bstride, s, e,
+      m_blocks, n_blocks, tpb);
+  ULM_LAUNCH_CHECK("simt_gemm_kernel");
+  return ULM_OK;
+}
+
+}  // namespace
+
+int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream) {
+  ULM_REQUIRE(A.ptr && B.ptr && e.out, "null operand or output pointer");
+  ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
+  ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
+  ULM_REQUIRE(e.out_dtype == ULM_F32 || e.out_dtype == ULM_BF16, "bad output dtype");
+  ULM_REQUIRE(e.kind != EPI_DECAY || e.g, "decay epilogue needs g");
+  if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
+    ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
+  if (s.batches == 0 || s.M == 0 || s.N == 0) return ULM_OK;
+  ULM_REQUIRE(s.K > 0, "empty contraction");
+  if (A.dtype == ULM_BF16) {
+    ULM_REQUIRE(is_aligned16(A.ptr) && is_aligned16(B.ptr), "bf16 operands must be 16-byte aligned");
+    ULM_REQUIRE(A.ld % 8 == 0 && B.ld % 8 == 0 && A.bstride % 8 == 0 && B.bstride % 8 == 0,
+                "bf16 operand strides must be multiples of 8 elements (lda=%lld ldb=%lld)", (long long)A.ld,
+                (long long)B.ld);
+    ULM_REQUIRE(A.ld >= A.inner && B.ld >= B.inner, "row stride shorter than the row");
+    if (s.N >= 256) return dispatch_tc_major<256>(A, B, s, e, stream);
+    return dispatch_tc_major<128>(A, B, s, e, stream);
+  }
+  ULM_REQUIRE(A.dtype == ULM_F32, "operands must be bf16 or fp32");
+  if (!A.mn_major && !B.mn_major) return launch_simt<false, false>(A, B, s, e, stream);
+  if (!A.mn_major && B.mn_major) return launch_simt<false, true>(A, B, s, e, stream);
+  if (A.mn_major && !B.mn_major) return launch_simt<true, false>(A, B, s, e, stream);
+  return launch_simt<true, true>(A, B, s, e, stream);
+}
+
+}  // namespace ulm

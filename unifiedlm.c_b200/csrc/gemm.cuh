@@ -1,0 +1,99 @@
+// Batched GEMM engine shared by every contraction of the fast-memory path.
+//
+//   C[b][m][n] = sum_k A[b][m][k] * B[b][n][k]          (per batch row b)
+//
+// A and B may each be stored K-major ([m][k], k contiguous) or MN-major ([k][m], m contiguous), so
+// the transposed products of the backward need no transposition pass. A causal mode restricts the
+// work to the triangle the fast memory needs:
+//   CAUSAL_NLOWER : only tiles with columns n <= rows m (decayed scores, s <= t)
+//   CAUSAL_KLOWER : the k range of a row block stops at the block's last row (forward read)
+//   CAUSAL_KUPPER : the k range of a row block starts at the block's first row (reversed read)
+// and a fused epilogue writes the tile (EPI_STORE) or the decayed causal score
+// lam^(m-n) * acc masked to n <= m (EPI_DECAY).
+//
+// Two back ends share the tile decomposition: a tcgen05/TMA/TMEM tensor-core kernel for bf16
+// operands (fp32 accumulation) and an fp32 FMA kernel for the 1e-5 parity mode.
+#pragma once
+
+#include "common.cuh"
+
+namespace ulm {
+
+enum { CAUSAL_NONE = 0, CAUSAL_KLOWER = 1, CAUSAL_KUPPER = 2, CAUSAL_NLOWER = 3 };
+enum { EPI_STORE = 0, EPI_DECAY = 1 };
+
+struct GemmShape {
+  int batches, M, N, K;
+  int causal;
+};
+
+struct GemmEpilogue {
+  int kind;            // EPI_STORE / EPI_DECAY
+  int out_dtype;       // ULM_F32 / ULM_BF16
+  void* out;
+  int64_t ldo;         // row stride of the output, elements
+  int64_t out_bstride; // batch stride of the output, elements
+  const float* g;      // log decay (device scalar), EPI_DECAY only
+  int vec_ok;          // output rows are 16-byte aligned for every tile (set by the host)
+};
+
+// A matrix operand in global memory: element (b, row, col) of its storage order at
+// ptr + b*bstride + row*ld + col, with `inner` = extent of col and `rows` = extent of row.
+struct Operand {
+  const void* ptr;
+  int64_t ld, bstride;
+  int64_t inner, rows;
+  int dtype;
+  bool mn_major;  // storage order is [k][m] (resp. [k][n]) rather than [m][k]
+};
+
+struct TileCoord {
+  int b, mb, nb, k_begin, k_end;
+};
+
+__host__ __device__ inline int nlower_tiles_in_row(int mb, int BM, int BN, int n_blocks) {
+  int c = ((mb + 1) * BM - 1) / BN + 1;
+  return c < n_blocks ? c : n_blocks;
+}
+
+// Map a linear tile index to (batch, row block, column block, k range). Tiles of one batch row are
+// consecutive (L2 locality); under CAUSAL_KLOWER the longest row blocks come first.
+template <int BM, int BN>
+__device__ __forceinline__ TileCoord decode_tile(int t, const GemmShape& s, int m_blocks, int n_blocks,
+                                                 int tiles_per_batch) {
+  TileCoord c;
+  c.b = t / tiles_per_batch;
+  int i = t - c.b * tiles_per_batch;
+  if (s.causal == CAUSAL_NLOWER) {
+    int mb = 0;
+    for (;;) {
+      const int cnt = nlower_tiles_in_row(mb, BM, BN, n_blocks);
+      if (i < cnt) break;
+      i -= cnt;
+      ++mb;
+    }
+    c.mb = mb;
+    c.nb = i;
+  } else {
+    c.mb = i / n_blocks;
+    c.nb = i - c.mb * n_blocks;
+    if (s.causal == CAUSAL_KLOWER) c.mb = m_blocks - 1 - c.mb;
+  }
+  c.k_begin = 0;
+  c.k_end = s.K;
+  if (s.causal == CAUSAL_KLOWER) c.k_end = min(s.K, (c.mb + 1) * BM);
+  if (s.causal == CAUSAL_KUPPER) c.k_begin = min(s.K, c.mb * BM);
+  return c;
+}
+
+inline int tiles_per_batch_host(const GemmShape& s, int BM, int BN, int m_blocks, int n_blocks) {
+  if (s.causal != CAUSAL_NLOWER) return m_blocks * n_blocks;
+  int n = 0;
+  for (int mb = 0; mb < m_blocks; ++mb) n += nlower_tiles_in_row(mb, BM, BN, n_blocks);
+  return n;
+}
+
+// Host entry: validates, picks the back end from the operand types, launches on `stream`.
+int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream);
+
+}  // namespace ulm

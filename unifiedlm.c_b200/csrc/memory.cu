@@ -1,0 +1,208 @@
+// The fast-memory operator (the reference's kernel.py:199-238) built from the batched GEMM engine
+// and the statistics scans, plus the library-level C ABI glue.
+//
+// Forward, per batch row (lam = exp(g), k = shift(r), D[t,s] = lam^(t-s) for s <= t):
+//   stats            q = r / (w + D k),  plus operand copies qop, kop
+//   scores           P = D * (qop kop^T)                     (B,T,T), tiles on/below the diagonal
+//   read             fast = P vop                             causal k range
+// Backward, with do = dfast:
+//   scores           dS = D * (do vop^T)
+//   reads            dqf = dS kop,  dk = dS^T qop,  dv = P^T do
+//   stats backward   dr, dw, dg (reverse scan, deterministic reductions)
+//
+// The reference carries a (K x V) state between 64-token chunks and materialises it for every chunk
+// (kernel.py:23-48). At the shapes this library targets (T up to a few thousand, K = slots up to
+// 2048, V = dim up to 768) the T x T score matrix is far smaller than the per-chunk states and the
+// whole-sequence products are fewer flops: forward T(M+D) per token against 4MD + 2C(M+D) for the
+// chunked form. Results are the same function; only the summation order differs.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "gemm.cuh"
+
+namespace ulm {
+
+static thread_local char g_error_msg[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error_msg, sizeof(g_error_msg), fmt, ap);
+  va_end(ap);
+}
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+int sm_count(int device) {
+  static int cache[64] = {};
+  if (device < 0 || device >= 64) return 148;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+namespace {
+
+int elem_size(int dtype) { return dtype == ULM_BF16 ? 2 : 4; }
+
+int op_dtype_of(int prec) { return prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16; }
+
+GemmEpilogue make_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int64_t bstride, const float* g) {
+  GemmEpilogue e;
+  e.kind = kind;
+  e.out_dtype = out_dtype;
+  e.out = out;
+  e.ldo = ldo;
+  e.out_bstride = bstride;
+  e.g = g;
+  const int vec = out_dtype == ULM_F32 ? 4 : 8;
+  e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
+  return e;
+}
+
+// elementwise copy with type conversion between row strides (fp32/bf16 -> fp32/bf16)
+__global__ void convert_rows_kernel(const void* __restrict__ src, int src_dtype, int64_t lds, void* __restrict__ dst,
+                                    int dst_dtype, int64_t ldd, int64_t rows, int64_t cols) {
+  const int64_t n = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rr = i / cols, cc = i - rr * cols;
+    const float v = src_dtype == ULM_F32 ? static_cast<const float*>(src)[rr * lds + cc]
+                                         : __bfloat162float(static_cast<const __nv_bfloat16*>(src)[rr * lds + cc]);
+    if (dst_dtype == ULM_F32)
+      static_cast<float*>(dst)[rr * ldd + cc] = v;
+    else
+      static_cast<__nv_bfloat16*>(dst)[rr * ldd + cc] = __float2bfloat16_rn(v);
+  }
+}
+
+int convert_rows(const void* src, int sdt, int64_t lds, void* dst, int ddt, int64_t ldd, int64_t rows, int64_t cols,
+                 cudaStream_t st) {
+  if (rows * cols == 0) return ULM_OK;
+  const int64_t blocks = cdiv(rows * cols, 256);
+  const unsigned grid = (unsigned)(blocks < 8 * 148 ? blocks : 8 * 148);
+  convert_rows_kernel<<<grid, 256, 0, st>>>(src, sdt, lds, dst, ddt, ldd, rows, cols);
+  ULM_LAUNCH_CHECK("convert_rows_kernel");
+  return ULM_OK;
+}
+
+int check_prec(int prec) {
+  ULM_REQUIRE(prec == ULM_PREC_BF16 || prec == ULM_PREC_FP32, "prec must be ULM_PREC_BF16 or ULM_PREC_FP32");
+  return ULM_OK;
+}
+
+}  // namespace
+
+}  // namespace ulm
+
+using namespace ulm;
+
+extern "C" const char* ulm_last_error(void) { return g_error_msg; }
+
+extern "C" int ulm_version(void) { return 1; }
+
+extern "C" int ulm_device_error(int* site) {
+  ULM_REQUIRE(site, "null site pointer");
+  ULM_CUDA_TRY(cudaDeviceSynchronize());
+  int v = 0;
+  ULM_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  const int zero = 0;
+  ULM_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  *site = v;
+  return ULM_OK;
+}
+
+extern "C" int64_t ulm_operand_ld(int64_t n) { return ((n + 7) / 8) * 8; }
+
+extern "C" int ulm_decayed_scores(const void* a, int64_t lda, const void* bb, int64_t ldb, void* P, int64_t ldp,
+                                  const float* g, int64_t B, int64_t T, int64_t K, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && K >= 0, "negative extent");
+  ULM_REQUIRE(T < (1 << 30) && K < (1 << 30) && B < (1 << 30), "extent too large");
+  ULM_REQUIRE(lda >= K && ldb >= K && ldp >= T, "row stride shorter than the row");
+  const int dt = op_dtype_of(prec);
+  Operand A{a, lda, T * lda, K, T, dt, false};
+  Operand Bo{bb, ldb, T * ldb, K, T, dt, false};
+  GemmShape s{(int)B, (int)T, (int)T, (int)K, CAUSAL_NLOWER};
+  GemmEpilogue e = make_epilogue(EPI_DECAY, dt, P, ldp, T * ldp, g);
+  return run_gemm(A, Bo, s, e, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ulm_causal_apply(const void* P, int64_t ldp, const void* c, int64_t ldc, void* o, int64_t ldo,
+                                int o_dtype, int transpose, int64_t B, int64_t T, int64_t V, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && V >= 0, "negative extent");
+  ULM_REQUIRE(T < (1 << 30) && V < (1 << 30) && B < (1 << 30), "extent too large");
+  ULM_REQUIRE(ldp >= T && ldc >= V && ldo >= V, "row stride shorter than the row");
+  ULM_REQUIRE(o_dtype == ULM_F32 || o_dtype == ULM_BF16, "bad o_dtype");
+  const int dt = op_dtype_of(prec);
+  // forward : o[t][v] = sum_s P[t][s] c[s][v]  -> A = P (K-major), B = c ([k=s][n=v], MN-major)
+  // reversed: o[s][v] = sum_t P[t][s] c[t][v]  -> A = P read as [k=t][m=s] (MN-major)
+  Operand A{P, ldp, T * ldp, T, T, dt, transpose != 0};
+  Operand Bo{c, ldc, T * ldc, V, T, dt, true};
+  GemmShape s{(int)B, (int)T, (int)V, (int)T, transpose ? CAUSAL_KUPPER : CAUSAL_KLOWER};
+  GemmEpilogue e = make_epilogue(EPI_STORE, o_dtype, o, ldo, T * ldo, nullptr);
+  return run_gemm(A, Bo, s, e, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const float* g, const float* w, float* q,
+                              void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
+                              int64_t M, int64_t D, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
+  ULM_REQUIRE(v_dtype == ULM_F32 || v_dtype == ULM_BF16, "v_dtype must be ULM_F32 or ULM_BF16");
+  if (B == 0 || T == 0) return ULM_OK;
+  ULM_REQUIRE(r && v && g && w && q && fast && c && qop && kop && vop && P, "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int dt = op_dtype_of(prec);
+  const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
+  if (int rc = ulm_memory_stats_fwd(r, w, g, q, c, qop, kop, dt, ldm, B, T, M, stream)) return rc;
+  if (M == 0) {
+    // no slots: the fast read is empty
+    ULM_CUDA_TRY(cudaMemsetAsync(fast, 0, B * T * D * elem_size(v_dtype), st));
+    return ULM_OK;
+  }
+  if (D == 0) return ULM_OK;
+  if (int rc = convert_rows(v, v_dtype, D, vop, dt, ldd, B * T, D, st)) return rc;
+  if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, P, ldt, g, B, T, M, prec, stream)) return rc;
+  return ulm_causal_apply(P, ldt, vop, ldd, fast, D, v_dtype, 0, B, T, D, prec, stream);
+}
+
+extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* g,
+                              const float* w, const float* q, const float* c, const void* qop, const void* kop,
+                              const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk,
+                              void* partial, float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T,
+                              int64_t M, int64_t D, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
+  ULM_REQUIRE(do_dtype == ULM_F32 || do_dtype == ULM_BF16, "do_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(dfast && dr && dv && dg && dw, "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int dt = op_dtype_of(prec);
+  const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
+  if (B == 0 || T == 0 || M == 0) {
+    if (B * T * D > 0) ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(do_dtype), st));
+    return ulm_memory_stats_bwd(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+  }
+  ULM_REQUIRE(r && g && w && q && c && qop && kop && vop && P && doop && dS && dqf && dk && partial,
+              "null pointer argument");
+  if (D == 0) {
+    ULM_CUDA_TRY(cudaMemsetAsync(dqf, 0, B * T * M * sizeof(float), st));
+    ULM_CUDA_TRY(cudaMemsetAsync(dk, 0, B * T * M * sizeof(float), st));
+  } else {
+    if (int rc = convert_rows(dfast, do_dtype, D, doop, dt, ldd, B * T, D, st)) return rc;
+    // dS = D * (do v^T): gradient of the scores, same causal decay as the forward
+    if (int rc = ulm_decayed_scores(doop, ldd, vop, ldd, dS, ldt, g, B, T, D, prec, stream)) return rc;
+    if (int rc = ulm_causal_apply(dS, ldt, kop, ldm, dqf, M, ULM_F32, 0, B, T, M, prec, stream)) return rc;
+    if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
+    if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
+  }
+  return ulm_memory_stats_bwd(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+}

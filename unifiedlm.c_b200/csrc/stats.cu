@@ -1,0 +1,246 @@
+// Slot statistics of the fast memory: the decayed running mass n_t of every slot and the posterior
+// rescale q = r / (w + n) (forward), and their reverse-time backward.
+//
+// Both passes are HBM-bound scans along time. A CTA owns 32 consecutive slots of one batch row
+// (lane = slot, so every load/store of a warp is one contiguous 128-byte row segment) and splits
+// time into 8 segments, one warp each. Pass 1 scans each segment from a zero carry and publishes
+// the segment's end value; the carries are combined in shared memory (lam^len per segment); pass 2
+// rescans with the true carry and writes the outputs. The second read of r hits L2 (a CTA's slice
+// is at most 32 x T x 4 bytes).
+#include "common.cuh"
+
+namespace ulm {
+
+constexpr int STATS_SEGS = 8;
+constexpr int STATS_THREADS = 32 * STATS_SEGS;
+
+template <typename T>
+__device__ __forceinline__ void store_op(void* base, int64_t idx, float v);
+template <>
+__device__ __forceinline__ void store_op<float>(void* base, int64_t idx, float v) {
+  static_cast<float*>(base)[idx] = v;
+}
+template <>
+__device__ __forceinline__ void store_op<__nv_bfloat16>(void* base, int64_t idx, float v) {
+  static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+}
+
+// kernel.py:109-136: k_t = r_{t-1}, c_t = w + sum_{s<=t} lam^(t-s) k_s, q_t = r_t / c_t
+template <typename OpT>
+__global__ void __launch_bounds__(STATS_THREADS)
+    stats_fwd_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
+                     float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop, void* __restrict__ kop,
+                     int64_t ldop, int T, int M) {
+  __shared__ float seg_end[STATS_SEGS][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int b = blockIdx.y;
+  const int m = blockIdx.x * 32 + lane;
+  const bool valid = m < M;
+  const int seg_len = (T + STATS_SEGS - 1) / STATS_SEGS;
+  const int t0 = min(T, seg * seg_len), t1 = min(T, t0 + seg_len);
+  const float gg = *g;
+  const float lam = expf(gg);
+  const int64_t row0 = (int64_t)b * T;
+  const float* rb = r + row0 * M + m;
+
+  // pass 1: the segment's own decayed sum of k, from a zero carry
+  float run = 0.f;
+  float kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
+#pragma unroll 4
+  for (int t = t0; t < t1; ++t) {
+    const float rt = valid ? rb[(int64_t)t * M] : 0.f;
+    run = fmaf(lam, run, kprev);
+    kprev = rt;
+  }
+  seg_end[seg][lane] = run;
+  __syncthreads();
+  float carry = 0.f;
+  for (int j = 0; j < seg; ++j) {
+    const int len = min(T, (j + 1) * seg_len) - min(T, j * seg_len);
+    carry = fmaf(carry, expf(gg * (float)len), seg_end[j][lane]);
+  }
+
+  // pass 2: rescan with the carry and write q, c and the operand copies of q and k
+  const float wm = valid ? w[m] : 1.f;
+  run = carry;
+  kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
+  if (valid) {
+#pragma unroll 4
+    for (int t = t0; t < t1; ++t) {
+      const float rt = rb[(int64_t)t * M];
+      run = fmaf(lam, run, kprev);
+      const float cc = wm + run;
+      const float qq = rt / cc;
+      const int64_t i = (row0 + t) * M + m;
+      q[i] = qq;
+      c[i] = cc;
+      const int64_t io = (row0 + t) * ldop + m;
+      store_op<OpT>(qop, io, qq);
+      store_op<OpT>(kop, io, kprev);
+      kprev = rt;
+    }
+  }
+}
+
+// kernel.py:139-180 and :232. With dq = dqf + dq_out, walking time backwards:
+//   dc_t = -dq_t q_t / c_t,  dkc_t = dc_t + lam dkc_{t+1}  (gradient reaching k through c)
+//   dkt_t = dk_t + dkc_t,    dr_t = dq_t / c_t + dkt_{t+1}  (k_{t+1} = r_t)
+//   dw += dc_t,  dg += (t - t_mid) (q.dqf - k.dk + dc (c - w) - k.dkc)
+// The position weight is centred at t_mid = (T-1)/2: the unweighted sums of q.dqf - k.dk and of
+// dc (c - w) - k.dkc are both zero (each pair is the same double sum over (t, s)), so centring
+// leaves dg unchanged and keeps the fp32 terms small. Partial sums go to `partial` (per batch row
+// and slot for dw, per batch row and slot group for dg, in double) and are reduced in a fixed
+// order by stats_bwd_finalize_kernel.
+__global__ void __launch_bounds__(STATS_THREADS)
+    stats_bwd_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out, const float* __restrict__ dk,
+                     const float* __restrict__ q, const float* __restrict__ c, const float* __restrict__ r,
+                     const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ dr,
+                     float* __restrict__ part_dw, double* __restrict__ part_dg, int T, int M) {
+  __shared__ float seg_start[STATS_SEGS][32];
+  __shared__ double red_dg[STATS_THREADS];
+  __shared__ float red_dw[STATS_SEGS][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int b = blockIdx.y;
+  const int m = blockIdx.x * 32 + lane;
+  const bool valid = m < M;
+  const int seg_len = (T + STATS_SEGS - 1) / STATS_SEGS;
+  const int t0 = min(T, seg * seg_len), t1 = min(T, t0 + seg_len);
+  const float gg = *g;
+  const float lam = expf(gg);
+  const int64_t base = (int64_t)b * T * M + m;
+  const bool has_dqo = dq_out != nullptr;
+
+  // pass 1: reverse decayed sum of dc over the segment, from a zero carry
+  float run = 0.f;
+  if (valid) {
+#pragma unroll 4
+    for (int t = t1 - 1; t >= t0; --t) {
+      const int64_t i = base + (int64_t)t * M;
+      const float dq = dqf[i] + (has_dqo ? dq_out[i] : 0.f);
+      const float cc = c[i];
+      const float dc = -dq * q[i] / cc;
+      run = fmaf(lam, run, dc);
+    }
+  }
+  seg_start[seg][lane] = run;
+  __syncthreads();
+  float carry = 0.f;  // dkc at position t1 (first position after this segment)
+  for (int j = STATS_SEGS - 1; j > seg; --j) {
+    const int len = min(T, (j + 1) * seg_len) - min(T, j * seg_len);
+    carry = fmaf(carry, expf(gg * (float)len), seg_start[j][lane]);
+  }
+
+  // pass 2
+  const float wm = valid ? w[m] : 0.f;
+  const float t_mid = 0.5f * (float)(T - 1);
+  double dg_acc = 0.0;
+  float dw_acc = 0.f;
+  if (valid && t0 < t1) {
+    run = carry;
+    float dkt_next = (t1 < T) ? dk[base + (int64_t)t1 * M] + carry : 0.f;
+#pragma unroll 2
+    for (int t = t1 - 1; t >= t0; --t) {
+      const int64_t i = base + (int64_t)t * M;
+      const float dqfv = dqf[i];
+      const float dq = dqfv + (has_dqo ? dq_out[i] : 0.f);
+      const float cc = c[i];
+      const float qq = q[i];
+      const float dc = -dq * qq / cc;
+      run = fmaf(lam, run, dc);  // dkc_t
+      const float dkv = dk[i];
+      const float kt = t > 0 ? r[i - M] : 0.f;
+      const float dkt = dkv + run;
+      dr[i] = dq / cc + dkt_next;
+      dkt_next = dkt;
+      const float term = qq * dqfv - kt * dkv + dc * (cc - wm) - kt * run;
+      dg_acc += (double)(((float)t - t_mid) * term);
+      dw_acc += dc;
+    }
+  }
+  red_dw[seg][lane] = dw_acc;
+  red_dg[threadIdx.x] = dg_acc;
+  __syncthreads();
+  if (seg == 0) {
+    float s = 0.f;
+    for (int j = 0; j < STATS_SEGS; ++j) s += red_dw[j][lane];
+    if (valid) part_dw[(int64_t)b * M + m] = s;
+  }
+  for (int stride = STATS_THREADS / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
+}
+
+// dw[m] = sum_b part_dw[b][m]; dg = sum over (b, slot group) of part_dg, both in index order.
+__global__ void stats_bwd_finalize_kernel(const float* __restrict__ part_dw, const double* __restrict__ part_dg,
+                                          float* __restrict__ dw, float* __restrict__ dg, int B, int M, int groups) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m < M) {
+    float s = 0.f;
+    for (int b = 0; b < B; ++b) s += part_dw[(int64_t)b * M + m];
+    dw[m] = s;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    double s = 0.0;
+    for (int i = 0; i < B * groups; ++i) s += part_dg[i];
+    *dg = (float)s;
+  }
+}
+
+}  // namespace ulm
+
+using namespace ulm;
+
+extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float* g, float* q, float* c, void* qop,
+                                    void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M,
+                                    void* stream) {
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
+  if (B == 0 || T == 0 || M == 0) return ULM_OK;
+  ULM_REQUIRE(r && w && g && q && c && qop && kop, "null pointer argument");
+  ULM_REQUIRE(ld_op >= M, "ld_op (%lld) < M (%lld)", (long long)ld_op, (long long)M);
+  ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+  dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (op_dtype == ULM_BF16)
+    stats_fwd_kernel<__nv_bfloat16><<<grid, STATS_THREADS, 0, st>>>(r, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
+  else
+    stats_fwd_kernel<float><<<grid, STATS_THREADS, 0, st>>>(r, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
+  ULM_LAUNCH_CHECK("stats_fwd_kernel");
+  return ULM_OK;
+}
+
+extern "C" int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M) {
+  (void)T;
+  const int64_t groups = cdiv(M, 32);
+  const int64_t dw_bytes = ((B * M * 4 + 255) / 256) * 256;
+  return dw_bytes + B * groups * 8;
+}
+
+extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk, const float* q,
+                                    const float* c, const float* r, const float* w, const float* g, float* dr,
+                                    float* dw, float* dg, void* partial, int64_t B, int64_t T, int64_t M,
+                                    void* stream) {
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
+  ULM_REQUIRE(dw && dg, "null dw/dg");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || T == 0 || M == 0) {
+    if (M > 0) ULM_CUDA_TRY(cudaMemsetAsync(dw, 0, M * sizeof(float), st));
+    ULM_CUDA_TRY(cudaMemsetAsync(dg, 0, sizeof(float), st));
+    return ULM_OK;
+  }
+  ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr && partial, "null pointer argument");
+  ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+  const int64_t groups = cdiv(M, 32);
+  float* part_dw = static_cast<float*>(partial);
+  double* part_dg = reinterpret_cast<double*>(static_cast<char*>(partial) + ((B * M * 4 + 255) / 256) * 256);
+  dim3 grid((unsigned)groups, (unsigned)B);
+  stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, part_dw, part_dg, (int)T,
+                                                   (int)M);
+  ULM_LAUNCH_CHECK("stats_bwd_kernel");
+  stats_bwd_finalize_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(part_dw, part_dg, dw, dg, (int)B, (int)M,
+                                                                     (int)groups);
+  ULM_LAUNCH_CHECK("stats_bwd_finalize_kernel");
+  return ULM_OK;
+}

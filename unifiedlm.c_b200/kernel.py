@@ -1,0 +1,146 @@
+"""Drop-in replacement of the reference's kernel.py: UnifiedBlock's fast memory on sm_100a.
+
+unified_memory(r, v, g, w) -> (q, fast), for every batch row and position t (kernel.py:1-15):
+
+    k_t    = r_{t-1}                                     (k_0 = 0, write address)
+    c_t    = w + sum_{s<=t} lam^(t-s) k_s                (slot evidence mass, lam = exp(g))
+    q_t    = r_t / c_t
+    fast_t = sum_{s<=t} lam^(t-s) (q_t . k_s) v_s
+
+Same names, argument meaning, dtypes and gradients as the reference (kernel.py:199-238): r any float
+(computed in fp32), v (B,T,D), g a 0-d tensor (log decay), w (M,); q is fp32, fast has v's dtype;
+the backward returns (dr fp32, dv in dfast's dtype, dg 0-d, dw (M,) fp32).
+
+The work runs in libulm_b200.so (include/ulm_b200.h) on the current CUDA stream, through two
+`torch.library` custom ops (`ulm::memory_fwd`, `ulm::memory_bwd`) with fake kernels, so the call is
+traceable by torch.compile. `precision="bf16"` (default) contracts bf16 operands on the tensor
+cores with fp32 accumulation like the reference; `precision="fp32"` contracts in fp32 for 1e-5
+parity. There is no CPU path: CPU tensors or a missing library raise.
+"""
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+
+CHUNK = 64  # the reference's chunk length (kernel.py:20); the products here span whole sequences
+
+PRECISION = {"bf16": L.ULM_PREC_BF16, "fp32": L.ULM_PREC_FP32}
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("unified_memory runs on CUDA tensors only (no CPU path)")
+
+
+def operand_ld(n):
+    return (n + 7) // 8 * 8
+
+
+def _op_dtype(precision):
+    return torch.float32 if precision == L.ULM_PREC_FP32 else torch.bfloat16
+
+
+@torch.library.custom_op("ulm::memory_fwd", mutates_args=())
+def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tensor, precision: int
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                          torch.Tensor]:
+    """Returns (q, fast, c, qop, kop, vop, P); the last five are saved for the backward."""
+    _require_cuda(r, v, g, w)
+    B, T, M = r.shape
+    D = v.shape[-1]
+    dev = r.device
+    opt = _op_dtype(precision)
+    q = torch.empty(B, T, M, device=dev, dtype=torch.float32)
+    c = torch.empty_like(q)
+    fast = torch.empty(B, T, D, device=dev, dtype=v.dtype)
+    qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
+    kop = torch.empty_like(qop)
+    vop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    with torch.cuda.device(dev):
+        L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w), L.ptr(q),
+                                       L.ptr(fast), L.ptr(c), L.ptr(qop), L.ptr(kop), L.ptr(vop), L.ptr(P),
+                                       B, T, M, D, precision, L.stream_of(r)))
+    return q, fast, c, qop, kop, vop, P
+
+
+@memory_fwd.register_fake
+def _memory_fwd_fake(r, v, g, w, precision):
+    B, T, M = r.shape
+    D = v.shape[-1]
+    opt = _op_dtype(precision)
+    return (r.new_empty(B, T, M, dtype=torch.float32), v.new_empty(B, T, D), r.new_empty(B, T, M, dtype=torch.float32),
+            r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
+            r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
+
+
+@torch.library.custom_op("ulm::memory_bwd", mutates_args=())
+def memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, r: torch.Tensor, g: torch.Tensor,
+               w: torch.Tensor, q: torch.Tensor, c: torch.Tensor, qop: torch.Tensor, kop: torch.Tensor,
+               vop: torch.Tensor, P: torch.Tensor, precision: int
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dr, dv, dg, dw) (kernel.py:216-233)."""
+    _require_cuda(dfast, r, g, w, q, c)
+    B, T, M = r.shape
+    D = dfast.shape[-1]
+    dev = r.device
+    opt = _op_dtype(precision)
+    dr = torch.empty(B, T, M, device=dev, dtype=torch.float32)
+    dv = torch.empty(B, T, D, device=dev, dtype=dfast.dtype)
+    dg = torch.empty((), device=dev, dtype=torch.float32)
+    dw = torch.empty(M, device=dev, dtype=torch.float32)
+    doop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
+    dk = torch.empty_like(dqf)
+    partial = torch.empty(int(L.lib().ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        L.check(L.lib().ulm_memory_bwd(L.ptr(dq_out), L.ptr(dfast), L.dtype_code(dfast.dtype), L.ptr(r), L.ptr(g),
+                                       L.ptr(w), L.ptr(q), L.ptr(c), L.ptr(qop), L.ptr(kop), L.ptr(vop), L.ptr(P),
+                                       L.ptr(doop), L.ptr(dS), L.ptr(dqf), L.ptr(dk), L.ptr(partial), L.ptr(dr),
+                                       L.ptr(dv), L.ptr(dg), L.ptr(dw), B, T, M, D, precision, L.stream_of(r)))
+    return dr, dv, dg, dw
+
+
+@memory_bwd.register_fake
+def _memory_bwd_fake(dq_out, dfast, r, g, w, q, c, qop, kop, vop, P, precision):
+    B, T, M = r.shape
+    return (r.new_empty(B, T, M, dtype=torch.float32), dfast.new_empty(dfast.shape),
+            r.new_empty((), dtype=torch.float32), r.new_empty(M, dtype=torch.float32))
+
+
+def _setup_context(ctx, inputs, output):
+    r, v, g, w, precision = inputs
+    q, fast, c, qop, kop, vop, P = output
+    ctx.save_for_backward(r, g, w, q, c, qop, kop, vop, P)
+    ctx.precision = precision
+    ctx.v_dtype = v.dtype
+    ctx.v_dim = v.shape[-1]
+    ctx.g_shape = g.shape
+    ctx.mark_non_differentiable(c, qop, kop, vop, P)
+
+
+def _backward(ctx, dq_out, dfast, *unused):
+    r, g, w, q, c, qop, kop, vop, P = ctx.saved_tensors
+    if dfast is None:
+        dfast = torch.zeros(q.shape[0], q.shape[1], ctx.v_dim, device=q.device, dtype=ctx.v_dtype)
+    dr, dv, dg, dw = memory_bwd(None if dq_out is None else dq_out.float().contiguous(), dfast.contiguous(),
+                                r, g, w, q, c, qop, kop, vop, P, ctx.precision)
+    return dr, dv.to(ctx.v_dtype), dg.reshape(ctx.g_shape), dw, None
+
+
+torch.library.register_autograd("ulm::memory_fwd", _backward, setup_context=_setup_context)
+
+
+def unified_memory(r, v, g, w, precision="bf16"):
+    """r: (B,T,M) read addresses, v: (B,T,D) values, g: scalar log decay, w: (M,) prior mass.
+    Returns (q fp32 (B,T,M), fast (B,T,D) in v's dtype)."""
+    prec = PRECISION[precision]
+    out_dtype = v.dtype
+    vv = v if v.dtype in (torch.float32, torch.bfloat16) else v.float()
+    g1 = g.float().reshape(())
+    q, fast, *_ = torch.ops.ulm.memory_fwd(r.float().contiguous(), vv.contiguous(), g1,
+                                           w.float().contiguous(), prec)
+    return q, fast.to(out_dtype)
