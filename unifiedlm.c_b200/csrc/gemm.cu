@@ -23,17 +23,57 @@ namespace ulm {
 // ------------------------------------------------------------------------------------------------
 // epilogue: one thread owns one output row segment of 32 columns
 
+// 32 consecutive elements of an aux row (the forward's scores) as floats; zero past `ncols`.
+__device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row, int col0, int ncols,
+                                           float (&p)[32]) {
+  const int64_t off = (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
+  if (e.out_dtype == ULM_F32) {
+    const float* a = reinterpret_cast<const float*>(e.aux) + off;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) p[i] = i < ncols ? a[i] : 0.f;
+  } else {
+    const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(e.aux) + off;
+    if (ncols == 32 && e.vec_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const uint4 pk = *reinterpret_cast<const uint4*>(a + i);
+        const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          __nv_bfloat162 h;
+          memcpy(&h, &w4[j], 4);
+          const float2 f = __bfloat1622float2(h);
+          p[i + 2 * j] = f.x;
+          p[i + 2 * j + 1] = f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[i] = i < ncols ? __bfloat162float(a[i]) : 0.f;
+    }
+  }
+}
+
 __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const GemmShape& s, float gl2, int b,
-                                                 int row, int col0, float (&v)[32]) {
+                                                 int row, int col0, float (&v)[32], float& dg_acc) {
   if (row >= s.M || col0 >= s.N) return;
-  if (e.kind == EPI_DECAY) {
+  const int ncols = min(32, s.N - col0);
+  if (e.kind == EPI_DECAY_DG) {
+    float p[32];
+    load_aux32(e, b, row, col0, ncols, p);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int lag = row - (col0 + i);
+      if (lag > 0) dg_acc = fmaf((float)lag * p[i], v[i], dg_acc);
+    }
+  }
+  if (e.kind != EPI_STORE) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int lag = row - (col0 + i);
       v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
     }
   }
-  const int ncols = min(32, s.N - col0);
   const int64_t off = (int64_t)b * e.out_bstride + (int64_t)row * e.ldo + col0;
   if (e.out_dtype == ULM_F32) {
     float* o = reinterpret_cast<float*>(e.out) + off;
@@ -265,7 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
-    const float gl2 = (epi.kind == EPI_DECAY) ? (*epi.g) * 1.4426950408889634f : 0.f;
+    const float gl2 = (epi.kind != EPI_STORE) ? (*epi.g) * 1.4426950408889634f : 0.f;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
       const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
@@ -275,15 +315,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
       const int row = tc.mb * TC_BM + row_in_tile;
       const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      float dg_acc = 0.f;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float v[32];
         tmem_ld_32x32(taddr + (uint32_t)c, v);
-        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v);
+        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (epi.kind == EPI_DECAY_DG) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
+        if (lane == 0) epi.tile_partial[4 * (int64_t)t + (warp - 2)] = dg_acc;
+      }
     }
   }
 
@@ -348,7 +394,8 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
-  const float g = (epi.kind == EPI_DECAY) ? *epi.g : 0.f;
+  const float g = (epi.kind != EPI_STORE) ? *epi.g : 0.f;
+  float dg_acc = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int row = tc.mb * BM + ty + 16 * i;
@@ -358,13 +405,29 @@ __global__ void __launch_bounds__(256)
       const int col = tc.nb * BN + tx + 16 * jj;
       if (col >= shape.N) continue;
       float v = acc[i][jj];
-      if (epi.kind == EPI_DECAY) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
+      if (epi.kind == EPI_DECAY_DG && col < row) {
+        const float p = reinterpret_cast<const float*>(epi.aux)[(int64_t)tc.b * epi.aux_bstride +
+                                                                (int64_t)row * epi.ld_aux + col];
+        dg_acc = fmaf((float)(row - col) * p, v, dg_acc);
+      }
+      if (epi.kind != EPI_STORE) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
       const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
       if (epi.out_dtype == ULM_F32)
         reinterpret_cast<float*>(epi.out)[off] = v;
       else
         reinterpret_cast<__nv_bfloat16*>(epi.out)[off] = __float2bfloat16_rn(v);
     }
+  }
+  if (epi.kind == EPI_DECAY_DG) {
+    // fixed-order block reduction, one partial per tile (slots 1..3 of the tile are zero)
+    __shared__ float red[256];
+    red[threadIdx.x] = dg_acc;
+    __syncthreads();
+    for (int stride = 128; stride > 0; stride >>= 1) {
+      if ((int)threadIdx.x < stride) red[threadIdx.x] += red[threadIdx.x + stride];
+      __syncthreads();
+    }
+    if (threadIdx.x < 4) epi.tile_partial[4 * (int64_t)blockIdx.x + threadIdx.x] = threadIdx.x == 0 ? red[0] : 0.f;
   }
 }
 
@@ -469,7 +532,8 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
   ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
   ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
   ULM_REQUIRE(e.out_dtype == ULM_F32 || e.out_dtype == ULM_BF16, "bad output dtype");
-  ULM_REQUIRE(e.kind != EPI_DECAY || e.g, "decay epilogue needs g");
+  ULM_REQUIRE(e.kind == EPI_STORE || e.g, "decay epilogue needs g");
+  ULM_REQUIRE(e.kind != EPI_DECAY_DG || (e.aux && e.tile_partial), "EPI_DECAY_DG needs aux and tile_partial");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
     ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
   if (s.batches == 0 || s.M == 0 || s.N == 0) return ULM_OK;

@@ -8,8 +8,9 @@
 //   CAUSAL_NLOWER : only tiles with columns n <= rows m (decayed scores, s <= t)
 //   CAUSAL_KLOWER : the k range of a row block stops at the block's last row (forward read)
 //   CAUSAL_KUPPER : the k range of a row block starts at the block's first row (reversed read)
-// and a fused epilogue writes the tile (EPI_STORE) or the decayed causal score
-// lam^(m-n) * acc masked to n <= m (EPI_DECAY).
+// and a fused epilogue writes the tile (EPI_STORE), the decayed causal score lam^(m-n) * acc
+// masked to n <= m (EPI_DECAY), or that score plus the per-tile partial of
+// sum (m-n) * aux[m][n] * acc[m][n] (EPI_DECAY_DG, the score gradient's share of d/dg).
 //
 // Two back ends share the tile decomposition: a tcgen05/TMA/TMEM tensor-core kernel for bf16
 // operands (fp32 accumulation) and an fp32 FMA kernel for the 1e-5 parity mode.
@@ -20,7 +21,7 @@
 namespace ulm {
 
 enum { CAUSAL_NONE = 0, CAUSAL_KLOWER = 1, CAUSAL_KUPPER = 2, CAUSAL_NLOWER = 3 };
-enum { EPI_STORE = 0, EPI_DECAY = 1 };
+enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2 };
 
 struct GemmShape {
   int batches, M, N, K;
@@ -33,8 +34,14 @@ struct GemmEpilogue {
   void* out;
   int64_t ldo;         // row stride of the output, elements
   int64_t out_bstride; // batch stride of the output, elements
-  const float* g;      // log decay (device scalar), EPI_DECAY only
-  int vec_ok;          // output rows are 16-byte aligned for every tile (set by the host)
+  const float* g;      // log decay (device scalar), EPI_DECAY / EPI_DECAY_DG
+  int vec_ok;          // output and aux rows are 16-byte aligned for every tile (set by the host)
+  // EPI_DECAY_DG: aux = the forward's decayed scores P (same layout and type as the output); each
+  // epilogue warp adds sum (m-n) * P[m][n] * acc[m][n] over its rows of a tile and writes it to
+  // tile_partial[4 * tile + warp] (d/dg of the fast read, no atomics)
+  const void* aux;
+  int64_t ld_aux, aux_bstride;
+  float* tile_partial;
 };
 
 // A matrix operand in global memory: element (b, row, col) of its storage order at
@@ -91,6 +98,12 @@ inline int tiles_per_batch_host(const GemmShape& s, int BM, int BN, int m_blocks
   int n = 0;
   for (int mb = 0; mb < m_blocks; ++mb) n += nlower_tiles_in_row(mb, BM, BN, n_blocks);
   return n;
+}
+
+// Upper bound of tile_partial entries an EPI_DECAY_DG launch over (batches, T x T) writes.
+inline int64_t decay_dg_partials(int64_t batches, int64_t T) {
+  const int64_t b = (T + 63) / 64;
+  return 4 * batches * b * b;
 }
 
 // Host entry: validates, picks the back end from the operand types, launches on `stream`.

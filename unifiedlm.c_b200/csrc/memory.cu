@@ -63,6 +63,10 @@ GemmEpilogue make_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int6
   e.ldo = ldo;
   e.out_bstride = bstride;
   e.g = g;
+  e.aux = nullptr;
+  e.ld_aux = 0;
+  e.aux_bstride = 0;
+  e.tile_partial = nullptr;
   const int vec = out_dtype == ULM_F32 ? 4 : 8;
   e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
   return e;
@@ -198,11 +202,28 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
     ULM_CUDA_TRY(cudaMemsetAsync(dk, 0, B * T * M * sizeof(float), st));
   } else {
     if (int rc = convert_rows(dfast, do_dtype, D, doop, dt, ldd, B * T, D, st)) return rc;
-    // dS = D * (do v^T): gradient of the scores, same causal decay as the forward
-    if (int rc = ulm_decayed_scores(doop, ldd, vop, ldd, dS, ldt, g, B, T, D, prec, stream)) return rc;
+    // dS = D * (do v^T): gradient of the scores, same causal decay as the forward; its epilogue
+    // also sums (t-s) P dP per tile, the fast read's share of d/dg
+    StatsScratch sc = carve_stats_scratch(partial, B, M);
+    const int64_t n_tiles = decay_dg_partials(B, T);
+    ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
+    {
+      Operand A{doop, ldd, T * ldd, D, T, dt, false};
+      Operand Bo{vop, ldd, T * ldd, D, T, dt, false};
+      GemmShape s{(int)B, (int)T, (int)T, (int)D, CAUSAL_NLOWER};
+      GemmEpilogue e = make_epilogue(EPI_DECAY_DG, dt, dS, ldt, T * ldt, g);
+      e.aux = P;
+      e.ld_aux = ldt;
+      e.aux_bstride = T * ldt;
+      e.tile_partial = sc.tiles;
+      e.vec_ok = e.vec_ok && is_aligned16(P);
+      if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
+    }
     if (int rc = ulm_causal_apply(dS, ldt, kop, ldm, dqf, M, ULM_F32, 0, B, T, M, prec, stream)) return rc;
     if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
     if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
+    ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+    return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles, n_tiles, st);
   }
   return ulm_memory_stats_bwd(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
 }

@@ -7,7 +7,7 @@
 // the segment's end value; the carries are combined in shared memory (lam^len per segment); pass 2
 // rescans with the true carry and writes the outputs. The second read of r hits L2 (a CTA's slice
 // is at most 32 x T x 4 bytes).
-#include "common.cuh"
+#include "gemm.cuh"
 
 namespace ulm {
 
@@ -85,17 +85,21 @@ __global__ void __launch_bounds__(STATS_THREADS)
 // kernel.py:139-180 and :232. With dq = dqf + dq_out, walking time backwards:
 //   dc_t = -dq_t q_t / c_t,  dkc_t = dc_t + lam dkc_{t+1}  (gradient reaching k through c)
 //   dkt_t = dk_t + dkc_t,    dr_t = dq_t / c_t + dkt_{t+1}  (k_{t+1} = r_t)
-//   dw += dc_t,  dg += (t - t_mid) (q.dqf - k.dk + dc (c - w) - k.dkc)
+//   dw += dc_t,  dg += (t - t_mid) (dc (c - w) - k.dkc)                      (through c)
+//               dg += (t - t_mid) (q.dqf - k.dk)        (through the fast read, if fast_identity)
 // The position weight is centred at t_mid = (T-1)/2: the unweighted sums of q.dqf - k.dk and of
 // dc (c - w) - k.dkc are both zero (each pair is the same double sum over (t, s)), so centring
-// leaves dg unchanged and keeps the fp32 terms small. Partial sums go to `partial` (per batch row
-// and slot for dw, per batch row and slot group for dg, in double) and are reduced in a fixed
-// order by stats_bwd_finalize_kernel.
+// leaves dg unchanged and keeps the fp32 terms small. The fast-read share by this identity is a
+// difference of two large sums of the products' outputs; with bf16 products it loses about one
+// digit, so the operator computes that share directly from the scores instead
+// (EPI_DECAY_DG in gemm.cu) and runs this kernel with fast_identity = false. Partial sums go to
+// `partial` (per batch row and slot for dw; per batch row and slot group for dg, in double) and
+// are reduced in a fixed order by the finalize kernels.
 __global__ void __launch_bounds__(STATS_THREADS)
     stats_bwd_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out, const float* __restrict__ dk,
                      const float* __restrict__ q, const float* __restrict__ c, const float* __restrict__ r,
                      const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ dr,
-                     float* __restrict__ part_dw, double* __restrict__ part_dg, int T, int M) {
+                     float* __restrict__ part_dw, double* __restrict__ part_dg, int T, int M, int fast_identity) {
   __shared__ float seg_start[STATS_SEGS][32];
   __shared__ double red_dg[STATS_THREADS];
   __shared__ float red_dw[STATS_SEGS][32];
@@ -152,7 +156,8 @@ __global__ void __launch_bounds__(STATS_THREADS)
       const float dkt = dkv + run;
       dr[i] = dq / cc + dkt_next;
       dkt_next = dkt;
-      const float term = qq * dqfv - kt * dkv + dc * (cc - wm) - kt * run;
+      float term = dc * (cc - wm) - kt * run;
+      if (fast_identity) term += qq * dqfv - kt * dkv;
       dg_acc += (double)(((float)t - t_mid) * term);
       dw_acc += dc;
     }
@@ -172,20 +177,72 @@ __global__ void __launch_bounds__(STATS_THREADS)
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
 }
 
-// dw[m] = sum_b part_dw[b][m]; dg = sum over (b, slot group) of part_dg, both in index order.
-__global__ void stats_bwd_finalize_kernel(const float* __restrict__ part_dw, const double* __restrict__ part_dg,
-                                          float* __restrict__ dw, float* __restrict__ dg, int B, int M, int groups) {
+// dw[m] = sum_b part_dw[b][m], in batch order.
+__global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int B, int M) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m < M) {
     float s = 0.f;
     for (int b = 0; b < B; ++b) s += part_dw[(int64_t)b * M + m];
     dw[m] = s;
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    double s = 0.0;
-    for (int i = 0; i < B * groups; ++i) s += part_dg[i];
-    *dg = (float)s;
+}
+
+// dg = sum of part_dg (n1 doubles) + sum of extra (n2 floats): one block, every thread sums a fixed
+// strided subset in order, then a fixed-shape tree. Deterministic for given inputs.
+__global__ void __launch_bounds__(256)
+    stats_bwd_dg_kernel(const double* __restrict__ part_dg, int64_t n1, const float* __restrict__ extra, int64_t n2,
+                        float* __restrict__ dg) {
+  __shared__ double red[256];
+  double s = 0.0;
+  for (int64_t i = threadIdx.x; i < n1; i += 256) s += part_dg[i];
+  for (int64_t i = threadIdx.x; i < n2; i += 256) s += (double)extra[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) red[threadIdx.x] += red[threadIdx.x + stride];
+    __syncthreads();
   }
+  if (threadIdx.x == 0) *dg = (float)red[0];
+}
+
+// scratch layout: [part_dw: B*M float][part_dg: B*groups double][tile partials: n float]
+struct StatsScratch {
+  float* part_dw;
+  double* part_dg;
+  float* tiles;
+};
+
+inline int64_t align256(int64_t n) { return (n + 255) / 256 * 256; }
+
+inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
+  const int64_t groups = cdiv(M, 32);
+  char* p = static_cast<char*>(base);
+  StatsScratch s;
+  s.part_dw = reinterpret_cast<float*>(p);
+  p += align256(B * M * 4);
+  s.part_dg = reinterpret_cast<double*>(p);
+  p += align256(B * groups * 8);
+  s.tiles = reinterpret_cast<float*>(p);
+  return s;
+}
+
+// Shared by the public statistics backward (fast_identity = 1, the reference's K5 semantics) and
+// the operator backward (fast_identity = 0, tile partials of the score epilogue added instead).
+int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
+                  const float* r, const float* w, const float* g, float* dr, float* dw, float* dg, void* partial,
+                  int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials, int64_t n_tiles,
+                  cudaStream_t st) {
+  const int64_t groups = cdiv(M, 32);
+  StatsScratch sc = carve_stats_scratch(partial, B, M);
+  dim3 grid((unsigned)groups, (unsigned)B);
+  stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw, sc.part_dg,
+                                                   (int)T, (int)M, fast_identity);
+  ULM_LAUNCH_CHECK("stats_bwd_kernel");
+  stats_bwd_dw_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(sc.part_dw, dw, (int)B, (int)M);
+  ULM_LAUNCH_CHECK("stats_bwd_dw_kernel");
+  stats_bwd_dg_kernel<<<1, 256, 0, st>>>(sc.part_dg, B * groups, tile_partials, tile_partials ? n_tiles : 0, dg);
+  ULM_LAUNCH_CHECK("stats_bwd_dg_kernel");
+  return ULM_OK;
 }
 
 }  // namespace ulm
@@ -212,10 +269,9 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
 }
 
 extern "C" int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M) {
-  (void)T;
+  if (B < 0 || T < 0 || M < 0) return -1;
   const int64_t groups = cdiv(M, 32);
-  const int64_t dw_bytes = ((B * M * 4 + 255) / 256) * 256;
-  return dw_bytes + B * groups * 8;
+  return align256(B * M * 4) + align256(B * groups * 8) + align256(decay_dg_partials(B, T) * 4);
 }
 
 extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk, const float* q,
@@ -232,15 +288,5 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
   }
   ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr && partial, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
-  const int64_t groups = cdiv(M, 32);
-  float* part_dw = static_cast<float*>(partial);
-  double* part_dg = reinterpret_cast<double*>(static_cast<char*>(partial) + ((B * M * 4 + 255) / 256) * 256);
-  dim3 grid((unsigned)groups, (unsigned)B);
-  stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, part_dw, part_dg, (int)T,
-                                                   (int)M);
-  ULM_LAUNCH_CHECK("stats_bwd_kernel");
-  stats_bwd_finalize_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(part_dw, part_dg, dw, dg, (int)B, (int)M,
-                                                                     (int)groups);
-  ULM_LAUNCH_CHECK("stats_bwd_finalize_kernel");
-  return ULM_OK;
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
 }

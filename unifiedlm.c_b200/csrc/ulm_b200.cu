@@ -1,5 +1,5 @@
 // Single translation unit of the library: the kernels share one device-side error flag, so they
 // are compiled together (no relocatable device code needed).
-#include "memory.cu"
 #include "gemm.cu"
 #include "stats.cu"
+#include "memory.cu"
