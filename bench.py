@@ -75,7 +75,7 @@ class ClockSampler:
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                                         stdout=open(self.path, "w"), stderr=subprocess.PIPE, text=True)
         except Exception:
             self.proc = None
         return self
@@ -91,6 +91,7 @@ class ClockSampler:
     def summary(self):
         if self.proc is None or not self.path:
             return None
+        err = self.proc.stderr.read() if self.proc.stderr else ""
         rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
@@ -100,9 +101,10 @@ class ClockSampler:
                 rows.append(parts)
             except Exception:
                 pass
+        raw = open(self.path).read()
         os.unlink(self.path)
         if not rows:
-            return None
+            return {"error": (err or raw)[-300:]}
         sm = [float(p[1]) for p in rows if p[1].replace(".", "").isdigit()]
         mx = [float(p[2]) for p in rows if p[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -207,6 +209,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -240,6 +244,13 @@ def main():
             dist.all_reduce(grads)
         return grads
 
+    if args.profile_step:
+        step(r, v, dq_out, dfast)
+        step(r, v, dq_out, dfast)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return
     for _ in range(args.warmup):
         step(r, v, dq_out, dfast)
     torch.cuda.synchronize()

@@ -177,3 +177,40 @@ def test_full_size_properties():
                                      w.double().cpu())
     assert rel(q[:1], q_ref) < 1e-5 and rel(f1[:1], fast_ref) < 1e-2
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("T", [37, 1500, 2500])
+def test_stats_kernels_through_c_abi(T):
+    """ulm_memory_stats_fwd / ulm_memory_stats_bwd (the reference's K1 / K5 interface, with the dg
+    identity) against the oracle, on both the register-resident and the two-pass scan paths."""
+    B, M, D = 2, 40, 16
+    r, v, g, w, dq_out, dfast = make_inputs(B, T, M, D, lam=0.99, seed=7)
+    k, c_ref, q_ref = O.memory_stats(r, g, w)
+    Dm = O.decay_matrix(T, g)
+    dS = (dfast @ v.transpose(1, 2)) * Dm
+    dqf_ref, dk_ref = dS @ k, dS.transpose(1, 2) @ q_ref
+    dr_ref, _, dg_ref, dw_ref = O.memory_grads(r, v, g, w, dq_out, dfast, form="dense")
+    lib = L.lib()
+    cu = lambda x: x.float().to(DEV).contiguous()  # noqa: E731
+    rr, gg, ww = cu(r), cu(g).reshape(1), cu(w)
+    q = torch.empty(B, T, M, device=DEV)
+    c = torch.empty_like(q)
+    qop = torch.empty(B, T, operand_ld(M), device=DEV)
+    kop = torch.empty_like(qop)
+    st = L.stream_of(q)
+    L.check(lib.ulm_memory_stats_fwd(L.ptr(rr), L.ptr(ww), L.ptr(gg), L.ptr(q), L.ptr(c), L.ptr(qop), L.ptr(kop),
+                                     L.ULM_F32, operand_ld(M), B, T, M, st))
+    torch.cuda.synchronize()
+    assert rel(q, q_ref) < 1e-6 and rel(c, c_ref) < 1e-6
+    assert torch.equal(qop[..., :M], q) and rel(kop[..., :M], k) == 0.0
+    dr = torch.empty_like(q)
+    dw = torch.empty(M, device=DEV)
+    dg = torch.empty(1, device=DEV)
+    part = torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=DEV, dtype=torch.uint8)
+    L.check(lib.ulm_memory_stats_bwd(L.ptr(cu(dqf_ref)), L.ptr(cu(dq_out)), L.ptr(cu(dk_ref)), L.ptr(q), L.ptr(c),
+                                     L.ptr(rr), L.ptr(ww), L.ptr(gg), L.ptr(dr), L.ptr(dw), L.ptr(dg), L.ptr(part),
+                                     B, T, M, st))
+    torch.cuda.synchronize()
+    assert rel(dr, dr_ref) < 1e-5 and rel(dw, dw_ref) < 1e-5, (rel(dr, dr_ref), rel(dw, dw_ref))
+    assert rel(dg, dg_ref.reshape(1)) < 1e-4, rel(dg, dg_ref.reshape(1))
+    assert L.device_error() == 0

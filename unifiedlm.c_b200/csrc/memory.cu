@@ -87,9 +87,58 @@ __global__ void convert_rows_kernel(const void* __restrict__ src, int src_dtype,
   }
 }
 
+// 8 consecutive elements per thread with 16-byte loads and stores
+__global__ void convert_rows_vec8_kernel(const void* __restrict__ src, int src_dtype, int64_t lds,
+                                         void* __restrict__ dst, int dst_dtype, int64_t ldd, int64_t rows,
+                                         int64_t cols8) {
+  const int64_t n = rows * cols8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rr = i / cols8, cc = (i - rr * cols8) * 8;
+    float v[8];
+    if (src_dtype == ULM_F32) {
+      const float4* s4 = reinterpret_cast<const float4*>(static_cast<const float*>(src) + rr * lds + cc);
+      const float4 a = s4[0], b = s4[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+      const uint4 pk = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(src) + rr * lds + cc);
+      const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h;
+        memcpy(&h, &w4[j], 4);
+        const float2 f = __bfloat1622float2(h);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+      }
+    }
+    if (dst_dtype == ULM_F32) {
+      float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(dst) + rr * ldd + cc);
+      d4[0] = make_float4(v[0], v[1], v[2], v[3]);
+      d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      uint4 pk;
+      uint32_t w4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        memcpy(&w4[j], &h, 4);
+      }
+      pk.x = w4[0]; pk.y = w4[1]; pk.z = w4[2]; pk.w = w4[3];
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(dst) + rr * ldd + cc) = pk;
+    }
+  }
+}
+
 int convert_rows(const void* src, int sdt, int64_t lds, void* dst, int ddt, int64_t ldd, int64_t rows, int64_t cols,
                  cudaStream_t st) {
   if (rows * cols == 0) return ULM_OK;
+  if (cols % 8 == 0 && lds % 8 == 0 && ldd % 8 == 0 && is_aligned16(src) && is_aligned16(dst)) {
+    const int64_t blocks = cdiv(rows * (cols / 8), 256);
+    const unsigned grid = (unsigned)(blocks < 16 * 148 ? blocks : 16 * 148);
+    convert_rows_vec8_kernel<<<grid, 256, 0, st>>>(src, sdt, lds, dst, ddt, ldd, rows, cols / 8);
+    ULM_LAUNCH_CHECK("convert_rows_vec8_kernel");
+    return ULM_OK;
+  }
   const int64_t blocks = cdiv(rows * cols, 256);
   const unsigned grid = (unsigned)(blocks < 8 * 148 ? blocks : 8 * 148);
   convert_rows_kernel<<<grid, 256, 0, st>>>(src, sdt, lds, dst, ddt, ldd, rows, cols);

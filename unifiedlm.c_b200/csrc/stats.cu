@@ -177,6 +177,171 @@ __global__ void __launch_bounds__(STATS_THREADS)
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
 }
 
+// ---- register-resident single-pass scans (T <= 64 * SEG) ---------------------------------------
+// A CTA owns SLOTS consecutive slots of one batch row and the whole sequence: thread (seg, slot)
+// keeps its SEG positions in registers, so every array is read from HBM exactly once. Segment
+// sums meet in shared memory; each thread then finishes its segment from its registers.
+
+template <int SEG, int SLOTS, typename OpT>
+__global__ void __launch_bounds__(1024)
+    stats_fwd_reg_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
+                         float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
+                         void* __restrict__ kop, int64_t ldop, int T, int M) {
+  extern __shared__ float seg_sum[];  // [nseg][SLOTS]
+  const int slot = threadIdx.x % SLOTS, seg = threadIdx.x / SLOTS;
+  const int nseg = blockDim.x / SLOTS;
+  const int b = blockIdx.y;
+  const int m = blockIdx.x * SLOTS + slot;
+  const bool valid = m < M;
+  const int t0 = seg * SEG;
+  const float gg = *g;
+  const float lam = expf(gg);
+  const int64_t row0 = (int64_t)b * T;
+  const float* rb = r + row0 * M + m;
+  float rv[SEG];
+  const float kfirst = (valid && t0 > 0 && t0 <= T) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
+#pragma unroll
+  for (int i = 0; i < SEG; ++i) rv[i] = (valid && t0 + i < T) ? rb[(int64_t)(t0 + i) * M] : 0.f;
+  float run = 0.f, kk = kfirst;
+#pragma unroll
+  for (int i = 0; i < SEG; ++i) {
+    run = fmaf(lam, run, kk);
+    kk = rv[i];
+  }
+  seg_sum[seg * SLOTS + slot] = run;
+  __syncthreads();
+  const float lam_seg = expf(gg * (float)SEG);
+  float carry = 0.f;
+  for (int j = 0; j < seg && j < nseg; ++j) carry = fmaf(carry, lam_seg, seg_sum[j * SLOTS + slot]);
+  if (!valid) return;
+  const float wm = w[m];
+  run = carry;
+  kk = kfirst;
+#pragma unroll
+  for (int i = 0; i < SEG; ++i) {
+    const int t = t0 + i;
+    if (t < T) {
+      run = fmaf(lam, run, kk);
+      const float cc = wm + run;
+      const float qq = rv[i] / cc;
+      const int64_t idx = (row0 + t) * M + m;
+      q[idx] = qq;
+      c[idx] = cc;
+      const int64_t io = (row0 + t) * ldop + m;
+      store_op<OpT>(qop, io, qq);
+      store_op<OpT>(kop, io, kk);
+    }
+    kk = rv[i];
+  }
+}
+
+template <int SEG, int SLOTS>
+__global__ void __launch_bounds__(512, 1)
+    stats_bwd_reg_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out,
+                         const float* __restrict__ dk, const float* __restrict__ q, const float* __restrict__ c,
+                         const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
+                         float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int T,
+                         int M, int fast_identity) {
+  extern __shared__ float smem_f[];  // seg_sum[nseg][SLOTS], then dw_red[nseg][SLOTS]
+  __shared__ double red_dg[512];
+  const int slot = threadIdx.x % SLOTS, seg = threadIdx.x / SLOTS;
+  const int nseg = blockDim.x / SLOTS;
+  float* seg_sum = smem_f;
+  float* dw_red = smem_f + nseg * SLOTS;
+  const int b = blockIdx.y;
+  const int m = blockIdx.x * SLOTS + slot;
+  const bool valid = m < M;
+  const int t0 = seg * SEG;
+  const float gg = *g;
+  const float lam = expf(gg);
+  const int64_t base = (int64_t)b * T * M + m;
+  const bool has_dqo = dq_out != nullptr;
+  const float wm = valid ? w[m] : 0.f;
+  const float t_mid = 0.5f * (float)(T - 1);
+
+  // all loads up front: the scan inputs and the values the second half needs
+  float drd[SEG], dcv[SEG], dkv[SEG], kv[SEG];
+  float dw_acc = 0.f, dg_f = 0.f;
+#pragma unroll
+  for (int i = 0; i < SEG; ++i) {
+    const int t = t0 + i;
+    const bool in = valid && t < T;
+    const int64_t idx = base + (int64_t)t * M;
+    const float dqfv = in ? dqf[idx] : 0.f;
+    const float dq = dqfv + ((in && has_dqo) ? dq_out[idx] : 0.f);
+    const float cc = in ? c[idx] : 1.f;
+    const float qq = in ? q[idx] : 0.f;
+    dkv[i] = in ? dk[idx] : 0.f;
+    kv[i] = (in && t > 0) ? r[idx - M] : 0.f;
+    drd[i] = dq / cc;
+    dcv[i] = -drd[i] * qq;
+    dw_acc += dcv[i];
+    float term = dcv[i] * (cc - wm);
+    if (fast_identity) term += qq * dqfv;
+    dg_f = fmaf((float)t - t_mid, term, dg_f);
+  }
+  float run = 0.f;
+#pragma unroll
+  for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dcv[i]);
+  seg_sum[seg * SLOTS + slot] = run;
+  dw_red[seg * SLOTS + slot] = dw_acc;
+  __syncthreads();
+  const float lam_seg = expf(gg * (float)SEG);
+  float carry = 0.f;  // dkc at position t0 + SEG
+  for (int j = nseg - 1; j > seg; --j) carry = fmaf(carry, lam_seg, seg_sum[j * SLOTS + slot]);
+  double dg_acc = (double)dg_f;
+  if (valid) {
+    const int t_end = t0 + SEG;
+    float dkt_next = (t_end < T) ? dk[base + (int64_t)t_end * M] + carry : 0.f;
+    run = carry;
+    float dg_s = 0.f;
+#pragma unroll
+    for (int i = SEG - 1; i >= 0; --i) {
+      const int t = t0 + i;
+      if (t < T) {
+        run = fmaf(lam, run, dcv[i]);  // dkc_t
+        const float dkt = dkv[i] + run;
+        dr[base + (int64_t)t * M] = drd[i] + dkt_next;
+        dkt_next = dkt;
+        float term = -kv[i] * run;
+        if (fast_identity) term -= kv[i] * dkv[i];
+        dg_s = fmaf((float)t - t_mid, term, dg_s);
+      }
+    }
+    dg_acc += (double)dg_s;
+  }
+  if (seg == 0 && valid) {
+    float s2 = 0.f;
+    for (int j = 0; j < nseg; ++j) s2 += dw_red[j * SLOTS + slot];
+    part_dw[(int64_t)b * M + m] = s2;
+  }
+  red_dg[threadIdx.x] = dg_acc;
+  __syncthreads();
+  for (int stride = 256; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride && threadIdx.x + stride < blockDim.x) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
+}
+
+constexpr int FWD_SLOTS = 16;
+constexpr int BWD_SLOTS = 8;
+constexpr int REG_MAX_SEGS = 64;
+
+inline int pick_seg(int64_t T, int max_seg) {
+  for (int s = 8; s <= max_seg; s *= 2)
+    if (cdiv(T, s) <= REG_MAX_SEGS) return s;
+  return 0;
+}
+
+// threads of a register-scan CTA: SLOTS x nseg, nseg rounded so the CTA is whole warps
+inline int reg_threads(int64_t T, int seg, int slots) {
+  int nseg = (int)cdiv(T, seg);
+  const int per_warp = 32 / slots;
+  nseg = (int)cdiv(nseg, per_warp) * per_warp;
+  return nseg * slots;
+}
+
 // dw[m] = sum_b part_dw[b][m], in batch order.
 __global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int B, int M) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
@@ -215,7 +380,7 @@ struct StatsScratch {
 inline int64_t align256(int64_t n) { return (n + 255) / 256 * 256; }
 
 inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
-  const int64_t groups = cdiv(M, 32);
+  const int64_t groups = cdiv(M, 8);
   char* p = static_cast<char*>(base);
   StatsScratch s;
   s.part_dw = reinterpret_cast<float*>(p);
@@ -232,12 +397,28 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
                   const float* r, const float* w, const float* g, float* dr, float* dw, float* dg, void* partial,
                   int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials, int64_t n_tiles,
                   cudaStream_t st) {
-  const int64_t groups = cdiv(M, 32);
   StatsScratch sc = carve_stats_scratch(partial, B, M);
-  dim3 grid((unsigned)groups, (unsigned)B);
-  stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw, sc.part_dg,
-                                                   (int)T, (int)M, fast_identity);
-  ULM_LAUNCH_CHECK("stats_bwd_kernel");
+  int64_t groups;
+  const int seg = pick_seg(T, 16);
+  if (seg) {
+    groups = cdiv(M, BWD_SLOTS);
+    const int threads = reg_threads(T, seg, BWD_SLOTS);
+    const size_t smem = (size_t)2 * threads * sizeof(float);
+    dim3 grid((unsigned)groups, (unsigned)B);
+    if (seg == 8)
+      stats_bwd_reg_kernel<8, BWD_SLOTS><<<grid, threads, smem, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw,
+                                                                      sc.part_dg, (int)T, (int)M, fast_identity);
+    else
+      stats_bwd_reg_kernel<16, BWD_SLOTS><<<grid, threads, smem, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw,
+                                                                       sc.part_dg, (int)T, (int)M, fast_identity);
+    ULM_LAUNCH_CHECK("stats_bwd_reg_kernel");
+  } else {
+    groups = cdiv(M, 32);
+    dim3 grid((unsigned)groups, (unsigned)B);
+    stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw, sc.part_dg,
+                                                     (int)T, (int)M, fast_identity);
+    ULM_LAUNCH_CHECK("stats_bwd_kernel");
+  }
   stats_bwd_dw_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(sc.part_dw, dw, (int)B, (int)M);
   ULM_LAUNCH_CHECK("stats_bwd_dw_kernel");
   stats_bwd_dg_kernel<<<1, 256, 0, st>>>(sc.part_dg, B * groups, tile_partials, tile_partials ? n_tiles : 0, dg);
@@ -258,8 +439,32 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
   ULM_REQUIRE(ld_op >= M, "ld_op (%lld) < M (%lld)", (long long)ld_op, (long long)M);
   ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
-  dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int seg = pick_seg(T, 32);
+  if (seg) {
+    dim3 grid((unsigned)cdiv(M, FWD_SLOTS), (unsigned)B);
+    const int threads = reg_threads(T, seg, FWD_SLOTS);
+    const size_t smem = (size_t)threads * sizeof(float);
+    const bool bf = op_dtype == ULM_BF16;
+#define ULM_FWD_REG(S)                                                                                        \
+  if (bf)                                                                                                     \
+    stats_fwd_reg_kernel<S, FWD_SLOTS, __nv_bfloat16><<<grid, threads, smem, st>>>(r, w, g, q, c, qop, kop,   \
+                                                                                   ld_op, (int)T, (int)M);    \
+  else                                                                                                        \
+    stats_fwd_reg_kernel<S, FWD_SLOTS, float><<<grid, threads, smem, st>>>(r, w, g, q, c, qop, kop, ld_op,    \
+                                                                           (int)T, (int)M);
+    if (seg == 8) {
+      ULM_FWD_REG(8)
+    } else if (seg == 16) {
+      ULM_FWD_REG(16)
+    } else {
+      ULM_FWD_REG(32)
+    }
+#undef ULM_FWD_REG
+    ULM_LAUNCH_CHECK("stats_fwd_reg_kernel");
+    return ULM_OK;
+  }
+  dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
   if (op_dtype == ULM_BF16)
     stats_fwd_kernel<__nv_bfloat16><<<grid, STATS_THREADS, 0, st>>>(r, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
   else
@@ -270,7 +475,7 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
 
 extern "C" int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M) {
   if (B < 0 || T < 0 || M < 0) return -1;
-  const int64_t groups = cdiv(M, 32);
+  const int64_t groups = cdiv(M, 8);
   return align256(B * M * 4) + align256(B * groups * 8) + align256(decay_dg_partials(B, T) * 4);
 }
 
