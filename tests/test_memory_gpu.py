@@ -208,7 +208,8 @@ def test_stats_kernels_through_c_abi(T):
     dw = torch.empty(M, device=DEV)
     dg = torch.empty(1, device=DEV)
     part = torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=DEV, dtype=torch.uint8)
-    L.check(lib.ulm_memory_stats_bwd(L.ptr(cu(dqf_ref)), L.ptr(cu(dq_out)), L.ptr(cu(dk_ref)), L.ptr(q), L.ptr(c),
+    dqf_d, dqo_d, dk_d = cu(dqf_ref), cu(dq_out), cu(dk_ref)  # keep the device copies alive across the call
+    L.check(lib.ulm_memory_stats_bwd(L.ptr(dqf_d), L.ptr(dqo_d), L.ptr(dk_d), L.ptr(q), L.ptr(c),
                                      L.ptr(rr), L.ptr(ww), L.ptr(gg), L.ptr(dr), L.ptr(dw), L.ptr(dg), L.ptr(part),
                                      B, T, M, st))
     torch.cuda.synchronize()
