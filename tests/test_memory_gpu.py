@@ -201,7 +201,7 @@ def test_stats_kernels_through_c_abi(T):
     L.check(lib.ulm_memory_stats_fwd(L.ptr(rr), L.ptr(ww), L.ptr(gg), L.ptr(q), L.ptr(c), L.ptr(qop), L.ptr(kop),
                                      L.ULM_F32, operand_ld(M), B, T, M, st))
     torch.cuda.synchronize()
-    assert rel(q, q_ref) < 1e-6 and rel(c, c_ref) < 1e-6
+    assert rel(q, q_ref) < 1e-5 and rel(c, c_ref) < 1e-5
     assert torch.equal(qop[..., :M], q)
     assert torch.equal(kop[:, 1:, :M], rr[:, :-1]) and not kop[:, 0, :M].any()
     dr = torch.empty_like(q)
