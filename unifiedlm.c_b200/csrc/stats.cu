@@ -7,6 +7,8 @@
 // the segment's end value; the carries are combined in shared memory (lam^len per segment); pass 2
 // rescans with the true carry and writes the outputs. The second read of r hits L2 (a CTA's slice
 // is at most 32 x T x 4 bytes).
+#include <cooperative_groups.h>
+
 #include "gemm.cuh"
 
 namespace ulm {
@@ -177,23 +179,31 @@ __global__ void __launch_bounds__(STATS_THREADS)
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
 }
 
-// ---- register-resident single-pass scans (T <= 64 * SEG) ---------------------------------------
-// A CTA owns SLOTS consecutive slots of one batch row and the whole sequence: thread (seg, slot)
-// keeps its SEG positions in registers, so every array is read from HBM exactly once. Segment
-// sums meet in shared memory; each thread then finishes its segment from its registers.
+// ---- cluster scans (T <= 8 * WARPS * SEG): lanes = 32 consecutive slots -------------------------
+// A cluster of C CTAs owns 32 slots of one batch row and the whole sequence. CTA rank j covers
+// positions [j*WARPS*SEG, (j+1)*WARPS*SEG); its warp w covers SEG consecutive positions, lane = slot,
+// so every load and store of a warp is one contiguous 128-byte row segment. Each thread keeps its
+// SEG positions in registers (every array is read from HBM once). Segment sums are folded inside
+// the CTA through shared memory and across the cluster through distributed shared memory after a
+// hardware cluster barrier (no spin waits).
 
-template <int SEG, int SLOTS, typename OpT>
-__global__ void __launch_bounds__(1024)
-    stats_fwd_reg_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
-                         float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
-                         void* __restrict__ kop, int64_t ldop, int T, int M) {
-  extern __shared__ float seg_sum[];  // [nseg][SLOTS]
-  const int slot = threadIdx.x % SLOTS, seg = threadIdx.x / SLOTS;
-  const int nseg = blockDim.x / SLOTS;
+namespace cg = cooperative_groups;
+
+template <int SEG, int WARPS, typename OpT>
+__global__ void __launch_bounds__(32 * WARPS)
+    stats_fwd_cluster_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
+                             float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
+                             void* __restrict__ kop, int64_t ldop, int T, int M) {
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float cta_total[32];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int b = blockIdx.y;
-  const int m = blockIdx.x * SLOTS + slot;
+  const int m = (blockIdx.x / C) * 32 + lane;
   const bool valid = m < M;
-  const int t0 = seg * SEG;
+  const int t0 = (cr * WARPS + wp) * SEG;
   const float gg = *g;
   const float lam = expf(gg);
   const int64_t row0 = (int64_t)b * T;
@@ -208,50 +218,62 @@ __global__ void __launch_bounds__(1024)
     run = fmaf(lam, run, kk);
     kk = rv[i];
   }
-  seg_sum[seg * SLOTS + slot] = run;
+  warp_sum[wp][lane] = run;  // decayed sum over this segment, seen from its last position
   __syncthreads();
   const float lam_seg = expf(gg * (float)SEG);
-  float carry = 0.f;
-  for (int j = 0; j < seg && j < nseg; ++j) carry = fmaf(carry, lam_seg, seg_sum[j * SLOTS + slot]);
-  if (!valid) return;
-  const float wm = w[m];
-  run = carry;
-  kk = kfirst;
-#pragma unroll
-  for (int i = 0; i < SEG; ++i) {
-    const int t = t0 + i;
-    if (t < T) {
-      run = fmaf(lam, run, kk);
-      const float cc = wm + run;
-      const float qq = rv[i] / cc;
-      const int64_t idx = (row0 + t) * M + m;
-      q[idx] = qq;
-      c[idx] = cc;
-      const int64_t io = (row0 + t) * ldop + m;
-      store_op<OpT>(qop, io, qq);
-      store_op<OpT>(kop, io, kk);
-    }
-    kk = rv[i];
+  if (wp == 0) {
+    float tot = 0.f;
+    for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
+    cta_total[lane] = tot;
   }
+  cluster.sync();
+  const float lam_cta = expf(gg * (float)(SEG * WARPS));
+  float carry = 0.f;
+  for (int j = 0; j < cr; ++j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  for (int j = 0; j < wp; ++j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
+  if (valid) {
+    const float wm = w[m];
+    run = carry;
+    kk = kfirst;
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      const int t = t0 + i;
+      if (t < T) {
+        run = fmaf(lam, run, kk);
+        const float cc = wm + run;
+        const float qq = rv[i] / cc;
+        const int64_t idx = (row0 + t) * M + m;
+        q[idx] = qq;
+        c[idx] = cc;
+        const int64_t io = (row0 + t) * ldop + m;
+        store_op<OpT>(qop, io, qq);
+        store_op<OpT>(kop, io, kk);
+      }
+      kk = rv[i];
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
-template <int SEG, int SLOTS>
-__global__ void __launch_bounds__(512, 1)
-    stats_bwd_reg_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out,
-                         const float* __restrict__ dk, const float* __restrict__ q, const float* __restrict__ c,
-                         const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
-                         float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int T,
-                         int M, int fast_identity) {
-  extern __shared__ float smem_f[];  // seg_sum[nseg][SLOTS], then dw_red[nseg][SLOTS]
-  __shared__ double red_dg[512];
-  const int slot = threadIdx.x % SLOTS, seg = threadIdx.x / SLOTS;
-  const int nseg = blockDim.x / SLOTS;
-  float* seg_sum = smem_f;
-  float* dw_red = smem_f + nseg * SLOTS;
+template <int SEG, int WARPS>
+__global__ void __launch_bounds__(32 * WARPS)
+    stats_bwd_cluster_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out,
+                             const float* __restrict__ dk, const float* __restrict__ q, const float* __restrict__ c,
+                             const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
+                             float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg,
+                             int T, int M, int fast_identity) {
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float warp_dw[WARPS][32];
+  __shared__ float cta_total[32];
+  __shared__ double red_dg[32 * WARPS];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int b = blockIdx.y;
-  const int m = blockIdx.x * SLOTS + slot;
+  const int m = (blockIdx.x / C) * 32 + lane;
   const bool valid = m < M;
-  const int t0 = seg * SEG;
+  const int t0 = (cr * WARPS + wp) * SEG;
   const float gg = *g;
   const float lam = expf(gg);
   const int64_t base = (int64_t)b * T * M + m;
@@ -259,8 +281,7 @@ __global__ void __launch_bounds__(512, 1)
   const float wm = valid ? w[m] : 0.f;
   const float t_mid = 0.5f * (float)(T - 1);
 
-  // all loads up front: the scan inputs and the values the second half needs
-  float drd[SEG], dcv[SEG], dkv[SEG], kv[SEG];
+  float drd[SEG], dcv[SEG];
   float dw_acc = 0.f, dg_f = 0.f;
 #pragma unroll
   for (int i = 0; i < SEG; ++i) {
@@ -271,8 +292,6 @@ __global__ void __launch_bounds__(512, 1)
     const float dq = dqfv + ((in && has_dqo) ? dq_out[idx] : 0.f);
     const float cc = in ? c[idx] : 1.f;
     const float qq = in ? q[idx] : 0.f;
-    dkv[i] = in ? dk[idx] : 0.f;
-    kv[i] = (in && t > 0) ? r[idx - M] : 0.f;
     drd[i] = dq / cc;
     dcv[i] = -drd[i] * qq;
     dw_acc += dcv[i];
@@ -283,12 +302,20 @@ __global__ void __launch_bounds__(512, 1)
   float run = 0.f;
 #pragma unroll
   for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dcv[i]);
-  seg_sum[seg * SLOTS + slot] = run;
-  dw_red[seg * SLOTS + slot] = dw_acc;
+  warp_sum[wp][lane] = run;  // reverse decayed sum of dc over the segment, seen from its first position
+  warp_dw[wp][lane] = dw_acc;
   __syncthreads();
   const float lam_seg = expf(gg * (float)SEG);
-  float carry = 0.f;  // dkc at position t0 + SEG
-  for (int j = nseg - 1; j > seg; --j) carry = fmaf(carry, lam_seg, seg_sum[j * SLOTS + slot]);
+  if (wp == 0) {
+    float tot = 0.f;
+    for (int j = WARPS - 1; j >= 0; --j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
+    cta_total[lane] = tot;
+  }
+  cluster.sync();
+  const float lam_cta = expf(gg * (float)(SEG * WARPS));
+  float carry = 0.f;  // dkc at the position just after this warp's segment
+  for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  for (int j = WARPS - 1; j > wp; --j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
   double dg_acc = (double)dg_f;
   if (valid) {
     const int t_end = t0 + SEG;
@@ -299,55 +326,72 @@ __global__ void __launch_bounds__(512, 1)
     for (int i = SEG - 1; i >= 0; --i) {
       const int t = t0 + i;
       if (t < T) {
+        const int64_t idx = base + (int64_t)t * M;
+        const float dkv = dk[idx];
+        const float kt = t > 0 ? r[idx - M] : 0.f;
         run = fmaf(lam, run, dcv[i]);  // dkc_t
-        const float dkt = dkv[i] + run;
-        dr[base + (int64_t)t * M] = drd[i] + dkt_next;
-        dkt_next = dkt;
-        float term = -kv[i] * run;
-        if (fast_identity) term -= kv[i] * dkv[i];
+        dr[idx] = drd[i] + dkt_next;
+        dkt_next = dkv + run;
+        float term = -kt * run;
+        if (fast_identity) term -= kt * dkv;
         dg_s = fmaf((float)t - t_mid, term, dg_s);
       }
     }
     dg_acc += (double)dg_s;
   }
-  if (seg == 0 && valid) {
+  // per-CTA partials: dw over this CTA's positions (slot-wise), dg over the CTA
+  if (wp == 0 && valid) {
     float s2 = 0.f;
-    for (int j = 0; j < nseg; ++j) s2 += dw_red[j * SLOTS + slot];
-    part_dw[(int64_t)b * M + m] = s2;
+    for (int j = 0; j < WARPS; ++j) s2 += warp_dw[j][lane];
+    part_dw[((int64_t)b * C + cr) * M + m] = s2;
   }
   red_dg[threadIdx.x] = dg_acc;
   __syncthreads();
-  for (int stride = 256; stride > 0; stride >>= 1) {
-    if ((int)threadIdx.x < stride && threadIdx.x + stride < blockDim.x) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
+  for (int stride = 16 * WARPS; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
     __syncthreads();
   }
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
+  cluster.sync();
 }
 
-constexpr int FWD_SLOTS = 16;
-constexpr int BWD_SLOTS = 8;
-constexpr int REG_MAX_SEGS = 64;
+struct ClusterPlan {
+  int seg, warps, ctas;  // 0 ctas = not applicable
+};
 
-inline int pick_seg(int64_t T, int max_seg) {
-  for (int s = 8; s <= max_seg; s *= 2)
-    if (cdiv(T, s) <= REG_MAX_SEGS) return s;
-  return 0;
+inline ClusterPlan plan_cluster(int64_t T) {
+  const int seg = T > 512 ? 32 : (T > 256 ? 16 : 8);
+  for (int warps = 4; warps <= 16; warps *= 2) {
+    const int64_t ctas = cdiv(T, (int64_t)seg * warps);
+    if (ctas <= 8) return {seg, warps, (int)ctas};
+  }
+  return {0, 0, 0};
 }
 
-// threads of a register-scan CTA: SLOTS x nseg, nseg rounded so the CTA is whole warps
-inline int reg_threads(int64_t T, int seg, int slots) {
-  int nseg = (int)cdiv(T, seg);
-  const int per_warp = 32 / slots;
-  nseg = (int)cdiv(nseg, per_warp) * per_warp;
-  return nseg * slots;
+template <typename K, typename... Args>
+int launch_cluster(K kernel, dim3 grid, int threads, int cluster_x, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+  return ULM_OK;
 }
 
-// dw[m] = sum_b part_dw[b][m], in batch order.
-__global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int B, int M) {
+// dw[m] = sum over the R partial rows of part_dw[.][m], in row order.
+__global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int R, int M) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m < M) {
     float s = 0.f;
-    for (int b = 0; b < B; ++b) s += part_dw[(int64_t)b * M + m];
+    for (int i = 0; i < R; ++i) s += part_dw[(int64_t)i * M + m];
     dw[m] = s;
   }
 }
@@ -370,7 +414,8 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) *dg = (float)red[0];
 }
 
-// scratch layout: [part_dw: B*M float][part_dg: B*groups double][tile partials: n float]
+// scratch layout: [part_dw: B*8*M float][part_dg: B*groups double][tile partials: n float]
+// (8 = largest cluster; groups = dg partials per batch row, at most 8 per 32-slot tile)
 struct StatsScratch {
   float* part_dw;
   double* part_dg;
@@ -379,12 +424,14 @@ struct StatsScratch {
 
 inline int64_t align256(int64_t n) { return (n + 255) / 256 * 256; }
 
+inline int64_t stats_dg_groups(int64_t M) { return cdiv(M, 32) * 8; }
+
 inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
-  const int64_t groups = cdiv(M, 8);
+  const int64_t groups = stats_dg_groups(M);
   char* p = static_cast<char*>(base);
   StatsScratch s;
   s.part_dw = reinterpret_cast<float*>(p);
-  p += align256(B * M * 4);
+  p += align256(B * 8 * M * 4);
   s.part_dg = reinterpret_cast<double*>(p);
   p += align256(B * groups * 8);
   s.tiles = reinterpret_cast<float*>(p);
@@ -398,30 +445,35 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
                   int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials, int64_t n_tiles,
                   cudaStream_t st) {
   StatsScratch sc = carve_stats_scratch(partial, B, M);
-  int64_t groups;
-  const int seg = pick_seg(T, 16);
-  if (seg) {
-    groups = cdiv(M, BWD_SLOTS);
-    const int threads = reg_threads(T, seg, BWD_SLOTS);
-    const size_t smem = (size_t)2 * threads * sizeof(float);
-    dim3 grid((unsigned)groups, (unsigned)B);
-    if (seg == 8)
-      stats_bwd_reg_kernel<8, BWD_SLOTS><<<grid, threads, smem, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw,
-                                                                      sc.part_dg, (int)T, (int)M, fast_identity);
-    else
-      stats_bwd_reg_kernel<16, BWD_SLOTS><<<grid, threads, smem, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw,
-                                                                       sc.part_dg, (int)T, (int)M, fast_identity);
-    ULM_LAUNCH_CHECK("stats_bwd_reg_kernel");
+  int64_t n_dg, dw_rows;
+  const ClusterPlan pl = plan_cluster(T);
+  if (pl.ctas) {
+    const int C = pl.ctas;
+    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
+    const int threads = 32 * pl.warps;
+    int rc = ULM_OK;
+#define ULM_BWD_CL(S, W)                                                                                  \
+  if (pl.seg == S && pl.warps == W)                                                                       \
+    rc = launch_cluster(stats_bwd_cluster_kernel<S, W>, grid, threads, C, st, dqf, dq_out, dk, q, c, r, w, g, \
+                        dr, sc.part_dw, sc.part_dg, (int)T, (int)M, fast_identity);
+    ULM_BWD_CL(8, 4) ULM_BWD_CL(8, 8) ULM_BWD_CL(8, 16) ULM_BWD_CL(16, 4) ULM_BWD_CL(16, 8) ULM_BWD_CL(16, 16)
+    ULM_BWD_CL(32, 4) ULM_BWD_CL(32, 8) ULM_BWD_CL(32, 16)
+#undef ULM_BWD_CL
+    if (rc) return rc;
+    n_dg = B * (int64_t)grid.x;
+    dw_rows = B * C;
   } else {
-    groups = cdiv(M, 32);
+    const int64_t groups = cdiv(M, 32);
     dim3 grid((unsigned)groups, (unsigned)B);
     stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw, sc.part_dg,
                                                      (int)T, (int)M, fast_identity);
     ULM_LAUNCH_CHECK("stats_bwd_kernel");
+    n_dg = B * groups;
+    dw_rows = B;
   }
-  stats_bwd_dw_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(sc.part_dw, dw, (int)B, (int)M);
+  stats_bwd_dw_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(sc.part_dw, dw, (int)dw_rows, (int)M);
   ULM_LAUNCH_CHECK("stats_bwd_dw_kernel");
-  stats_bwd_dg_kernel<<<1, 256, 0, st>>>(sc.part_dg, B * groups, tile_partials, tile_partials ? n_tiles : 0, dg);
+  stats_bwd_dg_kernel<<<1, 256, 0, st>>>(sc.part_dg, n_dg, tile_partials, tile_partials ? n_tiles : 0, dg);
   ULM_LAUNCH_CHECK("stats_bwd_dg_kernel");
   return ULM_OK;
 }
@@ -440,29 +492,26 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
   ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int seg = pick_seg(T, 32);
-  if (seg) {
-    dim3 grid((unsigned)cdiv(M, FWD_SLOTS), (unsigned)B);
-    const int threads = reg_threads(T, seg, FWD_SLOTS);
-    const size_t smem = (size_t)threads * sizeof(float);
+  const ClusterPlan pl = plan_cluster(T);
+  if (pl.ctas) {
+    const int C = pl.ctas;
+    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
+    const int threads = 32 * pl.warps;
     const bool bf = op_dtype == ULM_BF16;
-#define ULM_FWD_REG(S)                                                                                        \
-  if (bf)                                                                                                     \
-    stats_fwd_reg_kernel<S, FWD_SLOTS, __nv_bfloat16><<<grid, threads, smem, st>>>(r, w, g, q, c, qop, kop,   \
-                                                                                   ld_op, (int)T, (int)M);    \
-  else                                                                                                        \
-    stats_fwd_reg_kernel<S, FWD_SLOTS, float><<<grid, threads, smem, st>>>(r, w, g, q, c, qop, kop, ld_op,    \
-                                                                           (int)T, (int)M);
-    if (seg == 8) {
-      ULM_FWD_REG(8)
-    } else if (seg == 16) {
-      ULM_FWD_REG(16)
-    } else {
-      ULM_FWD_REG(32)
-    }
-#undef ULM_FWD_REG
-    ULM_LAUNCH_CHECK("stats_fwd_reg_kernel");
-    return ULM_OK;
+    int rc = ULM_OK;
+#define ULM_FWD_CL(S, W)                                                                                        \
+  if (pl.seg == S && pl.warps == W) {                                                                           \
+    if (bf)                                                                                                     \
+      rc = launch_cluster(stats_fwd_cluster_kernel<S, W, __nv_bfloat16>, grid, threads, C, st, r, w, g, q, c,  \
+                          qop, kop, ld_op, (int)T, (int)M);                                                     \
+    else                                                                                                        \
+      rc = launch_cluster(stats_fwd_cluster_kernel<S, W, float>, grid, threads, C, st, r, w, g, q, c, qop, kop, \
+                          ld_op, (int)T, (int)M);                                                               \
+  }
+    ULM_FWD_CL(8, 4) ULM_FWD_CL(8, 8) ULM_FWD_CL(8, 16) ULM_FWD_CL(16, 4) ULM_FWD_CL(16, 8) ULM_FWD_CL(16, 16)
+    ULM_FWD_CL(32, 4) ULM_FWD_CL(32, 8) ULM_FWD_CL(32, 16)
+#undef ULM_FWD_CL
+    return rc;
   }
   dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
   if (op_dtype == ULM_BF16)
@@ -475,8 +524,7 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
 
 extern "C" int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M) {
   if (B < 0 || T < 0 || M < 0) return -1;
-  const int64_t groups = cdiv(M, 8);
-  return align256(B * M * 4) + align256(B * groups * 8) + align256(decay_dg_partials(B, T) * 4);
+  return align256(B * 8 * M * 4) + align256(B * stats_dg_groups(M) * 8) + align256(decay_dg_partials(B, T) * 4);
 }
 
 extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk, const float* q,
