@@ -16,6 +16,10 @@ void set_error(const char* fmt, ...);
 int sm_count(int device);
 int current_device();
 
+// cuTensorMapEncodeTiled from the driver (nullptr if unavailable)
+#include <cudaTypedefs.h>
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
+
 #define ULM_REQUIRE(cond, ...)                                  \
   do {                                                          \
     if (!(cond)) {                                              \
@@ -57,6 +61,7 @@ enum DeviceErrorSite : int {
   DEVERR_GEMM_MMA_WAIT = 2,
   DEVERR_GEMM_EPILOGUE_WAIT = 3,
   DEVERR_GEMM_DRAIN_WAIT = 4,
+  DEVERR_SCAN_TMA_WAIT = 5,
 };
 
 __device__ __forceinline__ void raise_device_error(int site) { atomicCAS(&g_device_error, 0, site); }

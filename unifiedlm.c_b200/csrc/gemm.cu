@@ -434,8 +434,6 @@ __global__ void __launch_bounds__(256)
 // ------------------------------------------------------------------------------------------------
 // host side
 
-namespace {
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -448,6 +446,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   });
   return fn;
 }
+
+namespace {
 
 // 3-D tiled map over (inner, rows, batch) of a bf16 operand with a 128-byte swizzle.
 int make_tmap(CUtensorMap* map, const Operand& op, int batches, uint32_t box_inner, uint32_t box_rows) {

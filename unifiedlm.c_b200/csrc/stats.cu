@@ -355,6 +355,288 @@ __global__ void __launch_bounds__(32 * WARPS)
   cluster.sync();
 }
 
+// ---- TMA-staged cluster scans --------------------------------------------------------------------
+// Same decomposition as above (cluster = 32 slots x whole sequence, CTA = R = WARPS*SEG positions,
+// warp = SEG positions, lane = slot), but each CTA first brings its R x 32 tiles of every input
+// into shared memory with one TMA bulk-tensor load per array, so the loads need no registers and
+// the whole tile is in flight at once. Out-of-range rows and slots arrive as zeros; the write
+// address tile (k_t = r_{t-1}) is the r tile loaded one row earlier.
+
+template <int SEG, int WARPS, typename OpT>
+__global__ void __launch_bounds__(32 * WARPS)
+    stats_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_r, const float* __restrict__ w,
+                         const float* __restrict__ g, float* __restrict__ q, float* __restrict__ c,
+                         void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T, int M) {
+  constexpr int R = SEG * WARPS;
+  extern __shared__ __align__(128) float tile[];  // [0]: r rows t0.., [1]: k rows (r rows t0-1..)
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float cta_total[32];
+  __shared__ int ok_flag;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int b = blockIdx.y;
+  const int m0 = (blockIdx.x / C) * 32;
+  const int m = m0 + lane;
+  const int cta_t0 = cr * R;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, 2u * R * 32u * 4u);
+    tma_load_3d(&map_r, tile, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_r, tile + R * 32, &bar, m0, cta_t0 - 1, b);
+  }
+  if (threadIdx.x == 0) ok_flag = 1;
+  __syncthreads();
+  if (!mbar_wait_bounded(&bar, 0)) {
+    raise_device_error(DEVERR_SCAN_TMA_WAIT);
+    ok_flag = 0;
+  }
+  __syncthreads();
+  const bool ok = ok_flag != 0;
+  const float gg = *g;
+  const float lam = expf(gg);
+  const float* rt = tile + (wp * SEG) * 32 + lane;
+  const float* kt = tile + R * 32 + (wp * SEG) * 32 + lane;
+  float run = 0.f;
+  if (ok) {
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, kt[i * 32]);
+  }
+  warp_sum[wp][lane] = run;
+  __syncthreads();
+  const float lam_seg = expf(gg * (float)SEG);
+  if (wp == 0) {
+    float tot = 0.f;
+    for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
+    cta_total[lane] = tot;
+  }
+  cluster.sync();
+  const float lam_cta = expf(gg * (float)R);
+  float carry = 0.f;
+  for (int j = 0; j < cr; ++j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  for (int j = 0; j < wp; ++j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
+  if (ok && m < M) {
+    const float wm = w[m];
+    const int64_t row0 = (int64_t)b * T;
+    const int t0 = cta_t0 + wp * SEG;
+    run = carry;
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      const int t = t0 + i;
+      if (t < T) {
+        const float kk = kt[i * 32];
+        run = fmaf(lam, run, kk);
+        const float cc = wm + run;
+        const float qq = rt[i * 32] / cc;
+        const int64_t idx = (row0 + t) * M + m;
+        q[idx] = qq;
+        c[idx] = cc;
+        const int64_t io = (row0 + t) * ldop + m;
+        store_op<OpT>(qop, io, qq);
+        store_op<OpT>(kop, io, kk);
+      }
+    }
+  }
+  cluster.sync();
+}
+
+template <int SEG, int WARPS>
+__global__ void __launch_bounds__(32 * WARPS)
+    stats_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dqf, const __grid_constant__ CUtensorMap map_dqo,
+                         const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
+                         const __grid_constant__ CUtensorMap map_dk, const __grid_constant__ CUtensorMap map_r,
+                         const float* __restrict__ dk, const float* __restrict__ w, const float* __restrict__ g,
+                         float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int T,
+                         int M, int has_dqo, int fast_identity) {
+  constexpr int R = SEG * WARPS;
+  constexpr int TILE = R * 32;
+  // tiles: 0 dqf (then dr_direct = dq/c), 1 dq_out (then dc), 2 q, 3 c, 4 dk, 5 k
+  extern __shared__ __align__(128) float tile[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float warp_dw[WARPS][32];
+  __shared__ float cta_total[32];
+  __shared__ double red_dg[32 * WARPS];
+  __shared__ int ok_flag;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int b = blockIdx.y;
+  const int m0 = (blockIdx.x / C) * 32;
+  const int m = m0 + lane;
+  const bool valid = m < M;
+  const int cta_t0 = cr * R;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, (has_dqo ? 6u : 5u) * TILE * 4u);
+    tma_load_3d(&map_dqf, tile, &bar, m0, cta_t0, b);
+    if (has_dqo) tma_load_3d(&map_dqo, tile + TILE, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_q, tile + 2 * TILE, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_c, tile + 3 * TILE, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_dk, tile + 4 * TILE, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_r, tile + 5 * TILE, &bar, m0, cta_t0 - 1, b);
+    ok_flag = 1;
+  }
+  __syncthreads();
+  if (!mbar_wait_bounded(&bar, 0)) {
+    raise_device_error(DEVERR_SCAN_TMA_WAIT);
+    ok_flag = 0;
+  }
+  __syncthreads();
+  const bool ok = ok_flag != 0;
+  const float gg = *g;
+  const float lam = expf(gg);
+  const float wm = valid ? w[m] : 0.f;
+  const float t_mid = 0.5f * (float)(T - 1);
+  const int t0 = cta_t0 + wp * SEG;
+  float* s_dqf = tile + (wp * SEG) * 32 + lane;
+  float* s_dqo = s_dqf + TILE;
+  const float* s_q = s_dqf + 2 * TILE;
+  const float* s_c = s_dqf + 3 * TILE;
+  const float* s_dk = s_dqf + 4 * TILE;
+  const float* s_k = s_dqf + 5 * TILE;
+
+  float dw_acc = 0.f, dg_f = 0.f, run = 0.f;
+  if (ok) {
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      const int t = t0 + i;
+      const float dqfv = s_dqf[i * 32];
+      const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
+      const float cc = (t < T && valid) ? s_c[i * 32] : 1.f;
+      const float qq = s_q[i * 32];
+      const float drd = dq / cc;
+      const float dc = -drd * qq;
+      s_dqf[i * 32] = drd;
+      s_dqo[i * 32] = dc;
+      dw_acc += dc;
+      float term = dc * (cc - wm);
+      if (fast_identity) term += qq * dqfv;
+      dg_f = fmaf((float)t - t_mid, term, dg_f);
+    }
+#pragma unroll
+    for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, s_dqo[i * 32]);
+  }
+  warp_sum[wp][lane] = run;
+  warp_dw[wp][lane] = dw_acc;
+  __syncthreads();
+  const float lam_seg = expf(gg * (float)SEG);
+  if (wp == 0) {
+    float tot = 0.f;
+    for (int j = WARPS - 1; j >= 0; --j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
+    cta_total[lane] = tot;
+  }
+  cluster.sync();
+  const float lam_cta = expf(gg * (float)R);
+  float carry = 0.f;  // dkc at position t0 + SEG
+  for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  for (int j = WARPS - 1; j > wp; --j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
+  double dg_acc = (double)dg_f;
+  if (ok && valid) {
+    const int64_t base = (int64_t)b * T * M + m;
+    const int t_end = t0 + SEG;
+    float dk_end = 0.f;
+    if (t_end < T) dk_end = (wp + 1 < WARPS) ? s_dk[SEG * 32] : dk[base + (int64_t)t_end * M];
+    float dkt_next = (t_end < T) ? dk_end + carry : 0.f;
+    run = carry;
+    float dg_s = 0.f;
+#pragma unroll
+    for (int i = SEG - 1; i >= 0; --i) {
+      const int t = t0 + i;
+      if (t < T) {
+        const float dkv = s_dk[i * 32];
+        const float kv = s_k[i * 32];
+        run = fmaf(lam, run, s_dqo[i * 32]);  // dkc_t
+        dr[base + (int64_t)t * M] = s_dqf[i * 32] + dkt_next;
+        dkt_next = dkv + run;
+        float term = -kv * run;
+        if (fast_identity) term -= kv * dkv;
+        dg_s = fmaf((float)t - t_mid, term, dg_s);
+      }
+    }
+    dg_acc += (double)dg_s;
+  }
+  if (wp == 0 && valid) {
+    float s2 = 0.f;
+    for (int j = 0; j < WARPS; ++j) s2 += warp_dw[j][lane];
+    part_dw[((int64_t)b * C + cr) * M + m] = s2;
+  }
+  red_dg[threadIdx.x] = dg_acc;
+  __syncthreads();
+  for (int stride = 16 * WARPS; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
+  cluster.sync();
+}
+
+// 3-D map over an fp32 (B, T, M) array with a 32-slot x `rows` box, no swizzle.
+inline int make_rows_tmap(CUtensorMap* map, const float* ptr, int64_t B, int64_t T, int64_t M, int rows) {
+  auto fn = encode_tiled();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return ULM_ERR_UNSUPPORTED;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)M, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)M * 4, (cuuint64_t)(T * M) * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (scan tile) failed (%d)", (int)r);
+    return ULM_ERR_CUDA;
+  }
+  return ULM_OK;
+}
+
+// TMA-staged scans need 16-byte aligned bases and rows (M % 4 == 0) and T <= 8 * 256.
+struct TmaScanPlan {
+  int seg, warps, ctas;
+};
+
+inline TmaScanPlan plan_tma_scan(int64_t T, int64_t M, const void* const* ptrs, int n) {
+  if (M % 4 != 0) return {0, 0, 0};
+  for (int i = 0; i < n; ++i)
+    if (ptrs[i] && !is_aligned16(ptrs[i])) return {0, 0, 0};
+  if (T <= 8 * 128) return {16, 8, (int)cdiv(T, 128)};
+  if (T <= 8 * 256) return {16, 16, (int)cdiv(T, 256)};
+  return {0, 0, 0};
+}
+
+template <typename K, typename... Args>
+int launch_cluster_smem(K kernel, dim3 grid, int threads, int cluster_x, size_t smem, cudaStream_t st,
+                        Args... args) {
+  ULM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+  return ULM_OK;
+}
+
 struct ClusterPlan {
   int seg, warps, ctas;  // 0 ctas = not applicable
 };
@@ -446,8 +728,33 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
                   cudaStream_t st) {
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   int64_t n_dg, dw_rows;
+  const void* ptrs[7] = {dqf, dq_out, dk, q, c, r, dr};
+  const TmaScanPlan tp = plan_tma_scan(T, M, ptrs, 7);
   const ClusterPlan pl = plan_cluster(T);
-  if (pl.ctas) {
+  if (tp.ctas) {
+    const int R = tp.seg * tp.warps;
+    CUtensorMap mdqf, mdqo, mq, mc, mdk, mr;
+    if (int rc = make_rows_tmap(&mdqf, dqf, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mdqo, dq_out ? dq_out : dqf, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mq, q, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mc, c, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mdk, dk, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mr, r, B, T, M, R)) return rc;
+    const int C = tp.ctas;
+    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
+    const size_t smem = (size_t)6 * R * 32 * 4;
+    int rc;
+    if (tp.warps == 8)
+      rc = launch_cluster_smem(stats_bwd_tma_kernel<16, 8>, grid, 32 * 8, C, smem, st, mdqf, mdqo, mq, mc, mdk, mr,
+                               dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, dq_out ? 1 : 0, fast_identity);
+    else
+      rc = launch_cluster_smem(stats_bwd_tma_kernel<16, 16>, grid, 32 * 16, C, smem, st, mdqf, mdqo, mq, mc, mdk,
+                               mr, dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, dq_out ? 1 : 0,
+                               fast_identity);
+    if (rc) return rc;
+    n_dg = B * (int64_t)grid.x;
+    dw_rows = B * C;
+  } else if (pl.ctas) {
     const int C = pl.ctas;
     dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
     const int threads = 32 * pl.warps;
@@ -492,6 +799,26 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
   ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const void* ptrs[3] = {r, q, c};
+  const TmaScanPlan tp = plan_tma_scan(T, M, ptrs, 3);
+  if (tp.ctas) {
+    const int R = tp.seg * tp.warps;
+    CUtensorMap mr;
+    if (int rc = make_rows_tmap(&mr, r, B, T, M, R)) return rc;
+    const int C = tp.ctas;
+    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
+    const size_t smem = (size_t)2 * R * 32 * 4;
+    const bool bf = op_dtype == ULM_BF16;
+    if (tp.warps == 8)
+      return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, w, g, q,
+                                      c, qop, kop, ld_op, (int)T, (int)M)
+                : launch_cluster_smem(stats_fwd_tma_kernel<16, 8, float>, grid, 256, C, smem, st, mr, w, g, q, c, qop,
+                                      kop, ld_op, (int)T, (int)M);
+    return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 16, __nv_bfloat16>, grid, 512, C, smem, st, mr, w, g, q,
+                                    c, qop, kop, ld_op, (int)T, (int)M)
+              : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, w, g, q, c, qop,
+                                    kop, ld_op, (int)T, (int)M);
+  }
   const ClusterPlan pl = plan_cluster(T);
   if (pl.ctas) {
     const int C = pl.ctas;
