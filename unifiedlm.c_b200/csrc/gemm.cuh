@@ -63,39 +63,28 @@ __host__ __device__ inline int nlower_tiles_in_row(int mb, int BM, int BN, int n
   return c < n_blocks ? c : n_blocks;
 }
 
-// Map a linear tile index to (batch, row block, column block, k range). Equal-cost tiles
-// (CAUSAL_NONE, CAUSAL_NLOWER) go batch by batch (L2 locality). Under CAUSAL_KLOWER / KUPPER a
-// tile's k range, hence its cost, grows with (resp. shrinks with) its row block, so tiles are ordered
-// longest first across all batches: handing them out round-robin to the persistent CTAs then
-// approximates longest-processing-time-first scheduling.
+// Map a linear tile index to (batch, row block, column block, k range). Tiles of one batch row are
+// consecutive (L2 locality); under CAUSAL_KLOWER the longest row blocks come first.
 template <int BM, int BN>
 __device__ __forceinline__ TileCoord decode_tile(int t, const GemmShape& s, int m_blocks, int n_blocks,
                                                  int tiles_per_batch) {
   TileCoord c;
-  if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER) {
-    const int per_row = s.batches * n_blocks;
-    const int mi = t / per_row;
-    const int rem = t - mi * per_row;
-    c.b = rem / n_blocks;
-    c.nb = rem - c.b * n_blocks;
-    c.mb = s.causal == CAUSAL_KLOWER ? m_blocks - 1 - mi : mi;
-  } else {
-    c.b = t / tiles_per_batch;
-    int i = t - c.b * tiles_per_batch;
-    if (s.causal == CAUSAL_NLOWER) {
-      int mb = 0;
-      for (;;) {
-        const int cnt = nlower_tiles_in_row(mb, BM, BN, n_blocks);
-        if (i < cnt) break;
-        i -= cnt;
-        ++mb;
-      }
-      c.mb = mb;
-      c.nb = i;
-    } else {
-      c.mb = i / n_blocks;
-      c.nb = i - c.mb * n_blocks;
+  c.b = t / tiles_per_batch;
+  int i = t - c.b * tiles_per_batch;
+  if (s.causal == CAUSAL_NLOWER) {
+    int mb = 0;
+    for (;;) {
+      const int cnt = nlower_tiles_in_row(mb, BM, BN, n_blocks);
+      if (i < cnt) break;
+      i -= cnt;
+      ++mb;
     }
+    c.mb = mb;
+    c.nb = i;
+  } else {
+    c.mb = i / n_blocks;
+    c.nb = i - c.mb * n_blocks;
+    if (s.causal == CAUSAL_KLOWER) c.mb = m_blocks - 1 - c.mb;
   }
   c.k_begin = 0;
   c.k_end = s.K;
