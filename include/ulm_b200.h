@@ -83,6 +83,24 @@ int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk,
 
 int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M);
 
+/* Size of the scratch block built into the library for ulm_memory_stats_bwd_noalloc (per device). */
+#define ULM_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* Same computation and results as ulm_memory_stats_bwd, for callers that cannot allocate device
+ * memory when they call it (a serving runtime that reserves all of HBM for its own pool at start-up,
+ * a plugin host that owns every device allocation). No reference counterpart: the reference
+ * allocates its temporaries with torch (kernel.py:225-227).
+ * It allocates nothing: its scratch is an 8 MiB block compiled into the library, which every GPU
+ * that loads the library holds until the process exits. Limit: the scratch it needs, about
+ * 34 * B * M bytes, must fit that block, so B * M up to about 246,000 (B=16 with M=2048 uses 1.1 MiB;
+ * B=64 with M=3840 is about the largest); larger calls fail with ULM_ERR_INVALID and a message. The first call on each device looks up the block's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any stream
+ * capture. All calls share the one block, so calls that overlap on the GPU (different streams,
+ * no ordering between them) race and must be avoided; calls on one stream are safe. */
+int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_out, const float* dk, const float* q,
+                                 const float* c, const float* r, const float* w, const float* g, float* dr,
+                                 float* dw, float* dg, int64_t B, int64_t T, int64_t M, void* stream);
+
 /* ---- the chunk products -------------------------------------------------------------------- */
 
 /* Decayed causal scores over the whole sequence (the reference's intra-chunk matrix A_n,

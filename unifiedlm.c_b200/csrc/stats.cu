@@ -9,6 +9,8 @@
 // is at most 32 x T x 4 bytes).
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "gemm.cuh"
 
 namespace ulm {
@@ -869,4 +871,66 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
   ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr && partial, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
+}
+
+// ---- statistics backward without any allocation ------------------------------------------------
+// Some hosts cannot hand this library device memory at call time: a serving runtime that reserves
+// all of HBM for its own pool at start-up, or a plugin host that owns every device allocation.
+// For them the statistics backward can use a fixed scratch block that lives in the library's own
+// device image (ULM_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads the library until
+// the process exits). Host code cannot pass the array's name to a kernel (on the host it is only
+// a stand-in symbol), so its device address is looked up with cudaGetSymbolAddress once per device,
+// on the first call made while that device is current.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ULM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Bytes the public statistics backward actually uses (no score-epilogue partials).
+int64_t stats_bwd_core_scratch(int64_t B, int64_t M) {
+  return align256(B * 8 * M * 4) + align256(B * stats_dg_groups(M) * 8);
+}
+
+int noalloc_scratch(void** out) {
+  const int dev = current_device();
+  ULM_REQUIRE(dev >= 0 && dev < 64, "no current CUDA device (or ordinal >= 64)");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    ULM_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    ULM_REQUIRE(p != nullptr, "cudaGetSymbolAddress returned a null scratch address");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return ULM_OK;
+}
+
+}  // namespace
+
+extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_out, const float* dk, const float* q,
+                                            const float* c, const float* r, const float* w, const float* g,
+                                            float* dr, float* dw, float* dg, int64_t B, int64_t T, int64_t M,
+                                            void* stream) {
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
+  ULM_REQUIRE(dw && dg, "null dw/dg");
+  const int64_t need = stats_bwd_core_scratch(B, M);
+  ULM_REQUIRE(need <= (int64_t)ULM_NOALLOC_SCRATCH_BYTES,
+              "ulm_memory_stats_bwd_noalloc: B=%lld x M=%lld needs %lld bytes of scratch, the built-in block holds "
+              "%lld; use ulm_memory_stats_bwd with caller-provided scratch",
+              (long long)B, (long long)M, (long long)need, (long long)ULM_NOALLOC_SCRATCH_BYTES);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || T == 0 || M == 0) {
+    if (M > 0) ULM_CUDA_TRY(cudaMemsetAsync(dw, 0, M * sizeof(float), st));
+    ULM_CUDA_TRY(cudaMemsetAsync(dg, 0, sizeof(float), st));
+    return ULM_OK;
+  }
+  ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr, "null pointer argument");
+  ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  // every scratch entry the kernels read is written earlier in the same call: nothing to clear
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
 }
