@@ -18,6 +18,8 @@
  *   kernel.py:51-72    _la_attn_kernel (decayed chunk scores) -> ulm_decayed_scores
  *   kernel.py:23-48,
  *   kernel.py:75-101   _la_state / _la_out (apply scores)     -> ulm_causal_apply
+ *   model.py:88-111,   UnifiedBlock.init_state / step, and
+ *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
  */
 #ifndef ULM_B200_H
 #define ULM_B200_H
@@ -145,6 +147,47 @@ int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const f
                    const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
                    float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T, int64_t M, int64_t D,
                    int prec, void* stream);
+
+/* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */
+
+/* Per block, once per weight set: prior[d][m] = ((1 - lam) * mu[d][m]) * w[m], the constant part of
+ * the state update (run.c:251), stored as prior_dtype. mu: (D,M) fp32; w: (M,) fp32; lam: device
+ * scalar. */
+int ulm_decode_prepare_block(const float* mu, const float* w, const float* lam, void* prior, int prior_dtype,
+                             int64_t D, int64_t M, void* stream);
+
+/* Per block, at the start of every sequence batch (UnifiedBlock.init_state, model.py:88-94;
+ * run.c reset_state, run.c:121-138): U = mu * w (B,D,M), c = w (B,M), r_prev = 0 (B,M),
+ * conv buffer = 0 (B,D,conv_size-1). */
+int ulm_decode_reset_block(const float* mu, const float* w, float* U, float* c, float* r_prev, float* buf,
+                           int64_t B, int64_t D, int64_t M, int64_t conv_size, void* stream);
+
+/* One token through one UnifiedBlock for B sequences (UnifiedBlock.step, model.py:96-111; the block
+ * body of run.c forward, run.c:203-260): x (B,D) fp32 is updated in place (residual). Weights:
+ * norm_w (D), conv_w (D,conv_size) fp32 oldest -> newest, key_w (M,D), val_w (D,D) and prior (D,M)
+ * in weight_dtype (ULM_F32: fp32 FMA contractions, run.c's operation order in the state update;
+ * ULM_BF16: bf16 weights on the tensor cores), key_b and w (M) fp32, lam and eps device scalars.
+ * State (fp32, updated in place): U (B,D,M), c (B,M), r_prev (B,M), buf (B,D,conv_size-1).
+ * work: caller scratch of ulm_decode_block_work_bytes(B,D,M) bytes. M must be a multiple of 4. */
+int ulm_decode_block_step(float* x, const float* norm_w, const float* conv_w, const void* key_w, const float* key_b,
+                          const void* val_w, const void* prior, int weight_dtype, const float* w, const float* lam,
+                          const float* eps, float* U, float* c, float* r_prev, float* buf, void* work, int64_t B,
+                          int64_t D, int64_t M, int64_t conv_size, float norm_eps, void* stream);
+
+int64_t ulm_decode_block_work_bytes(int64_t B, int64_t D, int64_t M);
+
+/* x[b] = emb[tokens[b]] (B,D) fp32; emb (V,D) in emb_dtype; tokens int32 on the device. */
+int ulm_decode_embed(const int* tokens, const void* emb, int emb_dtype, float* x, int64_t B, int64_t D,
+                     void* stream);
+
+/* Final RMSNorm, logits = norm(x) cls_w^T (B,V) fp32, greedy next token (first index of the
+ * largest logit, run.c sample_argmax) into next_token (B,) int32, and x <- emb[next_token] ready for
+ * the next step. work: ulm_decode_head_work_bytes(B,D) bytes. */
+int ulm_decode_head(float* x, const float* norm_w, const void* cls_w, const void* emb, int weight_dtype,
+                    float* logits, int* next_token, void* work, int64_t B, int64_t D, int64_t V, float norm_eps,
+                    void* stream);
+
+int64_t ulm_decode_head_work_bytes(int64_t B, int64_t D);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,417 @@
+// Batched recurrent decode: UnifiedBlock.step (model.py:96-111) / run.c forward (run.c:193-265) for
+// B sequences at once, one token per call.
+//
+// Per block and token, for every sequence b (lam, eps scalars; w, mu per slot):
+//   h = RMSNorm(x)                          decode_prologue_kernel
+//   u = conv(window(buf), h), buf <- shift  decode_prologue_kernel
+//   a = K u + bias, v = W_v h               batched GEMMs (gemm.cu: fp32 FMA or tcgen05 bf16)
+//   z = relu(a)^2, r = z / (eps + sum z)    decode_address_kernel
+//   c = lam c + (1-lam) w + r_prev, q = r/c decode_address_kernel
+//   U = lam U + (1-lam) mu w + v r_prev^T   decode_state_kernel (U read once, written once)
+//   x += U q                                decode_state_kernel
+//   r_prev <- r                             copy_f32_kernel (after the state update has used r_prev)
+// The state U (B x D x M fp32 per block) is the only large traffic: 8 D M bytes per sequence per
+// block per token; every other tensor is O(B (D + M)) or a weight shared by the whole batch.
+//
+// fp32 mode keeps run.c's operation order for the state update, ((lam U) + (1-lam) mu w) + v r_prev,
+// with the constant middle term precomputed once per block by ulm_decode_prepare_block, and no
+// fused multiply-adds, so the state evolves as in run.c up to the order of the dot-product sums.
+#include <algorithm>
+#include <cstring>
+
+#include "gemm.cuh"
+
+namespace ulm {
+
+constexpr int DEC_THREADS = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  // sum over the block, fixed order
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  if (lane == 0) red[wp] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+    red[32] = s;
+  }
+  __syncthreads();
+  s = red[32];
+  __syncthreads();
+  return s;
+}
+
+// h = rmsnorm(x) * norm_w; u = conv over the window (buf oldest..newest, h); buf shifts.
+// Also writes bf16 copies of h and u when hop/uop are given (tensor-core GEMM operands).
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_prologue_kernel(const float* __restrict__ x, const float* __restrict__ norm_w,
+                           const float* __restrict__ conv_w, float* __restrict__ buf, float* __restrict__ h,
+                           float* __restrict__ u, __nv_bfloat16* __restrict__ hop, __nv_bfloat16* __restrict__ uop,
+                           int64_t ld_op, int D, int K, float norm_eps) {
+  __shared__ float red[33];
+  const int b = blockIdx.x;
+  const float* xb = x + (int64_t)b * D;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
+  ss = block_sum(ss, red);
+  const float scale = 1.0f / sqrtf(ss / (float)D + norm_eps);
+  const int kw = K - 1;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float hv = norm_w[i] * (scale * xb[i]);
+    h[(int64_t)b * D + i] = hv;
+    float* st = buf + ((int64_t)b * D + i) * kw;
+    const float* cw = conv_w + (int64_t)i * K;
+    float uv = __fmul_rn(cw[kw], hv);
+    for (int j = 0; j < kw; ++j) uv = __fadd_rn(uv, __fmul_rn(cw[j], st[j]));
+    for (int j = 0; j + 1 < kw; ++j) st[j] = st[j + 1];
+    if (kw > 0) st[kw - 1] = hv;
+    u[(int64_t)b * D + i] = uv;
+    if (hop) hop[(int64_t)b * ld_op + i] = __float2bfloat16_rn(hv);
+    if (uop) uop[(int64_t)b * ld_op + i] = __float2bfloat16_rn(uv);
+  }
+}
+
+// r = relu(a + bias)^2 / (eps + sum), c = lam c + (1-lam) w + r_prev, q = r / c
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_address_kernel(const float* __restrict__ a, const float* __restrict__ key_b, const float* __restrict__ w,
+                          const float* __restrict__ lam_p, const float* __restrict__ eps_p, float* __restrict__ c,
+                          const float* __restrict__ r_prev, float* __restrict__ r_new, float* __restrict__ q, int M) {
+  __shared__ float red[33];
+  const int b = blockIdx.x;
+  const float lam = *lam_p, eps = *eps_p;
+  const int64_t o = (int64_t)b * M;
+  float zs = 0.f;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    float z = a[o + m] + key_b[m];
+    z = z > 0.f ? z * z : 0.f;
+    r_new[o + m] = z;
+    zs += z;
+  }
+  zs = block_sum(zs, red);
+  const float denom = eps + zs;
+  const float one_minus = 1.0f - lam;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const float r = r_new[o + m] / denom;
+    r_new[o + m] = r;
+    const float cc = __fadd_rn(__fadd_rn(__fmul_rn(lam, c[o + m]), __fmul_rn(one_minus, w[m])), r_prev[o + m]);
+    c[o + m] = cc;
+    q[o + m] = r / cc;
+  }
+}
+
+// One warp per state row (b, d): U'[m] = ((lam U) + prior[d][m]) + v[d] r_prev[m]; x[b][d] += sum U' q.
+// prior = (1-lam) mu w, fp32 or bf16. The row is streamed once with 16-byte loads and stores.
+template <typename PriorT>
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_state_kernel(float* __restrict__ U, const PriorT* __restrict__ prior, const float* __restrict__ v,
+                        const float* __restrict__ r_prev, const float* __restrict__ q, const float* __restrict__ lam_p,
+                        float* __restrict__ x, int D, int M) {
+  const int warps = blockDim.x >> 5;
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * warps + wp;  // b * D + d
+  const int b = (int)(row / D);
+  const int d = (int)(row - (int64_t)b * D);
+  const float lam = *lam_p;
+  const float vd = v[row];
+  float* Ur = U + row * M;
+  const PriorT* pr = prior + (int64_t)d * M;
+  const float* rp = r_prev + (int64_t)b * M;
+  const float* qb = q + (int64_t)b * M;
+  float acc = 0.f;
+  for (int m = lane * 4; m < M; m += 128) {
+    float4 u4 = *reinterpret_cast<const float4*>(Ur + m);
+    const float4 r4 = *reinterpret_cast<const float4*>(rp + m);
+    const float4 q4 = *reinterpret_cast<const float4*>(qb + m);
+    float p0, p1, p2, p3;
+    if constexpr (sizeof(PriorT) == 4) {
+      const float4 p4 = *reinterpret_cast<const float4*>(pr + m);
+      p0 = p4.x; p1 = p4.y; p2 = p4.z; p3 = p4.w;
+    } else {
+      const uint2 raw = *reinterpret_cast<const uint2*>(pr + m);
+      __nv_bfloat162 h0, h1;
+      memcpy(&h0, &raw.x, 4);
+      memcpy(&h1, &raw.y, 4);
+      const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      p0 = f0.x; p1 = f0.y; p2 = f1.x; p3 = f1.y;
+    }
+    u4.x = __fadd_rn(__fadd_rn(__fmul_rn(lam, u4.x), p0), __fmul_rn(vd, r4.x));
+    u4.y = __fadd_rn(__fadd_rn(__fmul_rn(lam, u4.y), p1), __fmul_rn(vd, r4.y));
+    u4.z = __fadd_rn(__fadd_rn(__fmul_rn(lam, u4.z), p2), __fmul_rn(vd, r4.z));
+    u4.w = __fadd_rn(__fadd_rn(__fmul_rn(lam, u4.w), p3), __fmul_rn(vd, r4.w));
+    *reinterpret_cast<float4*>(Ur + m) = u4;
+    acc = fmaf(u4.x, q4.x, acc);
+    acc = fmaf(u4.y, q4.y, acc);
+    acc = fmaf(u4.z, q4.z, acc);
+    acc = fmaf(u4.w, q4.w, acc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) x[row] += acc;
+}
+
+// prior[d][m] = ((1 - lam) * mu[d][m]) * w[m], and the initial state U = mu * w (run.c:121-138)
+__global__ void decode_prepare_kernel(const float* __restrict__ mu, const float* __restrict__ w,
+                                      const float* __restrict__ lam_p, void* __restrict__ prior, int prior_bf16,
+                                      int D, int M) {
+  const float lam = *lam_p;
+  const int64_t n = (int64_t)D * M;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i % M);
+    const float p = __fmul_rn(__fmul_rn(1.0f - lam, mu[i]), w[m]);
+    if (prior_bf16)
+      static_cast<__nv_bfloat16*>(prior)[i] = __float2bfloat16_rn(p);
+    else
+      static_cast<float*>(prior)[i] = p;
+  }
+}
+
+__global__ void decode_reset_kernel(const float* __restrict__ mu, const float* __restrict__ w, float* __restrict__ U,
+                                    float* __restrict__ c, float* __restrict__ r_prev, float* __restrict__ buf,
+                                    int B, int D, int M, int kw) {
+  const int64_t nU = (int64_t)B * D * M;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nU; i += stride) {
+    const int64_t dm = i % ((int64_t)D * M);
+    U[i] = mu[dm] * w[dm % M];
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)B * M; i += stride) {
+    c[i] = w[i % M];
+    r_prev[i] = 0.f;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)B * D * kw; i += stride) buf[i] = 0.f;
+}
+
+__global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+// final RMSNorm of the residual stream, fp32 and optional bf16 copy
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_final_norm_kernel(const float* __restrict__ x, const float* __restrict__ norm_w, float* __restrict__ xn,
+                             __nv_bfloat16* __restrict__ xop, int64_t ld_op, int D, float norm_eps) {
+  __shared__ float red[33];
+  const int b = blockIdx.x;
+  const float* xb = x + (int64_t)b * D;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) ss += xb[i] * xb[i];
+  ss = block_sum(ss, red);
+  const float scale = 1.0f / sqrtf(ss / (float)D + norm_eps);
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const float v = norm_w[i] * (scale * xb[i]);
+    xn[(int64_t)b * D + i] = v;
+    if (xop) xop[(int64_t)b * ld_op + i] = __float2bfloat16_rn(v);
+  }
+}
+
+// greedy pick: first index of the largest logit (run.c sample_argmax), then gather the next
+// token's embedding row into x
+__global__ void __launch_bounds__(DEC_THREADS)
+    decode_argmax_embed_kernel(const float* __restrict__ logits, int64_t ld_logits, int V,
+                               const void* __restrict__ emb, int emb_bf16, int D, int* __restrict__ next_token,
+                               float* __restrict__ x) {
+  __shared__ float bv[DEC_THREADS];
+  __shared__ int bi[DEC_THREADS];
+  const int b = blockIdx.x;
+  const float* lg = logits + (int64_t)b * ld_logits;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = lg[i];
+    if (v > best || (v == best && i < idx)) {
+      best = v;
+      idx = i;
+    }
+  }
+  bv[threadIdx.x] = best;
+  bi[threadIdx.x] = idx;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) {
+      const float ov = bv[threadIdx.x + s];
+      const int oi = bi[threadIdx.x + s];
+      if (ov > bv[threadIdx.x] || (ov == bv[threadIdx.x] && oi < bi[threadIdx.x])) {
+        bv[threadIdx.x] = ov;
+        bi[threadIdx.x] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  const int tok = bi[0] == 0x7fffffff ? 0 : bi[0];
+  if (threadIdx.x == 0) next_token[b] = tok;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const int64_t o = (int64_t)tok * D + i;
+    x[(int64_t)b * D + i] = emb_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(emb)[o])
+                                     : static_cast<const float*>(emb)[o];
+  }
+}
+
+__global__ void decode_embed_kernel(const int* __restrict__ tokens, const void* __restrict__ emb, int emb_bf16, int D,
+                                    float* __restrict__ x) {
+  const int b = blockIdx.x;
+  const int tok = tokens[b];
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    const int64_t o = (int64_t)tok * D + i;
+    x[(int64_t)b * D + i] = emb_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(emb)[o])
+                                     : static_cast<const float*>(emb)[o];
+  }
+}
+
+}  // namespace ulm
+
+using namespace ulm;
+
+namespace {
+
+int weight_dtype_ok(int dt) { return dt == ULM_F32 || dt == ULM_BF16; }
+
+// C[b][n] = sum_k X[b][k] W[n][k] for the decode batch; fp32 FMA or bf16 tensor cores.
+int decode_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int wdt, float* out, int64_t ldo, int64_t B,
+                int64_t N, int64_t K, cudaStream_t st) {
+  Operand A{X, ldx, B * ldx, K, B, wdt, false};
+  Operand Bw{W, ldw, N * ldw, K, N, wdt, false};
+  GemmShape s{1, (int)B, (int)N, (int)K, CAUSAL_NONE};
+  GemmEpilogue e;
+  e.kind = EPI_STORE;
+  e.out_dtype = ULM_F32;
+  e.out = out;
+  e.ldo = ldo;
+  e.out_bstride = B * ldo;
+  e.g = nullptr;
+  e.aux = nullptr;
+  e.ld_aux = 0;
+  e.aux_bstride = 0;
+  e.tile_partial = nullptr;
+  e.vec_ok = is_aligned16(out) && ldo % 4 == 0;
+  return run_gemm(A, Bw, s, e, st);
+}
+
+}  // namespace
+
+extern "C" int ulm_decode_prepare_block(const float* mu, const float* w, const float* lam, void* prior,
+                                        int prior_dtype, int64_t D, int64_t M, void* stream) {
+  ULM_REQUIRE(mu && w && lam && prior, "null pointer argument");
+  ULM_REQUIRE(weight_dtype_ok(prior_dtype), "prior_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(D > 0 && M > 0, "empty block");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  decode_prepare_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 4 * 148), 256, 0, st>>>(
+      mu, w, lam, prior, prior_dtype == ULM_BF16, (int)D, (int)M);
+  ULM_LAUNCH_CHECK("decode_prepare_kernel");
+  return ULM_OK;
+}
+
+extern "C" int ulm_decode_reset_block(const float* mu, const float* w, float* U, float* c, float* r_prev, float* buf,
+                                      int64_t B, int64_t D, int64_t M, int64_t conv_size, void* stream) {
+  ULM_REQUIRE(mu && w && U && c && r_prev && (buf || conv_size <= 1), "null pointer argument");
+  ULM_REQUIRE(B > 0 && D > 0 && M > 0 && conv_size >= 1, "bad extents");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  decode_reset_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * D * M, 256), 8 * 148), 256, 0, st>>>(
+      mu, w, U, c, r_prev, buf, (int)B, (int)D, (int)M, (int)(conv_size - 1));
+  ULM_LAUNCH_CHECK("decode_reset_kernel");
+  return ULM_OK;
+}
+
+extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float* conv_w, const void* key_w,
+                                     const float* key_b, const void* val_w, const void* prior, int weight_dtype,
+                                     const float* w, const float* lam, const float* eps, float* U, float* c,
+                                     float* r_prev, float* buf, void* work, int64_t B, int64_t D, int64_t M,
+                                     int64_t conv_size, float norm_eps, void* stream) {
+  ULM_REQUIRE(x && norm_w && conv_w && key_w && key_b && val_w && prior && w && lam && eps && U && c && r_prev &&
+                  work,
+              "null pointer argument");
+  ULM_REQUIRE(weight_dtype_ok(weight_dtype), "weight_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(B > 0 && D > 0 && M > 0 && conv_size >= 1, "bad extents");
+  ULM_REQUIRE(M % 4 == 0, "decode needs M %% 4 == 0 (16-byte state rows), got %lld", (long long)M);
+  ULM_REQUIRE(is_aligned16(U) && is_aligned16(r_prev) && is_aligned16(prior), "state / prior must be 16-byte aligned");
+  ULM_REQUIRE(B * D < (1ll << 31) / 8, "batch x dim too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = weight_dtype == ULM_BF16;
+  const int64_t ldo = ulm_operand_ld(D);
+  // workspace: h, u, v (B x D fp32), a, r_new, q (B x M fp32), bf16 copies of h and u (B x ldo),
+  // each piece 256-byte aligned
+  char* wp = static_cast<char*>(work);
+  auto take = [&](int64_t bytes) {
+    char* p = wp;
+    wp += (bytes + 255) / 256 * 256;
+    return p;
+  };
+  float* h = reinterpret_cast<float*>(take(B * D * 4));
+  float* u = reinterpret_cast<float*>(take(B * D * 4));
+  float* v = reinterpret_cast<float*>(take(B * D * 4));
+  float* a = reinterpret_cast<float*>(take(B * M * 4));
+  float* r_new = reinterpret_cast<float*>(take(B * M * 4));
+  float* q = reinterpret_cast<float*>(take(B * M * 4));
+  __nv_bfloat16* hop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
+  __nv_bfloat16* uop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
+  decode_prologue_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(x, norm_w, conv_w, buf, h, u, bf ? hop : nullptr,
+                                                              bf ? uop : nullptr, ldo, (int)D, (int)conv_size,
+                                                              norm_eps);
+  ULM_LAUNCH_CHECK("decode_prologue_kernel");
+  if (bf) {
+    if (int rc = decode_gemm(uop, ldo, key_w, D, ULM_BF16, a, M, B, M, D, st)) return rc;
+    if (int rc = decode_gemm(hop, ldo, val_w, D, ULM_BF16, v, D, B, D, D, st)) return rc;
+  } else {
+    if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
+    if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
+  }
+  decode_address_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(a, key_b, w, lam, eps, c, r_prev, r_new, q, (int)M);
+  ULM_LAUNCH_CHECK("decode_address_kernel");
+  const int warps = DEC_THREADS / 32;
+  const unsigned blocks = (unsigned)cdiv(B * D, warps);
+  ULM_REQUIRE((B * D) % warps == 0, "B*D must be a multiple of %d", warps);
+  if (bf)
+    decode_state_kernel<__nv_bfloat16><<<blocks, DEC_THREADS, 0, st>>>(
+        U, static_cast<const __nv_bfloat16*>(prior), v, r_prev, q, lam, x, (int)D, (int)M);
+  else
+    decode_state_kernel<float><<<blocks, DEC_THREADS, 0, st>>>(U, static_cast<const float*>(prior), v, r_prev, q, lam,
+                                                               x, (int)D, (int)M);
+  ULM_LAUNCH_CHECK("decode_state_kernel");
+  copy_f32_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * M, 256), 4 * 148), 256, 0, st>>>(r_new, r_prev, B * M);
+  ULM_LAUNCH_CHECK("copy_f32_kernel");
+  return ULM_OK;
+}
+
+extern "C" int64_t ulm_decode_block_work_bytes(int64_t B, int64_t D, int64_t M) {
+  auto al = [](int64_t n) { return (n + 255) / 256 * 256; };
+  return 3 * al(B * D * 4) + 3 * al(B * M * 4) + 2 * al(B * ulm_operand_ld(D) * 2);
+}
+
+extern "C" int ulm_decode_embed(const int* tokens, const void* emb, int emb_dtype, float* x, int64_t B, int64_t D,
+                                void* stream) {
+  ULM_REQUIRE(tokens && emb && x, "null pointer argument");
+  ULM_REQUIRE(weight_dtype_ok(emb_dtype), "emb_dtype must be ULM_F32 or ULM_BF16");
+  decode_embed_kernel<<<(unsigned)B, 128, 0, static_cast<cudaStream_t>(stream)>>>(tokens, emb, emb_dtype == ULM_BF16,
+                                                                                  (int)D, x);
+  ULM_LAUNCH_CHECK("decode_embed_kernel");
+  return ULM_OK;
+}
+
+extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w, const void* emb, int weight_dtype,
+                               float* logits, int* next_token, void* work, int64_t B, int64_t D, int64_t V,
+                               float norm_eps, void* stream) {
+  ULM_REQUIRE(x && norm_w && cls_w && emb && logits && next_token && work, "null pointer argument");
+  ULM_REQUIRE(weight_dtype_ok(weight_dtype), "weight_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(B > 0 && D > 0 && V > 0, "bad extents");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = weight_dtype == ULM_BF16;
+  const int64_t ldo = ulm_operand_ld(D);
+  float* xn = static_cast<float*>(work);
+  __nv_bfloat16* xop = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(work) + (B * D * 4 + 255) / 256 * 256);
+  decode_final_norm_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(x, norm_w, xn, bf ? xop : nullptr, ldo, (int)D,
+                                                                norm_eps);
+  ULM_LAUNCH_CHECK("decode_final_norm_kernel");
+  if (bf) {
+    if (int rc = decode_gemm(xop, ldo, cls_w, D, ULM_BF16, logits, V, B, V, D, st)) return rc;
+  } else {
+    if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) return rc;
+  }
+  decode_argmax_embed_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(logits, V, (int)V, emb, bf, (int)D, next_token, x);
+  ULM_LAUNCH_CHECK("decode_argmax_embed_kernel");
+  return ULM_OK;
+}
+
+extern "C" int64_t ulm_decode_head_work_bytes(int64_t B, int64_t D) {
+  return (B * D * 4 + 255) / 256 * 256 + (B * ulm_operand_ld(D) * 2 + 255) / 256 * 256;
+}

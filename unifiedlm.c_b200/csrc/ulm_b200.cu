@@ -3,3 +3,4 @@
 #include "gemm.cu"
 #include "stats.cu"
 #include "memory.cu"
+#include "decode.cu"
