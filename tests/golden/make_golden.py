@@ -114,31 +114,38 @@ def runc_fixture(ref_model):
     ulm_export = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(ulm_export)
     write_model_bin, write_tokenizer_bin = ulm_export.write_model_bin, ulm_export.write_tokenizer_bin
-    torch.manual_seed(0)
     seq = 64
-    model = ref_model.UnifiedLM(ref_model.ModelArgs(dim=32, n_layers=2, hidden_dim=48, vocab_size=512,
-                                                    max_seq_len=seq)).eval()
-    with torch.no_grad():
-        for layer in model.layers:
-            layer.val.weight.normal_(std=0.2)
-            layer.conv.weight.normal_(std=0.5)
-    sd = {n: t.detach().clone() for n, t in model.state_dict().items()}
     steps = 40
     binary = os.path.join(REPO, "oracle", "_ref", "run")
-    with tempfile.TemporaryDirectory() as tmp:
-        mpath, tpath = os.path.join(tmp, "model.bin"), os.path.join(tmp, "tok.bin")
-        write_model_bin(sd, mpath, seq)
-        write_tokenizer_bin(tpath, [f"|{i}" for i in range(512)])
-        text = subprocess.run([binary, mpath, "-z", tpath, "-t", "0", "-n", str(steps)],
-                              capture_output=True, text=True, check=True).stdout
-    ids = [int(p) for p in text.strip().split("|") if p]
+    # the model of test_all.test_runc with an untied classifier: with tied embeddings and fresh
+    # blocks the greedy token after BOS is BOS again and run.c stops at once (the reference's test
+    # feeds a text prompt instead); take the first seed whose greedy run from BOS is long
+    for seed in range(100):
+        torch.manual_seed(seed)
+        model = ref_model.UnifiedLM(ref_model.ModelArgs(dim=32, n_layers=2, hidden_dim=48, vocab_size=512,
+                                                        max_seq_len=seq)).eval()
+        with torch.no_grad():
+            for layer in model.layers:
+                layer.val.weight.normal_(std=0.2)
+                layer.conv.weight.normal_(std=0.5)
+            model.output.weight = torch.nn.Parameter(torch.randn(512, 32) * 0.5)
+        sd = {n: t.detach().clone() for n, t in model.state_dict().items()}
+        with tempfile.TemporaryDirectory() as tmp:
+            mpath, tpath = os.path.join(tmp, "model.bin"), os.path.join(tmp, "tok.bin")
+            write_model_bin(sd, mpath, seq)
+            write_tokenizer_bin(tpath, [f"|{i}" for i in range(512)])
+            text = subprocess.run([binary, mpath, "-z", tpath, "-t", "0", "-n", str(steps)],
+                                  capture_output=True, text=True, check=True).stdout
+        ids = [int(p) for p in text.strip().split("|") if p]
+        if len(ids) >= 30:
+            break
     # the reference's own token-by-token PyTorch form must agree (test_all.py:169-193)
     toks = [1]
     with torch.no_grad():
         for _ in range(len(ids)):
             toks.append(int(model.forward_recurrent(torch.tensor([toks]))[0, -1].argmax()))
     assert toks[1:] == ids, (toks[1:], ids)
-    return {"state_dict": sd, "max_seq_len": seq, "steps": steps, "ids": torch.tensor(ids)}
+    return {"state_dict": sd, "max_seq_len": seq, "steps": steps, "seed": seed, "ids": torch.tensor(ids)}
 
 
 def main():

@@ -83,12 +83,14 @@ def test_model_bin_roundtrip(tmp_path, golden_dir):
     export.write_model_bin(sd, str(path), f["max_seq_len"])
     raw = open(path, "rb").read()
     magic, version, dim, nl, hid, vocab, seq, conv, shared = struct.unpack_from("<Ii7i", raw, 0)
-    assert (magic, version, dim, nl, hid, vocab, seq, conv, shared) == (0x554C4D65, 1, 32, 2, 48, 512, 64, 4, 1)
+    # the fixture's classifier is untied from the embedding, so it is written after the final norm
+    assert (magic, version, dim, nl, hid, vocab, seq, conv, shared) == (0x554C4D65, 1, 32, 2, 48, 512, 64, 4, 0)
     cfg, t = export.read_model_bin(str(path))
     assert cfg["dim"] == 32 and cfg["n_layers"] == 2
     assert torch.equal(t["layers.1.key.weight"], sd["layers.1.key.weight"].float())
     assert torch.equal(t["layers.0.conv"], sd["layers.0.conv.weight"][:, 0, :].float())
     lam = torch.exp(-torch.exp(sd["layers.0.log_rate"])).float()
     assert torch.equal(t["layers.0.lam"], lam.reshape(1))
-    expect = 256 + 4 * (512 * 32 + 2 * (32 + 32 * 4 + 48 * 32 + 48 + 32 * 48 + 32 * 32 + 48 + 2) + 32)
+    assert torch.equal(t["output.weight"], sd["output.weight"].float())
+    expect = 256 + 4 * (512 * 32 + 2 * (32 + 32 * 4 + 48 * 32 + 48 + 32 * 48 + 32 * 32 + 48 + 2) + 32 + 512 * 32)
     assert len(raw) == expect

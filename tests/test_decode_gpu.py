@@ -30,16 +30,18 @@ def load(golden_dir, name):
 def test_greedy_tokens_match_reference_runc(golden_dir, use_graph):
     f = load(golden_dir, "runc_tiny.pt")
     ids = f["ids"].tolist()
+    assert len(ids) >= 30
     dec = BatchedDecoder(f["state_dict"], batch=3, precision="fp32", use_graph=use_graph)
-    out = dec.generate(torch.ones(3, 1, dtype=torch.long), steps=len(ids))
+    out = dec.generate(torch.ones(3, 1, dtype=torch.long), steps=f["steps"])
     for row in out.tolist():
-        assert row == ids
+        assert row[:len(ids)] == ids
+        assert len(ids) == f["steps"] or row[len(ids)] == 1  # run.c stops at a predicted BOS
 
 
 def rand_params(seed, dim, n_layers, hidden, vocab):
     g = torch.Generator().manual_seed(seed)
     p = {"tok_embeddings.weight": torch.randn(vocab, dim, generator=g) * 0.3, "norm.weight": 1 + 0.1 * torch.randn(dim, generator=g)}
-    p["output.weight"] = p["tok_embeddings.weight"]
+    p["output.weight"] = torch.randn(vocab, dim, generator=g) * 0.3   # untied: greedy runs do not stick at BOS
     for i in range(n_layers):
         pre = f"layers.{i}."
         p[pre + "norm.weight"] = 1 + 0.1 * torch.randn(dim, generator=g)
@@ -76,14 +78,18 @@ def test_live_runc_token_identity(tmp_path):
     batched decoder in fp32 mode; the greedy tokens must be the same."""
     if not os.path.exists(RUNC):
         pytest.skip("oracle/_ref/run not built (needs the reference checkout)")
-    p = rand_params(3, 64, 3, 128, 512)
     steps = 64
     mpath, tpath = str(tmp_path / "m.bin"), str(tmp_path / "tok.bin")
-    export.write_model_bin(p, mpath, max_seq_len=steps)
     export.write_tokenizer_bin(tpath, [f"|{i}" for i in range(512)])
-    text = subprocess.run([RUNC, mpath, "-z", tpath, "-t", "0", "-n", str(steps)], capture_output=True, text=True,
-                          check=True).stdout
-    ids = [int(x) for x in text.strip().split("|") if x]
+    for seed in range(3, 50):  # first seed whose greedy run from BOS is long
+        p = rand_params(seed, 64, 3, 128, 512)
+        export.write_model_bin(p, mpath, max_seq_len=steps)
+        text = subprocess.run([RUNC, mpath, "-z", tpath, "-t", "0", "-n", str(steps)], capture_output=True,
+                              text=True, check=True).stdout
+        ids = [int(x) for x in text.strip().split("|") if x]
+        if len(ids) >= 48:
+            break
+    assert len(ids) >= 48
     dec = BatchedDecoder(p, batch=2, precision="fp32")
-    out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=len(ids))
-    assert out[0].tolist() == ids and out[1].tolist() == ids
+    out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=steps)
+    assert out[0, :len(ids)].tolist() == ids and out[1, :len(ids)].tolist() == ids
