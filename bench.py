@@ -154,8 +154,94 @@ def run_reference(args, rank):
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, "
                                        "chunked pure-PyTorch form (test_all.py:28-51 restated), fp32"},
-            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "decode": runc_decode_baseline()}
     print(json.dumps(line), flush=True)
+
+
+DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
+
+
+def decode_params(D, L, M, V, device, seed=0):
+    """Seeded random UnifiedLM weights at the 110M shape (untied classifier), on the device."""
+    import math
+    gen = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, device=device, generator=gen)  # noqa: E731
+    p = {"tok_embeddings.weight": rn(V, D) * 0.3, "norm.weight": 1 + 0.1 * rn(D), "output.weight": rn(V, D) * 0.3}
+    for i in range(L):
+        pre = f"layers.{i}."
+        p[pre + "norm.weight"] = 1 + 0.1 * rn(D)
+        p[pre + "conv.weight"] = rn(D, 1, 4) * 0.5
+        p[pre + "key.weight"] = rn(M, D) / math.sqrt(D)
+        p[pre + "key.bias"] = rn(M) * 0.3
+        p[pre + "mu.weight"] = rn(D, M) * 0.05
+        p[pre + "val.weight"] = rn(D, D) / math.sqrt(D)
+        p[pre + "log_eps"] = torch.zeros((), device=device)
+        p[pre + "log_rate"] = torch.tensor(math.log(-math.log(0.95)), device=device)
+        p[pre + "log_w"] = rn(M) * 0.5 + math.log(4.0)
+    return p
+
+
+def bench_decode(dev, pk):
+    """Greedy batched decode tokens/s at the 110M shape (bf16 weights, fp32 state), per batch size.
+    The state is constant in context length, so steps after a one-token prompt cost what steps after
+    a 1024-token prompt cost."""
+    from unifiedlm_c_b200.decode import BatchedDecoder
+    C = DECODE
+    params = decode_params(C["D"], C["L"], C["M"], C["V"], dev)
+    out = {}
+    for B in C["batches"]:
+        dec = BatchedDecoder(params, batch=B, precision="bf16", device=dev)
+        dec.prepare_graph()
+        dec.feed(torch.ones(B, dtype=torch.int32, device=dev))
+        for _ in range(C["warmup"]):
+            dec.step_greedy()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(C["steps"]):
+            dec.step_greedy()
+        e1.record()
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) / 1e3 / C["steps"]
+        state_bytes = 8 * C["D"] * C["M"] * C["L"] * B  # U read + write, fp32
+        out[B] = {"tokens_per_s": round(B / secs, 1), "ms_per_step": round(secs * 1e3, 4),
+                  "state_gbs": round(state_bytes / secs / 1e9, 1)}
+        del dec
+        torch.cuda.empty_cache()
+    top = out[max(C["batches"])]
+    return {"metric": "batched greedy decode tokens/s (110M shape)", "value": top["tokens_per_s"],
+            "unit": "tokens/s", "batch": max(C["batches"]), "precision": "bf16 weights, fp32 state",
+            "roofline": {"bound": "hbm", "achieved": top["state_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(top["state_gbs"] / pk["hbm_gbs"], 4),
+                         "bytes": "8*D*M*L*B per step (fp32 state read + write)",
+                         "kernel": "decode_state_kernel (plus per-step GEMMs and head)"},
+            "by_batch": out}
+
+
+def runc_decode_baseline(steps=32):
+    """The reference's own C decoder (run.c, built with its runomp flags into oracle/_ref/run_omp),
+    greedy, at the 110M shape with seeded random weights, all host cores. Returns tokens/s or None."""
+    binary = os.path.join(ROOT, "oracle", "_ref", "run_omp")
+    if not os.path.exists(binary):
+        return None
+    load_package()
+    from unifiedlm_c_b200 import export
+    C = DECODE
+    params = {k: v.cpu() for k, v in decode_params(C["D"], C["L"], C["M"], C["V"], "cpu").items()}
+    with tempfile.TemporaryDirectory() as tmp:
+        mpath, tpath = os.path.join(tmp, "model.bin"), os.path.join(tmp, "tok.bin")
+        export.write_model_bin(params, mpath, max_seq_len=steps)
+        export.write_tokenizer_bin(tpath, [f"|{i}" for i in range(C["V"])])
+        env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count() or 1))
+        res = subprocess.run([binary, mpath, "-z", tpath, "-t", "0", "-n", str(steps)], capture_output=True,
+                             text=True, env=env, timeout=600)
+    for line in res.stderr.splitlines():
+        if "achieved tok/s" in line:
+            return {"value": float(line.split(":")[1]), "unit": "tokens/s", "cores": os.cpu_count() or 1,
+                    "kind": "reference", "sample": f"run.c (runomp flags) greedy, batch 1, {steps} steps, "
+                                                  "110M shape, seeded random weights"}
+    return None
 
 
 def timed_products(ulm_lib, L_, tensors, W, prec):
@@ -209,6 +295,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
     args = ap.parse_args()
@@ -251,13 +338,14 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
-    for _ in range(args.warmup):
-        step(r, v, dq_out, dfast)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the sampler starts with the warm-up so that short timed regions still see >= 1 sample under load
     with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            step(r, v, dq_out, dfast)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         ev0.record()
         for _ in range(args.steps):
@@ -335,6 +423,12 @@ def main():
                          "pure-PyTorch form (test_all.py:28-51 restated in oracle/memory.py), fp32, "
                          "scaled to 12 blocks"}
 
+    decode = None
+    if not args.no_decode:
+        decode = bench_decode(dev, pk)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            decode["cpu_baseline"] = runc_decode_baseline()
+
     # kernels of ours per step: per block fwd 4 (stats, convert, scores, read), bwd 7 (convert,
     # scores, 3 reads, stats, finalize)
     launches = args.steps * W["L"] * 11
@@ -347,7 +441,8 @@ def main():
                        "l2": "inputs larger than L2 (r is 134 MB), no flush"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches}
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
+            "decode": decode}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
