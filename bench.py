@@ -298,6 +298,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
+    ap.add_argument("--profile-decode", action="store_true",
+                    help="run a few batch-16 decode steps at the 110M shape, no report (for ncu)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -313,6 +315,17 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.profile_decode:
+        from unifiedlm_c_b200.decode import BatchedDecoder
+        C = DECODE
+        dec = BatchedDecoder(decode_params(C["D"], C["L"], C["M"], C["V"], dev), batch=16, precision="bf16",
+                             device=dev, use_graph=False)
+        dec.reset()
+        dec.feed(torch.ones(16, dtype=torch.int32, device=dev))
+        for _ in range(2):
+            dec.step_greedy()
+        torch.cuda.synchronize()
+        return
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
