@@ -66,7 +66,8 @@ int ulm_device_error(int* site);
  *   k_t = r_{t-1} (k_0 = 0),  c_t = w + sum_{s<=t} lam^(t-s) k_s,  q_t = r_t / c_t.
  * r, q, c: (B,T,M) fp32 with row stride M. qop, kop: (B,T,M) copies of q and k in `op_dtype`
  * (ULM_BF16 for the tensor-core products, ULM_F32 for the fp32 mode) with row stride ld_op >= M.
- * w: (M,) fp32. g: device fp32 scalar. */
+ * w: (M,) fp32. g: device fp32 scalar. c may be NULL when ulm_memory_needs_c(T, M) is 0 (then the
+ * backward rebuilds it from r). */
 int ulm_memory_stats_fwd(const float* r, const float* w, const float* g, float* q, float* c, void* qop,
                          void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M,
                          void* stream);
@@ -78,12 +79,18 @@ int ulm_memory_stats_fwd(const float* r, const float* w, const float* g, float* 
  *   dw  (M,)    fp32 : sum over b,t of dc                          (overwritten, not accumulated)
  *   dg  (1,)    fp32 : d/dg of the memory terms                    (overwritten)
  * `partial` is caller-provided scratch of ulm_memory_stats_bwd_scratch(B,T,M) bytes.
+ * q and c may both be NULL when ulm_memory_needs_c(T, M) is 0 and every array is 16-byte aligned:
+ * the kernel then rebuilds them from r with the forward scan (saves reading two fp32 arrays).
  * The sums over batch rows and positions run in a fixed order: results are deterministic. */
 int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
                          const float* r, const float* w, const float* g, float* dr, float* dw, float* dg,
                          void* partial, int64_t B, int64_t T, int64_t M, void* stream);
 
 int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M);
+
+/* 1 if the statistics backward needs the saved c for a (T, M) problem, 0 if it can rebuild q and c
+ * from r (the TMA-staged scans: M % 4 == 0 and T <= 2048). */
+int ulm_memory_needs_c(int64_t T, int64_t M);
 
 /* Size of the scratch block built into the library for ulm_memory_stats_bwd_noalloc (per device). */
 #define ULM_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -132,8 +139,8 @@ int64_t ulm_operand_ld(int64_t n);
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
  * Outputs: q (B,T,M) fp32; fast (B,T,D) of type v_dtype.
  * Saved for the backward (caller-owned, element type = ULM_BF16 for ULM_PREC_BF16, ULM_F32 for
- * ULM_PREC_FP32): c (B,T,M) fp32; qop, kop (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D));
- * P (B,T,ulm_operand_ld(T)). */
+ * ULM_PREC_FP32): c (B,T,M) fp32, or NULL when ulm_memory_needs_c(T, M) is 0; qop, kop
+ * (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D)); P (B,T,ulm_operand_ld(T)). */
 int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const float* g, const float* w, float* q,
                    void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
                    int64_t M, int64_t D, int prec, void* stream);

@@ -215,4 +215,14 @@ def test_stats_kernels_through_c_abi(T):
     torch.cuda.synchronize()
     assert rel(dr, dr_ref) < 1e-5 and rel(dw, dw_ref) < 1e-5, (rel(dr, dr_ref), rel(dw, dw_ref))
     assert rel(dg, dg_ref.reshape(1)) < 1e-4, rel(dg, dg_ref.reshape(1))
+    # without the saved q and c: rebuilt from r where the TMA scans apply, refused elsewhere
+    dr2, dw2, dg2 = torch.empty_like(dr), torch.empty_like(dw), torch.empty_like(dg)
+    rc = lib.ulm_memory_stats_bwd(L.ptr(dqf_d), L.ptr(dqo_d), L.ptr(dk_d), None, None, L.ptr(rr), L.ptr(ww),
+                                  L.ptr(gg), L.ptr(dr2), L.ptr(dw2), L.ptr(dg2), L.ptr(part), B, T, M, st)
+    if lib.ulm_memory_needs_c(T, M):
+        assert rc == L.ULM_ERR_INVALID
+    else:
+        L.check(rc)
+        torch.cuda.synchronize()
+        assert rel(dr2, dr) < 1e-6 and rel(dw2, dw) < 1e-6 and rel(dg2, dg) < 1e-6
     assert L.device_error() == 0

@@ -27,6 +27,7 @@ SIGNATURES = {
     "ulm_memory_stats_bwd": (_I, [_P] * 12 + [_I64, _I64, _I64, _P]),
     "ulm_memory_stats_bwd_scratch": (_I64, [_I64, _I64, _I64]),
     "ulm_memory_stats_bwd_noalloc": (_I, [_P] * 11 + [_I64, _I64, _I64, _P]),
+    "ulm_memory_needs_c": (_I, [_I64, _I64]),
     "ulm_decayed_scores": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_causal_apply": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _P]),
     "ulm_operand_ld": (_I64, [_I64]),

@@ -212,7 +212,7 @@ extern "C" int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const 
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE(v_dtype == ULM_F32 || v_dtype == ULM_BF16, "v_dtype must be ULM_F32 or ULM_BF16");
   if (B == 0 || T == 0) return ULM_OK;
-  ULM_REQUIRE(r && v && g && w && q && fast && c && qop && kop && vop && P, "null pointer argument");
+  ULM_REQUIRE(r && v && g && w && q && fast && qop && kop && vop && P, "null pointer argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = op_dtype_of(prec);
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
@@ -242,10 +242,9 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
   if (B == 0 || T == 0 || M == 0) {
     if (B * T * D > 0) ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(do_dtype), st));
-    return ulm_memory_stats_bwd(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+    return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
   }
-  ULM_REQUIRE(r && g && w && q && c && qop && kop && vop && P && doop && dS && dqf && dk && partial,
-              "null pointer argument");
+  ULM_REQUIRE(r && g && w && qop && kop && vop && P && doop && dS && dqf && dk && partial, "null pointer argument");
   if (D == 0) {
     ULM_CUDA_TRY(cudaMemsetAsync(dqf, 0, B * T * M * sizeof(float), st));
     ULM_CUDA_TRY(cudaMemsetAsync(dk, 0, B * T * M * sizeof(float), st));
@@ -272,7 +271,9 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
     if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
     if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
     ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
-    return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles, n_tiles, st);
+    // without a saved c the statistics backward rebuilds q and c from r (TMA scan path)
+    return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles,
+                         n_tiles, st);
   }
-  return ulm_memory_stats_bwd(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+  return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
 }

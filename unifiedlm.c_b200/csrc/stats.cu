@@ -181,181 +181,7 @@ __global__ void __launch_bounds__(STATS_THREADS)
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
 }
 
-// ---- cluster scans (T <= 8 * WARPS * SEG): lanes = 32 consecutive slots -------------------------
-// A cluster of C CTAs owns 32 slots of one batch row and the whole sequence. CTA rank j covers
-// positions [j*WARPS*SEG, (j+1)*WARPS*SEG); its warp w covers SEG consecutive positions, lane = slot,
-// so every load and store of a warp is one contiguous 128-byte row segment. Each thread keeps its
-// SEG positions in registers (every array is read from HBM once). Segment sums are folded inside
-// the CTA through shared memory and across the cluster through distributed shared memory after a
-// hardware cluster barrier (no spin waits).
-
 namespace cg = cooperative_groups;
-
-template <int SEG, int WARPS, typename OpT>
-__global__ void __launch_bounds__(32 * WARPS)
-    stats_fwd_cluster_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
-                             float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
-                             void* __restrict__ kop, int64_t ldop, int T, int M) {
-  __shared__ float warp_sum[WARPS][32];
-  __shared__ float cta_total[32];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int C = (int)cluster.num_blocks();
-  const int cr = (int)cluster.block_rank();
-  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-  const int b = blockIdx.y;
-  const int m = (blockIdx.x / C) * 32 + lane;
-  const bool valid = m < M;
-  const int t0 = (cr * WARPS + wp) * SEG;
-  const float gg = *g;
-  const float lam = expf(gg);
-  const int64_t row0 = (int64_t)b * T;
-  const float* rb = r + row0 * M + m;
-  float rv[SEG];
-  const float kfirst = (valid && t0 > 0 && t0 <= T) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
-#pragma unroll
-  for (int i = 0; i < SEG; ++i) rv[i] = (valid && t0 + i < T) ? rb[(int64_t)(t0 + i) * M] : 0.f;
-  float run = 0.f, kk = kfirst;
-#pragma unroll
-  for (int i = 0; i < SEG; ++i) {
-    run = fmaf(lam, run, kk);
-    kk = rv[i];
-  }
-  warp_sum[wp][lane] = run;  // decayed sum over this segment, seen from its last position
-  __syncthreads();
-  const float lam_seg = expf(gg * (float)SEG);
-  if (wp == 0) {
-    float tot = 0.f;
-    for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
-    cta_total[lane] = tot;
-  }
-  cluster.sync();
-  const float lam_cta = expf(gg * (float)(SEG * WARPS));
-  float carry = 0.f;
-  for (int j = 0; j < cr; ++j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
-  for (int j = 0; j < wp; ++j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
-  if (valid) {
-    const float wm = w[m];
-    run = carry;
-    kk = kfirst;
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-      const int t = t0 + i;
-      if (t < T) {
-        run = fmaf(lam, run, kk);
-        const float cc = wm + run;
-        const float qq = rv[i] / cc;
-        const int64_t idx = (row0 + t) * M + m;
-        q[idx] = qq;
-        c[idx] = cc;
-        const int64_t io = (row0 + t) * ldop + m;
-        store_op<OpT>(qop, io, qq);
-        store_op<OpT>(kop, io, kk);
-      }
-      kk = rv[i];
-    }
-  }
-  cluster.sync();  // no CTA leaves while another may still read its shared memory
-}
-
-template <int SEG, int WARPS>
-__global__ void __launch_bounds__(32 * WARPS)
-    stats_bwd_cluster_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out,
-                             const float* __restrict__ dk, const float* __restrict__ q, const float* __restrict__ c,
-                             const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
-                             float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg,
-                             int T, int M, int fast_identity) {
-  __shared__ float warp_sum[WARPS][32];
-  __shared__ float warp_dw[WARPS][32];
-  __shared__ float cta_total[32];
-  __shared__ double red_dg[32 * WARPS];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int C = (int)cluster.num_blocks();
-  const int cr = (int)cluster.block_rank();
-  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-  const int b = blockIdx.y;
-  const int m = (blockIdx.x / C) * 32 + lane;
-  const bool valid = m < M;
-  const int t0 = (cr * WARPS + wp) * SEG;
-  const float gg = *g;
-  const float lam = expf(gg);
-  const int64_t base = (int64_t)b * T * M + m;
-  const bool has_dqo = dq_out != nullptr;
-  const float wm = valid ? w[m] : 0.f;
-  const float t_mid = 0.5f * (float)(T - 1);
-
-  float drd[SEG], dcv[SEG];
-  float dw_acc = 0.f, dg_f = 0.f;
-#pragma unroll
-  for (int i = 0; i < SEG; ++i) {
-    const int t = t0 + i;
-    const bool in = valid && t < T;
-    const int64_t idx = base + (int64_t)t * M;
-    const float dqfv = in ? dqf[idx] : 0.f;
-    const float dq = dqfv + ((in && has_dqo) ? dq_out[idx] : 0.f);
-    const float cc = in ? c[idx] : 1.f;
-    const float qq = in ? q[idx] : 0.f;
-    drd[i] = dq / cc;
-    dcv[i] = -drd[i] * qq;
-    dw_acc += dcv[i];
-    float term = dcv[i] * (cc - wm);
-    if (fast_identity) term += qq * dqfv;
-    dg_f = fmaf((float)t - t_mid, term, dg_f);
-  }
-  float run = 0.f;
-#pragma unroll
-  for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dcv[i]);
-  warp_sum[wp][lane] = run;  // reverse decayed sum of dc over the segment, seen from its first position
-  warp_dw[wp][lane] = dw_acc;
-  __syncthreads();
-  const float lam_seg = expf(gg * (float)SEG);
-  if (wp == 0) {
-    float tot = 0.f;
-    for (int j = WARPS - 1; j >= 0; --j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
-    cta_total[lane] = tot;
-  }
-  cluster.sync();
-  const float lam_cta = expf(gg * (float)(SEG * WARPS));
-  float carry = 0.f;  // dkc at the position just after this warp's segment
-  for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
-  for (int j = WARPS - 1; j > wp; --j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
-  double dg_acc = (double)dg_f;
-  if (valid) {
-    const int t_end = t0 + SEG;
-    float dkt_next = (t_end < T) ? dk[base + (int64_t)t_end * M] + carry : 0.f;
-    run = carry;
-    float dg_s = 0.f;
-#pragma unroll
-    for (int i = SEG - 1; i >= 0; --i) {
-      const int t = t0 + i;
-      if (t < T) {
-        const int64_t idx = base + (int64_t)t * M;
-        const float dkv = dk[idx];
-        const float kt = t > 0 ? r[idx - M] : 0.f;
-        run = fmaf(lam, run, dcv[i]);  // dkc_t
-        dr[idx] = drd[i] + dkt_next;
-        dkt_next = dkv + run;
-        float term = -kt * run;
-        if (fast_identity) term -= kt * dkv;
-        dg_s = fmaf((float)t - t_mid, term, dg_s);
-      }
-    }
-    dg_acc += (double)dg_s;
-  }
-  // per-CTA partials: dw over this CTA's positions (slot-wise), dg over the CTA
-  if (wp == 0 && valid) {
-    float s2 = 0.f;
-    for (int j = 0; j < WARPS; ++j) s2 += warp_dw[j][lane];
-    part_dw[((int64_t)b * C + cr) * M + m] = s2;
-  }
-  red_dg[threadIdx.x] = dg_acc;
-  __syncthreads();
-  for (int stride = 16 * WARPS; stride > 0; stride >>= 1) {
-    if ((int)threadIdx.x < stride) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
-  cluster.sync();
-}
 
 // ---- TMA-staged cluster scans --------------------------------------------------------------------
 // Same decomposition as above (cluster = 32 slots x whole sequence, CTA = R = WARPS*SEG positions,
@@ -438,7 +264,7 @@ __global__ void __launch_bounds__(32 * WARPS)
         const float qq = rt[i * 32] / cc;
         const int64_t idx = (row0 + t) * M + m;
         q[idx] = qq;
-        c[idx] = cc;
+        if (c) c[idx] = cc;
         const int64_t io = (row0 + t) * ldop + m;
         store_op<OpT>(qop, io, qq);
         store_op<OpT>(kop, io, kk);
@@ -448,7 +274,10 @@ __global__ void __launch_bounds__(32 * WARPS)
   cluster.sync();
 }
 
-template <int SEG, int WARPS>
+// RECOMPUTE: instead of reading the saved q and c (two fp32 arrays), rebuild them from the r tile
+// (loaded one row earlier and one row longer, so it holds both k_t = r_{t-1} and r_t) by running the
+// forward scan again with the same segment structure as stats_fwd_tma_kernel: identical c, q.
+template <int SEG, int WARPS, bool RECOMPUTE>
 __global__ void __launch_bounds__(32 * WARPS)
     stats_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dqf, const __grid_constant__ CUtensorMap map_dqo,
                          const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
@@ -458,11 +287,13 @@ __global__ void __launch_bounds__(32 * WARPS)
                          int M, int has_dqo, int fast_identity) {
   constexpr int R = SEG * WARPS;
   constexpr int TILE = R * 32;
-  // tiles: 0 dqf (then dr_direct = dq/c), 1 dq_out (then dc), 2 q, 3 c, 4 dk, 5 k
+  // tiles: dqf (then dq/c), dq_out (then dc), dk, then either q, c, k (saved) or the r tile
+  // rows t0-1 .. t0+R-1 (recompute)
   extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float warp_sum[WARPS][32];
   __shared__ float warp_dw[WARPS][32];
+  __shared__ float cta_total_f[32];
   __shared__ float cta_total[32];
   __shared__ double red_dg[32 * WARPS];
   __shared__ int ok_flag;
@@ -475,19 +306,28 @@ __global__ void __launch_bounds__(32 * WARPS)
   const int m = m0 + lane;
   const bool valid = m < M;
   const int cta_t0 = cr * R;
+  float* t_dqf = tile;
+  float* t_dqo = tile + TILE;
+  float* t_dk = tile + 2 * TILE;
+  float* t_x = tile + 3 * TILE;  // recompute: r rows (R+1); saved: q, c, k tiles
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bar, (has_dqo ? 6u : 5u) * TILE * 4u);
-    tma_load_3d(&map_dqf, tile, &bar, m0, cta_t0, b);
-    if (has_dqo) tma_load_3d(&map_dqo, tile + TILE, &bar, m0, cta_t0, b);
-    tma_load_3d(&map_q, tile + 2 * TILE, &bar, m0, cta_t0, b);
-    tma_load_3d(&map_c, tile + 3 * TILE, &bar, m0, cta_t0, b);
-    tma_load_3d(&map_dk, tile + 4 * TILE, &bar, m0, cta_t0, b);
-    tma_load_3d(&map_r, tile + 5 * TILE, &bar, m0, cta_t0 - 1, b);
+    const uint32_t bytes = ((has_dqo ? 3u : 2u) * TILE + (RECOMPUTE ? (uint32_t)(R + 1) * 32u : 3u * TILE)) * 4u;
+    mbar_arrive_expect_tx(&bar, bytes);
+    tma_load_3d(&map_dqf, t_dqf, &bar, m0, cta_t0, b);
+    if (has_dqo) tma_load_3d(&map_dqo, t_dqo, &bar, m0, cta_t0, b);
+    tma_load_3d(&map_dk, t_dk, &bar, m0, cta_t0, b);
+    if (RECOMPUTE) {
+      tma_load_3d(&map_r, t_x, &bar, m0, cta_t0 - 1, b);
+    } else {
+      tma_load_3d(&map_q, t_x, &bar, m0, cta_t0, b);
+      tma_load_3d(&map_c, t_x + TILE, &bar, m0, cta_t0, b);
+      tma_load_3d(&map_r, t_x + 2 * TILE, &bar, m0, cta_t0 - 1, b);
+    }
     ok_flag = 1;
   }
   __syncthreads();
@@ -499,25 +339,62 @@ __global__ void __launch_bounds__(32 * WARPS)
   const bool ok = ok_flag != 0;
   const float gg = *g;
   const float lam = expf(gg);
+  const float lam_seg = expf(gg * (float)SEG);
+  const float lam_cta = expf(gg * (float)R);
   const float wm = valid ? w[m] : 0.f;
   const float t_mid = 0.5f * (float)(T - 1);
   const int t0 = cta_t0 + wp * SEG;
-  float* s_dqf = tile + (wp * SEG) * 32 + lane;
-  float* s_dqo = s_dqf + TILE;
-  const float* s_q = s_dqf + 2 * TILE;
-  const float* s_c = s_dqf + 3 * TILE;
-  const float* s_dk = s_dqf + 4 * TILE;
-  const float* s_k = s_dqf + 5 * TILE;
+  const int o = (wp * SEG) * 32 + lane;
+  float* s_dqf = t_dqf + o;
+  float* s_dqo = t_dqo + o;
+  const float* s_dk = t_dk + o;
+  const float* s_k = RECOMPUTE ? t_x + o : t_x + 2 * TILE + o;   // k_t = r_{t-1}
+  const float* s_r = t_x + o + 32;                                // recompute: r_t
+  const float* s_q = t_x + o;                                     // saved q
+  const float* s_c = t_x + TILE + o;                              // saved c
+
+  float n_carry = 0.f;
+  if (RECOMPUTE) {
+    // forward scan of k, exactly as stats_fwd_tma_kernel does it, to rebuild n_t
+    float run = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_k[i * 32]);
+    }
+    warp_sum[wp][lane] = run;
+    __syncthreads();
+    if (wp == 0) {
+      float tot = 0.f;
+      for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
+      cta_total_f[lane] = tot;
+    }
+    cluster.sync();
+    for (int j = 0; j < cr; ++j) n_carry = fmaf(n_carry, lam_cta, *cluster.map_shared_rank(&cta_total_f[lane], j));
+    for (int j = 0; j < wp; ++j) n_carry = fmaf(n_carry, lam_seg, warp_sum[j][lane]);
+    __syncthreads();  // warp_sum is reused below
+  }
 
   float dw_acc = 0.f, dg_f = 0.f, run = 0.f;
   if (ok) {
+    float n = n_carry;
 #pragma unroll
     for (int i = 0; i < SEG; ++i) {
       const int t = t0 + i;
+      float cc, qq;
+      if (RECOMPUTE) {
+        n = fmaf(lam, n, s_k[i * 32]);
+        cc = wm + n;
+        qq = s_r[i * 32] / cc;
+      } else {
+        cc = s_c[i * 32];
+        qq = s_q[i * 32];
+      }
+      if (!(t < T && valid)) {
+        cc = 1.f;
+        qq = 0.f;
+      }
       const float dqfv = s_dqf[i * 32];
       const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
-      const float cc = (t < T && valid) ? s_c[i * 32] : 1.f;
-      const float qq = s_q[i * 32];
       const float drd = dq / cc;
       const float dc = -drd * qq;
       s_dqf[i * 32] = drd;
@@ -533,14 +410,12 @@ __global__ void __launch_bounds__(32 * WARPS)
   warp_sum[wp][lane] = run;
   warp_dw[wp][lane] = dw_acc;
   __syncthreads();
-  const float lam_seg = expf(gg * (float)SEG);
   if (wp == 0) {
     float tot = 0.f;
     for (int j = WARPS - 1; j >= 0; --j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
     cta_total[lane] = tot;
   }
   cluster.sync();
-  const float lam_cta = expf(gg * (float)R);
   float carry = 0.f;  // dkc at position t0 + SEG
   for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
   for (int j = WARPS - 1; j > wp; --j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
@@ -639,37 +514,6 @@ int launch_cluster_smem(K kernel, dim3 grid, int threads, int cluster_x, size_t 
   return ULM_OK;
 }
 
-struct ClusterPlan {
-  int seg, warps, ctas;  // 0 ctas = not applicable
-};
-
-inline ClusterPlan plan_cluster(int64_t T) {
-  const int seg = T > 512 ? 32 : (T > 256 ? 16 : 8);
-  for (int warps = 4; warps <= 16; warps *= 2) {
-    const int64_t ctas = cdiv(T, (int64_t)seg * warps);
-    if (ctas <= 8) return {seg, warps, (int)ctas};
-  }
-  return {0, 0, 0};
-}
-
-template <typename K, typename... Args>
-int launch_cluster(K kernel, dim3 grid, int threads, int cluster_x, cudaStream_t st, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster_x;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
-  return ULM_OK;
-}
-
 // dw[m] = sum over the R partial rows of part_dw[.][m], in row order.
 __global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int R, int M) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
@@ -722,52 +566,49 @@ inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
   return s;
 }
 
+// Can the TMA-staged scans handle this shape (and so the backward rebuild q and c)?
+inline bool tma_scan_ok(int64_t T, int64_t M, const void* const* ptrs, int n) {
+  return plan_tma_scan(T, M, ptrs, n).ctas != 0;
+}
+
 // Shared by the public statistics backward (fast_identity = 1, the reference's K5 semantics) and
 // the operator backward (fast_identity = 0, tile partials of the score epilogue added instead).
+// q == c == nullptr selects the recompute mode (TMA path only).
 int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
                   const float* r, const float* w, const float* g, float* dr, float* dw, float* dg, void* partial,
                   int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials, int64_t n_tiles,
                   cudaStream_t st) {
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   int64_t n_dg, dw_rows;
+  const bool recompute = q == nullptr && c == nullptr;
   const void* ptrs[7] = {dqf, dq_out, dk, q, c, r, dr};
   const TmaScanPlan tp = plan_tma_scan(T, M, ptrs, 7);
-  const ClusterPlan pl = plan_cluster(T);
+  ULM_REQUIRE(tp.ctas || !recompute,
+              "q and c may be omitted only when M %% 4 == 0, T <= 2048 and every array is 16-byte aligned");
+  ULM_REQUIRE(recompute || (q && c), "q and c must both be given or both be NULL");
   if (tp.ctas) {
     const int R = tp.seg * tp.warps;
     CUtensorMap mdqf, mdqo, mq, mc, mdk, mr;
     if (int rc = make_rows_tmap(&mdqf, dqf, B, T, M, R)) return rc;
     if (int rc = make_rows_tmap(&mdqo, dq_out ? dq_out : dqf, B, T, M, R)) return rc;
-    if (int rc = make_rows_tmap(&mq, q, B, T, M, R)) return rc;
-    if (int rc = make_rows_tmap(&mc, c, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mq, recompute ? dqf : q, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mc, recompute ? dqf : c, B, T, M, R)) return rc;
     if (int rc = make_rows_tmap(&mdk, dk, B, T, M, R)) return rc;
-    if (int rc = make_rows_tmap(&mr, r, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mr, r, B, T, M, recompute ? R + 1 : R)) return rc;
     const int C = tp.ctas;
     dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
-    const size_t smem = (size_t)6 * R * 32 * 4;
+    const size_t smem = (size_t)(recompute ? 4 * R + 1 : 6 * R) * 32 * 4;
+    const int hq = dq_out ? 1 : 0;
     int rc;
-    if (tp.warps == 8)
-      rc = launch_cluster_smem(stats_bwd_tma_kernel<16, 8>, grid, 32 * 8, C, smem, st, mdqf, mdqo, mq, mc, mdk, mr,
-                               dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, dq_out ? 1 : 0, fast_identity);
-    else
-      rc = launch_cluster_smem(stats_bwd_tma_kernel<16, 16>, grid, 32 * 16, C, smem, st, mdqf, mdqo, mq, mc, mdk,
-                               mr, dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, dq_out ? 1 : 0,
-                               fast_identity);
-    if (rc) return rc;
-    n_dg = B * (int64_t)grid.x;
-    dw_rows = B * C;
-  } else if (pl.ctas) {
-    const int C = pl.ctas;
-    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
-    const int threads = 32 * pl.warps;
-    int rc = ULM_OK;
-#define ULM_BWD_CL(S, W)                                                                                  \
-  if (pl.seg == S && pl.warps == W)                                                                       \
-    rc = launch_cluster(stats_bwd_cluster_kernel<S, W>, grid, threads, C, st, dqf, dq_out, dk, q, c, r, w, g, \
-                        dr, sc.part_dw, sc.part_dg, (int)T, (int)M, fast_identity);
-    ULM_BWD_CL(8, 4) ULM_BWD_CL(8, 8) ULM_BWD_CL(8, 16) ULM_BWD_CL(16, 4) ULM_BWD_CL(16, 8) ULM_BWD_CL(16, 16)
-    ULM_BWD_CL(32, 4) ULM_BWD_CL(32, 8) ULM_BWD_CL(32, 16)
-#undef ULM_BWD_CL
+#define ULM_BWD_TMA(W, RC)                                                                                       \
+  rc = launch_cluster_smem(stats_bwd_tma_kernel<16, W, RC>, grid, 32 * W, C, smem, st, mdqf, mdqo, mq, mc, mdk, mr, \
+                           dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, hq, fast_identity)
+    if (tp.warps == 8) {
+      if (recompute) ULM_BWD_TMA(8, true); else ULM_BWD_TMA(8, false);
+    } else {
+      if (recompute) ULM_BWD_TMA(16, true); else ULM_BWD_TMA(16, false);
+    }
+#undef ULM_BWD_TMA
     if (rc) return rc;
     n_dg = B * (int64_t)grid.x;
     dw_rows = B * C;
@@ -796,13 +637,14 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
                                     void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
   if (B == 0 || T == 0 || M == 0) return ULM_OK;
-  ULM_REQUIRE(r && w && g && q && c && qop && kop, "null pointer argument");
+  ULM_REQUIRE(r && w && g && q && qop && kop, "null pointer argument");
   ULM_REQUIRE(ld_op >= M, "ld_op (%lld) < M (%lld)", (long long)ld_op, (long long)M);
   ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const void* ptrs[3] = {r, q, c};
   const TmaScanPlan tp = plan_tma_scan(T, M, ptrs, 3);
+  ULM_REQUIRE(c || tp.ctas, "c may be omitted only when M %% 4 == 0, T <= 2048 and r, q are 16-byte aligned");
   if (tp.ctas) {
     const int R = tp.seg * tp.warps;
     CUtensorMap mr;
@@ -820,27 +662,6 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
                                     c, qop, kop, ld_op, (int)T, (int)M)
               : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, w, g, q, c, qop,
                                     kop, ld_op, (int)T, (int)M);
-  }
-  const ClusterPlan pl = plan_cluster(T);
-  if (pl.ctas) {
-    const int C = pl.ctas;
-    dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
-    const int threads = 32 * pl.warps;
-    const bool bf = op_dtype == ULM_BF16;
-    int rc = ULM_OK;
-#define ULM_FWD_CL(S, W)                                                                                        \
-  if (pl.seg == S && pl.warps == W) {                                                                           \
-    if (bf)                                                                                                     \
-      rc = launch_cluster(stats_fwd_cluster_kernel<S, W, __nv_bfloat16>, grid, threads, C, st, r, w, g, q, c,  \
-                          qop, kop, ld_op, (int)T, (int)M);                                                     \
-    else                                                                                                        \
-      rc = launch_cluster(stats_fwd_cluster_kernel<S, W, float>, grid, threads, C, st, r, w, g, q, c, qop, kop, \
-                          ld_op, (int)T, (int)M);                                                               \
-  }
-    ULM_FWD_CL(8, 4) ULM_FWD_CL(8, 8) ULM_FWD_CL(8, 16) ULM_FWD_CL(16, 4) ULM_FWD_CL(16, 8) ULM_FWD_CL(16, 16)
-    ULM_FWD_CL(32, 4) ULM_FWD_CL(32, 8) ULM_FWD_CL(32, 16)
-#undef ULM_FWD_CL
-    return rc;
   }
   dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
   if (op_dtype == ULM_BF16)
@@ -868,7 +689,7 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
     ULM_CUDA_TRY(cudaMemsetAsync(dg, 0, sizeof(float), st));
     return ULM_OK;
   }
-  ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr && partial, "null pointer argument");
+  ULM_REQUIRE(dqf && dk && r && w && g && dr && partial, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
 }
@@ -927,10 +748,17 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
     ULM_CUDA_TRY(cudaMemsetAsync(dg, 0, sizeof(float), st));
     return ULM_OK;
   }
-  ULM_REQUIRE(dqf && dk && q && c && r && w && g && dr, "null pointer argument");
+  ULM_REQUIRE(dqf && dk && r && w && g && dr, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // every scratch entry the kernels read is written earlier in the same call: nothing to clear
   return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
+}
+
+extern "C" int ulm_memory_needs_c(int64_t T, int64_t M) {
+  // whether the operator backward needs the saved c (it rebuilds q and c on the TMA scan path,
+  // which needs M % 4 == 0 and T <= 2048; the library's own buffers are 256-byte aligned)
+  const void* none[1] = {nullptr};
+  return tma_scan_ok(T, M, none, 0) ? 0 : 1;
 }

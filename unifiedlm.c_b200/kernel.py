@@ -53,7 +53,8 @@ def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tenso
     dev = r.device
     opt = _op_dtype(precision)
     q = torch.empty(B, T, M, device=dev, dtype=torch.float32)
-    c = torch.empty_like(q)
+    # the backward rebuilds c from r on the TMA scan path; an empty placeholder stands in for it
+    c = torch.empty_like(q) if L.lib().ulm_memory_needs_c(T, M) else q.new_empty(0)
     fast = torch.empty(B, T, D, device=dev, dtype=v.dtype)
     qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
     kop = torch.empty_like(qop)
@@ -61,7 +62,8 @@ def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tenso
     P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     with torch.cuda.device(dev):
         L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w), L.ptr(q),
-                                       L.ptr(fast), L.ptr(c), L.ptr(qop), L.ptr(kop), L.ptr(vop), L.ptr(P),
+                                       L.ptr(fast), L.ptr(c) if c.numel() else None, L.ptr(qop), L.ptr(kop),
+                                       L.ptr(vop), L.ptr(P),
                                        B, T, M, D, precision, L.stream_of(r)))
     return q, fast, c, qop, kop, vop, P
 
@@ -71,7 +73,8 @@ def _memory_fwd_fake(r, v, g, w, precision):
     B, T, M = r.shape
     D = v.shape[-1]
     opt = _op_dtype(precision)
-    return (r.new_empty(B, T, M, dtype=torch.float32), v.new_empty(B, T, D), r.new_empty(B, T, M, dtype=torch.float32),
+    c_shape = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
+    return (r.new_empty(B, T, M, dtype=torch.float32), v.new_empty(B, T, D), r.new_empty(c_shape, dtype=torch.float32),
             r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
             r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
 
@@ -98,7 +101,8 @@ def memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, r: torch.Ten
     partial = torch.empty(int(L.lib().ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
         L.check(L.lib().ulm_memory_bwd(L.ptr(dq_out), L.ptr(dfast), L.dtype_code(dfast.dtype), L.ptr(r), L.ptr(g),
-                                       L.ptr(w), L.ptr(q), L.ptr(c), L.ptr(qop), L.ptr(kop), L.ptr(vop), L.ptr(P),
+                                       L.ptr(w), L.ptr(q), L.ptr(c) if c.numel() else None, L.ptr(qop),
+                                       L.ptr(kop), L.ptr(vop), L.ptr(P),
                                        L.ptr(doop), L.ptr(dS), L.ptr(dqf), L.ptr(dk), L.ptr(partial), L.ptr(dr),
                                        L.ptr(dv), L.ptr(dg), L.ptr(dw), B, T, M, D, precision, L.stream_of(r)))
     return dr, dv, dg, dw
