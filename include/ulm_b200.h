@@ -89,7 +89,7 @@ int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const float* dk,
 int64_t ulm_memory_stats_bwd_scratch(int64_t B, int64_t T, int64_t M);
 
 /* 1 if the statistics backward needs the saved c for a (T, M) problem, 0 if it can rebuild q and c
- * from r (the TMA-staged scans: M % 4 == 0 and T <= 2048). */
+ * from r (the TMA-staged scans with 128-position CTAs: M % 4 == 0 and T <= 1024). */
 int ulm_memory_needs_c(int64_t T, int64_t M);
 
 /* Size of the scratch block built into the library for ulm_memory_stats_bwd_noalloc (per device). */

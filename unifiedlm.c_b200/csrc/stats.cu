@@ -567,10 +567,6 @@ inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
 }
 
 // Can the TMA-staged scans handle this shape (and so the backward rebuild q and c)?
-inline bool tma_scan_ok(int64_t T, int64_t M, const void* const* ptrs, int n) {
-  return plan_tma_scan(T, M, ptrs, n).ctas != 0;
-}
-
 // Shared by the public statistics backward (fast_identity = 1, the reference's K5 semantics) and
 // the operator backward (fast_identity = 0, tile partials of the score epilogue added instead).
 // q == c == nullptr selects the recompute mode (TMA path only).
@@ -583,8 +579,8 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
   const bool recompute = q == nullptr && c == nullptr;
   const void* ptrs[7] = {dqf, dq_out, dk, q, c, r, dr};
   const TmaScanPlan tp = plan_tma_scan(T, M, ptrs, 7);
-  ULM_REQUIRE(tp.ctas || !recompute,
-              "q and c may be omitted only when M %% 4 == 0, T <= 2048 and every array is 16-byte aligned");
+  ULM_REQUIRE((tp.ctas && tp.seg * tp.warps + 1 <= 256) || !recompute,
+              "q and c may be omitted only when M %% 4 == 0, T <= 1024 and every array is 16-byte aligned");
   ULM_REQUIRE(recompute || (q && c), "q and c must both be given or both be NULL");
   if (tp.ctas) {
     const int R = tp.seg * tp.warps;
@@ -757,8 +753,9 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
 }
 
 extern "C" int ulm_memory_needs_c(int64_t T, int64_t M) {
-  // whether the operator backward needs the saved c (it rebuilds q and c on the TMA scan path,
-  // which needs M % 4 == 0 and T <= 2048; the library's own buffers are 256-byte aligned)
+  // whether the operator backward needs the saved c: it rebuilds q and c on the TMA scan path when
+  // one CTA's r tile plus one row fits a TMA box (M % 4 == 0, T <= 1024; buffers 16-byte aligned)
   const void* none[1] = {nullptr};
-  return tma_scan_ok(T, M, none, 0) ? 0 : 1;
+  const TmaScanPlan tp = plan_tma_scan(T, M, none, 0);
+  return (tp.ctas && tp.seg * tp.warps + 1 <= 256) ? 0 : 1;
 }
