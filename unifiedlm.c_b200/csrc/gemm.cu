@@ -67,11 +67,28 @@ __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const Ge
       if (lag > 0) dg_acc = fmaf((float)lag * p[i], v[i], dg_acc);
     }
   }
-  if (e.kind != EPI_STORE) {
+  if (e.kind == EPI_DECAY || e.kind == EPI_DECAY_DG) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int lag = row - (col0 + i);
       v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
+    }
+  }
+  if (e.kind == EPI_STORE_ADD) {
+    const float* a = reinterpret_cast<const float*>(e.aux) + (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
+    if (ncols == 32 && e.vec_ok) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(a + i);
+        v[i] += a4.x;
+        v[i + 1] += a4.y;
+        v[i + 2] += a4.z;
+        v[i + 3] += a4.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) v[i] += a[i];
     }
   }
   const int64_t off = (int64_t)b * e.out_bstride + (int64_t)row * e.ldo + col0;
@@ -305,7 +322,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
-    const float gl2 = (epi.kind != EPI_STORE) ? (*epi.g) * 1.4426950408889634f : 0.f;
+    const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
       const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
@@ -394,7 +411,8 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
-  const float g = (epi.kind != EPI_STORE) ? *epi.g : 0.f;
+  const bool decay = epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG;
+  const float g = decay ? *epi.g : 0.f;
   float dg_acc = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -410,7 +428,9 @@ __global__ void __launch_bounds__(256)
                                                                 (int64_t)row * epi.ld_aux + col];
         dg_acc = fmaf((float)(row - col) * p, v, dg_acc);
       }
-      if (epi.kind != EPI_STORE) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
+      if (decay) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
+      if (epi.kind == EPI_STORE_ADD)
+        v += reinterpret_cast<const float*>(epi.aux)[(int64_t)tc.b * epi.aux_bstride + (int64_t)row * epi.ld_aux + col];
       const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
       if (epi.out_dtype == ULM_F32)
         reinterpret_cast<float*>(epi.out)[off] = v;
@@ -532,8 +552,9 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
   ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
   ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
   ULM_REQUIRE(e.out_dtype == ULM_F32 || e.out_dtype == ULM_BF16, "bad output dtype");
-  ULM_REQUIRE(e.kind == EPI_STORE || e.g, "decay epilogue needs g");
+  ULM_REQUIRE(e.kind == EPI_STORE || e.kind == EPI_STORE_ADD || e.g, "decay epilogue needs g");
   ULM_REQUIRE(e.kind != EPI_DECAY_DG || (e.aux && e.tile_partial), "EPI_DECAY_DG needs aux and tile_partial");
+  ULM_REQUIRE(e.kind != EPI_STORE_ADD || (e.aux && e.out_dtype == ULM_F32), "EPI_STORE_ADD needs an fp32 aux");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
     ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
   if (s.batches == 0 || s.M == 0 || s.N == 0) return ULM_OK;

@@ -267,12 +267,26 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
       e.vec_ok = e.vec_ok && is_aligned16(P);
       if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
     }
-    if (int rc = ulm_causal_apply(dS, ldt, kop, ldm, dqf, M, ULM_F32, 0, B, T, M, prec, stream)) return rc;
+    {
+      // dq = dS k, with the gradient of the q output added in the epilogue: the statistics backward
+      // only needs the sum (fast_identity = 0 below)
+      Operand A{dS, ldt, T * ldt, T, T, dt, false};
+      Operand Bo{kop, ldm, T * ldm, M, T, dt, true};
+      GemmShape s{(int)B, (int)T, (int)M, (int)T, CAUSAL_KLOWER};
+      GemmEpilogue e = make_epilogue(dq_out ? EPI_STORE_ADD : EPI_STORE, ULM_F32, dqf, M, T * M, nullptr);
+      if (dq_out) {
+        e.aux = dq_out;
+        e.ld_aux = M;
+        e.aux_bstride = T * M;
+        e.vec_ok = e.vec_ok && is_aligned16(dq_out);
+      }
+      if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
+    }
     if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
     if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
     ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
     // without a saved c the statistics backward rebuilds q and c from r (TMA scan path)
-    return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles,
+    return stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles,
                          n_tiles, st);
   }
   return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);

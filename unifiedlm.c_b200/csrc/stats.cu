@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(32 * WARPS)
         const float kk = kt[i * 32];
         run = fmaf(lam, run, kk);
         const float cc = wm + run;
-        const float qq = rt[i * 32] / cc;
+        const float qq = rt[i * 32] * __frcp_rn(cc);
         const int64_t idx = (row0 + t) * M + m;
         q[idx] = qq;
         if (c) c[idx] = cc;
@@ -381,21 +381,25 @@ __global__ void __launch_bounds__(32 * WARPS)
     for (int i = 0; i < SEG; ++i) {
       const int t = t0 + i;
       float cc, qq;
+      float inv;
       if (RECOMPUTE) {
         n = fmaf(lam, n, s_k[i * 32]);
         cc = wm + n;
-        qq = s_r[i * 32] / cc;
+        inv = __frcp_rn(cc);
+        qq = s_r[i * 32] * inv;
       } else {
         cc = s_c[i * 32];
         qq = s_q[i * 32];
+        inv = __frcp_rn(cc);
       }
       if (!(t < T && valid)) {
         cc = 1.f;
         qq = 0.f;
+        inv = 1.f;
       }
       const float dqfv = s_dqf[i * 32];
       const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
-      const float drd = dq / cc;
+      const float drd = dq * inv;
       const float dc = -drd * qq;
       s_dqf[i * 32] = drd;
       s_dqo[i * 32] = dc;
