@@ -18,6 +18,7 @@
  *   kernel.py:51-72    _la_attn_kernel (decayed chunk scores) -> ulm_decayed_scores
  *   kernel.py:23-48,
  *   kernel.py:75-101   _la_state / _la_out (apply scores)     -> ulm_causal_apply
+ *   model.py:61-79     conv + UnifiedBlock.code (address)     -> ulm_address_fwd, ulm_address_bwd
  *   model.py:88-111,   UnifiedBlock.init_state / step, and
  *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
  */
@@ -154,6 +155,27 @@ int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const f
                    const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
                    float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T, int64_t M, int64_t D,
                    int prec, void* stream);
+
+/* ---- the addressing prologue (model.py:61-62, 70-72, 79) -------------------------------------- */
+
+/* r = z / (eps + sum_m z), z = relu(u key_w^T + key_b)^2, u = causal depthwise conv(h).
+ * h: (B,T,D) of h_dtype; conv_w: (D,conv_size) fp32 oldest -> newest; key_w: (M, ld_kw) in the
+ * operand type of prec (bf16 for ULM_PREC_BF16, fp32 for ULM_PREC_FP32); key_b: (M,) fp32;
+ * eps: device scalar. Outputs: r (B,T,M) fp32, den (B*T) fp32 = eps + sum z (saved), u_op (B*T, ld_u)
+ * in the operand type (saved). */
+int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w,
+                    int64_t ld_kw, const float* key_b, const float* eps, float* r, float* den, void* u_op,
+                    int64_t ld_u, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream);
+
+/* Backward of ulm_address_fwd from dr (B,T,M) fp32: dh (B,T,D) fp32, dconv_w (D,conv_size),
+ * dkey_w (M,D), dkey_b (M,) and deps (1,) fp32 (all overwritten). work: caller scratch of
+ * ulm_address_bwd_work_bytes(B,T,D,M,prec) bytes. Column sums run in a fixed order. */
+int ulm_address_bwd(const float* dr, const float* r, const float* den, const void* u_op, int64_t ld_u, const void* h,
+                    int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w, int64_t ld_kw, float* dh,
+                    float* dconv_w, float* dkey_w, float* dkey_b, float* deps, void* work, int64_t B, int64_t T,
+                    int64_t D, int64_t M, int prec, void* stream);
+
+int64_t ulm_address_bwd_work_bytes(int64_t B, int64_t T, int64_t D, int64_t M, int prec);
 
 /* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */
 

@@ -74,6 +74,14 @@ __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const Ge
       v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
     }
   }
+  if (e.kind == EPI_RELU2) {
+    const float* bias = reinterpret_cast<const float*>(e.aux) + col0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float a = v[i] + (i < ncols ? bias[i] : 0.f);
+      v[i] = a > 0.f ? a * a : 0.f;
+    }
+  }
   if (e.kind == EPI_STORE_ADD) {
     const float* a = reinterpret_cast<const float*>(e.aux) + (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
     if (ncols == 32 && e.vec_ok) {
@@ -431,6 +439,10 @@ __global__ void __launch_bounds__(256)
       if (decay) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
       if (epi.kind == EPI_STORE_ADD)
         v += reinterpret_cast<const float*>(epi.aux)[(int64_t)tc.b * epi.aux_bstride + (int64_t)row * epi.ld_aux + col];
+      if (epi.kind == EPI_RELU2) {
+        const float a = v + reinterpret_cast<const float*>(epi.aux)[col];
+        v = a > 0.f ? a * a : 0.f;
+      }
       const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
       if (epi.out_dtype == ULM_F32)
         reinterpret_cast<float*>(epi.out)[off] = v;
@@ -552,7 +564,9 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
   ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
   ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
   ULM_REQUIRE(e.out_dtype == ULM_F32 || e.out_dtype == ULM_BF16, "bad output dtype");
-  ULM_REQUIRE(e.kind == EPI_STORE || e.kind == EPI_STORE_ADD || e.g, "decay epilogue needs g");
+  ULM_REQUIRE(e.kind == EPI_STORE || e.kind == EPI_STORE_ADD || e.kind == EPI_RELU2 || e.g,
+              "decay epilogue needs g");
+  ULM_REQUIRE(e.kind != EPI_RELU2 || e.aux, "EPI_RELU2 needs the bias");
   ULM_REQUIRE(e.kind != EPI_DECAY_DG || (e.aux && e.tile_partial), "EPI_DECAY_DG needs aux and tile_partial");
   ULM_REQUIRE(e.kind != EPI_STORE_ADD || (e.aux && e.out_dtype == ULM_F32), "EPI_STORE_ADD needs an fp32 aux");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)

@@ -21,7 +21,7 @@
 namespace ulm {
 
 enum { CAUSAL_NONE = 0, CAUSAL_KLOWER = 1, CAUSAL_KUPPER = 2, CAUSAL_NLOWER = 3 };
-enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3 };
+enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RELU2 = 4 };
 
 struct GemmShape {
   int batches, M, N, K;
@@ -37,6 +37,7 @@ struct GemmEpilogue {
   const float* g;      // log decay (device scalar), EPI_DECAY / EPI_DECAY_DG
   int vec_ok;          // output and aux rows are 16-byte aligned for every tile (set by the host)
   // EPI_STORE_ADD: out = acc + aux (aux fp32, same layout as the fp32 output).
+  // EPI_RELU2: out = relu(acc + bias[n])^2, bias = aux (fp32, one value per output column).
   // EPI_DECAY_DG: aux = the forward's decayed scores P (same layout and type as the output); each
   // epilogue warp adds sum (m-n) * P[m][n] * acc[m][n] over its rows of a tile and writes it to
   // tile_partial[4 * tile + warp] (d/dg of the fast read, no atomics)

@@ -4,3 +4,4 @@
 #include "stats.cu"
 #include "memory.cu"
 #include "decode.cu"
+#include "address.cu"

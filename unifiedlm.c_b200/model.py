@@ -2,8 +2,10 @@
 
 ModelArgs, RMSNorm, UnifiedBlock and UnifiedLM keep the reference's constructor arguments,
 parameter names, shapes and initialisation (model.py:13-204), so state_dicts, checkpoints and the
-model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the fast read to
-`kernel.unified_memory` (libulm_b200.so); `step` / `init_state` / `forward_recurrent` keep the
+model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the addressing prologue to
+`prologue.address` and the fast read to `kernel.unified_memory` (libulm_b200.so); the val and mu
+projections and RMSNorm stay PyTorch (cuBLAS) as in the reference; `step` / `init_state` /
+`forward_recurrent` keep the
 reference's token-by-token semantics (model.py:88-111, 164-175) for small-batch use, and
 `decode.py` holds the batched CUDA decoder.
 
@@ -20,6 +22,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .kernel import CHUNK, unified_memory
+from .prologue import address
 
 
 @dataclass
@@ -83,8 +86,9 @@ class UnifiedBlock(nn.Module):
 
     def forward(self, x):
         h = self.norm(x)
-        u = self.conv(h.transpose(1, 2))[..., : h.size(1)].transpose(1, 2)
-        r = self.code(u)
+        # conv + code(u) in one fused call on the GPU (model.py:79-80)
+        eps = self.log_eps.clamp(-10, 10).exp()
+        r = address(h, self.conv.weight, self.key.weight, self.key.bias, eps, precision=self.precision)
         v = self.val(h)
         w = self._w()
         q, fast = unified_memory(r, v, -self.log_rate.exp(), w, precision=self.precision)
