@@ -1,17 +1,20 @@
 """Benchmark of the fast-memory path at the 110M shape.
 
-One step = the fast-memory operator forward + backward (unified_memory, kernel.py:199-238 of the
-reference) for every one of the 12 UnifiedBlocks, on 16 sequences x 1024 tokens per GPU
-(dim D=768, slots M=2048), followed at N>1 by the data-parallel all-reduce of the operator's
-parameter gradients (dw, dg of every block) over NCCL. Inputs are seeded synthetic relu^2-normalised
-addresses r and Gaussian values v, resident in HBM and larger than L2 (r alone is 134 MB), so no L2
-flush is needed between steps. Metric: tokens per second through all 12 blocks, whole job.
+One step = the fast-memory path of every one of the 12 UnifiedBlocks, forward and backward, on
+16 sequences x 1024 tokens per GPU (dim D=768, slots M=2048): the addressing prologue
+(conv -> key GEMM -> relu^2 -> normalise, model.py:70-72, 79), the fast-memory operator
+(unified_memory, kernel.py:199-238), then the operator's backward and the prologue's backward, which
+yield the path's parameter gradients (key weight and bias, conv, eps, prior mass w, decay). At N>1
+those gradients are all-reduced over NCCL (data parallel, 16 sequences per GPU). Inputs are seeded
+synthetic normalised hidden states and values, resident in HBM and larger than L2, so no L2 flush is
+needed between steps. Metric: tokens per second through all 12 blocks, whole job.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--precision bf16|fp32]
 
 Under torchrun each rank drives one GPU; the step time is the max over ranks of the CUDA-event time.
-`--impl reference` times the reference's CPU algorithm (the chunked pure-PyTorch form of
-test_all.py:28-51, restated in oracle/memory.py) on this host's cores.
+`--impl reference` times the reference's CPU algorithm for the same path (the chunked pure-PyTorch
+form of test_all.py:28-51 with the model.py prologue, restated in oracle/memory.py) on this host's
+cores.
 """
 import argparse
 import json
@@ -43,18 +46,22 @@ def peaks():
         return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def make_inputs(B, T, M, D, lam, prior, device, seed=0):
+def make_inputs(B, T, M, D, L, lam, prior, device, seed=0):
+    """Seeded synthetic inputs of one step and per-block weights (the reference's init scales)."""
+    import math
     gen = torch.Generator(device=device).manual_seed(seed)
-    a = torch.randn(B, T, M, device=device, generator=gen) + 0.3
-    a.relu_().square_()
-    r = a / (1.0 + a.sum(-1, keepdim=True))
-    del a
-    v = torch.randn(B, T, D, device=device, generator=gen)
-    g = torch.tensor(float(torch.log(torch.tensor(lam))), device=device)
-    w = torch.full((M,), prior, device=device)
-    dq_out = torch.randn(B, T, M, device=device, generator=gen) * 1e-3
-    dfast = torch.randn(B, T, D, device=device, generator=gen) * 1e-3
-    return r, v, g, w, dq_out, dfast
+    rn = lambda *s_: torch.randn(*s_, device=device, generator=gen)  # noqa: E731
+    h = rn(B, T, D)
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
+    v = rn(B, T, D)
+    dq_out = rn(B, T, M) * 1e-3
+    dfast = rn(B, T, D) * 1e-3
+    blocks = []
+    for _ in range(L):
+        blocks.append({"conv": rn(D, 1, 4) * 0.5, "key_w": rn(M, D) / math.sqrt(D), "key_b": rn(M) * 0.1,
+                       "eps": torch.ones((), device=device),
+                       "g": torch.tensor(math.log(lam), device=device), "w": torch.full((M,), prior, device=device)})
+    return h, v, dq_out, dfast, blocks
 
 
 class ClockSampler:
@@ -114,22 +121,32 @@ class ClockSampler:
 
 
 def cpu_reference_seconds(T, M, D, lam, prior, reps, threads):
-    """Seconds for one sequence x one block of the reference's chunked CPU form, fwd + bwd, fp32."""
+    """Seconds for one sequence x one block of the reference's CPU form of the path (prologue +
+    chunked fast memory, forward and backward, fp32)."""
+    import math
     from oracle import memory as O
     torch.set_num_threads(threads)
     g_ = torch.Generator().manual_seed(0)
-    a = torch.randn(1, T, M, generator=g_) + 0.3
-    z = torch.relu(a).square()
-    r = z / (1.0 + z.sum(-1, keepdim=True))
+    h = torch.randn(1, T, D, generator=g_)
     v = torch.randn(1, T, D, generator=g_)
-    g = torch.tensor(float(torch.log(torch.tensor(lam))))
-    w = torch.full((M,), prior)
+    conv = (torch.randn(D, 1, 4, generator=g_) * 0.5).requires_grad_(True)
+    kw = (torch.randn(M, D, generator=g_) / math.sqrt(D)).requires_grad_(True)
+    kb = (torch.randn(M, generator=g_) * 0.1).requires_grad_(True)
+    log_eps = torch.zeros((), requires_grad=True)
+    g = torch.tensor(math.log(lam), requires_grad=True)
+    w = torch.full((M,), prior, requires_grad=True)
     dq_out = torch.randn(1, T, M, generator=g_)
     dfast = torch.randn(1, T, D, generator=g_)
-    O.memory_grads(r, v, g, w, dq_out, dfast, form="chunked", chunk=64)  # warm-up
+
+    def once():
+        r = O.prologue(h, conv, kw, kb, log_eps)
+        q, fast = O.memory_chunked(r, v, g, w, 64)
+        ((q * dq_out).sum() + (fast * dfast).sum()).backward()
+
+    once()  # warm-up
     t0 = time.perf_counter()
     for _ in range(reps):
-        O.memory_grads(r, v, g, w, dq_out, dfast, form="chunked", chunk=64)
+        once()
     return (time.perf_counter() - t0) / reps
 
 
@@ -149,11 +166,13 @@ def run_reference(args, rank):
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_sample * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "unified_memory fwd+bwd, 1 sequence x 1 block per sample, scaled to 12 blocks",
+            "config": {"workload": "fast-memory path fwd+bwd (prologue + unified_memory), 1 sequence x 1 block "
+                                   "per sample, scaled to 12 blocks",
                        "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"]},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, "
-                                       "chunked pure-PyTorch form (test_all.py:28-51 restated), fp32"},
+                                       "prologue + chunked pure-PyTorch form (model.py:70-79, test_all.py:28-51 "
+                                       "restated), fp32"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "decode": runc_decode_baseline()}
     print(json.dumps(line), flush=True)
@@ -312,6 +331,7 @@ def main():
     load_package()
     import unifiedlm_c_b200._lib as L_
     from unifiedlm_c_b200.kernel import memory_fwd, memory_bwd, PRECISION
+    from unifiedlm_c_b200.prologue import address_fwd, address_bwd
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -331,22 +351,27 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     W = WORKLOAD
     prec = PRECISION[args.precision]
-    r, v, g, w, dq_out, dfast = make_inputs(W["B"], W["T"], W["M"], W["D"], W["lam"], W["prior"], dev, seed=rank)
-    grads = torch.zeros(W["L"], W["M"] + 1, device=dev)
+    h, v, dq_out, dfast, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
+                                              seed=rank)
+    per_block = W["M"] * W["D"] + W["M"] + W["D"] * 4 + 1 + W["M"] + 1
+    grads = torch.zeros(W["L"], per_block, device=dev)
 
-    def step(r_, v_, dq_, df_):
-        for layer in range(W["L"]):
-            q, fast, c, qop, kop, vop, P = memory_fwd(r_, v_, g, w, prec)
-            dr, dv, dg, dw = memory_bwd(dq_, df_, r_, g, w, q, c, qop, kop, vop, P, prec)
-            grads[layer, :W["M"]] = dw
-            grads[layer, W["M"]] = dg
+    def step(h_, v_, dq_, df_):
+        for layer, blk in enumerate(blocks):
+            r, den, u_op, kw = address_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], prec)
+            q, fast, c, qop, kop, vop, P = memory_fwd(r, v_, blk["g"], blk["w"], prec)
+            dr, dv, dg, dw = memory_bwd(dq_, df_, r, blk["g"], blk["w"], q, c, qop, kop, vop, P, prec)
+            dh, dconv, dkw, dkb, deps = address_bwd(dr, r, den, u_op, kw, h_, blk["conv"], prec)
+            # the block's parameter gradients, gathered for the all-reduce (and the e2e read-back)
+            torch.cat([dkw.reshape(-1), dkb, dconv.reshape(-1), deps.reshape(1), dw, dg.reshape(1)],
+                      out=grads[layer])
         if world > 1:
             dist.all_reduce(grads)
         return grads
 
     if args.profile_step:
-        step(r, v, dq_out, dfast)
-        step(r, v, dq_out, dfast)
+        step(h, v, dq_out, dfast)
+        step(h, v, dq_out, dfast)
         torch.cuda.synchronize()
         if world > 1:
             dist.destroy_process_group()
@@ -355,14 +380,14 @@ def main():
     # the sampler starts with the warm-up so that short timed regions still see >= 1 sample under load
     with ClockSampler(local) as clocks:
         for _ in range(args.warmup):
-            step(r, v, dq_out, dfast)
+            step(h, v, dq_out, dfast)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         ev0.record()
         for _ in range(args.steps):
-            step(r, v, dq_out, dfast)
+            step(h, v, dq_out, dfast)
         ev1.record()
         torch.cuda.synchronize()
     if world > 1:
@@ -377,8 +402,8 @@ def main():
         raise RuntimeError("a kernel reported a device-side error during the bench")
 
     # e2e: inputs copied from pinned host memory every step, parameter gradients read back
-    host = [t.cpu().pin_memory() for t in (r, v, dq_out, dfast)]
-    dev_in = [torch.empty_like(t) for t in (r, v, dq_out, dfast)]
+    host = [t.cpu().pin_memory() for t in (h, v, dq_out, dfast)]
+    dev_in = [torch.empty_like(t) for t in (h, v, dq_out, dfast)]
     host_out = torch.empty(grads.shape, dtype=grads.dtype).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = host_out.numel() * host_out.element_size()
@@ -407,6 +432,9 @@ def main():
     del dev_in, host
 
     # roofline of the dominant kernel family (tensor-core products), CUDA events per launch
+    blk0 = blocks[0]
+    g, w = blk0["g"], blk0["w"]
+    r, _, _, _ = address_fwd(h, blk0["conv"], blk0["key_w"], blk0["key_b"], blk0["eps"], prec)
     q, fast, c, qop, kop, vop, P = memory_fwd(r, v, g, w, prec)
     ldd, ldt = L_.lib().ulm_operand_ld(W["D"]), L_.lib().ulm_operand_ld(W["T"])
     opt = qop.dtype
@@ -432,9 +460,9 @@ def main():
         threads = os.cpu_count() or 1
         s = cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 2, threads)
         cpu = {"value": W["T"] / (W["L"] * s), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd x2, chunked "
-                         "pure-PyTorch form (test_all.py:28-51 restated in oracle/memory.py), fp32, "
-                         "scaled to 12 blocks"}
+               "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd x2, prologue + chunked "
+                         "pure-PyTorch form (model.py:70-79, test_all.py:28-51 restated in oracle/memory.py), "
+                         "fp32, scaled to 12 blocks"}
 
     decode = None
     if not args.no_decode:
@@ -442,13 +470,15 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = runc_decode_baseline()
 
-    # kernels of ours per step: per block fwd 4 (stats, convert, scores, read), bwd 7 (convert,
-    # scores, 3 reads, stats, finalize)
-    launches = args.steps * W["L"] * 11
+    # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, normalise); operator fwd 4
+    # (stats, convert, scores, read); operator bwd 8 (convert, memset-free scores, 3 reads, stats scan,
+    # dw, dg); prologue bwd 8 (addr_bwd, db, deps, dK GEMM, dK sum, du GEMM, conv bwd, dconv sum)
+    launches = args.steps * W["L"] * (3 + 4 + 7 + 8)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-            "config": {"workload": "unified_memory fwd+bwd x 12 blocks (110M shape), 16 seq x 1024 tok per GPU",
+            "config": {"workload": "fast-memory path fwd+bwd (addressing prologue + unified_memory) x 12 blocks "
+                                   "(110M shape), 16 seq x 1024 tok per GPU",
                        "B_per_gpu": W["B"], "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"],
                        "lam": W["lam"], "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (r is 134 MB), no flush"},
