@@ -11,6 +11,7 @@
 // The contractions run on the GEMM engine (gemm.cu): tcgen05 with bf16 operands, or fp32 FMA in the
 // fp32 parity mode. Column sums (db, dconv) go through per-CTA partials reduced in a fixed order.
 #include <algorithm>
+#include <cstring>
 
 #include "gemm.cuh"
 
@@ -34,21 +35,71 @@ __device__ __forceinline__ void st_as(void* p, int64_t i, float v, int dt) {
     static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
 }
 
-// u[b,t,d] = sum_j conv_w[d, j] * h[b, t-K+1+j, d] (zero before the sequence start)
 template <typename InT>
-__global__ void addr_conv_kernel(const void* __restrict__ h, const float* __restrict__ conv_w, void* __restrict__ u,
-                                 int u_dtype, int64_t ld_u, int T, int D, int K, int64_t rows) {
-  const int64_t n = rows * D;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / D;
-    const int d = (int)(i - row * D);
-    const int t = (int)(row % T);
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-      const int tt = t - K + 1 + j;
-      if (tt >= 0) acc = fmaf(conv_w[d * K + j], ld_as_float<InT>(h, (row - t + tt) * D + d), acc);
+__device__ __forceinline__ float4 ld4(const void* p, int64_t i);
+template <>
+__device__ __forceinline__ float4 ld4<float>(const void* p, int64_t i) {
+  return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+}
+template <>
+__device__ __forceinline__ float4 ld4<__nv_bfloat16>(const void* p, int64_t i) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i);
+  __nv_bfloat162 a, b;
+  memcpy(&a, &raw.x, 4);
+  memcpy(&b, &raw.y, 4);
+  const float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  return make_float4(fa.x, fa.y, fb.x, fb.y);
+}
+
+__device__ __forceinline__ void st4(void* p, int64_t i, float4 v, int dt) {
+  if (dt == ULM_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = v;
+  } else {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    uint2 raw;
+    memcpy(&raw.x, &a, 4);
+    memcpy(&raw.y, &b, 4);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) = raw;
+  }
+}
+
+__device__ __forceinline__ float4 fma4(float4 w, float4 x, float4 acc) {
+  return make_float4(fmaf(w.x, x.x, acc.x), fmaf(w.y, x.y, acc.y), fmaf(w.z, x.z, acc.z), fmaf(w.w, x.w, acc.w));
+}
+
+constexpr int CONV_ROWS = 64;  // positions per CTA of the conv kernels
+constexpr int CONV_MAXK = 8;
+
+// u[b,t,d] = sum_j conv_w[d, j] * h[b, t-K+1+j, d] (zero before the sequence start).
+// CTA = (batch row, CONV_ROWS positions); a thread owns 4 channels and slides a window of the last
+// K rows of h down its positions, so every row of h is read once (plus K-1 halo rows).
+template <typename InT, int K>
+__global__ void __launch_bounds__(256)
+    addr_conv_kernel(const void* __restrict__ h, const float* __restrict__ conv_w, void* __restrict__ u, int u_dtype,
+                     int64_t ld_u, int T, int D) {
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * CONV_ROWS, t1 = min(T, t0 + CONV_ROWS);
+  for (int d4 = threadIdx.x * 4; d4 < D; d4 += blockDim.x * 4) {
+    float4 w[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+      w[j] = make_float4(conv_w[(d4 + 0) * K + j], conv_w[(d4 + 1) * K + j], conv_w[(d4 + 2) * K + j],
+                         conv_w[(d4 + 3) * K + j]);
+    float4 win[K];  // win[j] = h[t-K+1+j]
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
+      const int tt = t0 - K + 1 + j;
+      win[j] = tt >= 0 ? ld4<InT>(h, ((int64_t)b * T + tt) * D + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    st_as(u, row * ld_u + d, acc, u_dtype);
+    for (int t = t0; t < t1; ++t) {
+      win[K - 1] = ld4<InT>(h, ((int64_t)b * T + t) * D + d4);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  #pragma unroll
+    for (int j = 0; j < K; ++j) acc = fma4(w[j], win[j], acc);
+      st4(u, ((int64_t)b * T + t) * ld_u + d4, acc, u_dtype);
+  #pragma unroll
+    for (int j = 0; j + 1 < K; ++j) win[j] = win[j + 1];
+    }
   }
 }
 
@@ -73,51 +124,62 @@ __global__ void addr_normalize_kernel(float* __restrict__ zr, float* __restrict_
   if (lane == 0) den[row] = dn;
 }
 
-// one warp per row: s = sum dr r, da = 2 sqrt(r den) (dr - s) / den; the CTA also sums da over its
-// rows per column (db partial) and -s/den over its rows (d eps partial)
-template <int WARPS>
-__global__ void __launch_bounds__(32 * WARPS)
+// one warp per row: s = sum dr r, then da = 2 sqrt(r den) (dr - s) / den; -s/den summed per CTA
+// (d eps partial). Rows are read with 16-byte loads; the second pass over a row hits L1.
+__global__ void __launch_bounds__(256)
     addr_bwd_kernel(const float* __restrict__ dr, const float* __restrict__ r, const float* __restrict__ den,
-                    void* __restrict__ da, int da_dtype, int64_t ld_da, float* __restrict__ db_part,
-                    float* __restrict__ deps_part, int64_t rows, int M, int rows_per_cta) {
-  extern __shared__ float col_acc[];  // [WARPS][M]
-  __shared__ float deps_w[WARPS];
+                    void* __restrict__ da, int da_dtype, int64_t ld_da, float* __restrict__ deps_part, int64_t rows,
+                    int M, int rows_per_cta) {
+  __shared__ float deps_w[8];
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int m = threadIdx.x; m < WARPS * M; m += blockDim.x) col_acc[m] = 0.f;
-  __syncthreads();
   float deps_acc = 0.f;
   const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
-  for (int rr = wp; rr < rows_per_cta; rr += WARPS) {
+  for (int rr = wp; rr < rows_per_cta; rr += 8) {
     const int64_t row = row0 + rr;
     if (row >= rows) break;
     const float* drr = dr + row * M;
     const float* rrow = r + row * M;
     float s = 0.f;
-    for (int m = lane; m < M; m += 32) s = fmaf(drr[m], rrow[m], s);
+    for (int m = lane * 4; m < M; m += 128) {
+      const float4 a = *reinterpret_cast<const float4*>(drr + m);
+      const float4 c = *reinterpret_cast<const float4*>(rrow + m);
+      s = fmaf(a.x, c.x, fmaf(a.y, c.y, fmaf(a.z, c.z, fmaf(a.w, c.w, s))));
+    }
     s = warp_sum(s);
     const float dn = den[row];
     const float inv = 1.0f / dn;
     deps_acc -= s * inv;
-    float* acc = col_acc + wp * M;
-    for (int m = lane; m < M; m += 32) {
-      const float rv = rrow[m];
-      const float dav = 2.f * sqrtf(rv * dn) * ((drr[m] - s) * inv);
-      st_as(da, row * ld_da + m, dav, da_dtype);
-      acc[m] += dav;
+    for (int m = lane * 4; m < M; m += 128) {
+      const float4 a = *reinterpret_cast<const float4*>(drr + m);
+      const float4 c = *reinterpret_cast<const float4*>(rrow + m);
+      float4 o;
+      o.x = 2.f * sqrtf(c.x * dn) * ((a.x - s) * inv);
+      o.y = 2.f * sqrtf(c.y * dn) * ((a.y - s) * inv);
+      o.z = 2.f * sqrtf(c.z * dn) * ((a.z - s) * inv);
+      o.w = 2.f * sqrtf(c.w * dn) * ((a.w - s) * inv);
+      st4(da, row * ld_da + m, o, da_dtype);
     }
   }
   if (lane == 0) deps_w[wp] = deps_acc;
   __syncthreads();
-  for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    float t = 0.f;
-    for (int w = 0; w < WARPS; ++w) t += col_acc[w * M + m];
-    db_part[(int64_t)blockIdx.x * M + m] = t;
-  }
   if (threadIdx.x == 0) {
     float t = 0.f;
-    for (int w = 0; w < WARPS; ++w) t += deps_w[w];
+    for (int w = 0; w < 8; ++w) t += deps_w[w];
     deps_part[blockIdx.x] = t;
   }
+}
+
+// column sums of a (rows x cols) operand-type array over chunks of rows: part[chunk][col]
+template <typename InT>
+__global__ void col_sum_kernel(const void* __restrict__ x, int64_t ld, int64_t rows, int cols, int rows_per_chunk,
+                               float* __restrict__ part) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= cols) return;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
+  const int64_t r1 = min(rows, r0 + rows_per_chunk);
+  float s = 0.f;
+  for (int64_t rr = r0; rr < r1; ++rr) s += ld_as_float<InT>(x, rr * ld + col);
+  part[(int64_t)blockIdx.y * cols + col] = s;
 }
 
 // out[i] = sum_p part[p][i] over nparts, in order (dK from the split-K partials, db)
@@ -143,45 +205,56 @@ __global__ void __launch_bounds__(256) sum_all_kernel(const float* __restrict__ 
   if (threadIdx.x == 0) *out = (float)red[0];
 }
 
-// dh and the conv-weight partials. CTA = 32 channels x 8 time lanes over a chunk of positions of one
-// batch row; dconv partial per (chunk, b) reduced later.
-template <typename InT>
+// dh[t] = sum_j w[j] du[t+K-1-j] and the conv-weight partials dconv[j] += du[t] h[t-K+1+j], CTA =
+// (batch row, CONV_ROWS positions), thread = 4 channels with windows of du (ahead) and h (behind);
+// each CTA writes its dconv partial, reduced later in a fixed order.
+template <typename InT, int K>
 __global__ void __launch_bounds__(256)
     addr_conv_bwd_kernel(const float* __restrict__ du, const void* __restrict__ h, const float* __restrict__ conv_w,
-                         float* __restrict__ dh, float* __restrict__ dconv_part, int T, int D, int K, int t_chunk) {
-  __shared__ float red[8][32][8];  // [time lane][channel][tap], K <= 8
-  const int lane = threadIdx.x & 31, tl = threadIdx.x >> 5;
-  const int d = blockIdx.x * 32 + lane;
+                         float* __restrict__ dh, float* __restrict__ dconv_part, int T, int D) {
   const int b = blockIdx.y;
-  const int t0 = blockIdx.z * t_chunk, t1 = min(T, t0 + t_chunk);
-  float acc[8];
+  const int t0 = blockIdx.x * CONV_ROWS, t1 = min(T, t0 + CONV_ROWS);
+  const int64_t part = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int d4 = threadIdx.x * 4; d4 < D; d4 += blockDim.x * 4) {
+    float4 w[K], acc[K];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-  if (d < D) {
-    const int64_t base = (int64_t)b * T;
-    for (int t = t0 + tl; t < t1; t += 8) {
-      float g = 0.f;
-      for (int j = 0; j < K; ++j) {
-        const int tt = t + K - 1 - j;  // output position that used h[t] through tap j
-        if (tt < T) g = fmaf(conv_w[d * K + j], du[(base + tt) * D + d], g);
-      }
-      dh[(base + t) * D + d] = g;
-      const float dut = du[(base + t) * D + d];
-      for (int j = 0; j < K; ++j) {
-        const int ts = t - K + 1 + j;
-        if (ts >= 0) acc[j] = fmaf(dut, ld_as_float<InT>(h, (base + ts) * D + d), acc[j]);
+    for (int j = 0; j < K; ++j) {
+      w[j] = make_float4(conv_w[(d4 + 0) * K + j], conv_w[(d4 + 1) * K + j], conv_w[(d4 + 2) * K + j],
+                         conv_w[(d4 + 3) * K + j]);
+      acc[j] = z4;
+    }
+    float4 hw[K];   // hw[j] = h[t-K+1+j]
+    float4 dw[K];   // dw[j] = du[t+j]
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) {
+      const int tt = t0 - K + 1 + j;
+      hw[j] = tt >= 0 ? ld4<InT>(h, ((int64_t)b * T + tt) * D + d4) : z4;
+      const int tf = t0 + j;
+      dw[j] = tf < T ? *reinterpret_cast<const float4*>(du + ((int64_t)b * T + tf) * D + d4) : z4;
+    }
+    for (int t = t0; t < t1; ++t) {
+      hw[K - 1] = ld4<InT>(h, ((int64_t)b * T + t) * D + d4);
+      const int tf = t + K - 1;
+      dw[K - 1] = tf < T ? *reinterpret_cast<const float4*>(du + ((int64_t)b * T + tf) * D + d4) : z4;
+      float4 g = z4;
+  #pragma unroll
+    for (int j = 0; j < K; ++j) g = fma4(w[j], dw[K - 1 - j], g);
+      *reinterpret_cast<float4*>(dh + ((int64_t)b * T + t) * D + d4) = g;
+  #pragma unroll
+    for (int j = 0; j < K; ++j) acc[j] = fma4(dw[0], hw[j], acc[j]);
+  #pragma unroll
+    for (int j = 0; j + 1 < K; ++j) {
+        hw[j] = hw[j + 1];
+        dw[j] = dw[j + 1];
       }
     }
-  }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) red[tl][lane][j] = acc[j];
-  __syncthreads();
-  if (tl == 0 && d < D) {
-    const int64_t part = (int64_t)blockIdx.z * gridDim.y + blockIdx.y;
     for (int j = 0; j < K; ++j) {
-      float s = 0.f;
-      for (int l = 0; l < 8; ++l) s += red[l][lane][j];
-      dconv_part[(part * D + d) * K + j] = s;
+      dconv_part[(part * D + d4 + 0) * K + j] = acc[j].x;
+      dconv_part[(part * D + d4 + 1) * K + j] = acc[j].y;
+      dconv_part[(part * D + d4 + 2) * K + j] = acc[j].z;
+      dconv_part[(part * D + d4 + 3) * K + j] = acc[j].w;
     }
   }
 }
@@ -207,22 +280,22 @@ struct AddrBwdWork {
   void* da;         // rows x ld_m, op dtype
   float* du;        // rows x D
   float* dk_part;   // S x M x D
-  float* db_part;   // ctas x M
+  float* db_part;   // db_chunks x M
   float* deps_part; // ctas
   float* dconv_part;
   int64_t ld_m;
-  int S, ctas, chunks;
+  int S, ctas, chunks, db_chunks;
   int64_t bytes;
 };
 
-constexpr int ADDR_ROWS_PER_CTA = 64;
-constexpr int ADDR_CONV_CHUNK = 64;
+constexpr int ADDR_ROWS_PER_CTA = 32;
+constexpr int DB_ROWS_PER_CHUNK = 256;
 
 inline int64_t al256(int64_t n) { return (n + 255) / 256 * 256; }
 
 inline int addr_split(int64_t rows) {
   // split the B*T contraction of dK into S chunks so the product has enough tiles
-  for (int s = 8; s > 1; s /= 2)
+  for (int s = 4; s > 1; s /= 2)
     if (rows % s == 0 && rows / s >= 256) return s;
   return 1;
 }
@@ -233,7 +306,8 @@ inline AddrBwdWork carve_addr_work(void* base, int64_t B, int64_t T, int64_t D, 
   w.ld_m = ulm_operand_ld(M);
   w.S = addr_split(rows);
   w.ctas = (int)cdiv(rows, ADDR_ROWS_PER_CTA);
-  w.chunks = (int)cdiv(T, ADDR_CONV_CHUNK);
+  w.chunks = (int)cdiv(T, CONV_ROWS);
+  w.db_chunks = (int)cdiv(rows, DB_ROWS_PER_CHUNK);
   char* p = static_cast<char*>(base);
   char* p0 = p;
   auto take = [&](int64_t bytes) {
@@ -244,9 +318,9 @@ inline AddrBwdWork carve_addr_work(void* base, int64_t B, int64_t T, int64_t D, 
   w.da = take(rows * w.ld_m * (op_dt == ULM_F32 ? 4 : 2));
   w.du = reinterpret_cast<float*>(take(rows * D * 4));
   w.dk_part = reinterpret_cast<float*>(take((int64_t)w.S * M * D * 4));
-  w.db_part = reinterpret_cast<float*>(take((int64_t)w.ctas * M * 4));
+  w.db_part = reinterpret_cast<float*>(take((int64_t)w.db_chunks * M * 4));
   w.deps_part = reinterpret_cast<float*>(take((int64_t)w.ctas * 4));
-  w.dconv_part = reinterpret_cast<float*>(take((int64_t)w.chunks * B * D * 8 * 4));
+  w.dconv_part = reinterpret_cast<float*>(take((int64_t)w.chunks * B * D * CONV_MAXK * 4));
   w.bytes = p - p0;
   return w;
 }
@@ -263,6 +337,7 @@ int addr_check(int h_dtype, int prec, int64_t B, int64_t T, int64_t D, int64_t M
   ULM_REQUIRE(B > 0 && T > 0 && D > 0 && M > 0, "empty problem");
   ULM_REQUIRE(K >= 1 && K <= 8, "conv_size must be in [1, 8]");
   ULM_REQUIRE(B * T < (1ll << 31) && M < (1 << 30) && D < (1 << 30), "extent too large");
+  ULM_REQUIRE(D % 4 == 0 && M % 4 == 0, "the addressing kernels need D %% 4 == 0 and M %% 4 == 0");
   return ULM_OK;
 }
 
@@ -277,12 +352,17 @@ extern "C" int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16;
   const int64_t rows = B * T;
-  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows * D, 256), 16 * 148);
-  if (h_dtype == ULM_F32)
-    addr_conv_kernel<float><<<grid, 256, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D, (int)conv_size, rows);
-  else
-    addr_conv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D, (int)conv_size,
-                                                          rows);
+  dim3 cgrid((unsigned)cdiv(T, CONV_ROWS), (unsigned)B);
+  const int cthreads = (int)std::min<int64_t>(256, cdiv(D, 4));
+#define ULM_CONV(KK)                                                                                            \
+  if (conv_size == KK) {                                                                                        \
+    if (h_dtype == ULM_F32)                                                                                     \
+      addr_conv_kernel<float, KK><<<cgrid, cthreads, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D);       \
+    else                                                                                                        \
+      addr_conv_kernel<__nv_bfloat16, KK><<<cgrid, cthreads, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D); \
+  }
+  ULM_CONV(1) ULM_CONV(2) ULM_CONV(3) ULM_CONV(4) ULM_CONV(5) ULM_CONV(6) ULM_CONV(7) ULM_CONV(8)
+#undef ULM_CONV
   ULM_LAUNCH_CHECK("addr_conv_kernel");
   // z = relu(u K^T + b)^2 written into r
   Operand A{u_op, ld_u, rows * ld_u, D, rows, dt, false};
@@ -311,16 +391,21 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   const int dt = prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16;
   const int64_t rows = B * T;
   AddrBwdWork wk = carve_addr_work(work, B, T, D, M, dt);
-  // da, and the db / d eps partials
-  constexpr int W = 8;
-  const size_t smem = (size_t)W * M * sizeof(float);
-  ULM_REQUIRE(smem <= 200 * 1024, "M too large for the addressing backward (M <= 6400)");
-  ULM_CUDA_TRY(cudaFuncSetAttribute(addr_bwd_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  addr_bwd_kernel<W><<<(unsigned)wk.ctas, 32 * W, smem, st>>>(dr, r, den, wk.da, dt, wk.ld_m, wk.db_part,
-                                                              wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
+  // da and the d eps partials
+  addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M,
+                                                     ADDR_ROWS_PER_CTA);
   ULM_LAUNCH_CHECK("addr_bwd_kernel");
-  sum_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(wk.db_part, wk.ctas, M, dkey_b);
-  ULM_LAUNCH_CHECK("sum_parts_kernel");
+  // db = column sums of da
+  {
+    dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
+    if (dt == ULM_F32)
+      col_sum_kernel<float><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
+    else
+      col_sum_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
+    ULM_LAUNCH_CHECK("col_sum_kernel");
+    sum_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(wk.db_part, wk.db_chunks, M, dkey_b);
+    ULM_LAUNCH_CHECK("sum_parts_kernel");
+  }
   sum_all_kernel<<<1, 256, 0, st>>>(wk.deps_part, wk.ctas, deps);
   ULM_LAUNCH_CHECK("sum_all_kernel");
   // dK = da^T u, split over S chunks of rows (each chunk a GEMM batch), then summed in order
@@ -344,13 +429,19 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
     if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
   }
   // through the conv
-  dim3 grid((unsigned)cdiv(D, 32), (unsigned)B, (unsigned)wk.chunks);
-  if (h_dtype == ULM_F32)
-    addr_conv_bwd_kernel<float><<<grid, 256, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, (int)T, (int)D,
-                                                       (int)conv_size, ADDR_CONV_CHUNK);
-  else
-    addr_conv_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, (int)T, (int)D,
-                                                               (int)conv_size, ADDR_CONV_CHUNK);
+  dim3 grid((unsigned)wk.chunks, (unsigned)B);
+  const int cthreads = (int)std::min<int64_t>(256, cdiv(D, 4));
+#define ULM_CONVB(KK)                                                                                        \
+  if (conv_size == KK) {                                                                                     \
+    if (h_dtype == ULM_F32)                                                                                  \
+      addr_conv_bwd_kernel<float, KK><<<grid, cthreads, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, (int)T, \
+                                                                  (int)D);                                    \
+    else                                                                                                     \
+      addr_conv_bwd_kernel<__nv_bfloat16, KK><<<grid, cthreads, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, \
+                                                                          (int)T, (int)D);                    \
+  }
+  ULM_CONVB(1) ULM_CONVB(2) ULM_CONVB(3) ULM_CONVB(4) ULM_CONVB(5) ULM_CONVB(6) ULM_CONVB(7) ULM_CONVB(8)
+#undef ULM_CONVB
   ULM_LAUNCH_CHECK("addr_conv_bwd_kernel");
   sum_parts_kernel<<<(unsigned)cdiv(D * conv_size, 256), 256, 0, st>>>(wk.dconv_part, (int64_t)wk.chunks * B,
                                                                        D * conv_size, dconv_w);
