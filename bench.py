@@ -353,21 +353,22 @@ def main():
     prec = PRECISION[args.precision]
     h, v, dq_out, dfast, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
                                               seed=rank)
-    per_block = W["M"] * W["D"] + W["M"] + W["D"] * 4 + 1 + W["M"] + 1
-    grads = torch.zeros(W["L"], per_block, device=dev)
+    from unifiedlm_c_b200.dp import GradBucket
+    M_, D_ = W["M"], W["D"]
+    bucket = GradBucket([(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"], device=dev)
 
     def step(h_, v_, dq_, df_):
-        for layer, blk in enumerate(blocks):
+        grads = []
+        for blk in blocks:
             r, den, u_op, kw = address_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], prec)
             q, fast, c, qop, kop, vop, P = memory_fwd(r, v_, blk["g"], blk["w"], prec)
             dr, dv, dg, dw = memory_bwd(dq_, df_, r, blk["g"], blk["w"], q, c, qop, kop, vop, P, prec)
             dh, dconv, dkw, dkb, deps = address_bwd(dr, r, den, u_op, kw, h_, blk["conv"], prec)
-            # the block's parameter gradients, gathered for the all-reduce (and the e2e read-back)
-            torch.cat([dkw.reshape(-1), dkb, dconv.reshape(-1), deps.reshape(1), dw, dg.reshape(1)],
-                      out=grads[layer])
-        if world > 1:
-            dist.all_reduce(grads)
-        return grads
+            grads += [dkw, dkb, dconv, deps, dw, dg]
+        # the path's parameter gradients in one bucket: one NCCL all-reduce per step (DP average)
+        bucket.pack(grads)
+        bucket.all_reduce(average=True)
+        return bucket.flat
 
     if args.profile_step:
         step(h, v, dq_out, dfast)
@@ -404,7 +405,7 @@ def main():
     # e2e: inputs copied from pinned host memory every step, parameter gradients read back
     host = [t.cpu().pin_memory() for t in (h, v, dq_out, dfast)]
     dev_in = [torch.empty_like(t) for t in (h, v, dq_out, dfast)]
-    host_out = torch.empty(grads.shape, dtype=grads.dtype).pin_memory()
+    host_out = torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory()
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = host_out.numel() * host_out.element_size()
 
