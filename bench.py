@@ -178,6 +178,10 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (read + write) of the six fast-memory products of one block at the 110M shape, summed
+# over one ncu capture of `bench.py --profile-step` (the launch list in profiles/)
+PRODUCTS_DRAM_BYTES = 770134528
+
 DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
 
 
@@ -450,7 +454,10 @@ def main():
     pk = peaks()
     achieved = flops / psecs / 1e12
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None,
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": PRODUCTS_DRAM_BYTES,
+                "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the six products of one block, "
+                                "one ncu capture (profiles/fast_memory_path_step_110M_launches.md)",
+                "algorithmic_flops_per_block": flops,
                 "kernel": "tc_gemm_kernel (6 causal products per block fwd+bwd)",
                 "peak_source": pk["source"],
                 "per_launch_ms": [round(s * 1e3, 4) for _, s in per],
