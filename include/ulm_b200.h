@@ -136,6 +136,11 @@ int ulm_causal_apply(const void* P, int64_t ldp, const void* c, int64_t ldc, voi
 /* Padded row stride used for the operand copies of a length-n row (multiple of 8 elements). */
 int64_t ulm_operand_ld(int64_t n);
 
+/* Library-wide choice for bf16 products with M, N >= 256: 1 (default) runs them on CTA pairs with the
+ * 2-SM MMA (256 x 256 tiles), 0 on single CTAs (128 x 256 tiles). Returns the previous setting.
+ * Both compute the same products; the switch exists for comparisons and tuning. */
+int ulm_set_gemm_pairs(int enable);
+
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
  * Outputs: q (B,T,M) fp32; fast (B,T,D) of type v_dtype.

@@ -226,3 +226,41 @@ def test_stats_kernels_through_c_abi(T):
         torch.cuda.synchronize()
         assert rel(dr2, dr) < 1e-6 and rel(dw2, dw) < 1e-6 and rel(dg2, dg) < 1e-6
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("kind", ["scores", "read", "read_t"])
+def test_pair_and_single_cta_products_agree(kind):
+    """The 2-SM (CTA pair) and single-CTA tensor-core kernels compute the same products."""
+    torch.manual_seed(1)
+    B, T, K, V = 2, 640, 384, 512
+    lib = L.lib()
+    ldk, ldt, ldv = operand_ld(K), operand_ld(T), operand_ld(V)
+    a = torch.randn(B, T, ldk, device=DEV).bfloat16()
+    b = torch.randn(B, T, ldk, device=DEV).bfloat16()
+    c = torch.randn(B, T, ldv, device=DEV).bfloat16()
+    g = torch.tensor([-0.01], device=DEV)
+    outs = []
+    for pairs in (1, 0):
+        old = lib.ulm_set_gemm_pairs(pairs)
+        try:
+            P = torch.zeros(B, T, ldt, device=DEV, dtype=torch.bfloat16)
+            st = L.stream_of(P)
+            L.check(lib.ulm_decayed_scores(L.ptr(a), ldk, L.ptr(b), ldk, L.ptr(P), ldt, L.ptr(g), B, T, K,
+                                           L.ULM_PREC_BF16, st))
+            if kind == "scores":
+                outs.append(P[..., :T].float())
+            else:
+                o = torch.empty(B, T, V, device=DEV)
+                L.check(lib.ulm_causal_apply(L.ptr(P), ldt, L.ptr(c), ldv, L.ptr(o), V, L.ULM_F32,
+                                             1 if kind == "read_t" else 0, B, T, V, L.ULM_PREC_BF16, st))
+                outs.append(o)
+            torch.cuda.synchronize()
+        finally:
+            lib.ulm_set_gemm_pairs(old)
+    assert rel(outs[0], outs[1].double().cpu()) < 1e-6
+    t = torch.arange(T, device=DEV, dtype=torch.float32)
+    Dm = torch.where(t[:, None] >= t[None, :], torch.exp(g * (t[:, None] - t[None, :])), torch.zeros(()))
+    ref = (a[..., :K].float() @ b[..., :K].float().transpose(1, 2)) * Dm
+    if kind == "scores":
+        assert rel(outs[0], ref.double().cpu()) < 5e-3
+    assert L.device_error() == 0

@@ -367,6 +367,228 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // ------------------------------------------------------------------------------------------------
+// tensor-core back end, CTA pairs: 256 x 256 tiles with the 2-SM MMA (tcgen05 cta_group::2)
+//
+// A cluster of two CTAs computes one 256 x 256 tile: each CTA loads its 128 rows of A and its 128
+// columns of B (so every SM streams half of B), the leader (cluster rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256, N = 256, and each CTA's TMEM receives its 128 rows. Stage
+// hand-off: both CTAs' TMA loads complete on the leader's `full` barrier (the leader posts the
+// expected bytes of both), the leader's commit arrives on `empty` / `tfull` of both CTAs, and both
+// CTAs' epilogue warps arrive on the leader's `tempty`.
+
+constexpr int TC2_BN = 256;
+constexpr int TC2_STAGES = 6;
+
+struct Tc2Config {
+  static constexpr uint32_t A_BYTES = 128 * TC_BK * 2;  // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = 128 * TC_BK * 2;  // this CTA's 128 columns of B
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * TC2_BN;
+  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+    tc2_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
+                    const int tiles_per_batch, const int total_tiles) {
+  using Cfg = Tc2Config;
+  constexpr int STAGES = TC2_STAGES;
+  constexpr int BM = 256, BN = TC2_BN;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+  constexpr uint32_t SBO = 1024;
+  constexpr uint32_t MN_LBO = TC_BK * 128;
+  constexpr uint32_t A_KSTEP = A_MN ? 16 * 128 : 32;
+  constexpr uint32_t B_KSTEP = B_MN ? 16 * 128 : 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM of the pair allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (both CTAs) ----------------
+      const uint32_t leader_full = mapa_shared(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += pairs) {
+        const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+        const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int row0 = tc.mb * BM + (int)rank * 128;
+        const int col0 = tc.nb * BN + (int)rank * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sb = sa + Cfg::A_BYTES;
+          const uint32_t bar = leader_full + (uint32_t)(stage * sizeof(uint64_t));
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+          const int k0 = kb * TC_BK;
+          if (!A_MN) {
+            tma_load_3d_pair(&tma_a, sa, bar, k0, row0, tc.b);
+          } else {
+            tma_load_3d_pair(&tma_a, sa, bar, row0, k0, tc.b);
+            tma_load_3d_pair(&tma_a, sa + MN_LBO, bar, row0 + 64, k0, tc.b);
+          }
+          if (!B_MN) {
+            tma_load_3d_pair(&tma_b, sb, bar, k0, col0, tc.b);
+          } else {
+            tma_load_3d_pair(&tma_b, sb, bar, col0, k0, tc.b);
+            tma_load_3d_pair(&tma_b, sb + MN_LBO, bar, col0 + 64, k0, tc.b);
+          }
+          issued = min(issued + 1, STAGES);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && leader) {
+        for (int i = 0; i < issued; ++i) {
+          if (--stage < 0) {
+            stage = STAGES - 1;
+            phase ^= 1u;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[stage], phase) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader CTA) ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int j = 0;
+      bool ok = true, issued_any = false;
+      for (int t = pair; t < total_tiles && ok; t += pairs, ++j) {
+        const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+        const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int acc = j & 1;
+        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM2_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
+            const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
+            umma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit_pair(&empty[stage], 0x3);  // frees this stage in both CTAs
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);  // both halves of the accumulator ready
+      }
+      if (!ok && issued_any) {
+        umma_commit_pair(drain, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int quad = warp & 3;
+    const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
+    const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
+    const uint32_t leader_tempty = mapa_shared(smem_u32(tempty), 0);
+    int j = 0;
+    for (int t = pair; t < total_tiles; t += pairs, ++j) {
+      const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+      const int acc = j & 1;
+      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+      if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, DEVERR_GEMM2_WAIT)) break;
+      tc_fence_after();
+      const int row = tc.mb * BM + row_in_tile;
+      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      float dg_acc = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld_32x32(taddr + (uint32_t)c, v);
+        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty + (uint32_t)(acc * sizeof(uint64_t)));
+      if (epi.kind == EPI_DECAY_DG) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
+        if (lane == 0) epi.tile_partial[8 * (int64_t)t + rank * 4 + (warp - 2)] = dg_acc;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // all MMAs done and all TMEM reads finished in both CTAs
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // FMA back end
 
 template <bool A_MN, bool B_MN>
@@ -466,6 +688,9 @@ __global__ void __launch_bounds__(256)
 // ------------------------------------------------------------------------------------------------
 // host side
 
+// whether large products use the CTA-pair (2-SM MMA) kernel; ulm_set_gemm_pairs switches it
+static int g_gemm_pairs = 1;
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -544,6 +769,46 @@ int dispatch_tc_major(const Operand& A, const Operand& B, const GemmShape& s, co
 }
 
 template <bool A_MN, bool B_MN>
+int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+  using Cfg = Tc2Config;
+  CUtensorMap ta, tb;
+  int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : 128);
+  if (rc) return rc;
+  rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : 128);
+  if (rc) return rc;
+  const int dev = current_device();
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) {
+    set_error("device ordinal %d out of range", dev);
+    return ULM_ERR_INVALID;
+  }
+  if (!configured[dev]) {
+    ULM_CUDA_TRY(cudaFuncSetAttribute(tc2_gemm_kernel<A_MN, B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Cfg::SMEM_BYTES));
+    configured[dev] = true;
+  }
+  const int m_blocks = (int)cdiv(s.M, 256), n_blocks = (int)cdiv(s.N, TC2_BN);
+  const int tpb = tiles_per_batch_host(s, 256, TC2_BN, m_blocks, n_blocks);
+  const int64_t total64 = (int64_t)tpb * s.batches;
+  ULM_REQUIRE(total64 < (1ll << 31), "too many tiles (%lld)", (long long)total64);
+  const int total = (int)total64;
+  if (total == 0) return ULM_OK;
+  const int max_pairs = sm_count(dev) / 2;
+  const int pairs = total < max_pairs ? total : max_pairs;
+  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, s, e, m_blocks, n_blocks, tpb,
+                                                                           total);
+  ULM_LAUNCH_CHECK("tc2_gemm_kernel");
+  return ULM_OK;
+}
+
+int dispatch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+  if (!A.mn_major && !B.mn_major) return launch_tc2<false, false>(A, B, s, e, st);
+  if (!A.mn_major && B.mn_major) return launch_tc2<false, true>(A, B, s, e, st);
+  if (A.mn_major && !B.mn_major) return launch_tc2<true, false>(A, B, s, e, st);
+  return launch_tc2<true, true>(A, B, s, e, st);
+}
+
+template <bool A_MN, bool B_MN>
 int launch_simt(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
   const int m_blocks = (int)cdiv(s.M, 64), n_blocks = (int)cdiv(s.N, 64);
   const int tpb = tiles_per_batch_host(s, 64, 64, m_blocks, n_blocks);
@@ -579,6 +844,7 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
                 "bf16 operand strides must be multiples of 8 elements (lda=%lld ldb=%lld)", (long long)A.ld,
                 (long long)B.ld);
     ULM_REQUIRE(A.ld >= A.inner && B.ld >= B.inner, "row stride shorter than the row");
+    if (s.N >= 256 && s.M >= 256 && g_gemm_pairs) return dispatch_tc2(A, B, s, e, stream);
     if (s.N >= 256) return dispatch_tc_major<256>(A, B, s, e, stream);
     return dispatch_tc_major<128>(A, B, s, e, stream);
   }

@@ -174,6 +174,12 @@ extern "C" int ulm_device_error(int* site) {
 
 extern "C" int64_t ulm_operand_ld(int64_t n) { return ((n + 7) / 8) * 8; }
 
+extern "C" int ulm_set_gemm_pairs(int enable) {
+  const int old = g_gemm_pairs;
+  g_gemm_pairs = enable ? 1 : 0;
+  return old;
+}
+
 extern "C" int ulm_decayed_scores(const void* a, int64_t lda, const void* bb, int64_t ldb, void* P, int64_t ldp,
                                   const float* g, int64_t B, int64_t T, int64_t K, int prec, void* stream) {
   if (int rc = check_prec(prec)) return rc;
