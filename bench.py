@@ -334,8 +334,9 @@ def main():
 
     load_package()
     import unifiedlm_c_b200._lib as L_
-    from unifiedlm_c_b200.kernel import memory_fwd, memory_bwd, PRECISION
-    from unifiedlm_c_b200.prologue import address_fwd, address_bwd
+    from unifiedlm_c_b200.kernel import memory_fwd, PRECISION
+    from unifiedlm_c_b200.prologue import address_fwd
+    from unifiedlm_c_b200.block import addressed_memory_fwd, addressed_memory_bwd
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -364,10 +365,10 @@ def main():
     def step(h_, v_, dq_, df_):
         grads = []
         for blk in blocks:
-            r, den, u_op, kw = address_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], prec)
-            q, fast, c, qop, kop, vop, P = memory_fwd(r, v_, blk["g"], blk["w"], prec)
-            dr, dv, dg, dw = memory_bwd(dq_, df_, r, blk["g"], blk["w"], q, c, qop, kop, vop, P, prec)
-            dh, dconv, dkw, dkb, deps = address_bwd(dr, r, den, u_op, kw, h_, blk["conv"], prec)
+            q, fast, z, den, u_op, kw, c, qop, kop, vop, P = addressed_memory_fwd(
+                h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_, blk["g"], blk["w"], prec)
+            dh, dconv, dkw, dkb, deps, dv, dg, dw = addressed_memory_bwd(
+                dq_, df_, h_, blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop, vop, P, prec)
             grads += [dkw, dkb, dconv, deps, dw, dg]
         # the path's parameter gradients in one bucket: one NCCL all-reduce per step (DP average)
         bucket.pack(grads)
@@ -478,10 +479,11 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = runc_decode_baseline()
 
-    # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, normalise); operator fwd 4
-    # (stats, convert, scores, read); operator bwd 8 (convert, memset-free scores, 3 reads, stats scan,
-    # dw, dg); prologue bwd 8 (addr_bwd, db, deps, dK GEMM, dK sum, du GEMM, conv bwd, dconv sum)
-    launches = args.steps * W["L"] * (3 + 4 + 7 + 8)
+    # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, den); operator fwd 4
+    # (stats scan, convert v, scores, read); operator bwd 8 (convert dfast, scores grad, dq, dk, dv,
+    # stats scan, dw, dg); prologue bwd 9 (addr_bwd, db column sums + their sum, deps, dK GEMM,
+    # dK sum, du GEMM, conv bwd, dconv sum)
+    launches = args.steps * W["L"] * (3 + 4 + 8 + 9)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",

@@ -143,20 +143,25 @@ int ulm_set_gemm_pairs(int enable);
 
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
+ * den: NULL when r holds the read addresses; otherwise r holds their unnormalised form z
+ * (ulm_address_fwd with normalize = 0) and den (B*T,) fp32 the row denominators, r = z / den,
+ * applied as the rows are loaded.
  * Outputs: q (B,T,M) fp32; fast (B,T,D) of type v_dtype.
  * Saved for the backward (caller-owned, element type = ULM_BF16 for ULM_PREC_BF16, ULM_F32 for
  * ULM_PREC_FP32): c (B,T,M) fp32, or NULL when ulm_memory_needs_c(T, M) is 0; qop, kop
  * (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D)); P (B,T,ulm_operand_ld(T)). */
-int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const float* g, const float* w, float* q,
-                   void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
+int ulm_memory_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g, const float* w,
+                   float* q, void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
                    int64_t M, int64_t D, int prec, void* stream);
 
-/* Backward of unified_memory. dq_out may be NULL; dfast (B,T,D) of type do_dtype. Workspace
- * buffers (caller-owned): doop (B,T,ulm_operand_ld(D)) and dS (B,T,ulm_operand_ld(T)) in the
- * operand type, dqf and dk (B,T,M) fp32, `partial` of ulm_memory_stats_bwd_scratch bytes.
- * Outputs: dr (B,T,M) fp32, dv (B,T,D) of type do_dtype, dg (1,) fp32, dw (M,) fp32. */
-int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* g,
-                   const float* w, const float* q, const float* c, const void* qop, const void* kop,
+/* Backward of unified_memory. dq_out may be NULL; dfast (B,T,D) of type do_dtype; r and den as
+ * given to ulm_memory_fwd. Workspace buffers (caller-owned): doop (B,T,ulm_operand_ld(D)) and dS
+ * (B,T,ulm_operand_ld(T)) in the operand type, dqf and dk (B,T,M) fp32, `partial` of
+ * ulm_memory_stats_bwd_scratch bytes.
+ * Outputs: dr (B,T,M) fp32 (the gradient of the normalised addresses in both forms), dv (B,T,D)
+ * of type do_dtype, dg (1,) fp32, dw (M,) fp32. */
+int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
+                   const float* g, const float* w, const float* q, const float* c, const void* qop, const void* kop,
                    const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
                    float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T, int64_t M, int64_t D,
                    int prec, void* stream);
@@ -166,19 +171,28 @@ int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const f
 /* r = z / (eps + sum_m z), z = relu(u key_w^T + key_b)^2, u = causal depthwise conv(h).
  * h: (B,T,D) of h_dtype; conv_w: (D,conv_size) fp32 oldest -> newest; key_w: (M, ld_kw) in the
  * operand type of prec (bf16 for ULM_PREC_BF16, fp32 for ULM_PREC_FP32); key_b: (M,) fp32;
- * eps: device scalar. Outputs: r (B,T,M) fp32, den (B*T) fp32 = eps + sum z (saved), u_op (B*T, ld_u)
- * in the operand type (saved). */
+ * eps: device scalar. Outputs: den (B*T) fp32 = eps + sum z (saved), u_op (B*T, ld_u) in the
+ * operand type (saved), and in r (B,T,M) fp32: the addresses when normalize = 1, or z when
+ * normalize = 0 (the row sums then come from the key product's epilogue and no pass rewrites r;
+ * ulm_memory_fwd / ulm_memory_bwd / ulm_address_bwd take the pair (z, den)). work: caller scratch
+ * of ulm_address_fwd_work_bytes(B,T,M) bytes, needed only when normalize = 0 (may be NULL
+ * otherwise). */
 int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w,
-                    int64_t ld_kw, const float* key_b, const float* eps, float* r, float* den, void* u_op,
-                    int64_t ld_u, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream);
+                    int64_t ld_kw, const float* key_b, const float* eps, float* r, float* den, int normalize,
+                    void* work, void* u_op, int64_t ld_u, int64_t B, int64_t T, int64_t D, int64_t M, int prec,
+                    void* stream);
 
-/* Backward of ulm_address_fwd from dr (B,T,M) fp32: dh (B,T,D) fp32, dconv_w (D,conv_size),
- * dkey_w (M,D), dkey_b (M,) and deps (1,) fp32 (all overwritten). work: caller scratch of
- * ulm_address_bwd_work_bytes(B,T,D,M,prec) bytes. Column sums run in a fixed order. */
-int ulm_address_bwd(const float* dr, const float* r, const float* den, const void* u_op, int64_t ld_u, const void* h,
-                    int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w, int64_t ld_kw, float* dh,
-                    float* dconv_w, float* dkey_w, float* dkey_b, float* deps, void* work, int64_t B, int64_t T,
-                    int64_t D, int64_t M, int prec, void* stream);
+int64_t ulm_address_fwd_work_bytes(int64_t B, int64_t T, int64_t M);
+
+/* Backward of ulm_address_fwd from dr (B,T,M) fp32, the gradient of the normalised addresses:
+ * dh (B,T,D) fp32, dconv_w (D,conv_size), dkey_w (M,D), dkey_b (M,) and deps (1,) fp32 (all
+ * overwritten). r and den as ulm_address_fwd left them; normalized = the normalize flag it ran
+ * with. work: caller scratch of ulm_address_bwd_work_bytes(B,T,D,M,prec) bytes. Column sums run in
+ * a fixed order. */
+int ulm_address_bwd(const float* dr, const float* r, const float* den, int normalized, const void* u_op,
+                    int64_t ld_u, const void* h, int h_dtype, const float* conv_w, int64_t conv_size,
+                    const void* key_w, int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w, float* dkey_b,
+                    float* deps, void* work, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream);
 
 int64_t ulm_address_bwd_work_bytes(int64_t B, int64_t T, int64_t D, int64_t M, int prec);
 

@@ -54,9 +54,13 @@ def test_validation_rejects_bad_arguments_without_device_work():
     rc = lib.ulm_memory_stats_fwd(dummy, dummy, dummy, dummy, dummy, dummy, dummy, L.ULM_BF16, 8, 1, 4, 16, None)
     assert rc == L.ULM_ERR_INVALID and b"ld_op" in lib.ulm_last_error()
     # null pointers
-    rc = lib.ulm_memory_fwd(None, None, L.ULM_F32, None, None, None, None, None, None, None, None, None,
+    rc = lib.ulm_memory_fwd(None, None, None, L.ULM_F32, None, None, None, None, None, None, None, None, None,
                             1, 4, 8, 8, L.ULM_PREC_BF16, None)
     assert rc == L.ULM_ERR_INVALID and b"null" in lib.ulm_last_error()
+    # the unnormalised address form without its work buffer
+    rc = lib.ulm_address_fwd(dummy, L.ULM_F32, dummy, 4, dummy, 64, dummy, dummy, dummy, dummy, 0, None, dummy, 64,
+                             1, 8, 64, 64, L.ULM_PREC_BF16, None)
+    assert rc == L.ULM_ERR_INVALID and b"work" in lib.ulm_last_error()
     # bad dtype
     rc = lib.ulm_causal_apply(dummy, 64, dummy, 64, dummy, 64, 5, 0, 1, 64, 64, L.ULM_PREC_BF16, None)
     assert rc == L.ULM_ERR_INVALID

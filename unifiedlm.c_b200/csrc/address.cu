@@ -124,12 +124,25 @@ __global__ void addr_normalize_kernel(float* __restrict__ zr, float* __restrict_
   if (lane == 0) den[row] = dn;
 }
 
+// den[row] = eps + sum of the row's partial sums, written by the key GEMM's epilogue (one per
+// column block, unused slots zero), summed in a fixed order
+__global__ void addr_den_kernel(const float* __restrict__ part, int part_ld, const float* __restrict__ eps,
+                                float* __restrict__ den, int64_t rows) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float* p = part + row * part_ld;
+  float s = 0.f;
+  for (int j = 0; j < part_ld; ++j) s += p[j];
+  den[row] = *eps + s;
+}
+
 // one warp per row: s = sum dr r, then da = 2 sqrt(r den) (dr - s) / den; -s/den summed per CTA
-// (d eps partial). Rows are read with 16-byte loads; the second pass over a row hits L1.
+// (d eps partial). With `unnormalised`, x holds z = r den instead of r: s = sum dr z / den and
+// da = 2 sqrt(z) (dr - s) / den. Rows are read with 16-byte loads; the second pass over a row hits L1.
 __global__ void __launch_bounds__(256)
     addr_bwd_kernel(const float* __restrict__ dr, const float* __restrict__ r, const float* __restrict__ den,
-                    void* __restrict__ da, int da_dtype, int64_t ld_da, float* __restrict__ deps_part, int64_t rows,
-                    int M, int rows_per_cta) {
+                    int unnormalised, void* __restrict__ da, int da_dtype, int64_t ld_da,
+                    float* __restrict__ deps_part, int64_t rows, int M, int rows_per_cta) {
   __shared__ float deps_w[8];
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float deps_acc = 0.f;
@@ -148,15 +161,18 @@ __global__ void __launch_bounds__(256)
     s = warp_sum(s);
     const float dn = den[row];
     const float inv = 1.0f / dn;
+    // z scale: sqrt(z) = sqrt(x * zs) with zs = den for normalised rows, 1 for z rows
+    const float zs = unnormalised ? 1.f : dn;
+    if (unnormalised) s *= inv;
     deps_acc -= s * inv;
     for (int m = lane * 4; m < M; m += 128) {
       const float4 a = *reinterpret_cast<const float4*>(drr + m);
       const float4 c = *reinterpret_cast<const float4*>(rrow + m);
       float4 o;
-      o.x = 2.f * sqrtf(c.x * dn) * ((a.x - s) * inv);
-      o.y = 2.f * sqrtf(c.y * dn) * ((a.y - s) * inv);
-      o.z = 2.f * sqrtf(c.z * dn) * ((a.z - s) * inv);
-      o.w = 2.f * sqrtf(c.w * dn) * ((a.w - s) * inv);
+      o.x = 2.f * sqrtf(c.x * zs) * ((a.x - s) * inv);
+      o.y = 2.f * sqrtf(c.y * zs) * ((a.y - s) * inv);
+      o.z = 2.f * sqrtf(c.z * zs) * ((a.z - s) * inv);
+      o.w = 2.f * sqrtf(c.w * zs) * ((a.w - s) * inv);
       st4(da, row * ld_da + m, o, da_dtype);
     }
   }
@@ -271,6 +287,8 @@ GemmEpilogue plain_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int
   e.ld_aux = 0;
   e.aux_bstride = 0;
   e.tile_partial = nullptr;
+  e.row_partial = nullptr;
+  e.part_ld = 0;
   const int vec = out_dtype == ULM_F32 ? 4 : 8;
   e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
   return e;
@@ -343,11 +361,20 @@ int addr_check(int h_dtype, int prec, int64_t B, int64_t T, int64_t D, int64_t M
 
 }  // namespace
 
+// column blocks of the key GEMM's row partial sums: the narrowest tile of any GEMM back end is 64
+int64_t addr_part_ld(int64_t M) { return cdiv(M, 64); }
+
+extern "C" int64_t ulm_address_fwd_work_bytes(int64_t B, int64_t T, int64_t M) {
+  return B * T * addr_part_ld(M) * (int64_t)sizeof(float);
+}
+
 extern "C" int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w,
-                               int64_t ld_kw, const float* key_b, const float* eps, float* r, float* den, void* u_op,
-                               int64_t ld_u, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream) {
+                               int64_t ld_kw, const float* key_b, const float* eps, float* r, float* den,
+                               int normalize, void* work, void* u_op, int64_t ld_u, int64_t B, int64_t T, int64_t D,
+                               int64_t M, int prec, void* stream) {
   if (int rc = addr_check(h_dtype, prec, B, T, D, M, conv_size)) return rc;
   ULM_REQUIRE(h && conv_w && key_w && key_b && eps && r && den && u_op, "null pointer argument");
+  ULM_REQUIRE(normalize || work, "the unnormalised form needs ulm_address_fwd_work_bytes of work");
   ULM_REQUIRE(ld_u >= D && ld_kw >= D, "row stride shorter than the row");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16;
@@ -370,9 +397,21 @@ extern "C" int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, 
   GemmShape s{1, (int)rows, (int)M, (int)D, CAUSAL_NONE};
   GemmEpilogue e = plain_epilogue(EPI_RELU2, ULM_F32, r, M, rows * M);
   e.aux = key_b;
+  if (normalize) {
+    if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
+    addr_normalize_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, st>>>(r, den, eps, rows, (int)M);
+    ULM_LAUNCH_CHECK("addr_normalize_kernel");
+    return ULM_OK;
+  }
+  // z stays unnormalised: the epilogue leaves one row sum per column block, den sums them
+  float* part = static_cast<float*>(work);
+  const int64_t pld = addr_part_ld(M);
+  ULM_CUDA_TRY(cudaMemsetAsync(part, 0, rows * pld * sizeof(float), st));
+  e.row_partial = part;
+  e.part_ld = (int)pld;
   if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
-  addr_normalize_kernel<<<(unsigned)cdiv(rows, 8), 256, 0, st>>>(r, den, eps, rows, (int)M);
-  ULM_LAUNCH_CHECK("addr_normalize_kernel");
+  addr_den_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(part, (int)pld, eps, den, rows);
+  ULM_LAUNCH_CHECK("addr_den_kernel");
   return ULM_OK;
 }
 
@@ -380,7 +419,8 @@ extern "C" int64_t ulm_address_bwd_work_bytes(int64_t B, int64_t T, int64_t D, i
   return carve_addr_work(nullptr, B, T, D, M, prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16).bytes;
 }
 
-extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den, const void* u_op, int64_t ld_u,
+extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den, int normalized, const void* u_op,
+                               int64_t ld_u,
                                const void* h, int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w,
                                int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w, float* dkey_b, float* deps,
                                void* work, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream) {
@@ -392,8 +432,8 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   const int64_t rows = B * T;
   AddrBwdWork wk = carve_addr_work(work, B, T, D, M, dt);
   // da and the d eps partials
-  addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M,
-                                                     ADDR_ROWS_PER_CTA);
+  addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, normalized ? 0 : 1, wk.da, dt, wk.ld_m,
+                                                     wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
   ULM_LAUNCH_CHECK("addr_bwd_kernel");
   // db = column sums of da
   {

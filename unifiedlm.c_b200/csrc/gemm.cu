@@ -79,7 +79,8 @@ __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const Ge
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const float a = v[i] + (i < ncols ? bias[i] : 0.f);
-      v[i] = a > 0.f ? a * a : 0.f;
+      v[i] = a > 0.f && i < ncols ? a * a : 0.f;
+      dg_acc += v[i];  // row sum of this tile row (used when e.row_partial is set)
     }
   }
   if (e.kind == EPI_STORE_ADD) {
@@ -350,6 +351,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
+        epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
       if (epi.kind == EPI_DECAY_DG) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
@@ -572,6 +575,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty + (uint32_t)(acc * sizeof(uint64_t)));
+      if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
+        epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
       if (epi.kind == EPI_DECAY_DG) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
@@ -644,6 +649,7 @@ __global__ void __launch_bounds__(256)
   const bool decay = epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG;
   const float g = decay ? *epi.g : 0.f;
   float dg_acc = 0.f;
+  float rowsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int row = tc.mb * BM + ty + 16 * i;
@@ -664,12 +670,24 @@ __global__ void __launch_bounds__(256)
       if (epi.kind == EPI_RELU2) {
         const float a = v + reinterpret_cast<const float*>(epi.aux)[col];
         v = a > 0.f ? a * a : 0.f;
+        rowsum[i] += v;
       }
       const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
       if (epi.out_dtype == ULM_F32)
         reinterpret_cast<float*>(epi.out)[off] = v;
       else
         reinterpret_cast<__nv_bfloat16*>(epi.out)[off] = __float2bfloat16_rn(v);
+    }
+  }
+  if (epi.kind == EPI_RELU2 && epi.row_partial) {
+    // the 16 threads sharing a row (same ty, tx = 0..15) are 16 consecutive lanes of one warp
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float rs = rowsum[i];
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+      const int row = tc.mb * BM + ty + 16 * i;
+      if (tx == 0 && row < shape.M) epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = rs;
     }
   }
   if (epi.kind == EPI_DECAY_DG) {

@@ -44,6 +44,10 @@ struct GemmEpilogue {
   const void* aux;
   int64_t ld_aux, aux_bstride;
   float* tile_partial;
+  // EPI_RELU2 only, optional: row_partial[row * part_ld + column block] = sum of the tile row's
+  // outputs (blocks of 256, 128 or 64 columns depending on the back end; unused slots untouched)
+  float* row_partial;
+  int part_ld;
 };
 
 // A matrix operand in global memory: element (b, row, col) of its storage order at

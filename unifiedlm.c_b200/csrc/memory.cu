@@ -67,6 +67,8 @@ GemmEpilogue make_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int6
   e.ld_aux = 0;
   e.aux_bstride = 0;
   e.tile_partial = nullptr;
+  e.row_partial = nullptr;
+  e.part_ld = 0;
   const int vec = out_dtype == ULM_F32 ? 4 : 8;
   e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
   return e;
@@ -211,7 +213,8 @@ extern "C" int ulm_causal_apply(const void* P, int64_t ldp, const void* c, int64
   return run_gemm(A, Bo, s, e, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const float* g, const float* w, float* q,
+extern "C" int ulm_memory_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g,
+                              const float* w, float* q,
                               void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
                               int64_t M, int64_t D, int prec, void* stream) {
   if (int rc = check_prec(prec)) return rc;
@@ -222,7 +225,7 @@ extern "C" int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = op_dtype_of(prec);
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
-  if (int rc = ulm_memory_stats_fwd(r, w, g, q, c, qop, kop, dt, ldm, B, T, M, stream)) return rc;
+  if (int rc = stats_fwd_run(r, den, w, g, q, c, qop, kop, dt, ldm, B, T, M, stream)) return rc;
   if (M == 0) {
     // no slots: the fast read is empty
     ULM_CUDA_TRY(cudaMemsetAsync(fast, 0, B * T * D * elem_size(v_dtype), st));
@@ -234,8 +237,8 @@ extern "C" int ulm_memory_fwd(const float* r, const void* v, int v_dtype, const 
   return ulm_causal_apply(P, ldt, vop, ldd, fast, D, v_dtype, 0, B, T, D, prec, stream);
 }
 
-extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* g,
-                              const float* w, const float* q, const float* c, const void* qop, const void* kop,
+extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
+                              const float* g, const float* w, const float* q, const float* c, const void* qop, const void* kop,
                               const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk,
                               void* partial, float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T,
                               int64_t M, int64_t D, int prec, void* stream) {
@@ -248,6 +251,7 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
   if (B == 0 || T == 0 || M == 0) {
     if (B * T * D > 0) ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(do_dtype), st));
+    // nothing reads r or den here
     return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
   }
   ULM_REQUIRE(r && g && w && qop && kop && vop && P && doop && dS && dqf && dk && partial, "null pointer argument");
@@ -292,8 +296,9 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
     if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
     ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
     // without a saved c the statistics backward rebuilds q and c from r (TMA scan path)
-    return stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, 0, sc.tiles,
-                         n_tiles, st);
+    return stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
+                         sc.tiles, n_tiles, st);
   }
-  return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+  return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0,
+                       st);
 }

@@ -29,12 +29,28 @@ __device__ __forceinline__ void store_op<__nv_bfloat16>(void* base, int64_t idx,
   static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
 }
 
+// Row scale of an unnormalised address: r = z * (1 / den[row]) when den is given (the addressing
+// prologue can hand over z and its row denominators instead of r), 1 otherwise.
+__device__ __forceinline__ float row_scale(const float* __restrict__ den, int64_t row) {
+  return den ? __frcp_rn(den[row]) : 1.f;
+}
+
+// sinv[j] = 1 / den of row t = t_first + j for j <= n (1 everywhere without den; 0 outside [0, T),
+// where the tiles hold zeros), filled by the whole CTA
+__device__ __forceinline__ void fill_row_scales(float* sinv, const float* __restrict__ den, int b, int T,
+                                                int t_first, int n) {
+  for (int j = threadIdx.x; j <= n; j += blockDim.x) {
+    const int t = t_first + j;
+    sinv[j] = den ? ((t >= 0 && t < T) ? __frcp_rn(den[(int64_t)b * T + t]) : 0.f) : 1.f;
+  }
+}
+
 // kernel.py:109-136: k_t = r_{t-1}, c_t = w + sum_{s<=t} lam^(t-s) k_s, q_t = r_t / c_t
 template <typename OpT>
 __global__ void __launch_bounds__(STATS_THREADS)
-    stats_fwd_kernel(const float* __restrict__ r, const float* __restrict__ w, const float* __restrict__ g,
-                     float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop, void* __restrict__ kop,
-                     int64_t ldop, int T, int M) {
+    stats_fwd_kernel(const float* __restrict__ r, const float* __restrict__ den, const float* __restrict__ w,
+                     const float* __restrict__ g, float* __restrict__ q, float* __restrict__ c,
+                     void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T, int M) {
   __shared__ float seg_end[STATS_SEGS][32];
   const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -49,10 +65,10 @@ __global__ void __launch_bounds__(STATS_THREADS)
 
   // pass 1: the segment's own decayed sum of k, from a zero carry
   float run = 0.f;
-  float kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
+  float kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] * row_scale(den, row0 + t0 - 1) : 0.f;
 #pragma unroll 4
   for (int t = t0; t < t1; ++t) {
-    const float rt = valid ? rb[(int64_t)t * M] : 0.f;
+    const float rt = valid ? rb[(int64_t)t * M] * row_scale(den, row0 + t) : 0.f;
     run = fmaf(lam, run, kprev);
     kprev = rt;
   }
@@ -67,11 +83,11 @@ __global__ void __launch_bounds__(STATS_THREADS)
   // pass 2: rescan with the carry and write q, c and the operand copies of q and k
   const float wm = valid ? w[m] : 1.f;
   run = carry;
-  kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] : 0.f;
+  kprev = (valid && t0 > 0 && t0 < t1) ? rb[(int64_t)(t0 - 1) * M] * row_scale(den, row0 + t0 - 1) : 0.f;
   if (valid) {
 #pragma unroll 4
     for (int t = t0; t < t1; ++t) {
-      const float rt = rb[(int64_t)t * M];
+      const float rt = rb[(int64_t)t * M] * row_scale(den, row0 + t);
       run = fmaf(lam, run, kprev);
       const float cc = wm + run;
       const float qq = rt / cc;
@@ -102,8 +118,9 @@ __global__ void __launch_bounds__(STATS_THREADS)
 __global__ void __launch_bounds__(STATS_THREADS)
     stats_bwd_kernel(const float* __restrict__ dqf, const float* __restrict__ dq_out, const float* __restrict__ dk,
                      const float* __restrict__ q, const float* __restrict__ c, const float* __restrict__ r,
-                     const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ dr,
-                     float* __restrict__ part_dw, double* __restrict__ part_dg, int T, int M, int fast_identity) {
+                     const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
+                     float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int T, int M,
+                     int fast_identity) {
   __shared__ float seg_start[STATS_SEGS][32];
   __shared__ double red_dg[STATS_THREADS];
   __shared__ float red_dw[STATS_SEGS][32];
@@ -156,7 +173,7 @@ __global__ void __launch_bounds__(STATS_THREADS)
       const float dc = -dq * qq / cc;
       run = fmaf(lam, run, dc);  // dkc_t
       const float dkv = dk[i];
-      const float kt = t > 0 ? r[i - M] : 0.f;
+      const float kt = t > 0 ? r[i - M] * row_scale(den, (int64_t)b * T + t - 1) : 0.f;
       const float dkt = dkv + run;
       dr[i] = dq / cc + dkt_next;
       dkt_next = dkt;
@@ -192,14 +209,16 @@ namespace cg = cooperative_groups;
 
 template <int SEG, int WARPS, typename OpT>
 __global__ void __launch_bounds__(32 * WARPS)
-    stats_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_r, const float* __restrict__ w,
-                         const float* __restrict__ g, float* __restrict__ q, float* __restrict__ c,
-                         void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T, int M) {
+    stats_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_r, const float* __restrict__ den,
+                         const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ q,
+                         float* __restrict__ c, void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T,
+                         int M) {
   constexpr int R = SEG * WARPS;
   extern __shared__ __align__(128) float tile[];  // [0]: r rows t0.., [1]: k rows (r rows t0-1..)
   __shared__ __align__(8) uint64_t bar;
   __shared__ float warp_sum[WARPS][32];
   __shared__ float cta_total[32];
+  __shared__ float sinv[R + 1];  // row scales of rows cta_t0 - 1 .. cta_t0 + R - 1
   __shared__ int ok_flag;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
@@ -219,6 +238,7 @@ __global__ void __launch_bounds__(32 * WARPS)
     tma_load_3d(&map_r, tile, &bar, m0, cta_t0, b);
     tma_load_3d(&map_r, tile + R * 32, &bar, m0, cta_t0 - 1, b);
   }
+  fill_row_scales(sinv, den, b, T, cta_t0 - 1, R);  // overlaps the tile load
   if (threadIdx.x == 0) ok_flag = 1;
   __syncthreads();
   if (!mbar_wait_bounded(&bar, 0)) {
@@ -231,10 +251,11 @@ __global__ void __launch_bounds__(32 * WARPS)
   const float lam = expf(gg);
   const float* rt = tile + (wp * SEG) * 32 + lane;
   const float* kt = tile + R * 32 + (wp * SEG) * 32 + lane;
+  const float* si = sinv + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
   float run = 0.f;
   if (ok) {
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, kt[i * 32]);
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, kt[i * 32] * si[i]);
   }
   warp_sum[wp][lane] = run;
   __syncthreads();
@@ -258,10 +279,11 @@ __global__ void __launch_bounds__(32 * WARPS)
     for (int i = 0; i < SEG; ++i) {
       const int t = t0 + i;
       if (t < T) {
-        const float kk = kt[i * 32];
+        const float kk = kt[i * 32] * si[i];
         run = fmaf(lam, run, kk);
         const float cc = wm + run;
-        const float qq = rt[i * 32] * __frcp_rn(cc);
+        const float rv = rt[i * 32] * si[i + 1];
+        const float qq = rv * __frcp_rn(cc);
         const int64_t idx = (row0 + t) * M + m;
         q[idx] = qq;
         if (c) c[idx] = cc;
@@ -282,9 +304,9 @@ __global__ void __launch_bounds__(32 * WARPS)
     stats_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_dqf, const __grid_constant__ CUtensorMap map_dqo,
                          const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
                          const __grid_constant__ CUtensorMap map_dk, const __grid_constant__ CUtensorMap map_r,
-                         const float* __restrict__ dk, const float* __restrict__ w, const float* __restrict__ g,
-                         float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int T,
-                         int M, int has_dqo, int fast_identity) {
+                         const float* __restrict__ dk, const float* __restrict__ den, const float* __restrict__ w,
+                         const float* __restrict__ g, float* __restrict__ dr, float* __restrict__ part_dw,
+                         double* __restrict__ part_dg, int T, int M, int has_dqo, int fast_identity) {
   constexpr int R = SEG * WARPS;
   constexpr int TILE = R * 32;
   // tiles: dqf (then dq/c), dq_out (then dc), dk, then either q, c, k (saved) or the r tile
@@ -296,6 +318,7 @@ __global__ void __launch_bounds__(32 * WARPS)
   __shared__ float cta_total_f[32];
   __shared__ float cta_total[32];
   __shared__ double red_dg[32 * WARPS];
+  __shared__ float sinv[R + 1];  // row scales of the r tile's rows cta_t0 - 1 .. cta_t0 + R - 1
   __shared__ int ok_flag;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
@@ -330,6 +353,7 @@ __global__ void __launch_bounds__(32 * WARPS)
     }
     ok_flag = 1;
   }
+  fill_row_scales(sinv, den, b, T, cta_t0 - 1, R);  // overlaps the tile loads
   __syncthreads();
   if (!mbar_wait_bounded(&bar, 0)) {
     raise_device_error(DEVERR_SCAN_TMA_WAIT);
@@ -352,6 +376,7 @@ __global__ void __launch_bounds__(32 * WARPS)
   const float* s_r = t_x + o + 32;                                // recompute: r_t
   const float* s_q = t_x + o;                                     // saved q
   const float* s_c = t_x + TILE + o;                              // saved c
+  const float* si = sinv + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
 
   float n_carry = 0.f;
   if (RECOMPUTE) {
@@ -359,7 +384,7 @@ __global__ void __launch_bounds__(32 * WARPS)
     float run = 0.f;
     if (ok) {
 #pragma unroll
-      for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_k[i * 32]);
+      for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_k[i * 32] * si[i]);
     }
     warp_sum[wp][lane] = run;
     __syncthreads();
@@ -383,10 +408,10 @@ __global__ void __launch_bounds__(32 * WARPS)
       float cc, qq;
       float inv;
       if (RECOMPUTE) {
-        n = fmaf(lam, n, s_k[i * 32]);
+        n = fmaf(lam, n, s_k[i * 32] * si[i]);
         cc = wm + n;
         inv = __frcp_rn(cc);
-        qq = s_r[i * 32] * inv;
+        qq = (s_r[i * 32] * si[i + 1]) * inv;
       } else {
         cc = s_c[i * 32];
         qq = s_q[i * 32];
@@ -437,7 +462,7 @@ __global__ void __launch_bounds__(32 * WARPS)
       const int t = t0 + i;
       if (t < T) {
         const float dkv = s_dk[i * 32];
-        const float kv = s_k[i * 32];
+        const float kv = s_k[i * 32] * si[i];
         run = fmaf(lam, run, s_dqo[i * 32]);  // dkc_t
         dr[base + (int64_t)t * M] = s_dqf[i * 32] + dkt_next;
         dkt_next = dkv + run;
@@ -575,9 +600,9 @@ inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
 // the operator backward (fast_identity = 0, tile partials of the score epilogue added instead).
 // q == c == nullptr selects the recompute mode (TMA path only).
 int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
-                  const float* r, const float* w, const float* g, float* dr, float* dw, float* dg, void* partial,
-                  int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials, int64_t n_tiles,
-                  cudaStream_t st) {
+                  const float* r, const float* den, const float* w, const float* g, float* dr, float* dw, float* dg,
+                  void* partial, int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials,
+                  int64_t n_tiles, cudaStream_t st) {
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   int64_t n_dg, dw_rows;
   const bool recompute = q == nullptr && c == nullptr;
@@ -602,7 +627,7 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     int rc;
 #define ULM_BWD_TMA(W, RC)                                                                                       \
   rc = launch_cluster_smem(stats_bwd_tma_kernel<16, W, RC>, grid, 32 * W, C, smem, st, mdqf, mdqo, mq, mc, mdk, mr, \
-                           dk, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, hq, fast_identity)
+                           dk, den, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, hq, fast_identity)
     if (tp.warps == 8) {
       if (recompute) ULM_BWD_TMA(8, true); else ULM_BWD_TMA(8, false);
     } else {
@@ -615,8 +640,8 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
   } else {
     const int64_t groups = cdiv(M, 32);
     dim3 grid((unsigned)groups, (unsigned)B);
-    stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, w, g, dr, sc.part_dw, sc.part_dg,
-                                                     (int)T, (int)M, fast_identity);
+    stats_bwd_kernel<<<grid, STATS_THREADS, 0, st>>>(dqf, dq_out, dk, q, c, r, den, w, g, dr, sc.part_dw,
+                                                     sc.part_dg, (int)T, (int)M, fast_identity);
     ULM_LAUNCH_CHECK("stats_bwd_kernel");
     n_dg = B * groups;
     dw_rows = B;
@@ -632,9 +657,17 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
 
 using namespace ulm;
 
+int stats_fwd_run(const float* r, const float* den, const float* w, const float* g, float* q, float* c, void* qop,
+                  void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M, void* stream);
+
 extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float* g, float* q, float* c, void* qop,
                                     void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M,
                                     void* stream) {
+  return stats_fwd_run(r, nullptr, w, g, q, c, qop, kop, op_dtype, ld_op, B, T, M, stream);
+}
+
+int stats_fwd_run(const float* r, const float* den, const float* w, const float* g, float* q, float* c, void* qop,
+                  void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M, void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
   if (B == 0 || T == 0 || M == 0) return ULM_OK;
   ULM_REQUIRE(r && w && g && q && qop && kop, "null pointer argument");
@@ -654,20 +687,21 @@ extern "C" int ulm_memory_stats_fwd(const float* r, const float* w, const float*
     const size_t smem = (size_t)2 * R * 32 * 4;
     const bool bf = op_dtype == ULM_BF16;
     if (tp.warps == 8)
-      return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, w, g, q,
-                                      c, qop, kop, ld_op, (int)T, (int)M)
-                : launch_cluster_smem(stats_fwd_tma_kernel<16, 8, float>, grid, 256, C, smem, st, mr, w, g, q, c, qop,
-                                      kop, ld_op, (int)T, (int)M);
-    return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 16, __nv_bfloat16>, grid, 512, C, smem, st, mr, w, g, q,
-                                    c, qop, kop, ld_op, (int)T, (int)M)
-              : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, w, g, q, c, qop,
-                                    kop, ld_op, (int)T, (int)M);
+      return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, den, w,
+                                      g, q, c, qop, kop, ld_op, (int)T, (int)M)
+                : launch_cluster_smem(stats_fwd_tma_kernel<16, 8, float>, grid, 256, C, smem, st, mr, den, w, g, q, c,
+                                      qop, kop, ld_op, (int)T, (int)M);
+    return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 16, __nv_bfloat16>, grid, 512, C, smem, st, mr, den, w,
+                                    g, q, c, qop, kop, ld_op, (int)T, (int)M)
+              : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, den, w, g, q, c,
+                                    qop, kop, ld_op, (int)T, (int)M);
   }
   dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
   if (op_dtype == ULM_BF16)
-    stats_fwd_kernel<__nv_bfloat16><<<grid, STATS_THREADS, 0, st>>>(r, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
+    stats_fwd_kernel<__nv_bfloat16><<<grid, STATS_THREADS, 0, st>>>(r, den, w, g, q, c, qop, kop, ld_op, (int)T,
+                                                                    (int)M);
   else
-    stats_fwd_kernel<float><<<grid, STATS_THREADS, 0, st>>>(r, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
+    stats_fwd_kernel<float><<<grid, STATS_THREADS, 0, st>>>(r, den, w, g, q, c, qop, kop, ld_op, (int)T, (int)M);
   ULM_LAUNCH_CHECK("stats_fwd_kernel");
   return ULM_OK;
 }
@@ -691,7 +725,7 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
   }
   ULM_REQUIRE(dqf && dk && r && w && g && dr && partial, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
-  return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
 }
 
 // ---- statistics backward without any allocation ------------------------------------------------
@@ -753,7 +787,7 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // every scratch entry the kernels read is written earlier in the same call: nothing to clear
-  return stats_bwd_run(dqf, dq_out, dk, q, c, r, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
 }
 
 extern "C" int ulm_memory_needs_c(int64_t T, int64_t M) {

@@ -42,12 +42,10 @@ def _op_dtype(precision):
     return torch.float32 if precision == L.ULM_PREC_FP32 else torch.bfloat16
 
 
-@torch.library.custom_op("ulm::memory_fwd", mutates_args=())
-def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tensor, precision: int
-               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
-                          torch.Tensor]:
-    """Returns (q, fast, c, qop, kop, vop, P); the last five are saved for the backward."""
-    _require_cuda(r, v, g, w)
+def memory_fwd_raw(r, den, v, g, w, precision):
+    """ulm_memory_fwd on fresh buffers: (q, fast, c, qop, kop, vop, P). den None: r holds the
+    addresses; else r holds z and den the row denominators (r = z / den)."""
+    _require_cuda(r, v, g, w, den)
     B, T, M = r.shape
     D = v.shape[-1]
     dev = r.device
@@ -61,15 +59,14 @@ def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tenso
     vop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
     P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     with torch.cuda.device(dev):
-        L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w), L.ptr(q),
-                                       L.ptr(fast), L.ptr(c) if c.numel() else None, L.ptr(qop), L.ptr(kop),
-                                       L.ptr(vop), L.ptr(P),
+        L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(den), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w),
+                                       L.ptr(q), L.ptr(fast), L.ptr(c) if c.numel() else None, L.ptr(qop),
+                                       L.ptr(kop), L.ptr(vop), L.ptr(P),
                                        B, T, M, D, precision, L.stream_of(r)))
     return q, fast, c, qop, kop, vop, P
 
 
-@memory_fwd.register_fake
-def _memory_fwd_fake(r, v, g, w, precision):
+def memory_fwd_fake(r, v, precision):
     B, T, M = r.shape
     D = v.shape[-1]
     opt = _op_dtype(precision)
@@ -79,13 +76,10 @@ def _memory_fwd_fake(r, v, g, w, precision):
             r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
 
 
-@torch.library.custom_op("ulm::memory_bwd", mutates_args=())
-def memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, r: torch.Tensor, g: torch.Tensor,
-               w: torch.Tensor, q: torch.Tensor, c: torch.Tensor, qop: torch.Tensor, kop: torch.Tensor,
-               vop: torch.Tensor, P: torch.Tensor, precision: int
-               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Returns (dr, dv, dg, dw) (kernel.py:216-233)."""
-    _require_cuda(dfast, r, g, w, q, c)
+def memory_bwd_raw(dq_out, dfast, r, den, g, w, q, c, qop, kop, vop, P, precision):
+    """ulm_memory_bwd on fresh buffers: (dr, dv, dg, dw); dr is the gradient of the normalised
+    addresses whether r holds them or z (with den)."""
+    _require_cuda(dfast, r, g, w, q, c, den)
     B, T, M = r.shape
     D = dfast.shape[-1]
     dev = r.device
@@ -100,12 +94,34 @@ def memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, r: torch.Ten
     dk = torch.empty_like(dqf)
     partial = torch.empty(int(L.lib().ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8)
     with torch.cuda.device(dev):
-        L.check(L.lib().ulm_memory_bwd(L.ptr(dq_out), L.ptr(dfast), L.dtype_code(dfast.dtype), L.ptr(r), L.ptr(g),
-                                       L.ptr(w), L.ptr(q), L.ptr(c) if c.numel() else None, L.ptr(qop),
+        L.check(L.lib().ulm_memory_bwd(L.ptr(dq_out), L.ptr(dfast), L.dtype_code(dfast.dtype), L.ptr(r), L.ptr(den),
+                                       L.ptr(g), L.ptr(w), L.ptr(q), L.ptr(c) if c.numel() else None, L.ptr(qop),
                                        L.ptr(kop), L.ptr(vop), L.ptr(P),
                                        L.ptr(doop), L.ptr(dS), L.ptr(dqf), L.ptr(dk), L.ptr(partial), L.ptr(dr),
                                        L.ptr(dv), L.ptr(dg), L.ptr(dw), B, T, M, D, precision, L.stream_of(r)))
     return dr, dv, dg, dw
+
+
+@torch.library.custom_op("ulm::memory_fwd", mutates_args=())
+def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tensor, precision: int
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                          torch.Tensor]:
+    """Returns (q, fast, c, qop, kop, vop, P); the last five are saved for the backward."""
+    return memory_fwd_raw(r, None, v, g, w, precision)
+
+
+@memory_fwd.register_fake
+def _memory_fwd_fake(r, v, g, w, precision):
+    return memory_fwd_fake(r, v, precision)
+
+
+@torch.library.custom_op("ulm::memory_bwd", mutates_args=())
+def memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, r: torch.Tensor, g: torch.Tensor,
+               w: torch.Tensor, q: torch.Tensor, c: torch.Tensor, qop: torch.Tensor, kop: torch.Tensor,
+               vop: torch.Tensor, P: torch.Tensor, precision: int
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dr, dv, dg, dw) (kernel.py:216-233)."""
+    return memory_bwd_raw(dq_out, dfast, r, None, g, w, q, c, qop, kop, vop, P, precision)
 
 
 @memory_bwd.register_fake

@@ -2,11 +2,11 @@
 
 ModelArgs, RMSNorm, UnifiedBlock and UnifiedLM keep the reference's constructor arguments,
 parameter names, shapes and initialisation (model.py:13-204), so state_dicts, checkpoints and the
-model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the addressing prologue to
-`prologue.address` and the fast read to `kernel.unified_memory` (libulm_b200.so); the val and mu
-projections and RMSNorm stay PyTorch (cuBLAS) as in the reference; `step` / `init_state` /
-`forward_recurrent` keep the
-reference's token-by-token semantics (model.py:88-111, 164-175) for small-batch use, and
+model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the addressing prologue and
+the fast read to `block.addressed_memory` (libulm_b200.so; the same result as
+`kernel.unified_memory(prologue.address(...))` without materialising the normalised addresses);
+the val and mu projections and RMSNorm stay PyTorch (cuBLAS) as in the reference; `step` /
+`init_state` / `forward_recurrent` keep the reference's token-by-token semantics (model.py:88-111, 164-175) for small-batch use, and
 `decode.py` holds the batched CUDA decoder.
 
 The block's precision follows `UnifiedBlock.precision` ("bf16" tensor-core products, default; or
@@ -21,8 +21,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .kernel import CHUNK, unified_memory
-from .prologue import address
+from .block import addressed_memory
+from .kernel import CHUNK
 
 
 @dataclass
@@ -86,12 +86,13 @@ class UnifiedBlock(nn.Module):
 
     def forward(self, x):
         h = self.norm(x)
-        # conv + code(u) in one fused call on the GPU (model.py:79-80)
         eps = self.log_eps.clamp(-10, 10).exp()
-        r = address(h, self.conv.weight, self.key.weight, self.key.bias, eps, precision=self.precision)
         v = self.val(h)
         w = self._w()
-        q, fast = unified_memory(r, v, -self.log_rate.exp(), w, precision=self.precision)
+        # conv + code(u) + the fast memory in one call on the GPU (model.py:79-83); the addresses
+        # stay unnormalised between the two (addressed_memory)
+        q, fast = addressed_memory(h, self.conv.weight, self.key.weight, self.key.bias, eps, v,
+                                   -self.log_rate.exp(), w, precision=self.precision)
         return x + self.dropout(self.mu((q * w).type_as(x)) + fast.type_as(x))
 
     # ---- token-by-token form (the reference for run.c) ----

@@ -25,10 +25,9 @@ def _weight_op(key_w, precision):
     return kw
 
 
-@torch.library.custom_op("ulm::address_fwd", mutates_args=())
-def address_fwd(h: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Tensor, key_b: torch.Tensor, eps: torch.Tensor,
-                precision: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Returns (r, den, u_op, kw_op); the last three are saved for the backward."""
+def address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=True):
+    """ulm_address_fwd on fresh buffers: (r, den, u_op, kw_op); with normalize=False the first
+    output holds z = r * den (the row sums come from the key product's epilogue)."""
     B, T, D = h.shape
     M = key_w.shape[0]
     K = conv_w.shape[-1]
@@ -39,15 +38,17 @@ def address_fwd(h: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Tensor, key_
     kw = _weight_op(key_w, precision)
     cw = conv_w.detach().reshape(D, K).float().contiguous()
     kb = key_b.detach().float().contiguous()
+    lib = L.lib()
+    work = None if normalize else torch.empty(int(lib.ulm_address_fwd_work_bytes(B, T, M)), device=dev,
+                                              dtype=torch.uint8)
     with torch.cuda.device(dev):
-        L.check(L.lib().ulm_address_fwd(L.ptr(h), L.dtype_code(h.dtype), L.ptr(cw), K, L.ptr(kw), kw.shape[1],
-                                        L.ptr(kb), L.ptr(eps), L.ptr(r), L.ptr(den), L.ptr(u_op), u_op.shape[1],
-                                        B, T, D, M, precision, L.stream_of(h)))
+        L.check(lib.ulm_address_fwd(L.ptr(h), L.dtype_code(h.dtype), L.ptr(cw), K, L.ptr(kw), kw.shape[1],
+                                    L.ptr(kb), L.ptr(eps), L.ptr(r), L.ptr(den), 1 if normalize else 0, L.ptr(work),
+                                    L.ptr(u_op), u_op.shape[1], B, T, D, M, precision, L.stream_of(h)))
     return r, den, u_op, kw
 
 
-@address_fwd.register_fake
-def _address_fwd_fake(h, conv_w, key_w, key_b, eps, precision):
+def address_fwd_fake(h, key_w, precision):
     B, T, D = h.shape
     M = key_w.shape[0]
     opt = _op_dtype(precision)
@@ -55,11 +56,9 @@ def _address_fwd_fake(h, conv_w, key_w, key_b, eps, precision):
             h.new_empty(B * T, operand_ld(D), dtype=opt), h.new_empty(M, operand_ld(D), dtype=opt))
 
 
-@torch.library.custom_op("ulm::address_bwd", mutates_args=())
-def address_bwd(dr: torch.Tensor, r: torch.Tensor, den: torch.Tensor, u_op: torch.Tensor, kw: torch.Tensor,
-                h: torch.Tensor, conv_w: torch.Tensor, precision: int
-                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Returns (dh fp32, dconv_w (D,1,K), dkey_w (M,D), dkey_b (M,), deps 0-d)."""
+def address_bwd_raw(dr, r, den, u_op, kw, h, conv_w, precision, normalized=True):
+    """ulm_address_bwd on fresh buffers: (dh fp32, dconv_w (D,1,K), dkey_w (M,D), dkey_b (M,),
+    deps 0-d); r and den as address_fwd_raw returned them with the same normalize flag."""
     B, T, D = h.shape
     M = r.shape[-1]
     K = conv_w.shape[-1]
@@ -73,21 +72,45 @@ def address_bwd(dr: torch.Tensor, r: torch.Tensor, den: torch.Tensor, u_op: torc
     cw = conv_w.detach().reshape(D, K).float().contiguous()
     drc = dr.float().contiguous()
     with torch.cuda.device(dev):
-        L.check(L.lib().ulm_address_bwd(L.ptr(drc), L.ptr(r), L.ptr(den), L.ptr(u_op), u_op.shape[1], L.ptr(h),
-                                        L.dtype_code(h.dtype), L.ptr(cw), K, L.ptr(kw), kw.shape[1], L.ptr(dh),
-                                        L.ptr(dconv), L.ptr(dkw), L.ptr(dkb), L.ptr(deps), L.ptr(work),
-                                        B, T, D, M, precision, L.stream_of(h)))
+        L.check(L.lib().ulm_address_bwd(L.ptr(drc), L.ptr(r), L.ptr(den), 1 if normalized else 0, L.ptr(u_op),
+                                        u_op.shape[1], L.ptr(h), L.dtype_code(h.dtype), L.ptr(cw), K, L.ptr(kw),
+                                        kw.shape[1], L.ptr(dh), L.ptr(dconv), L.ptr(dkw), L.ptr(dkb), L.ptr(deps),
+                                        L.ptr(work), B, T, D, M, precision, L.stream_of(h)))
     return dh, dconv.reshape(D, 1, K), dkw, dkb, deps
 
 
-@address_bwd.register_fake
-def _address_bwd_fake(dr, r, den, u_op, kw, h, conv_w, precision):
+def address_bwd_fake(h, r, conv_w):
     B, T, D = h.shape
     M = r.shape[-1]
     K = conv_w.shape[-1]
     return (h.new_empty(B, T, D, dtype=torch.float32), h.new_empty(D, 1, K, dtype=torch.float32),
             h.new_empty(M, D, dtype=torch.float32), h.new_empty(M, dtype=torch.float32),
             h.new_empty((), dtype=torch.float32))
+
+
+@torch.library.custom_op("ulm::address_fwd", mutates_args=())
+def address_fwd(h: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Tensor, key_b: torch.Tensor, eps: torch.Tensor,
+                precision: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (r, den, u_op, kw_op); the last three are saved for the backward."""
+    return address_fwd_raw(h, conv_w, key_w, key_b, eps, precision)
+
+
+@address_fwd.register_fake
+def _address_fwd_fake(h, conv_w, key_w, key_b, eps, precision):
+    return address_fwd_fake(h, key_w, precision)
+
+
+@torch.library.custom_op("ulm::address_bwd", mutates_args=())
+def address_bwd(dr: torch.Tensor, r: torch.Tensor, den: torch.Tensor, u_op: torch.Tensor, kw: torch.Tensor,
+                h: torch.Tensor, conv_w: torch.Tensor, precision: int
+                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dh fp32, dconv_w (D,1,K), dkey_w (M,D), dkey_b (M,), deps 0-d)."""
+    return address_bwd_raw(dr, r, den, u_op, kw, h, conv_w, precision)
+
+
+@address_bwd.register_fake
+def _address_bwd_fake(dr, r, den, u_op, kw, h, conv_w, precision):
+    return address_bwd_fake(h, r, conv_w)
 
 
 def _setup(ctx, inputs, output):
