@@ -32,6 +32,7 @@ SIGNATURES = {
     "ulm_causal_apply": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _P]),
     "ulm_operand_ld": (_I64, [_I64]),
     "ulm_set_gemm_pairs": (_I, [_I]),
+    "ulm_set_epilogue_mode": (_I, [_I]),
     "ulm_memory_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_bwd": (_I, [_P, _P, _I] + [_P] * 19 + [_I64, _I64, _I64, _I64, _I, _P]),
     "ulm_address_fwd": (_I, [_P, _I, _P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _I64, _I64,

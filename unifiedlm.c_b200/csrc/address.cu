@@ -289,6 +289,7 @@ GemmEpilogue plain_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int
   e.tile_partial = nullptr;
   e.row_partial = nullptr;
   e.part_ld = 0;
+  e.staged = 0;
   const int vec = out_dtype == ULM_F32 ? 4 : 8;
   e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
   return e;

@@ -286,6 +286,7 @@ int decode_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int wdt,
   e.tile_partial = nullptr;
   e.row_partial = nullptr;
   e.part_ld = 0;
+  e.staged = 0;
   e.vec_ok = is_aligned16(out) && ldo % 4 == 0;
   return run_gemm(A, Bw, s, e, st);
 }

@@ -23,14 +23,28 @@ namespace ulm {
 // ------------------------------------------------------------------------------------------------
 // epilogue: one thread owns one output row segment of 32 columns
 
-// 32 consecutive elements of an aux row (the forward's scores) as floats; zero past `ncols`.
+__host__ __device__ __forceinline__ bool has_tile_aux(int kind) { return kind == EPI_DECAY_DG || kind == EPI_STORE_ADD; }
+
+// 32 consecutive elements of an aux row (EPI_DECAY_DG: the forward's scores; EPI_STORE_ADD: the
+// fp32 addend; both in the output's type) as floats; zero past `ncols`.
 __device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row, int col0, int ncols,
                                            float (&p)[32]) {
   const int64_t off = (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
   if (e.out_dtype == ULM_F32) {
     const float* a = reinterpret_cast<const float*>(e.aux) + off;
+    if (ncols == 32 && e.vec_ok) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) p[i] = i < ncols ? a[i] : 0.f;
+      for (int i = 0; i < 32; i += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(a + i);
+        p[i] = a4.x;
+        p[i + 1] = a4.y;
+        p[i + 2] = a4.z;
+        p[i + 3] = a4.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[i] = i < ncols ? a[i] : 0.f;
+    }
   } else {
     const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(e.aux) + off;
     if (ncols == 32 && e.vec_ok) {
@@ -54,52 +68,68 @@ __device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row
   }
 }
 
-__device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const GemmShape& s, float gl2, int b,
-                                                 int row, int col0, float (&v)[32], float& dg_acc) {
-  if (row >= s.M || col0 >= s.N) return;
-  const int ncols = min(32, s.N - col0);
+// The epilogue's arithmetic on NC accumulator values v of row `row`, columns col0..col0+NC-1
+// (ncols of them inside the output); p holds the tile aux values of the same positions.
+template <int NC>
+__device__ __forceinline__ void epilogue_math(const GemmEpilogue& e, float gl2, int row, int col0, int ncols,
+                                              float* v, const float* p, float& dg_acc) {
   if (e.kind == EPI_DECAY_DG) {
-    float p[32];
-    load_aux32(e, b, row, col0, ncols, p);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < NC; ++i) {
       const int lag = row - (col0 + i);
       if (lag > 0) dg_acc = fmaf((float)lag * p[i], v[i], dg_acc);
     }
   }
   if (e.kind == EPI_DECAY || e.kind == EPI_DECAY_DG) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < NC; ++i) {
       const int lag = row - (col0 + i);
       v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
     }
   }
   if (e.kind == EPI_RELU2) {
     const float* bias = reinterpret_cast<const float*>(e.aux) + col0;
+    float bv[NC];
+    if (ncols == NC && (reinterpret_cast<uintptr_t>(bias) & 15) == 0) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float a = v[i] + (i < ncols ? bias[i] : 0.f);
+      for (int i = 0; i < NC; i += 4) {
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias + i));
+        bv[i] = b4.x;
+        bv[i + 1] = b4.y;
+        bv[i + 2] = b4.z;
+        bv[i + 3] = b4.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NC; ++i) bv[i] = i < ncols ? bias[i] : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const float a = v[i] + bv[i];
       v[i] = a > 0.f && i < ncols ? a * a : 0.f;
       dg_acc += v[i];  // row sum of this tile row (used when e.row_partial is set)
     }
   }
   if (e.kind == EPI_STORE_ADD) {
-    const float* a = reinterpret_cast<const float*>(e.aux) + (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
-    if (ncols == 32 && e.vec_ok) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 a4 = *reinterpret_cast<const float4*>(a + i);
-        v[i] += a4.x;
-        v[i + 1] += a4.y;
-        v[i + 2] += a4.z;
-        v[i + 3] += a4.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < ncols) v[i] += a[i];
-    }
+    for (int i = 0; i < NC; ++i) v[i] += p[i];
   }
+}
+
+// Direct epilogue: each thread stores its own row segment (used when the output or aux layout does
+// not allow the tensor-map path below).
+__device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const GemmShape& s, float gl2, int b,
+                                                 int row, int col0, float (&v)[32], float& dg_acc) {
+  if (row >= s.M || col0 >= s.N) return;
+  const int ncols = min(32, s.N - col0);
+  float p[32];
+  if (has_tile_aux(e.kind)) {
+    load_aux32(e, b, row, col0, ncols, p);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) p[i] = 0.f;
+  }
+  epilogue_math<32>(e, gl2, row, col0, ncols, v, p, dg_acc);
   const int64_t off = (int64_t)b * e.out_bstride + (int64_t)row * e.ldo + col0;
   if (e.out_dtype == ULM_F32) {
     float* o = reinterpret_cast<float*>(e.out) + off;
@@ -135,24 +165,6 @@ __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const Ge
   }
 }
 
-// ------------------------------------------------------------------------------------------------
-// tensor-core back end
-
-constexpr int TC_BM = 128;
-constexpr int TC_BK = 64;
-constexpr int TC_THREADS = 192;
-
-template <int BN>
-struct TcConfig {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
-  static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
-  static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
-  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
-  // stages + 1024 alignment slack + barriers / TMEM slot / flags
-  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-};
-
 // Wait on an mbarrier phase unless the CTA is aborting; false on timeout or abort.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -170,9 +182,304 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   }
 }
 
+// ---- staged epilogues -------------------------------------------------------------------------
+// The output leaves through shared memory and TMA tensor stores, so global writes are whole lines
+// instead of 32 row fragments per store instruction; a tile aux (scores / addend) arrives the same
+// way through a TMA load into the staging tile, and the epilogue computes in place. Two layouts:
+//   EPI_MODE_WARP : each epilogue warp stages 32 rows x 128 bytes (32 fp32 / 64 bf16 columns,
+//                   128-byte swizzle) in two 4 KB slots of its own
+//   EPI_MODE_CTA  : the four epilogue warps stage 128 rows x 128 bytes together (32 fp32 / 64 bf16
+//                   columns, 128-byte swizzle) in two 16 KB slots; named barriers order the warps
+//                   and one thread issues the 16 KB copies
+// Writes of one row per lane into the swizzled layout are conflict-free 16-byte stores.
+enum { EPI_MODE_DIRECT = 0, EPI_MODE_WARP = 1, EPI_MODE_CTA = 2 };
+constexpr uint32_t EPI_SMEM_BYTES = 32768;
+constexpr int EPI_BAR_ID = 1;  // named barrier of the 128 epilogue threads
+
+__device__ __forceinline__ uint32_t sw128_off(int r, int k) { return (uint32_t)(r * 128 + ((k ^ (r & 7)) << 4)); }
+
+// 32 values of row r of a tile with 128-byte rows (128-byte swizzle), starting at 16-byte unit u0
+// (fp32: 8 units, bf16: 4 units)
+template <bool F32>
+__device__ __forceinline__ void stage_write(uint8_t* tile, int r, int u0, const float* v) {
+#pragma unroll
+  for (int k = 0; k < (F32 ? 8 : 4); ++k) {
+    const uint32_t off = sw128_off(r, u0 + k);
+    if (F32) {
+      *reinterpret_cast<float4*>(tile + off) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+    } else {
+      uint4 pk;
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(v[8 * k], v[8 * k + 1]);
+      __nv_bfloat162 p1 = __floats2bfloat162_rn(v[8 * k + 2], v[8 * k + 3]);
+      __nv_bfloat162 p2 = __floats2bfloat162_rn(v[8 * k + 4], v[8 * k + 5]);
+      __nv_bfloat162 p3 = __floats2bfloat162_rn(v[8 * k + 6], v[8 * k + 7]);
+      memcpy(&pk.x, &p0, 4);
+      memcpy(&pk.y, &p1, 4);
+      memcpy(&pk.z, &p2, 4);
+      memcpy(&pk.w, &p3, 4);
+      *reinterpret_cast<uint4*>(tile + off) = pk;
+    }
+  }
+}
+
+template <bool F32>
+__device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, float* p) {
+#pragma unroll
+  for (int k = 0; k < (F32 ? 8 : 4); ++k) {
+    const uint32_t off = sw128_off(r, u0 + k);
+    if (F32) {
+      const float4 a = *reinterpret_cast<const float4*>(tile + off);
+      p[4 * k] = a.x;
+      p[4 * k + 1] = a.y;
+      p[4 * k + 2] = a.z;
+      p[4 * k + 3] = a.w;
+    } else {
+      const uint4 pk = *reinterpret_cast<const uint4*>(tile + off);
+      const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h;
+        memcpy(&h, &w4[j], 4);
+        const float2 f = __bfloat1622float2(h);
+        p[8 * k + 2 * j] = f.x;
+        p[8 * k + 2 * j + 1] = f.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync %0, 128;" ::"n"(EPI_BAR_ID) : "memory"); }
+
+// named barrier of the epilogue threads that also ANDs a predicate over them (uniform decisions)
+__device__ __forceinline__ bool epi_bar_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(EPI_BAR_ID)
+      : "memory");
+  return r != 0;
+}
+
+// EPI_MODE_WARP: one chunk (32 rows x 128 bytes: 32 fp32 / 64 bf16 columns at col0) of the warp's
+// rows row_base..+31; taddr = this warp's TMEM quadrant at the chunk's first column. n counts the
+// warp's staged chunks (slot n % 2, barrier phase n / 2). False if the aux wait gave up.
+template <bool F32>
+__device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
+                                               const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
+                                               float gl2, int b, int row_base, int col0, uint32_t taddr,
+                                               float& dg_acc, volatile int* abort_flag, int site) {
+  const int lane = threadIdx.x & 31;
+  const bool aux = has_tile_aux(e.kind);
+  const int sl = n & 1;
+  const uint32_t parity = (uint32_t)(n >> 1) & 1u;
+  ++n;
+  uint8_t* tile = slots + sl * 4096;
+  if (lane == 0) {
+    bulk_wait_group_read<1>();  // the store of this warp's chunk n - 2 has read the slot
+    if (aux) {
+      mbar_arrive_expect_tx(&abar[sl], 4096u);
+      tma_load_3d(tma_aux, tile, &abar[sl], col0, row_base, b);
+    }
+  }
+  __syncwarp();
+  if (aux && !wait_or_abort(&abar[sl], parity, abort_flag, site)) return false;
+#pragma unroll 1
+  for (int h = 0; h < (F32 ? 1 : 2); ++h) {
+    float v[32], p[32];
+    tmem_ld_32x32(taddr + (uint32_t)(32 * h), v);
+    if (aux) {
+      stage_read<F32>(tile, lane, 4 * h, p);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[i] = 0.f;
+    }
+    const int c = col0 + 32 * h;
+    epilogue_math<32>(e, gl2, row_base + lane, c, min(32, s.N - c), v, p, dg_acc);
+    stage_write<F32>(tile, lane, 4 * h, v);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tma_out, tile, col0, row_base, b);
+    bulk_commit_group();
+  }
+  return true;
+}
+
+// EPI_MODE_CTA: one 128-row chunk (32 fp32 / 64 bf16 columns at col0) of the CTA's tile rows
+// row0..row0+127, all four epilogue warps; taddr = this warp's TMEM quadrant at the chunk's first
+// column. n counts the CTA's staged chunks. False (uniformly) if an aux wait gave up.
+template <bool F32>
+__device__ __forceinline__ bool epi_chunk_cta(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
+                                              const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
+                                              float gl2, int b, int row0, int col0, uint32_t taddr, float& dg_acc,
+                                              volatile int* abort_flag, int site) {
+  const int lane = threadIdx.x & 31;
+  const int r = ((threadIdx.x >> 5) & 3) * 32 + lane;  // row in the CTA's 128 (TMEM lane quadrant)
+  const bool issuer = threadIdx.x == 64;               // warp 2, lane 0
+  const bool aux = has_tile_aux(e.kind);
+  const int sl = n & 1;
+  const uint32_t parity = (uint32_t)(n >> 1) & 1u;
+  ++n;
+  uint8_t* tile = slots + sl * 16384;
+  if (issuer) {
+    bulk_wait_group_read<1>();  // the store of chunk n - 2 has read the slot
+    if (aux) {
+      mbar_arrive_expect_tx(&abar[sl], 16384u);
+      tma_load_3d(tma_aux, tile, &abar[sl], col0, row0, b);
+    }
+  }
+  epi_bar_sync();  // slot free for every thread
+  bool ok = true;
+  if (aux) ok = wait_or_abort(&abar[sl], parity, abort_flag, site);
+  if (aux && !epi_bar_and(ok)) return false;
+#pragma unroll 1
+  for (int h = 0; h < (F32 ? 1 : 2); ++h) {
+    float v[32], p[32];
+    tmem_ld_32x32(taddr + (uint32_t)(32 * h), v);
+    if (aux) {
+      stage_read<F32>(tile, r, 4 * h, p);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[i] = 0.f;
+    }
+    const int c = col0 + 32 * h;
+    epilogue_math<32>(e, gl2, row0 + r, c, min(32, s.N - c), v, p, dg_acc);
+    stage_write<F32>(tile, r, 4 * h, v);
+  }
+  fence_proxy_async_smem();
+  epi_bar_sync();  // the chunk is complete in shared memory
+  if (issuer) {
+    tma_store_3d(tma_out, tile, col0, row0, b);
+    bulk_commit_group();
+  }
+  return true;
+}
+
+// The epilogue warps (2..5) of both tensor-core kernels: for every tile of this CTA (t_first,
+// t_first + t_stride, ...) wait for its accumulator, write it through the epilogue and hand the
+// TMEM buffer back. cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows);
+// partials for EPI_DECAY_DG go to tile_partial[part_stride * t + part_off + epilogue warp].
+template <int BM, int BN, bool PAIR>
+__device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const GemmEpilogue& epi,
+                                               const CUtensorMap* tma_out, const CUtensorMap* tma_aux,
+                                               int m_blocks, int n_blocks, int tiles_per_batch, int total_tiles,
+                                               int t_first, int t_stride, int cta_rows, uint32_t tmem_base,
+                                               uint64_t* tfull, uint64_t* tempty, uint32_t leader_tempty,
+                                               uint8_t* stage, uint64_t* aux_bar, volatile int* abort_flag,
+                                               int site, int part_stride, int part_off) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int quad = warp & 3;
+  const int mode = epi.staged;
+  const bool f32 = epi.out_dtype == ULM_F32;
+  const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
+  uint8_t* wslots = stage + (warp - 2) * 8192;  // EPI_MODE_WARP: this warp's two 4 KB slots
+  uint64_t* wbar = aux_bar + (warp - 2) * 2;
+  int n = 0;
+  int j = 0;
+  bool ok = true;
+  for (int t = t_first; t < total_tiles; t += t_stride, ++j) {
+    const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+    const int acc = j & 1;
+    const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+    ok = wait_or_abort(&tfull[acc], acc_phase, abort_flag, site);
+    if (mode == EPI_MODE_CTA) ok = epi_bar_and(ok);
+    if (!ok) break;
+    tc_fence_after();
+    const int row0 = tc.mb * BM + cta_rows;  // the CTA's first tile row
+    const int row = row0 + quad * 32 + lane;
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+    float dg_acc = 0.f;
+    if (mode == EPI_MODE_CTA) {
+      const int cw = f32 ? 32 : 64;
+#pragma unroll 1
+      for (int c = 0; c < BN && ok; c += cw) {
+        const int col0 = tc.nb * BN + c;
+        if (col0 >= shape.N) break;
+        ok = f32 ? epi_chunk_cta<true>(epi, shape, tma_out, tma_aux, stage, aux_bar, n, gl2, tc.b, row0, col0,
+                                       taddr + (uint32_t)c, dg_acc, abort_flag, site)
+                 : epi_chunk_cta<false>(epi, shape, tma_out, tma_aux, stage, aux_bar, n, gl2, tc.b, row0, col0,
+                                        taddr + (uint32_t)c, dg_acc, abort_flag, site);
+      }
+    } else if (mode == EPI_MODE_WARP) {
+      const int row_base = row0 + quad * 32;
+      const int cw = f32 ? 32 : 64;
+#pragma unroll 1
+      for (int c = 0; c < BN && ok; c += cw) {
+        const int col0 = tc.nb * BN + c;
+        if (row_base >= shape.M || col0 >= shape.N) break;
+        ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, gl2, tc.b, row_base, col0,
+                                        taddr + (uint32_t)c, dg_acc, abort_flag, site)
+                 : epi_chunk_warp<false>(epi, shape, tma_out, tma_aux, wslots, wbar, n, gl2, tc.b, row_base, col0,
+                                         taddr + (uint32_t)c, dg_acc, abort_flag, site);
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld_32x32(taddr + (uint32_t)c, v);
+        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
+      }
+    }
+    if (!ok) break;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (PAIR)
+        mbar_arrive_cluster(leader_tempty + (uint32_t)(acc * sizeof(uint64_t)));
+      else
+        mbar_arrive(&tempty[acc]);
+    }
+    if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
+      epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
+    if (epi.kind == EPI_DECAY_DG) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
+      if (lane == 0) epi.tile_partial[part_stride * (int64_t)t + part_off + (warp - 2)] = dg_acc;
+    }
+  }
+  if (mode != EPI_MODE_DIRECT) {
+    // an aux load still in flight after an abort lands before the CTA exits; stores complete
+    const bool issuer = mode == EPI_MODE_CTA ? threadIdx.x == 64 : lane == 0;
+    if (issuer) {
+      uint64_t* bars = mode == EPI_MODE_CTA ? aux_bar : wbar;
+      if (!ok && has_tile_aux(epi.kind) && n > 0) {
+        const int k = n - 1;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&bars[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+      bulk_wait_group<0>();
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// tensor-core back end
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;
+constexpr int TC_THREADS = 192;
+
+template <int BN>
+struct TcConfig {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
+  static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // stages + staging tiles of the epilogue + 1024 alignment slack + barriers / TMEM slot / flags
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+};
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_aux,
                    const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
                    const int tiles_per_batch, const int total_tiles) {
   using Cfg = TcConfig<BN>;
@@ -188,12 +495,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_bar = drain + 1;  // 4 warps x 2 slots
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -209,12 +518,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 4);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (epi.staged != EPI_MODE_DIRECT) {
+      tma_prefetch_desc(&tma_out);
+      if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -329,36 +643,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
-    const int quad = warp & 3;
-    const int row_in_tile = quad * 32 + lane;
-    const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
-    int j = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++j) {
-      const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
-      const int acc = j & 1;
-      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-      if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, DEVERR_GEMM_EPILOGUE_WAIT)) break;
-      tc_fence_after();
-      const int row = tc.mb * TC_BM + row_in_tile;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      float dg_acc = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld_32x32(taddr + (uint32_t)c, v);
-        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
-        epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
-      if (epi.kind == EPI_DECAY_DG) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
-        if (lane == 0) epi.tile_partial[4 * (int64_t)t + (warp - 2)] = dg_acc;
-      }
-    }
+    epilogue_warps<TC_BM, BN, false>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
+                                     blockIdx.x, gridDim.x, 0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar,
+                                     abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, 4, 0);
   }
 
   tc_fence_before();
@@ -387,12 +674,13 @@ struct Tc2Config {
   static constexpr uint32_t B_BYTES = 128 * TC_BK * 2;  // this CTA's 128 columns of B
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * TC2_BN;
-  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
 };
 
 template <bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_aux,
                     const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
                     const int tiles_per_batch, const int total_tiles) {
   using Cfg = Tc2Config;
@@ -406,12 +694,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 staging tiles
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_bar = drain + 1;  // 4 warps x 2 slots
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -431,12 +721,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (epi.staged != EPI_MODE_DIRECT) {
+      tma_prefetch_desc(&tma_out);
+      if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
@@ -552,37 +847,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
-    const int quad = warp & 3;
-    const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
-    const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
-    const uint32_t leader_tempty = mapa_shared(smem_u32(tempty), 0);
-    int j = 0;
-    for (int t = pair; t < total_tiles; t += pairs, ++j) {
-      const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
-      const int acc = j & 1;
-      const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-      if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, DEVERR_GEMM2_WAIT)) break;
-      tc_fence_after();
-      const int row = tc.mb * BM + row_in_tile;
-      const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      float dg_acc = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld_32x32(taddr + (uint32_t)c, v);
-        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(leader_tempty + (uint32_t)(acc * sizeof(uint64_t)));
-      if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
-        epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
-      if (epi.kind == EPI_DECAY_DG) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
-        if (lane == 0) epi.tile_partial[8 * (int64_t)t + rank * 4 + (warp - 2)] = dg_acc;
-      }
-    }
+    epilogue_warps<BM, BN, true>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
+                                 pairs, (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0),
+                                 epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 8, (int)rank * 4);
   }
 
   tc_fence_before();
@@ -746,14 +1013,55 @@ int make_tmap(CUtensorMap* map, const Operand& op, int batches, uint32_t box_inn
   return ULM_OK;
 }
 
+// 3-D map over (cols, rows, batch) of an epilogue array (output or tile aux) whose boxes are the
+// staging tiles of `mode`: 32 (EPI_MODE_WARP) or 128 (EPI_MODE_CTA) rows x 128 bytes, 128-byte
+// swizzle.
+bool make_epi_tmap(CUtensorMap* map, int mode, const void* ptr, int dtype, int64_t cols, int64_t rows, int batches,
+                   int64_t ld, int64_t bstride) {
+  auto fn = encode_tiled();
+  if (!fn || !ptr) return false;
+  const bool f32 = dtype == ULM_F32;
+  const int64_t es = f32 ? 4 : 2;
+  if (!is_aligned16(ptr) || (ld * es) % 16 != 0) return false;
+  const int64_t bs_bytes = batches > 1 ? bstride * es : rows * ld * es;
+  if (bs_bytes % 16 != 0 || bs_bytes <= 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * es), (cuuint64_t)bs_bytes};
+  const bool cta = mode == EPI_MODE_CTA;
+  cuuint32_t box[3] = {f32 ? 32u : 64u, cta ? 128u : 32u, 1};  // 128-byte rows
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// library-wide epilogue layout of the tensor-core kernels (ulm_set_epilogue_mode)
+static int g_epi_mode = EPI_MODE_WARP;
+
+// Tensor maps of the staged epilogue; falls back to direct stores when the layout does not allow it.
+void prepare_epilogue(GemmEpilogue& e, const GemmShape& s, CUtensorMap* tout, CUtensorMap* taux) {
+  memset(tout, 0, sizeof(CUtensorMap));
+  memset(taux, 0, sizeof(CUtensorMap));
+  const int mode = g_epi_mode;
+  bool ok = mode != EPI_MODE_DIRECT && e.vec_ok && s.N >= 32 &&
+            make_epi_tmap(tout, mode, e.out, e.out_dtype, s.N, s.M, s.batches, e.ldo, e.out_bstride);
+  if (ok && has_tile_aux(e.kind))
+    ok = make_epi_tmap(taux, mode, e.aux, e.out_dtype, s.N, s.M, s.batches, e.ld_aux, e.aux_bstride);
+  e.staged = ok ? mode : EPI_MODE_DIRECT;
+}
+
 template <int BN, bool A_MN, bool B_MN>
-int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e_in, cudaStream_t st) {
   using Cfg = TcConfig<BN>;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tout, taux;
   int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : TC_BM);
   if (rc) return rc;
   rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : BN);
   if (rc) return rc;
+  GemmEpilogue e = e_in;
+  prepare_epilogue(e, s, &tout, &taux);
   const int dev = current_device();
   static bool configured[64] = {};
   if (dev < 0 || dev >= 64) {
@@ -772,8 +1080,8 @@ int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const Gemm
   const int total = (int)total64;
   if (total == 0) return ULM_OK;
   const int grid = total < sm_count(dev) ? total : sm_count(dev);
-  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, s, e, m_blocks, n_blocks, tpb,
-                                                                            total);
+  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, s, e, m_blocks,
+                                                                            n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc_gemm_kernel");
   return ULM_OK;
 }
@@ -787,13 +1095,15 @@ int dispatch_tc_major(const Operand& A, const Operand& B, const GemmShape& s, co
 }
 
 template <bool A_MN, bool B_MN>
-int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e_in, cudaStream_t st) {
   using Cfg = Tc2Config;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tout, taux;
   int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : 128);
   if (rc) return rc;
   rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : 128);
   if (rc) return rc;
+  GemmEpilogue e = e_in;
+  prepare_epilogue(e, s, &tout, &taux);
   const int dev = current_device();
   static bool configured[64] = {};
   if (dev < 0 || dev >= 64) {
@@ -813,8 +1123,8 @@ int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const Gem
   if (total == 0) return ULM_OK;
   const int max_pairs = sm_count(dev) / 2;
   const int pairs = total < max_pairs ? total : max_pairs;
-  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, s, e, m_blocks, n_blocks, tpb,
-                                                                           total);
+  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, s, e, m_blocks,
+                                                                           n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc2_gemm_kernel");
   return ULM_OK;
 }

@@ -48,6 +48,9 @@ struct GemmEpilogue {
   // outputs (blocks of 256, 128 or 64 columns depending on the back end; unused slots untouched)
   float* row_partial;
   int part_ld;
+  // set by the tensor-core launch: stage output chunks in shared memory and write them (and read a
+  // tile aux) with TMA tensor copies
+  int staged;
 };
 
 // A matrix operand in global memory: element (b, row, col) of its storage order at

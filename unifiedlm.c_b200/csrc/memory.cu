@@ -69,6 +69,7 @@ GemmEpilogue make_epilogue(int kind, int out_dtype, void* out, int64_t ldo, int6
   e.tile_partial = nullptr;
   e.row_partial = nullptr;
   e.part_ld = 0;
+  e.staged = 0;
   const int vec = out_dtype == ULM_F32 ? 4 : 8;
   e.vec_ok = is_aligned16(out) && ldo % vec == 0 && bstride % vec == 0;
   return e;
@@ -179,6 +180,13 @@ extern "C" int64_t ulm_operand_ld(int64_t n) { return ((n + 7) / 8) * 8; }
 extern "C" int ulm_set_gemm_pairs(int enable) {
   const int old = g_gemm_pairs;
   g_gemm_pairs = enable ? 1 : 0;
+  return old;
+}
+
+extern "C" int ulm_set_epilogue_mode(int mode) {
+  if (mode < EPI_MODE_DIRECT || mode > EPI_MODE_CTA) return -1;
+  const int old = g_epi_mode;
+  g_epi_mode = mode;
   return old;
 }
 
