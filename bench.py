@@ -481,8 +481,8 @@ def main():
 
     # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, den); operator fwd 4
     # (stats scan, convert v, scores, read); operator bwd 8 (convert dfast, scores grad, dq, dk, dv,
-    # stats scan, dw, dg); prologue bwd 9 (addr_bwd, db column sums + their sum, deps, dK GEMM,
-    # dK sum, du GEMM, conv bwd, dconv sum)
+    # stats scan, dw, dg); prologue bwd 9 (address backward, db column sums + their sum, deps,
+    # dK GEMM, dK sum, du GEMM, conv bwd, dconv sum)
     launches = args.steps * W["L"] * (3 + 4 + 8 + 9)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,

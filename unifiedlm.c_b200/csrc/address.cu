@@ -185,6 +185,45 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// column sums of a bf16 (rows x cols) array over chunks of rows, part[chunk][col]: a CTA covers
+// 256 columns (8 per lane, one 16-byte load per row: a warp reads 512 contiguous bytes) of one chunk;
+// warp w adds rows w, w + 8, ... of the chunk in order, then the warps' sums are added in warp order.
+__global__ void __launch_bounds__(256)
+    col_sum_bf16x8_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows, int cols,
+                          int rows_per_chunk, float* __restrict__ part) {
+  __shared__ float red[8][257];
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_chunk;
+  const int64_t r1 = min(rows, r0 + rows_per_chunk);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < cols) {
+#pragma unroll 4
+    for (int64_t rr = r0 + wp; rr < r1; rr += 8) {
+      const uint4 pk = *reinterpret_cast<const uint4*>(x + rr * ld + c0);
+      const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h;
+        memcpy(&h, &w4[j], 4);
+        const float2 f = __bfloat1622float2(h);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[wp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  const int col = blockIdx.x * 256 + threadIdx.x;
+  if (col < cols) {
+    float t = red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) t += red[w][threadIdx.x];
+    part[(int64_t)blockIdx.y * cols + col] = t;
+  }
+}
+
 // column sums of a (rows x cols) operand-type array over chunks of rows: part[chunk][col]
 template <typename InT>
 __global__ void col_sum_kernel(const void* __restrict__ x, int64_t ld, int64_t rows, int cols, int rows_per_chunk,
@@ -198,7 +237,40 @@ __global__ void col_sum_kernel(const void* __restrict__ x, int64_t ld, int64_t r
   part[(int64_t)blockIdx.y * cols + col] = s;
 }
 
-// out[i] = sum_p part[p][i] over nparts, in order (dK from the split-K partials, db)
+// out[i] = sum over p of part[p][i] for n % 4 == 0 and 16-byte aligned rows: a CTA covers 128
+// consecutive outputs (4 per lane); warp w adds parts w, w + 8, ... in order, then the eight warp
+// sums are added in warp order (a fixed order: deterministic)
+__global__ void __launch_bounds__(256)
+    sum_parts4_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, float* __restrict__ out) {
+  __shared__ float4 red[8][32];
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = ((int64_t)blockIdx.x * 32 + lane) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (i < n) {
+    for (int64_t p = wp; p < nparts; p += 8) {
+      const float4 a = *reinterpret_cast<const float4*>(part + p * n + i);
+      acc.x += a.x;
+      acc.y += a.y;
+      acc.z += a.z;
+      acc.w += a.w;
+    }
+  }
+  red[wp][lane] = acc;
+  __syncthreads();
+  if (wp == 0 && i < n) {
+    float4 t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      t.x += red[w][lane].x;
+      t.y += red[w][lane].y;
+      t.z += red[w][lane].z;
+      t.w += red[w][lane].w;
+    }
+    *reinterpret_cast<float4*>(out + i) = t;
+  }
+}
+
+// out[i] = sum_p part[p][i] over nparts, in order (any n)
 __global__ void sum_parts_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, float* __restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
@@ -362,6 +434,18 @@ int addr_check(int h_dtype, int prec, int64_t B, int64_t T, int64_t D, int64_t M
 
 }  // namespace
 
+// out = sum of nparts arrays of n floats, in a fixed order
+int sum_parts(const float* part, int64_t nparts, int64_t n, float* out, cudaStream_t st) {
+  if (n % 4 == 0 && is_aligned16(part) && is_aligned16(out)) {
+    sum_parts4_kernel<<<(unsigned)cdiv(n, 128), 256, 0, st>>>(part, nparts, n, out);
+    ULM_LAUNCH_CHECK("sum_parts4_kernel");
+  } else {
+    sum_parts_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 16 * 148), 256, 0, st>>>(part, nparts, n, out);
+    ULM_LAUNCH_CHECK("sum_parts_kernel");
+  }
+  return ULM_OK;
+}
+
 // column blocks of the key GEMM's row partial sums: the narrowest tile of any GEMM back end is 64
 int64_t addr_part_ld(int64_t M) { return cdiv(M, 64); }
 
@@ -432,21 +516,24 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   const int dt = prec == ULM_PREC_FP32 ? ULM_F32 : ULM_BF16;
   const int64_t rows = B * T;
   AddrBwdWork wk = carve_addr_work(work, B, T, D, M, dt);
-  // da and the d eps partials
+  // da and the d eps partials, then db = column sums of da
   addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, normalized ? 0 : 1, wk.da, dt, wk.ld_m,
                                                      wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
   ULM_LAUNCH_CHECK("addr_bwd_kernel");
-  // db = column sums of da
-  {
+  if (dt == ULM_BF16 && M % 8 == 0 && wk.ld_m % 8 == 0) {
+    dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
+    col_sum_bf16x8_kernel<<<g2, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(wk.da), wk.ld_m, rows, (int)M,
+                                              DB_ROWS_PER_CHUNK, wk.db_part);
+    ULM_LAUNCH_CHECK("col_sum_bf16x8_kernel");
+  } else {
     dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
     if (dt == ULM_F32)
       col_sum_kernel<float><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
     else
       col_sum_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
     ULM_LAUNCH_CHECK("col_sum_kernel");
-    sum_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(wk.db_part, wk.db_chunks, M, dkey_b);
-    ULM_LAUNCH_CHECK("sum_parts_kernel");
   }
+  if (int rc = sum_parts(wk.db_part, wk.db_chunks, M, dkey_b, st)) return rc;
   sum_all_kernel<<<1, 256, 0, st>>>(wk.deps_part, wk.ctas, deps);
   ULM_LAUNCH_CHECK("sum_all_kernel");
   // dK = da^T u, split over S chunks of rows (each chunk a GEMM batch), then summed in order
@@ -457,9 +544,7 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
     GemmShape s{wk.S, (int)M, (int)D, (int)rc_rows, CAUSAL_NONE};
     GemmEpilogue e = plain_epilogue(EPI_STORE, ULM_F32, wk.dk_part, D, M * D);
     if (int rc = run_gemm(A, Bu, s, e, st)) return rc;
-    sum_parts_kernel<<<(unsigned)std::min<int64_t>(cdiv(M * D, 256), 16 * 148), 256, 0, st>>>(wk.dk_part, wk.S,
-                                                                                              M * D, dkey_w);
-    ULM_LAUNCH_CHECK("sum_parts_kernel");
+    if (int rc = sum_parts(wk.dk_part, wk.S, M * D, dkey_w, st)) return rc;
   }
   // du = da K
   {
@@ -484,8 +569,6 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   ULM_CONVB(1) ULM_CONVB(2) ULM_CONVB(3) ULM_CONVB(4) ULM_CONVB(5) ULM_CONVB(6) ULM_CONVB(7) ULM_CONVB(8)
 #undef ULM_CONVB
   ULM_LAUNCH_CHECK("addr_conv_bwd_kernel");
-  sum_parts_kernel<<<(unsigned)cdiv(D * conv_size, 256), 256, 0, st>>>(wk.dconv_part, (int64_t)wk.chunks * B,
-                                                                       D * conv_size, dconv_w);
-  ULM_LAUNCH_CHECK("sum_parts_kernel");
+  if (int rc = sum_parts(wk.dconv_part, (int64_t)wk.chunks * B, D * conv_size, dconv_w, st)) return rc;
   return ULM_OK;
 }

@@ -209,16 +209,19 @@ namespace cg = cooperative_groups;
 
 template <int SEG, int WARPS, typename OpT>
 __global__ void __launch_bounds__(32 * WARPS)
-    stats_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_r, const float* __restrict__ den,
+    stats_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_r, const __grid_constant__ CUtensorMap map_r1,
+                         const float* __restrict__ den,
                          const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ q,
                          float* __restrict__ c, void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T,
                          int M) {
   constexpr int R = SEG * WARPS;
-  extern __shared__ __align__(128) float tile[];  // [0]: r rows t0.., [1]: k rows (r rows t0-1..)
+  // rows cta_t0 - 1 .. cta_t0 + R - 1 of r: row i is the write address k of position cta_t0 + i and
+  // the read address of position cta_t0 + i - 1 (R rows in one box, the last row in a second)
+  extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float warp_sum[WARPS][32];
   __shared__ float cta_total[32];
-  __shared__ float sinv[R + 1];  // row scales of rows cta_t0 - 1 .. cta_t0 + R - 1
+  __shared__ float sinv[R + 1];  // row scales of the tile's rows
   __shared__ int ok_flag;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
@@ -234,9 +237,9 @@ __global__ void __launch_bounds__(32 * WARPS)
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bar, 2u * R * 32u * 4u);
-    tma_load_3d(&map_r, tile, &bar, m0, cta_t0, b);
-    tma_load_3d(&map_r, tile + R * 32, &bar, m0, cta_t0 - 1, b);
+    mbar_arrive_expect_tx(&bar, (R + 1) * 32u * 4u);
+    tma_load_3d(&map_r, tile, &bar, m0, cta_t0 - 1, b);
+    tma_load_3d(&map_r1, tile + R * 32, &bar, m0, cta_t0 + R - 1, b);
   }
   fill_row_scales(sinv, den, b, T, cta_t0 - 1, R);  // overlaps the tile load
   if (threadIdx.x == 0) ok_flag = 1;
@@ -249,13 +252,12 @@ __global__ void __launch_bounds__(32 * WARPS)
   const bool ok = ok_flag != 0;
   const float gg = *g;
   const float lam = expf(gg);
-  const float* rt = tile + (wp * SEG) * 32 + lane;
-  const float* kt = tile + R * 32 + (wp * SEG) * 32 + lane;
-  const float* si = sinv + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
+  const float* xt = tile + (wp * SEG) * 32 + lane;  // xt[i * 32]: k of position t0 + i, r of t0 + i - 1
+  const float* si = sinv + wp * SEG;
   float run = 0.f;
   if (ok) {
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, kt[i * 32] * si[i]);
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, xt[i * 32] * si[i]);
   }
   warp_sum[wp][lane] = run;
   __syncthreads();
@@ -272,25 +274,26 @@ __global__ void __launch_bounds__(32 * WARPS)
   for (int j = 0; j < wp; ++j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
   if (ok && m < M) {
     const float wm = w[m];
-    const int64_t row0 = (int64_t)b * T;
     const int t0 = cta_t0 + wp * SEG;
+    const int64_t row = (int64_t)b * T + t0;
+    float* qp = q + row * M + m;
+    float* cp = c ? c + row * M + m : nullptr;
+    const int64_t io = row * ldop + m;
     run = carry;
+    float kk = xt[0] * si[0];
 #pragma unroll
     for (int i = 0; i < SEG; ++i) {
-      const int t = t0 + i;
-      if (t < T) {
-        const float kk = kt[i * 32] * si[i];
+      const float rv = xt[(i + 1) * 32] * si[i + 1];
+      if (t0 + i < T) {
         run = fmaf(lam, run, kk);
         const float cc = wm + run;
-        const float rv = rt[i * 32] * si[i + 1];
-        const float qq = rv * __frcp_rn(cc);
-        const int64_t idx = (row0 + t) * M + m;
-        q[idx] = qq;
-        if (c) c[idx] = cc;
-        const int64_t io = (row0 + t) * ldop + m;
-        store_op<OpT>(qop, io, qq);
-        store_op<OpT>(kop, io, kk);
+        const float qq = rv * fast_rcp(cc);
+        qp[(int64_t)i * M] = qq;
+        if (cp) cp[(int64_t)i * M] = cc;
+        store_op<OpT>(qop, io + (int64_t)i * ldop, qq);
+        store_op<OpT>(kop, io + (int64_t)i * ldop, kk);
       }
+      kk = rv;
     }
   }
   cluster.sync();
@@ -309,8 +312,8 @@ __global__ void __launch_bounds__(32 * WARPS)
                          double* __restrict__ part_dg, int T, int M, int has_dqo, int fast_identity) {
   constexpr int R = SEG * WARPS;
   constexpr int TILE = R * 32;
-  // tiles: dqf (then dq/c), dq_out (then dc), dk, then either q, c, k (saved) or the r tile
-  // rows t0-1 .. t0+R-1 (recompute)
+  // tiles: dqf, dk, then either the r tile rows t0-1 .. t0+R-1 (recompute) or q, c, k (saved),
+  // then dq_out when given
   extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float warp_sum[WARPS][32];
@@ -330,9 +333,9 @@ __global__ void __launch_bounds__(32 * WARPS)
   const bool valid = m < M;
   const int cta_t0 = cr * R;
   float* t_dqf = tile;
-  float* t_dqo = tile + TILE;
-  float* t_dk = tile + 2 * TILE;
-  float* t_x = tile + 3 * TILE;  // recompute: r rows (R+1); saved: q, c, k tiles
+  float* t_dk = tile + TILE;
+  float* t_x = tile + 2 * TILE;  // recompute: r rows (R+1); saved: q, c, k tiles
+  float* t_dqo = t_x + (RECOMPUTE ? R + 1 : 3 * R) * 32;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_barrier_init();
@@ -369,8 +372,8 @@ __global__ void __launch_bounds__(32 * WARPS)
   const float t_mid = 0.5f * (float)(T - 1);
   const int t0 = cta_t0 + wp * SEG;
   const int o = (wp * SEG) * 32 + lane;
-  float* s_dqf = t_dqf + o;
-  float* s_dqo = t_dqo + o;
+  const float* s_dqf = t_dqf + o;
+  const float* s_dqo = t_dqo + o;
   const float* s_dk = t_dk + o;
   const float* s_k = RECOMPUTE ? t_x + o : t_x + 2 * TILE + o;   // k_t = r_{t-1}
   const float* s_r = t_x + o + 32;                                // recompute: r_t
@@ -400,6 +403,7 @@ __global__ void __launch_bounds__(32 * WARPS)
   }
 
   float dw_acc = 0.f, dg_f = 0.f, run = 0.f;
+  float drd_v[SEG], dc_v[SEG];  // dq / c and dc per row, kept for the reverse pass
   if (ok) {
     float n = n_carry;
 #pragma unroll
@@ -410,12 +414,12 @@ __global__ void __launch_bounds__(32 * WARPS)
       if (RECOMPUTE) {
         n = fmaf(lam, n, s_k[i * 32] * si[i]);
         cc = wm + n;
-        inv = __frcp_rn(cc);
+        inv = fast_rcp(cc);
         qq = (s_r[i * 32] * si[i + 1]) * inv;
       } else {
         cc = s_c[i * 32];
         qq = s_q[i * 32];
-        inv = __frcp_rn(cc);
+        inv = fast_rcp(cc);
       }
       if (!(t < T && valid)) {
         cc = 1.f;
@@ -426,15 +430,18 @@ __global__ void __launch_bounds__(32 * WARPS)
       const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
       const float drd = dq * inv;
       const float dc = -drd * qq;
-      s_dqf[i * 32] = drd;
-      s_dqo[i * 32] = dc;
+      drd_v[i] = drd;
+      dc_v[i] = dc;
       dw_acc += dc;
       float term = dc * (cc - wm);
       if (fast_identity) term += qq * dqfv;
       dg_f = fmaf((float)t - t_mid, term, dg_f);
     }
 #pragma unroll
-    for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, s_dqo[i * 32]);
+    for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dc_v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) drd_v[i] = dc_v[i] = 0.f;
   }
   warp_sum[wp][lane] = run;
   warp_dw[wp][lane] = dw_acc;
@@ -463,8 +470,8 @@ __global__ void __launch_bounds__(32 * WARPS)
       if (t < T) {
         const float dkv = s_dk[i * 32];
         const float kv = s_k[i * 32] * si[i];
-        run = fmaf(lam, run, s_dqo[i * 32]);  // dkc_t
-        dr[base + (int64_t)t * M] = s_dqf[i * 32] + dkt_next;
+        run = fmaf(lam, run, dc_v[i]);  // dkc_t
+        dr[base + (int64_t)t * M] = drd_v[i] + dkt_next;
         dkt_next = dkv + run;
         float term = -kv * run;
         if (fast_identity) term -= kv * dkv;
@@ -622,7 +629,7 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     if (int rc = make_rows_tmap(&mr, r, B, T, M, recompute ? R + 1 : R)) return rc;
     const int C = tp.ctas;
     dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
-    const size_t smem = (size_t)(recompute ? 4 * R + 1 : 6 * R) * 32 * 4;
+    const size_t smem = (size_t)((recompute ? 3 * R + 1 : 5 * R) + (dq_out ? R : 0)) * 32 * 4;
     const int hq = dq_out ? 1 : 0;
     int rc;
 #define ULM_BWD_TMA(W, RC)                                                                                       \
@@ -681,19 +688,21 @@ int stats_fwd_run(const float* r, const float* den, const float* w, const float*
   if (tp.ctas) {
     const int R = tp.seg * tp.warps;
     CUtensorMap mr;
+    CUtensorMap mr1;
     if (int rc = make_rows_tmap(&mr, r, B, T, M, R)) return rc;
+    if (int rc = make_rows_tmap(&mr1, r, B, T, M, 1)) return rc;
     const int C = tp.ctas;
     dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
-    const size_t smem = (size_t)2 * R * 32 * 4;
+    const size_t smem = (size_t)(R + 1) * 32 * 4;
     const bool bf = op_dtype == ULM_BF16;
     if (tp.warps == 8)
-      return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, den, w,
+      return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, mr1, den, w,
                                       g, q, c, qop, kop, ld_op, (int)T, (int)M)
-                : launch_cluster_smem(stats_fwd_tma_kernel<16, 8, float>, grid, 256, C, smem, st, mr, den, w, g, q, c,
+                : launch_cluster_smem(stats_fwd_tma_kernel<16, 8, float>, grid, 256, C, smem, st, mr, mr1, den, w, g, q, c,
                                       qop, kop, ld_op, (int)T, (int)M);
-    return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 16, __nv_bfloat16>, grid, 512, C, smem, st, mr, den, w,
+    return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 16, __nv_bfloat16>, grid, 512, C, smem, st, mr, mr1, den, w,
                                     g, q, c, qop, kop, ld_op, (int)T, (int)M)
-              : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, den, w, g, q, c,
+              : launch_cluster_smem(stats_fwd_tma_kernel<16, 16, float>, grid, 512, C, smem, st, mr, mr1, den, w, g, q, c,
                                     qop, kop, ld_op, (int)T, (int)M);
   }
   dim3 grid((unsigned)cdiv(M, 32), (unsigned)B);
