@@ -143,9 +143,8 @@ int ulm_set_gemm_pairs(int enable);
 
 /* Library-wide epilogue layout of the bf16 products: 0 = each thread stores its output row
  * segment directly; 1 (default) = each epilogue warp stages 32-row x 128-byte chunks in shared
- * memory and writes them with TMA tensor stores; 2 = the four epilogue warps stage 128-row x
- * 128-byte chunks together and one thread writes each with a TMA tensor store. All compute the
- * same values. Returns the previous mode, or -1 (no change) for an unknown mode. */
+ * memory and writes them with TMA tensor stores. Both compute the same values. Returns the
+ * previous mode, or -1 (no change) for an unknown mode. */
 int ulm_set_epilogue_mode(int mode);
 
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).

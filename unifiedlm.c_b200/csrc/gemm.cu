@@ -185,16 +185,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // ---- staged epilogues -------------------------------------------------------------------------
 // The output leaves through shared memory and TMA tensor stores, so global writes are whole lines
 // instead of 32 row fragments per store instruction; a tile aux (scores / addend) arrives the same
-// way through a TMA load into the staging tile, and the epilogue computes in place. Two layouts:
-//   EPI_MODE_WARP : each epilogue warp stages 32 rows x 128 bytes (32 fp32 / 64 bf16 columns,
-//                   128-byte swizzle) in two 4 KB slots of its own
-//   EPI_MODE_CTA  : the four epilogue warps stage 128 rows x 128 bytes together (32 fp32 / 64 bf16
-//                   columns, 128-byte swizzle) in two 16 KB slots; named barriers order the warps
-//                   and one thread issues the 16 KB copies
-// Writes of one row per lane into the swizzled layout are conflict-free 16-byte stores.
-enum { EPI_MODE_DIRECT = 0, EPI_MODE_WARP = 1, EPI_MODE_CTA = 2 };
-constexpr uint32_t EPI_SMEM_BYTES = 32768;
-constexpr int EPI_BAR_ID = 1;  // named barrier of the 128 epilogue threads
+// way through a TMA load into the staging tile, and the epilogue computes in place. Each epilogue
+// warp stages 32 rows x 128 bytes (32 fp32 / 64 bf16 columns, 128-byte swizzle: one row per lane,
+// conflict-free 16-byte shared stores) in two 4 KB slots of its own (EPI_MODE_WARP);
+// EPI_MODE_DIRECT stores row segments straight from registers.
+enum { EPI_MODE_DIRECT = 0, EPI_MODE_WARP = 1 };
+// Epilogue warps per CTA: two per TMEM lane quadrant, each taking half of the tile's columns.
+constexpr int EPI_WARPS = 8;
+constexpr uint32_t EPI_SMEM_BYTES = EPI_WARPS * 2 * 4096;
 
 __device__ __forceinline__ uint32_t sw128_off(int r, int k) { return (uint32_t)(r * 128 + ((k ^ (r & 7)) << 4)); }
 
@@ -248,22 +246,6 @@ __device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, f
   }
 }
 
-__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync %0, 128;" ::"n"(EPI_BAR_ID) : "memory"); }
-
-// named barrier of the epilogue threads that also ANDs a predicate over them (uniform decisions)
-__device__ __forceinline__ bool epi_bar_and(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "n"(EPI_BAR_ID)
-      : "memory");
-  return r != 0;
-}
-
 // EPI_MODE_WARP: one chunk (32 rows x 128 bytes: 32 fp32 / 64 bf16 columns at col0) of the warp's
 // rows row_base..+31; taddr = this warp's TMEM quadrant at the chunk's first column. n counts the
 // warp's staged chunks (slot n % 2, barrier phase n / 2). False if the aux wait gave up.
@@ -310,60 +292,12 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
   return true;
 }
 
-// EPI_MODE_CTA: one 128-row chunk (32 fp32 / 64 bf16 columns at col0) of the CTA's tile rows
-// row0..row0+127, all four epilogue warps; taddr = this warp's TMEM quadrant at the chunk's first
-// column. n counts the CTA's staged chunks. False (uniformly) if an aux wait gave up.
-template <bool F32>
-__device__ __forceinline__ bool epi_chunk_cta(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
-                                              const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
-                                              float gl2, int b, int row0, int col0, uint32_t taddr, float& dg_acc,
-                                              volatile int* abort_flag, int site) {
-  const int lane = threadIdx.x & 31;
-  const int r = ((threadIdx.x >> 5) & 3) * 32 + lane;  // row in the CTA's 128 (TMEM lane quadrant)
-  const bool issuer = threadIdx.x == 64;               // warp 2, lane 0
-  const bool aux = has_tile_aux(e.kind);
-  const int sl = n & 1;
-  const uint32_t parity = (uint32_t)(n >> 1) & 1u;
-  ++n;
-  uint8_t* tile = slots + sl * 16384;
-  if (issuer) {
-    bulk_wait_group_read<1>();  // the store of chunk n - 2 has read the slot
-    if (aux) {
-      mbar_arrive_expect_tx(&abar[sl], 16384u);
-      tma_load_3d(tma_aux, tile, &abar[sl], col0, row0, b);
-    }
-  }
-  epi_bar_sync();  // slot free for every thread
-  bool ok = true;
-  if (aux) ok = wait_or_abort(&abar[sl], parity, abort_flag, site);
-  if (aux && !epi_bar_and(ok)) return false;
-#pragma unroll 1
-  for (int h = 0; h < (F32 ? 1 : 2); ++h) {
-    float v[32], p[32];
-    tmem_ld_32x32(taddr + (uint32_t)(32 * h), v);
-    if (aux) {
-      stage_read<F32>(tile, r, 4 * h, p);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = 0.f;
-    }
-    const int c = col0 + 32 * h;
-    epilogue_math<32>(e, gl2, row0 + r, c, min(32, s.N - c), v, p, dg_acc);
-    stage_write<F32>(tile, r, 4 * h, v);
-  }
-  fence_proxy_async_smem();
-  epi_bar_sync();  // the chunk is complete in shared memory
-  if (issuer) {
-    tma_store_3d(tma_out, tile, col0, row0, b);
-    bulk_commit_group();
-  }
-  return true;
-}
-
-// The epilogue warps (2..5) of both tensor-core kernels: for every tile of this CTA (t_first,
-// t_first + t_stride, ...) wait for its accumulator, write it through the epilogue and hand the
-// TMEM buffer back. cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows);
-// partials for EPI_DECAY_DG go to tile_partial[part_stride * t + part_off + epilogue warp].
+// The epilogue warps (2 .. 2 + EPI_WARPS - 1) of both tensor-core kernels: for every tile of this
+// CTA (t_first, t_first + t_stride, ...) wait for its accumulator, write it through the epilogue
+// and hand the TMEM buffer back. Warp w reads TMEM lane quadrant w % 4 and column half
+// (w - 2) / 4. cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows); partials for
+// EPI_DECAY_DG go to tile_partial[part_stride * t + part_off + (w - 2)], row sums for EPI_RELU2 to
+// row_partial[row][2 * column block + half].
 template <int BM, int BN, bool PAIR>
 __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const GemmEpilogue& epi,
                                                const CUtensorMap* tma_out, const CUtensorMap* tma_aux,
@@ -372,13 +306,16 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
                                                uint64_t* tfull, uint64_t* tempty, uint32_t leader_tempty,
                                                uint8_t* stage, uint64_t* aux_bar, volatile int* abort_flag,
                                                int site, int part_stride, int part_off) {
+  constexpr int HALF = BN / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ew = warp - 2;
   const int quad = warp & 3;
+  const int half = ew >> 2;
   const int mode = epi.staged;
   const bool f32 = epi.out_dtype == ULM_F32;
   const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
-  uint8_t* wslots = stage + (warp - 2) * 8192;  // EPI_MODE_WARP: this warp's two 4 KB slots
-  uint64_t* wbar = aux_bar + (warp - 2) * 2;
+  uint8_t* wslots = stage + ew * 8192;  // this warp's two 4 KB slots
+  uint64_t* wbar = aux_bar + ew * 2;
   int n = 0;
   int j = 0;
   bool ok = true;
@@ -386,31 +323,21 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
     const int acc = j & 1;
     const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
-    ok = wait_or_abort(&tfull[acc], acc_phase, abort_flag, site);
-    if (mode == EPI_MODE_CTA) ok = epi_bar_and(ok);
-    if (!ok) break;
+    if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, site)) {
+      ok = false;
+      break;
+    }
     tc_fence_after();
-    const int row0 = tc.mb * BM + cta_rows;  // the CTA's first tile row
-    const int row = row0 + quad * 32 + lane;
-    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+    const int row_base = tc.mb * BM + cta_rows + quad * 32;
+    const int row = row_base + lane;
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + half * HALF);
+    const int col_base = tc.nb * BN + half * HALF;
     float dg_acc = 0.f;
-    if (mode == EPI_MODE_CTA) {
+    if (mode == EPI_MODE_WARP) {
       const int cw = f32 ? 32 : 64;
 #pragma unroll 1
-      for (int c = 0; c < BN && ok; c += cw) {
-        const int col0 = tc.nb * BN + c;
-        if (col0 >= shape.N) break;
-        ok = f32 ? epi_chunk_cta<true>(epi, shape, tma_out, tma_aux, stage, aux_bar, n, gl2, tc.b, row0, col0,
-                                       taddr + (uint32_t)c, dg_acc, abort_flag, site)
-                 : epi_chunk_cta<false>(epi, shape, tma_out, tma_aux, stage, aux_bar, n, gl2, tc.b, row0, col0,
-                                        taddr + (uint32_t)c, dg_acc, abort_flag, site);
-      }
-    } else if (mode == EPI_MODE_WARP) {
-      const int row_base = row0 + quad * 32;
-      const int cw = f32 ? 32 : 64;
-#pragma unroll 1
-      for (int c = 0; c < BN && ok; c += cw) {
-        const int col0 = tc.nb * BN + c;
+      for (int c = 0; c < HALF && ok; c += cw) {
+        const int col0 = col_base + c;
         if (row_base >= shape.M || col0 >= shape.N) break;
         ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, gl2, tc.b, row_base, col0,
                                         taddr + (uint32_t)c, dg_acc, abort_flag, site)
@@ -419,10 +346,10 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < HALF; c += 32) {
         float v[32];
         tmem_ld_32x32(taddr + (uint32_t)c, v);
-        epilogue_store32(epi, shape, gl2, tc.b, row, tc.nb * BN + c, v, dg_acc);
+        epilogue_store32(epi, shape, gl2, tc.b, row, col_base + c, v, dg_acc);
       }
     }
     if (!ok) break;
@@ -435,26 +362,22 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
         mbar_arrive(&tempty[acc]);
     }
     if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
-      epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + tc.nb] = dg_acc;
+      epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + 2 * tc.nb + half] = dg_acc;
     if (epi.kind == EPI_DECAY_DG) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
-      if (lane == 0) epi.tile_partial[part_stride * (int64_t)t + part_off + (warp - 2)] = dg_acc;
+      if (lane == 0) epi.tile_partial[part_stride * (int64_t)t + part_off + ew] = dg_acc;
     }
   }
-  if (mode != EPI_MODE_DIRECT) {
+  if (mode == EPI_MODE_WARP && lane == 0) {
     // an aux load still in flight after an abort lands before the CTA exits; stores complete
-    const bool issuer = mode == EPI_MODE_CTA ? threadIdx.x == 64 : lane == 0;
-    if (issuer) {
-      uint64_t* bars = mode == EPI_MODE_CTA ? aux_bar : wbar;
-      if (!ok && has_tile_aux(epi.kind) && n > 0) {
-        const int k = n - 1;
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&bars[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
-        }
+    if (!ok && has_tile_aux(epi.kind) && n > 0) {
+      const int k = n - 1;
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&wbar[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
       }
-      bulk_wait_group<0>();
     }
+    bulk_wait_group<0>();
   }
 }
 
@@ -463,17 +386,17 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 64 + 32 * EPI_WARPS;
 
 template <int BN>
 struct TcConfig {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int STAGES = BN == 256 ? 3 : 5;
   static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
   static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   // stages + staging tiles of the epilogue + 1024 alignment slack + barriers / TMEM slot / flags
-  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 512;
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -501,8 +424,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // 4 warps x 2 slots
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 8);
+  uint64_t* aux_bar = drain + 1;  // 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -515,10 +438,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -645,7 +568,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
     epilogue_warps<TC_BM, BN, false>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
                                      blockIdx.x, gridDim.x, 0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar,
-                                     abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, 4, 0);
+                                     abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, EPI_WARPS, 0);
   }
 
   tc_fence_before();
@@ -667,14 +590,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // CTAs' epilogue warps arrive on the leader's `tempty`.
 
 constexpr int TC2_BN = 256;
-constexpr int TC2_STAGES = 6;
+constexpr int TC2_STAGES = 5;
 
 struct Tc2Config {
   static constexpr uint32_t A_BYTES = 128 * TC_BK * 2;  // this CTA's 128 rows of A
   static constexpr uint32_t B_BYTES = 128 * TC_BK * 2;  // this CTA's 128 columns of B
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * TC2_BN;
-  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 256;
+  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 512;
 };
 
 template <bool A_MN, bool B_MN>
@@ -700,8 +623,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // 4 warps x 2 slots
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 8);
+  uint64_t* aux_bar = drain + 1;  // 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -718,10 +641,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&tempty[a], 2 * EPI_WARPS);  // the epilogue warps of both CTAs of the pair
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 8; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -849,7 +772,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     epilogue_warps<BM, BN, true>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
                                  pairs, (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0),
-                                 epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 8, (int)rank * 4);
+                                 epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 2 * EPI_WARPS,
+                                 (int)rank * EPI_WARPS);
   }
 
   tc_fence_before();
@@ -1014,8 +938,7 @@ int make_tmap(CUtensorMap* map, const Operand& op, int batches, uint32_t box_inn
 }
 
 // 3-D map over (cols, rows, batch) of an epilogue array (output or tile aux) whose boxes are the
-// staging tiles of `mode`: 32 (EPI_MODE_WARP) or 128 (EPI_MODE_CTA) rows x 128 bytes, 128-byte
-// swizzle.
+// staging tiles of EPI_MODE_WARP: 32 rows x 128 bytes, 128-byte swizzle.
 bool make_epi_tmap(CUtensorMap* map, int mode, const void* ptr, int dtype, int64_t cols, int64_t rows, int batches,
                    int64_t ld, int64_t bstride) {
   auto fn = encode_tiled();
@@ -1027,8 +950,8 @@ bool make_epi_tmap(CUtensorMap* map, int mode, const void* ptr, int dtype, int64
   if (bs_bytes % 16 != 0 || bs_bytes <= 0) return false;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batches};
   cuuint64_t strides[2] = {(cuuint64_t)(ld * es), (cuuint64_t)bs_bytes};
-  const bool cta = mode == EPI_MODE_CTA;
-  cuuint32_t box[3] = {f32 ? 32u : 64u, cta ? 128u : 32u, 1};  // 128-byte rows
+  (void)mode;
+  cuuint32_t box[3] = {f32 ? 32u : 64u, 32u, 1};  // 32 rows x 128 bytes
   cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,

@@ -39,13 +39,14 @@ struct GemmEpilogue {
   // EPI_STORE_ADD: out = acc + aux (aux fp32, same layout as the fp32 output).
   // EPI_RELU2: out = relu(acc + bias[n])^2, bias = aux (fp32, one value per output column).
   // EPI_DECAY_DG: aux = the forward's decayed scores P (same layout and type as the output); each
-  // epilogue warp adds sum (m-n) * P[m][n] * acc[m][n] over its rows of a tile and writes it to
-  // tile_partial[4 * tile + warp] (d/dg of the fast read, no atomics)
+  // epilogue warp adds sum (m-n) * P[m][n] * acc[m][n] over its part of a tile and writes it to its
+  // own slot of tile_partial (d/dg of the fast read, no atomics; decay_dg_partials slots in all)
   const void* aux;
   int64_t ld_aux, aux_bstride;
   float* tile_partial;
-  // EPI_RELU2 only, optional: row_partial[row * part_ld + column block] = sum of the tile row's
-  // outputs (blocks of 256, 128 or 64 columns depending on the back end; unused slots untouched)
+  // EPI_RELU2 only, optional: row_partial[row * part_ld + j] = sum of the row's outputs in column
+  // block j (blocks of 128 or 64 columns depending on the back end; part_ld >= N / 64; unused
+  // slots untouched)
   float* row_partial;
   int part_ld;
   // set by the tensor-core launch: stage output chunks in shared memory and write them (and read a

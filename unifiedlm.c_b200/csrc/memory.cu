@@ -184,7 +184,7 @@ extern "C" int ulm_set_gemm_pairs(int enable) {
 }
 
 extern "C" int ulm_set_epilogue_mode(int mode) {
-  if (mode < EPI_MODE_DIRECT || mode > EPI_MODE_CTA) return -1;
+  if (mode < EPI_MODE_DIRECT || mode > EPI_MODE_WARP) return -1;
   const int old = g_epi_mode;
   g_epi_mode = mode;
   return old;
