@@ -182,6 +182,18 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   }
 }
 
+// The tile that slot t of a persistent launch with P CTAs (or CTA pairs) works on, or -1. CTA p
+// takes slots p, p + P, p + 2P, ... When balanced (causal k-range products with few tiles per CTA,
+// where the uneven k ranges would leave CTAs idle at the end) the tile index space is ordered by
+// decreasing work (decode_tile) and every other round of P slots runs backwards (snake order),
+// close to a longest-first greedy assignment; otherwise tiles are taken in index order.
+__device__ __forceinline__ int schedule_tile(int t, int P, int total, int balanced) {
+  if (!balanced) return t < total ? t : -1;
+  const int rnd = t / P, pos = t - rnd * P;
+  const int s = rnd * P + ((rnd & 1) ? P - 1 - pos : pos);
+  return s < total ? s : -1;
+}
+
 // ---- staged epilogues -------------------------------------------------------------------------
 // The output leaves through shared memory and TMA tensor stores, so global writes are whole lines
 // instead of 32 row fragments per store instruction; a tile aux (scores / addend) arrives the same
@@ -319,10 +331,14 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
   int n = 0;
   int j = 0;
   bool ok = true;
-  for (int t = t_first; t < total_tiles; t += t_stride, ++j) {
+  const int rounded = (total_tiles + t_stride - 1) / t_stride * t_stride;
+  for (int tt = t_first; tt < rounded; tt += t_stride) {
+    const int t = schedule_tile(tt, t_stride, total_tiles, shape.balanced);
+    if (t < 0) continue;
     const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
-    const int acc = j & 1;
-    const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+    const int jj = j++;
+    const int acc = jj & 1;
+    const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
     if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, site)) {
       ok = false;
       break;
@@ -469,7 +485,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages issued and possibly not yet consumed (for draining on abort)
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const int rounded = (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
+      for (int tt = blockIdx.x; tt < rounded && ok; tt += gridDim.x) {
+        const int t = schedule_tile(tt, gridDim.x, total_tiles, shape.balanced);
+        if (t < 0) continue;
         const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -522,11 +541,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int j = 0;
       bool ok = true, issued_any = false;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++j) {
+      const int rounded = (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
+      for (int tt = blockIdx.x; tt < rounded && ok; tt += gridDim.x) {
+        const int t = schedule_tile(tt, gridDim.x, total_tiles, shape.balanced);
+        if (t < 0) continue;
         const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
-        const int acc = j & 1;
-        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        const int jj = j++;
+        const int acc = jj & 1;
+        const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
         if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM_MMA_WAIT)) {
           ok = false;
           break;
@@ -673,7 +696,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += pairs) {
+      const int rounded = (total_tiles + pairs - 1) / pairs * pairs;
+      for (int tt = pair; tt < rounded && ok; tt += pairs) {
+        const int t = schedule_tile(tt, pairs, total_tiles, shape.balanced);
+        if (t < 0) continue;
         const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
         const int row0 = tc.mb * BM + (int)rank * 128;
@@ -726,11 +752,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int j = 0;
       bool ok = true, issued_any = false;
-      for (int t = pair; t < total_tiles && ok; t += pairs, ++j) {
+      const int rounded = (total_tiles + pairs - 1) / pairs * pairs;
+      for (int tt = pair; tt < rounded && ok; tt += pairs) {
+        const int t = schedule_tile(tt, pairs, total_tiles, shape.balanced);
+        if (t < 0) continue;
         const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
-        const int acc = j & 1;
-        const uint32_t acc_phase = (uint32_t)(j >> 1) & 1u;
+        const int jj = j++;
+        const int acc = jj & 1;
+        const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
         if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) {
           ok = false;
           break;
@@ -960,6 +990,15 @@ bool make_epi_tmap(CUtensorMap* map, int mode, const void* ptr, int dtype, int64
   return r == CUDA_SUCCESS;
 }
 
+// Tile order of a persistent launch over `total` tiles on P CTAs (pairs): the balanced snake order
+// for causal k-range products with at most 4 tiles per CTA (the idle tail of uneven k ranges
+// dominates there); index order otherwise (keeps concurrent tiles within few batch rows, L2).
+GemmShape with_schedule(const GemmShape& s, int total, int P) {
+  GemmShape r = s;
+  r.balanced = (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER) && total <= 4 * P ? 1 : 0;
+  return r;
+}
+
 // library-wide epilogue layout of the tensor-core kernels (ulm_set_epilogue_mode)
 static int g_epi_mode = EPI_MODE_WARP;
 
@@ -1003,7 +1042,8 @@ int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const Gemm
   const int total = (int)total64;
   if (total == 0) return ULM_OK;
   const int grid = total < sm_count(dev) ? total : sm_count(dev);
-  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, s, e, m_blocks,
+  const GemmShape sb = with_schedule(s, total, grid);
+  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, sb, e, m_blocks,
                                                                             n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc_gemm_kernel");
   return ULM_OK;
@@ -1046,7 +1086,8 @@ int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const Gem
   if (total == 0) return ULM_OK;
   const int max_pairs = sm_count(dev) / 2;
   const int pairs = total < max_pairs ? total : max_pairs;
-  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, s, e, m_blocks,
+  const GemmShape sb = with_schedule(s, total, pairs);
+  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, sb, e, m_blocks,
                                                                            n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc2_gemm_kernel");
   return ULM_OK;

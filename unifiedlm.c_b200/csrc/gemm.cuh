@@ -26,6 +26,9 @@ enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RE
 struct GemmShape {
   int batches, M, N, K;
   int causal;
+  // set by the tensor-core launch: 1 = causal k-range tiles in decreasing-work order, taken in
+  // snake order (schedule_tile); 0 = index order (batch rows consecutive)
+  int balanced;
 };
 
 struct GemmEpilogue {
@@ -73,8 +76,10 @@ __host__ __device__ inline int nlower_tiles_in_row(int mb, int BM, int BN, int n
   return c < n_blocks ? c : n_blocks;
 }
 
-// Map a linear tile index to (batch, row block, column block, k range). Tiles of one batch row are
-// consecutive (L2 locality); under CAUSAL_KLOWER the longest row blocks come first.
+// Map a linear tile index to (batch, row block, column block, k range). Normally the tiles of one
+// batch row are consecutive (L2 locality; under CAUSAL_KLOWER the longest row blocks first). With
+// s.balanced (causal k ranges only) the index runs over work levels first (the row blocks with the
+// longest k range first), then batch rows, then column blocks: decreasing work (schedule_tile).
 template <int BM, int BN>
 __device__ __forceinline__ TileCoord decode_tile(int t, const GemmShape& s, int m_blocks, int n_blocks,
                                                  int tiles_per_batch) {
@@ -91,6 +96,13 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const GemmShape& s, int 
     }
     c.mb = mb;
     c.nb = i;
+  } else if (s.balanced) {
+    const int per_level = s.batches * n_blocks;
+    const int level = t / per_level;
+    const int rem = t - level * per_level;
+    c.b = rem / n_blocks;
+    c.nb = rem - c.b * n_blocks;
+    c.mb = s.causal == CAUSAL_KLOWER ? m_blocks - 1 - level : level;
   } else {
     c.mb = i / n_blocks;
     c.nb = i - c.mb * n_blocks;
