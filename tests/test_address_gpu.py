@@ -1,6 +1,7 @@
 """The fused addressing prologue (conv -> key GEMM -> relu^2 -> normalise) and its backward against
 the float64 oracle (oracle.memory.prologue, model.py:61-62, 70-72, 79). Bars as elsewhere: 1e-2
-relative with bf16 products, 1e-5 in fp32 mode."""
+relative with bf16 products, 1e-5 in fp32 mode. The largest shape (4096 rows) runs the key-weight
+gradient as a split-K product."""
 import math
 
 import pytest
@@ -19,7 +20,7 @@ def rel(a, b):
 
 
 @pytest.mark.parametrize("precision", ["bf16", "fp32"])
-@pytest.mark.parametrize("shape", [(2, 200, 64, 140), (1, 40, 32, 48), (2, 256, 768, 2048)],
+@pytest.mark.parametrize("shape", [(2, 200, 64, 140), (1, 40, 32, 48), (2, 256, 768, 2048), (4, 1024, 768, 2048)],
                          ids=lambda s: "x".join(map(str, s)))
 def test_address_matches_oracle(precision, shape):
     B, T, D, M = shape

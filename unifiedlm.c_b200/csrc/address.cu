@@ -384,18 +384,22 @@ constexpr int DB_ROWS_PER_CHUNK = 256;
 
 inline int64_t al256(int64_t n) { return (n + 255) / 256 * 256; }
 
-inline int addr_split(int64_t rows) {
-  // split the B*T contraction of dK into S chunks so the product has enough tiles
-  for (int s = 4; s > 1; s /= 2)
-    if (rows % s == 0 && rows / s >= 256) return s;
-  return 1;
+// Split of the B*T contraction of dK = da^T u into S k ranges: enough 256 x 256 tiles to fill the
+// CTA pairs once (S x tiles <= pairs), at most 8, each range at least 1024 rows and none empty.
+inline int addr_split(int64_t rows, int64_t M, int64_t D) {
+  const int dev = current_device();
+  const int pairs = (dev >= 0 ? sm_count(dev) : 148) / 2;
+  const int64_t tiles = cdiv(M, 256) * cdiv(D, 256);
+  int S = (int)std::max<int64_t>(1, std::min<int64_t>(8, pairs / std::max<int64_t>(1, tiles)));
+  while (S > 1 && (rows / S < 1024 || (int64_t)(S - 1) * ksplit_chunk((int)rows, S) >= rows)) --S;
+  return S;
 }
 
 inline AddrBwdWork carve_addr_work(void* base, int64_t B, int64_t T, int64_t D, int64_t M, int op_dt) {
   AddrBwdWork w;
   const int64_t rows = B * T;
   w.ld_m = ulm_operand_ld(M);
-  w.S = addr_split(rows);
+  w.S = addr_split(rows, M, D);
   w.ctas = (int)cdiv(rows, ADDR_ROWS_PER_CTA);
   w.chunks = (int)cdiv(T, CONV_ROWS);
   w.db_chunks = (int)cdiv(rows, DB_ROWS_PER_CHUNK);
@@ -408,7 +412,8 @@ inline AddrBwdWork carve_addr_work(void* base, int64_t B, int64_t T, int64_t D, 
   };
   w.da = take(rows * w.ld_m * (op_dt == ULM_F32 ? 4 : 2));
   w.du = reinterpret_cast<float*>(take(rows * D * 4));
-  w.dk_part = reinterpret_cast<float*>(take((int64_t)w.S * M * D * 4));
+  // sized for the largest split so the byte count does not depend on the device queried
+  w.dk_part = reinterpret_cast<float*>(take((int64_t)8 * M * D * 4));
   w.db_part = reinterpret_cast<float*>(take((int64_t)w.db_chunks * M * 4));
   w.deps_part = reinterpret_cast<float*>(take((int64_t)w.ctas * 4));
   w.dconv_part = reinterpret_cast<float*>(take((int64_t)w.chunks * B * D * CONV_MAXK * 4));
@@ -536,12 +541,12 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   if (int rc = sum_parts(wk.db_part, wk.db_chunks, M, dkey_b, st)) return rc;
   sum_all_kernel<<<1, 256, 0, st>>>(wk.deps_part, wk.ctas, deps);
   ULM_LAUNCH_CHECK("sum_all_kernel");
-  // dK = da^T u, split over S chunks of rows (each chunk a GEMM batch), then summed in order
+  // dK = da^T u, split over S k ranges of rows (split-K product), then the partials summed in order
   {
-    const int64_t rc_rows = rows / wk.S;
-    Operand A{wk.da, wk.ld_m, rc_rows * wk.ld_m, M, rc_rows, dt, true};
-    Operand Bu{u_op, ld_u, rc_rows * ld_u, D, rc_rows, dt, true};
-    GemmShape s{wk.S, (int)M, (int)D, (int)rc_rows, CAUSAL_NONE};
+    Operand A{wk.da, wk.ld_m, rows * wk.ld_m, M, rows, dt, true};
+    Operand Bu{u_op, ld_u, rows * ld_u, D, rows, dt, true};
+    GemmShape s{wk.S, (int)M, (int)D, (int)rows, CAUSAL_NONE};
+    s.ksplit = wk.S;
     GemmEpilogue e = plain_epilogue(EPI_STORE, ULM_F32, wk.dk_part, D, M * D);
     if (int rc = run_gemm(A, Bu, s, e, st)) return rc;
     if (int rc = sum_parts(wk.dk_part, wk.S, M * D, dkey_w, st)) return rc;

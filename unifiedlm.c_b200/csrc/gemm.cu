@@ -418,6 +418,7 @@ struct TcConfig {
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_a2, const __grid_constant__ CUtensorMap tma_b2,
                    const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_aux,
                    const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
                    const int tiles_per_batch, const int total_tiles) {
@@ -464,6 +465,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (shape.K2 > 0) {
+      tma_prefetch_desc(&tma_a2);
+      tma_prefetch_desc(&tma_b2);
+    }
     if (epi.staged != EPI_MODE_DIRECT) {
       tma_prefetch_desc(&tma_out);
       if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
@@ -491,7 +496,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (t < 0) continue;
         const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const int n1 = kb1 - kb0, nkb = n1 + (shape.K2 + TC_BK - 1) / TC_BK;
+        const int ob = shape.ksplit > 1 ? 0 : tc.b;  // operand batch coordinate
+        for (int i = 0; i < nkb; ++i) {
           if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM_PRODUCER_WAIT)) {
             ok = false;
             break;
@@ -499,20 +506,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          const int k0 = kb * TC_BK;
+          // k blocks of the first operand pair, then those of the second (shape.K2)
+          const bool s2 = i >= n1;
+          const CUtensorMap* ma = s2 ? &tma_a2 : &tma_a;
+          const CUtensorMap* mbm = s2 ? &tma_b2 : &tma_b;
+          const int k0 = (s2 ? i - n1 : kb0 + i) * TC_BK;
+          const int oa = s2 ? (shape.a2_batched ? tc.b : 0) : ob;
+          const int obb = s2 ? (shape.b2_batched ? tc.b : 0) : ob;
           if (!A_MN) {
-            tma_load_3d(&tma_a, sa, &full[stage], k0, tc.mb * TC_BM, tc.b);
+            tma_load_3d(ma, sa, &full[stage], k0, tc.mb * TC_BM, oa);
           } else {
 #pragma unroll
             for (int j = 0; j < TC_BM / 64; ++j)
-              tma_load_3d(&tma_a, sa + j * MN_LBO, &full[stage], tc.mb * TC_BM + j * 64, k0, tc.b);
+              tma_load_3d(ma, sa + j * MN_LBO, &full[stage], tc.mb * TC_BM + j * 64, k0, oa);
           }
           if (!B_MN) {
-            tma_load_3d(&tma_b, sb, &full[stage], k0, tc.nb * BN, tc.b);
+            tma_load_3d(mbm, sb, &full[stage], k0, tc.nb * BN, obb);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(&tma_b, sb + j * MN_LBO, &full[stage], tc.nb * BN + j * 64, k0, tc.b);
+              tma_load_3d(mbm, sb + j * MN_LBO, &full[stage], tc.nb * BN + j * 64, k0, obb);
           }
           issued = min(issued + 1, STAGES);
           if (++stage == STAGES) {
@@ -547,6 +560,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (t < 0) continue;
         const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int nkb = kb1 - kb0 + (shape.K2 + TC_BK - 1) / TC_BK;
         const int jj = j++;
         const int acc = jj & 1;
         const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
@@ -556,7 +570,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < nkb; ++i) {
           if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM_MMA_WAIT)) {
             ok = false;
             break;
@@ -568,7 +582,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int kk = 0; kk < TC_BK / 16; ++kk) {
             const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
             const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
-            umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ss(d_tmem, ad, bd, IDESC, (i > 0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(&empty[stage]);  // frees the stage once these MMAs have read it
@@ -626,6 +640,7 @@ struct Tc2Config {
 template <bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                    const __grid_constant__ CUtensorMap tma_a2, const __grid_constant__ CUtensorMap tma_b2,
                     const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_aux,
                     const GemmShape shape, const GemmEpilogue epi, const int m_blocks, const int n_blocks,
                     const int tiles_per_batch, const int total_tiles) {
@@ -674,6 +689,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (shape.K2 > 0) {
+      tma_prefetch_desc(&tma_a2);
+      tma_prefetch_desc(&tma_b2);
+    }
     if (epi.staged != EPI_MODE_DIRECT) {
       tma_prefetch_desc(&tma_out);
       if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
@@ -702,9 +721,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         if (t < 0) continue;
         const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int n1 = kb1 - kb0, nkb = n1 + (shape.K2 + TC_BK - 1) / TC_BK;
+        const int ob = shape.ksplit > 1 ? 0 : tc.b;  // operand batch coordinate
         const int row0 = tc.mb * BM + (int)rank * 128;
         const int col0 = tc.nb * BN + (int)rank * 128;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < nkb; ++i) {
           if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) {
             ok = false;
             break;
@@ -713,18 +734,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
           uint8_t* sb = sa + Cfg::A_BYTES;
           const uint32_t bar = leader_full + (uint32_t)(stage * sizeof(uint64_t));
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
-          const int k0 = kb * TC_BK;
+          // k blocks of the first operand pair, then those of the second (shape.K2)
+          const bool s2 = i >= n1;
+          const CUtensorMap* ma = s2 ? &tma_a2 : &tma_a;
+          const CUtensorMap* mbm = s2 ? &tma_b2 : &tma_b;
+          const int k0 = (s2 ? i - n1 : kb0 + i) * TC_BK;
+          const int oa = s2 ? (shape.a2_batched ? tc.b : 0) : ob;
+          const int obb = s2 ? (shape.b2_batched ? tc.b : 0) : ob;
           if (!A_MN) {
-            tma_load_3d_pair(&tma_a, sa, bar, k0, row0, tc.b);
+            tma_load_3d_pair(ma, sa, bar, k0, row0, oa);
           } else {
-            tma_load_3d_pair(&tma_a, sa, bar, row0, k0, tc.b);
-            tma_load_3d_pair(&tma_a, sa + MN_LBO, bar, row0 + 64, k0, tc.b);
+            tma_load_3d_pair(ma, sa, bar, row0, k0, oa);
+            tma_load_3d_pair(ma, sa + MN_LBO, bar, row0 + 64, k0, oa);
           }
           if (!B_MN) {
-            tma_load_3d_pair(&tma_b, sb, bar, k0, col0, tc.b);
+            tma_load_3d_pair(mbm, sb, bar, k0, col0, obb);
           } else {
-            tma_load_3d_pair(&tma_b, sb, bar, col0, k0, tc.b);
-            tma_load_3d_pair(&tma_b, sb + MN_LBO, bar, col0 + 64, k0, tc.b);
+            tma_load_3d_pair(mbm, sb, bar, col0, k0, obb);
+            tma_load_3d_pair(mbm, sb + MN_LBO, bar, col0 + 64, k0, obb);
           }
           issued = min(issued + 1, STAGES);
           if (++stage == STAGES) {
@@ -758,6 +785,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         if (t < 0) continue;
         const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
         const int kb0 = tc.k_begin / TC_BK, kb1 = (tc.k_end + TC_BK - 1) / TC_BK;
+        const int nkb = kb1 - kb0 + (shape.K2 + TC_BK - 1) / TC_BK;
         const int jj = j++;
         const int acc = jj & 1;
         const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
@@ -767,7 +795,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int i = 0; i < nkb; ++i) {
           if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM2_WAIT)) {
             ok = false;
             break;
@@ -779,7 +807,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
           for (int kk = 0; kk < TC_BK / 16; ++kk) {
             const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
             const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
-            umma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (i > 0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit_pair(&empty[stage], 0x3);  // frees this stage in both CTAs
@@ -820,8 +848,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(256)
     simt_gemm_kernel(const float* __restrict__ A, int64_t lda, int64_t bsA, const float* __restrict__ Bm, int64_t ldb,
-                     int64_t bsB, const GemmShape shape, const GemmEpilogue epi, const int m_blocks,
-                     const int n_blocks, const int tiles_per_batch) {
+                     int64_t bsB, const float* __restrict__ A2, int64_t lda2, int64_t bsA2,
+                     const float* __restrict__ B2, int64_t ldb2, int64_t bsB2, const GemmShape shape,
+                     const GemmEpilogue epi, const int m_blocks, const int n_blocks, const int tiles_per_batch) {
   constexpr int BM = 64, BN = 64, BK = 16;
   __shared__ float As[BK][BM + 1];
   __shared__ float Bs[BK][BN + 1];
@@ -835,13 +864,15 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) acc[i][jj] = 0.f;
 
-  for (int k0 = tc.k_begin; k0 < tc.k_end; k0 += BK) {
+  // the k range of the first operand pair, then all of K2 over the second (when shape.K2 > 0)
+  auto segment = [&](const float* Ap, int64_t la, const float* Bp, int64_t lb, int kbeg, int kend) {
+  for (int k0 = kbeg; k0 < kend; k0 += BK) {
     for (int i = threadIdx.x; i < BM * BK; i += 256) {
       int mm, kk;
       if (A_MN) { kk = i / BM; mm = i % BM; } else { mm = i / BK; kk = i % BK; }
       const int gm = tc.mb * BM + mm, gk = k0 + kk;
       float val = 0.f;
-      if (gm < shape.M && gk < tc.k_end) val = A_MN ? Ab[(int64_t)gk * lda + gm] : Ab[(int64_t)gm * lda + gk];
+      if (gm < shape.M && gk < kend) val = A_MN ? Ap[(int64_t)gk * la + gm] : Ap[(int64_t)gm * la + gk];
       As[kk][mm] = val;
     }
     for (int i = threadIdx.x; i < BN * BK; i += 256) {
@@ -849,7 +880,7 @@ __global__ void __launch_bounds__(256)
       if (B_MN) { kk = i / BN; nn = i % BN; } else { nn = i / BK; kk = i % BK; }
       const int gn = tc.nb * BN + nn, gk = k0 + kk;
       float val = 0.f;
-      if (gn < shape.N && gk < tc.k_end) val = B_MN ? Bb[(int64_t)gk * ldb + gn] : Bb[(int64_t)gn * ldb + gk];
+      if (gn < shape.N && gk < kend) val = B_MN ? Bp[(int64_t)gk * lb + gn] : Bp[(int64_t)gn * lb + gk];
       Bs[kk][nn] = val;
     }
     __syncthreads();
@@ -867,6 +898,11 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
+  };
+  segment(Ab, lda, Bb, ldb, tc.k_begin, tc.k_end);
+  if (shape.K2 > 0)
+    segment(A2 + (shape.a2_batched ? (int64_t)tc.b * bsA2 : 0), lda2, B2 + (shape.b2_batched ? (int64_t)tc.b * bsB2 : 0),
+            ldb2, 0, shape.K2);
   const bool decay = epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG;
   const float g = decay ? *epi.g : 0.f;
   float dg_acc = 0.f;
@@ -1014,14 +1050,28 @@ void prepare_epilogue(GemmEpilogue& e, const GemmShape& s, CUtensorMap* tout, CU
   e.staged = ok ? mode : EPI_MODE_DIRECT;
 }
 
+// Tensor maps of the second operand pair (zeroed and unused without one); a pair member with
+// batch stride 0 is one matrix shared by all batch rows.
+int make_second_pair(CUtensorMap* ta2, CUtensorMap* tb2, const Operand* A2, const Operand* B2, int batches,
+                     uint32_t a_rows, uint32_t b_rows, bool a_mn, bool b_mn) {
+  memset(ta2, 0, sizeof(CUtensorMap));
+  memset(tb2, 0, sizeof(CUtensorMap));
+  if (!A2) return ULM_OK;
+  if (int rc = make_tmap(ta2, *A2, A2->bstride ? batches : 1, 64, a_mn ? 64 : a_rows)) return rc;
+  return make_tmap(tb2, *B2, B2->bstride ? batches : 1, 64, b_mn ? 64 : b_rows);
+}
+
 template <int BN, bool A_MN, bool B_MN>
-int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e_in, cudaStream_t st) {
+int launch_tc(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+              const GemmEpilogue& e_in, cudaStream_t st) {
   using Cfg = TcConfig<BN>;
-  CUtensorMap ta, tb, tout, taux;
-  int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : TC_BM);
+  CUtensorMap ta, tb, ta2, tb2, tout, taux;
+  const int ob = s.ksplit > 1 ? 1 : s.batches;  // split-K operands are not batched
+  int rc = make_tmap(&ta, A, ob, 64, A_MN ? 64 : TC_BM);
   if (rc) return rc;
-  rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : BN);
+  rc = make_tmap(&tb, B, ob, 64, B_MN ? 64 : BN);
   if (rc) return rc;
+  if ((rc = make_second_pair(&ta2, &tb2, A2, B2, s.batches, TC_BM, BN, A_MN, B_MN))) return rc;
   GemmEpilogue e = e_in;
   prepare_epilogue(e, s, &tout, &taux);
   const int dev = current_device();
@@ -1043,28 +1093,32 @@ int launch_tc(const Operand& A, const Operand& B, const GemmShape& s, const Gemm
   if (total == 0) return ULM_OK;
   const int grid = total < sm_count(dev) ? total : sm_count(dev);
   const GemmShape sb = with_schedule(s, total, grid);
-  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, sb, e, m_blocks,
-                                                                            n_blocks, tpb, total);
+  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, ta2, tb2, tout, taux, sb, e,
+                                                                            m_blocks, n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc_gemm_kernel");
   return ULM_OK;
 }
 
 template <int BN>
-int dispatch_tc_major(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
-  if (!A.mn_major && !B.mn_major) return launch_tc<BN, false, false>(A, B, s, e, st);
-  if (!A.mn_major && B.mn_major) return launch_tc<BN, false, true>(A, B, s, e, st);
-  if (A.mn_major && !B.mn_major) return launch_tc<BN, true, false>(A, B, s, e, st);
-  return launch_tc<BN, true, true>(A, B, s, e, st);
+int dispatch_tc_major(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+                      const GemmEpilogue& e, cudaStream_t st) {
+  if (!A.mn_major && !B.mn_major) return launch_tc<BN, false, false>(A, B, A2, B2, s, e, st);
+  if (!A.mn_major && B.mn_major) return launch_tc<BN, false, true>(A, B, A2, B2, s, e, st);
+  if (A.mn_major && !B.mn_major) return launch_tc<BN, true, false>(A, B, A2, B2, s, e, st);
+  return launch_tc<BN, true, true>(A, B, A2, B2, s, e, st);
 }
 
 template <bool A_MN, bool B_MN>
-int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e_in, cudaStream_t st) {
+int launch_tc2(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+               const GemmEpilogue& e_in, cudaStream_t st) {
   using Cfg = Tc2Config;
-  CUtensorMap ta, tb, tout, taux;
-  int rc = make_tmap(&ta, A, s.batches, 64, A_MN ? 64 : 128);
+  CUtensorMap ta, tb, ta2, tb2, tout, taux;
+  const int ob = s.ksplit > 1 ? 1 : s.batches;  // split-K operands are not batched
+  int rc = make_tmap(&ta, A, ob, 64, A_MN ? 64 : 128);
   if (rc) return rc;
-  rc = make_tmap(&tb, B, s.batches, 64, B_MN ? 64 : 128);
+  rc = make_tmap(&tb, B, ob, 64, B_MN ? 64 : 128);
   if (rc) return rc;
+  if ((rc = make_second_pair(&ta2, &tb2, A2, B2, s.batches, 128, 128, A_MN, B_MN))) return rc;
   GemmEpilogue e = e_in;
   prepare_epilogue(e, s, &tout, &taux);
   const int dev = current_device();
@@ -1087,36 +1141,61 @@ int launch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const Gem
   const int max_pairs = sm_count(dev) / 2;
   const int pairs = total < max_pairs ? total : max_pairs;
   const GemmShape sb = with_schedule(s, total, pairs);
-  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tout, taux, sb, e, m_blocks,
-                                                                           n_blocks, tpb, total);
+  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, ta2, tb2, tout, taux, sb, e,
+                                                                           m_blocks, n_blocks, tpb, total);
   ULM_LAUNCH_CHECK("tc2_gemm_kernel");
   return ULM_OK;
 }
 
-int dispatch_tc2(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
-  if (!A.mn_major && !B.mn_major) return launch_tc2<false, false>(A, B, s, e, st);
-  if (!A.mn_major && B.mn_major) return launch_tc2<false, true>(A, B, s, e, st);
-  if (A.mn_major && !B.mn_major) return launch_tc2<true, false>(A, B, s, e, st);
-  return launch_tc2<true, true>(A, B, s, e, st);
+int dispatch_tc2(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+                 const GemmEpilogue& e, cudaStream_t st) {
+  if (!A.mn_major && !B.mn_major) return launch_tc2<false, false>(A, B, A2, B2, s, e, st);
+  if (!A.mn_major && B.mn_major) return launch_tc2<false, true>(A, B, A2, B2, s, e, st);
+  if (A.mn_major && !B.mn_major) return launch_tc2<true, false>(A, B, A2, B2, s, e, st);
+  return launch_tc2<true, true>(A, B, A2, B2, s, e, st);
 }
 
 template <bool A_MN, bool B_MN>
-int launch_simt(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t st) {
+int launch_simt(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+                const GemmEpilogue& e, cudaStream_t st) {
   const int m_blocks = (int)cdiv(s.M, 64), n_blocks = (int)cdiv(s.N, 64);
   const int tpb = tiles_per_batch_host(s, 64, 64, m_blocks, n_blocks);
   const int64_t total = (int64_t)tpb * s.batches;
   ULM_REQUIRE(total < (1ll << 31), "too many tiles (%lld)", (long long)total);
   if (total == 0) return ULM_OK;
+  const bool split = s.ksplit > 1;  // split-K operands are not batched
   simt_gemm_kernel<A_MN, B_MN><<<(unsigned)total, 256, 0, st>>>(
-      static_cast<const float*>(A.ptr), A.ld, A.bstride, static_cast<const float*>(B.ptr), B.ld, B.bstride, s, e,
-      m_blocks, n_blocks, tpb);
+      static_cast<const float*>(A.ptr), A.ld, split ? 0 : A.bstride, static_cast<const float*>(B.ptr), B.ld,
+      split ? 0 : B.bstride, A2 ? static_cast<const float*>(A2->ptr) : nullptr, A2 ? A2->ld : 0,
+      A2 ? A2->bstride : 0, B2 ? static_cast<const float*>(B2->ptr) : nullptr, B2 ? B2->ld : 0,
+      B2 ? B2->bstride : 0, s, e, m_blocks, n_blocks, tpb);
   ULM_LAUNCH_CHECK("simt_gemm_kernel");
   return ULM_OK;
 }
 
 }  // namespace
 
-int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream) {
+int run_gemm2(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s_in,
+              const GemmEpilogue& e, cudaStream_t stream) {
+  GemmShape s = s_in;
+  if (!A2 || !B2 || s.K2 <= 0) {
+    A2 = B2 = nullptr;
+    s.K2 = 0;
+  } else {
+    ULM_REQUIRE(A2->ptr && B2->ptr, "null second operand");
+    ULM_REQUIRE(A2->dtype == A.dtype && B2->dtype == B.dtype, "the second operand pair must have the first's type");
+    ULM_REQUIRE(A2->mn_major == A.mn_major && B2->mn_major == B.mn_major,
+                "the second operand pair must have the first's storage orders");
+    ULM_REQUIRE(s.ksplit <= 1, "split K with a second operand pair is not supported");
+    s.a2_batched = A2->bstride != 0;
+    s.b2_batched = B2->bstride != 0;
+    if (A2->dtype == ULM_BF16) {
+      ULM_REQUIRE(is_aligned16(A2->ptr) && is_aligned16(B2->ptr), "bf16 operands must be 16-byte aligned");
+      ULM_REQUIRE(A2->ld % 8 == 0 && B2->ld % 8 == 0 && A2->bstride % 8 == 0 && B2->bstride % 8 == 0,
+                  "bf16 operand strides must be multiples of 8 elements");
+      ULM_REQUIRE(A2->ld >= A2->inner && B2->ld >= B2->inner, "row stride shorter than the row");
+    }
+  }
   ULM_REQUIRE(A.ptr && B.ptr && e.out, "null operand or output pointer");
   ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
   ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
@@ -1128,6 +1207,9 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
   ULM_REQUIRE(e.kind != EPI_STORE_ADD || (e.aux && e.out_dtype == ULM_F32), "EPI_STORE_ADD needs an fp32 aux");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
     ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
+  ULM_REQUIRE(s.ksplit <= 1 || (s.causal == CAUSAL_NONE && s.ksplit == s.batches &&
+                                 (int64_t)(s.ksplit - 1) * ksplit_chunk(s.K, s.ksplit) < s.K),
+              "split K needs a non-causal product, batches == ksplit and no empty k range");
   if (s.batches == 0 || s.M == 0 || s.N == 0) return ULM_OK;
   ULM_REQUIRE(s.K > 0, "empty contraction");
   if (A.dtype == ULM_BF16) {
@@ -1136,15 +1218,19 @@ int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmE
                 "bf16 operand strides must be multiples of 8 elements (lda=%lld ldb=%lld)", (long long)A.ld,
                 (long long)B.ld);
     ULM_REQUIRE(A.ld >= A.inner && B.ld >= B.inner, "row stride shorter than the row");
-    if (s.N >= 256 && s.M >= 256 && g_gemm_pairs) return dispatch_tc2(A, B, s, e, stream);
-    if (s.N >= 256) return dispatch_tc_major<256>(A, B, s, e, stream);
-    return dispatch_tc_major<128>(A, B, s, e, stream);
+    if (s.N >= 256 && s.M >= 256 && g_gemm_pairs) return dispatch_tc2(A, B, A2, B2, s, e, stream);
+    if (s.N >= 256) return dispatch_tc_major<256>(A, B, A2, B2, s, e, stream);
+    return dispatch_tc_major<128>(A, B, A2, B2, s, e, stream);
   }
   ULM_REQUIRE(A.dtype == ULM_F32, "operands must be bf16 or fp32");
-  if (!A.mn_major && !B.mn_major) return launch_simt<false, false>(A, B, s, e, stream);
-  if (!A.mn_major && B.mn_major) return launch_simt<false, true>(A, B, s, e, stream);
-  if (A.mn_major && !B.mn_major) return launch_simt<true, false>(A, B, s, e, stream);
-  return launch_simt<true, true>(A, B, s, e, stream);
+  if (!A.mn_major && !B.mn_major) return launch_simt<false, false>(A, B, A2, B2, s, e, stream);
+  if (!A.mn_major && B.mn_major) return launch_simt<false, true>(A, B, A2, B2, s, e, stream);
+  if (A.mn_major && !B.mn_major) return launch_simt<true, false>(A, B, A2, B2, s, e, stream);
+  return launch_simt<true, true>(A, B, A2, B2, s, e, stream);
+}
+
+int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream) {
+  return run_gemm2(A, B, nullptr, nullptr, s, e, stream);
 }
 
 }  // namespace ulm

@@ -29,7 +29,17 @@ struct GemmShape {
   // set by the tensor-core launch: 1 = causal k-range tiles in decreasing-work order, taken in
   // snake order (schedule_tile); 0 = index order (batch rows consecutive)
   int balanced;
+  // > 1: split-K product. The operands are single (not batched); "batch" b = 0 .. ksplit - 1 of the
+  // output takes the k range [b * kc, min(K, (b + 1) * kc)), kc = K / ksplit rounded up to 64.
+  // ksplit must equal batches. The caller sums the partial outputs.
+  int ksplit;
+  // second operand pair (run_gemm2): K2 more k steps after the first pair's range, over A2 / B2;
+  // a2_batched / b2_batched (set by run_gemm2) say whether they have a batch stride
+  int K2;
+  int a2_batched, b2_batched;
 };
+
+__host__ __device__ inline int ksplit_chunk(int K, int ksplit) { return ((K + ksplit - 1) / ksplit + 63) / 64 * 64; }
 
 struct GemmEpilogue {
   int kind;            // EPI_STORE / EPI_DECAY
@@ -112,6 +122,11 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const GemmShape& s, int 
   c.k_end = s.K;
   if (s.causal == CAUSAL_KLOWER) c.k_end = min(s.K, (c.mb + 1) * BM);
   if (s.causal == CAUSAL_KUPPER) c.k_begin = min(s.K, c.mb * BM);
+  if (s.ksplit > 1) {
+    const int kc = ksplit_chunk(s.K, s.ksplit);
+    c.k_begin = min(s.K, c.b * kc);
+    c.k_end = min(s.K, c.k_begin + kc);
+  }
   return c;
 }
 
@@ -130,5 +145,10 @@ inline int64_t decay_dg_partials(int64_t batches, int64_t T) {
 
 // Host entry: validates, picks the back end from the operand types, launches on `stream`.
 int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream);
+
+// C = A B^T (over A's k range) + A2 B2^T (over K2), one accumulator: the second pair has the first
+// pair's element type and storage orders; a member with batch stride 0 is shared by all batch rows.
+int run_gemm2(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,
+              const GemmEpilogue& e, cudaStream_t stream);
 
 }  // namespace ulm
