@@ -245,6 +245,22 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_saddr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_saddr) : "memory");
 }
 
+// Split cluster barrier: every thread arrives (release) early and waits (acquire) later.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Store one float into a shared-memory word of another CTA of the cluster (both addresses from
+// mapa), completing 4 bytes of transaction count on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_f32(uint32_t remote_saddr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote_saddr),
+               "r"(__float_as_uint(v)), "r"(remote_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

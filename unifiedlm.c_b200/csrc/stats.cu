@@ -45,6 +45,9 @@ __device__ __forceinline__ void fill_row_scales(float* sinv, const float* __rest
   }
 }
 
+// largest cluster of the TMA-staged scans (CTAs along T)
+constexpr int SCAN_MAX_CLUSTER = 8;
+
 // kernel.py:109-136: k_t = r_{t-1}, c_t = w + sum_{s<=t} lam^(t-s) k_s, q_t = r_t / c_t
 template <typename OpT>
 __global__ void __launch_bounds__(STATS_THREADS)
@@ -219,8 +222,9 @@ __global__ void __launch_bounds__(32 * WARPS)
   // the read address of position cta_t0 + i - 1 (R rows in one box, the last row in a second)
   extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t xbar;  // completes when the lower ranks' totals have arrived
   __shared__ float warp_sum[WARPS][32];
-  __shared__ float cta_total[32];
+  __shared__ float ctot[SCAN_MAX_CLUSTER][32];  // ctot[j]: CTA total of rank j < this rank
   __shared__ float sinv[R + 1];  // row scales of the tile's rows
   __shared__ int ok_flag;
   cg::cluster_group cluster = cg::this_cluster();
@@ -233,14 +237,18 @@ __global__ void __launch_bounds__(32 * WARPS)
   const int cta_t0 = cr * R;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
+    mbar_init(&xbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&xbar, (uint32_t)cr * 32u * 4u);
     mbar_arrive_expect_tx(&bar, (R + 1) * 32u * 4u);
     tma_load_3d(&map_r, tile, &bar, m0, cta_t0 - 1, b);
     tma_load_3d(&map_r1, tile + R * 32, &bar, m0, cta_t0 + R - 1, b);
   }
+  // the barriers of every CTA are initialised before any CTA sends into them (wait below)
+  cluster_arrive_release();
   fill_row_scales(sinv, den, b, T, cta_t0 - 1, R);  // overlaps the tile load
   if (threadIdx.x == 0) ok_flag = 1;
   __syncthreads();
@@ -262,15 +270,18 @@ __global__ void __launch_bounds__(32 * WARPS)
   warp_sum[wp][lane] = run;
   __syncthreads();
   const float lam_seg = expf(gg * (float)SEG);
+  cluster_wait_acquire();
   if (wp == 0) {
+    // this CTA's total goes straight into the shared memory of every higher rank
     float tot = 0.f;
     for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
-    cta_total[lane] = tot;
+    const uint32_t slot = smem_u32(&ctot[cr][lane]), xb = smem_u32(&xbar);
+    for (int j = cr + 1; j < C; ++j) st_async_f32(mapa_shared(slot, j), tot, mapa_shared(xb, j));
   }
-  cluster.sync();
   const float lam_cta = expf(gg * (float)R);
   float carry = 0.f;
-  for (int j = 0; j < cr; ++j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  if (cr > 0 && !mbar_wait_bounded(&xbar, 0)) raise_device_error(DEVERR_SCAN_TMA_WAIT);
+  for (int j = 0; j < cr; ++j) carry = fmaf(carry, lam_cta, ctot[j][lane]);
   for (int j = 0; j < wp; ++j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
   if (ok && m < M) {
     const float wm = w[m];
@@ -296,7 +307,6 @@ __global__ void __launch_bounds__(32 * WARPS)
       kk = rv;
     }
   }
-  cluster.sync();
 }
 
 // RECOMPUTE: instead of reading the saved q and c (two fp32 arrays), rebuild them from the r tile
@@ -318,8 +328,10 @@ __global__ void __launch_bounds__(32 * WARPS)
   __shared__ __align__(8) uint64_t bar;
   __shared__ float warp_sum[WARPS][32];
   __shared__ float warp_dw[WARPS][32];
-  __shared__ float cta_total_f[32];
-  __shared__ float cta_total[32];
+  __shared__ __align__(8) uint64_t xbar_f;  // lower ranks' forward totals have arrived (recompute)
+  __shared__ __align__(8) uint64_t xbar_r;  // higher ranks' reverse totals have arrived
+  __shared__ float ctot_f[SCAN_MAX_CLUSTER][32];
+  __shared__ float ctot_r[SCAN_MAX_CLUSTER][32];
   __shared__ double red_dg[32 * WARPS];
   __shared__ float sinv[R + 1];  // row scales of the r tile's rows cta_t0 - 1 .. cta_t0 + R - 1
   __shared__ int ok_flag;
@@ -338,10 +350,14 @@ __global__ void __launch_bounds__(32 * WARPS)
   float* t_dqo = t_x + (RECOMPUTE ? R + 1 : 3 * R) * 32;
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
+    mbar_init(&xbar_f, 1);
+    mbar_init(&xbar_r, 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&xbar_f, RECOMPUTE ? (uint32_t)cr * 128u : 0u);
+    mbar_arrive_expect_tx(&xbar_r, (uint32_t)(C - 1 - cr) * 128u);
     const uint32_t bytes = ((has_dqo ? 3u : 2u) * TILE + (RECOMPUTE ? (uint32_t)(R + 1) * 32u : 3u * TILE)) * 4u;
     mbar_arrive_expect_tx(&bar, bytes);
     tma_load_3d(&map_dqf, t_dqf, &bar, m0, cta_t0, b);
@@ -356,6 +372,8 @@ __global__ void __launch_bounds__(32 * WARPS)
     }
     ok_flag = 1;
   }
+  // the barriers of every CTA are initialised before any CTA sends into them (wait below)
+  cluster_arrive_release();
   fill_row_scales(sinv, den, b, T, cta_t0 - 1, R);  // overlaps the tile loads
   __syncthreads();
   if (!mbar_wait_bounded(&bar, 0)) {
@@ -391,15 +409,19 @@ __global__ void __launch_bounds__(32 * WARPS)
     }
     warp_sum[wp][lane] = run;
     __syncthreads();
+    cluster_wait_acquire();
     if (wp == 0) {
       float tot = 0.f;
       for (int j = 0; j < WARPS; ++j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
-      cta_total_f[lane] = tot;
+      const uint32_t slot = smem_u32(&ctot_f[cr][lane]), xb = smem_u32(&xbar_f);
+      for (int j = cr + 1; j < C; ++j) st_async_f32(mapa_shared(slot, j), tot, mapa_shared(xb, j));
     }
-    cluster.sync();
-    for (int j = 0; j < cr; ++j) n_carry = fmaf(n_carry, lam_cta, *cluster.map_shared_rank(&cta_total_f[lane], j));
+    if (cr > 0 && !mbar_wait_bounded(&xbar_f, 0)) raise_device_error(DEVERR_SCAN_TMA_WAIT);
+    for (int j = 0; j < cr; ++j) n_carry = fmaf(n_carry, lam_cta, ctot_f[j][lane]);
     for (int j = 0; j < wp; ++j) n_carry = fmaf(n_carry, lam_seg, warp_sum[j][lane]);
     __syncthreads();  // warp_sum is reused below
+  } else {
+    cluster_wait_acquire();
   }
 
   float dw_acc = 0.f, dg_f = 0.f, run = 0.f;
@@ -447,13 +469,15 @@ __global__ void __launch_bounds__(32 * WARPS)
   warp_dw[wp][lane] = dw_acc;
   __syncthreads();
   if (wp == 0) {
+    // this CTA's reverse total goes into the shared memory of every lower rank
     float tot = 0.f;
     for (int j = WARPS - 1; j >= 0; --j) tot = fmaf(tot, lam_seg, warp_sum[j][lane]);
-    cta_total[lane] = tot;
+    const uint32_t slot = smem_u32(&ctot_r[cr][lane]), xb = smem_u32(&xbar_r);
+    for (int j = 0; j < cr; ++j) st_async_f32(mapa_shared(slot, j), tot, mapa_shared(xb, j));
   }
-  cluster.sync();
+  if (cr < C - 1 && !mbar_wait_bounded(&xbar_r, 0)) raise_device_error(DEVERR_SCAN_TMA_WAIT);
   float carry = 0.f;  // dkc at position t0 + SEG
-  for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, *cluster.map_shared_rank(&cta_total[lane], j));
+  for (int j = C - 1; j > cr; --j) carry = fmaf(carry, lam_cta, ctot_r[j][lane]);
   for (int j = WARPS - 1; j > wp; --j) carry = fmaf(carry, lam_seg, warp_sum[j][lane]);
   double dg_acc = (double)dg_f;
   if (ok && valid) {
@@ -492,7 +516,6 @@ __global__ void __launch_bounds__(32 * WARPS)
     __syncthreads();
   }
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
-  cluster.sync();
 }
 
 // 3-D map over an fp32 (B, T, M) array with a 32-slot x `rows` box, no swizzle.
