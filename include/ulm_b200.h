@@ -19,6 +19,7 @@
  *   kernel.py:23-48,
  *   kernel.py:75-101   _la_state / _la_out (apply scores)     -> ulm_causal_apply
  *   model.py:61-79     conv + UnifiedBlock.code (address)     -> ulm_address_fwd, ulm_address_bwd
+ *   model.py:84-85     unified_memory + mu(q w) + residual    -> ulm_memory_combine_fwd, _bwd
  *   model.py:88-111,   UnifiedBlock.init_state / step, and
  *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
  */
@@ -171,6 +172,33 @@ int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const f
                    const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
                    float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T, int64_t M, int64_t D,
                    int prec, void* stream);
+
+/* ---- the block's combine fused into the fast memory (model.py:84-85) ------------------------- */
+
+/* y = x + mu(q * w) + fast, (q, fast) = unified_memory(r, v, g, w): UnifiedBlock.forward's last
+ * line (model.py:85, dropout off) with the combine's product mu(q w) accumulated in the same
+ * tensor-core tiles as the fast read. Inputs as ulm_memory_fwd plus mu (D,M) fp32 (the `mu`
+ * Linear's weight) and x (B,T,D) of x_dtype; y (B,T,D) of x_dtype. q (B,T,M) fp32 may be NULL when
+ * c is NULL (the fp32 copy of q is then not written). Saved / scratch as ulm_memory_fwd plus wmu
+ * (M, ulm_operand_ld(D)) in the operand type. */
+int ulm_memory_combine_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g,
+                           const float* w, const float* mu, const void* x, int x_dtype, void* y, float* q, float* c,
+                           void* qop, void* kop, void* vop, void* P, void* wmu, int64_t B, int64_t T, int64_t M,
+                           int64_t D, int prec, void* stream);
+
+/* Backward of ulm_memory_combine_fwd from dy (B,T,D) of dy_dtype (dx = dy is the caller's). Saved
+ * tensors and workspaces as ulm_memory_bwd plus mw (D, ulm_operand_ld(M)) in the operand type and
+ * gpart of ulm_combine_grad_scratch bytes. Outputs: dr (B,T,M) fp32 (gradient of the normalised
+ * addresses), dv (B,T,D) of dv_dtype, dg (1,), dw (M,) (both the statistics' and the combine's
+ * share), dmu (D,M) fp32. */
+int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float* r, const float* den, const float* g,
+                           const float* w, const float* mu, const float* q, const float* c, const void* qop,
+                           const void* kop, const void* vop, const void* P, void* doop, void* dS, void* mw,
+                           float* dqf, float* dk, void* partial, float* gpart, float* dr, void* dv, int dv_dtype,
+                           float* dg, float* dw, float* dmu, int64_t B, int64_t T, int64_t M, int64_t D, int prec,
+                           void* stream);
+
+int64_t ulm_combine_grad_scratch(int64_t B, int64_t T, int64_t M, int64_t D);
 
 /* ---- the addressing prologue (model.py:61-62, 70-72, 79) -------------------------------------- */
 

@@ -35,6 +35,10 @@ SIGNATURES = {
     "ulm_set_epilogue_mode": (_I, [_I]),
     "ulm_memory_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_bwd": (_I, [_P, _P, _I] + [_P] * 19 + [_I64, _I64, _I64, _I64, _I, _P]),
+    "ulm_memory_combine_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P,
+                                    _I64, _I64, _I64, _I64, _I, _P]),
+    "ulm_memory_combine_bwd": (_I, [_P, _I] + [_P] * 20 + [_I, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "ulm_combine_grad_scratch": (_I64, [_I64, _I64, _I64, _I64]),
     "ulm_address_fwd": (_I, [_P, _I, _P, _I64, _P, _I64, _P, _P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _I64, _I64,
                              _I, _P]),
     "ulm_address_fwd_work_bytes": (_I64, [_I64, _I64, _I64]),

@@ -17,7 +17,8 @@ from typing import Optional
 
 import torch
 
-from .kernel import PRECISION, memory_bwd_raw, memory_fwd_fake, memory_fwd_raw
+from .kernel import (PRECISION, combine_bwd_raw, combine_fwd_fake, combine_fwd_raw, memory_bwd_raw, memory_fwd_fake,
+                     memory_fwd_raw)
 from .prologue import address_bwd_fake, address_bwd_raw, address_fwd_fake, address_fwd_raw
 
 _OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
@@ -102,3 +103,86 @@ def addressed_memory(h, conv_weight, key_weight, key_bias, eps, v, g, w, precisi
                                                      eps.float().reshape(()), vv.contiguous(), g.float().reshape(()),
                                                      w.float().contiguous(), PRECISION[precision])
     return q, fast.to(out_dtype)
+
+
+# ---- the whole mixing span of UnifiedBlock.forward with the combine fused (model.py:79-85) -------
+
+_MIX_OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                 torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]
+
+
+@torch.library.custom_op("ulm::mixer_fwd", mutates_args=())
+def mixer_fwd(x: torch.Tensor, h: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Tensor, key_b: torch.Tensor,
+              eps: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tensor, mu: torch.Tensor,
+              precision: int) -> _MIX_OUT:
+    """Returns (y, z, den, u_op, kw_op, q, c, qop, kop, vop, P); all but y are saved for the backward."""
+    z, den, u_op, kw = address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=False)
+    y, q, c, qop, kop, vop, P = combine_fwd_raw(z, den, v, g, w, mu, x, precision)
+    return y, z, den, u_op, kw, q, c, qop, kop, vop, P
+
+
+@mixer_fwd.register_fake
+def _mixer_fwd_fake(x, h, conv_w, key_w, key_b, eps, v, g, w, mu, precision):
+    z, den, u_op, kw = address_fwd_fake(h, key_w, precision)
+    y, q, c, qop, kop, vop, P = combine_fwd_fake(z, v, x, precision)
+    return y, z, den, u_op, kw, q, c, qop, kop, vop, P
+
+
+@torch.library.custom_op("ulm::mixer_bwd", mutates_args=())
+def mixer_bwd(dy: torch.Tensor, h: torch.Tensor, conv_w: torch.Tensor, g: torch.Tensor, w: torch.Tensor,
+              mu: torch.Tensor, z: torch.Tensor, den: torch.Tensor, u_op: torch.Tensor, kw: torch.Tensor,
+              q: torch.Tensor, c: torch.Tensor, qop: torch.Tensor, kop: torch.Tensor, vop: torch.Tensor,
+              P: torch.Tensor, v_dtype: torch.dtype, precision: int
+              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                         torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dh fp32, dconv_w, dkey_w, dkey_b, deps, dv, dg, dw, dmu)."""
+    dr, dv, dg, dw, dmu = combine_bwd_raw(dy, z, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, precision)
+    dh, dconv, dkw, dkb, deps = address_bwd_raw(dr, z, den, u_op, kw, h, conv_w, precision, normalized=False)
+    return dh, dconv, dkw, dkb, deps, dv, dg, dw, dmu
+
+
+@mixer_bwd.register_fake
+def _mixer_bwd_fake(dy, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, v_dtype, precision):
+    dh, dconv, dkw, dkb, deps = address_bwd_fake(h, z, conv_w)
+    M = z.shape[-1]
+    return (dh, dconv, dkw, dkb, deps, dy.new_empty(dy.shape, dtype=v_dtype), z.new_empty((), dtype=torch.float32),
+            z.new_empty(M, dtype=torch.float32), z.new_empty(mu.shape, dtype=torch.float32))
+
+
+def _mix_setup(ctx, inputs, output):
+    x, h, conv_w, key_w, key_b, eps, v, g, w, mu, precision = inputs
+    y, z, den, u_op, kw, q, c, qop, kop, vop, P = output
+    ctx.save_for_backward(h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P)
+    ctx.precision = precision
+    ctx.dtypes = (x.dtype, h.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype, v.dtype, mu.dtype)
+    ctx.g_shape = g.shape
+    ctx.mark_non_differentiable(z, den, u_op, kw, q, c, qop, kop, vop, P)
+
+
+def _mix_backward(ctx, dy, *unused):
+    h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P = ctx.saved_tensors
+    xd, hd, cd, kd, bd, ed, vd, md = ctx.dtypes
+    dh, dconv, dkw, dkb, deps, dv, dg, dw, dmu = mixer_bwd(dy.contiguous(), h, conv_w, g, w, mu, z, den, u_op, kw, q,
+                                                           c, qop, kop, vop, P, vd, ctx.precision)
+    return (dy, dh.to(hd), dconv.to(cd), dkw.to(kd), dkb.to(bd), deps.to(ed), dv, dg.reshape(ctx.g_shape), dw,
+            dmu.to(md), None)
+
+
+torch.library.register_autograd("ulm::mixer_fwd", _mix_backward, setup_context=_mix_setup)
+
+
+def block_mixer(x, h, conv_weight, key_weight, key_bias, eps, v, g, w, mu_weight, precision="bf16"):
+    """UnifiedBlock.forward's output without dropout (model.py:79-85):
+    y = x + mu((q w)) + fast, (q, fast) = unified_memory(address(h, ...), v, g, w), in x's dtype,
+    with the combine's product accumulated in the fast read's tiles and its gradient in the dq
+    product's. mu_weight: the `mu` Linear's weight (D, M)."""
+    for t in (x, h, v, g, w, mu_weight):
+        if not t.is_cuda:
+            raise RuntimeError("block_mixer runs on CUDA tensors only (no CPU path)")
+    xx = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+    hh = h if h.dtype in (torch.float32, torch.bfloat16) else h.float()
+    vv = v if v.dtype in (torch.float32, torch.bfloat16) else v.float()
+    y, *_ = torch.ops.ulm.mixer_fwd(xx.contiguous(), hh.contiguous(), conv_weight, key_weight, key_bias,
+                                    eps.float().reshape(()), vv.contiguous(), g.float().reshape(()),
+                                    w.float().contiguous(), mu_weight.float().contiguous(), PRECISION[precision])
+    return y.to(x.dtype)

@@ -922,8 +922,11 @@ __global__ void __launch_bounds__(256)
         dg_acc = fmaf((float)(row - col) * p, v, dg_acc);
       }
       if (decay) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
-      if (epi.kind == EPI_STORE_ADD)
-        v += reinterpret_cast<const float*>(epi.aux)[(int64_t)tc.b * epi.aux_bstride + (int64_t)row * epi.ld_aux + col];
+      if (epi.kind == EPI_STORE_ADD) {
+        const int64_t ai = (int64_t)tc.b * epi.aux_bstride + (int64_t)row * epi.ld_aux + col;
+        v += epi.out_dtype == ULM_F32 ? reinterpret_cast<const float*>(epi.aux)[ai]
+                                      : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.aux)[ai]);
+      }
       if (epi.kind == EPI_RELU2) {
         const float a = v + reinterpret_cast<const float*>(epi.aux)[col];
         v = a > 0.f ? a * a : 0.f;
@@ -1204,7 +1207,7 @@ int run_gemm2(const Operand& A, const Operand& B, const Operand* A2, const Opera
               "decay epilogue needs g");
   ULM_REQUIRE(e.kind != EPI_RELU2 || e.aux, "EPI_RELU2 needs the bias");
   ULM_REQUIRE(e.kind != EPI_DECAY_DG || (e.aux && e.tile_partial), "EPI_DECAY_DG needs aux and tile_partial");
-  ULM_REQUIRE(e.kind != EPI_STORE_ADD || (e.aux && e.out_dtype == ULM_F32), "EPI_STORE_ADD needs an fp32 aux");
+  ULM_REQUIRE(e.kind != EPI_STORE_ADD || e.aux, "EPI_STORE_ADD needs the addend (in the output's type)");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
     ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
   ULM_REQUIRE(s.ksplit <= 1 || (s.causal == CAUSAL_NONE && s.ksplit == s.batches &&

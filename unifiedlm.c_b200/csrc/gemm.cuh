@@ -49,7 +49,7 @@ struct GemmEpilogue {
   int64_t out_bstride; // batch stride of the output, elements
   const float* g;      // log decay (device scalar), EPI_DECAY / EPI_DECAY_DG
   int vec_ok;          // output and aux rows are 16-byte aligned for every tile (set by the host)
-  // EPI_STORE_ADD: out = acc + aux (aux fp32, same layout as the fp32 output).
+  // EPI_STORE_ADD: out = acc + aux (aux in the output's type and layout).
   // EPI_RELU2: out = relu(acc + bias[n])^2, bias = aux (fp32, one value per output column).
   // EPI_DECAY_DG: aux = the forward's decayed scores P (same layout and type as the output); each
   // epilogue warp adds sum (m-n) * P[m][n] * acc[m][n] over its part of a tile and writes it to its

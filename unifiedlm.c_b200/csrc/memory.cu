@@ -149,6 +149,65 @@ int convert_rows(const void* src, int sdt, int64_t lds, void* dst, int ddt, int6
   return ULM_OK;
 }
 
+// wmu[m][d] = w[m] * mu[d][m] (the combine's weight as the second B operand of the read product,
+// MN-major over d) in the operand type, rows padded to ld
+__global__ void combine_weight_t_kernel(const float* __restrict__ mu, const float* __restrict__ w,
+                                        void* __restrict__ out, int dt, int64_t ld, int D, int M) {
+  __shared__ float tile[32][33];
+  const int m0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
+  for (int i = ty; i < 32; i += 8) {
+    const int d = d0 + i, m = m0 + tx;
+    tile[i][tx] = (d < D && m < M) ? mu[(int64_t)d * M + m] * w[m] : 0.f;
+  }
+  __syncthreads();
+  for (int i = ty; i < 32; i += 8) {
+    const int m = m0 + i, d = d0 + tx;
+    if (m < M && d < D) {
+      const float v = tile[tx][i];
+      if (dt == ULM_F32)
+        static_cast<float*>(out)[(int64_t)m * ld + d] = v;
+      else
+        static_cast<__nv_bfloat16*>(out)[(int64_t)m * ld + d] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// mw[d][m] = mu[d][m] * w[m] (the combine's weight as the second B operand of the dq product,
+// MN-major over m) in the operand type, rows padded to ld
+__global__ void combine_weight_kernel(const float* __restrict__ mu, const float* __restrict__ w,
+                                      void* __restrict__ out, int dt, int64_t ld, int D, int M) {
+  const int64_t n = (int64_t)D * M;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i / M, m = i - d * M;
+    const float v = mu[i] * w[m];
+    if (dt == ULM_F32)
+      static_cast<float*>(out)[d * ld + m] = v;
+    else
+      static_cast<__nv_bfloat16*>(out)[d * ld + m] = __float2bfloat16_rn(v);
+  }
+}
+
+// The combine's parameter gradients from the split-K partials of G = dy^T q (S x D x M):
+// dmu[d][m] = w[m] G[d][m] and dw[m] += sum_d mu[d][m] G[d][m], one thread per slot m, partials and
+// rows added in a fixed order.
+__global__ void combine_grad_kernel(const float* __restrict__ gpart, int S, const float* __restrict__ mu,
+                                    const float* __restrict__ w, float* __restrict__ dmu, float* __restrict__ dw,
+                                    int D, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  const float wm = w[m];
+  float acc = 0.f;
+  for (int d = 0; d < D; ++d) {
+    const int64_t i = (int64_t)d * M + m;
+    float gsum = 0.f;
+    for (int sp = 0; sp < S; ++sp) gsum += gpart[(int64_t)sp * D * M + i];
+    dmu[i] = gsum * wm;
+    acc = fmaf(mu[i], gsum, acc);
+  }
+  dw[m] += acc;
+}
+
 int check_prec(int prec) {
   ULM_REQUIRE(prec == ULM_PREC_BF16 || prec == ULM_PREC_FP32, "prec must be ULM_PREC_BF16 or ULM_PREC_FP32");
   return ULM_OK;
@@ -309,4 +368,138 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
   }
   return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0,
                        st);
+}
+
+// ---- the block's combine fused into the fast memory (model.py:79-85) -------------------------------
+namespace ulm {
+namespace {
+
+// Split of a contraction over `rows` into S k ranges so an (N1 x N2) product fills the CTA pairs once
+// (S x tiles <= pairs), at most 8, each range at least 1024 rows and none empty.
+int fill_split(int64_t rows, int64_t N1, int64_t N2) {
+  const int dev = current_device();
+  const int pairs = (dev >= 0 ? sm_count(dev) : 148) / 2;
+  const int64_t tiles = cdiv(N1, 256) * cdiv(N2, 256);
+  int S = (int)std::max<int64_t>(1, std::min<int64_t>(8, pairs / std::max<int64_t>(1, tiles)));
+  while (S > 1 && (rows / S < 1024 || (int64_t)(S - 1) * ksplit_chunk((int)rows, S) >= rows)) --S;
+  return S;
+}
+
+}  // namespace
+}  // namespace ulm
+
+extern "C" int64_t ulm_combine_grad_scratch(int64_t B, int64_t T, int64_t M, int64_t D) {
+  if (B < 0 || T < 0 || M < 0 || D < 0) return -1;
+  return 8 * D * M * (int64_t)sizeof(float);  // sized for the largest split
+}
+
+extern "C" int ulm_memory_combine_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g,
+                                      const float* w, const float* mu, const void* x, int x_dtype, void* y, float* q,
+                                      float* c, void* qop, void* kop, void* vop, void* P, void* wmu, int64_t B,
+                                      int64_t T, int64_t M, int64_t D, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
+  ULM_REQUIRE(v_dtype == ULM_F32 || v_dtype == ULM_BF16, "v_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(x_dtype == ULM_F32 || x_dtype == ULM_BF16, "x_dtype must be ULM_F32 or ULM_BF16");
+  if (B == 0 || T == 0 || D == 0) return ULM_OK;
+  ULM_REQUIRE(v && x && y && g && w, "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M == 0) return convert_rows(x, x_dtype, D, y, x_dtype, D, B * T, D, st);  // no slots: y = x
+  ULM_REQUIRE(r && mu && qop && kop && vop && P && wmu, "null pointer argument");
+  ULM_REQUIRE(B <= 65535 && T < (1 << 30) && M < (1 << 30) && D < (1 << 30), "extent too large");
+  const int dt = op_dtype_of(prec);
+  const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
+  if (int rc = stats_fwd_run(r, den, w, g, q, c, qop, kop, dt, ldm, B, T, M, stream)) return rc;
+  if (int rc = convert_rows(v, v_dtype, D, vop, dt, ldd, B * T, D, st)) return rc;
+  combine_weight_t_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)cdiv(D, 32)), 256, 0, st>>>(mu, w, wmu, dt, ldd,
+                                                                                            (int)D, (int)M);
+  ULM_LAUNCH_CHECK("combine_weight_t_kernel");
+  if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, P, ldt, g, B, T, M, prec, stream)) return rc;
+  // y = x + P v (causal k range) + q (w mu)^T (all M) in one accumulator
+  Operand A{P, ldt, T * ldt, T, T, dt, false};
+  Operand Bv{vop, ldd, T * ldd, D, T, dt, true};
+  Operand A2{qop, ldm, T * ldm, M, T, dt, false};
+  Operand B2{wmu, ldd, 0, D, M, dt, true};
+  GemmShape s{(int)B, (int)T, (int)D, (int)T, CAUSAL_KLOWER};
+  s.K2 = (int)M;
+  GemmEpilogue e = make_epilogue(EPI_STORE_ADD, x_dtype, y, D, T * D, nullptr);
+  e.aux = x;
+  e.ld_aux = D;
+  e.aux_bstride = T * D;
+  e.vec_ok = e.vec_ok && is_aligned16(x);
+  return run_gemm2(A, Bv, &A2, &B2, s, e, st);
+}
+
+extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float* r, const float* den, const float* g,
+                                      const float* w, const float* mu, const float* q, const float* c,
+                                      const void* qop, const void* kop, const void* vop, const void* P, void* doop,
+                                      void* dS, void* mw, float* dqf, float* dk, void* partial, float* gpart,
+                                      float* dr, void* dv, int dv_dtype, float* dg, float* dw, float* dmu,
+                                      int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream) {
+  if (int rc = check_prec(prec)) return rc;
+  ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
+  ULM_REQUIRE(dy_dtype == ULM_F32 || dy_dtype == ULM_BF16, "dy_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(dv_dtype == ULM_F32 || dv_dtype == ULM_BF16, "dv_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(dy && dr && dv && dg && dw && dmu, "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || T == 0 || M == 0 || D == 0) {
+    if (B * T * D > 0) ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(dv_dtype), st));
+    if (D * M > 0) ULM_CUDA_TRY(cudaMemsetAsync(dmu, 0, D * M * sizeof(float), st));
+    return ulm_memory_stats_bwd(dqf, nullptr, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
+  }
+  ULM_REQUIRE(r && g && w && mu && qop && kop && vop && P && doop && dS && mw && dqf && dk && partial && gpart,
+              "null pointer argument");
+  ULM_REQUIRE(B <= 65535 && T < (1 << 30) && M < (1 << 30) && D < (1 << 30), "extent too large");
+  const int dt = op_dtype_of(prec);
+  const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
+  // dfast = dy: its operand copy is the A operand of the score gradient, of dv and of d(q w)
+  if (int rc = convert_rows(dy, dy_dtype, D, doop, dt, ldd, B * T, D, st)) return rc;
+  StatsScratch sc = carve_stats_scratch(partial, B, M);
+  const int64_t n_tiles = decay_dg_partials(B, T);
+  ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
+  {
+    Operand A{doop, ldd, T * ldd, D, T, dt, false};
+    Operand Bo{vop, ldd, T * ldd, D, T, dt, false};
+    GemmShape s{(int)B, (int)T, (int)T, (int)D, CAUSAL_NLOWER};
+    GemmEpilogue e = make_epilogue(EPI_DECAY_DG, dt, dS, ldt, T * ldt, g);
+    e.aux = P;
+    e.ld_aux = ldt;
+    e.aux_bstride = T * ldt;
+    e.tile_partial = sc.tiles;
+    e.vec_ok = e.vec_ok && is_aligned16(P);
+    if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
+  }
+  combine_weight_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 8 * 148), 256, 0, st>>>(mu, w, mw, dt, ldm,
+                                                                                             (int)D, (int)M);
+  ULM_LAUNCH_CHECK("combine_weight_kernel");
+  {
+    // dq = dS k + dy (mu w): the gradient reaching q through the combine joins the product
+    Operand A{dS, ldt, T * ldt, T, T, dt, false};
+    Operand Bk{kop, ldm, T * ldm, M, T, dt, true};
+    Operand A2{doop, ldd, T * ldd, D, T, dt, false};
+    Operand B2{mw, ldm, 0, M, D, dt, true};
+    GemmShape s{(int)B, (int)T, (int)M, (int)T, CAUSAL_KLOWER};
+    s.K2 = (int)D;
+    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, dqf, M, T * M, nullptr);
+    if (int rc = run_gemm2(A, Bk, &A2, &B2, s, e, st)) return rc;
+  }
+  if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
+  if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, dv_dtype, 1, B, T, D, prec, stream)) return rc;
+  if (int rc = stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
+                             sc.tiles, n_tiles, st))
+    return rc;
+  {
+    // G = dy^T q over all B*T rows (split K), then dmu = G w and dw += sum_d mu G
+    const int64_t rows = B * T;
+    const int S = fill_split(rows, D, M);
+    Operand A{doop, ldd, 0, D, rows, dt, true};
+    Operand Bq{qop, ldm, 0, M, rows, dt, true};
+    GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
+    s.ksplit = S;
+    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
+    if (int rc = run_gemm(A, Bq, s, e, st)) return rc;
+    combine_grad_kernel<<<(unsigned)cdiv(M, 128), 128, 0, st>>>(gpart, S, mu, w, dmu, dw, (int)D, (int)M);
+    ULM_LAUNCH_CHECK("combine_grad_kernel");
+  }
+  return ULM_OK;
 }

@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(32 * WARPS)
     const float wm = w[m];
     const int t0 = cta_t0 + wp * SEG;
     const int64_t row = (int64_t)b * T + t0;
-    float* qp = q + row * M + m;
+    float* qp = q ? q + row * M + m : nullptr;
     float* cp = c ? c + row * M + m : nullptr;
     const int64_t io = row * ldop + m;
     run = carry;
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(32 * WARPS)
         run = fmaf(lam, run, kk);
         const float cc = wm + run;
         const float qq = rv * fast_rcp(cc);
-        qp[(int64_t)i * M] = qq;
+        if (qp) qp[(int64_t)i * M] = qq;
         if (cp) cp[(int64_t)i * M] = cc;
         store_op<OpT>(qop, io + (int64_t)i * ldop, qq);
         store_op<OpT>(kop, io + (int64_t)i * ldop, kk);
@@ -700,7 +700,8 @@ int stats_fwd_run(const float* r, const float* den, const float* w, const float*
                   void* kop, int op_dtype, int64_t ld_op, int64_t B, int64_t T, int64_t M, void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
   if (B == 0 || T == 0 || M == 0) return ULM_OK;
-  ULM_REQUIRE(r && w && g && q && qop && kop, "null pointer argument");
+  ULM_REQUIRE(r && w && g && qop && kop, "null pointer argument");
+  ULM_REQUIRE(q || !c, "q may be omitted only together with c");
   ULM_REQUIRE(ld_op >= M, "ld_op (%lld) < M (%lld)", (long long)ld_op, (long long)M);
   ULM_REQUIRE(op_dtype == ULM_F32 || op_dtype == ULM_BF16, "op_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");

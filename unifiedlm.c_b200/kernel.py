@@ -164,3 +164,69 @@ def unified_memory(r, v, g, w, precision="bf16"):
     q, fast, *_ = torch.ops.ulm.memory_fwd(r.float().contiguous(), vv.contiguous(), g1,
                                            w.float().contiguous(), prec)
     return q, fast.to(out_dtype)
+
+
+def combine_fwd_raw(r, den, v, g, w, mu, x, precision):
+    """ulm_memory_combine_fwd on fresh buffers: y = x + mu(q w) + fast, plus the tensors saved for
+    the backward (q, c, qop, kop, vop, P); q and c are empty when the backward rebuilds them."""
+    _require_cuda(r, v, g, w, mu, x, den)
+    B, T, M = r.shape
+    D = v.shape[-1]
+    dev = r.device
+    opt = _op_dtype(precision)
+    lib = L.lib()
+    keep = bool(lib.ulm_memory_needs_c(T, M))
+    q = torch.empty(B, T, M, device=dev, dtype=torch.float32) if keep else r.new_empty(0)
+    c = torch.empty(B, T, M, device=dev, dtype=torch.float32) if keep else r.new_empty(0)
+    y = torch.empty(B, T, D, device=dev, dtype=x.dtype)
+    qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
+    kop = torch.empty_like(qop)
+    vop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    wmu = torch.empty(M, operand_ld(D), device=dev, dtype=opt)
+    with torch.cuda.device(dev):
+        L.check(lib.ulm_memory_combine_fwd(
+            L.ptr(r), L.ptr(den), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w), L.ptr(mu), L.ptr(x),
+            L.dtype_code(x.dtype), L.ptr(y), L.ptr(q) if keep else None, L.ptr(c) if keep else None, L.ptr(qop),
+            L.ptr(kop), L.ptr(vop), L.ptr(P), L.ptr(wmu), B, T, M, D, precision, L.stream_of(r)))
+    return y, q, c, qop, kop, vop, P
+
+
+def combine_fwd_fake(r, v, x, precision):
+    B, T, M = r.shape
+    D = v.shape[-1]
+    opt = _op_dtype(precision)
+    keep = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
+    return (x.new_empty(B, T, D), r.new_empty(keep, dtype=torch.float32), r.new_empty(keep, dtype=torch.float32),
+            r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
+            r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
+
+
+def combine_bwd_raw(dy, r, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, precision):
+    """ulm_memory_combine_bwd on fresh buffers: (dr, dv, dg, dw, dmu)."""
+    _require_cuda(dy, r, g, w, mu, den)
+    B, T, M = r.shape
+    D = dy.shape[-1]
+    dev = r.device
+    opt = _op_dtype(precision)
+    lib = L.lib()
+    dr = torch.empty(B, T, M, device=dev, dtype=torch.float32)
+    dv = torch.empty(B, T, D, device=dev, dtype=v_dtype)
+    dg = torch.empty((), device=dev, dtype=torch.float32)
+    dw = torch.empty(M, device=dev, dtype=torch.float32)
+    dmu = torch.empty(D, M, device=dev, dtype=torch.float32)
+    doop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    mw = torch.empty(D, operand_ld(M), device=dev, dtype=opt)
+    dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
+    dk = torch.empty_like(dqf)
+    partial = torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8)
+    gpart = torch.empty(int(lib.ulm_combine_grad_scratch(B, T, M, D)), device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        L.check(lib.ulm_memory_combine_bwd(
+            L.ptr(dy), L.dtype_code(dy.dtype), L.ptr(r), L.ptr(den), L.ptr(g), L.ptr(w), L.ptr(mu),
+            L.ptr(q) if q.numel() else None, L.ptr(c) if c.numel() else None, L.ptr(qop), L.ptr(kop), L.ptr(vop),
+            L.ptr(P), L.ptr(doop), L.ptr(dS), L.ptr(mw), L.ptr(dqf), L.ptr(dk), L.ptr(partial), L.ptr(gpart),
+            L.ptr(dr), L.ptr(dv), L.dtype_code(v_dtype), L.ptr(dg), L.ptr(dw), L.ptr(dmu), B, T, M, D, precision,
+            L.stream_of(r)))
+    return dr, dv, dg, dw, dmu

@@ -2,12 +2,13 @@
 
 ModelArgs, RMSNorm, UnifiedBlock and UnifiedLM keep the reference's constructor arguments,
 parameter names, shapes and initialisation (model.py:13-204), so state_dicts, checkpoints and the
-model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the addressing prologue and
-the fast read to `block.addressed_memory` (libulm_b200.so; the same result as
-`kernel.unified_memory(prologue.address(...))` without materialising the normalised addresses);
-the val and mu projections and RMSNorm stay PyTorch (cuBLAS) as in the reference; `step` /
-`init_state` / `forward_recurrent` keep the reference's token-by-token semantics (model.py:88-111, 164-175) for small-batch use, and
-`decode.py` holds the batched CUDA decoder.
+model.bin exporter interoperate unchanged. UnifiedBlock.forward routes the addressing prologue, the
+fast read and the `mu` combine with the residual to `block.block_mixer` (libulm_b200.so; the same
+result as `x + mu(q w) + fast` with `q, fast = kernel.unified_memory(prologue.address(...))`,
+without materialising the normalised addresses or q); with dropout active in training the combine
+runs as the reference's separate Linear. The val projection and RMSNorm stay PyTorch (cuBLAS).
+`step` / `init_state` / `forward_recurrent` keep the reference's token-by-token semantics
+(model.py:88-111, 164-175) for small-batch use, and `decode.py` holds the batched CUDA decoder.
 
 The block's precision follows `UnifiedBlock.precision` ("bf16" tensor-core products, default; or
 "fp32" for the 1e-5 parity mode), set for a whole model by `UnifiedLM.set_precision`.
@@ -21,7 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .block import addressed_memory
+from .block import addressed_memory, block_mixer
 from .kernel import CHUNK
 
 
@@ -89,10 +90,15 @@ class UnifiedBlock(nn.Module):
         eps = self.log_eps.clamp(-10, 10).exp()
         v = self.val(h)
         w = self._w()
-        # conv + code(u) + the fast memory in one call on the GPU (model.py:79-83); the addresses
-        # stay unnormalised between the two (addressed_memory)
-        q, fast = addressed_memory(h, self.conv.weight, self.key.weight, self.key.bias, eps, v,
-                                   -self.log_rate.exp(), w, precision=self.precision)
+        g = -self.log_rate.exp()
+        if self.dropout.p == 0.0 or not self.training:
+            # conv + code(u) + the fast memory + mu(q w) + residual in one call pair on the GPU
+            # (model.py:79-85): the combine accumulates in the fast read's tensor-core tiles
+            return block_mixer(x, h, self.conv.weight, self.key.weight, self.key.bias, eps, v, g, w,
+                               self.mu.weight, precision=self.precision)
+        # with dropout on the mixed output the combine stays a separate product
+        q, fast = addressed_memory(h, self.conv.weight, self.key.weight, self.key.bias, eps, v, g, w,
+                                   precision=self.precision)
         return x + self.dropout(self.mu((q * w).type_as(x)) + fast.type_as(x))
 
     # ---- token-by-token form (the reference for run.c) ----
