@@ -242,6 +242,60 @@ def bench_decode(dev, pk):
             "by_batch": out}
 
 
+def bench_mixer(dev, W, blocks, precision, steps=5, warmup=3):
+    """UnifiedBlock's mixing span (address + fast memory + mu(q w) + residual, model.py:79-85) fwd+bwd
+    over the 12 blocks at the 110M shape, through autograd, in two forms: the fused combine
+    (block.block_mixer: mu(q w) in the fast read's tiles, its gradient in the dq product) and the
+    reference's structure on top of the same fast memory (addressed_memory, then a bf16 Linear for
+    mu and the residual in PyTorch). bf16 activations, fp32 parameters, as under autocast."""
+    import math
+    import torch.nn.functional as F
+    from unifiedlm_c_b200.block import addressed_memory, block_mixer
+    B, T, M, D, L = W["B"], W["T"], W["M"], W["D"], W["L"]
+    gen = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(B, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    h = (torch.randn(B, T, D, device=dev, generator=gen)).to(torch.bfloat16)
+    v = torch.randn(B, T, D, device=dev, generator=gen).to(torch.bfloat16)
+    dy = (torch.randn(B, T, D, device=dev, generator=gen) * 1e-3).to(torch.bfloat16)
+    params = []
+    for blk in blocks:
+        p = {k: blk[k].detach().clone().requires_grad_(True) for k in ("conv", "key_w", "key_b", "g", "w")}
+        p["eps"] = blk["eps"].detach().clone().requires_grad_(True)
+        p["mu"] = (torch.randn(D, M, device=dev, generator=gen) * 0.02 / math.sqrt(L)).requires_grad_(True)
+        params.append(p)
+    xs = x.clone().requires_grad_(True)
+
+    def step(fused):
+        for p in params:
+            if fused:
+                y = block_mixer(xs, h, p["conv"], p["key_w"], p["key_b"], p["eps"], v, p["g"], p["w"], p["mu"],
+                                precision=precision)
+            else:
+                q, fast = addressed_memory(h, p["conv"], p["key_w"], p["key_b"], p["eps"], v, p["g"], p["w"],
+                                           precision=precision)
+                y = xs + (F.linear((q * p["w"]).to(torch.bfloat16), p["mu"].to(torch.bfloat16)) + fast.to(xs.dtype))
+            y.backward(dy)
+
+    out = {}
+    for fused in (True, False):
+        for _ in range(warmup):
+            step(fused)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            step(fused)
+        e1.record()
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) / 1e3 / steps
+        out["fused" if fused else "unfused"] = {"tokens_per_s": round(B * T / secs, 1), "ms_per_step": round(secs * 1e3, 3)}
+    return {"metric": "block mixing span fwd+bwd tokens/s (110M shape, 12 blocks)",
+            "value": out["fused"]["tokens_per_s"], "unit": "tokens/s",
+            "workload": "address + fast memory + mu(q w) + residual per block, autograd, bf16 activations",
+            "fused": out["fused"], "unfused_torch_combine": out["unfused"],
+            "speedup": round(out["fused"]["tokens_per_s"] / out["unfused"]["tokens_per_s"], 3)}
+
+
 def runc_decode_baseline(steps=32):
     """The reference's own C decoder (run.c, built with its runomp flags into oracle/_ref/run_omp),
     greedy, at the 110M shape with seeded random weights, all host cores. Returns tokens/s or None."""
@@ -319,6 +373,7 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
+    ap.add_argument("--no-mixer", action="store_true", help="skip the fused-combine measurement")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
     ap.add_argument("--profile-decode", action="store_true",
@@ -473,6 +528,10 @@ def main():
                          "pure-PyTorch form (model.py:70-79, test_all.py:28-51 restated in oracle/memory.py), "
                          "fp32, scaled to 12 blocks"}
 
+    mixer = None
+    if world == 1 and not args.no_mixer:
+        mixer = bench_mixer(dev, W, blocks, args.precision)
+
     decode = None
     if not args.no_decode:
         decode = bench_decode(dev, pk)
@@ -495,7 +554,7 @@ def main():
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
-            "decode": decode}
+            "mixer": mixer, "decode": decode}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

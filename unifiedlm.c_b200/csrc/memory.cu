@@ -188,24 +188,45 @@ __global__ void combine_weight_kernel(const float* __restrict__ mu, const float*
   }
 }
 
-// The combine's parameter gradients from the split-K partials of G = dy^T q (S x D x M):
-// dmu[d][m] = w[m] G[d][m] and dw[m] += sum_d mu[d][m] G[d][m], one thread per slot m, partials and
-// rows added in a fixed order.
-__global__ void combine_grad_kernel(const float* __restrict__ gpart, int S, const float* __restrict__ mu,
-                                    const float* __restrict__ w, float* __restrict__ dmu, float* __restrict__ dw,
-                                    int D, int M) {
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
-  if (m >= M) return;
-  const float wm = w[m];
+// The combine's parameter gradients from the split-K partials of G = dy^T q (S x D x M): a CTA takes
+// 32 slots x 32 rows (threads: 32 slots x 8 row groups), writes dmu[d][m] = w[m] G[d][m] and one
+// partial of sum_d mu[d][m] G[d][m] per slot, partials and rows added in a fixed order.
+constexpr int COMBINE_ROWS = 32;
+__global__ void __launch_bounds__(256)
+    combine_grad_kernel(const float* __restrict__ gpart, int S, const float* __restrict__ mu,
+                        const float* __restrict__ w, float* __restrict__ dmu, float* __restrict__ dw_part, int D,
+                        int M) {
+  __shared__ float red[8][32];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int m = blockIdx.x * 32 + tx;
+  const int d0 = blockIdx.y * COMBINE_ROWS;
   float acc = 0.f;
-  for (int d = 0; d < D; ++d) {
-    const int64_t i = (int64_t)d * M + m;
-    float gsum = 0.f;
-    for (int sp = 0; sp < S; ++sp) gsum += gpart[(int64_t)sp * D * M + i];
-    dmu[i] = gsum * wm;
-    acc = fmaf(mu[i], gsum, acc);
+  if (m < M) {
+    const float wm = w[m];
+    for (int d = d0 + ty; d < min(D, d0 + COMBINE_ROWS); d += 8) {
+      const int64_t i = (int64_t)d * M + m;
+      float gsum = 0.f;
+      for (int sp = 0; sp < S; ++sp) gsum += gpart[(int64_t)sp * D * M + i];
+      dmu[i] = gsum * wm;
+      acc = fmaf(mu[i], gsum, acc);
+    }
   }
-  dw[m] += acc;
+  red[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && m < M) {
+    float t = red[0][tx];
+    for (int j = 1; j < 8; ++j) t += red[j][tx];
+    dw_part[(int64_t)blockIdx.y * M + m] = t;
+  }
+}
+
+// out[i] += sum over p of part[p][i], in order
+__global__ void add_parts_kernel(const float* __restrict__ part, int nparts, int64_t n, float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float t = 0.f;
+  for (int p = 0; p < nparts; ++p) t += part[(int64_t)p * n + i];
+  out[i] += t;
 }
 
 int check_prec(int prec) {
@@ -390,7 +411,8 @@ int fill_split(int64_t rows, int64_t N1, int64_t N2) {
 
 extern "C" int64_t ulm_combine_grad_scratch(int64_t B, int64_t T, int64_t M, int64_t D) {
   if (B < 0 || T < 0 || M < 0 || D < 0) return -1;
-  return 8 * D * M * (int64_t)sizeof(float);  // sized for the largest split
+  // split-K partials of G, sized for the largest split, then the dw partials per row block
+  return (8 * D * M + cdiv(D, COMBINE_ROWS) * M) * (int64_t)sizeof(float);
 }
 
 extern "C" int ulm_memory_combine_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g,
@@ -498,8 +520,13 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     s.ksplit = S;
     GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
     if (int rc = run_gemm(A, Bq, s, e, st)) return rc;
-    combine_grad_kernel<<<(unsigned)cdiv(M, 128), 128, 0, st>>>(gpart, S, mu, w, dmu, dw, (int)D, (int)M);
+    float* dw_part = gpart + 8 * D * M;
+    const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
+    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, st>>>(gpart, S, mu, w, dmu, dw_part,
+                                                                                (int)D, (int)M);
     ULM_LAUNCH_CHECK("combine_grad_kernel");
+    add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(dw_part, (int)row_blocks, M, dw);
+    ULM_LAUNCH_CHECK("add_parts_kernel");
   }
   return ULM_OK;
 }
