@@ -53,9 +53,11 @@ def make_inputs(B, T, M, D, L, lam, prior, device, seed=0):
     rn = lambda *s_: torch.randn(*s_, device=device, generator=gen)  # noqa: E731
     h = rn(B, T, D)
     h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
-    v = rn(B, T, D)
+    # dtypes as under the reference's bf16 autocast: the residual stream and h = norm(x) stay fp32,
+    # v = val(h) is bf16, so fast and its gradient are bf16; q and its gradient are fp32
+    v = rn(B, T, D).to(torch.bfloat16)
     dq_out = rn(B, T, M) * 1e-3
-    dfast = rn(B, T, D) * 1e-3
+    dfast = (rn(B, T, D) * 1e-3).to(torch.bfloat16)
     blocks = []
     for _ in range(L):
         blocks.append({"conv": rn(D, 1, 4) * 0.5, "key_w": rn(M, D) / math.sqrt(D), "key_b": rn(M) * 0.1,
@@ -335,7 +337,7 @@ def timed_products(ulm_lib, L_, tensors, W, prec):
         (2 * B * pairs * M, lambda: lib.ulm_decayed_scores(L_.ptr(qop), ldm, L_.ptr(kop), ldm, L_.ptr(P), ldt,
                                                            L_.ptr(g), B, T, M, prec, sp)),
         (2 * B * pairs * D, lambda: lib.ulm_causal_apply(L_.ptr(P), ldt, L_.ptr(vop), ldd, L_.ptr(fast), D,
-                                                         L_.ULM_F32, 0, B, T, D, prec, sp)),
+                                                         L_.dtype_code(fast.dtype), 0, B, T, D, prec, sp)),
         (2 * B * pairs * D, lambda: lib.ulm_decayed_scores(L_.ptr(doop), ldd, L_.ptr(vop), ldd, L_.ptr(dS), ldt,
                                                            L_.ptr(g), B, T, D, prec, sp)),
         (2 * B * pairs * M, lambda: lib.ulm_causal_apply(L_.ptr(dS), ldt, L_.ptr(kop), ldm, L_.ptr(dqf), M,
@@ -343,7 +345,7 @@ def timed_products(ulm_lib, L_, tensors, W, prec):
         (2 * B * pairs * M, lambda: lib.ulm_causal_apply(L_.ptr(dS), ldt, L_.ptr(qop), ldm, L_.ptr(dk), M,
                                                          L_.ULM_F32, 1, B, T, M, prec, sp)),
         (2 * B * pairs * D, lambda: lib.ulm_causal_apply(L_.ptr(P), ldt, L_.ptr(doop), ldd, L_.ptr(dv), D,
-                                                         L_.ULM_F32, 1, B, T, D, prec, sp)),
+                                                         L_.dtype_code(dv.dtype), 1, B, T, D, prec, sp)),
     ]
     flops, secs = 0, 0.0
     per = []
@@ -389,7 +391,7 @@ def main():
 
     load_package()
     import unifiedlm_c_b200._lib as L_
-    from unifiedlm_c_b200.kernel import memory_fwd, PRECISION
+    from unifiedlm_c_b200.kernel import memory_fwd, operand_or_input, PRECISION
     from unifiedlm_c_b200.prologue import address_fwd
     from unifiedlm_c_b200.block import addressed_memory_fwd, addressed_memory_bwd
 
@@ -423,7 +425,8 @@ def main():
             q, fast, z, den, u_op, kw, c, qop, kop, vop, P = addressed_memory_fwd(
                 h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_, blk["g"], blk["w"], prec)
             dh, dconv, dkw, dkb, deps, dv, dg, dw = addressed_memory_bwd(
-                dq_, df_, h_, blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop, vop, P, prec)
+                dq_, df_, h_, blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop,
+                operand_or_input(vop, v_), P, prec)
             grads += [dkw, dkb, dconv, deps, dw, dg]
         # the path's parameter gradients in one bucket: one NCCL all-reduce per step (DP average)
         bucket.pack(grads)
@@ -497,6 +500,7 @@ def main():
     g, w = blk0["g"], blk0["w"]
     r, _, _, _ = address_fwd(h, blk0["conv"], blk0["key_w"], blk0["key_b"], blk0["eps"], prec)
     q, fast, c, qop, kop, vop, P = memory_fwd(r, v, g, w, prec)
+    vop = operand_or_input(vop, v)
     ldd, ldt = L_.lib().ulm_operand_ld(W["D"]), L_.lib().ulm_operand_ld(W["T"])
     opt = qop.dtype
     doop = torch.zeros(W["B"], W["T"], ldd, device=dev, dtype=opt)
@@ -504,9 +508,10 @@ def main():
     dS = torch.empty(W["B"], W["T"], ldt, device=dev, dtype=opt)
     dqf = torch.empty(W["B"], W["T"], W["M"], device=dev)
     dk = torch.empty_like(dqf)
-    dvb = torch.empty(W["B"], W["T"], W["D"], device=dev)
-    fast32 = torch.empty(W["B"], W["T"], W["D"], device=dev)
-    flops, psecs, per = timed_products(None, L_, (qop, kop, vop, P, doop, dS, dqf, dk, dvb, fast32, g), W, prec)
+    # outputs in the step's types: fast and dv in v's / dfast's type, dq and dk fp32
+    dvb = torch.empty(W["B"], W["T"], W["D"], device=dev, dtype=dfast.dtype)
+    fastb = torch.empty(W["B"], W["T"], W["D"], device=dev, dtype=v.dtype)
+    flops, psecs, per = timed_products(None, L_, (qop, kop, vop, P, doop, dS, dqf, dk, dvb, fastb, g), W, prec)
     pk = peaks()
     achieved = flops / psecs / 1e12
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",

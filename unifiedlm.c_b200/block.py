@@ -18,7 +18,7 @@ from typing import Optional
 import torch
 
 from .kernel import (PRECISION, combine_bwd_raw, combine_fwd_fake, combine_fwd_raw, memory_bwd_raw, memory_fwd_fake,
-                     memory_fwd_raw)
+                     memory_fwd_raw, operand_or_input, unaliased)
 from .prologue import address_bwd_fake, address_bwd_raw, address_fwd_fake, address_fwd_raw
 
 _OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
@@ -32,7 +32,7 @@ def addressed_memory_fwd(h: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Ten
     for the backward."""
     z, den, u_op, kw = address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=False)
     q, fast, c, qop, kop, vop, P = memory_fwd_raw(z, den, v, g, w, precision)
-    return q, fast, z, den, u_op, kw, c, qop, kop, vop, P
+    return q, fast, z, den, u_op, kw, c, qop, kop, unaliased(vop, v), P
 
 
 @addressed_memory_fwd.register_fake
@@ -66,7 +66,7 @@ def _bwd_fake(dq_out, dfast, h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, 
 def _setup(ctx, inputs, output):
     h, conv_w, key_w, key_b, eps, v, g, w, precision = inputs
     q, fast, z, den, u_op, kw, c, qop, kop, vop, P = output
-    ctx.save_for_backward(h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, vop, P)
+    ctx.save_for_backward(h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, operand_or_input(vop, v), P)
     ctx.precision = precision
     ctx.dtypes = (h.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype, v.dtype)
     ctx.v_dim = v.shape[-1]
@@ -118,7 +118,7 @@ def mixer_fwd(x: torch.Tensor, h: torch.Tensor, conv_w: torch.Tensor, key_w: tor
     """Returns (y, z, den, u_op, kw_op, q, c, qop, kop, vop, P); all but y are saved for the backward."""
     z, den, u_op, kw = address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=False)
     y, q, c, qop, kop, vop, P = combine_fwd_raw(z, den, v, g, w, mu, x, precision)
-    return y, z, den, u_op, kw, q, c, qop, kop, vop, P
+    return y, z, den, u_op, kw, q, c, qop, kop, unaliased(vop, v), P
 
 
 @mixer_fwd.register_fake
@@ -152,7 +152,7 @@ def _mixer_bwd_fake(dy, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, v
 def _mix_setup(ctx, inputs, output):
     x, h, conv_w, key_w, key_b, eps, v, g, w, mu, precision = inputs
     y, z, den, u_op, kw, q, c, qop, kop, vop, P = output
-    ctx.save_for_backward(h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P)
+    ctx.save_for_backward(h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, operand_or_input(vop, v), P)
     ctx.precision = precision
     ctx.dtypes = (x.dtype, h.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype, v.dtype, mu.dtype)
     ctx.g_shape = g.shape

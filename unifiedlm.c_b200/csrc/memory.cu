@@ -135,6 +135,7 @@ __global__ void convert_rows_vec8_kernel(const void* __restrict__ src, int src_d
 int convert_rows(const void* src, int sdt, int64_t lds, void* dst, int ddt, int64_t ldd, int64_t rows, int64_t cols,
                  cudaStream_t st) {
   if (rows * cols == 0) return ULM_OK;
+  if (src == dst && sdt == ddt && lds == ldd) return ULM_OK;  // the caller passed the array as its own copy
   if (cols % 8 == 0 && lds % 8 == 0 && ldd % 8 == 0 && is_aligned16(src) && is_aligned16(dst)) {
     const int64_t blocks = cdiv(rows * (cols / 8), 256);
     const unsigned grid = (unsigned)(blocks < 16 * 148 ? blocks : 16 * 148);

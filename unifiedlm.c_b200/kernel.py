@@ -42,6 +42,15 @@ def _op_dtype(precision):
     return torch.float32 if precision == L.ULM_PREC_FP32 else torch.bfloat16
 
 
+def operand_copy(x, opt):
+    """Buffer for the tensor-core operand copy of a (B,T,D) array: x itself when it already has the
+    operand type, padded row stride and alignment (the library then skips the copy), else a new one."""
+    B, T, D = x.shape
+    if x.dtype == opt and operand_ld(D) == D and x.is_contiguous() and x.data_ptr() % 16 == 0:
+        return x
+    return torch.empty(B, T, operand_ld(D), device=x.device, dtype=opt)
+
+
 def memory_fwd_raw(r, den, v, g, w, precision):
     """ulm_memory_fwd on fresh buffers: (q, fast, c, qop, kop, vop, P). den None: r holds the
     addresses; else r holds z and den the row denominators (r = z / den)."""
@@ -56,7 +65,7 @@ def memory_fwd_raw(r, den, v, g, w, precision):
     fast = torch.empty(B, T, D, device=dev, dtype=v.dtype)
     qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
     kop = torch.empty_like(qop)
-    vop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    vop = operand_copy(v, opt)
     P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     with torch.cuda.device(dev):
         L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(den), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w),
@@ -88,7 +97,7 @@ def memory_bwd_raw(dq_out, dfast, r, den, g, w, q, c, qop, kop, vop, P, precisio
     dv = torch.empty(B, T, D, device=dev, dtype=dfast.dtype)
     dg = torch.empty((), device=dev, dtype=torch.float32)
     dw = torch.empty(M, device=dev, dtype=torch.float32)
-    doop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    doop = operand_copy(dfast, opt)
     dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
     dk = torch.empty_like(dqf)
@@ -106,8 +115,20 @@ def memory_bwd_raw(dq_out, dfast, r, den, g, w, q, c, qop, kop, vop, P, precisio
 def memory_fwd(r: torch.Tensor, v: torch.Tensor, g: torch.Tensor, w: torch.Tensor, precision: int
                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                           torch.Tensor]:
-    """Returns (q, fast, c, qop, kop, vop, P); the last five are saved for the backward."""
-    return memory_fwd_raw(r, None, v, g, w, precision)
+    """Returns (q, fast, c, qop, kop, vop, P); the last five are saved for the backward (vop is
+    empty when v itself serves as the operand copy)."""
+    q, fast, c, qop, kop, vop, P = memory_fwd_raw(r, None, v, g, w, precision)
+    return q, fast, c, qop, kop, unaliased(vop, v), P
+
+
+def unaliased(op, x):
+    """An op's output must not alias its input: an empty placeholder when the operand copy is x."""
+    return x.new_empty(0) if op.data_ptr() == x.data_ptr() else op
+
+
+def operand_or_input(op, x):
+    """The operand copy saved for a backward: the placeholder stands for the input x itself."""
+    return x if op.numel() == 0 else op
 
 
 @memory_fwd.register_fake
@@ -134,7 +155,7 @@ def _memory_bwd_fake(dq_out, dfast, r, g, w, q, c, qop, kop, vop, P, precision):
 def _setup_context(ctx, inputs, output):
     r, v, g, w, precision = inputs
     q, fast, c, qop, kop, vop, P = output
-    ctx.save_for_backward(r, g, w, q, c, qop, kop, vop, P)
+    ctx.save_for_backward(r, g, w, q, c, qop, kop, operand_or_input(vop, v), P)
     ctx.precision = precision
     ctx.v_dtype = v.dtype
     ctx.v_dim = v.shape[-1]
@@ -181,7 +202,7 @@ def combine_fwd_raw(r, den, v, g, w, mu, x, precision):
     y = torch.empty(B, T, D, device=dev, dtype=x.dtype)
     qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
     kop = torch.empty_like(qop)
-    vop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    vop = operand_copy(v, opt)
     P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     wmu = torch.empty(M, operand_ld(D), device=dev, dtype=opt)
     with torch.cuda.device(dev):
@@ -215,7 +236,7 @@ def combine_bwd_raw(dy, r, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, preci
     dg = torch.empty((), device=dev, dtype=torch.float32)
     dw = torch.empty(M, device=dev, dtype=torch.float32)
     dmu = torch.empty(D, M, device=dev, dtype=torch.float32)
-    doop = torch.empty(B, T, operand_ld(D), device=dev, dtype=opt)
+    doop = operand_copy(dy, opt)
     dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
     mw = torch.empty(D, operand_ld(M), device=dev, dtype=opt)
     dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
