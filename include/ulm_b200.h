@@ -22,6 +22,7 @@
  *   model.py:84-85     unified_memory + mu(q w) + residual    -> ulm_memory_combine_fwd, _bwd
  *   model.py:88-111,   UnifiedBlock.init_state / step, and
  *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
+ *   run.c:460-534      run.c sample (argmax / mult / top-p)   -> ulm_decode_head, ulm_decode_sample
  */
 #ifndef ULM_B200_H
 #define ULM_B200_H
@@ -270,6 +271,18 @@ int ulm_decode_head(float* x, const float* norm_w, const void* cls_w, const void
                     void* stream);
 
 int64_t ulm_decode_head_work_bytes(int64_t B, int64_t D);
+
+/* run.c's sample() with temperature > 0 (run.c:460-534) for B sequences on the device:
+ * softmax(logits[b] / temperature), a coin from the sequence's xorshift64* state rng_state[b]
+ * (advanced in place, run.c random_f32), then the first index whose cumulative probability exceeds
+ * the coin (topp <= 0 or >= 1, run.c sample_mult) or top-p sampling over the probabilities sorted
+ * in descending order (run.c sample_topp; ties by ascending index). Writes next_token (B,) int32
+ * and x[b] = emb[next_token[b]]. The sums are parallel reductions, so a coin within about 1e-7 of a
+ * cumulative boundary can pick the neighbouring token where run.c's sequential sums would not.
+ * logits (B,V) fp32, V <= 50000; emb (V,D) in emb_dtype; x (B,D) fp32. */
+int ulm_decode_sample(const float* logits, int64_t B, int64_t V, float temperature, float topp,
+                      unsigned long long* rng_state, int* next_token, const void* emb, int emb_dtype, float* x,
+                      int64_t D, void* stream);
 
 #ifdef __cplusplus
 }

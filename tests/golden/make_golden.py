@@ -19,6 +19,9 @@ Fixtures:
   runc_tiny.pt  : the model of test_all.test_runc (fp32), and the greedy token ids that the
                   reference's run.c prints for it from BOS, read through a vocabulary whose
                   pieces are "|<id>" so the text maps back to ids.
+  runc_sampled.pt: run.c's sampled token ids for the same model from BOS (temperature > 0, top-p
+                  and plain multinomial, fixed seeds). `python make_golden.py --sampled` writes only
+                  this file (it needs runc_tiny.pt and oracle/_ref/run, not the reference's Python).
 """
 import os
 import subprocess
@@ -148,11 +151,41 @@ def runc_fixture(ref_model):
     return {"state_dict": sd, "max_seq_len": seq, "steps": steps, "seed": seed, "ids": torch.tensor(ids)}
 
 
+SAMPLED_RUNS = [(1.0, 0.9, 42), (0.8, 0.9, 7), (1.0, 1.0, 3), (0.7, 0.0, 11)]  # (temperature, topp, seed)
+
+
+def runc_sampled_fixture():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ulm_export", os.path.join(REPO, "unifiedlm.c_b200", "export.py"))
+    ulm_export = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ulm_export)
+    base = torch.load(os.path.join(HERE, "runc_tiny.pt"), weights_only=False)
+    binary = os.path.join(REPO, "oracle", "_ref", "run")
+    steps = 48
+    runs = []
+    with tempfile.TemporaryDirectory() as tmp:
+        mpath, tpath = os.path.join(tmp, "model.bin"), os.path.join(tmp, "tok.bin")
+        ulm_export.write_model_bin(base["state_dict"], mpath, base["max_seq_len"])
+        ulm_export.write_tokenizer_bin(tpath, [f"|{i}" for i in range(512)])
+        for temperature, topp, seed in SAMPLED_RUNS:
+            text = subprocess.run([binary, mpath, "-z", tpath, "-t", str(temperature), "-p", str(topp), "-s",
+                                   str(seed), "-n", str(steps)], capture_output=True, text=True, check=True).stdout
+            ids = [int(p) for p in text.strip().split("|") if p]
+            runs.append({"temperature": temperature, "topp": topp, "seed": seed, "steps": steps,
+                         "ids": torch.tensor(ids)})
+    return {"runs": runs}
+
+
 def main():
+    import sys
+    if "--sampled" in sys.argv:
+        torch.save(runc_sampled_fixture(), os.path.join(HERE, "runc_sampled.pt"))
+        return
     ref_model, ref_tests = load_reference()
     torch.save(memory_op_fixture(ref_model, ref_tests), os.path.join(HERE, "memory_op.pt"))
     torch.save(model_fixture(ref_tests), os.path.join(HERE, "model_tiny.pt"))
     torch.save(runc_fixture(ref_model), os.path.join(HERE, "runc_tiny.pt"))
+    torch.save(runc_sampled_fixture(), os.path.join(HERE, "runc_sampled.pt"))
     for f in sorted(os.listdir(HERE)):
         print(f, os.path.getsize(os.path.join(HERE, f)))
 

@@ -93,3 +93,83 @@ def test_live_runc_token_identity(tmp_path):
     dec = BatchedDecoder(p, batch=2, precision="fp32")
     out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=steps)
     assert out[0, :len(ids)].tolist() == ids and out[1, :len(ids)].tolist() == ids
+
+
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_sampled_tokens_match_reference_runc(golden_dir, use_graph):
+    """Sampling on the device (temperature > 0, top-p and plain multinomial) reproduces the token ids
+    the reference's run.c printed for the same model and seeds (fixture runc_sampled.pt)."""
+    base = load(golden_dir, "runc_tiny.pt")
+    for run in load(golden_dir, "runc_sampled.pt")["runs"]:
+        ids = run["ids"].tolist()
+        dec = BatchedDecoder(base["state_dict"], batch=2, precision="fp32", use_graph=use_graph,
+                             temperature=run["temperature"], topp=run["topp"], seed=[run["seed"], run["seed"]])
+        out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=run["steps"])
+        for row in out.tolist():
+            assert row[:len(ids)] == ids, (run["temperature"], run["topp"], run["seed"])
+
+
+@pytest.mark.parametrize("topp", [0.9, 0.5, 1.0])
+@pytest.mark.parametrize("scale", [0.3, 3.0, 30.0], ids=["flat", "medium", "peaked"])
+def test_device_sampler_matches_oracle(topp, scale):
+    """ulm_decode_sample on random logits (V = 32000, 64 sequences, own seeds) against run.c's
+    sampler restated in oracle.sampler with exact (float64) running sums: same tokens and advanced
+    states, except where the decisive comparison is within 2e-6 of its boundary (the device's
+    parallel sums differ in the last bits; run.c's sequential float32 sums drift further on flat
+    distributions, where tens of thousands of terms are summed)."""
+    import numpy as np
+    import unifiedlm_c_b200._lib as L
+    from oracle import sampler as S
+    B, V, D = 64, 32000, 8
+    g = torch.Generator().manual_seed(int(scale * 10) + int(topp * 100))
+    logits = torch.randn(B, V, generator=g) * scale
+    seeds = [int(x) for x in torch.randint(1, 2**62, (B,), generator=g)]
+    rng = torch.tensor(seeds, dtype=torch.int64, device="cuda")
+    emb = torch.randn(V, D, device="cuda")
+    x = torch.empty(B, D, device="cuda")
+    nxt = torch.empty(B, dtype=torch.int32, device="cuda")
+    lg = logits.cuda()
+    temperature = 0.8
+    L.check(L.lib().ulm_decode_sample(L.ptr(lg), B, V, temperature, topp, L.ptr(rng), L.ptr(nxt), L.ptr(emb),
+                                      L.ULM_F32, L.ptr(x), D, None))
+    torch.cuda.synchronize()
+    got, states = nxt.cpu().tolist(), [s & S.MASK64 for s in rng.cpu().tolist()]
+    checked = 0
+    for b in range(B):
+        tok, st, margin = S.sample(logits[b].numpy(), temperature, topp, seeds[b], acc=np.float64)
+        assert states[b] == st
+        if margin > 2e-6:
+            assert got[b] == tok, (b, got[b], tok, margin)
+            checked += 1
+    assert checked >= B // 2  # flat distributions put many cumulative boundaries near any coin
+    assert torch.equal(x.cpu(), emb.cpu()[torch.tensor(got)])
+    assert L.device_error() == 0
+
+
+def test_decoder_from_model_bin(golden_dir, tmp_path):
+    """BatchedDecoder.from_model_bin over run.c's checkpoint file gives run.c's greedy tokens."""
+    f = load(golden_dir, "runc_tiny.pt")
+    path = str(tmp_path / "m.bin")
+    export.write_model_bin(f["state_dict"], path, f["max_seq_len"])
+    dec = BatchedDecoder.from_model_bin(path, batch=2, precision="fp32")
+    out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=f["steps"])
+    ids = f["ids"].tolist()
+    assert out[0, :len(ids)].tolist() == ids and out[1, :len(ids)].tolist() == ids
+
+
+def test_live_runc_sampled_identity(tmp_path):
+    """Sampled decode (temperature 1, top-p 0.9, seed 5) of an exported model against a live run of
+    the reference's run.c."""
+    if not os.path.exists(RUNC):
+        pytest.skip("oracle/_ref/run not built (needs the reference checkout)")
+    steps = 48
+    mpath, tpath = str(tmp_path / "m.bin"), str(tmp_path / "tok.bin")
+    export.write_tokenizer_bin(tpath, [f"|{i}" for i in range(512)])
+    p = rand_params(9, 64, 3, 128, 512)
+    export.write_model_bin(p, mpath, max_seq_len=steps)
+    text = subprocess.run([RUNC, mpath, "-z", tpath, "-t", "1.0", "-p", "0.9", "-s", "5", "-n", str(steps)],
+                          capture_output=True, text=True, check=True).stdout
+    ids = [int(x) for x in text.strip().split("|") if x]
+    dec = BatchedDecoder.from_model_bin(mpath, batch=1, precision="fp32", temperature=1.0, topp=0.9, seed=5)
+    out = dec.generate(torch.ones(1, 1, dtype=torch.long), steps=steps)
+    assert out[0, :len(ids)].tolist() == ids

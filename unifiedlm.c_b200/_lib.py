@@ -51,6 +51,7 @@ SIGNATURES = {
     "ulm_decode_block_work_bytes": (_I64, [_I64, _I64, _I64]),
     "ulm_decode_embed": (_I, [_P, _P, _I, _P, _I64, _I64, _P]),
     "ulm_decode_head": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P]),
+    "ulm_decode_sample": (_I, [_P, _I64, _I64, ctypes.c_float, ctypes.c_float, _P, _P, _P, _I, _P, _I64, _P]),
     "ulm_decode_head_work_bytes": (_I64, [_I64, _I64]),
 }
 

@@ -293,6 +293,205 @@ int decode_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int wdt,
 
 }  // namespace
 
+// ---- sampling (run.c sample, run.c:460-534) ---------------------------------------------------
+// One CTA of SMP_THREADS per sequence.
+// Order of the probabilities for top-p: descending value, ties by ascending index, encoded as the
+// 64-bit key (float bits of p) << 32 | (~index); excluded entries have key 0.
+constexpr int SMP_THREADS = 1024;
+constexpr int SMP_MAX_V = 50000;  // probabilities of one sequence in shared memory (200 KB)
+
+__device__ __forceinline__ uint64_t smp_key(float p, int i) {
+  return ((uint64_t)__float_as_uint(p) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)i);
+}
+
+// fixed-order block reductions over SMP_THREADS threads (scratch: 32 slots)
+__device__ __forceinline__ float smp_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wp] = v;
+  __syncthreads();
+  if (wp == 0) {
+    v = red[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ __forceinline__ float smp_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wp] = v;
+  __syncthreads();
+  if (wp == 0) {
+    v = red[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ __forceinline__ uint64_t smp_max_u64(uint64_t v, uint64_t* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
+  }
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[wp] = v;
+  __syncthreads();
+  if (wp == 0) {
+    v = red[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = u > v ? u : v;
+    }
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// key of entry i (0 when excluded by the cutoff or past V)
+__device__ __forceinline__ uint64_t smp_entry_key(const float* ps, int i, int V, float cutoff) {
+  return (i < V && ps[i] >= cutoff) ? smp_key(ps[i], i) : 0ull;
+}
+
+// the largest key K in [lo, hi] with sum over entries with key >= K of p > thresh (hi is a key; the
+// answer is an entry's key), or 0 when even the sum over [lo, ...] does not exceed thresh
+__device__ uint64_t smp_search(const float* ps, int V, float cutoff, uint64_t lo, uint64_t hi, float thresh,
+                               float* red) {
+  uint64_t ans = 0;
+  while (lo <= hi && hi != 0) {
+    const uint64_t mid = lo + (hi - lo) / 2;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < V; i += SMP_THREADS) s += smp_entry_key(ps, i, V, cutoff) >= mid ? ps[i] : 0.f;
+    s = smp_sum(s, red);
+    if (s > thresh) {
+      ans = mid;
+      lo = mid + 1;
+    } else {
+      if (mid == 0) break;
+      hi = mid - 1;
+    }
+  }
+  return ans;
+}
+
+// next_token[b] from logits[b] as run.c's sample() with temperature > 0: softmax(logits / T), a coin
+// from the sequence's xorshift64* state (run.c random_f32), then multinomial over the index order
+// (topp outside (0, 1)) or top-p over the probabilities sorted descending; x[b] <- emb[next_token].
+// The V probabilities live in dynamic shared memory (entry i at ps[i], thread i % SMP_THREADS).
+__global__ void __launch_bounds__(SMP_THREADS)
+    decode_sample_kernel(const float* __restrict__ logits, int V, float temperature, float topp,
+                         unsigned long long* __restrict__ rng, int* __restrict__ next_token,
+                         const void* __restrict__ emb, int emb_bf16, int D, float* __restrict__ x) {
+  extern __shared__ float ps[];
+  __shared__ float red[33];
+  __shared__ uint64_t redk[33];
+  __shared__ float coin_s;
+  __shared__ int pick;
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float* lg = logits + (int64_t)b * V;
+  float mx = -INFINITY;
+  for (int i = tid; i < V; i += SMP_THREADS) {
+    const float v = lg[i] / temperature;
+    ps[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = smp_max(mx, red);
+  float s = 0.f;
+  for (int i = tid; i < V; i += SMP_THREADS) {
+    const float e = expf(ps[i] - mx);
+    ps[i] = e;
+    s += e;
+  }
+  s = smp_sum(s, red);
+  for (int i = tid; i < V; i += SMP_THREADS) ps[i] = ps[i] / s;
+  if (tid == 0) {
+    // xorshift64* step and 24-bit uniform (the published generator run.c uses)
+    unsigned long long st = rng[b];
+    st ^= st >> 12;
+    st ^= st << 25;
+    st ^= st >> 27;
+    rng[b] = st;
+    const uint32_t u = (uint32_t)((st * 0x2545F4914F6CDD1Dull) >> 32);
+    coin_s = (float)(u >> 8) / 16777216.0f;
+    pick = V - 1;
+  }
+  __syncthreads();
+  const float coin = coin_s;
+  if (!(topp > 0.f && topp < 1.f)) {
+    // multinomial in index order: first i with coin < cdf_i, chunks of SMP_THREADS entries scanned
+    // in turn (run.c sample_mult)
+    __shared__ float wtot[32];
+    __shared__ int hit_idx;
+    if (tid == 0) hit_idx = 0x7fffffff;
+    const int lane = tid & 31, wp = tid >> 5;
+    float base = 0.f;
+    for (int c0 = 0; c0 < V; c0 += SMP_THREADS) {
+      const int i = c0 + tid;
+      float v = i < V ? ps[i] : 0.f;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      __syncthreads();
+      if (lane == 31) wtot[wp] = v;
+      __syncthreads();
+      float off = base, tot = 0.f;
+      for (int w2 = 0; w2 < 32; ++w2) {
+        if (w2 < wp) off += wtot[w2];
+        tot += wtot[w2];
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, i < V && coin < off + v);
+      if (lane == 0 && mask) atomicMin(&hit_idx, c0 + wp * 32 + __ffs(mask) - 1);
+      base += tot;
+      __syncthreads();
+      if (hit_idx != 0x7fffffff) break;
+    }
+    if (tid == 0 && hit_idx != 0x7fffffff) pick = hit_idx;
+    __syncthreads();
+  } else {
+    const float cutoff = (1.0f - topp) / (float)(V - 1);
+    uint64_t kmax = 0;
+    for (int i = tid; i < V; i += SMP_THREADS) {
+      const uint64_t k = smp_entry_key(ps, i, V, cutoff);
+      kmax = k > kmax ? k : kmax;
+    }
+    kmax = smp_max_u64(kmax, redk);
+    // the top-p prefix: the largest key whose cumulative mass (descending order) exceeds topp
+    uint64_t k1 = smp_search(ps, V, cutoff, 1, kmax, topp, red);
+    if (k1 == 0) k1 = 1;  // rounding: the whole candidate set
+    float pk = 0.f;
+    for (int i = tid; i < V; i += SMP_THREADS) pk += smp_entry_key(ps, i, V, cutoff) >= k1 ? ps[i] : 0.f;
+    pk = smp_sum(pk, red);
+    // the first entry (descending order) whose cumulative mass exceeds coin * pk
+    const uint64_t k2 = smp_search(ps, V, cutoff, k1, kmax, coin * pk, red);
+    const uint64_t kk = k2 ? k2 : k1;
+    if (tid == 0) pick = (int)(0xFFFFFFFFu - (uint32_t)(kk & 0xFFFFFFFFull));
+    __syncthreads();
+  }
+  const int tok = pick;
+  if (tid == 0) next_token[b] = tok;
+  for (int i = tid; i < D; i += blockDim.x) {
+    const int64_t o = (int64_t)tok * D + i;
+    x[(int64_t)b * D + i] = emb_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(emb)[o])
+                                     : static_cast<const float*>(emb)[o];
+  }
+}
+
 extern "C" int ulm_decode_prepare_block(const float* mu, const float* w, const float* lam, void* prior,
                                         int prior_dtype, int64_t D, int64_t M, void* stream) {
   ULM_REQUIRE(mu && w && lam && prior, "null pointer argument");
@@ -417,4 +616,22 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
 
 extern "C" int64_t ulm_decode_head_work_bytes(int64_t B, int64_t D) {
   return (B * D * 4 + 255) / 256 * 256 + (B * ulm_operand_ld(D) * 2 + 255) / 256 * 256;
+}
+
+extern "C" int ulm_decode_sample(const float* logits, int64_t B, int64_t V, float temperature, float topp,
+                                 unsigned long long* rng_state, int* next_token, const void* emb, int emb_dtype,
+                                 float* x, int64_t D, void* stream) {
+  ULM_REQUIRE(logits && rng_state && next_token && emb && x, "null pointer argument");
+  ULM_REQUIRE(weight_dtype_ok(emb_dtype), "emb_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(B > 0 && V > 1 && D > 0 && B < (1 << 30), "bad extents");
+  ULM_REQUIRE(V <= SMP_MAX_V, "vocabulary larger than %d", SMP_MAX_V);
+  ULM_REQUIRE(temperature > 0.f, "temperature must be > 0 (0 is the greedy pick of ulm_decode_head)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)V * sizeof(float);
+  ULM_CUDA_TRY(cudaFuncSetAttribute(decode_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  decode_sample_kernel<<<(unsigned)B, SMP_THREADS, smem, st>>>(logits, (int)V, temperature, topp, rng_state,
+                                                                next_token, emb, emb_dtype == ULM_BF16 ? 1 : 0,
+                                                                (int)D, x);
+  ULM_LAUNCH_CHECK("decode_sample_kernel");
+  return ULM_OK;
 }
