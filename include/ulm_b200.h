@@ -23,6 +23,7 @@
  *   model.py:88-111,   UnifiedBlock.init_state / step, and
  *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
  *   run.c:460-534      run.c sample (argmax / mult / top-p)   -> ulm_decode_head, ulm_decode_sample
+ *   model.py:153-157   output Linear + F.cross_entropy        -> ulm_lm_head_loss_fwd, _bwd
  */
 #ifndef ULM_B200_H
 #define ULM_B200_H
@@ -230,6 +231,26 @@ int ulm_address_bwd(const float* dr, const float* r, const float* den, int norma
                     float* deps, void* work, int64_t B, int64_t T, int64_t D, int64_t M, int prec, void* stream);
 
 int64_t ulm_address_bwd_work_bytes(int64_t B, int64_t T, int64_t D, int64_t M, int prec);
+
+/* ---- the language-model head with its cross-entropy loss (model.py:153-157) ------------------ */
+
+/* loss = F.cross_entropy(h W^T, targets, ignore_index=-1) without writing the (N,V) logits.
+ * h_op (N, ld_h) and w_op (V, ld_w): the final-normed hidden states and the classifier weight in
+ * the operand type of prec (bf16 for ULM_PREC_BF16, fp32 for ULM_PREC_FP32); targets (N,) int64.
+ * Outputs: lse (N,) fp32 (each row's logsumexp, saved for the backward), loss (1,) fp32 (mean over
+ * the rows whose target is not -1; nan when there are none), count (1,) fp32 (that number of rows).
+ * work: ulm_lm_head_work_bytes(N,V,D,prec) bytes, shared with the backward. */
+int ulm_lm_head_loss_fwd(const void* h_op, int64_t ld_h, const void* w_op, int64_t ld_w, const int64_t* targets,
+                         float* lse, float* loss, float* count, void* work, int64_t N, int64_t V, int64_t D,
+                         int prec, void* stream);
+
+/* Backward: dh (N,D) fp32 and dW (V,D) fp32 for the upstream gradient dloss (device scalar);
+ * count and lse as the forward left them. The logits are recomputed. */
+int ulm_lm_head_loss_bwd(const float* dloss, const float* count, const void* h_op, int64_t ld_h, const void* w_op,
+                         int64_t ld_w, const int64_t* targets, const float* lse, float* dh, float* dw, void* work,
+                         int64_t N, int64_t V, int64_t D, int prec, void* stream);
+
+int64_t ulm_lm_head_work_bytes(int64_t N, int64_t V, int64_t D, int prec);
 
 /* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */
 

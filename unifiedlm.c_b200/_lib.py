@@ -45,6 +45,9 @@ SIGNATURES = {
     "ulm_address_bwd": (_I, [_P, _P, _P, _I, _P, _I64, _P, _I, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P,
                              _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_address_bwd_work_bytes": (_I64, [_I64, _I64, _I64, _I64, _I]),
+    "ulm_lm_head_loss_fwd": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "ulm_lm_head_loss_bwd": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "ulm_lm_head_work_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "ulm_decode_prepare_block": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _P]),
     "ulm_decode_reset_block": (_I, [_P] * 6 + [_I64] * 4 + [_P]),
     "ulm_decode_block_step": (_I, [_P] * 7 + [_I] + [_P] * 8 + [_I64] * 4 + [ctypes.c_float, _P]),

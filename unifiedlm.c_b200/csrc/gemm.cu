@@ -114,6 +114,38 @@ __device__ __forceinline__ void epilogue_math(const GemmEpilogue& e, float gl2, 
 #pragma unroll
     for (int i = 0; i < NC; ++i) v[i] += p[i];
   }
+  if (e.kind == EPI_CE_GRAD) {
+    const bool rv = row < e.rows_valid;
+    const int64_t tgt = rv ? e.targets[row] : -1;
+    const float lse = rv ? e.row_lse[row] : 0.f;
+    const float sc = tgt >= 0 ? *e.scale : 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) v[i] = (__expf(v[i] - lse) - ((int64_t)(col0 + i) == tgt ? 1.f : 0.f)) * sc;
+  }
+}
+
+// EPI_LSE over 32 logits of row `row` at col0 (ncols valid): merge into the running (m, s) of the
+// row and record the target's logit
+__device__ __forceinline__ void lse_update32(const GemmEpilogue& e, int row, int col0, int ncols, const float (&v)[32],
+                                             float& m, float& s) {
+  if (row >= e.rows_valid || ncols <= 0) return;
+  float lm = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i < ncols) lm = fmaxf(lm, v[i]);
+  const float nm = fmaxf(m, lm);
+  float acc = s * __expf(m - nm);
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i < ncols) acc += __expf(v[i] - nm);
+  m = nm;
+  s = acc;
+  const int64_t tgt = e.targets[row];
+  if (tgt >= col0 && tgt < col0 + ncols) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if ((int64_t)(col0 + i) == tgt) e.tile_partial[row] = v[i];
+  }
 }
 
 // Direct epilogue: each thread stores its own row segment (used when the output or aux layout does
@@ -349,7 +381,20 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + half * HALF);
     const int col_base = tc.nb * BN + half * HALF;
     float dg_acc = 0.f;
-    if (mode == EPI_MODE_WARP) {
+    if (epi.kind == EPI_LSE) {
+      float m = -INFINITY, ssum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < HALF; c += 32) {
+        float v[32];
+        tmem_ld_32x32(taddr + (uint32_t)c, v);
+        lse_update32(epi, row, col_base + c, min(32, shape.N - (col_base + c)), v, m, ssum);
+      }
+      if (row < shape.M) {
+        float* pp = epi.row_partial + ((int64_t)row * epi.part_ld + 2 * tc.nb + half) * 2;
+        pp[0] = m;
+        pp[1] = ssum;
+      }
+    } else if (mode == EPI_MODE_WARP) {
       const int cw = f32 ? 32 : 64;
 #pragma unroll 1
       for (int c = 0; c < HALF && ok; c += cw) {
@@ -903,6 +948,40 @@ __global__ void __launch_bounds__(256)
   if (shape.K2 > 0)
     segment(A2 + (shape.a2_batched ? (int64_t)tc.b * bsA2 : 0), lda2, B2 + (shape.b2_batched ? (int64_t)tc.b * bsB2 : 0),
             ldb2, 0, shape.K2);
+  if (epi.kind == EPI_LSE) {
+    // per row: (max, sum exp) over this tile's columns, merged across the 16 lanes of the row
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = tc.mb * BM + ty + 16 * i;
+      const bool rv = row < shape.M && row < epi.rows_valid;
+      const int64_t tgt = rv ? epi.targets[row] : -1;
+      float m = -INFINITY, sm = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int col = tc.nb * BN + tx + 16 * jj;
+        if (rv && col < shape.N) {
+          const float v = acc[i][jj];
+          const float nm = fmaxf(m, v);
+          sm = sm * expf(m - nm) + expf(v - nm);
+          m = nm;
+          if ((int64_t)col == tgt) epi.tile_partial[row] = v;
+        }
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, sm, o);
+        const float nm = fmaxf(m, om);
+        sm = (nm == -INFINITY) ? 0.f : sm * expf(m - nm) + os * expf(om - nm);
+        m = nm;
+      }
+      if (tx == 0 && rv) {
+        float* pp = epi.row_partial + ((int64_t)row * epi.part_ld + tc.nb) * 2;
+        pp[0] = m;
+        pp[1] = sm;
+      }
+    }
+    return;
+  }
   const bool decay = epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG;
   const float g = decay ? *epi.g : 0.f;
   float dg_acc = 0.f;
@@ -931,6 +1010,10 @@ __global__ void __launch_bounds__(256)
         const float a = v + reinterpret_cast<const float*>(epi.aux)[col];
         v = a > 0.f ? a * a : 0.f;
         rowsum[i] += v;
+      }
+      if (epi.kind == EPI_CE_GRAD) {
+        const int64_t tgt = row < epi.rows_valid ? epi.targets[row] : -1;
+        v = tgt >= 0 ? (expf(v - epi.row_lse[row]) - ((int64_t)col == tgt ? 1.f : 0.f)) * (*epi.scale) : 0.f;
       }
       const int64_t off = (int64_t)tc.b * epi.out_bstride + (int64_t)row * epi.ldo + col;
       if (epi.out_dtype == ULM_F32)
@@ -1199,11 +1282,16 @@ int run_gemm2(const Operand& A, const Operand& B, const Operand* A2, const Opera
       ULM_REQUIRE(A2->ld >= A2->inner && B2->ld >= B2->inner, "row stride shorter than the row");
     }
   }
-  ULM_REQUIRE(A.ptr && B.ptr && e.out, "null operand or output pointer");
+  ULM_REQUIRE(A.ptr && B.ptr && (e.out || e.kind == EPI_LSE), "null operand or output pointer");
+  ULM_REQUIRE((e.kind != EPI_LSE && e.kind != EPI_CE_GRAD) ||
+                  (e.targets && s.batches == 1 && (e.kind == EPI_CE_GRAD ? e.row_lse && e.scale
+                                                                         : e.row_partial && e.tile_partial)),
+              "cross-entropy epilogue needs targets, one batch row and its row buffers");
   ULM_REQUIRE(s.batches >= 0 && s.M >= 0 && s.N >= 0 && s.K >= 0, "negative extent");
   ULM_REQUIRE(A.dtype == B.dtype, "A and B must have the same element type");
   ULM_REQUIRE(e.out_dtype == ULM_F32 || e.out_dtype == ULM_BF16, "bad output dtype");
-  ULM_REQUIRE(e.kind == EPI_STORE || e.kind == EPI_STORE_ADD || e.kind == EPI_RELU2 || e.g,
+  ULM_REQUIRE(e.kind == EPI_STORE || e.kind == EPI_STORE_ADD || e.kind == EPI_RELU2 || e.kind == EPI_LSE ||
+                  e.kind == EPI_CE_GRAD || e.g,
               "decay epilogue needs g");
   ULM_REQUIRE(e.kind != EPI_RELU2 || e.aux, "EPI_RELU2 needs the bias");
   ULM_REQUIRE(e.kind != EPI_DECAY_DG || (e.aux && e.tile_partial), "EPI_DECAY_DG needs aux and tile_partial");

@@ -21,7 +21,7 @@
 namespace ulm {
 
 enum { CAUSAL_NONE = 0, CAUSAL_KLOWER = 1, CAUSAL_KUPPER = 2, CAUSAL_NLOWER = 3 };
-enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RELU2 = 4 };
+enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RELU2 = 4, EPI_LSE = 5, EPI_CE_GRAD = 6 };
 
 struct GemmShape {
   int batches, M, N, K;
@@ -65,6 +65,16 @@ struct GemmEpilogue {
   // set by the tensor-core launch: stage output chunks in shared memory and write them (and read a
   // tile aux) with TMA tensor copies
   int staged;
+  // cross-entropy epilogues over logits = acc (one batch row; row r has class targets[r], -1 =
+  // ignored):
+  // EPI_LSE: nothing is stored; row_partial[(r * part_ld + j) * 2 + {0, 1}] = (max, sum exp(x - max))
+  //   of the row's logits in column block j (as for EPI_RELU2), tile_partial[r] = the logit of
+  //   column targets[r];
+  // EPI_CE_GRAD: out = (exp(acc - row_lse[r]) - [col == targets[r]]) * (*scale), 0 for ignored rows.
+  const int64_t* targets = nullptr;
+  const float* row_lse = nullptr;
+  const float* scale = nullptr;
+  int rows_valid = 0;  // rows of the product (bound for targets / row_lse reads)
 };
 
 // A matrix operand in global memory: element (b, row, col) of its storage order at

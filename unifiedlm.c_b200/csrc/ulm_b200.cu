@@ -5,3 +5,4 @@
 #include "memory.cu"
 #include "decode.cu"
 #include "address.cu"
+#include "head.cu"

@@ -23,6 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .block import addressed_memory, block_mixer
+from .head import lm_head_loss
 from .kernel import CHUNK
 
 
@@ -151,6 +152,9 @@ class UnifiedLM(nn.Module):
                     p.zero_()
                     p[:, 0, -1] = 1.0
         self.last_loss = None
+        # True: forward(tokens, targets) computes last_loss with the fused head and returns None
+        # instead of the logits (training loops that only read last_loss, as train.py does)
+        self.fused_head = False
 
     def _init_weights(self, module):
         if isinstance(module, nn.Linear):
@@ -170,6 +174,12 @@ class UnifiedLM(nn.Module):
         for layer in self.layers:
             h = layer(h)
         h = self.norm(h)
+        if targets is not None and self.fused_head:
+            # output Linear + cross entropy in one pass that never writes the (B, T, V) logits
+            # (head.lm_head_loss); the logits are not returned in this mode
+            prec = self.layers[0].precision if len(self.layers) else "bf16"
+            self.last_loss = lm_head_loss(h, self.output.weight, targets, precision=prec)
+            return None
         if targets is not None:
             logits = self.output(h)
             self.last_loss = F.cross_entropy(logits.view(-1, logits.size(-1)), targets.view(-1), ignore_index=-1)
