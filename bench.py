@@ -298,6 +298,47 @@ def bench_mixer(dev, W, blocks, precision, steps=5, warmup=3):
             "speedup": round(out["fused"]["tokens_per_s"] / out["unfused"]["tokens_per_s"], 3)}
 
 
+def bench_head(dev, W, steps=5, warmup=3):
+    """Output Linear + cross entropy fwd+bwd at the 110M shape (16 x 1024 rows, V 32000, D 768):
+    the fused head (head.lm_head_loss, no logits written) and the reference's form under bf16
+    autocast (bf16 Linear, then F.cross_entropy), both through autograd."""
+    import torch.nn.functional as F
+    from unifiedlm_c_b200.head import lm_head_loss
+    B, T, D, V = W["B"], W["T"], W["D"], 32000
+    gen = torch.Generator(device=dev).manual_seed(11)
+    h = torch.randn(B * T, D, device=dev, generator=gen).requires_grad_(True)
+    Wt = (torch.randn(V, D, device=dev, generator=gen) * 0.02).requires_grad_(True)
+    tgt = torch.randint(0, V, (B * T,), device=dev, generator=gen)
+
+    def step(fused):
+        if fused:
+            loss = lm_head_loss(h, Wt, tgt)
+        else:
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                logits = F.linear(h, Wt)
+            loss = F.cross_entropy(logits.float(), tgt, ignore_index=-1)
+        loss.backward()
+
+    out = {}
+    for fused in (True, False):
+        for _ in range(warmup):
+            step(fused)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            step(fused)
+        e1.record()
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) / 1e3 / steps
+        out["fused" if fused else "torch_autocast"] = {"tokens_per_s": round(B * T / secs, 1),
+                                                       "ms_per_step": round(secs * 1e3, 3)}
+    return {"metric": "LM head + cross entropy fwd+bwd tokens/s (110M shape, V 32000)",
+            "value": out["fused"]["tokens_per_s"], "unit": "tokens/s", "fused": out["fused"],
+            "torch_autocast": out["torch_autocast"],
+            "speedup": round(out["fused"]["tokens_per_s"] / out["torch_autocast"]["tokens_per_s"], 3)}
+
+
 def runc_decode_baseline(steps=32):
     """The reference's own C decoder (run.c, built with its runomp flags into oracle/_ref/run_omp),
     greedy, at the 110M shape with seeded random weights, all host cores. Returns tokens/s or None."""
@@ -376,6 +417,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
     ap.add_argument("--no-mixer", action="store_true", help="skip the fused-combine measurement")
+    ap.add_argument("--no-head", action="store_true", help="skip the fused LM-head measurement")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
     ap.add_argument("--profile-decode", action="store_true",
@@ -536,6 +578,9 @@ def main():
     mixer = None
     if world == 1 and not args.no_mixer:
         mixer = bench_mixer(dev, W, blocks, args.precision)
+    head = None
+    if world == 1 and not args.no_head:
+        head = bench_head(dev, W)
 
     decode = None
     if not args.no_decode:
@@ -559,7 +604,7 @@ def main():
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
-            "mixer": mixer, "decode": decode}
+            "mixer": mixer, "head": head, "decode": decode}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
