@@ -150,6 +150,12 @@ int ulm_set_gemm_pairs(int enable);
  * previous mode, or -1 (no change) for an unknown mode. */
 int ulm_set_epilogue_mode(int mode);
 
+/* Library-wide choice of the slot-statistics scan kernels for T <= 1024: 1 (default) = persistent
+ * clusters that walk (batch row, 32-slot block) items with the next item's tiles loading while the
+ * current one is scanned; 0 = one cluster per item. Both compute the same values in the same
+ * order. Returns the previous mode, or -1 (no change) for an unknown mode. */
+int ulm_set_scan_mode(int mode);
+
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
  * den: NULL when r holds the read addresses; otherwise r holds their unnormalised form z

@@ -264,3 +264,52 @@ def test_pair_and_single_cta_products_agree(kind):
     if kind == "scores":
         assert rel(outs[0], ref.double().cpu()) < 5e-3
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("shape", [(3, 1000, 200), (16, 1024, 2048), (5, 300, 68), (1, 128, 36)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_scan_modes_agree(shape):
+    """The persistent pipelined scans (ulm_set_scan_mode(1), the default) and the one-cluster-per-item
+    scans compute the same q, c, operand copies, dr and dw bit for bit (same arithmetic in the same
+    order), with and without dq_out; dg differs only in the order its partials are added."""
+    B, T, M = shape
+    gen = torch.Generator().manual_seed(B * T + M)
+    a = torch.randn(B, T, M, generator=gen) + 0.3
+    z = torch.relu(a).square()
+    r = (z / (1.0 + z.sum(-1, keepdim=True))).to(DEV)
+    w = torch.exp(torch.randn(M, generator=gen)).to(DEV)
+    g = torch.tensor([-0.03], device=DEV)
+    dqf = torch.randn(B, T, M, generator=gen).to(DEV)
+    dqo = torch.randn(B, T, M, generator=gen).to(DEV)
+    dk = torch.randn(B, T, M, generator=gen).to(DEV)
+    lib = L.lib()
+    ldo = operand_ld(M)
+    st = L.stream_of(r)
+    part = torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=DEV, dtype=torch.uint8)
+    res = {}
+    for mode in (0, 1):
+        old = lib.ulm_set_scan_mode(mode)
+        try:
+            q, c = torch.empty(B, T, M, device=DEV), torch.empty(B, T, M, device=DEV)
+            qop = torch.empty(B, T, ldo, device=DEV, dtype=torch.bfloat16)
+            kop = torch.empty_like(qop)
+            L.check(lib.ulm_memory_stats_fwd(L.ptr(r), L.ptr(w), L.ptr(g), L.ptr(q), L.ptr(c), L.ptr(qop), L.ptr(kop),
+                                             L.ULM_BF16, ldo, B, T, M, st))
+            outs = [q, c, qop[..., :M].float(), kop[..., :M].float()]
+            for dq_out in (dqo, None):
+                dr, dw, dg = torch.empty(B, T, M, device=DEV), torch.empty(M, device=DEV), torch.empty(1, device=DEV)
+                L.check(lib.ulm_memory_stats_bwd(L.ptr(dqf), L.ptr(dq_out) if dq_out is not None else None, L.ptr(dk),
+                                                 None, None, L.ptr(r), L.ptr(w), L.ptr(g), L.ptr(dr), L.ptr(dw),
+                                                 L.ptr(dg), L.ptr(part), B, T, M, st))
+                torch.cuda.synchronize()
+                outs += [dr.clone(), dw.clone(), dg.clone()]
+            res[mode] = outs
+        finally:
+            lib.ulm_set_scan_mode(old)
+    names = ["q", "c", "qop", "kop", "dr", "dw", "dg", "dr0", "dw0", "dg0"]
+    for name, x0, x1 in zip(names, res[0], res[1]):
+        if name.startswith("dg"):
+            assert abs(float(x0) - float(x1)) <= 1e-6 * abs(float(x0)) + 1e-12, (name, float(x0), float(x1))
+        else:
+            assert torch.equal(x0, x1), (name, float((x0 - x1).abs().max()))
+    assert L.device_error() == 0

@@ -525,21 +525,33 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, normalized ? 0 : 1, wk.da, dt, wk.ld_m,
                                                      wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
   ULM_LAUNCH_CHECK("addr_bwd_kernel");
+  // du = da K and the conv backward stay on the caller's stream (launched first); db, deps and
+  // dK = da^T u run beside them on the side stream
+  cudaStream_t side = nullptr;
+  if (int rc = side_stream(&side)) return rc;
+  if (int rc = stream_after(side, st)) return rc;
+  {
+    Operand A{wk.da, wk.ld_m, rows * wk.ld_m, M, rows, dt, false};
+    Operand Bw{key_w, ld_kw, M * ld_kw, D, M, dt, true};
+    GemmShape s{1, (int)rows, (int)D, (int)M, CAUSAL_NONE};
+    GemmEpilogue e = plain_epilogue(EPI_STORE, ULM_F32, wk.du, D, rows * D);
+    if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
+  }
   if (dt == ULM_BF16 && M % 8 == 0 && wk.ld_m % 8 == 0) {
     dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
-    col_sum_bf16x8_kernel<<<g2, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(wk.da), wk.ld_m, rows, (int)M,
+    col_sum_bf16x8_kernel<<<g2, 256, 0, side>>>(static_cast<const __nv_bfloat16*>(wk.da), wk.ld_m, rows, (int)M,
                                               DB_ROWS_PER_CHUNK, wk.db_part);
     ULM_LAUNCH_CHECK("col_sum_bf16x8_kernel");
   } else {
     dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
     if (dt == ULM_F32)
-      col_sum_kernel<float><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
+      col_sum_kernel<float><<<g2, 256, 0, side>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
     else
-      col_sum_kernel<__nv_bfloat16><<<g2, 256, 0, st>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
+      col_sum_kernel<__nv_bfloat16><<<g2, 256, 0, side>>>(wk.da, wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part);
     ULM_LAUNCH_CHECK("col_sum_kernel");
   }
-  if (int rc = sum_parts(wk.db_part, wk.db_chunks, M, dkey_b, st)) return rc;
-  sum_all_kernel<<<1, 256, 0, st>>>(wk.deps_part, wk.ctas, deps);
+  if (int rc = sum_parts(wk.db_part, wk.db_chunks, M, dkey_b, side)) return rc;
+  sum_all_kernel<<<1, 256, 0, side>>>(wk.deps_part, wk.ctas, deps);
   ULM_LAUNCH_CHECK("sum_all_kernel");
   // dK = da^T u, split over S k ranges of rows (split-K product), then the partials summed in order
   {
@@ -548,16 +560,8 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
     GemmShape s{wk.S, (int)M, (int)D, (int)rows, CAUSAL_NONE};
     s.ksplit = wk.S;
     GemmEpilogue e = plain_epilogue(EPI_STORE, ULM_F32, wk.dk_part, D, M * D);
-    if (int rc = run_gemm(A, Bu, s, e, st)) return rc;
-    if (int rc = sum_parts(wk.dk_part, wk.S, M * D, dkey_w, st)) return rc;
-  }
-  // du = da K
-  {
-    Operand A{wk.da, wk.ld_m, rows * wk.ld_m, M, rows, dt, false};
-    Operand Bw{key_w, ld_kw, M * ld_kw, D, M, dt, true};
-    GemmShape s{1, (int)rows, (int)D, (int)M, CAUSAL_NONE};
-    GemmEpilogue e = plain_epilogue(EPI_STORE, ULM_F32, wk.du, D, rows * D);
-    if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
+    if (int rc = run_gemm(A, Bu, s, e, side)) return rc;
+    if (int rc = sum_parts(wk.dk_part, wk.S, M * D, dkey_w, side)) return rc;
   }
   // through the conv
   dim3 grid((unsigned)wk.chunks, (unsigned)B);
@@ -575,5 +579,5 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
 #undef ULM_CONVB
   ULM_LAUNCH_CHECK("addr_conv_bwd_kernel");
   if (int rc = sum_parts(wk.dconv_part, (int64_t)wk.chunks * B, D * conv_size, dconv_w, st)) return rc;
-  return ULM_OK;
+  return stream_after(st, side);  // join
 }

@@ -15,6 +15,12 @@ namespace ulm {
 void set_error(const char* fmt, ...);
 int sm_count(int device);
 int current_device();
+// Side stream of the current device, for products that can run beside the caller's stream (two
+// persistent kernels then share the machine: the second one's CTAs start as the first one's finish).
+int side_stream(cudaStream_t* out);
+// `to` waits for all work enqueued on `from` so far (an event recorded on `from`); both orders are
+// used: fork (caller -> side) and join (side -> caller). Works under stream capture.
+int stream_after(cudaStream_t to, cudaStream_t from);
 
 // cuTensorMapEncodeTiled from the driver (nullptr if unavailable)
 #include <cudaTypedefs.h>

@@ -18,6 +18,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "gemm.cuh"
 
@@ -47,6 +48,45 @@ int sm_count(int device) {
     cache[device] = n;
   }
   return cache[device];
+}
+
+namespace {
+
+struct SideStreams {
+  std::mutex mu;
+  cudaStream_t stream[64] = {};
+  cudaEvent_t event[64] = {};
+};
+
+SideStreams& side_streams() {
+  static SideStreams s;
+  return s;
+}
+
+}  // namespace
+
+int side_stream(cudaStream_t* out) {
+  const int dev = current_device();
+  ULM_REQUIRE(dev >= 0 && dev < 64, "no current CUDA device (or ordinal >= 64)");
+  SideStreams& ss = side_streams();
+  std::lock_guard<std::mutex> lock(ss.mu);
+  if (!ss.stream[dev]) {
+    ULM_CUDA_TRY(cudaStreamCreateWithFlags(&ss.stream[dev], cudaStreamNonBlocking));
+    ULM_CUDA_TRY(cudaEventCreateWithFlags(&ss.event[dev], cudaEventDisableTiming));
+  }
+  *out = ss.stream[dev];
+  return ULM_OK;
+}
+
+int stream_after(cudaStream_t to, cudaStream_t from) {
+  const int dev = current_device();
+  ULM_REQUIRE(dev >= 0 && dev < 64, "no current CUDA device (or ordinal >= 64)");
+  SideStreams& ss = side_streams();
+  std::lock_guard<std::mutex> lock(ss.mu);  // one event per device: record and wait as one step
+  ULM_REQUIRE(ss.event[dev] != nullptr, "stream_after before side_stream on this device");
+  ULM_CUDA_TRY(cudaEventRecord(ss.event[dev], from));
+  ULM_CUDA_TRY(cudaStreamWaitEvent(to, ss.event[dev], 0));
+  return ULM_OK;
 }
 
 namespace {
@@ -354,6 +394,11 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
     StatsScratch sc = carve_stats_scratch(partial, B, M);
     const int64_t n_tiles = decay_dg_partials(B, T);
     ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
+    // dv = P^T do and dk = dS^T q run on the side stream beside dS and dq; dS and dq are launched
+    // first, so the chain dS -> dq -> statistics gets the SMs first
+    cudaStream_t side = nullptr;
+    if (int rc = side_stream(&side)) return rc;
+    if (int rc = stream_after(side, st)) return rc;
     {
       Operand A{doop, ldd, T * ldd, D, T, dt, false};
       Operand Bo{vop, ldd, T * ldd, D, T, dt, false};
@@ -366,6 +411,8 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
       e.vec_ok = e.vec_ok && is_aligned16(P);
       if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
     }
+    if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, side)) return rc;
+    if (int rc = stream_after(side, st)) return rc;  // dS is ready for dk
     {
       // dq = dS k, with the gradient of the q output added in the epilogue: the statistics backward
       // only needs the sum (fast_identity = 0 below)
@@ -381,8 +428,8 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
       }
       if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
     }
-    if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
-    if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, do_dtype, 1, B, T, D, prec, stream)) return rc;
+    if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, side)) return rc;
+    if (int rc = stream_after(st, side)) return rc;  // join: dk and dv are done
     ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
     // without a saved c the statistics backward rebuilds q and c from r (TMA scan path)
     return stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
@@ -480,6 +527,10 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   const int64_t n_tiles = decay_dg_partials(B, T);
   ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
+  // side stream: dv beside dS, dk beside dq, then G = dy^T q beside the statistics backward
+  cudaStream_t side = nullptr;
+  if (int rc = side_stream(&side)) return rc;
+  if (int rc = stream_after(side, st)) return rc;
   {
     Operand A{doop, ldd, T * ldd, D, T, dt, false};
     Operand Bo{vop, ldd, T * ldd, D, T, dt, false};
@@ -492,6 +543,8 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     e.vec_ok = e.vec_ok && is_aligned16(P);
     if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
   }
+  if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, dv_dtype, 1, B, T, D, prec, side)) return rc;
+  if (int rc = stream_after(side, st)) return rc;  // dS is ready for dk
   combine_weight_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 8 * 148), 256, 0, st>>>(mu, w, mw, dt, ldm,
                                                                                              (int)D, (int)M);
   ULM_LAUNCH_CHECK("combine_weight_kernel");
@@ -506,8 +559,8 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, dqf, M, T * M, nullptr);
     if (int rc = run_gemm2(A, Bk, &A2, &B2, s, e, st)) return rc;
   }
-  if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, stream)) return rc;
-  if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, dv_dtype, 1, B, T, D, prec, stream)) return rc;
+  if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, side)) return rc;
+  if (int rc = stream_after(st, side)) return rc;  // dk and dv are done
   if (int rc = stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
                              sc.tiles, n_tiles, st))
     return rc;
@@ -520,12 +573,13 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
     s.ksplit = S;
     GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
-    if (int rc = run_gemm(A, Bq, s, e, st)) return rc;
+    if (int rc = run_gemm(A, Bq, s, e, side)) return rc;
     float* dw_part = gpart + 8 * D * M;
     const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
-    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, st>>>(gpart, S, mu, w, dmu, dw_part,
-                                                                                (int)D, (int)M);
+    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, side>>>(gpart, S, mu, w, dmu, dw_part,
+                                                                                  (int)D, (int)M);
     ULM_LAUNCH_CHECK("combine_grad_kernel");
+    if (int rc = stream_after(st, side)) return rc;  // join before dw gets the combine's share
     add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(dw_part, (int)row_blocks, M, dw);
     ULM_LAUNCH_CHECK("add_parts_kernel");
   }

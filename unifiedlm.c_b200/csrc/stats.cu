@@ -518,6 +518,401 @@ __global__ void __launch_bounds__(32 * WARPS)
   if (threadIdx.x == 0) part_dg[(int64_t)b * gridDim.x + blockIdx.x] = red_dg[0];
 }
 
+// ---- persistent, pipelined cluster scans ---------------------------------------------------------
+// The kernels above give every (batch row, 32 slots) item its own cluster: a CTA loads its tiles,
+// scans, exchanges carries and stores, so its loads never overlap its own compute. Here a cluster
+// of C CTAs (C = cdiv(T, R)) stays resident and walks a list of items (item = batch row b and slot
+// block m0; cluster k takes items k, k + G, k + 2G, ... for G clusters), with the TMA loads of the
+// next STAGES - 1 items in flight while the current one is scanned. Per item the arithmetic is that
+// of the kernels above, in the same order (identical results). Carry slots are reused from item to
+// item. In the backward a rank cannot run ahead of the peers it exchanges with: its next forward
+// total waits for their reverse totals of the current item and vice versa, and two slots per
+// direction (alternating by item) keep every slot unread-safe. The forward has no reply, so after
+// reading its carries each CTA arrives on the cluster barrier and waits on it before its next send.
+// Each exchange mbarrier is armed (expect_tx) before any total of its item can be sent, and re-armed
+// for its next use only after every thread of the CTA has passed the wait on the current one.
+// Every mbarrier wait is bounded; after a timeout the CTA records the error and keeps the protocol
+// going with short limits, so its peers are never left waiting.
+
+constexpr uint64_t SCAN_SHORT_WAIT_NS = 10000000ull;  // waits after an error: 10 ms
+
+// Row scales of the next item, in two steps so that the global load's latency overlaps the current
+// item: thread i (i <= n) loads den of row t_first + i early (den_prefetch) and stores the scale
+// later (den_store): 1 / den, or 1 without den, 0 outside [0, T), as fill_row_scales.
+__device__ __forceinline__ float den_prefetch(const float* __restrict__ den, int b, int T, int t_first, int n) {
+  const int i = threadIdx.x, t = t_first + i;
+  return (den && i <= n && t >= 0 && t < T) ? den[(int64_t)b * T + t] : 0.f;
+}
+__device__ __forceinline__ void den_store(float* sinv, const float* den, float dv, int T, int t_first, int n) {
+  const int i = threadIdx.x, t = t_first + i;
+  if (i <= n) sinv[i] = den ? ((t >= 0 && t < T) ? __frcp_rn(dv) : 0.f) : 1.f;
+}
+
+template <int SEG, int WARPS, int STAGES, typename OpT>
+__global__ void __launch_bounds__(32 * WARPS)
+    stats_fwd_pipe_kernel(const __grid_constant__ CUtensorMap map_r, const __grid_constant__ CUtensorMap map_r1,
+                          const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
+                          float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
+                          void* __restrict__ kop, int64_t ldop, int B, int T, int M) {
+  constexpr int R = SEG * WARPS;
+  constexpr int STAGE_FLOATS = (R + 1) * 32;
+  extern __shared__ __align__(128) float tile[];
+  __shared__ __align__(8) uint64_t full[STAGES];
+  __shared__ __align__(8) uint64_t xbar;
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float ctot[SCAN_MAX_CLUSTER][32];
+  __shared__ float sinv[2][R + 1];  // row scales of the current and the next item
+  __shared__ int ok_flag;
+  static_assert(32 * WARPS > R, "one thread per row scale");
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int cta_t0 = cr * R;
+  const int nmb = (M + 31) / 32;
+  const int n_items = B * nmb;
+  const int G = (int)gridDim.x / C;
+  const int k0 = (int)blockIdx.x / C;
+  auto issue = [&](int j) {
+    const int item = k0 + j * G;
+    if (item >= n_items) return;
+    const int bb = item / nmb, mm0 = (item % nmb) * 32;
+    float* st = tile + (j % STAGES) * STAGE_FLOATS;
+    uint64_t* bar = &full[j % STAGES];
+    mbar_arrive_expect_tx(bar, (uint32_t)STAGE_FLOATS * 4u);
+    tma_load_3d(&map_r, st, bar, mm0, cta_t0 - 1, bb);
+    tma_load_3d(&map_r1, st + R * 32, bar, mm0, cta_t0 + R - 1, bb);
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    mbar_init(&xbar, 1);
+    fence_barrier_init();
+    if (cr > 0) mbar_arrive_expect_tx(&xbar, (uint32_t)cr * 128u);  // armed for the first item
+    ok_flag = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int j = 0; j < STAGES; ++j) issue(j);
+  // the barriers of every CTA are initialised before any CTA sends into them
+  __syncwarp();
+  cluster_sync_all();
+  const float gg = *g;
+  const float lam = expf(gg);
+  const float lam_seg = expf(gg * (float)SEG);
+  const float lam_cta = expf(gg * (float)R);
+  float w_cur = 0.f;
+  if (k0 < n_items) {
+    const int m_first = (k0 % nmb) * 32 + lane;
+    w_cur = m_first < M ? w[m_first] : 0.f;
+    den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
+  }
+  for (int j = 0;; ++j) {
+    const int item = k0 + j * G;
+    if (item >= n_items) break;
+    const int b = item / nmb;
+    const int m = (item % nmb) * 32 + lane;
+    const float* xs = tile + (j % STAGES) * STAGE_FLOATS;
+    // the next item's row scales and prior masses: loaded now, used after this item
+    const int item_n = item + G;
+    const bool has_next = item_n < n_items;
+    const int m_n = (item_n % nmb) * 32 + lane;
+    const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
+    const float w_n = (has_next && m_n < M) ? w[m_n] : 0.f;
+    const uint64_t lim = ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS;
+    if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, lim)) {
+      raise_device_error(DEVERR_SCAN_TMA_WAIT);
+      ok_flag = 0;
+    }
+    __syncthreads();
+    const float* xt = xs + (wp * SEG) * 32 + lane;  // xt[i * 32]: k of position t0 + i, r of t0 + i - 1
+    const float* si = sinv[j & 1] + wp * SEG;
+    float run = 0.f;
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, xt[i * 32] * si[i]);
+    warp_sum[wp][lane] = run;
+    __syncthreads();
+    __syncwarp();
+    if (j > 0) cluster_wait_acquire();  // every CTA has read the previous item's totals
+    if (wp == 0) {
+      float tot = 0.f;
+      for (int jj = 0; jj < WARPS; ++jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
+      const uint32_t slot = smem_u32(&ctot[cr][lane]), xb = smem_u32(&xbar);
+      for (int jj = cr + 1; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
+    }
+    if (cr > 0) {
+      if (!mbar_wait_bounded(&xbar, (uint32_t)j & 1u, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+        raise_device_error(DEVERR_SCAN_TMA_WAIT);
+        ok_flag = 0;
+      }
+      // armed for the next item: its totals are sent only after this CTA's cluster arrive below
+      if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar, (uint32_t)cr * 128u);
+    }
+    float carry = 0.f;
+    for (int jj = 0; jj < cr; ++jj) carry = fmaf(carry, lam_cta, ctot[jj][lane]);
+    for (int jj = 0; jj < wp; ++jj) carry = fmaf(carry, lam_seg, warp_sum[jj][lane]);
+    __syncwarp();  // the aligned cluster barrier wants converged warps (the waits above spin per thread)
+    cluster_arrive_release();  // this CTA's totals slots may be written again
+    if (m < M) {
+      const float wm = w_cur;
+      const int t0 = cta_t0 + wp * SEG;
+      const int64_t row = (int64_t)b * T + t0;
+      float* qp = q ? q + row * M + m : nullptr;
+      float* cp = c ? c + row * M + m : nullptr;
+      const int64_t io = row * ldop + m;
+      run = carry;
+      float kk = xt[0] * si[0];
+#pragma unroll
+      for (int i = 0; i < SEG; ++i) {
+        const float rv = xt[(i + 1) * 32] * si[i + 1];
+        if (t0 + i < T) {
+          run = fmaf(lam, run, kk);
+          const float cc = wm + run;
+          const float qq = rv * fast_rcp(cc);
+          if (qp) qp[(int64_t)i * M] = qq;
+          if (cp) cp[(int64_t)i * M] = cc;
+          store_op<OpT>(qop, io + (int64_t)i * ldop, qq);
+          store_op<OpT>(kop, io + (int64_t)i * ldop, kk);
+        }
+        kk = rv;
+      }
+    }
+    if (has_next) den_store(sinv[(j + 1) & 1], den, den_n, T, cta_t0 - 1, R);  // last read in item j - 1
+    w_cur = w_n;
+    __syncthreads();  // the stage, sinv[j & 1] and warp_sum are free again
+    if (threadIdx.x == 0) {
+      fence_proxy_async_smem();
+      issue(j + STAGES);
+    }
+  }
+  // pairs the last arrive; no CTA leaves while a peer may still send into its shared memory
+  __syncwarp();
+  if (k0 < n_items) cluster_wait_acquire();
+}
+
+// Backward with q and c rebuilt from the r tile (the RECOMPUTE form of stats_bwd_tma_kernel).
+// Stage layout: dqf (R rows), dk (R + 1 rows), r (R + 1 rows from position cta_t0 - 1), dq_out (R
+// rows, when given). part_dg gets one partial per CTA (its items' sum); part_dw one row per (b, rank).
+template <int SEG, int WARPS, int STAGES>
+__global__ void __launch_bounds__(32 * WARPS, 2)
+    stats_bwd_pipe_kernel(const __grid_constant__ CUtensorMap map_dqf, const __grid_constant__ CUtensorMap map_dqo,
+                          const __grid_constant__ CUtensorMap map_dk, const __grid_constant__ CUtensorMap map_r,
+                          const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
+                          float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int B,
+                          int T, int M, int has_dqo, int fast_identity) {
+  constexpr int R = SEG * WARPS;
+  constexpr int TILE = R * 32;
+  extern __shared__ __align__(128) float tile[];
+  __shared__ __align__(8) uint64_t full[STAGES];
+  __shared__ __align__(8) uint64_t xbar_f[2];  // lower ranks' forward totals of the item have arrived
+  __shared__ __align__(8) uint64_t xbar_r[2];  // higher ranks' reverse totals have arrived
+  __shared__ float warp_sum[WARPS][32];
+  __shared__ float warp_dw[WARPS][32];
+  __shared__ float ctot_f[2][SCAN_MAX_CLUSTER][32];
+  __shared__ float ctot_r[2][SCAN_MAX_CLUSTER][32];
+  __shared__ double red_dg[32 * WARPS];
+  __shared__ float sinv[2][R + 1];  // row scales of the current and the next item
+  __shared__ int ok_flag;
+  static_assert(32 * WARPS > R, "one thread per row scale");
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int cr = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int cta_t0 = cr * R;
+  const int nmb = (M + 31) / 32;
+  const int n_items = B * nmb;
+  const int G = (int)gridDim.x / C;
+  const int k0 = (int)blockIdx.x / C;
+  const int stage_floats = (3 * R + 2 + (has_dqo ? R : 0)) * 32;
+  auto issue = [&](int j) {
+    const int item = k0 + j * G;
+    if (item >= n_items) return;
+    const int bb = item / nmb, mm0 = (item % nmb) * 32;
+    float* st = tile + (j % STAGES) * stage_floats;
+    uint64_t* bar = &full[j % STAGES];
+    mbar_arrive_expect_tx(bar, (uint32_t)stage_floats * 4u);
+    tma_load_3d(&map_dqf, st, bar, mm0, cta_t0, bb);
+    tma_load_3d(&map_dk, st + TILE, bar, mm0, cta_t0, bb);  // R + 1 rows: the next CTA's first one too
+    tma_load_3d(&map_r, st + 2 * TILE + 32, bar, mm0, cta_t0 - 1, bb);
+    if (has_dqo) tma_load_3d(&map_dqo, st + 3 * TILE + 64, bar, mm0, cta_t0, bb);
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&xbar_f[s], 1);
+      mbar_init(&xbar_r[s], 1);
+    }
+    fence_barrier_init();
+    // armed for the first two items; each is re-armed for the item after next once read
+    for (int s = 0; s < 2; ++s) {
+      if (cr > 0) mbar_arrive_expect_tx(&xbar_f[s], (uint32_t)cr * 128u);
+      if (cr < C - 1) mbar_arrive_expect_tx(&xbar_r[s], (uint32_t)(C - 1 - cr) * 128u);
+    }
+    ok_flag = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int j = 0; j < STAGES; ++j) issue(j);
+  // the barriers of every CTA are initialised before any CTA sends into them
+  __syncwarp();
+  cluster_sync_all();
+  const float gg = *g;
+  const float lam = expf(gg);
+  const float lam_seg = expf(gg * (float)SEG);
+  const float lam_cta = expf(gg * (float)R);
+  const float t_mid = 0.5f * (float)(T - 1);
+  const int t0 = cta_t0 + wp * SEG;
+  const int o = (wp * SEG) * 32 + lane;
+  double dg_acc = 0.0;
+  float w_cur = 0.f;
+  if (k0 < n_items) {
+    const int m_first = (k0 % nmb) * 32 + lane;
+    w_cur = m_first < M ? w[m_first] : 0.f;
+    den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
+  }
+  for (int j = 0;; ++j) {
+    const int item = k0 + j * G;
+    if (item >= n_items) break;
+    const int b = item / nmb;
+    const int m = (item % nmb) * 32 + lane;
+    const bool valid = m < M;
+    const int xp = j & 1;
+    const uint32_t xph = (uint32_t)(j >> 1) & 1u;
+    const float* st = tile + (j % STAGES) * stage_floats;
+    // the next item's row scales and prior masses: loaded now, used after this item
+    const int item_n = item + G;
+    const bool has_next = item_n < n_items;
+    const int m_n = (item_n % nmb) * 32 + lane;
+    const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
+    const float w_n = (has_next && m_n < M) ? w[m_n] : 0.f;
+    if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u,
+                           ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+      raise_device_error(DEVERR_SCAN_TMA_WAIT);
+      ok_flag = 0;
+    }
+    __syncthreads();
+    const float* s_dqf = st + o;
+    const float* s_dk = st + TILE + o;
+    const float* s_k = st + 2 * TILE + 32 + o;  // k_t = r_{t-1}
+    const float* s_r = st + 2 * TILE + 64 + o;  // r_t
+    const float* s_dqo = st + 3 * TILE + 64 + o;
+    const float* si = sinv[j & 1] + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
+    const float wm = w_cur;
+
+    // forward scan of k to rebuild n_t (as stats_fwd_pipe_kernel)
+    float run = 0.f;
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_k[i * 32] * si[i]);
+    warp_sum[wp][lane] = run;
+    __syncthreads();
+    if (wp == 0) {
+      float tot = 0.f;
+      for (int jj = 0; jj < WARPS; ++jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
+      const uint32_t slot = smem_u32(&ctot_f[xp][cr][lane]), xb = smem_u32(&xbar_f[xp]);
+      for (int jj = cr + 1; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
+    }
+    if (cr > 0 && !mbar_wait_bounded(&xbar_f[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+      raise_device_error(DEVERR_SCAN_TMA_WAIT);
+      ok_flag = 0;
+    }
+    float n = 0.f;
+    for (int jj = 0; jj < cr; ++jj) n = fmaf(n, lam_cta, ctot_f[xp][jj][lane]);
+    for (int jj = 0; jj < wp; ++jj) n = fmaf(n, lam_seg, warp_sum[jj][lane]);
+    __syncthreads();  // warp_sum is reused below; every thread is past the wait on xbar_f[xp]
+    if (threadIdx.x == 0 && cr > 0) mbar_arrive_expect_tx(&xbar_f[xp], (uint32_t)cr * 128u);
+
+    float dw_acc = 0.f, dg_f = 0.f;
+    float drd_v[SEG], dc_v[SEG];
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      const int t = t0 + i;
+      n = fmaf(lam, n, s_k[i * 32] * si[i]);
+      float cc = wm + n;
+      float inv = fast_rcp(cc);
+      float qq = (s_r[i * 32] * si[i + 1]) * inv;
+      if (!(t < T && valid)) {
+        cc = 1.f;
+        qq = 0.f;
+        inv = 1.f;
+      }
+      const float dqfv = s_dqf[i * 32];
+      const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
+      const float drd = dq * inv;
+      const float dc = -drd * qq;
+      drd_v[i] = drd;
+      dc_v[i] = dc;
+      dw_acc += dc;
+      float term = dc * (cc - wm);
+      if (fast_identity) term += qq * dqfv;
+      dg_f = fmaf((float)t - t_mid, term, dg_f);
+    }
+    run = 0.f;
+#pragma unroll
+    for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dc_v[i]);
+    warp_sum[wp][lane] = run;
+    warp_dw[wp][lane] = dw_acc;
+    __syncthreads();
+    if (wp == 0) {
+      float tot = 0.f;
+      for (int jj = WARPS - 1; jj >= 0; --jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
+      const uint32_t slot = smem_u32(&ctot_r[xp][cr][lane]), xb = smem_u32(&xbar_r[xp]);
+      for (int jj = 0; jj < cr; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
+      if (valid) {
+        float s2 = 0.f;
+        for (int jj = 0; jj < WARPS; ++jj) s2 += warp_dw[jj][lane];
+        part_dw[((int64_t)b * C + cr) * M + m] = s2;
+      }
+    }
+    if (cr < C - 1 && !mbar_wait_bounded(&xbar_r[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+      raise_device_error(DEVERR_SCAN_TMA_WAIT);
+      ok_flag = 0;
+    }
+    float carry = 0.f;  // dkc at position t0 + SEG
+    for (int jj = C - 1; jj > cr; --jj) carry = fmaf(carry, lam_cta, ctot_r[xp][jj][lane]);
+    for (int jj = WARPS - 1; jj > wp; --jj) carry = fmaf(carry, lam_seg, warp_sum[jj][lane]);
+    dg_acc += (double)dg_f;
+    if (valid) {
+      const int64_t base = (int64_t)b * T * M + m;
+      const int t_end = t0 + SEG;
+      float dkt_next = (t_end < T) ? s_dk[SEG * 32] + carry : 0.f;  // the dk tile holds row t_end
+      run = carry;
+      float dg_s = 0.f;
+#pragma unroll
+      for (int i = SEG - 1; i >= 0; --i) {
+        const int t = t0 + i;
+        if (t < T) {
+          const float dkv = s_dk[i * 32];
+          const float kv = s_k[i * 32] * si[i];
+          run = fmaf(lam, run, dc_v[i]);  // dkc_t
+          dr[base + (int64_t)t * M] = drd_v[i] + dkt_next;
+          dkt_next = dkv + run;
+          float term = -kv * run;
+          if (fast_identity) term -= kv * dkv;
+          dg_s = fmaf((float)t - t_mid, term, dg_s);
+        }
+      }
+      dg_acc += (double)dg_s;
+    }
+    if (has_next) den_store(sinv[(j + 1) & 1], den, den_n, T, cta_t0 - 1, R);  // last read in item j - 1
+    w_cur = w_n;
+    __syncthreads();  // the stage, sinv[j & 1], warp_sum and warp_dw are free again
+    if (threadIdx.x == 0) {
+      if (cr < C - 1) mbar_arrive_expect_tx(&xbar_r[xp], (uint32_t)(C - 1 - cr) * 128u);
+      fence_proxy_async_smem();
+      issue(j + STAGES);
+    }
+  }
+  red_dg[threadIdx.x] = dg_acc;
+  __syncthreads();
+  for (int stride = 16 * WARPS; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) red_dg[threadIdx.x] += red_dg[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part_dg[blockIdx.x] = red_dg[0];
+  // no CTA leaves while a peer may still send into its shared memory
+  __syncwarp();
+  cluster_sync_all();
+}
+
 // 3-D map over an fp32 (B, T, M) array with a 32-slot x `rows` box, no swizzle.
 inline int make_rows_tmap(CUtensorMap* map, const float* ptr, int64_t B, int64_t T, int64_t M, int rows) {
   auto fn = encode_tiled();
@@ -570,6 +965,56 @@ int launch_cluster_smem(K kernel, dim3 grid, int threads, int cluster_x, size_t 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+  return ULM_OK;
+}
+
+// library-wide choice of scan kernels (ulm_set_scan_mode): 1 = persistent pipelined, 0 = per item
+static int g_scan_mode = 1;
+constexpr int SCAN_PIPE_STAGES = 2;  // backward: two stages of up to 66 KB
+constexpr int SCAN_FWD_STAGES = 3;   // forward: three stages of 16.5 KB
+
+// Clusters of a persistent scan that fit on the device at once (cached per device, kernel and
+// shared-memory size), at most n_items.
+template <typename K>
+int pipe_clusters(K kernel, int threads, int C, size_t smem, int64_t n_items, int* out) {
+  struct Entry {
+    int dev, C;
+    const void* fn;
+    size_t smem;
+    int n;
+  };
+  static std::mutex mu;
+  static Entry cache[32];
+  static int n_cache = 0;
+  const int dev = current_device();
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n_cache; ++i)
+      if (cache[i].dev == dev && cache[i].C == C && cache[i].fn == (const void*)kernel && cache[i].smem == smem) {
+        *out = (int)std::min<int64_t>(cache[i].n, n_items);
+        return ULM_OK;
+      }
+  }
+  ULM_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  ULM_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+  ULM_REQUIRE(n > 0, "no cluster of %d CTAs with %zu bytes of shared memory fits on the device", C, smem);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (n_cache < 32) cache[n_cache++] = Entry{dev, C, (const void*)kernel, smem, n};
+  }
+  *out = (int)std::min<int64_t>(n, n_items);
   return ULM_OK;
 }
 
@@ -655,18 +1100,34 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     const size_t smem = (size_t)((recompute ? 3 * R + 1 : 5 * R) + (dq_out ? R : 0)) * 32 * 4;
     const int hq = dq_out ? 1 : 0;
     int rc;
+    if (g_scan_mode == 1 && recompute && tp.warps == 8) {
+      const int64_t n_items = B * cdiv(M, 32);
+      const size_t smem_p = (size_t)(3 * R + 2 + (dq_out ? R : 0)) * 32 * 4 * SCAN_PIPE_STAGES;
+      auto kern = stats_bwd_pipe_kernel<16, 8, SCAN_PIPE_STAGES>;
+      CUtensorMap mdk1;
+      if ((rc = make_rows_tmap(&mdk1, dk, B, T, M, R + 1))) return rc;
+      int nc = 0;
+      if ((rc = pipe_clusters(kern, 256, C, smem_p, n_items, &nc))) return rc;
+      const dim3 pgrid((unsigned)(nc * C));
+      rc = launch_cluster_smem(kern, pgrid, 256, C, smem_p, st, mdqf, mdqo, mdk1, mr, den, w, g, dr, sc.part_dw,
+                               sc.part_dg, (int)B, (int)T, (int)M, hq, fast_identity);
+      if (rc) return rc;
+      n_dg = pgrid.x;  // one partial per CTA (at most B x cdiv(M, 32) x 8)
+      dw_rows = B * C;
+    } else {
 #define ULM_BWD_TMA(W, RC)                                                                                       \
   rc = launch_cluster_smem(stats_bwd_tma_kernel<16, W, RC>, grid, 32 * W, C, smem, st, mdqf, mdqo, mq, mc, mdk, mr, \
                            dk, den, w, g, dr, sc.part_dw, sc.part_dg, (int)T, (int)M, hq, fast_identity)
-    if (tp.warps == 8) {
-      if (recompute) ULM_BWD_TMA(8, true); else ULM_BWD_TMA(8, false);
-    } else {
-      if (recompute) ULM_BWD_TMA(16, true); else ULM_BWD_TMA(16, false);
-    }
+      if (tp.warps == 8) {
+        if (recompute) ULM_BWD_TMA(8, true); else ULM_BWD_TMA(8, false);
+      } else {
+        if (recompute) ULM_BWD_TMA(16, true); else ULM_BWD_TMA(16, false);
+      }
 #undef ULM_BWD_TMA
-    if (rc) return rc;
-    n_dg = B * (int64_t)grid.x;
-    dw_rows = B * C;
+      if (rc) return rc;
+      n_dg = B * (int64_t)grid.x;
+      dw_rows = B * C;
+    }
   } else {
     const int64_t groups = cdiv(M, 32);
     dim3 grid((unsigned)groups, (unsigned)B);
@@ -719,6 +1180,20 @@ int stats_fwd_run(const float* r, const float* den, const float* w, const float*
     dim3 grid((unsigned)(cdiv(M, 32) * C), (unsigned)B);
     const size_t smem = (size_t)(R + 1) * 32 * 4;
     const bool bf = op_dtype == ULM_BF16;
+    if (g_scan_mode == 1 && tp.warps == 8) {
+      const int64_t n_items = B * cdiv(M, 32);
+      const size_t smem_p = smem * SCAN_FWD_STAGES;
+      auto kb = stats_fwd_pipe_kernel<16, 8, SCAN_FWD_STAGES, __nv_bfloat16>;
+      auto kf = stats_fwd_pipe_kernel<16, 8, SCAN_FWD_STAGES, float>;
+      int nc = 0;
+      if (int rc = bf ? pipe_clusters(kb, 256, C, smem_p, n_items, &nc) : pipe_clusters(kf, 256, C, smem_p, n_items, &nc))
+        return rc;
+      const dim3 pgrid((unsigned)(nc * C));
+      return bf ? launch_cluster_smem(kb, pgrid, 256, C, smem_p, st, mr, mr1, den, w, g, q, c, qop, kop, ld_op, (int)B,
+                                      (int)T, (int)M)
+                : launch_cluster_smem(kf, pgrid, 256, C, smem_p, st, mr, mr1, den, w, g, q, c, qop, kop, ld_op, (int)B,
+                                      (int)T, (int)M);
+    }
     if (tp.warps == 8)
       return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, mr1, den, w,
                                       g, q, c, qop, kop, ld_op, (int)T, (int)M)
@@ -821,6 +1296,13 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // every scratch entry the kernels read is written earlier in the same call: nothing to clear
   return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
+}
+
+extern "C" int ulm_set_scan_mode(int mode) {
+  if (mode < 0 || mode > 1) return -1;
+  const int old = g_scan_mode;
+  g_scan_mode = mode;
+  return old;
 }
 
 extern "C" int ulm_memory_needs_c(int64_t T, int64_t M) {
