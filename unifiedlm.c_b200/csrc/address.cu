@@ -67,7 +67,8 @@ __device__ __forceinline__ float4 fma4(float4 w, float4 x, float4 acc) {
   return make_float4(fmaf(w.x, x.x, acc.x), fmaf(w.y, x.y, acc.y), fmaf(w.z, x.z, acc.z), fmaf(w.w, x.w, acc.w));
 }
 
-constexpr int CONV_ROWS = 64;  // positions per CTA of the conv kernels
+constexpr int CONV_ROWS = 32;    // positions per CTA of the conv kernels
+constexpr int CONV_UNROLL = 4;   // positions per step of a thread's sliding window (loads in flight)
 constexpr int CONV_MAXK = 8;
 
 // u[b,t,d] = sum_j conv_w[d, j] * h[b, t-K+1+j, d] (zero before the sequence start).
@@ -79,26 +80,34 @@ __global__ void __launch_bounds__(256)
                      int64_t ld_u, int T, int D) {
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * CONV_ROWS, t1 = min(T, t0 + CONV_ROWS);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int d4 = threadIdx.x * 4; d4 < D; d4 += blockDim.x * 4) {
     float4 w[K];
 #pragma unroll
     for (int j = 0; j < K; ++j)
       w[j] = make_float4(conv_w[(d4 + 0) * K + j], conv_w[(d4 + 1) * K + j], conv_w[(d4 + 2) * K + j],
                          conv_w[(d4 + 3) * K + j]);
-    float4 win[K];  // win[j] = h[t-K+1+j]
+    float4 win[K - 1 + CONV_UNROLL];  // win[j] = h[t - K + 1 + j] for the CONV_UNROLL positions from t
 #pragma unroll
     for (int j = 0; j < K - 1; ++j) {
       const int tt = t0 - K + 1 + j;
-      win[j] = tt >= 0 ? ld4<InT>(h, ((int64_t)b * T + tt) * D + d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      win[j] = tt >= 0 ? ld4<InT>(h, ((int64_t)b * T + tt) * D + d4) : z4;
     }
-    for (int t = t0; t < t1; ++t) {
-      win[K - 1] = ld4<InT>(h, ((int64_t)b * T + t) * D + d4);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  #pragma unroll
-    for (int j = 0; j < K; ++j) acc = fma4(w[j], win[j], acc);
-      st4(u, ((int64_t)b * T + t) * ld_u + d4, acc, u_dtype);
-  #pragma unroll
-    for (int j = 0; j + 1 < K; ++j) win[j] = win[j + 1];
+    for (int t = t0; t < t1; t += CONV_UNROLL) {
+#pragma unroll
+      for (int i = 0; i < CONV_UNROLL; ++i)  // all loads of the step first
+        win[K - 1 + i] = t + i < t1 ? ld4<InT>(h, ((int64_t)b * T + t + i) * D + d4) : z4;
+#pragma unroll
+      for (int i = 0; i < CONV_UNROLL; ++i) {
+        if (t + i < t1) {
+          float4 acc = z4;
+#pragma unroll
+          for (int j = 0; j < K; ++j) acc = fma4(w[j], win[i + j], acc);
+          st4(u, ((int64_t)b * T + t + i) * ld_u + d4, acc, u_dtype);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) win[j] = win[CONV_UNROLL + j];
     }
   }
 }
@@ -312,8 +321,9 @@ __global__ void __launch_bounds__(256)
                          conv_w[(d4 + 3) * K + j]);
       acc[j] = z4;
     }
-    float4 hw[K];   // hw[j] = h[t-K+1+j]
-    float4 dw[K];   // dw[j] = du[t+j]
+    // for the CONV_UNROLL positions from t: hw[j] = h[t - K + 1 + j], dw[j] = du[t + j]
+    float4 hw[K - 1 + CONV_UNROLL];
+    float4 dw[K - 1 + CONV_UNROLL];
 #pragma unroll
     for (int j = 0; j < K - 1; ++j) {
       const int tt = t0 - K + 1 + j;
@@ -321,20 +331,28 @@ __global__ void __launch_bounds__(256)
       const int tf = t0 + j;
       dw[j] = tf < T ? *reinterpret_cast<const float4*>(du + ((int64_t)b * T + tf) * D + d4) : z4;
     }
-    for (int t = t0; t < t1; ++t) {
-      hw[K - 1] = ld4<InT>(h, ((int64_t)b * T + t) * D + d4);
-      const int tf = t + K - 1;
-      dw[K - 1] = tf < T ? *reinterpret_cast<const float4*>(du + ((int64_t)b * T + tf) * D + d4) : z4;
-      float4 g = z4;
-  #pragma unroll
-    for (int j = 0; j < K; ++j) g = fma4(w[j], dw[K - 1 - j], g);
-      *reinterpret_cast<float4*>(dh + ((int64_t)b * T + t) * D + d4) = g;
-  #pragma unroll
-    for (int j = 0; j < K; ++j) acc[j] = fma4(dw[0], hw[j], acc[j]);
-  #pragma unroll
-    for (int j = 0; j + 1 < K; ++j) {
-        hw[j] = hw[j + 1];
-        dw[j] = dw[j + 1];
+    for (int t = t0; t < t1; t += CONV_UNROLL) {
+#pragma unroll
+      for (int i = 0; i < CONV_UNROLL; ++i) {  // all loads of the step first
+        hw[K - 1 + i] = t + i < t1 ? ld4<InT>(h, ((int64_t)b * T + t + i) * D + d4) : z4;
+        const int tf = t + K - 1 + i;
+        dw[K - 1 + i] = tf < T ? *reinterpret_cast<const float4*>(du + ((int64_t)b * T + tf) * D + d4) : z4;
+      }
+#pragma unroll
+      for (int i = 0; i < CONV_UNROLL; ++i) {
+        if (t + i < t1) {
+          float4 g = z4;
+#pragma unroll
+          for (int j = 0; j < K; ++j) g = fma4(w[j], dw[i + K - 1 - j], g);
+          *reinterpret_cast<float4*>(dh + ((int64_t)b * T + t + i) * D + d4) = g;
+#pragma unroll
+          for (int j = 0; j < K; ++j) acc[j] = fma4(dw[i], hw[i + j], acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) {
+        hw[j] = hw[CONV_UNROLL + j];
+        dw[j] = dw[CONV_UNROLL + j];
       }
     }
 #pragma unroll

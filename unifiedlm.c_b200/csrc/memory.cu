@@ -527,7 +527,7 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   const int64_t n_tiles = decay_dg_partials(B, T);
   ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
-  // side stream: dv beside dS, dk beside dq, then G = dy^T q beside the statistics backward
+  // side stream: dv and G = dy^T q beside dS and dq, then dk
   cudaStream_t side = nullptr;
   if (int rc = side_stream(&side)) return rc;
   if (int rc = stream_after(side, st)) return rc;
@@ -544,6 +544,23 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
   }
   if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, dv_dtype, 1, B, T, D, prec, side)) return rc;
+  float* dw_part = gpart + 8 * D * M;
+  const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
+  {
+    // G = dy^T q over all B*T rows (split K), then dmu = G w and the combine's share of dw,
+    // sum_d mu G (partials, added to dw after the statistics backward)
+    const int64_t rows = B * T;
+    const int S = fill_split(rows, D, M);
+    Operand A{doop, ldd, 0, D, rows, dt, true};
+    Operand Bq{qop, ldm, 0, M, rows, dt, true};
+    GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
+    s.ksplit = S;
+    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
+    if (int rc = run_gemm(A, Bq, s, e, side)) return rc;
+    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, side>>>(gpart, S, mu, w, dmu, dw_part,
+                                                                                  (int)D, (int)M);
+    ULM_LAUNCH_CHECK("combine_grad_kernel");
+  }
   if (int rc = stream_after(side, st)) return rc;  // dS is ready for dk
   combine_weight_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 8 * 148), 256, 0, st>>>(mu, w, mw, dt, ldm,
                                                                                              (int)D, (int)M);
@@ -560,26 +577,11 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
     if (int rc = run_gemm2(A, Bk, &A2, &B2, s, e, st)) return rc;
   }
   if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, side)) return rc;
-  if (int rc = stream_after(st, side)) return rc;  // dk and dv are done
+  if (int rc = stream_after(st, side)) return rc;  // dk, dv and the combine's partials are done
   if (int rc = stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
                              sc.tiles, n_tiles, st))
     return rc;
   {
-    // G = dy^T q over all B*T rows (split K), then dmu = G w and dw += sum_d mu G
-    const int64_t rows = B * T;
-    const int S = fill_split(rows, D, M);
-    Operand A{doop, ldd, 0, D, rows, dt, true};
-    Operand Bq{qop, ldm, 0, M, rows, dt, true};
-    GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
-    s.ksplit = S;
-    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
-    if (int rc = run_gemm(A, Bq, s, e, side)) return rc;
-    float* dw_part = gpart + 8 * D * M;
-    const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
-    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, side>>>(gpart, S, mu, w, dmu, dw_part,
-                                                                                  (int)D, (int)M);
-    ULM_LAUNCH_CHECK("combine_grad_kernel");
-    if (int rc = stream_after(st, side)) return rc;  // join before dw gets the combine's share
     add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(dw_part, (int)row_blocks, M, dw);
     ULM_LAUNCH_CHECK("add_parts_kernel");
   }
