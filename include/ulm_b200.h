@@ -156,6 +156,12 @@ int ulm_set_epilogue_mode(int mode);
  * order. Returns the previous mode, or -1 (no change) for an unknown mode. */
 int ulm_set_scan_mode(int mode);
 
+/* Library-wide switch of programmatic dependent launch: 1 (default) lets each kernel of the library
+ * be scheduled while the previous kernel on its stream finishes (it waits for that kernel's results
+ * on the device before touching memory); 0 launches every kernel after its predecessor has
+ * completed. Results do not depend on it. Returns the previous setting. */
+int ulm_set_pdl(int enable);
+
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
  * den: NULL when r holds the read addresses; otherwise r holds their unnormalised form z

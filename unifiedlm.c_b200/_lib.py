@@ -34,6 +34,7 @@ SIGNATURES = {
     "ulm_set_gemm_pairs": (_I, [_I]),
     "ulm_set_epilogue_mode": (_I, [_I]),
     "ulm_set_scan_mode": (_I, [_I]),
+    "ulm_set_pdl": (_I, [_I]),
     "ulm_memory_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_bwd": (_I, [_P, _P, _I] + [_P] * 19 + [_I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_combine_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P,

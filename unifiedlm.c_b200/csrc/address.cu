@@ -78,6 +78,7 @@ template <typename InT, int K>
 __global__ void __launch_bounds__(256)
     addr_conv_kernel(const void* __restrict__ h, const float* __restrict__ conv_w, void* __restrict__ u, int u_dtype,
                      int64_t ld_u, int T, int D) {
+  pdl_enter();
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * CONV_ROWS, t1 = min(T, t0 + CONV_ROWS);
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -137,6 +138,7 @@ __global__ void addr_normalize_kernel(float* __restrict__ zr, float* __restrict_
 // column block, unused slots zero), summed in a fixed order
 __global__ void addr_den_kernel(const float* __restrict__ part, int part_ld, const float* __restrict__ eps,
                                 float* __restrict__ den, int64_t rows) {
+  pdl_enter();
   const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   const float* p = part + row * part_ld;
@@ -152,6 +154,7 @@ __global__ void __launch_bounds__(256)
     addr_bwd_kernel(const float* __restrict__ dr, const float* __restrict__ r, const float* __restrict__ den,
                     int unnormalised, void* __restrict__ da, int da_dtype, int64_t ld_da,
                     float* __restrict__ deps_part, int64_t rows, int M, int rows_per_cta) {
+  pdl_enter();
   __shared__ float deps_w[8];
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float deps_acc = 0.f;
@@ -200,6 +203,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     col_sum_bf16x8_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows, int cols,
                           int rows_per_chunk, float* __restrict__ part) {
+  pdl_enter();
   __shared__ float red[8][257];
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c0 = blockIdx.x * 256 + lane * 8;
@@ -251,6 +255,7 @@ __global__ void col_sum_kernel(const void* __restrict__ x, int64_t ld, int64_t r
 // sums are added in warp order (a fixed order: deterministic)
 __global__ void __launch_bounds__(256)
     sum_parts4_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, float* __restrict__ out) {
+  pdl_enter();
   __shared__ float4 red[8][32];
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t i = ((int64_t)blockIdx.x * 32 + lane) * 4;
@@ -290,6 +295,7 @@ __global__ void sum_parts_kernel(const float* __restrict__ part, int64_t nparts,
 
 // deterministic sum of n floats into *out (one block)
 __global__ void __launch_bounds__(256) sum_all_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+  pdl_enter();
   __shared__ double red[256];
   double s = 0.0;
   for (int64_t i = threadIdx.x; i < n; i += 256) s += x[i];
@@ -309,6 +315,7 @@ template <typename InT, int K>
 __global__ void __launch_bounds__(256)
     addr_conv_bwd_kernel(const float* __restrict__ du, const void* __restrict__ h, const float* __restrict__ conv_w,
                          float* __restrict__ dh, float* __restrict__ dconv_part, int T, int D) {
+  pdl_enter();
   const int b = blockIdx.y;
   const int t0 = blockIdx.x * CONV_ROWS, t1 = min(T, t0 + CONV_ROWS);
   const int64_t part = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
@@ -460,8 +467,8 @@ int addr_check(int h_dtype, int prec, int64_t B, int64_t T, int64_t D, int64_t M
 // out = sum of nparts arrays of n floats, in a fixed order
 int sum_parts(const float* part, int64_t nparts, int64_t n, float* out, cudaStream_t st) {
   if (n % 4 == 0 && is_aligned16(part) && is_aligned16(out)) {
-    sum_parts4_kernel<<<(unsigned)cdiv(n, 128), 256, 0, st>>>(part, nparts, n, out);
-    ULM_LAUNCH_CHECK("sum_parts4_kernel");
+    if (int rc = launch_pdl(sum_parts4_kernel, dim3((unsigned)cdiv(n, 128)), dim3(256), 0, st, part, nparts, n, out))
+      return rc;
   } else {
     sum_parts_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 16 * 148), 256, 0, st>>>(part, nparts, n, out);
     ULM_LAUNCH_CHECK("sum_parts_kernel");
@@ -489,16 +496,17 @@ extern "C" int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, 
   const int64_t rows = B * T;
   dim3 cgrid((unsigned)cdiv(T, CONV_ROWS), (unsigned)B);
   const int cthreads = (int)std::min<int64_t>(256, cdiv(D, 4));
-#define ULM_CONV(KK)                                                                                            \
-  if (conv_size == KK) {                                                                                        \
-    if (h_dtype == ULM_F32)                                                                                     \
-      addr_conv_kernel<float, KK><<<cgrid, cthreads, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D);       \
-    else                                                                                                        \
-      addr_conv_kernel<__nv_bfloat16, KK><<<cgrid, cthreads, 0, st>>>(h, conv_w, u_op, dt, ld_u, (int)T, (int)D); \
-  }
+  int crc = ULM_OK;
+#define ULM_CONV(KK)                                                                                             \
+  if (conv_size == KK)                                                                                           \
+    crc = h_dtype == ULM_F32                                                                                     \
+              ? launch_pdl(addr_conv_kernel<float, KK>, cgrid, dim3(cthreads), 0, st, h, conv_w, u_op, dt, ld_u, \
+                           (int)T, (int)D)                                                                       \
+              : launch_pdl(addr_conv_kernel<__nv_bfloat16, KK>, cgrid, dim3(cthreads), 0, st, h, conv_w, u_op,   \
+                           dt, ld_u, (int)T, (int)D);
   ULM_CONV(1) ULM_CONV(2) ULM_CONV(3) ULM_CONV(4) ULM_CONV(5) ULM_CONV(6) ULM_CONV(7) ULM_CONV(8)
 #undef ULM_CONV
-  ULM_LAUNCH_CHECK("addr_conv_kernel");
+  if (crc) return crc;
   // z = relu(u K^T + b)^2 written into r
   Operand A{u_op, ld_u, rows * ld_u, D, rows, dt, false};
   Operand Bw{key_w, ld_kw, M * ld_kw, D, M, dt, false};
@@ -518,8 +526,9 @@ extern "C" int ulm_address_fwd(const void* h, int h_dtype, const float* conv_w, 
   e.row_partial = part;
   e.part_ld = (int)pld;
   if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
-  addr_den_kernel<<<(unsigned)cdiv(rows, 256), 256, 0, st>>>(part, (int)pld, eps, den, rows);
-  ULM_LAUNCH_CHECK("addr_den_kernel");
+  if (int rc = launch_pdl(addr_den_kernel, dim3((unsigned)cdiv(rows, 256)), dim3(256), 0, st, (const float*)part,
+                          (int)pld, eps, den, rows))
+    return rc;
   return ULM_OK;
 }
 
@@ -540,9 +549,9 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   const int64_t rows = B * T;
   AddrBwdWork wk = carve_addr_work(work, B, T, D, M, dt);
   // da and the d eps partials, then db = column sums of da
-  addr_bwd_kernel<<<(unsigned)wk.ctas, 256, 0, st>>>(dr, r, den, normalized ? 0 : 1, wk.da, dt, wk.ld_m,
-                                                     wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
-  ULM_LAUNCH_CHECK("addr_bwd_kernel");
+  if (int rc = launch_pdl(addr_bwd_kernel, dim3((unsigned)wk.ctas), dim3(256), 0, st, dr, r, den, normalized ? 0 : 1,
+                          wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA))
+    return rc;
   // du = da K and the conv backward stay on the caller's stream (launched first); db, deps and
   // dK = da^T u run beside them on the side stream
   cudaStream_t side = nullptr;
@@ -557,9 +566,9 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   }
   if (dt == ULM_BF16 && M % 8 == 0 && wk.ld_m % 8 == 0) {
     dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
-    col_sum_bf16x8_kernel<<<g2, 256, 0, side>>>(static_cast<const __nv_bfloat16*>(wk.da), wk.ld_m, rows, (int)M,
-                                              DB_ROWS_PER_CHUNK, wk.db_part);
-    ULM_LAUNCH_CHECK("col_sum_bf16x8_kernel");
+    if (int rc = launch_pdl(col_sum_bf16x8_kernel, g2, dim3(256), 0, side, static_cast<const __nv_bfloat16*>(wk.da),
+                            wk.ld_m, rows, (int)M, DB_ROWS_PER_CHUNK, wk.db_part))
+      return rc;
   } else {
     dim3 g2((unsigned)cdiv(M, 256), (unsigned)wk.db_chunks);
     if (dt == ULM_F32)
@@ -569,8 +578,9 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
     ULM_LAUNCH_CHECK("col_sum_kernel");
   }
   if (int rc = sum_parts(wk.db_part, wk.db_chunks, M, dkey_b, side)) return rc;
-  sum_all_kernel<<<1, 256, 0, side>>>(wk.deps_part, wk.ctas, deps);
-  ULM_LAUNCH_CHECK("sum_all_kernel");
+  if (int rc = launch_pdl(sum_all_kernel, dim3(1), dim3(256), 0, side, (const float*)wk.deps_part, (int64_t)wk.ctas,
+                          deps))
+    return rc;
   // dK = da^T u, split over S k ranges of rows (split-K product), then the partials summed in order
   {
     Operand A{wk.da, wk.ld_m, rows * wk.ld_m, M, rows, dt, true};
@@ -584,18 +594,16 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   // through the conv
   dim3 grid((unsigned)wk.chunks, (unsigned)B);
   const int cthreads = (int)std::min<int64_t>(256, cdiv(D, 4));
-#define ULM_CONVB(KK)                                                                                        \
-  if (conv_size == KK) {                                                                                     \
-    if (h_dtype == ULM_F32)                                                                                  \
-      addr_conv_bwd_kernel<float, KK><<<grid, cthreads, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, (int)T, \
-                                                                  (int)D);                                    \
-    else                                                                                                     \
-      addr_conv_bwd_kernel<__nv_bfloat16, KK><<<grid, cthreads, 0, st>>>(wk.du, h, conv_w, dh, wk.dconv_part, \
-                                                                          (int)T, (int)D);                    \
-  }
+  int crc = ULM_OK;
+#define ULM_CONVB(KK)                                                                                           \
+  if (conv_size == KK)                                                                                          \
+    crc = h_dtype == ULM_F32 ? launch_pdl(addr_conv_bwd_kernel<float, KK>, grid, dim3(cthreads), 0, st,          \
+                                          (const float*)wk.du, h, conv_w, dh, wk.dconv_part, (int)T, (int)D)     \
+                             : launch_pdl(addr_conv_bwd_kernel<__nv_bfloat16, KK>, grid, dim3(cthreads), 0, st,  \
+                                          (const float*)wk.du, h, conv_w, dh, wk.dconv_part, (int)T, (int)D);
   ULM_CONVB(1) ULM_CONVB(2) ULM_CONVB(3) ULM_CONVB(4) ULM_CONVB(5) ULM_CONVB(6) ULM_CONVB(7) ULM_CONVB(8)
 #undef ULM_CONVB
-  ULM_LAUNCH_CHECK("addr_conv_bwd_kernel");
+  if (crc) return crc;
   if (int rc = sum_parts(wk.dconv_part, (int64_t)wk.chunks * B, D * conv_size, dconv_w, st)) return rc;
   return stream_after(st, side);  // join
 }

@@ -54,6 +54,36 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// ---- programmatic dependent launch ----------------------------------------------------------
+// Kernels started with launch_pdl may be scheduled while the previous kernel on their stream is
+// still finishing: their CTAs take SMs as the predecessor's CTAs leave and do their set-up
+// (barriers, tensor memory) early. Each such kernel calls pdl_enter() before its first access to
+// global memory: it waits until the predecessor grid has completed with its writes visible, then
+// lets the next kernel on the stream be scheduled the same way. Without the launch attribute both
+// instructions return at once, so every kernel calls pdl_enter() however it is launched.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// library-wide switch of the early scheduling (ulm_set_pdl); the results do not depend on it
+int pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
+  return ULM_OK;
+}
+
 inline bool is_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---- device-side error flag (read and cleared by ulm_device_error) ------------------------

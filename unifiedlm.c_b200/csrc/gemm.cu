@@ -527,6 +527,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_enter();  // set-up done: wait for the previous kernel's results before touching global memory
 
   if (warp == 0) {
     if (lane == 0) {
@@ -751,6 +752,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM of the pair allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_enter();  // set-up done: wait for the previous kernel's results before touching global memory
 
   if (warp == 0) {
     if (lane == 0) {
@@ -899,6 +901,7 @@ __global__ void __launch_bounds__(256)
   constexpr int BM = 64, BN = 64, BK = 16;
   __shared__ float As[BK][BM + 1];
   __shared__ float Bs[BK][BN + 1];
+  pdl_enter();
   const TileCoord tc = decode_tile<BM, BN>(blockIdx.x, shape, m_blocks, n_blocks, tiles_per_batch);
   const float* Ab = A + (int64_t)tc.b * bsA;
   const float* Bb = Bm + (int64_t)tc.b * bsB;
@@ -1179,10 +1182,8 @@ int launch_tc(const Operand& A, const Operand& B, const Operand* A2, const Opera
   if (total == 0) return ULM_OK;
   const int grid = total < sm_count(dev) ? total : sm_count(dev);
   const GemmShape sb = with_schedule(s, total, grid);
-  tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, ta2, tb2, tout, taux, sb, e,
-                                                                            m_blocks, n_blocks, tpb, total);
-  ULM_LAUNCH_CHECK("tc_gemm_kernel");
-  return ULM_OK;
+  return launch_pdl(tc_gemm_kernel<BN, A_MN, B_MN>, dim3(grid), dim3(TC_THREADS), Cfg::SMEM_BYTES, st, ta, tb, ta2,
+                    tb2, tout, taux, sb, e, m_blocks, n_blocks, tpb, total);
 }
 
 template <int BN>
@@ -1227,10 +1228,8 @@ int launch_tc2(const Operand& A, const Operand& B, const Operand* A2, const Oper
   const int max_pairs = sm_count(dev) / 2;
   const int pairs = total < max_pairs ? total : max_pairs;
   const GemmShape sb = with_schedule(s, total, pairs);
-  tc2_gemm_kernel<A_MN, B_MN><<<2 * pairs, TC_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, ta2, tb2, tout, taux, sb, e,
-                                                                           m_blocks, n_blocks, tpb, total);
-  ULM_LAUNCH_CHECK("tc2_gemm_kernel");
-  return ULM_OK;
+  return launch_pdl(tc2_gemm_kernel<A_MN, B_MN>, dim3(2 * pairs), dim3(TC_THREADS), Cfg::SMEM_BYTES, st, ta, tb, ta2,
+                    tb2, tout, taux, sb, e, m_blocks, n_blocks, tpb, total);
 }
 
 int dispatch_tc2(const Operand& A, const Operand& B, const Operand* A2, const Operand* B2, const GemmShape& s,

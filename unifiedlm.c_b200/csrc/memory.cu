@@ -65,6 +65,10 @@ SideStreams& side_streams() {
 
 }  // namespace
 
+static int g_pdl = 1;
+
+int pdl_enabled() { return g_pdl; }
+
 int side_stream(cudaStream_t* out) {
   const int dev = current_device();
   ULM_REQUIRE(dev >= 0 && dev < 64, "no current CUDA device (or ordinal >= 64)");
@@ -134,6 +138,7 @@ __global__ void convert_rows_kernel(const void* __restrict__ src, int src_dtype,
 __global__ void convert_rows_vec8_kernel(const void* __restrict__ src, int src_dtype, int64_t lds,
                                          void* __restrict__ dst, int dst_dtype, int64_t ldd, int64_t rows,
                                          int64_t cols8) {
+  pdl_enter();
   const int64_t n = rows * cols8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t rr = i / cols8, cc = (i - rr * cols8) * 8;
@@ -179,9 +184,8 @@ int convert_rows(const void* src, int sdt, int64_t lds, void* dst, int ddt, int6
   if (cols % 8 == 0 && lds % 8 == 0 && ldd % 8 == 0 && is_aligned16(src) && is_aligned16(dst)) {
     const int64_t blocks = cdiv(rows * (cols / 8), 256);
     const unsigned grid = (unsigned)(blocks < 16 * 148 ? blocks : 16 * 148);
-    convert_rows_vec8_kernel<<<grid, 256, 0, st>>>(src, sdt, lds, dst, ddt, ldd, rows, cols / 8);
-    ULM_LAUNCH_CHECK("convert_rows_vec8_kernel");
-    return ULM_OK;
+    return launch_pdl(convert_rows_vec8_kernel, dim3(grid), dim3(256), 0, st, src, sdt, lds, dst, ddt, ldd, rows,
+                      cols / 8);
   }
   const int64_t blocks = cdiv(rows * cols, 256);
   const unsigned grid = (unsigned)(blocks < 8 * 148 ? blocks : 8 * 148);
@@ -301,6 +305,12 @@ extern "C" int64_t ulm_operand_ld(int64_t n) { return ((n + 7) / 8) * 8; }
 extern "C" int ulm_set_gemm_pairs(int enable) {
   const int old = g_gemm_pairs;
   g_gemm_pairs = enable ? 1 : 0;
+  return old;
+}
+
+extern "C" int ulm_set_pdl(int enable) {
+  const int old = g_pdl;
+  g_pdl = enable ? 1 : 0;
   return old;
 }
 

@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(32 * WARPS)
                          const float* __restrict__ w, const float* __restrict__ g, float* __restrict__ q,
                          float* __restrict__ c, void* __restrict__ qop, void* __restrict__ kop, int64_t ldop, int T,
                          int M) {
+  pdl_enter();
   constexpr int R = SEG * WARPS;
   // rows cta_t0 - 1 .. cta_t0 + R - 1 of r: row i is the write address k of position cta_t0 + i and
   // the read address of position cta_t0 + i - 1 (R rows in one box, the last row in a second)
@@ -320,6 +321,7 @@ __global__ void __launch_bounds__(32 * WARPS)
                          const float* __restrict__ dk, const float* __restrict__ den, const float* __restrict__ w,
                          const float* __restrict__ g, float* __restrict__ dr, float* __restrict__ part_dw,
                          double* __restrict__ part_dg, int T, int M, int has_dqo, int fast_identity) {
+  pdl_enter();
   constexpr int R = SEG * WARPS;
   constexpr int TILE = R * 32;
   // tiles: dqf, dk, then either the r tile rows t0-1 .. t0+R-1 (recompute) or q, c, k (saved),
@@ -554,6 +556,7 @@ __global__ void __launch_bounds__(32 * WARPS)
                           const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
                           float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
                           void* __restrict__ kop, int64_t ldop, int B, int T, int M) {
+  pdl_enter();
   constexpr int R = SEG * WARPS;
   constexpr int STAGE_FLOATS = (R + 1) * 32;
   extern __shared__ __align__(128) float tile[];
@@ -699,6 +702,7 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
                           const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
                           float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int B,
                           int T, int M, int has_dqo, int fast_identity) {
+  pdl_enter();
   constexpr int R = SEG * WARPS;
   constexpr int TILE = R * 32;
   extern __shared__ __align__(128) float tile[];
@@ -957,13 +961,15 @@ int launch_cluster_smem(K kernel, dim3 grid, int threads, int cluster_x, size_t 
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = cluster_x;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled();
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   ULM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, args...));
   return ULM_OK;
 }
@@ -1020,6 +1026,7 @@ int pipe_clusters(K kernel, int threads, int C, size_t smem, int64_t n_items, in
 
 // dw[m] = sum over the R partial rows of part_dw[.][m], in row order.
 __global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int R, int M) {
+  pdl_enter();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m < M) {
     float s = 0.f;
@@ -1033,6 +1040,7 @@ __global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __
 __global__ void __launch_bounds__(256)
     stats_bwd_dg_kernel(const double* __restrict__ part_dg, int64_t n1, const float* __restrict__ extra, int64_t n2,
                         float* __restrict__ dg) {
+  pdl_enter();
   __shared__ double red[256];
   double s = 0.0;
   for (int64_t i = threadIdx.x; i < n1; i += 256) s += part_dg[i];
@@ -1137,10 +1145,12 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     n_dg = B * groups;
     dw_rows = B;
   }
-  stats_bwd_dw_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(sc.part_dw, dw, (int)dw_rows, (int)M);
-  ULM_LAUNCH_CHECK("stats_bwd_dw_kernel");
-  stats_bwd_dg_kernel<<<1, 256, 0, st>>>(sc.part_dg, n_dg, tile_partials, tile_partials ? n_tiles : 0, dg);
-  ULM_LAUNCH_CHECK("stats_bwd_dg_kernel");
+  if (int rc = launch_pdl(stats_bwd_dw_kernel, dim3((unsigned)cdiv(M, 256)), dim3(256), 0, st, (const float*)sc.part_dw,
+                          dw, (int)dw_rows, (int)M))
+    return rc;
+  if (int rc = launch_pdl(stats_bwd_dg_kernel, dim3(1), dim3(256), 0, st, (const double*)sc.part_dg, n_dg,
+                          tile_partials, tile_partials ? n_tiles : (int64_t)0, dg))
+    return rc;
   return ULM_OK;
 }
 
