@@ -507,35 +507,75 @@ def main():
     if L_.device_error() != 0:
         raise RuntimeError("a kernel reported a device-side error during the bench")
 
-    # e2e: inputs copied from pinned host memory every step, parameter gradients read back
+    # e2e: every step's inputs copied from pinned host memory and its parameter gradients read back,
+    # pipelined as a training loop with a prefetching loader does it: the host-to-device copy of
+    # step i+1 and the device-to-host read of step i-1 run on their own streams during step i
+    # (two device input slots, two output slots); the timed region spans the first copy to the
+    # last read
     host = [t.cpu().pin_memory() for t in (h, v, dq_out, dfast)]
-    dev_in = [torch.empty_like(t) for t in (h, v, dq_out, dfast)]
-    host_out = torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory()
+    slots_in = [[torch.empty_like(t) for t in (h, v, dq_out, dfast)] for _ in range(2)]
+    slots_out = [torch.empty_like(bucket.flat) for _ in range(2)]
+    host_out = [torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host)
-    d2h = host_out.numel() * host_out.element_size()
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    main_s = torch.cuda.current_stream(dev)
+    h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-    def e2e_step():
-        for d_, h_ in zip(dev_in, host):
-            d_.copy_(h_, non_blocking=True)
-        out = step(*dev_in)
-        host_out.copy_(out, non_blocking=True)
+    def e2e_run(n, start_ev=None):
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [None, None]    # the step that last read the slot has finished
+        out_ready = [torch.cuda.Event() for _ in range(2)]
+        out_free = [None, None]   # the read of the slot's previous result has finished
 
-    e2e_step()
+        def copy_in(i):
+            k = i % 2
+            with torch.cuda.stream(h2d_s):
+                if start_ev is not None and i == 0:
+                    h2d_s.wait_event(start_ev)
+                if in_free[k] is not None:
+                    h2d_s.wait_event(in_free[k])
+                for d_, h_ in zip(slots_in[k], host):
+                    d_.copy_(h_, non_blocking=True)
+                in_ready[k].record(h2d_s)
+
+        copy_in(0)
+        for i in range(n):
+            k = i % 2
+            main_s.wait_event(in_ready[k])
+            if i + 1 < n:
+                copy_in(i + 1)
+            out = step(*slots_in[k])
+            ev = torch.cuda.Event()
+            ev.record(main_s)
+            in_free[k] = ev
+            if out_free[k] is not None:
+                main_s.wait_event(out_free[k])
+            slots_out[k].copy_(out)
+            out_ready[k].record(main_s)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(out_ready[k])
+                host_out[k].copy_(slots_out[k], non_blocking=True)
+                ev2 = torch.cuda.Event()
+                ev2.record(d2h_s)
+                out_free[k] = ev2
+        main_s.wait_stream(d2h_s)
+        main_s.wait_stream(h2d_s)
+
+    e2e_run(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(1, min(args.steps, 5))
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
+    e2e_steps = max(2, args.steps)
+    e0.record(main_s)
+    e2e_run(e2e_steps, start_ev=e0)
+    e1.record(main_s)
     torch.cuda.synchronize()
     e2e_secs = torch.tensor(e0.elapsed_time(e1) / 1e3, device=dev)
     if world > 1:
         dist.all_reduce(e2e_secs, op=dist.ReduceOp.MAX)
     e2e_value = world * W["B"] * W["T"] * e2e_steps / float(e2e_secs)
-    del dev_in, host
+    del slots_in, slots_out, host_out, host
 
     # roofline of the dominant kernel family (tensor-core products), CUDA events per launch
     blk0 = blocks[0]
@@ -602,7 +642,9 @@ def main():
                        "lam": W["lam"], "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (r is 134 MB), no flush"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 on their own streams "
+                              "during step i (double-buffered), timed from the first copy to the last read"},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
             "mixer": mixer, "head": head, "decode": decode}
     if rank == 0:
