@@ -293,26 +293,37 @@ __device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, f
 // EPI_MODE_WARP: one chunk (32 rows x 128 bytes: 32 fp32 / 64 bf16 columns at col0) of the warp's
 // rows row_base..+31; taddr = this warp's TMEM quadrant at the chunk's first column. n counts the
 // warp's staged chunks (slot n % 2, barrier phase n / 2). False if the aux wait gave up.
+// Aux tile of one staged chunk (32 rows x 128 bytes) into slot n & 1 of this warp; lane 0 only. The
+// caller has made sure the slot's previous store has read it.
+__device__ __forceinline__ void epi_aux_issue(const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int n,
+                                              int col0, int row_base, int b) {
+  const int sl = n & 1;
+  mbar_arrive_expect_tx(&abar[sl], 4096u);
+  tma_load_3d(tma_aux, slots + sl * 4096, &abar[sl], col0, row_base, b);
+}
+
+// One staged chunk of a warp: 32 rows x (32 fp32 | 64 bf16) columns through slot n & 1. With a tile
+// aux, the chunk's aux was issued earlier (epi_aux_issue with the same n); after the chunk's store
+// the slot is refilled with the aux of the chunk two ahead (next_col0 >= 0), which then loads while
+// the next chunk is processed.
 template <bool F32>
 __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
                                                const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
-                                               float gl2, int b, int row_base, int col0, uint32_t taddr,
-                                               float& dg_acc, volatile int* abort_flag, int site) {
+                                               int& n_issued, float gl2, int b, int row_base, int col0,
+                                               int next_col0, uint32_t taddr, float& dg_acc,
+                                               volatile int* abort_flag, int site) {
   const int lane = threadIdx.x & 31;
   const bool aux = has_tile_aux(e.kind);
   const int sl = n & 1;
   const uint32_t parity = (uint32_t)(n >> 1) & 1u;
   ++n;
   uint8_t* tile = slots + sl * 4096;
-  if (lane == 0) {
-    bulk_wait_group_read<1>();  // the store of this warp's chunk n - 2 has read the slot
-    if (aux) {
-      mbar_arrive_expect_tx(&abar[sl], 4096u);
-      tma_load_3d(tma_aux, tile, &abar[sl], col0, row_base, b);
-    }
+  if (!aux) {
+    if (lane == 0) bulk_wait_group_read<1>();  // the store of this warp's chunk n - 2 has read the slot
+    __syncwarp();
+  } else if (!wait_or_abort(&abar[sl], parity, abort_flag, site)) {
+    return false;
   }
-  __syncwarp();
-  if (aux && !wait_or_abort(&abar[sl], parity, abort_flag, site)) return false;
 #pragma unroll 1
   for (int h = 0; h < (F32 ? 1 : 2); ++h) {
     float v[32], p[32];
@@ -332,6 +343,11 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
   if (lane == 0) {
     tma_store_3d(tma_out, tile, col0, row_base, b);
     bulk_commit_group();
+    if (aux && next_col0 >= 0) {
+      bulk_wait_group_read<0>();  // the store just issued has read the slot
+      epi_aux_issue(tma_aux, slots, abar, n + 1, next_col0, row_base, b);
+      ++n_issued;
+    }
   }
   return true;
 }
@@ -360,9 +376,12 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
   const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
   uint8_t* wslots = stage + ew * 8192;  // this warp's two 4 KB slots
   uint64_t* wbar = aux_bar + ew * 2;
-  int n = 0;
+  int n = 0;         // staged chunks of this warp so far (slot n & 1)
+  int n_issued = 0;  // aux loads issued by this warp (lane 0's count)
   int j = 0;
   bool ok = true;
+  const bool warp_aux = mode == EPI_MODE_WARP && has_tile_aux(epi.kind);
+  const int cw = f32 ? 32 : 64;  // columns of a staged chunk
   const int rounded = (total_tiles + t_stride - 1) / t_stride * t_stride;
   for (int tt = t_first; tt < rounded; tt += t_stride) {
     const int t = schedule_tile(tt, t_stride, total_tiles, shape.balanced);
@@ -371,15 +390,25 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     const int jj = j++;
     const int acc = jj & 1;
     const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
+    const int row_base = tc.mb * BM + cta_rows + quad * 32;
+    const int row = row_base + lane;
+    const int col_base = tc.nb * BN + half * HALF;
+    // staged chunks of this warp in this tile; with a tile aux the first two chunks' aux tiles load
+    // now, while the tile's MMAs run
+    const int nch = (row_base < shape.M && col_base < shape.N) ? min(HALF / cw, (shape.N - col_base + cw - 1) / cw) : 0;
+    if (warp_aux && lane == 0 && epi.kind != EPI_LSE) {
+      bulk_wait_group_read<0>();  // every earlier store of this warp has read its slot
+      for (int i = 0; i < nch && i < 2; ++i) {
+        epi_aux_issue(tma_aux, wslots, wbar, n + i, col_base + i * cw, row_base, tc.b);
+        ++n_issued;
+      }
+    }
     if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, site)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    const int row_base = tc.mb * BM + cta_rows + quad * 32;
-    const int row = row_base + lane;
     const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + half * HALF);
-    const int col_base = tc.nb * BN + half * HALF;
     float dg_acc = 0.f;
     if (epi.kind == EPI_LSE) {
       float m = -INFINITY, ssum = 0.f;
@@ -395,15 +424,14 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
         pp[1] = ssum;
       }
     } else if (mode == EPI_MODE_WARP) {
-      const int cw = f32 ? 32 : 64;
 #pragma unroll 1
-      for (int c = 0; c < HALF && ok; c += cw) {
-        const int col0 = col_base + c;
-        if (row_base >= shape.M || col0 >= shape.N) break;
-        ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, gl2, tc.b, row_base, col0,
-                                        taddr + (uint32_t)c, dg_acc, abort_flag, site)
-                 : epi_chunk_warp<false>(epi, shape, tma_out, tma_aux, wslots, wbar, n, gl2, tc.b, row_base, col0,
-                                         taddr + (uint32_t)c, dg_acc, abort_flag, site);
+      for (int i = 0; i < nch && ok; ++i) {
+        const int c = i * cw;
+        const int next = i + 2 < nch ? col_base + c + 2 * cw : -1;
+        ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b, row_base,
+                                        col_base + c, next, taddr + (uint32_t)c, dg_acc, abort_flag, site)
+                 : epi_chunk_warp<false>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b,
+                                         row_base, col_base + c, next, taddr + (uint32_t)c, dg_acc, abort_flag, site);
       }
     } else {
 #pragma unroll 1
@@ -431,11 +459,13 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     }
   }
   if (mode == EPI_MODE_WARP && lane == 0) {
-    // an aux load still in flight after an abort lands before the CTA exits; stores complete
-    if (!ok && has_tile_aux(epi.kind) && n > 0) {
-      const int k = n - 1;
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&wbar[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+    // aux loads still in flight after an abort (the last one of each slot) land before the CTA
+    // exits; stores complete
+    if (!ok && warp_aux) {
+      for (int k = max(0, n_issued - 2); k < n_issued; ++k) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&wbar[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+        }
       }
     }
     bulk_wait_group<0>();
