@@ -163,6 +163,14 @@ __device__ __forceinline__ float fast_rcp(float x) {
   return y;
 }
 
+// 2^x by the hardware approximation (PTX ex2.approx.ftz: relative error about 2^-22, results below
+// the normal range flushed to zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---- TMA -------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -73,18 +73,38 @@ __device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row
 template <int NC>
 __device__ __forceinline__ void epilogue_math(const GemmEpilogue& e, float gl2, int row, int col0, int ncols,
                                               float* v, const float* p, float& dg_acc) {
-  if (e.kind == EPI_DECAY_DG) {
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int lag = row - (col0 + i);
-      if (lag > 0) dg_acc = fmaf((float)lag * p[i], v[i], dg_acc);
-    }
-  }
   if (e.kind == EPI_DECAY || e.kind == EPI_DECAY_DG) {
+    // element i has lag = row - col0 - i (exact in float); decay lam^lag = 2^(gl2 lag) on and below
+    // the diagonal, 0 above it
+    const float lag0 = (float)(row - col0);
+    if (e.kind == EPI_DECAY_DG) {
+      // d/dg share: sum of lag * P * dP (P, the aux, is zero above the diagonal; lag is zero on it)
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int lag = row - (col0 + i);
-      v[i] = lag >= 0 ? v[i] * exp2f(gl2 * (float)lag) : 0.f;
+      for (int i = 0; i < NC; ++i) dg_acc = fmaf((lag0 - (float)i) * p[i], v[i], dg_acc);
+    }
+    if (row - col0 >= NC - 1) {
+      // the whole chunk is on or below the diagonal: for i = NC-1-8j-k the factor is
+      // lam^(lag0-NC+1) * lam^(8j) * lam^k, all factors <= 1, three exp2 per chunk
+      static_assert(NC % 8 == 0, "chunks of 8 columns");
+      const float l1 = fast_exp2(gl2);
+      float pw[8];
+      pw[0] = 1.f;
+#pragma unroll
+      for (int k = 1; k < 8; ++k) pw[k] = pw[k - 1] * l1;
+      const float l8 = fast_exp2(gl2 * 8.f);
+      float fj = fast_exp2(gl2 * (lag0 - (float)(NC - 1)));
+#pragma unroll
+      for (int j = 0; j < NC / 8; ++j) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[NC - 1 - 8 * j - k] *= fj * pw[k];
+        fj *= l8;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const float lag = lag0 - (float)i;
+        v[i] = lag >= 0.f ? v[i] * fast_exp2(gl2 * lag) : 0.f;
+      }
     }
   }
   if (e.kind == EPI_RELU2) {
