@@ -293,6 +293,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_saddr) {
 __device__ __forceinline__ void cluster_arrive_release() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
+// Arrive without release semantics: for a CTA whose threads have passed a __syncthreads() after their
+// last shared-memory access that the arrive is meant to cover (no wait for earlier global stores).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }

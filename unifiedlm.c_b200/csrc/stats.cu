@@ -530,7 +530,8 @@ __global__ void __launch_bounds__(32 * WARPS)
 // item. In the backward a rank cannot run ahead of the peers it exchanges with: its next forward
 // total waits for their reverse totals of the current item and vice versa, and two slots per
 // direction (alternating by item) keep every slot unread-safe. The forward has no reply, so after
-// reading its carries each CTA arrives on the cluster barrier and waits on it before its next send.
+// reading its carries (and a CTA barrier) each CTA arrives on the cluster barrier, relaxed, and
+// waits on it before its next send.
 // Each exchange mbarrier is armed (expect_tx) before any total of its item can be sent, and re-armed
 // for its next use only after every thread of the CTA has passed the wait on the current one.
 // Every mbarrier wait is bounded; after a timeout the CTA records the error and keeps the protocol
@@ -653,8 +654,10 @@ __global__ void __launch_bounds__(32 * WARPS)
     float carry = 0.f;
     for (int jj = 0; jj < cr; ++jj) carry = fmaf(carry, lam_cta, ctot[jj][lane]);
     for (int jj = 0; jj < wp; ++jj) carry = fmaf(carry, lam_seg, warp_sum[jj][lane]);
-    __syncwarp();  // the aligned cluster barrier wants converged warps (the waits above spin per thread)
-    cluster_arrive_release();  // this CTA's totals slots may be written again
+    // this CTA's totals slots may be written again: every thread has read them (the CTA barrier),
+    // so the arrive needs no release ordering (which would also wait for the previous item's stores)
+    __syncthreads();
+    cluster_arrive_relaxed();
     if (m < M) {
       const float wm = w_cur;
       const int t0 = cta_t0 + wp * SEG;
