@@ -551,11 +551,7 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   // da and the d eps partials, then db = column sums of da
   if (int rc = launch_pdl(addr_bwd_kernel, dim3((unsigned)wk.ctas), dim3(256), 0, st, dr, r, den, normalized ? 0 : 1,
                           wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA))
-    return rc; else if (int rc = launch_pdl(addr_bwd_kernel, dim3((unsigned)wk.ctas), dim3(256), 0, st, dr, r, den,
-                                 normalized ? 0 : 1, wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M,
-                                 ADDR_ROWS_PER_CTA)) {
     return rc;
-  }
   // du = da K and the conv backward stay on the caller's stream (launched first); db, deps and
   // dK = da^T u run beside them on the side stream
   cudaStream_t side = nullptr;
