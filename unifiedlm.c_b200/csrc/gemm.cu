@@ -4,7 +4,9 @@
 //   warp 0        : TMA producer - 128B-swizzled tiles of A (128 x 64) and B (BN x 64) per stage
 //   warp 1        : allocates TMEM, one elected lane issues tcgen05.mma (M=128, N=BN, K=16) into a
 //                   double-buffered fp32 accumulator (2 x BN TMEM columns)
-//   warps 2..5    : epilogue - tcgen05.ld 32 columns at a time, fused decay/mask, vector stores
+//   warps 2..17   : epilogue - four warps per TMEM lane quadrant, each with its share of the
+//                   columns: tcgen05.ld 32 columns at a time, the fused epilogue arithmetic, a
+//                   swizzled shared-memory staging tile and a TMA tensor store
 // Stage hand-offs use mbarriers; the accumulator is double-buffered so the epilogue of tile i
 // overlaps the MMAs of tile i+1. Every wait is bounded: on timeout the kernel records a device
 // error, drains what it has in flight, frees its TMEM and returns.
@@ -25,16 +27,16 @@ namespace ulm {
 
 __host__ __device__ __forceinline__ bool has_tile_aux(int kind) { return kind == EPI_DECAY_DG || kind == EPI_STORE_ADD; }
 
-// 32 consecutive elements of an aux row (EPI_DECAY_DG: the forward's scores; EPI_STORE_ADD: the
+// NC consecutive elements of an aux row (EPI_DECAY_DG: the forward's scores; EPI_STORE_ADD: the
 // fp32 addend; both in the output's type) as floats; zero past `ncols`.
-__device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row, int col0, int ncols,
-                                           float (&p)[32]) {
+template <int NC>
+__device__ __forceinline__ void load_aux(const GemmEpilogue& e, int b, int row, int col0, int ncols, float (&p)[NC]) {
   const int64_t off = (int64_t)b * e.aux_bstride + (int64_t)row * e.ld_aux + col0;
   if (e.out_dtype == ULM_F32) {
     const float* a = reinterpret_cast<const float*>(e.aux) + off;
-    if (ncols == 32 && e.vec_ok) {
+    if (ncols == NC && e.vec_ok) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
+      for (int i = 0; i < NC; i += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(a + i);
         p[i] = a4.x;
         p[i + 1] = a4.y;
@@ -43,13 +45,13 @@ __device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = i < ncols ? a[i] : 0.f;
+      for (int i = 0; i < NC; ++i) p[i] = i < ncols ? a[i] : 0.f;
     }
   } else {
     const __nv_bfloat16* a = reinterpret_cast<const __nv_bfloat16*>(e.aux) + off;
-    if (ncols == 32 && e.vec_ok) {
+    if (ncols == NC && e.vec_ok) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 8) {
+      for (int i = 0; i < NC; i += 8) {
         const uint4 pk = *reinterpret_cast<const uint4*>(a + i);
         const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
 #pragma unroll
@@ -63,7 +65,7 @@ __device__ __forceinline__ void load_aux32(const GemmEpilogue& e, int b, int row
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = i < ncols ? __bfloat162float(a[i]) : 0.f;
+      for (int i = 0; i < NC; ++i) p[i] = i < ncols ? __bfloat162float(a[i]) : 0.f;
     }
   }
 }
@@ -144,60 +146,62 @@ __device__ __forceinline__ void epilogue_math(const GemmEpilogue& e, float gl2, 
   }
 }
 
-// EPI_LSE over 32 logits of row `row` at col0 (ncols valid): merge into the running (m, s) of the
+// EPI_LSE over NC logits of row `row` at col0 (ncols valid): merge into the running (m, s) of the
 // row and record the target's logit
-__device__ __forceinline__ void lse_update32(const GemmEpilogue& e, int row, int col0, int ncols, const float (&v)[32],
+template <int NC>
+__device__ __forceinline__ void lse_update(const GemmEpilogue& e, int row, int col0, int ncols, const float (&v)[NC],
                                              float& m, float& s) {
   if (row >= e.rows_valid || ncols <= 0) return;
   float lm = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < 32; ++i)
+  for (int i = 0; i < NC; ++i)
     if (i < ncols) lm = fmaxf(lm, v[i]);
   const float nm = fmaxf(m, lm);
   float acc = s * __expf(m - nm);
 #pragma unroll
-  for (int i = 0; i < 32; ++i)
+  for (int i = 0; i < NC; ++i)
     if (i < ncols) acc += __expf(v[i] - nm);
   m = nm;
   s = acc;
   const int64_t tgt = e.targets[row];
   if (tgt >= col0 && tgt < col0 + ncols) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < NC; ++i)
       if ((int64_t)(col0 + i) == tgt) e.tile_partial[row] = v[i];
   }
 }
 
 // Direct epilogue: each thread stores its own row segment (used when the output or aux layout does
 // not allow the tensor-map path below).
-__device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const GemmShape& s, float gl2, int b,
-                                                 int row, int col0, float (&v)[32], float& dg_acc) {
+template <int NC>
+__device__ __forceinline__ void epilogue_store(const GemmEpilogue& e, const GemmShape& s, float gl2, int b, int row,
+                                               int col0, float (&v)[NC], float& dg_acc) {
   if (row >= s.M || col0 >= s.N) return;
-  const int ncols = min(32, s.N - col0);
-  float p[32];
+  const int ncols = min(NC, s.N - col0);
+  float p[NC];
   if (has_tile_aux(e.kind)) {
-    load_aux32(e, b, row, col0, ncols, p);
+    load_aux<NC>(e, b, row, col0, ncols, p);
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) p[i] = 0.f;
+    for (int i = 0; i < NC; ++i) p[i] = 0.f;
   }
-  epilogue_math<32>(e, gl2, row, col0, ncols, v, p, dg_acc);
+  epilogue_math<NC>(e, gl2, row, col0, ncols, v, p, dg_acc);
   const int64_t off = (int64_t)b * e.out_bstride + (int64_t)row * e.ldo + col0;
   if (e.out_dtype == ULM_F32) {
     float* o = reinterpret_cast<float*>(e.out) + off;
-    if (ncols == 32 && e.vec_ok) {
+    if (ncols == NC && e.vec_ok) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      for (int i = 0; i < NC; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
+      for (int i = 0; i < NC; ++i)
         if (i < ncols) o[i] = v[i];
     }
   } else {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out) + off;
-    if (ncols == 32 && e.vec_ok) {
+    if (ncols == NC && e.vec_ok) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 8) {
+      for (int i = 0; i < NC; i += 8) {
         uint4 pk;
         __nv_bfloat162 p0 = __floats2bfloat162_rn(v[i], v[i + 1]);
         __nv_bfloat162 p1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
@@ -211,7 +215,7 @@ __device__ __forceinline__ void epilogue_store32(const GemmEpilogue& e, const Ge
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
+      for (int i = 0; i < NC; ++i)
         if (i < ncols) o[i] = __float2bfloat16_rn(v[i]);
     }
   }
@@ -254,18 +258,20 @@ __device__ __forceinline__ int schedule_tile(int t, int P, int total, int balanc
 // conflict-free 16-byte shared stores) in two 4 KB slots of its own (EPI_MODE_WARP);
 // EPI_MODE_DIRECT stores row segments straight from registers.
 enum { EPI_MODE_DIRECT = 0, EPI_MODE_WARP = 1 };
-// Epilogue warps per CTA: two per TMEM lane quadrant, each taking half of the tile's columns.
+// Epilogue warps per CTA: EPI_WARPS / 4 per TMEM lane quadrant, each taking an equal share (at least
+// 64 columns) of the tile's columns; EPI_SLOTS staging tiles of 4 KB per warp.
 constexpr int EPI_WARPS = 8;
-constexpr uint32_t EPI_SMEM_BYTES = EPI_WARPS * 2 * 4096;
+constexpr int EPI_SLOTS = 2;
+constexpr uint32_t EPI_SMEM_BYTES = EPI_WARPS * EPI_SLOTS * 4096;
 
 __device__ __forceinline__ uint32_t sw128_off(int r, int k) { return (uint32_t)(r * 128 + ((k ^ (r & 7)) << 4)); }
 
-// 32 values of row r of a tile with 128-byte rows (128-byte swizzle), starting at 16-byte unit u0
-// (fp32: 8 units, bf16: 4 units)
-template <bool F32>
+// NV values of row r of a tile with 128-byte rows (128-byte swizzle), starting at 16-byte unit u0
+// (NV / 4 units in fp32, NV / 8 in bf16)
+template <bool F32, int NV>
 __device__ __forceinline__ void stage_write(uint8_t* tile, int r, int u0, const float* v) {
 #pragma unroll
-  for (int k = 0; k < (F32 ? 8 : 4); ++k) {
+  for (int k = 0; k < (F32 ? NV / 4 : NV / 8); ++k) {
     const uint32_t off = sw128_off(r, u0 + k);
     if (F32) {
       *reinterpret_cast<float4*>(tile + off) = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
@@ -284,10 +290,10 @@ __device__ __forceinline__ void stage_write(uint8_t* tile, int r, int u0, const 
   }
 }
 
-template <bool F32>
+template <bool F32, int NV>
 __device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, float* p) {
 #pragma unroll
-  for (int k = 0; k < (F32 ? 8 : 4); ++k) {
+  for (int k = 0; k < (F32 ? NV / 4 : NV / 8); ++k) {
     const uint32_t off = sw128_off(r, u0 + k);
     if (F32) {
       const float4 a = *reinterpret_cast<const float4*>(tile + off);
@@ -313,19 +319,19 @@ __device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, f
 // EPI_MODE_WARP: one chunk (32 rows x 128 bytes: 32 fp32 / 64 bf16 columns at col0) of the warp's
 // rows row_base..+31; taddr = this warp's TMEM quadrant at the chunk's first column. n counts the
 // warp's staged chunks (slot n % 2, barrier phase n / 2). False if the aux wait gave up.
-// Aux tile of one staged chunk (32 rows x 128 bytes) into slot n & 1 of this warp; lane 0 only. The
-// caller has made sure the slot's previous store has read it.
+// Aux tile of one staged chunk (32 rows x 128 bytes) into slot n % EPI_SLOTS of this warp; lane 0
+// only. The caller has made sure the slot's previous store has read it.
 __device__ __forceinline__ void epi_aux_issue(const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int n,
                                               int col0, int row_base, int b) {
-  const int sl = n & 1;
+  const int sl = n % EPI_SLOTS;
   mbar_arrive_expect_tx(&abar[sl], 4096u);
   tma_load_3d(tma_aux, slots + sl * 4096, &abar[sl], col0, row_base, b);
 }
 
-// One staged chunk of a warp: 32 rows x (32 fp32 | 64 bf16) columns through slot n & 1. With a tile
-// aux, the chunk's aux was issued earlier (epi_aux_issue with the same n); after the chunk's store
-// the slot is refilled with the aux of the chunk two ahead (next_col0 >= 0), which then loads while
-// the next chunk is processed.
+// One staged chunk of a warp: 32 rows x (32 fp32 | 64 bf16) columns through slot n % EPI_SLOTS. With
+// a tile aux, the chunk's aux was issued earlier (epi_aux_issue with the same n); after the chunk's
+// store the slot is refilled with the aux of the chunk EPI_SLOTS ahead (next_col0 >= 0), which then
+// loads while the chunks in between are processed.
 template <bool F32>
 __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
                                                const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
@@ -334,29 +340,31 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
                                                volatile int* abort_flag, int site) {
   const int lane = threadIdx.x & 31;
   const bool aux = has_tile_aux(e.kind);
-  const int sl = n & 1;
-  const uint32_t parity = (uint32_t)(n >> 1) & 1u;
+  const int sl = n % EPI_SLOTS;
+  const uint32_t parity = (uint32_t)(n / EPI_SLOTS) & 1u;
   ++n;
   uint8_t* tile = slots + sl * 4096;
   if (!aux) {
-    if (lane == 0) bulk_wait_group_read<1>();  // the store of this warp's chunk n - 2 has read the slot
+    if (lane == 0) bulk_wait_group_read<EPI_SLOTS - 1>();  // the store of chunk n - EPI_SLOTS has read the slot
     __syncwarp();
   } else if (!wait_or_abort(&abar[sl], parity, abort_flag, site)) {
     return false;
   }
+  // 16 columns at a time (registers: 16 accumulator + 16 aux values)
 #pragma unroll 1
-  for (int h = 0; h < (F32 ? 1 : 2); ++h) {
-    float v[32], p[32];
-    tmem_ld_32x32(taddr + (uint32_t)(32 * h), v);
+  for (int h = 0; h < (F32 ? 2 : 4); ++h) {
+    float v[16], p[16];
+    tmem_ld_32x16(taddr + (uint32_t)(16 * h), v);
+    const int u0 = F32 ? 4 * h : 2 * h;
     if (aux) {
-      stage_read<F32>(tile, lane, 4 * h, p);
+      stage_read<F32, 16>(tile, lane, u0, p);
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = 0.f;
+      for (int i = 0; i < 16; ++i) p[i] = 0.f;
     }
-    const int c = col0 + 32 * h;
-    epilogue_math<32>(e, gl2, row_base + lane, c, min(32, s.N - c), v, p, dg_acc);
-    stage_write<F32>(tile, lane, 4 * h, v);
+    const int c = col0 + 16 * h;
+    epilogue_math<16>(e, gl2, row_base + lane, c, min(16, s.N - c), v, p, dg_acc);
+    stage_write<F32, 16>(tile, lane, u0, v);
   }
   fence_proxy_async_smem();
   __syncwarp();
@@ -365,7 +373,7 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
     bulk_commit_group();
     if (aux && next_col0 >= 0) {
       bulk_wait_group_read<0>();  // the store just issued has read the slot
-      epi_aux_issue(tma_aux, slots, abar, n + 1, next_col0, row_base, b);
+      epi_aux_issue(tma_aux, slots, abar, n - 1 + EPI_SLOTS, next_col0, row_base, b);
       ++n_issued;
     }
   }
@@ -374,10 +382,11 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
 
 // The epilogue warps (2 .. 2 + EPI_WARPS - 1) of both tensor-core kernels: for every tile of this
 // CTA (t_first, t_first + t_stride, ...) wait for its accumulator, write it through the epilogue
-// and hand the TMEM buffer back. Warp w reads TMEM lane quadrant w % 4 and column half
-// (w - 2) / 4. cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows); partials for
-// EPI_DECAY_DG go to tile_partial[part_stride * t + part_off + (w - 2)], row sums for EPI_RELU2 to
-// row_partial[row][2 * column block + half].
+// and hand the TMEM buffer back. Warp w reads TMEM lane quadrant w % 4 and the PART columns from
+// part * PART, part = (w - 2) / 4 (warps past the tile width only keep the barrier count).
+// cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows); partials for EPI_DECAY_DG go
+// to tile_partial[part_stride * t + part_off + (w - 2)], row sums for EPI_RELU2 and the (max, sum)
+// pairs of EPI_LSE to the 64-column slot of the warp's first column.
 template <int BM, int BN, bool PAIR>
 __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const GemmEpilogue& epi,
                                                const CUtensorMap* tma_out, const CUtensorMap* tma_aux,
@@ -386,17 +395,18 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
                                                uint64_t* tfull, uint64_t* tempty, uint32_t leader_tempty,
                                                uint8_t* stage, uint64_t* aux_bar, volatile int* abort_flag,
                                                int site, int part_stride, int part_off) {
-  constexpr int HALF = BN / 2;
+  constexpr int PART = BN / (EPI_WARPS / 4) < 64 ? 64 : BN / (EPI_WARPS / 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ew = warp - 2;
   const int quad = warp & 3;
-  const int half = ew >> 2;
+  const int part = ew >> 2;
+  const bool active = part * PART < BN;
   const int mode = epi.staged;
   const bool f32 = epi.out_dtype == ULM_F32;
   const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
-  uint8_t* wslots = stage + ew * 8192;  // this warp's two 4 KB slots
-  uint64_t* wbar = aux_bar + ew * 2;
-  int n = 0;         // staged chunks of this warp so far (slot n & 1)
+  uint8_t* wslots = stage + ew * (EPI_SLOTS * 4096);  // this warp's staging tiles
+  uint64_t* wbar = aux_bar + ew * EPI_SLOTS;
+  int n = 0;         // staged chunks of this warp so far (slot n % EPI_SLOTS)
   int n_issued = 0;  // aux loads issued by this warp (lane 0's count)
   int j = 0;
   bool ok = true;
@@ -412,13 +422,14 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     const uint32_t acc_phase = (uint32_t)(jj >> 1) & 1u;
     const int row_base = tc.mb * BM + cta_rows + quad * 32;
     const int row = row_base + lane;
-    const int col_base = tc.nb * BN + half * HALF;
-    // staged chunks of this warp in this tile; with a tile aux the first two chunks' aux tiles load
-    // now, while the tile's MMAs run
-    const int nch = (row_base < shape.M && col_base < shape.N) ? min(HALF / cw, (shape.N - col_base + cw - 1) / cw) : 0;
+    const int col_base = tc.nb * BN + part * PART;
+    const bool cols = active && row_base < shape.M && col_base < shape.N;
+    // staged chunks of this warp in this tile; with a tile aux the first EPI_SLOTS chunks' aux tiles
+    // load now, while the tile's MMAs run
+    const int nch = cols ? min(PART / cw, (shape.N - col_base + cw - 1) / cw) : 0;
     if (warp_aux && lane == 0 && epi.kind != EPI_LSE) {
       bulk_wait_group_read<0>();  // every earlier store of this warp has read its slot
-      for (int i = 0; i < nch && i < 2; ++i) {
+      for (int i = 0; i < nch && i < EPI_SLOTS; ++i) {
         epi_aux_issue(tma_aux, wslots, wbar, n + i, col_base + i * cw, row_base, tc.b);
         ++n_issued;
       }
@@ -428,18 +439,20 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
       break;
     }
     tc_fence_after();
-    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + half * HALF);
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + part * PART);
     float dg_acc = 0.f;
-    if (epi.kind == EPI_LSE) {
+    if (!cols) {
+      // nothing of this tile for this warp: only its barrier arrival below
+    } else if (epi.kind == EPI_LSE) {
       float m = -INFINITY, ssum = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < HALF; c += 32) {
-        float v[32];
-        tmem_ld_32x32(taddr + (uint32_t)c, v);
-        lse_update32(epi, row, col_base + c, min(32, shape.N - (col_base + c)), v, m, ssum);
+      for (int c = 0; c < PART; c += 16) {
+        float v[16];
+        tmem_ld_32x16(taddr + (uint32_t)c, v);
+        lse_update<16>(epi, row, col_base + c, min(16, shape.N - (col_base + c)), v, m, ssum);
       }
       if (row < shape.M) {
-        float* pp = epi.row_partial + ((int64_t)row * epi.part_ld + 2 * tc.nb + half) * 2;
+        float* pp = epi.row_partial + ((int64_t)row * epi.part_ld + col_base / 64) * 2;
         pp[0] = m;
         pp[1] = ssum;
       }
@@ -447,7 +460,7 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
 #pragma unroll 1
       for (int i = 0; i < nch && ok; ++i) {
         const int c = i * cw;
-        const int next = i + 2 < nch ? col_base + c + 2 * cw : -1;
+        const int next = i + EPI_SLOTS < nch ? col_base + c + EPI_SLOTS * cw : -1;
         ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b, row_base,
                                         col_base + c, next, taddr + (uint32_t)c, dg_acc, abort_flag, site)
                  : epi_chunk_warp<false>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b,
@@ -455,10 +468,10 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
       }
     } else {
 #pragma unroll 1
-      for (int c = 0; c < HALF; c += 32) {
-        float v[32];
-        tmem_ld_32x32(taddr + (uint32_t)c, v);
-        epilogue_store32(epi, shape, gl2, tc.b, row, col_base + c, v, dg_acc);
+      for (int c = 0; c < PART; c += 16) {
+        float v[16];
+        tmem_ld_32x16(taddr + (uint32_t)c, v);
+        epilogue_store<16>(epi, shape, gl2, tc.b, row, col_base + c, v, dg_acc);
       }
     }
     if (!ok) break;
@@ -470,8 +483,8 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
       else
         mbar_arrive(&tempty[acc]);
     }
-    if (epi.kind == EPI_RELU2 && epi.row_partial && row < shape.M)
-      epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + 2 * tc.nb + half] = dg_acc;
+    if (epi.kind == EPI_RELU2 && epi.row_partial && cols && row < shape.M)
+      epi.row_partial[((int64_t)tc.b * shape.M + row) * epi.part_ld + col_base / 64] = dg_acc;
     if (epi.kind == EPI_DECAY_DG) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dg_acc += __shfl_xor_sync(0xffffffffu, dg_acc, o);
@@ -482,9 +495,10 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     // aux loads still in flight after an abort (the last one of each slot) land before the CTA
     // exits; stores complete
     if (!ok && warp_aux) {
-      for (int k = max(0, n_issued - 2); k < n_issued; ++k) {
+      for (int k = max(0, n_issued - EPI_SLOTS); k < n_issued; ++k) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&wbar[k & 1], (uint32_t)(k >> 1) & 1u) && globaltimer_ns() - t0 < 100000000ull) {
+        while (!mbar_try_wait(&wbar[k % EPI_SLOTS], (uint32_t)(k / EPI_SLOTS) & 1u) &&
+               globaltimer_ns() - t0 < 100000000ull) {
         }
       }
     }
@@ -530,14 +544,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 staging tiles
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // EPI_SLOTS staging tiles per epilogue warp
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // 2 per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * EPI_WARPS);
+  uint64_t* aux_bar = drain + 1;  // EPI_SLOTS per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_SLOTS * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -553,7 +567,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < EPI_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -698,7 +712,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5, TMEM lane quadrant = warp % 4) ----------------
+    // ---------------- epilogue (warps 2.., TMEM lane quadrant = warp % 4) ----------------
     epilogue_warps<TC_BM, BN, false>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
                                      blockIdx.x, gridDim.x, 0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar,
                                      abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, EPI_WARPS, 0);
@@ -751,14 +765,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 staging tiles
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // EPI_SLOTS staging tiles per epilogue warp
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // 2 per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + 2 * EPI_WARPS);
+  uint64_t* aux_bar = drain + 1;  // EPI_SLOTS per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_SLOTS * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -778,7 +792,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 2 * EPI_WARPS);  // the epilogue warps of both CTAs of the pair
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < 2 * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < EPI_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -924,7 +938,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    // ---------------- epilogue (warps 2.. of both CTAs) ----------------
     epilogue_warps<BM, BN, true>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
                                  pairs, (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0),
                                  epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 2 * EPI_WARPS,
