@@ -259,10 +259,11 @@ __device__ __forceinline__ int schedule_tile(int t, int P, int total, int balanc
 // EPI_MODE_DIRECT stores row segments straight from registers.
 enum { EPI_MODE_DIRECT = 0, EPI_MODE_WARP = 1 };
 // Epilogue warps per CTA: EPI_WARPS / 4 per TMEM lane quadrant, each taking an equal share (at least
-// 64 columns) of the tile's columns; EPI_SLOTS staging tiles of 4 KB per warp.
+// 64 columns) of the tile's columns, with SLOTS staging tiles of 4 KB (a kernel parameter: more
+// slots let more aux tiles load ahead, fewer leave room for more operand stages).
 constexpr int EPI_WARPS = 8;
-constexpr int EPI_SLOTS = 2;
-constexpr uint32_t EPI_SMEM_BYTES = EPI_WARPS * EPI_SLOTS * 4096;
+constexpr int EPI_MAX_SLOTS = 2;
+__host__ __device__ constexpr uint32_t epi_smem_bytes(int slots) { return EPI_WARPS * slots * 4096u; }
 
 __device__ __forceinline__ uint32_t sw128_off(int r, int k) { return (uint32_t)(r * 128 + ((k ^ (r & 7)) << 4)); }
 
@@ -319,20 +320,21 @@ __device__ __forceinline__ void stage_read(const uint8_t* tile, int r, int u0, f
 // EPI_MODE_WARP: one chunk (32 rows x 128 bytes: 32 fp32 / 64 bf16 columns at col0) of the warp's
 // rows row_base..+31; taddr = this warp's TMEM quadrant at the chunk's first column. n counts the
 // warp's staged chunks (slot n % 2, barrier phase n / 2). False if the aux wait gave up.
-// Aux tile of one staged chunk (32 rows x 128 bytes) into slot n % EPI_SLOTS of this warp; lane 0
-// only. The caller has made sure the slot's previous store has read it.
+// Aux tile of one staged chunk (32 rows x 128 bytes) into slot n % SLOTS of this warp; lane 0 only.
+// The caller has made sure the slot's previous store has read it.
+template <int SLOTS>
 __device__ __forceinline__ void epi_aux_issue(const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int n,
                                               int col0, int row_base, int b) {
-  const int sl = n % EPI_SLOTS;
+  const int sl = n % SLOTS;
   mbar_arrive_expect_tx(&abar[sl], 4096u);
   tma_load_3d(tma_aux, slots + sl * 4096, &abar[sl], col0, row_base, b);
 }
 
-// One staged chunk of a warp: 32 rows x (32 fp32 | 64 bf16) columns through slot n % EPI_SLOTS. With
-// a tile aux, the chunk's aux was issued earlier (epi_aux_issue with the same n); after the chunk's
-// store the slot is refilled with the aux of the chunk EPI_SLOTS ahead (next_col0 >= 0), which then
-// loads while the chunks in between are processed.
-template <bool F32>
+// One staged chunk of a warp: 32 rows x (32 fp32 | 64 bf16) columns through slot n % SLOTS. With a
+// tile aux, the chunk's aux was issued earlier (epi_aux_issue with the same n); after the chunk's
+// store the slot is refilled with the aux of the chunk SLOTS ahead (next_col0 >= 0), which then loads
+// while the chunks in between are processed.
+template <bool F32, int SLOTS>
 __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const GemmShape& s, const CUtensorMap* tma_out,
                                                const CUtensorMap* tma_aux, uint8_t* slots, uint64_t* abar, int& n,
                                                int& n_issued, float gl2, int b, int row_base, int col0,
@@ -340,12 +342,12 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
                                                volatile int* abort_flag, int site) {
   const int lane = threadIdx.x & 31;
   const bool aux = has_tile_aux(e.kind);
-  const int sl = n % EPI_SLOTS;
-  const uint32_t parity = (uint32_t)(n / EPI_SLOTS) & 1u;
+  const int sl = n % SLOTS;
+  const uint32_t parity = (uint32_t)(n / SLOTS) & 1u;
   ++n;
   uint8_t* tile = slots + sl * 4096;
   if (!aux) {
-    if (lane == 0) bulk_wait_group_read<EPI_SLOTS - 1>();  // the store of chunk n - EPI_SLOTS has read the slot
+    if (lane == 0) bulk_wait_group_read<SLOTS - 1>();  // the store of chunk n - SLOTS has read the slot
     __syncwarp();
   } else if (!wait_or_abort(&abar[sl], parity, abort_flag, site)) {
     return false;
@@ -373,7 +375,7 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
     bulk_commit_group();
     if (aux && next_col0 >= 0) {
       bulk_wait_group_read<0>();  // the store just issued has read the slot
-      epi_aux_issue(tma_aux, slots, abar, n - 1 + EPI_SLOTS, next_col0, row_base, b);
+      epi_aux_issue<SLOTS>(tma_aux, slots, abar, n - 1 + SLOTS, next_col0, row_base, b);
       ++n_issued;
     }
   }
@@ -387,7 +389,7 @@ __device__ __forceinline__ bool epi_chunk_warp(const GemmEpilogue& e, const Gemm
 // cta_rows = the CTA's row offset inside a BM-row tile (its 128 rows); partials for EPI_DECAY_DG go
 // to tile_partial[part_stride * t + part_off + (w - 2)], row sums for EPI_RELU2 and the (max, sum)
 // pairs of EPI_LSE to the 64-column slot of the warp's first column.
-template <int BM, int BN, bool PAIR>
+template <int BM, int BN, bool PAIR, int SLOTS>
 __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const GemmEpilogue& epi,
                                                const CUtensorMap* tma_out, const CUtensorMap* tma_aux,
                                                int m_blocks, int n_blocks, int tiles_per_batch, int total_tiles,
@@ -404,9 +406,9 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
   const int mode = epi.staged;
   const bool f32 = epi.out_dtype == ULM_F32;
   const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
-  uint8_t* wslots = stage + ew * (EPI_SLOTS * 4096);  // this warp's staging tiles
-  uint64_t* wbar = aux_bar + ew * EPI_SLOTS;
-  int n = 0;         // staged chunks of this warp so far (slot n % EPI_SLOTS)
+  uint8_t* wslots = stage + ew * (SLOTS * 4096);  // this warp's staging tiles
+  uint64_t* wbar = aux_bar + ew * SLOTS;
+  int n = 0;         // staged chunks of this warp so far (slot n % SLOTS)
   int n_issued = 0;  // aux loads issued by this warp (lane 0's count)
   int j = 0;
   bool ok = true;
@@ -424,13 +426,13 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     const int row = row_base + lane;
     const int col_base = tc.nb * BN + part * PART;
     const bool cols = active && row_base < shape.M && col_base < shape.N;
-    // staged chunks of this warp in this tile; with a tile aux the first EPI_SLOTS chunks' aux tiles
-    // load now, while the tile's MMAs run
+    // staged chunks of this warp in this tile; with a tile aux the first SLOTS chunks' aux tiles load
+    // now, while the tile's MMAs run
     const int nch = cols ? min(PART / cw, (shape.N - col_base + cw - 1) / cw) : 0;
     if (warp_aux && lane == 0 && epi.kind != EPI_LSE) {
       bulk_wait_group_read<0>();  // every earlier store of this warp has read its slot
-      for (int i = 0; i < nch && i < EPI_SLOTS; ++i) {
-        epi_aux_issue(tma_aux, wslots, wbar, n + i, col_base + i * cw, row_base, tc.b);
+      for (int i = 0; i < nch && i < SLOTS; ++i) {
+        epi_aux_issue<SLOTS>(tma_aux, wslots, wbar, n + i, col_base + i * cw, row_base, tc.b);
         ++n_issued;
       }
     }
@@ -460,10 +462,10 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
 #pragma unroll 1
       for (int i = 0; i < nch && ok; ++i) {
         const int c = i * cw;
-        const int next = i + EPI_SLOTS < nch ? col_base + c + EPI_SLOTS * cw : -1;
-        ok = f32 ? epi_chunk_warp<true>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b, row_base,
+        const int next = i + SLOTS < nch ? col_base + c + SLOTS * cw : -1;
+        ok = f32 ? epi_chunk_warp<true, SLOTS>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b, row_base,
                                         col_base + c, next, taddr + (uint32_t)c, dg_acc, abort_flag, site)
-                 : epi_chunk_warp<false>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b,
+                 : epi_chunk_warp<false, SLOTS>(epi, shape, tma_out, tma_aux, wslots, wbar, n, n_issued, gl2, tc.b,
                                          row_base, col_base + c, next, taddr + (uint32_t)c, dg_acc, abort_flag, site);
       }
     } else {
@@ -495,9 +497,9 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
     // aux loads still in flight after an abort (the last one of each slot) land before the CTA
     // exits; stores complete
     if (!ok && warp_aux) {
-      for (int k = max(0, n_issued - EPI_SLOTS); k < n_issued; ++k) {
+      for (int k = max(0, n_issued - SLOTS); k < n_issued; ++k) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&wbar[k % EPI_SLOTS], (uint32_t)(k / EPI_SLOTS) & 1u) &&
+        while (!mbar_try_wait(&wbar[k % SLOTS], (uint32_t)(k / SLOTS) & 1u) &&
                globaltimer_ns() - t0 < 100000000ull) {
         }
       }
@@ -516,12 +518,13 @@ constexpr int TC_THREADS = 64 + 32 * EPI_WARPS;
 template <int BN>
 struct TcConfig {
   static constexpr int STAGES = BN == 256 ? 3 : 5;
+  static constexpr int EPI_SLOTS = 2;
   static constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;
   static constexpr uint32_t B_BYTES = BN * TC_BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   // stages + staging tiles of the epilogue + 1024 alignment slack + barriers / TMEM slot / flags
-  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 512;
+  static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + epi_smem_bytes(EPI_SLOTS) + 1024 + 512;
 };
 
 template <int BN, bool A_MN, bool B_MN>
@@ -544,14 +547,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // EPI_SLOTS staging tiles per epilogue warp
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // Cfg::EPI_SLOTS staging tiles per epilogue warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + epi_smem_bytes(Cfg::EPI_SLOTS));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // EPI_SLOTS per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_SLOTS * EPI_WARPS);
+  uint64_t* aux_bar = drain + 1;  // up to EPI_MAX_SLOTS per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_MAX_SLOTS * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -567,7 +570,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], EPI_WARPS);
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < EPI_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < EPI_MAX_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -713,7 +716,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2.., TMEM lane quadrant = warp % 4) ----------------
-    epilogue_warps<TC_BM, BN, false>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
+    epilogue_warps<TC_BM, BN, false, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
                                      blockIdx.x, gridDim.x, 0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar,
                                      abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, EPI_WARPS, 0);
   }
@@ -744,7 +747,10 @@ struct Tc2Config {
   static constexpr uint32_t B_BYTES = 128 * TC_BK * 2;  // this CTA's 128 columns of B
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TMEM_COLS = 2 * TC2_BN;
-  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + EPI_SMEM_BYTES + 1024 + 512;
+  // two staging tiles per epilogue warp (three would leave room for only four operand stages, which
+  // slows the long-K products more than the extra aux load in flight speeds up the fp32 epilogues)
+  static constexpr int EPI_SLOTS = 2;
+  static constexpr uint32_t SMEM_BYTES = TC2_STAGES * STAGE_BYTES + epi_smem_bytes(EPI_SLOTS) + 1024 + 512;
 };
 
 template <bool A_MN, bool B_MN>
@@ -765,14 +771,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // EPI_SLOTS staging tiles per epilogue warp
-  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + EPI_SMEM_BYTES);
+  uint8_t* epi_stage = smem + STAGES * Cfg::STAGE_BYTES;  // Cfg::EPI_SLOTS staging tiles per epilogue warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + epi_smem_bytes(Cfg::EPI_SLOTS));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_bar = drain + 1;  // EPI_SLOTS per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_SLOTS * EPI_WARPS);
+  uint64_t* aux_bar = drain + 1;  // up to EPI_MAX_SLOTS per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_bar + EPI_MAX_SLOTS * EPI_WARPS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -792,7 +798,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 2 * EPI_WARPS);  // the epilogue warps of both CTAs of the pair
     }
     mbar_init(drain, 1);
-    for (int i = 0; i < EPI_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
+    for (int i = 0; i < EPI_MAX_SLOTS * EPI_WARPS; ++i) mbar_init(&aux_bar[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -939,7 +945,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2.. of both CTAs) ----------------
-    epilogue_warps<BM, BN, true>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
+    epilogue_warps<BM, BN, true, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
                                  pairs, (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0),
                                  epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 2 * EPI_WARPS,
                                  (int)rank * EPI_WARPS);
