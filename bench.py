@@ -181,8 +181,8 @@ def run_reference(args, rank):
 
 
 # DRAM bytes (read + write) of the six fast-memory products of one block at the 110M shape, summed
-# over one ncu capture of `bench.py --profile-step` (the launch list in profiles/)
-PRODUCTS_DRAM_BYTES = 770134528
+# over one ncu capture of `bench.py --profile-block` (profiles/tc_gemm_products_110M.md)
+PRODUCTS_DRAM_BYTES = 783100000
 
 DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
 
@@ -420,6 +420,9 @@ def main():
     ap.add_argument("--no-head", action="store_true", help="skip the fused LM-head measurement")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
+    ap.add_argument("--profile-block", action="store_true",
+                    help="run one block of the step (fwd + bwd) twice, no timing or report (for ncu captures "
+                         "of single kernels on a small case)")
     ap.add_argument("--profile-decode", action="store_true",
                     help="run a few batch-16 decode steps at the 110M shape, no report (for ncu)")
     args = ap.parse_args()
@@ -453,7 +456,7 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    W = WORKLOAD
+    W = dict(WORKLOAD, L=1) if args.profile_block else WORKLOAD
     prec = PRECISION[args.precision]
     h, v, dq_out, dfast, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
                                               seed=rank)
@@ -475,7 +478,7 @@ def main():
         bucket.all_reduce(average=True)
         return bucket.flat
 
-    if args.profile_step:
+    if args.profile_step or args.profile_block:
         step(h, v, dq_out, dfast)
         step(h, v, dq_out, dfast)
         torch.cuda.synchronize()
@@ -599,9 +602,9 @@ def main():
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": PRODUCTS_DRAM_BYTES,
                 "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the six products of one block, "
-                                "one ncu capture (profiles/fast_memory_path_step_110M_launches.md)",
+                                "one ncu capture (profiles/tc_gemm_products_110M.md)",
                 "algorithmic_flops_per_block": flops,
-                "kernel": "tc_gemm_kernel (6 causal products per block fwd+bwd)",
+                "kernel": "tc2_gemm_kernel (6 causal products per block fwd+bwd)",
                 "peak_source": pk["source"],
                 "per_launch_ms": [round(s * 1e3, 4) for _, s in per],
                 "per_launch_tflops": [round(f / s / 1e12, 1) for f, s in per]}

@@ -250,18 +250,39 @@ __global__ void col_sum_kernel(const void* __restrict__ x, int64_t ld, int64_t r
   part[(int64_t)blockIdx.y * cols + col] = s;
 }
 
-// out[i] = sum over p of part[p][i] for n % 4 == 0 and 16-byte aligned rows: a CTA covers 128
-// consecutive outputs (4 per lane); warp w adds parts w, w + 8, ... in order, then the eight warp
-// sums are added in warp order (a fixed order: deterministic)
+// out[g][i] = sum of part[p][i] over the parts p of group g (parts g * per .. g * per + per - 1, in
+// order): one thread per 4 consecutive outputs, blockIdx.y = group; n % 4 == 0, 16-byte aligned rows
 __global__ void __launch_bounds__(256)
-    sum_parts4_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, float* __restrict__ out) {
+    sum_groups4_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, int64_t per, float* __restrict__ out) {
   pdl_enter();
-  __shared__ float4 red[8][32];
-  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t i = ((int64_t)blockIdx.x * 32 + lane) * 4;
+  const int64_t i = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
+  if (i >= n) return;
+  const int64_t p0 = (int64_t)blockIdx.y * per, p1 = min(nparts, p0 + per);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int64_t p = p0; p < p1; ++p) {
+    const float4 a = *reinterpret_cast<const float4*>(part + p * n + i);
+    acc.x += a.x;
+    acc.y += a.y;
+    acc.z += a.z;
+    acc.w += a.w;
+  }
+  *reinterpret_cast<float4*>(out + (int64_t)blockIdx.y * n + i) = acc;
+}
+
+// out[i] = sum over p of part[p][i] for many parts and few outputs: a CTA covers 8 groups of 4
+// consecutive outputs; its 32 part lanes (threadIdx.x / 8) add parts lane, lane + 32, ... in order,
+// then the 32 lane sums are added by a fixed tree. n % 4 == 0, 16-byte aligned rows.
+__global__ void __launch_bounds__(256)
+    sum_parts_tree_kernel(const float* __restrict__ part, int64_t nparts, int64_t n, float* __restrict__ out) {
+  pdl_enter();
+  __shared__ float4 red[32][8];
+  const int c = threadIdx.x & 7, pl = threadIdx.x >> 3;
+  const int64_t i = ((int64_t)blockIdx.x * 8 + c) * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (i < n) {
-    for (int64_t p = wp; p < nparts; p += 8) {
+#pragma unroll 4
+    for (int64_t p = pl; p < nparts; p += 32) {
       const float4 a = *reinterpret_cast<const float4*>(part + p * n + i);
       acc.x += a.x;
       acc.y += a.y;
@@ -269,19 +290,20 @@ __global__ void __launch_bounds__(256)
       acc.w += a.w;
     }
   }
-  red[wp][lane] = acc;
+  red[pl][c] = acc;
   __syncthreads();
-  if (wp == 0 && i < n) {
-    float4 t = red[0][lane];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) {
-      t.x += red[w][lane].x;
-      t.y += red[w][lane].y;
-      t.z += red[w][lane].z;
-      t.w += red[w][lane].w;
+  for (int st = 16; st > 0; st >>= 1) {
+    if (pl < st) {
+      const float4 b = red[pl + st][c];
+      float4& a = red[pl][c];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
     }
-    *reinterpret_cast<float4*>(out + i) = t;
+    __syncthreads();
   }
+  if (pl == 0 && i < n) *reinterpret_cast<float4*>(out + i) = red[0][c];
 }
 
 // out[i] = sum_p part[p][i] over nparts, in order (any n)
@@ -409,6 +431,9 @@ constexpr int DB_ROWS_PER_CHUNK = 256;
 
 inline int64_t al256(int64_t n) { return (n + 255) / 256 * 256; }
 
+// Partial sums over more than SUM_GROUP parts use the 32-lane tree kernel.
+constexpr int64_t SUM_GROUP = 16;
+
 // Split of the B*T contraction of dK = da^T u into S k ranges: enough 256 x 256 tiles to fill the
 // CTA pairs once (S x tiles <= pairs), at most 8, each range at least 1024 rows and none empty.
 inline int addr_split(int64_t rows, int64_t M, int64_t D) {
@@ -464,15 +489,18 @@ int addr_check(int h_dtype, int prec, int64_t B, int64_t T, int64_t D, int64_t M
 
 }  // namespace
 
-// out = sum of nparts arrays of n floats, in a fixed order
+// out = sum of nparts arrays of n floats, in a fixed order: one thread per 4 outputs adding the parts
+// in order when they are few (at most SUM_GROUP), else 32 part lanes per output and a fixed tree.
 int sum_parts(const float* part, int64_t nparts, int64_t n, float* out, cudaStream_t st) {
   if (n % 4 == 0 && is_aligned16(part) && is_aligned16(out)) {
-    if (int rc = launch_pdl(sum_parts4_kernel, dim3((unsigned)cdiv(n, 128)), dim3(256), 0, st, part, nparts, n, out))
-      return rc;
-  } else {
-    sum_parts_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 16 * 148), 256, 0, st>>>(part, nparts, n, out);
-    ULM_LAUNCH_CHECK("sum_parts_kernel");
+    if (nparts > SUM_GROUP)
+      return launch_pdl(sum_parts_tree_kernel, dim3((unsigned)cdiv(n / 4, 8)), dim3(256), 0, st, part, nparts, n,
+                        out);
+    return launch_pdl(sum_groups4_kernel, dim3((unsigned)cdiv(n / 4, 256), 1), dim3(256), 0, st, part, nparts, n,
+                      nparts, out);
   }
+  sum_parts_kernel<<<(unsigned)std::min<int64_t>(cdiv(n, 256), 16 * 148), 256, 0, st>>>(part, nparts, n, out);
+  ULM_LAUNCH_CHECK("sum_parts_kernel");
   return ULM_OK;
 }
 
