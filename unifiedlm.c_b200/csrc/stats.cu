@@ -712,7 +712,8 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
   __shared__ __align__(8) uint64_t full[STAGES];
   __shared__ __align__(8) uint64_t xbar_f[2];  // lower ranks' forward totals of the item have arrived
   __shared__ __align__(8) uint64_t xbar_r[2];  // higher ranks' reverse totals have arrived
-  __shared__ float warp_sum[WARPS][32];
+  __shared__ float warp_sum[WARPS][32];     // reverse partial sums of the current item
+  __shared__ float warp_sum_f[2][WARPS][32];  // forward partial sums, by item parity
   __shared__ float warp_dw[WARPS][32];
   __shared__ float ctot_f[2][SCAN_MAX_CLUSTER][32];
   __shared__ float ctot_r[2][SCAN_MAX_CLUSTER][32];
@@ -771,10 +772,36 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
   const int o = (wp * SEG) * 32 + lane;
   double dg_acc = 0.0;
   float w_cur = 0.f;
+  // Forward part of item jn: wait for its tile, rescan the write addresses k of this CTA's rows from
+  // zero (warp_sum_f) and send the CTA's total into the higher ranks' slot jn & 1. Item jn + 1's
+  // forward part runs during item jn (after its reverse totals are sent), so the forward exchange
+  // is complete by the time item jn + 1 needs it.
+  auto forward_part = [&](int jn) {
+    if (!mbar_wait_bounded(&full[jn % STAGES], (uint32_t)(jn / STAGES) & 1u,
+                           ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+      raise_device_error(DEVERR_SCAN_TMA_WAIT);
+      ok_flag = 0;
+    }
+    __syncthreads();  // the tile and this item's row scales are visible to every thread
+    const float* s_kn = tile + (jn % STAGES) * stage_floats + 2 * TILE + 32 + o;
+    const float* sin = sinv[jn & 1] + wp * SEG;
+    float run = 0.f;
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_kn[i * 32] * sin[i]);
+    warp_sum_f[jn & 1][wp][lane] = run;
+    __syncthreads();
+    if (wp == 0) {
+      float tot = 0.f;
+      for (int jj = 0; jj < WARPS; ++jj) tot = fmaf(tot, lam_seg, warp_sum_f[jn & 1][jj][lane]);
+      const uint32_t slot = smem_u32(&ctot_f[jn & 1][cr][lane]), xb = smem_u32(&xbar_f[jn & 1]);
+      for (int jj = cr + 1; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
+    }
+  };
   if (k0 < n_items) {
     const int m_first = (k0 % nmb) * 32 + lane;
     w_cur = m_first < M ? w[m_first] : 0.f;
     den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
+    forward_part(0);
   }
   for (int j = 0;; ++j) {
     const int item = k0 + j * G;
@@ -785,18 +812,12 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
     const int xp = j & 1;
     const uint32_t xph = (uint32_t)(j >> 1) & 1u;
     const float* st = tile + (j % STAGES) * stage_floats;
-    // the next item's row scales and prior masses: loaded now, used after this item
+    // the next item's row scales and prior masses: loaded now, used from its forward part on
     const int item_n = item + G;
     const bool has_next = item_n < n_items;
     const int m_n = (item_n % nmb) * 32 + lane;
     const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
     const float w_n = (has_next && m_n < M) ? w[m_n] : 0.f;
-    if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u,
-                           ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
-      raise_device_error(DEVERR_SCAN_TMA_WAIT);
-      ok_flag = 0;
-    }
-    __syncthreads();
     const float* s_dqf = st + o;
     const float* s_dk = st + TILE + o;
     const float* s_k = st + 2 * TILE + 32 + o;  // k_t = r_{t-1}
@@ -805,26 +826,15 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
     const float* si = sinv[j & 1] + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
     const float wm = w_cur;
 
-    // forward scan of k to rebuild n_t (as stats_fwd_pipe_kernel)
-    float run = 0.f;
-#pragma unroll
-    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_k[i * 32] * si[i]);
-    warp_sum[wp][lane] = run;
-    __syncthreads();
-    if (wp == 0) {
-      float tot = 0.f;
-      for (int jj = 0; jj < WARPS; ++jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
-      const uint32_t slot = smem_u32(&ctot_f[xp][cr][lane]), xb = smem_u32(&xbar_f[xp]);
-      for (int jj = cr + 1; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
-    }
+    // carry of the forward scan into this warp's rows: lower ranks' totals, then lower warps'
     if (cr > 0 && !mbar_wait_bounded(&xbar_f[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
       ok_flag = 0;
     }
     float n = 0.f;
     for (int jj = 0; jj < cr; ++jj) n = fmaf(n, lam_cta, ctot_f[xp][jj][lane]);
-    for (int jj = 0; jj < wp; ++jj) n = fmaf(n, lam_seg, warp_sum[jj][lane]);
-    __syncthreads();  // warp_sum is reused below; every thread is past the wait on xbar_f[xp]
+    for (int jj = 0; jj < wp; ++jj) n = fmaf(n, lam_seg, warp_sum_f[xp][jj][lane]);
+    __syncthreads();  // every thread is past the wait on xbar_f[xp]
     if (threadIdx.x == 0 && cr > 0) mbar_arrive_expect_tx(&xbar_f[xp], (uint32_t)cr * 128u);
 
     float dw_acc = 0.f, dg_f = 0.f;
@@ -852,7 +862,7 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
       if (fast_identity) term += qq * dqfv;
       dg_f = fmaf((float)t - t_mid, term, dg_f);
     }
-    run = 0.f;
+    float run = 0.f;
 #pragma unroll
     for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dc_v[i]);
     warp_sum[wp][lane] = run;
@@ -868,6 +878,10 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
         for (int jj = 0; jj < WARPS; ++jj) s2 += warp_dw[jj][lane];
         part_dw[((int64_t)b * C + cr) * M + m] = s2;
       }
+    }
+    if (has_next) {
+      den_store(sinv[(j + 1) & 1], den, den_n, T, cta_t0 - 1, R);  // last read in item j - 1
+      forward_part(j + 1);
     }
     if (cr < C - 1 && !mbar_wait_bounded(&xbar_r[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
@@ -899,9 +913,8 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
       }
       dg_acc += (double)dg_s;
     }
-    if (has_next) den_store(sinv[(j + 1) & 1], den, den_n, T, cta_t0 - 1, R);  // last read in item j - 1
     w_cur = w_n;
-    __syncthreads();  // the stage, sinv[j & 1], warp_sum and warp_dw are free again
+    __syncthreads();  // this item's stage, sinv[j & 1], warp_sum and warp_dw are free again
     if (threadIdx.x == 0) {
       if (cr < C - 1) mbar_arrive_expect_tx(&xbar_r[xp], (uint32_t)(C - 1 - cr) * 128u);
       fence_proxy_async_smem();
