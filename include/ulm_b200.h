@@ -264,6 +264,32 @@ int ulm_lm_head_loss_bwd(const float* dloss, const float* count, const void* h_o
 
 int64_t ulm_lm_head_work_bytes(int64_t N, int64_t V, int64_t D, int prec);
 
+/* The path's whole backward for one block with unnormalised addresses z (ulm_address_fwd with
+ * normalize = 0): ulm_memory_bwd(dq_out, dfast, .., r = z, den, ..) followed by
+ * ulm_address_bwd(dr, z, den, normalized = 0, ..), in one call; same arguments and outputs as the
+ * two calls (dr is written as there), and the same results. In one call the statistics' dw / dg
+ * reductions overlap the address backward; all work is ordered on `stream` when it returns.
+ * Replaces: the backward of UnifiedBlock.forward's read path, model.py:70-84 (kernel.py:216-233
+ * and the prologue's autograd). */
+int ulm_addressed_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* z, const float* den,
+                             const float* g, const float* w, const float* q, const float* c, const void* qop,
+                             const void* kop, const void* vop, const void* P, void* doop, void* dS, float* dqf,
+                             float* dk, void* partial, float* dr, void* dv, float* dg, float* dw, const void* u_op,
+                             int64_t ld_u, const void* h, int h_dtype, const float* conv_w, int64_t conv_size,
+                             const void* key_w, int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w,
+                             float* dkey_b, float* deps, void* work, int64_t B, int64_t T, int64_t M, int64_t D,
+                             int prec, void* stream);
+
+/* The same for the fused combine: ulm_memory_combine_bwd followed by ulm_address_bwd (model.py:70-85
+ * with dropout 0). */
+int ulm_mixer_bwd(const void* dy, int dy_dtype, const float* z, const float* den, const float* g, const float* w,
+                  const float* mu, const float* q, const float* c, const void* qop, const void* kop, const void* vop,
+                  const void* P, void* doop, void* dS, void* mw, float* dqf, float* dk, void* partial, float* gpart,
+                  float* dr, void* dv, int dv_dtype, float* dg, float* dw, float* dmu, const void* u_op,
+                  int64_t ld_u, const void* h, int h_dtype, const float* conv_w, int64_t conv_size,
+                  const void* key_w, int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w, float* dkey_b,
+                  float* deps, void* work, int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream);
+
 /* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */
 
 /* Per block, once per weight set: prior[d][m] = ((1 - lam) * mu[d][m]) * w[m], the constant part of

@@ -47,6 +47,10 @@ SIGNATURES = {
     "ulm_address_bwd": (_I, [_P, _P, _P, _I, _P, _I64, _P, _I, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _P,
                              _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_address_bwd_work_bytes": (_I64, [_I64, _I64, _I64, _I64, _I]),
+    "ulm_addressed_memory_bwd": (_I, [_P, _P, _I] + [_P] * 19 + [_P, _I64, _P, _I, _P, _I64, _P, _I64] + [_P] * 6 +
+                                 [_I64] * 4 + [_I, _P]),
+    "ulm_mixer_bwd": (_I, [_P, _I] + [_P] * 20 + [_I, _P, _P, _P] + [_P, _I64, _P, _I, _P, _I64, _P, _I64] +
+                      [_P] * 6 + [_I64] * 4 + [_I, _P]),
     "ulm_lm_head_loss_fwd": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_lm_head_loss_bwd": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_lm_head_work_bytes": (_I64, [_I64, _I64, _I64, _I]),

@@ -10,16 +10,18 @@ and backward scans, the address backward) applies 1 / den to the rows it loads. 
 read-modify-write pass over the (B,T,M) fp32 addresses per block.
 
 The pair is the `torch.library` ops `ulm::addressed_memory_fwd` / `ulm::addressed_memory_bwd`
-(libulm_b200.so: ulm_address_fwd with normalize = 0, ulm_memory_fwd / ulm_memory_bwd with den,
-ulm_address_bwd with normalized = 0).
+(libulm_b200.so: ulm_address_fwd with normalize = 0 and ulm_memory_fwd with den; the backward is
+one call, ulm_addressed_memory_bwd = ulm_memory_bwd with den followed by ulm_address_bwd with
+normalized = 0).
 """
 from typing import Optional
 
 import torch
 
-from .kernel import (PRECISION, combine_bwd_raw, combine_fwd_fake, combine_fwd_raw, memory_bwd_raw, memory_fwd_fake,
-                     memory_fwd_raw, operand_or_input, unaliased)
-from .prologue import address_bwd_fake, address_bwd_raw, address_fwd_fake, address_fwd_raw
+from . import _lib as L
+from .kernel import (PRECISION, _op_dtype, _require_cuda, combine_fwd_fake, combine_fwd_raw, memory_fwd_fake,
+                     memory_fwd_raw, operand_copy, operand_ld, operand_or_input, unaliased)
+from .prologue import address_bwd_fake, address_fwd_fake, address_fwd_raw
 
 _OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
              torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]
@@ -42,6 +44,70 @@ def _fwd_fake(h, conv_w, key_w, key_b, eps, v, g, w, precision):
     return q, fast, z, den, u_op, kw, c, qop, kop, vop, P
 
 
+def _block_bwd_buffers(dfast_like, z, h, conv_w, v_dtype, precision, combine):
+    """Outputs and work buffers of the fused block backward (ulm_addressed_memory_bwd / ulm_mixer_bwd)."""
+    B, T, M = z.shape
+    D = h.shape[-1]
+    K = conv_w.shape[-1]
+    dev = z.device
+    opt = _op_dtype(precision)
+    lib = L.lib()
+    f32 = dict(device=dev, dtype=torch.float32)
+    bufs = dict(
+        dr=torch.empty(B, T, M, **f32), dv=torch.empty(B, T, D, device=dev, dtype=v_dtype),
+        dg=torch.empty((), **f32), dw=torch.empty(M, **f32), doop=operand_copy(dfast_like, opt),
+        dS=torch.empty(B, T, operand_ld(T), device=dev, dtype=opt), dqf=torch.empty(B, T, M, **f32),
+        dk=torch.empty(B, T, M, **f32),
+        partial=torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8),
+        dh=torch.empty(B, T, D, **f32), dconv=torch.empty(D, K, **f32), dkw=torch.empty(M, D, **f32),
+        dkb=torch.empty(M, **f32), deps=torch.empty((), **f32),
+        work=torch.empty(int(lib.ulm_address_bwd_work_bytes(B, T, D, M, precision)), device=dev, dtype=torch.uint8),
+        cw=conv_w.detach().reshape(D, K).float().contiguous())
+    if combine:
+        bufs["dmu"] = torch.empty(D, M, **f32)
+        bufs["mw"] = torch.empty(D, operand_ld(M), device=dev, dtype=opt)
+        bufs["gpart"] = torch.empty(int(lib.ulm_combine_grad_scratch(B, T, M, D)), device=dev, dtype=torch.uint8)
+    return bufs
+
+
+def addressed_memory_bwd_raw(dq_out, dfast, h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, vop, P, precision):
+    """ulm_addressed_memory_bwd on fresh buffers: (dh fp32, dconv_w, dkey_w, dkey_b, deps, dv, dg, dw)."""
+    _require_cuda(dfast, z, g, w, q, c, den, h)
+    B, T, M = z.shape
+    D = dfast.shape[-1]
+    K = conv_w.shape[-1]
+    o = _block_bwd_buffers(dfast, z, h, conv_w, dfast.dtype, precision, combine=False)
+    p = L.ptr
+    with torch.cuda.device(z.device):
+        L.check(L.lib().ulm_addressed_memory_bwd(
+            p(dq_out), p(dfast), L.dtype_code(dfast.dtype), p(z), p(den), p(g), p(w), p(q),
+            p(c) if c.numel() else None, p(qop), p(kop), p(vop), p(P), p(o["doop"]), p(o["dS"]), p(o["dqf"]),
+            p(o["dk"]), p(o["partial"]), p(o["dr"]), p(o["dv"]), p(o["dg"]), p(o["dw"]), p(u_op), u_op.shape[1],
+            p(h), L.dtype_code(h.dtype), p(o["cw"]), K, p(kw), kw.shape[1], p(o["dh"]), p(o["dconv"]), p(o["dkw"]),
+            p(o["dkb"]), p(o["deps"]), p(o["work"]), B, T, M, D, precision, L.stream_of(z)))
+    return (o["dh"], o["dconv"].reshape(D, 1, K), o["dkw"], o["dkb"], o["deps"], o["dv"], o["dg"], o["dw"])
+
+
+def mixer_bwd_raw(dy, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, v_dtype, precision):
+    """ulm_mixer_bwd on fresh buffers: (dh fp32, dconv_w, dkey_w, dkey_b, deps, dv, dg, dw, dmu)."""
+    _require_cuda(dy, z, g, w, mu, den, h)
+    B, T, M = z.shape
+    D = dy.shape[-1]
+    K = conv_w.shape[-1]
+    o = _block_bwd_buffers(dy, z, h, conv_w, v_dtype, precision, combine=True)
+    p = L.ptr
+    with torch.cuda.device(z.device):
+        L.check(L.lib().ulm_mixer_bwd(
+            p(dy), L.dtype_code(dy.dtype), p(z), p(den), p(g), p(w), p(mu), p(q) if q.numel() else None,
+            p(c) if c.numel() else None, p(qop), p(kop), p(vop), p(P), p(o["doop"]), p(o["dS"]), p(o["mw"]),
+            p(o["dqf"]), p(o["dk"]), p(o["partial"]), p(o["gpart"]), p(o["dr"]), p(o["dv"]), L.dtype_code(v_dtype),
+            p(o["dg"]), p(o["dw"]), p(o["dmu"]), p(u_op), u_op.shape[1], p(h), L.dtype_code(h.dtype), p(o["cw"]), K,
+            p(kw), kw.shape[1], p(o["dh"]), p(o["dconv"]), p(o["dkw"]), p(o["dkb"]), p(o["deps"]), p(o["work"]), B, T,
+            M, D, precision, L.stream_of(z)))
+    return (o["dh"], o["dconv"].reshape(D, 1, K), o["dkw"], o["dkb"], o["deps"], o["dv"], o["dg"], o["dw"],
+            o["dmu"])
+
+
 @torch.library.custom_op("ulm::addressed_memory_bwd", mutates_args=())
 def addressed_memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, h: torch.Tensor, conv_w: torch.Tensor,
                          g: torch.Tensor, w: torch.Tensor, q: torch.Tensor, z: torch.Tensor, den: torch.Tensor,
@@ -50,9 +116,8 @@ def addressed_memory_bwd(dq_out: Optional[torch.Tensor], dfast: torch.Tensor, h:
                          ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                                     torch.Tensor, torch.Tensor, torch.Tensor]:
     """Returns (dh fp32, dconv_w, dkey_w, dkey_b, deps, dv, dg, dw)."""
-    dr, dv, dg, dw = memory_bwd_raw(dq_out, dfast, z, den, g, w, q, c, qop, kop, vop, P, precision)
-    dh, dconv, dkw, dkb, deps = address_bwd_raw(dr, z, den, u_op, kw, h, conv_w, precision, normalized=False)
-    return dh, dconv, dkw, dkb, deps, dv, dg, dw
+    return addressed_memory_bwd_raw(dq_out, dfast, h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, vop, P,
+                                    precision)
 
 
 @addressed_memory_bwd.register_fake
@@ -136,9 +201,7 @@ def mixer_bwd(dy: torch.Tensor, h: torch.Tensor, conv_w: torch.Tensor, g: torch.
               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
                          torch.Tensor, torch.Tensor, torch.Tensor]:
     """Returns (dh fp32, dconv_w, dkey_w, dkey_b, deps, dv, dg, dw, dmu)."""
-    dr, dv, dg, dw, dmu = combine_bwd_raw(dy, z, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, precision)
-    dh, dconv, dkw, dkb, deps = address_bwd_raw(dr, z, den, u_op, kw, h, conv_w, precision, normalized=False)
-    return dh, dconv, dkw, dkb, deps, dv, dg, dw, dmu
+    return mixer_bwd_raw(dy, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, v_dtype, precision)
 
 
 @mixer_bwd.register_fake

@@ -635,3 +635,48 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   if (int rc = sum_parts(wk.dconv_part, (int64_t)wk.chunks * B, D * conv_size, dconv_w, st)) return rc;
   return stream_after(st, side);  // join
 }
+
+// The path's whole backward for one block with unnormalised addresses (z, den): the operator backward
+// (ulm_memory_bwd, or its fused-combine form ulm_memory_combine_bwd) followed by the prologue
+// backward (ulm_address_bwd), as one call so that the statistics' dw / dg reductions run on the
+// library's side stream beside the address backward; everything is joined to `stream` on return.
+extern "C" int ulm_addressed_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* z,
+                                        const float* den, const float* g, const float* w, const float* q,
+                                        const float* c, const void* qop, const void* kop, const void* vop,
+                                        const void* P, void* doop, void* dS, float* dqf, float* dk, void* partial,
+                                        float* dr, void* dv, float* dg, float* dw, const void* u_op, int64_t ld_u,
+                                        const void* h, int h_dtype, const float* conv_w, int64_t conv_size,
+                                        const void* key_w, int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w,
+                                        float* dkey_b, float* deps, void* work, int64_t B, int64_t T, int64_t M,
+                                        int64_t D, int prec, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStream_t side = nullptr;
+  if (int rc = side_stream(&side)) return rc;
+  int rc = memory_bwd_impl(dq_out, dfast, do_dtype, z, den, g, w, q, c, qop, kop, vop, P, doop, dS, dqf, dk, partial,
+                           dr, dv, dg, dw, B, T, M, D, prec, stream, side);
+  if (!rc)
+    rc = ulm_address_bwd(dr, z, den, 0, u_op, ld_u, h, h_dtype, conv_w, conv_size, key_w, ld_kw, dh, dconv_w, dkey_w,
+                         dkey_b, deps, work, B, T, D, M, prec, stream);
+  const int jrc = stream_after(st, side);  // also on failure: nothing of the call is left unjoined
+  return rc ? rc : jrc;
+}
+
+extern "C" int ulm_mixer_bwd(const void* dy, int dy_dtype, const float* z, const float* den, const float* g,
+                             const float* w, const float* mu, const float* q, const float* c, const void* qop,
+                             const void* kop, const void* vop, const void* P, void* doop, void* dS, void* mw,
+                             float* dqf, float* dk, void* partial, float* gpart, float* dr, void* dv, int dv_dtype,
+                             float* dg, float* dw, float* dmu, const void* u_op, int64_t ld_u, const void* h,
+                             int h_dtype, const float* conv_w, int64_t conv_size, const void* key_w, int64_t ld_kw,
+                             float* dh, float* dconv_w, float* dkey_w, float* dkey_b, float* deps, void* work,
+                             int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStream_t side = nullptr;
+  if (int rc = side_stream(&side)) return rc;
+  int rc = combine_bwd_impl(dy, dy_dtype, z, den, g, w, mu, q, c, qop, kop, vop, P, doop, dS, mw, dqf, dk, partial,
+                            gpart, dr, dv, dv_dtype, dg, dw, dmu, B, T, M, D, prec, stream, side);
+  if (!rc)
+    rc = ulm_address_bwd(dr, z, den, 0, u_op, ld_u, h, h_dtype, conv_w, conv_size, key_w, ld_kw, dh, dconv_w, dkey_w,
+                         dkey_b, deps, work, B, T, D, M, prec, stream);
+  const int jrc = stream_after(st, side);
+  return rc ? rc : jrc;
+}

@@ -376,11 +376,13 @@ extern "C" int ulm_memory_fwd(const float* r, const float* den, const void* v, i
   return ulm_causal_apply(P, ldt, vop, ldd, fast, D, v_dtype, 0, B, T, D, prec, stream);
 }
 
-extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
-                              const float* g, const float* w, const float* q, const float* c, const void* qop, const void* kop,
-                              const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk,
-                              void* partial, float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T,
-                              int64_t M, int64_t D, int prec, void* stream) {
+// red_st: stream for the statistics backward's dw / dg reductions (nullptr = the caller's stream);
+// a caller passing the side stream joins it later (ulm_addressed_memory_bwd)
+static int memory_bwd_impl(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
+                           const float* g, const float* w, const float* q, const float* c, const void* qop,
+                           const void* kop, const void* vop, const void* P, void* doop, void* dS, float* dqf,
+                           float* dk, void* partial, float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T,
+                           int64_t M, int64_t D, int prec, void* stream, cudaStream_t red_st) {
   if (int rc = check_prec(prec)) return rc;
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE(do_dtype == ULM_F32 || do_dtype == ULM_BF16, "do_dtype must be ULM_F32 or ULM_BF16");
@@ -443,10 +445,19 @@ extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dty
     ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
     // without a saved c the statistics backward rebuilds q and c from r (TMA scan path)
     return stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
-                         sc.tiles, n_tiles, st);
+                         sc.tiles, n_tiles, st, red_st);
   }
   return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0,
-                       st);
+                       st, red_st);
+}
+
+extern "C" int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
+                              const float* g, const float* w, const float* q, const float* c, const void* qop, const void* kop,
+                              const void* vop, const void* P, void* doop, void* dS, float* dqf, float* dk,
+                              void* partial, float* dr, void* dv, float* dg, float* dw, int64_t B, int64_t T,
+                              int64_t M, int64_t D, int prec, void* stream) {
+  return memory_bwd_impl(dq_out, dfast, do_dtype, r, den, g, w, q, c, qop, kop, vop, P, doop, dS, dqf, dk, partial, dr,
+                         dv, dg, dw, B, T, M, D, prec, stream, nullptr);
 }
 
 // ---- the block's combine fused into the fast memory (model.py:79-85) -------------------------------
@@ -510,12 +521,12 @@ extern "C" int ulm_memory_combine_fwd(const float* r, const float* den, const vo
   return run_gemm2(A, Bv, &A2, &B2, s, e, st);
 }
 
-extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float* r, const float* den, const float* g,
-                                      const float* w, const float* mu, const float* q, const float* c,
-                                      const void* qop, const void* kop, const void* vop, const void* P, void* doop,
-                                      void* dS, void* mw, float* dqf, float* dk, void* partial, float* gpart,
-                                      float* dr, void* dv, int dv_dtype, float* dg, float* dw, float* dmu,
-                                      int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream) {
+static int combine_bwd_impl(const void* dy, int dy_dtype, const float* r, const float* den, const float* g,
+                            const float* w, const float* mu, const float* q, const float* c, const void* qop,
+                            const void* kop, const void* vop, const void* P, void* doop, void* dS, void* mw, float* dqf,
+                            float* dk, void* partial, float* gpart, float* dr, void* dv, int dv_dtype, float* dg,
+                            float* dw, float* dmu, int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream,
+                            cudaStream_t red_st) {
   if (int rc = check_prec(prec)) return rc;
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE(dy_dtype == ULM_F32 || dy_dtype == ULM_BF16, "dy_dtype must be ULM_F32 or ULM_BF16");
@@ -589,11 +600,22 @@ extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float*
   if (int rc = ulm_causal_apply(dS, ldt, qop, ldm, dk, M, ULM_F32, 1, B, T, M, prec, side)) return rc;
   if (int rc = stream_after(st, side)) return rc;  // dk, dv and the combine's partials are done
   if (int rc = stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
-                             sc.tiles, n_tiles, st))
+                             sc.tiles, n_tiles, st, red_st))
     return rc;
   {
-    add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, st>>>(dw_part, (int)row_blocks, M, dw);
+    // on the stream of the dw reduction it adds to
+    add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, red_st ? red_st : st>>>(dw_part, (int)row_blocks, M, dw);
     ULM_LAUNCH_CHECK("add_parts_kernel");
   }
   return ULM_OK;
+}
+
+extern "C" int ulm_memory_combine_bwd(const void* dy, int dy_dtype, const float* r, const float* den, const float* g,
+                                      const float* w, const float* mu, const float* q, const float* c,
+                                      const void* qop, const void* kop, const void* vop, const void* P, void* doop,
+                                      void* dS, void* mw, float* dqf, float* dk, void* partial, float* gpart,
+                                      float* dr, void* dv, int dv_dtype, float* dg, float* dw, float* dmu,
+                                      int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream) {
+  return combine_bwd_impl(dy, dy_dtype, r, den, g, w, mu, q, c, qop, kop, vop, P, doop, dS, mw, dqf, dk, partial,
+                          gpart, dr, dv, dv_dtype, dg, dw, dmu, B, T, M, D, prec, stream, nullptr);
 }

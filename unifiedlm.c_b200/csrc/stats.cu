@@ -1101,7 +1101,7 @@ inline StatsScratch carve_stats_scratch(void* base, int64_t B, int64_t M) {
 int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const float* q, const float* c,
                   const float* r, const float* den, const float* w, const float* g, float* dr, float* dw, float* dg,
                   void* partial, int64_t B, int64_t T, int64_t M, int fast_identity, const float* tile_partials,
-                  int64_t n_tiles, cudaStream_t st) {
+                  int64_t n_tiles, cudaStream_t st, cudaStream_t red_st) {
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   int64_t n_dg, dw_rows;
   const bool recompute = q == nullptr && c == nullptr;
@@ -1161,10 +1161,16 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     n_dg = B * groups;
     dw_rows = B;
   }
-  if (int rc = launch_pdl(stats_bwd_dw_kernel, dim3((unsigned)cdiv(M, 256)), dim3(256), 0, st, (const float*)sc.part_dw,
+  // the dw / dg reductions on red_st when given (forked after the scan; the caller joins)
+  cudaStream_t rs = st;
+  if (red_st && red_st != st) {
+    if (int rc = stream_after(red_st, st)) return rc;
+    rs = red_st;
+  }
+  if (int rc = launch_pdl(stats_bwd_dw_kernel, dim3((unsigned)cdiv(M, 256)), dim3(256), 0, rs, (const float*)sc.part_dw,
                           dw, (int)dw_rows, (int)M))
     return rc;
-  if (int rc = launch_pdl(stats_bwd_dg_kernel, dim3(1), dim3(256), 0, st, (const double*)sc.part_dg, n_dg,
+  if (int rc = launch_pdl(stats_bwd_dg_kernel, dim3(1), dim3(256), 0, rs, (const double*)sc.part_dg, n_dg,
                           tile_partials, tile_partials ? n_tiles : (int64_t)0, dg))
     return rc;
   return ULM_OK;
@@ -1259,7 +1265,7 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
   }
   ULM_REQUIRE(dqf && dk && r && w && g && dr && partial, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
-  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st);
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, partial, B, T, M, 1, nullptr, 0, st, nullptr);
 }
 
 // ---- statistics backward without any allocation ------------------------------------------------
@@ -1321,7 +1327,7 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   // every scratch entry the kernels read is written earlier in the same call: nothing to clear
-  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st);
+  return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st, nullptr);
 }
 
 extern "C" int ulm_set_scan_mode(int mode) {
