@@ -993,7 +993,7 @@ int launch_cluster_smem(K kernel, dim3 grid, int threads, int cluster_x, size_t 
 // library-wide choice of scan kernels (ulm_set_scan_mode): 1 = persistent pipelined, 0 = per item
 static int g_scan_mode = 1;
 constexpr int SCAN_PIPE_STAGES = 2;  // backward: two stages of up to 66 KB
-constexpr int SCAN_FWD_STAGES = 3;   // forward: three stages of 16.5 KB
+constexpr int SCAN_FWD_STAGES = 2;   // forward: two stages of 16.5 KB (more CTAs per SM beat a deeper ring)
 
 // Clusters of a persistent scan that fit on the device at once (cached per device, kernel and
 // shared-memory size), at most n_items.
