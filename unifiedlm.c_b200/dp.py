@@ -23,7 +23,12 @@ class GradBucket:
         return [self.flat[a:b].view(s) for a, b, s in zip(self.offsets, self.offsets[1:], self.shapes)]
 
     def pack(self, grads):
-        torch.cat([g.reshape(-1).to(self.flat.dtype) for g in grads], out=self.flat)
+        """Copy the gradients into the bucket (one multi-tensor copy launch for same-dtype inputs)."""
+        views = self.views()
+        if all(g.dtype == self.flat.dtype and tuple(g.shape) == v.shape for g, v in zip(grads, views)):
+            torch._foreach_copy_(views, list(grads))
+        else:
+            torch.cat([g.reshape(-1).to(self.flat.dtype) for g in grads], out=self.flat)
         return self.flat
 
     def all_reduce(self, average=True, group=None):
