@@ -415,6 +415,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--grad-segments", type=int, default=1,
+                    help="with N>1 ranks: all-reduce the gradients in this many runs of blocks, each started "
+                         "as soon as its backward is issued (default 1: one all-reduce after the backward)")
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
     ap.add_argument("--no-mixer", action="store_true", help="skip the fused-combine measurement")
     ap.add_argument("--no-head", action="store_true", help="skip the fused LM-head measurement")
@@ -462,20 +465,39 @@ def main():
                                               seed=rank)
     from unifiedlm_c_b200.dp import GradBucket
     M_, D_ = W["M"], W["D"]
-    bucket = GradBucket([(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"], device=dev)
+    # the path's parameter gradients in one flat bucket, DP-averaged every step: by default one NCCL
+    # all-reduce after the last backward. With --grad-segments S the bucket is cut into S runs of
+    # blocks, each packed and its all-reduce started as soon as the backward reaches its first
+    # block, so the exchange overlaps the rest of the backward (DDP's gradient buckets)
+    segs = args.grad_segments if world > 1 else 1
+    if W["L"] % segs:
+        raise SystemExit(f"--grad-segments {segs} does not divide the {W['L']} blocks")
+    per_seg = W["L"] // segs
+    bucket = GradBucket([(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"], device=dev, segments=segs)
 
-    def step(h_, v_, dq_, df_):
-        grads = []
+    def step(h_, v_, dq_, df_, before_bwd=None):
+        """One training step of the path, in a model's order: every block's forward, then the
+        backward from the last block to the first. `before_bwd` runs between the two phases (the
+        e2e loop makes the stream wait there for the gradient inputs, which it copies last)."""
+        saved = []
         for blk in blocks:
-            q, fast, z, den, u_op, kw, c, qop, kop, vop, P = addressed_memory_fwd(
-                h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_, blk["g"], blk["w"], prec)
+            saved.append(addressed_memory_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_,
+                                              blk["g"], blk["w"], prec))
+        if before_bwd is not None:
+            before_bwd()
+        grads = [None] * len(blocks)
+        for i in reversed(range(len(blocks))):
+            blk = blocks[i]
+            q, fast, z, den, u_op, kw, c, qop, kop, vop, P = saved[i]
+            saved[i] = None
             dh, dconv, dkw, dkb, deps, dv, dg, dw = addressed_memory_bwd(
                 dq_, df_, h_, blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop,
                 operand_or_input(vop, v_), P, prec)
-            grads += [dkw, dkb, dconv, deps, dw, dg]
-        # the path's parameter gradients in one bucket: one NCCL all-reduce per step (DP average)
-        bucket.pack(grads)
-        bucket.all_reduce(average=True)
+            grads[i] = [dkw, dkb, dconv, deps, dw, dg]
+            if i % per_seg == 0:
+                bucket.pack_segment(i // per_seg, [t for g6 in grads[i:i + per_seg] for t in g6])
+                bucket.start_segment(i // per_seg)
+        bucket.finish(average=True)
         return bucket.flat
 
     if args.profile_step or args.profile_block:
@@ -525,7 +547,9 @@ def main():
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
     def e2e_run(n, start_ev=None):
+        # per slot: the forward inputs (h, v) and the gradient inputs (dq_out, dfast) have arrived
         in_ready = [torch.cuda.Event() for _ in range(2)]
+        grad_ready = [torch.cuda.Event() for _ in range(2)]
         in_free = [None, None]    # the step that last read the slot has finished
         out_ready = [torch.cuda.Event() for _ in range(2)]
         out_free = [None, None]   # the read of the slot's previous result has finished
@@ -537,9 +561,11 @@ def main():
                     h2d_s.wait_event(start_ev)
                 if in_free[k] is not None:
                     h2d_s.wait_event(in_free[k])
-                for d_, h_ in zip(slots_in[k], host):
+                for j, (d_, h_) in enumerate(zip(slots_in[k], host)):
                     d_.copy_(h_, non_blocking=True)
-                in_ready[k].record(h2d_s)
+                    if j == 1:
+                        in_ready[k].record(h2d_s)
+                grad_ready[k].record(h2d_s)
 
         copy_in(0)
         for i in range(n):
@@ -547,7 +573,7 @@ def main():
             main_s.wait_event(in_ready[k])
             if i + 1 < n:
                 copy_in(i + 1)
-            out = step(*slots_in[k])
+            out = step(*slots_in[k], before_bwd=lambda k=k: main_s.wait_event(grad_ready[k]))
             ev = torch.cuda.Event()
             ev.record(main_s)
             in_free[k] = ev
@@ -642,7 +668,7 @@ def main():
             "config": {"workload": "fast-memory path fwd+bwd (addressing prologue + unified_memory) x 12 blocks "
                                    "(110M shape), 16 seq x 1024 tok per GPU",
                        "B_per_gpu": W["B"], "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"],
-                       "lam": W["lam"], "parallelism": f"dp{world}",
+                       "lam": W["lam"], "parallelism": f"dp{world}", "grad_allreduce_segments": segs,
                        "l2": "inputs larger than L2 (r is 134 MB), no flush"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
