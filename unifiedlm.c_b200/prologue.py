@@ -20,8 +20,11 @@ def _op_dtype(precision):
 
 def _weight_op(key_w, precision):
     M, D = key_w.shape
-    kw = torch.zeros(M, operand_ld(D), device=key_w.device, dtype=_op_dtype(precision))
-    kw[:, :D] = key_w.detach()
+    ld = operand_ld(D)
+    kw = torch.empty(M, ld, device=key_w.device, dtype=_op_dtype(precision))
+    kw[:, :D].copy_(key_w.detach())
+    if ld > D:
+        kw[:, D:].zero_()
     return kw
 
 
