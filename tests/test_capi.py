@@ -37,6 +37,42 @@ def test_binding_covers_header():
     assert sorted(L.SIGNATURES) == declared_functions()
 
 
+def _ctype_of(decl):
+    """The ctypes type a C parameter or return declaration binds to."""
+    decl = re.sub(r"\b(const|restrict)\b", " ", decl).strip()
+    base = decl.replace("*", " ").split()[0]
+    if "*" in decl:
+        return ctypes.c_char_p if base == "char" else "ptr"
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float, "void": None}[base]
+
+
+def declared_prototypes():
+    """name -> (return type, [parameter types]) parsed from the header's prototypes."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"([A-Za-z_][A-Za-z0-9_ \*]*?)\b(ulm_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        ret, name, params = m.group(1), m.group(2), m.group(3).strip()
+        args = [] if params in ("", "void") else [_ctype_of(p_) for p_ in params.split(",")]
+        protos[name] = (_ctype_of(ret), args)
+    return protos
+
+
+def test_binding_argument_types_match_header():
+    """Every ctypes argtypes / restype in the binding agrees with the prototype in the header (count
+    and kind of each parameter), so no call passes a mistyped or shifted argument."""
+    protos = declared_prototypes()
+    assert sorted(protos) == declared_functions()
+    for name, (res, args) in L.SIGNATURES.items():
+        want_res, want_args = protos[name]
+        got_args = ["ptr" if a is ctypes.c_void_p or (isinstance(a, type) and issubclass(a, ctypes._Pointer))
+                    else a for a in args]
+        assert len(got_args) == len(want_args), (name, len(got_args), len(want_args))
+        for i, (g, w) in enumerate(zip(got_args, want_args)):
+            assert g == w, (name, i, g, w)
+        assert (res if res is not None else None) == want_res, (name, res, want_res)
+
+
 def test_version_and_helpers():
     lib = L.lib()
     assert lib.ulm_version() >= 1
