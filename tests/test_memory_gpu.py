@@ -107,6 +107,26 @@ def test_golden_fixture(golden_dir):
         check(errs, precision)
 
 
+@pytest.mark.parametrize("shape", [(0, 16, 32, 24), (2, 0, 32, 24), (2, 16, 0, 24), (2, 16, 8, 0)],
+                         ids=["no_rows", "no_positions", "no_slots", "no_channels"])
+def test_empty_extents(shape):
+    """Empty batches and sequences (and the degenerate no-slot / no-channel shapes) give outputs and
+    gradients of the right shapes: zero where the sums are empty, the oracle's values elsewhere."""
+    r, v, g, w, dq_out, dfast = make_inputs(*shape)
+    q, fast, grads = run_gpu(r, v, g, w, dq_out, dfast, "fp32")
+    q_ref, fast_ref = O.memory_dense(r, v, g, w)
+    refs = O.memory_grads(r, v, g, w, dq_out, dfast, form="dense")
+    assert q.shape == q_ref.shape and fast.shape == fast_ref.shape
+    for gr, rf in zip(grads, refs):
+        assert gr.shape == rf.shape
+    for x, ref in [(q, q_ref), (fast, fast_ref)] + list(zip(grads, refs)):
+        if ref.numel() and float(ref.abs().max()) == 0.0:
+            assert float(x.abs().max()) == 0.0
+        elif ref.numel():
+            assert rel(x, ref) < 1e-5
+    assert L.device_error() == 0
+
+
 def test_without_q_gradient_and_bf16_values():
     r, v, g, w, dq_out, dfast = make_inputs(2, 200, 140, 64, seed=3)
     q, fast, grads = run_gpu(r, v, g, w, dq_out, dfast, "bf16", v_dtype=torch.bfloat16, use_dq=False)

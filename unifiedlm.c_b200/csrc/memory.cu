@@ -360,17 +360,22 @@ extern "C" int ulm_memory_fwd(const float* r, const float* den, const void* v, i
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE(v_dtype == ULM_F32 || v_dtype == ULM_BF16, "v_dtype must be ULM_F32 or ULM_BF16");
   if (B == 0 || T == 0) return ULM_OK;
-  ULM_REQUIRE(r && v && g && w && q && fast && qop && kop && vop && P, "null pointer argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M == 0) {
+    // no slots: q is empty and the fast read is zero
+    if (D > 0) {
+      ULM_REQUIRE(fast, "null pointer argument");
+      ULM_CUDA_TRY(cudaMemsetAsync(fast, 0, B * T * D * elem_size(v_dtype), st));
+    }
+    return ULM_OK;
+  }
+  // pointers are checked only where the extents give them elements (an empty tensor's may be null)
+  ULM_REQUIRE(r && g && w && q && qop && kop, "null pointer argument");
   const int dt = op_dtype_of(prec);
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
   if (int rc = stats_fwd_run(r, den, w, g, q, c, qop, kop, dt, ldm, B, T, M, stream)) return rc;
-  if (M == 0) {
-    // no slots: the fast read is empty
-    ULM_CUDA_TRY(cudaMemsetAsync(fast, 0, B * T * D * elem_size(v_dtype), st));
-    return ULM_OK;
-  }
   if (D == 0) return ULM_OK;
+  ULM_REQUIRE(v && fast && vop && P, "null pointer argument");
   if (int rc = convert_rows(v, v_dtype, D, vop, dt, ldd, B * T, D, st)) return rc;
   if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, P, ldt, g, B, T, M, prec, stream)) return rc;
   return ulm_causal_apply(P, ldt, vop, ldd, fast, D, v_dtype, 0, B, T, D, prec, stream);
@@ -386,16 +391,21 @@ static int memory_bwd_impl(const float* dq_out, const void* dfast, int do_dtype,
   if (int rc = check_prec(prec)) return rc;
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE(do_dtype == ULM_F32 || do_dtype == ULM_BF16, "do_dtype must be ULM_F32 or ULM_BF16");
-  ULM_REQUIRE(dfast && dr && dv && dg && dw, "null pointer argument");
+  // pointers are checked only where the extents give them elements (an empty tensor's may be null)
+  ULM_REQUIRE(dg && (dw || M == 0), "null pointer argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = op_dtype_of(prec);
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
   if (B == 0 || T == 0 || M == 0) {
-    if (B * T * D > 0) ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(do_dtype), st));
+    if (B * T * D > 0) {
+      ULM_REQUIRE(dv, "null pointer argument");
+      ULM_CUDA_TRY(cudaMemsetAsync(dv, 0, B * T * D * elem_size(do_dtype), st));
+    }
     // nothing reads r or den here
     return ulm_memory_stats_bwd(dqf, dq_out, dk, c ? q : nullptr, c, r, w, g, dr, dw, dg, partial, B, T, M, stream);
   }
-  ULM_REQUIRE(r && g && w && qop && kop && vop && P && doop && dS && dqf && dk && partial, "null pointer argument");
+  ULM_REQUIRE(dr && r && g && w && qop && kop && dqf && dk && partial, "null pointer argument");
+  ULM_REQUIRE(D == 0 || (dfast && dv && vop && P && doop && dS), "null pointer argument");
   if (D == 0) {
     ULM_CUDA_TRY(cudaMemsetAsync(dqf, 0, B * T * M * sizeof(float), st));
     ULM_CUDA_TRY(cudaMemsetAsync(dk, 0, B * T * M * sizeof(float), st));

@@ -1256,7 +1256,7 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
                                     float* dw, float* dg, void* partial, int64_t B, int64_t T, int64_t M,
                                     void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
-  ULM_REQUIRE(dw && dg, "null dw/dg");
+  ULM_REQUIRE(dg && (dw || M == 0), "null dw/dg");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0 || T == 0 || M == 0) {
     if (M > 0) ULM_CUDA_TRY(cudaMemsetAsync(dw, 0, M * sizeof(float), st));
@@ -1310,7 +1310,7 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
                                             float* dr, float* dw, float* dg, int64_t B, int64_t T, int64_t M,
                                             void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
-  ULM_REQUIRE(dw && dg, "null dw/dg");
+  ULM_REQUIRE(dg && (dw || M == 0), "null dw/dg");
   const int64_t need = stats_bwd_core_scratch(B, M);
   ULM_REQUIRE(need <= (int64_t)ULM_NOALLOC_SCRATCH_BYTES,
               "ulm_memory_stats_bwd_noalloc: B=%lld x M=%lld needs %lld bytes of scratch, the built-in block holds "
