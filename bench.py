@@ -472,13 +472,17 @@ def main():
     segs = args.grad_segments if world > 1 else 1
     if W["L"] % segs:
         raise SystemExit(f"--grad-segments {segs} does not divide the {W['L']} blocks")
-    per_seg = W["L"] // segs
-    bucket = GradBucket([(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"], device=dev, segments=segs)
+    grad_shapes = [(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"]
+    bucket = GradBucket(grad_shapes, device=dev, segments=segs)
 
-    def step(h_, v_, dq_, df_, before_bwd=None):
+    def step(h_, v_, dq_, df_, before_bwd=None, bk=None, after_segment=None):
         """One training step of the path, in a model's order: every block's forward, then the
-        backward from the last block to the first. `before_bwd` runs between the two phases (the
-        e2e loop makes the stream wait there for the gradient inputs, which it copies last)."""
+        backward from the last block to the first, the gradients packed into bucket `bk` (default
+        `bucket`) segment by segment. `before_bwd` runs between the two phases (the e2e loop makes
+        the stream wait there for the gradient inputs, which it copies last); `after_segment(s)`
+        runs once segment s is packed (and, with N ranks, its all-reduce started)."""
+        bk = bucket if bk is None else bk
+        per_seg = len(blocks) // bk.segments
         saved = []
         for blk in blocks:
             saved.append(addressed_memory_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_,
@@ -495,10 +499,12 @@ def main():
                 operand_or_input(vop, v_), P, prec)
             grads[i] = [dkw, dkb, dconv, deps, dw, dg]
             if i % per_seg == 0:
-                bucket.pack_segment(i // per_seg, [t for g6 in grads[i:i + per_seg] for t in g6])
-                bucket.start_segment(i // per_seg)
-        bucket.finish(average=True)
-        return bucket.flat
+                bk.pack_segment(i // per_seg, [t for g6 in grads[i:i + per_seg] for t in g6])
+                bk.start_segment(i // per_seg)
+                if after_segment is not None:
+                    after_segment(i // per_seg)
+        bk.finish(average=True)
+        return bk.flat
 
     if args.profile_step or args.profile_block:
         step(h, v, dq_out, dfast)
@@ -534,12 +540,14 @@ def main():
 
     # e2e: every step's inputs copied from pinned host memory and its parameter gradients read back,
     # pipelined as a training loop with a prefetching loader does it: the host-to-device copy of
-    # step i+1 and the device-to-host read of step i-1 run on their own streams during step i
-    # (two device input slots, two output slots); the timed region spans the first copy to the
-    # last read
+    # step i+1 runs on its own stream during step i (two device input slots), and the gradients are
+    # read back on another stream into one of two pinned host buffers (two device buckets). On one
+    # GPU each block's gradients are read back as soon as its backward has packed them, so only the
+    # first block's 6 MB remain after the last step; with N ranks the read follows the all-reduce.
+    # The timed region spans the first copy to the last read.
     host = [t.cpu().pin_memory() for t in (h, v, dq_out, dfast)]
     slots_in = [[torch.empty_like(t) for t in (h, v, dq_out, dfast)] for _ in range(2)]
-    slots_out = [torch.empty_like(bucket.flat) for _ in range(2)]
+    out_buckets = [GradBucket(grad_shapes, device=dev, segments=W["L"] if world == 1 else segs) for _ in range(2)]
     host_out = [torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = host_out[0].numel() * host_out[0].element_size()
@@ -551,8 +559,7 @@ def main():
         in_ready = [torch.cuda.Event() for _ in range(2)]
         grad_ready = [torch.cuda.Event() for _ in range(2)]
         in_free = [None, None]    # the step that last read the slot has finished
-        out_ready = [torch.cuda.Event() for _ in range(2)]
-        out_free = [None, None]   # the read of the slot's previous result has finished
+        out_free = [None, None]   # the read of the bucket's previous result has finished
 
         def copy_in(i):
             k = i % 2
@@ -567,26 +574,37 @@ def main():
                         in_ready[k].record(h2d_s)
                 grad_ready[k].record(h2d_s)
 
+        def read_back(src, dst):
+            ready = torch.cuda.Event()
+            ready.record(main_s)
+            with torch.cuda.stream(d2h_s):
+                d2h_s.wait_event(ready)
+                dst.copy_(src, non_blocking=True)
+
         copy_in(0)
         for i in range(n):
             k = i % 2
+            bk = out_buckets[k]
             main_s.wait_event(in_ready[k])
+            if out_free[k] is not None:  # the read of step i-2's gradients (done during step i-1)
+                main_s.wait_event(out_free[k])
             if i + 1 < n:
                 copy_in(i + 1)
-            out = step(*slots_in[k], before_bwd=lambda k=k: main_s.wait_event(grad_ready[k]))
+            per_segment = None
+            if world == 1:
+                def per_segment(s_, bk=bk, dst=host_out[k]):
+                    a, b = bk.offsets[s_ * bk.per_segment], bk.offsets[(s_ + 1) * bk.per_segment]
+                    read_back(bk.segment(s_), dst[a:b])
+            out = step(*slots_in[k], before_bwd=lambda k=k: main_s.wait_event(grad_ready[k]), bk=bk,
+                       after_segment=per_segment)
             ev = torch.cuda.Event()
             ev.record(main_s)
             in_free[k] = ev
-            if out_free[k] is not None:
-                main_s.wait_event(out_free[k])
-            slots_out[k].copy_(out)
-            out_ready[k].record(main_s)
-            with torch.cuda.stream(d2h_s):
-                d2h_s.wait_event(out_ready[k])
-                host_out[k].copy_(slots_out[k], non_blocking=True)
-                ev2 = torch.cuda.Event()
-                ev2.record(d2h_s)
-                out_free[k] = ev2
+            if world > 1:
+                read_back(out, host_out[k])
+            done = torch.cuda.Event()
+            done.record(d2h_s)
+            out_free[k] = done
         main_s.wait_stream(d2h_s)
         main_s.wait_stream(h2d_s)
 
@@ -604,7 +622,7 @@ def main():
     if world > 1:
         dist.all_reduce(e2e_secs, op=dist.ReduceOp.MAX)
     e2e_value = world * W["B"] * W["T"] * e2e_steps / float(e2e_secs)
-    del slots_in, slots_out, host_out, host
+    del slots_in, out_buckets, host_out, host
 
     # roofline of the dominant kernel family (tensor-core products), CUDA events per launch
     blk0 = blocks[0]
@@ -672,8 +690,11 @@ def main():
                        "l2": "inputs larger than L2 (r is 134 MB), no flush"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "copies": "pinned host buffers; H2D of step i+1 and D2H of step i-1 on their own streams "
-                              "during step i (double-buffered), timed from the first copy to the last read"},
+                    "copies": "pinned host buffers; H2D of step i+1 during step i on its own stream "
+                              "(double-buffered; forward inputs first, the step waits for the gradient inputs "
+                              "before its backward); the gradients read back on another stream, per block as "
+                              "the backward packs them on one GPU, after the all-reduce with N ranks; timed "
+                              "from the first copy to the last read"},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
             "mixer": mixer, "head": head, "decode": decode}
     if rank == 0:

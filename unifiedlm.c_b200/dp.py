@@ -47,6 +47,11 @@ class GradBucket:
             raise IndexError(f"segment {i} of {self.segments}")
         return i * self.per_segment, (i + 1) * self.per_segment
 
+    def segment(self, i):
+        """The slice of the flat buffer that holds segment `i`."""
+        a, b = self._segment_range(i)
+        return self.flat[self.offsets[a]:self.offsets[b]]
+
     def pack_segment(self, i, grads):
         """Copy the gradients of segment `i` (its tensors, in order) into the bucket."""
         a, b = self._segment_range(i)
@@ -59,16 +64,14 @@ class GradBucket:
         else:
             for v, g in zip(views, grads):
                 v.copy_(g.reshape(v.shape))
-        return self.flat[self.offsets[a]:self.offsets[b]]
+        return self.segment(i)
 
     def start_segment(self, i, group=None):
         """Start the sum over ranks of segment `i` without waiting for it. With NCCL the collective
         is queued behind the work already issued on the current stream and runs on NCCL's own
         stream; `finish` makes the current stream wait for it. No-op without a process group."""
         if _world(group) > 1:
-            a, b = self._segment_range(i)
-            seg = self.flat[self.offsets[a]:self.offsets[b]]
-            self._pending.append((i, dist.all_reduce(seg, group=group, async_op=True)))
+            self._pending.append((i, dist.all_reduce(self.segment(i), group=group, async_op=True)))
 
     def finish(self, average=True, group=None):
         """Wait for every started segment (then divide those by the world size if `average`)."""
@@ -82,8 +85,7 @@ class GradBucket:
                 self.flat.div_(world)
             else:
                 for i in started:
-                    a, b = self._segment_range(i)
-                    self.flat[self.offsets[a]:self.offsets[b]].div_(world)
+                    self.segment(i).div_(world)
         return self.views()
 
     def all_reduce(self, average=True, group=None):
