@@ -281,8 +281,21 @@ __global__ void __launch_bounds__(256)
   const int64_t i = ((int64_t)blockIdx.x * 8 + c) * 4;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (i < n) {
-#pragma unroll 4
-    for (int64_t p = pl; p < nparts; p += 32) {
+    // parts pl, pl + 32, ... added in that order; eight loads in flight per step
+    int64_t p = pl;
+    for (; p + 32 * 7 < nparts; p += 32 * 8) {
+      float4 a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = *reinterpret_cast<const float4*>(part + (p + 32 * u) * n + i);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc.x += a[u].x;
+        acc.y += a[u].y;
+        acc.z += a[u].z;
+        acc.w += a[u].w;
+      }
+    }
+    for (; p < nparts; p += 32) {
       const float4 a = *reinterpret_cast<const float4*>(part + p * n + i);
       acc.x += a.x;
       acc.y += a.y;
