@@ -164,20 +164,53 @@ __global__ void __launch_bounds__(256)
     if (row >= rows) break;
     const float* drr = dr + row * M;
     const float* rrow = r + row * M;
+    const float dn = den[row];  // issued first: its latency hides behind the row's loads
     float s = 0.f;
-    for (int m = lane * 4; m < M; m += 128) {
+    int m = lane * 4;
+    // four 16-byte loads of each array in flight, then the products in the same order as one by one
+    for (; m + 384 < M; m += 512) {
+      float4 a[4], c[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a[u] = *reinterpret_cast<const float4*>(drr + m + 128 * u);
+        c[u] = *reinterpret_cast<const float4*>(rrow + m + 128 * u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        s = fmaf(a[u].x, c[u].x, fmaf(a[u].y, c[u].y, fmaf(a[u].z, c[u].z, fmaf(a[u].w, c[u].w, s))));
+    }
+    for (; m < M; m += 128) {
       const float4 a = *reinterpret_cast<const float4*>(drr + m);
       const float4 c = *reinterpret_cast<const float4*>(rrow + m);
       s = fmaf(a.x, c.x, fmaf(a.y, c.y, fmaf(a.z, c.z, fmaf(a.w, c.w, s))));
     }
     s = warp_sum(s);
-    const float dn = den[row];
     const float inv = 1.0f / dn;
     // z scale: sqrt(z) = sqrt(x * zs) with zs = den for normalised rows, 1 for z rows
     const float zs = unnormalised ? 1.f : dn;
     if (unnormalised) s *= inv;
     deps_acc -= s * inv;
-    for (int m = lane * 4; m < M; m += 128) {
+    // second pass over the row (mostly cache hits), four loads of each array in flight as well
+    m = lane * 4;
+    for (; m + 384 < M; m += 512) {
+      float4 a4[4], c4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        a4[u] = *reinterpret_cast<const float4*>(drr + m + 128 * u);
+        c4[u] = *reinterpret_cast<const float4*>(rrow + m + 128 * u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4 a = a4[u], c = c4[u];
+        float4 o;
+        o.x = 2.f * sqrtf(c.x * zs) * ((a.x - s) * inv);
+        o.y = 2.f * sqrtf(c.y * zs) * ((a.y - s) * inv);
+        o.z = 2.f * sqrtf(c.z * zs) * ((a.z - s) * inv);
+        o.w = 2.f * sqrtf(c.w * zs) * ((a.w - s) * inv);
+        st4(da, row * ld_da + m + 128 * u, o, da_dtype);
+      }
+    }
+    for (; m < M; m += 128) {
       const float4 a = *reinterpret_cast<const float4*>(drr + m);
       const float4 c = *reinterpret_cast<const float4*>(rrow + m);
       float4 o;
