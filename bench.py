@@ -439,7 +439,7 @@ def main():
 
     load_package()
     import unifiedlm_c_b200._lib as L_
-    from unifiedlm_c_b200.kernel import memory_fwd, operand_or_input, PRECISION
+    from unifiedlm_c_b200.kernel import memory_fwd, operand_copy, operand_or_input, PRECISION
     from unifiedlm_c_b200.prologue import address_fwd
     from unifiedlm_c_b200.block import addressed_memory_fwd, addressed_memory_bwd
 
@@ -675,11 +675,14 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             decode["cpu_baseline"] = runc_decode_baseline()
 
-    # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, den); operator fwd 4
-    # (stats scan, convert v, scores, read); operator bwd 8 (convert dfast, scores grad, dq, dk, dv,
-    # stats scan, dw, dg); prologue bwd 9 (address backward, db column sums + their sum, deps,
-    # dK GEMM, dK sum, du GEMM, conv bwd, dconv sum)
-    launches = args.steps * W["L"] * (3 + 4 + 8 + 9)
+    # kernels of ours per step, per block: prologue fwd 3 (conv, key GEMM, den); operator fwd 3
+    # (stats scan, scores, read) + the conversion of v to the operand type when v is not already
+    # one; operator bwd 7 (scores grad, dq, dk, dv, stats scan, dw, dg) + the conversion of dfast
+    # likewise; prologue bwd 9 (address backward, db column sums + their sum, deps, dK GEMM, dK sum,
+    # du GEMM, conv bwd, dconv sum)
+    opt_dtype = torch.float32 if args.precision == "fp32" else torch.bfloat16
+    converts = sum(int(operand_copy(x, opt_dtype) is not x) for x in (v, dfast))
+    launches = args.steps * W["L"] * (3 + 3 + 7 + 9 + converts)
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
