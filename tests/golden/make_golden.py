@@ -1,6 +1,6 @@
 """Generate the golden fixtures in this folder from the reference implementation itself.
 
-Run where the reference checkout is present (default /root/reference, or REF_DIR=...):
+Run where the reference checkout is present (its directory in REF_DIR, else the default in REF below):
 
     python tests/golden/make_golden.py
 
