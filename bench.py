@@ -152,6 +152,13 @@ def cpu_reference_seconds(T, M, D, lam, prior, reps, threads):
     return (time.perf_counter() - t0) / reps
 
 
+def workload_config(W):
+    """The workload both arms name in their JSON line."""
+    return {"workload": f"fast-memory path fwd+bwd (addressing prologue + unified_memory) x {W['L']} blocks "
+                        f"(110M shape), {W['B']} seq x {W['T']} tok per GPU",
+            "B_per_gpu": W["B"], "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"], "lam": W["lam"]}
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -168,9 +175,9 @@ def run_reference(args, rank):
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": per_sample * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "fast-memory path fwd+bwd (prologue + unified_memory), 1 sequence x 1 block "
-                                   "per sample, scaled to 12 blocks",
-                       "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"]},
+            "config": dict(workload_config(W), parallelism=f"dp{args.gpus}",
+                           sample="1 sequence x 1 block per timed sample on the host cores, scaled to the "
+                                  "workload's tokens"),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, "
                                        "prologue + chunked pure-PyTorch form (model.py:70-79, test_all.py:28-51 "
@@ -686,11 +693,8 @@ def main():
     line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-            "config": {"workload": "fast-memory path fwd+bwd (addressing prologue + unified_memory) x 12 blocks "
-                                   "(110M shape), 16 seq x 1024 tok per GPU",
-                       "B_per_gpu": W["B"], "T": W["T"], "M": W["M"], "D": W["D"], "layers": W["L"],
-                       "lam": W["lam"], "parallelism": f"dp{world}", "grad_allreduce_segments": segs,
-                       "l2": "inputs larger than L2 (r is 134 MB), no flush"},
+            "config": dict(workload_config(W), parallelism=f"dp{world}", grad_allreduce_segments=segs,
+                           l2="inputs larger than L2 (r is 134 MB), no flush"),
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "copies": "pinned host buffers; H2D of step i+1 during step i on its own stream "
