@@ -188,7 +188,8 @@ def run_reference(args, rank):
 
 
 # DRAM bytes (read + write) of the six fast-memory products of one block at the 110M shape, summed
-# over one ncu capture of `bench.py --profile-block` (profiles/tc_gemm_products_110M.md)
+# over one-kernel ncu captures of `bench.py --profile-block` (dram__bytes_read.sum +
+# dram__bytes_write.sum per launch)
 PRODUCTS_DRAM_BYTES = 783100000
 
 DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
@@ -653,7 +654,7 @@ def main():
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": PRODUCTS_DRAM_BYTES,
                 "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the six products of one block, "
-                                "one ncu capture (profiles/tc_gemm_products_110M.md)",
+                                "from one-kernel ncu captures of bench.py --profile-block",
                 "algorithmic_flops_per_block": flops,
                 "kernel": "tc2_gemm_kernel (6 causal products per block fwd+bwd)",
                 "peak_source": pk["source"],

@@ -106,10 +106,14 @@ int ulm_memory_needs_c(int64_t T, int64_t M);
  * It allocates nothing: its scratch is an 8 MiB block compiled into the library, which every GPU
  * that loads the library holds until the process exits. Limit: the scratch it needs, about
  * 34 * B * M bytes, must fit that block, so B * M up to about 246,000 (B=16 with M=2048 uses 1.1 MiB;
- * B=64 with M=3840 is about the largest); larger calls fail with ULM_ERR_INVALID and a message. The first call on each device looks up the block's device address
- * (cudaGetSymbolAddress) with that device current; make that first call before any stream
- * capture. All calls share the one block, so calls that overlap on the GPU (different streams,
- * no ordering between them) race and must be avoided; calls on one stream are safe. */
+ * B=64 with M=3840 is about the largest); larger calls fail with ULM_ERR_INVALID and a message
+ * (calls with B, T or M zero only zero dw and dg, as ulm_memory_stats_bwd does). Each call outside
+ * stream capture looks up the block's device address (cudaGetSymbolAddress) in the calling
+ * thread's current context, so contexts a host creates itself and the primary context after a
+ * cudaDeviceReset each get their own address; a call during stream capture reuses the address an
+ * earlier call in the same context recorded, so make one call in each context before capturing.
+ * All calls share the one block, so calls that overlap on the GPU (different streams, no ordering
+ * between them) race and must be avoided; calls on one stream are safe. */
 int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_out, const float* dk, const float* q,
                                  const float* c, const float* r, const float* w, const float* g, float* dr,
                                  float* dw, float* dg, int64_t B, int64_t T, int64_t M, void* stream);

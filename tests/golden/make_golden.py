@@ -1,6 +1,7 @@
 """Generate the golden fixtures in this folder from the reference implementation itself.
 
-Run where the reference checkout is present (its directory in REF_DIR, else the default in REF below):
+Run where the reference checkout is present (its directory in ULM_REFERENCE_DIR, else a `reference`
+directory beside this repository):
 
     python tests/golden/make_golden.py
 
@@ -33,7 +34,7 @@ import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("REF_DIR", "/root/reference")
+REF = os.environ.get("ULM_REFERENCE_DIR") or os.path.normpath(os.path.join(REPO, os.pardir, "reference"))
 
 
 def load_reference():

@@ -1,12 +1,15 @@
 // The two back ends of the batched GEMM engine (see gemm.cuh).
 //
-// Tensor-core back end (bf16 operands): a persistent, warp-specialised sm_100a kernel.
-//   warp 0        : TMA producer - 128B-swizzled tiles of A (128 x 64) and B (BN x 64) per stage
-//   warp 1        : allocates TMEM, one elected lane issues tcgen05.mma (M=128, N=BN, K=16) into a
-//                   double-buffered fp32 accumulator (2 x BN TMEM columns)
-//   warps 2..17   : epilogue - four warps per TMEM lane quadrant, each with its share of the
-//                   columns: tcgen05.ld 32 columns at a time, the fused epilogue arithmetic, a
-//                   swizzled shared-memory staging tile and a TMA tensor store
+// Tensor-core back end (bf16 operands): persistent, warp-specialised sm_100a kernels, on single
+// CTAs (tc_gemm_kernel: 128 x BN tiles) or on CTA pairs (tc2_gemm_kernel: 256 x 256 tiles,
+// cta_group::2, each CTA holding 128 rows of A and 128 columns of B).
+//   warp 0        : TMA producer - 128B-swizzled tiles of A and B (64 k values) per stage
+//   warp 1        : allocates TMEM, one elected lane (of the pair's leader CTA) issues tcgen05.mma
+//                   (K=16 steps) into a double-buffered fp32 accumulator (2 x BN TMEM columns)
+//   warps 2..9    : epilogue - EPI_WARPS = 8 warps, two per TMEM lane quadrant, each with half of
+//                   the tile's columns: tcgen05.ld 16 columns at a time, the fused epilogue
+//                   arithmetic, two 4 KB swizzled shared-memory staging tiles per warp and TMA
+//                   tensor stores (tile aux operands arrive the same way, loaded ahead)
 // Stage hand-offs use mbarriers; the accumulator is double-buffered so the epilogue of tile i
 // overlaps the MMAs of tile i+1. Every wait is bounded: on timeout the kernel records a device
 // error, drains what it has in flight, frees its TMEM and returns.

@@ -1274,32 +1274,75 @@ extern "C" int ulm_memory_stats_bwd(const float* dqf, const float* dq_out, const
 // For them the statistics backward can use a fixed scratch block that lives in the library's own
 // device image (ULM_NOALLOC_SCRATCH_BYTES per device, held by every GPU that loads the library until
 // the process exits). Host code cannot pass the array's name to a kernel (on the host it is only
-// a stand-in symbol), so its device address is looked up with cudaGetSymbolAddress once per device,
-// on the first call made while that device is current.
+// a stand-in symbol), so its device address is looked up with cudaGetSymbolAddress in the calling
+// thread's current context. Outside stream capture every call looks it up again (so a context
+// created later, or the primary context after cudaDeviceReset, gets its own address); during a
+// capture the address recorded for the current context by an earlier call is used, and a capture
+// with no earlier call in that context is refused.
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[ULM_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+constexpr int NOALLOC_CONTEXTS = 64;
+CUcontext g_noalloc_ctx[NOALLOC_CONTEXTS] = {};
+void* g_noalloc_addr[NOALLOC_CONTEXTS] = {};
+int g_noalloc_next = 0;  // next table entry to (re)use once all are taken
 
 // Bytes the public statistics backward actually uses (no score-epilogue partials).
 int64_t stats_bwd_core_scratch(int64_t B, int64_t M) {
   return align256(B * 8 * M * 4) + align256(B * stats_dg_groups(M) * 8);
 }
 
-int noalloc_scratch(void** out) {
-  const int dev = current_device();
-  ULM_REQUIRE(dev >= 0 && dev < 64, "no current CUDA device (or ordinal >= 64)");
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    ULM_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    ULM_REQUIRE(p != nullptr, "cudaGetSymbolAddress returned a null scratch address");
-    g_noalloc_addr[dev] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+int noalloc_scratch(cudaStream_t st, void** out) {
+  const int dev = current_device();
+  ULM_REQUIRE(dev >= 0, "no current CUDA device");
+  // a runtime call on the stream first: it makes the device's primary context current if the
+  // thread has none yet
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  ULM_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+  CtxGetCurrentFn get = ctx_get_current();
+  ULM_REQUIRE(get, "cuCtxGetCurrent is not available from the driver");
+  CUcontext ctx = nullptr;
+  ULM_REQUIRE(get(&ctx) == CUDA_SUCCESS && ctx, "no current CUDA context");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  int slot = -1;
+  for (int i = 0; i < NOALLOC_CONTEXTS; ++i)
+    if (g_noalloc_ctx[i] == ctx) slot = i;
+  if (cs != cudaStreamCaptureStatusNone) {
+    ULM_REQUIRE(slot >= 0 && g_noalloc_addr[slot],
+                "ulm_memory_stats_bwd_noalloc: first call in this context during stream capture; make one call "
+                "outside capture first");
+    *out = g_noalloc_addr[slot];
+    return ULM_OK;
   }
-  *out = g_noalloc_addr[dev];
+  void* p = nullptr;
+  ULM_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  ULM_REQUIRE(p != nullptr, "cudaGetSymbolAddress returned a null scratch address");
+  if (slot < 0) {
+    for (int i = 0; i < NOALLOC_CONTEXTS && slot < 0; ++i)
+      if (!g_noalloc_ctx[i]) slot = i;
+    if (slot < 0) slot = g_noalloc_next++ % NOALLOC_CONTEXTS;
+    g_noalloc_ctx[slot] = ctx;
+  }
+  g_noalloc_addr[slot] = p;
+  *out = p;
   return ULM_OK;
 }
 
@@ -1311,21 +1354,22 @@ extern "C" int ulm_memory_stats_bwd_noalloc(const float* dqf, const float* dq_ou
                                             void* stream) {
   ULM_REQUIRE(B >= 0 && T >= 0 && M >= 0, "negative extent");
   ULM_REQUIRE(dg && (dw || M == 0), "null dw/dg");
-  const int64_t need = stats_bwd_core_scratch(B, M);
-  ULM_REQUIRE(need <= (int64_t)ULM_NOALLOC_SCRATCH_BYTES,
-              "ulm_memory_stats_bwd_noalloc: B=%lld x M=%lld needs %lld bytes of scratch, the built-in block holds "
-              "%lld; use ulm_memory_stats_bwd with caller-provided scratch",
-              (long long)B, (long long)M, (long long)need, (long long)ULM_NOALLOC_SCRATCH_BYTES);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0 || T == 0 || M == 0) {
+    // the same result as ulm_memory_stats_bwd for empty extents: dw and dg are zero
     if (M > 0) ULM_CUDA_TRY(cudaMemsetAsync(dw, 0, M * sizeof(float), st));
     ULM_CUDA_TRY(cudaMemsetAsync(dg, 0, sizeof(float), st));
     return ULM_OK;
   }
   ULM_REQUIRE(dqf && dk && r && w && g && dr, "null pointer argument");
   ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+  const int64_t need = stats_bwd_core_scratch(B, M);
+  ULM_REQUIRE(need <= (int64_t)ULM_NOALLOC_SCRATCH_BYTES,
+              "ulm_memory_stats_bwd_noalloc: B=%lld x M=%lld needs %lld bytes of scratch, the built-in block holds "
+              "%lld; use ulm_memory_stats_bwd with caller-provided scratch",
+              (long long)B, (long long)M, (long long)need, (long long)ULM_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
-  if (int rc = noalloc_scratch(&scratch)) return rc;
+  if (int rc = noalloc_scratch(st, &scratch)) return rc;
   // every scratch entry the kernels read is written earlier in the same call: nothing to clear
   return stats_bwd_run(dqf, dq_out, dk, q, c, r, nullptr, w, g, dr, dw, dg, scratch, B, T, M, 1, nullptr, 0, st, nullptr);
 }
