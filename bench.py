@@ -190,7 +190,7 @@ def run_reference(args, rank):
 # DRAM bytes (read + write) of the six fast-memory products of one block at the 110M shape, summed
 # over one-kernel ncu captures of `bench.py --profile-block` (dram__bytes_read.sum +
 # dram__bytes_write.sum per launch)
-PRODUCTS_DRAM_BYTES = 783100000
+PRODUCTS_DRAM_BYTES = 801400000
 
 DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
 
