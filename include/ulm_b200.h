@@ -166,6 +166,26 @@ int ulm_set_scan_mode(int mode);
  * completed. Results do not depend on it. Returns the previous setting. */
 int ulm_set_pdl(int enable);
 
+/* Form of the fast read's products (replaces the reference's fixed chunk length, kernel.py:20, 183-196).
+ * Whole-sequence form: the decayed T x T scores and causal reads. Chunk-carry form with chunk length
+ * C: a carry product walks the chunks with the (M x D) state in the tensor cores' accumulator and
+ * writes one state per chunk boundary (the reference writes them for 64-token chunks, kernel.py:23-48),
+ * an inter-chunk read against those states, and the whole-sequence products inside each chunk.
+ * ulm_memory_chunk_len returns the chunk length the operator entry points use for (T, M, D, prec),
+ * 0 for the whole-sequence form, -1 for bad arguments. Automatic choice (mode -1, default): C = 256
+ * (ULM_PREC_BF16) or 64 (ULM_PREC_FP32) where T is a multiple of C with at least two chunks and
+ * T (M + D) > 4 M D + 2 C (M + D) (fewer flops than the whole-sequence form).
+ * ulm_set_chunk_mode: -1 automatic, 0 always the whole-sequence form, C > 0 (a multiple of 64, at
+ * most 4096) that chunk length wherever T is a multiple of C with at least two chunks. Returns the
+ * previous mode, or -2 (no change) for a bad mode. Buffers sized with ulm_memory_saved_bytes /
+ * ulm_memory_bwd_work_bytes belong to the mode they were sized under. */
+int ulm_set_chunk_mode(int mode);
+int ulm_memory_chunk_len(int64_t T, int64_t M, int64_t D, int prec);
+/* Bytes of the fast read's saved buffer (the `P` argument of the operator forwards) and of the
+ * backward's work buffer (the `dS` argument of the operator backwards); -1 for bad arguments. */
+int64_t ulm_memory_saved_bytes(int64_t B, int64_t T, int64_t M, int64_t D, int prec);
+int64_t ulm_memory_bwd_work_bytes(int64_t B, int64_t T, int64_t M, int64_t D, int prec);
+
 /* Forward of unified_memory(r, v, g, w) -> (q, fast).
  * Inputs : r (B,T,M) fp32; v (B,T,D) of type v_dtype, row stride D; g device scalar; w (M,) fp32.
  * den: NULL when r holds the read addresses; otherwise r holds their unnormalised form z
@@ -174,15 +194,20 @@ int ulm_set_pdl(int enable);
  * Outputs: q (B,T,M) fp32; fast (B,T,D) of type v_dtype.
  * Saved for the backward (caller-owned, element type = ULM_BF16 for ULM_PREC_BF16, ULM_F32 for
  * ULM_PREC_FP32): c (B,T,M) fp32, or NULL when ulm_memory_needs_c(T, M) is 0; qop, kop
- * (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D)); P (B,T,ulm_operand_ld(T)). */
+ * (B,T,ulm_operand_ld(M)); vop (B,T,ulm_operand_ld(D)); P: the fast read's saved buffer,
+ * ulm_memory_saved_bytes(B,T,M,D,prec) bytes, 256-byte aligned. In the whole-sequence form
+ * (ulm_memory_chunk_len(T,M,D,prec) == 0) it holds the decayed scores (B,T,ulm_operand_ld(T));
+ * in the chunk-carry form the intra-chunk scores, the chunk-boundary states and the inter-chunk
+ * read. */
 int ulm_memory_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g, const float* w,
                    float* q, void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
                    int64_t M, int64_t D, int prec, void* stream);
 
 /* Backward of unified_memory. dq_out may be NULL; dfast (B,T,D) of type do_dtype; r and den as
- * given to ulm_memory_fwd. Workspace buffers (caller-owned): doop (B,T,ulm_operand_ld(D)) and dS
- * (B,T,ulm_operand_ld(T)) in the operand type, dqf and dk (B,T,M) fp32, `partial` of
- * ulm_memory_stats_bwd_scratch bytes.
+ * given to ulm_memory_fwd. Workspace buffers (caller-owned): doop (B,T,ulm_operand_ld(D)) in the
+ * operand type, dS of ulm_memory_bwd_work_bytes(B,T,M,D,prec) bytes (256-byte aligned; the score
+ * gradient (B,T,ulm_operand_ld(T)) in the whole-sequence form), dqf and dk (B,T,M) fp32, `partial`
+ * of ulm_memory_stats_bwd_scratch bytes.
  * Outputs: dr (B,T,M) fp32 (the gradient of the normalised addresses in both forms), dv (B,T,D)
  * of type do_dtype, dg (1,) fp32, dw (M,) fp32. */
 int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const float* r, const float* den,
@@ -294,6 +319,35 @@ int ulm_mixer_bwd(const void* dy, int dy_dtype, const float* z, const float* den
                   const void* key_w, int64_t ld_kw, float* dh, float* dconv_w, float* dkey_w, float* dkey_b,
                   float* deps, void* work, int64_t B, int64_t T, int64_t M, int64_t D, int prec, void* stream);
 
+/* ---- RMSNorm and Linear of the block's input side (model.py:31-42, 65, 81) --------------------- */
+
+/* y = round_x(x * rstd) * weight, rstd = 1 / sqrt(mean(x^2) + eps) per row, in fp32 (the reference's
+ * RMSNorm.forward, model.py:31-42; round_x = rounding to x's type, the reference's type_as(x)).
+ * x (rows, D) of x_dtype, weight (D,) fp32, y (rows, D) of y_dtype, rstd (rows,) fp32 (may be NULL;
+ * the backward needs it). */
+int ulm_rms_norm_fwd(const void* x, int x_dtype, const float* weight, void* y, int y_dtype, float* rstd,
+                     int64_t rows, int64_t D, float eps, void* stream);
+/* Backward of ulm_rms_norm_fwd from dy (rows, D) of dy_dtype: dx (rows, D) fp32, dweight (D,) fp32
+ * (overwritten; summed over rows in a fixed order). work: ulm_rms_norm_bwd_work_bytes(rows, D)
+ * bytes. D * 32 bytes must fit the backward's shared memory (D <= 6400). */
+int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int x_dtype, const float* weight,
+                     const float* rstd, float* dx, float* dweight, void* work, int64_t rows, int64_t D,
+                     void* stream);
+int64_t ulm_rms_norm_bwd_work_bytes(int64_t rows, int64_t D);
+
+/* y = x W^T (nn.Linear without bias; UnifiedBlock.val, model.py:65, 81): x (N, K) of x_dtype, weight
+ * (Nout, K) fp32, y (N, Nout) of y_dtype. Writes the operand copies x_op (N, ulm_operand_ld(K)) and
+ * w_op (Nout, ulm_operand_ld(K)) (bf16 for ULM_PREC_BF16, fp32 for ULM_PREC_FP32), which the
+ * backward reads. */
+int ulm_linear_fwd(const void* x, int x_dtype, const float* weight, void* x_op, void* w_op, void* y, int y_dtype,
+                   int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
+/* Backward of ulm_linear_fwd from dy (N, Nout) of dy_dtype: dx (N, K) fp32 = dy W, dw (Nout, K)
+ * fp32 = dy^T x (split over the rows, partials summed in a fixed order). work:
+ * ulm_linear_bwd_work_bytes(N, K, Nout, prec) bytes. */
+int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx, float* dw,
+                   void* work, int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
+int64_t ulm_linear_bwd_work_bytes(int64_t N, int64_t K, int64_t Nout, int prec);
+
 /* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */
 
 /* Per block, once per weight set: prior[d][m] = ((1 - lam) * mu[d][m]) * w[m], the constant part of
@@ -334,6 +388,22 @@ int ulm_decode_head(float* x, const float* norm_w, const void* cls_w, const void
                     void* stream);
 
 int64_t ulm_decode_head_work_bytes(int64_t B, int64_t D);
+
+/* Parallel prefill of one block (replaces feeding a prompt through UnifiedBlock.step token by
+ * token, model.py:96-111 / run.c:193-265): after the training-form forward of the block over T
+ * prompt positions (z and den from ulm_address_fwd with normalize = 0; kop (B,T,ulm_operand_ld(M))
+ * and vop (B,T,ulm_operand_ld(D)) the operand copies of ulm_memory_fwd / ulm_memory_combine_fwd;
+ * h (B,T,D) of h_dtype the block's normalised input), writes the decode state that T steps would
+ * leave: U (B,D,M) = w mu + sum_s lam^(T-1-s) v_s k_s^T (k_s = r_{s-1}; one carry product over a
+ * single chunk of T positions, straight into the (D,M) layout), c (B,M) = the evidence mass after
+ * position T-1 (step's update order), r_prev (B,M) = r_{T-1}, buf (B,D,conv_size-1) = the last
+ * conv_size-1 rows of h, oldest first (zero before position 0). g = log(lam) and lam are device
+ * scalars; mu (D,M), w (M,) fp32; work: ulm_decode_prefill_work_bytes(B,T,D,prec) bytes. */
+int ulm_decode_prefill_block(const void* kop, const void* vop, const float* g, const float* lam, const float* z,
+                             const float* den, const void* h, int h_dtype, const float* mu, const float* w, void* work,
+                             float* U, float* c, float* r_prev, float* buf, int64_t B, int64_t T, int64_t D, int64_t M,
+                             int64_t conv_size, int prec, void* stream);
+int64_t ulm_decode_prefill_work_bytes(int64_t B, int64_t T, int64_t D, int prec);
 
 /* run.c's sample() with temperature > 0 (run.c:460-534) for B sequences on the device:
  * softmax(logits[b] / temperature), a coin from the sequence's xorshift64* state rng_state[b]

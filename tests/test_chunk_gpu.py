@@ -1,0 +1,143 @@
+"""The chunk-carry form of the fast read against the float64 oracle.
+
+Above the flop crossover (T (M + D) > 4 M D + 2 C (M + D)) the operator's products run in chunks
+of C positions: a carry product keeps the (M x D) state in tensor memory across the chunks and
+writes one state per chunk boundary, an inter-chunk read applies those states, and the intra-chunk
+products are the whole-sequence ones on C-long pieces (the reference's chunked form,
+kernel.py:23-101, 183-196, with its chunk length chosen for the 256-row tensor-core tiles). These
+tests force the form with ulm_set_chunk_mode on small shapes (every back end: CTA pairs, single
+CTAs, the fp32 FMA kernels, partial tiles), run BASELINE config 3's T = 2048 and a T = 8192 sequence
+in the automatic choice, and the fused combine in the chunked form. Bars as everywhere: 1e-2
+relative with bf16 products, 1e-5 in fp32 mode; the decay gradient at 3e-2 (bf16) or the
+summation bound 1e-4 x sum |terms| where the dense terms are affordable.
+"""
+import math
+
+import pytest
+import torch
+
+import unifiedlm_c_b200._lib as L
+from oracle import memory as O
+from unifiedlm_c_b200.kernel import PRECISION, unified_memory
+from test_configs_gpu import config3_inputs
+import test_mixer_gpu as MX
+
+pytestmark = pytest.mark.gpu
+TOL = {"bf16": 1e-2, "fp32": 1e-5}
+DG_TOL = {"bf16": 3e-2, "fp32": 1e-5}
+DEV = "cuda:0"
+
+
+@pytest.fixture
+def chunk_mode():
+    """Set the library's chunk mode for one test and restore the automatic choice after it."""
+    lib = L.lib()
+    yield lambda mode: lib.ulm_set_chunk_mode(mode)
+    lib.ulm_set_chunk_mode(-1)
+
+
+def rel(a, b):
+    b = b.double().cpu()
+    return float((a.detach().double().cpu() - b).norm() / b.norm().clamp(min=1e-30))
+
+
+def inputs(B, T, M, D, lam, seed):
+    g_ = torch.Generator().manual_seed(seed)
+    a = torch.randn(B, T, M, generator=g_, dtype=torch.float64) + 0.3
+    z = torch.relu(a).square()
+    r = z / (1.0 + z.sum(-1, keepdim=True))
+    v = torch.randn(B, T, D, generator=g_, dtype=torch.float64)
+    lg = torch.tensor(math.log(lam), dtype=torch.float64)
+    w = torch.exp(torch.randn(M, generator=g_, dtype=torch.float64))
+    dq = torch.randn(B, T, M, generator=g_, dtype=torch.float64)
+    df = torch.randn(B, T, D, generator=g_, dtype=torch.float64)
+    return r, v, lg, w, dq, df
+
+
+def run_and_compare(r, v, lg, w, dq, df, precision, form="dense", v_dtype=torch.float32, dg_terms=True,
+                    dg_tol=None):
+    B, T, M = r.shape
+    leaves = [t.clone().requires_grad_(True) for t in (r, v, lg, w)]
+    if form == "dense":
+        q_ref, f_ref = O.memory_dense(*leaves)
+    else:
+        q_ref, f_ref = O.memory_chunked(*leaves, 64)
+    ((q_ref * dq).sum() + (f_ref * df).sum()).backward()
+    refs = [t.grad for t in leaves]
+    dev = [t.float().to(DEV).requires_grad_(True) for t in (r, v, lg, w)]
+    q, fast = unified_memory(dev[0], dev[1].to(v_dtype), dev[2], dev[3], precision=precision)
+    ((q * dq.float().to(DEV)).sum() + (fast.float() * df.float().to(DEV)).sum()).backward()
+    torch.cuda.synchronize()
+    errs = {"q": rel(q, q_ref), "fast": rel(fast, f_ref)}
+    errs.update({n: rel(d.grad, rf) for n, d, rf in zip(("dr", "dv", "dg", "dw"), dev, refs)})
+    dg_rel = errs.pop("dg")
+    if dg_rel >= DG_TOL[precision] and dg_terms:
+        terms = float(O.decay_grad_terms(r, v, lg, w, dq, df).abs().sum())
+        dg_abs = abs(float(dev[2].grad) - float(refs[2]))
+        assert dg_abs < (1e-4 if precision == "bf16" else 5e-8) * terms, (dg_rel, dg_abs, terms)
+    else:
+        assert dg_rel < (dg_tol or DG_TOL[precision]), dg_rel
+    assert max(errs.values()) < TOL[precision], errs
+    assert L.device_error() == 0
+
+
+# (B, T, M, D, C): pair-kernel carries (M, D >= 256), single-CTA carries (D < 256), ragged M / D
+FORCED = [(2, 512, 256, 256, 256), (2, 768, 96, 40, 256), (2, 512, 140, 64, 128), (1, 1024, 512, 320, 256),
+          (2, 256, 48, 24, 64)]
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+@pytest.mark.parametrize("shape", FORCED, ids=lambda s: "x".join(map(str, s)))
+def test_forced_chunk_form_matches_oracle(chunk_mode, shape, precision):
+    B, T, M, D, C = shape
+    chunk_mode(C)
+    assert L.lib().ulm_memory_chunk_len(T, M, D, PRECISION[precision]) == C
+    run_and_compare(*inputs(B, T, M, D, 0.95, seed=T + M), precision)
+
+
+@pytest.mark.parametrize("lam", [0.9, 0.999])
+def test_forced_chunk_decay_sweep(chunk_mode, lam):
+    chunk_mode(256)
+    run_and_compare(*inputs(2, 1024, 256, 256, lam, seed=3), "bf16")
+
+
+def test_ragged_T_keeps_whole_sequence_form(chunk_mode):
+    # T not a multiple of the chunk: the whole-sequence form (same results)
+    chunk_mode(256)
+    assert L.lib().ulm_memory_chunk_len(600, 256, 256, PRECISION["bf16"]) == 0
+    run_and_compare(*inputs(1, 600, 256, 256, 0.95, seed=5), "bf16")
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+def test_config3_T2048_chunked(precision):
+    # BASELINE config 3's longest sequence: the automatic choice is the chunk-carry form
+    B, T, D, M = 1, 2048, 512, 1024
+    assert L.lib().ulm_memory_chunk_len(T, M, D, PRECISION[precision]) > 0
+    r, v, lg, w, dq, df = config3_inputs(B, T, D, M, 0.99, seed=21)
+    run_and_compare(r, v, lg, w, dq, df, precision, v_dtype=torch.bfloat16 if precision == "bf16" else torch.float32)
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+def test_long_sequence_T8192(precision):
+    # a sequence 4x past config 3: checked against the oracle's chunked float64 form
+    B, T, D, M = 1, 8192, 512, 1024
+    assert L.lib().ulm_memory_chunk_len(T, M, D, PRECISION[precision]) > 0
+    # lam 0.999 (a 1000-position memory) in bf16; in fp32 mode lam 0.99: with lam 0.999 over 8192
+    # positions the fp32 slot-statistics recurrence itself (c_t = w + lam n_{t-1} + k_t, the
+    # reference's scan in fp32) rounds q to 7e-6 and dw to 1.6e-5, past the 1e-5 bar whatever form
+    # the fast read takes; dg, a sum of B*T^2 cancelling terms whose dense list is too large to
+    # form here, is held to 3e-5 in fp32
+    lam = 0.999 if precision == "bf16" else 0.99
+    r, v, lg, w, dq, df = config3_inputs(B, T, D, M, lam, seed=22)
+    run_and_compare(r, v, lg, w, dq, df, precision, form="chunked", dg_terms=False,
+                    dg_tol=3e-5 if precision == "fp32" else None)
+
+
+@pytest.mark.parametrize("precision", ["bf16", "fp32"])
+def test_mixer_in_chunk_form(chunk_mode, precision):
+    # the fused combine y = x + mu(q w) + fast with the fast read in chunks: the mixer test's checks
+    # (every gradient, dw against its two parts, the cancelling scalars) at a chunked shape
+    chunk_mode(256 if precision == "bf16" else 64)
+    B, T, D, M = 2, 512, 256, 256
+    assert L.lib().ulm_memory_chunk_len(T, M, D, PRECISION[precision]) > 0
+    MX.test_mixer_matches_oracle(precision, (B, T, D, M))

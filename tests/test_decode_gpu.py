@@ -173,3 +173,59 @@ def test_live_runc_sampled_identity(tmp_path):
     dec = BatchedDecoder.from_model_bin(mpath, batch=1, precision="fp32", temperature=1.0, topp=0.9, seed=5)
     out = dec.generate(torch.ones(1, 1, dtype=torch.long), steps=steps)
     assert out[0, :len(ids)].tolist() == ids
+
+
+@pytest.mark.parametrize("precision,P", [("fp32", 37), ("fp32", 512), ("bf16", 300), ("bf16", 1024)])
+def test_prefill_matches_token_by_token(precision, P):
+    """BatchedDecoder.prefill (the prompt in one parallel pass, the state from one carry product per
+    block) against feeding the prompt token by token: the last position's logits within 1e-4 (fp32)
+    or 2e-2 (bf16 products against bf16-weight steps), and in fp32 mode the greedy continuation
+    identical. P = 512 (fp32) and 1024 (bf16) run the blocks' fast read in the chunk-carry form."""
+    p = rand_params(7, 64, 3, 128, 512)
+    B, steps = 3, 24
+    prompt = torch.randint(0, 512, (B, P), generator=torch.Generator().manual_seed(P))
+    a = BatchedDecoder(p, batch=B, precision=precision)
+    a.prepare_graph()
+    for t in range(P):
+        nt = a.feed(prompt[:, t])
+    ref_logits = a.logits.double().cpu()
+    ref = [nt.clone()] + [a.step_greedy().clone() for _ in range(steps)]
+    b = BatchedDecoder(p, batch=B, precision=precision)
+    b.prepare_graph()
+    nt = b.prefill(prompt)
+    err = float((b.logits.double().cpu() - ref_logits).norm() / ref_logits.norm())
+    assert err < (1e-4 if precision == "fp32" else 2e-2), err
+    got = [nt.clone()] + [b.step_greedy().clone() for _ in range(steps)]
+    if precision == "fp32":
+        assert torch.equal(torch.stack(got), torch.stack(ref))
+
+
+def test_model_step_and_forward_recurrent_use_the_decoder():
+    """UnifiedBlock.init_state / step and UnifiedLM.forward_recurrent (model.py:88-111, 164-175) on
+    the library's decode kernels, against the oracle's token-by-token form in float64."""
+    from unifiedlm_c_b200.model import ModelArgs, UnifiedLM
+    p = rand_params(3, 32, 2, 48, 97)
+    args = ModelArgs(dim=32, n_layers=2, hidden_dim=48, vocab_size=97, max_seq_len=64)
+    model = UnifiedLM(args)
+    model.load_state_dict(p, strict=False)
+    with torch.no_grad():
+        model.output.weight.copy_(p["output.weight"])  # tied: the embedding follows
+    tied = {k: v for k, v in p.items()}
+    tied["tok_embeddings.weight"] = p["output.weight"]
+    model = model.cuda()
+    tokens = torch.randint(0, 97, (2, 12), generator=torch.Generator().manual_seed(2))
+    ref = O.lm_forward_recurrent({k: v.double() for k, v in tied.items()}, tokens)
+    got = model.forward_recurrent(tokens.cuda()).double().cpu()
+    assert float((got - ref).norm() / ref.norm()) < 1e-4
+    # the block API: one block's steps against the oracle's step
+    blk = model.layers[0]
+    s = blk.init_state(2, "cuda")
+    so = O.block_init_state({k[len("layers.0."):]: v.double() for k, v in tied.items() if k.startswith("layers.0.")},
+                            2)
+    x = torch.randn(2, 32, generator=torch.Generator().manual_seed(4))
+    pb = {k[len("layers.0."):]: v.double() for k, v in tied.items() if k.startswith("layers.0.")}
+    for _ in range(5):
+        y = blk.step(x.cuda(), s)
+        yo = O.block_step(pb, x.double(), so)
+        assert float((y.double().cpu() - yo).norm() / yo.norm()) < 1e-5
+        x = yo.float()

@@ -35,6 +35,10 @@ SIGNATURES = {
     "ulm_set_epilogue_mode": (_I, [_I]),
     "ulm_set_scan_mode": (_I, [_I]),
     "ulm_set_pdl": (_I, [_I]),
+    "ulm_set_chunk_mode": (_I, [_I]),
+    "ulm_memory_chunk_len": (_I, [_I64, _I64, _I64, _I]),
+    "ulm_memory_saved_bytes": (_I64, [_I64, _I64, _I64, _I64, _I]),
+    "ulm_memory_bwd_work_bytes": (_I64, [_I64, _I64, _I64, _I64, _I]),
     "ulm_memory_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_bwd": (_I, [_P, _P, _I] + [_P] * 19 + [_I64, _I64, _I64, _I64, _I, _P]),
     "ulm_memory_combine_fwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P,
@@ -51,6 +55,12 @@ SIGNATURES = {
                                  [_I64] * 4 + [_I, _P]),
     "ulm_mixer_bwd": (_I, [_P, _I] + [_P] * 20 + [_I, _P, _P, _P] + [_P, _I64, _P, _I, _P, _I64, _P, _I64] +
                       [_P] * 6 + [_I64] * 4 + [_I, _P]),
+    "ulm_rms_norm_fwd": (_I, [_P, _I, _P, _P, _I, _P, _I64, _I64, ctypes.c_float, _P]),
+    "ulm_rms_norm_bwd": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _P]),
+    "ulm_rms_norm_bwd_work_bytes": (_I64, [_I64, _I64]),
+    "ulm_linear_fwd": (_I, [_P, _I, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
+    "ulm_linear_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "ulm_linear_bwd_work_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "ulm_lm_head_loss_fwd": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_lm_head_loss_bwd": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_lm_head_work_bytes": (_I64, [_I64, _I64, _I64, _I]),
@@ -62,6 +72,8 @@ SIGNATURES = {
     "ulm_decode_head": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P]),
     "ulm_decode_sample": (_I, [_P, _I64, _I64, ctypes.c_float, ctypes.c_float, _P, _P, _P, _I, _P, _I64, _P]),
     "ulm_decode_head_work_bytes": (_I64, [_I64, _I64]),
+    "ulm_decode_prefill_block": (_I, [_P] * 7 + [_I] + [_P] * 7 + [_I64] * 5 + [_I, _P]),
+    "ulm_decode_prefill_work_bytes": (_I64, [_I64, _I64, _I64, _I]),
 }
 
 _lib = None

@@ -19,8 +19,8 @@ from typing import Optional
 import torch
 
 from . import _lib as L
-from .kernel import (PRECISION, _op_dtype, _require_cuda, combine_fwd_fake, combine_fwd_raw, memory_fwd_fake,
-                     memory_fwd_raw, operand_copy, operand_ld, operand_or_input, unaliased)
+from .kernel import (PRECISION, _op_dtype, _require_cuda, bwd_work_buffer, combine_fwd_fake, combine_fwd_raw,
+                     memory_fwd_fake, memory_fwd_raw, operand_copy, operand_ld, operand_or_input, unaliased)
 from .prologue import address_bwd_fake, address_fwd_fake, address_fwd_raw
 
 _OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
@@ -56,7 +56,7 @@ def _block_bwd_buffers(dfast_like, z, h, conv_w, v_dtype, precision, combine):
     bufs = dict(
         dr=torch.empty(B, T, M, **f32), dv=torch.empty(B, T, D, device=dev, dtype=v_dtype),
         dg=torch.empty((), **f32), dw=torch.empty(M, **f32), doop=operand_copy(dfast_like, opt),
-        dS=torch.empty(B, T, operand_ld(T), device=dev, dtype=opt), dqf=torch.empty(B, T, M, **f32),
+        dS=bwd_work_buffer(B, T, M, D, precision, dev), dqf=torch.empty(B, T, M, **f32),
         dk=torch.empty(B, T, M, **f32),
         partial=torch.empty(int(lib.ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8),
         dh=torch.empty(B, T, D, **f32), dconv=torch.empty(D, K, **f32), dkw=torch.empty(M, D, **f32),
@@ -168,6 +168,14 @@ def addressed_memory(h, conv_weight, key_weight, key_bias, eps, v, g, w, precisi
                                                      eps.float().reshape(()), vv.contiguous(), g.float().reshape(()),
                                                      w.float().contiguous(), PRECISION[precision])
     return q, fast.to(out_dtype)
+
+
+def mixer_fwd_raw(x, h, conv_w, key_w, key_b, eps, v, g, w, mu, precision):
+    """The mixing span's forward without autograd (y = x + mu(q w) + fast, model.py:79-85) for
+    inference: returns (y, z, den, kop, vop), the output and what a decode prefill reads."""
+    z, den, u_op, kw = address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=False)
+    y, q, c, qop, kop, vop, P = combine_fwd_raw(z, den, v, g, w, mu, x, precision)
+    return y, z, den, kop, vop
 
 
 # ---- the whole mixing span of UnifiedBlock.forward with the combine fused (model.py:79-85) -------

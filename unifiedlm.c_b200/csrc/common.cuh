@@ -395,4 +395,21 @@ __device__ __forceinline__ void tmem_ld_32x16(uint32_t taddr, float (&out)[16]) 
   for (int i = 0; i < 16; ++i) out[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes written from registers (one row per
+// thread), followed by the wait that completes the stores before the thread reads them again or
+// signals another thread (which then needs tcgen05.fence::before_thread_sync on this side).
+__device__ __forceinline__ void tmem_st_32x16(uint32_t taddr, const float (&in)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(in[0])), "r"(__float_as_uint(in[1])), "r"(__float_as_uint(in[2])),
+      "r"(__float_as_uint(in[3])), "r"(__float_as_uint(in[4])), "r"(__float_as_uint(in[5])),
+      "r"(__float_as_uint(in[6])), "r"(__float_as_uint(in[7])), "r"(__float_as_uint(in[8])),
+      "r"(__float_as_uint(in[9])), "r"(__float_as_uint(in[10])), "r"(__float_as_uint(in[11])),
+      "r"(__float_as_uint(in[12])), "r"(__float_as_uint(in[13])), "r"(__float_as_uint(in[14])),
+      "r"(__float_as_uint(in[15]))
+      : "memory");
+}
+
 }  // namespace ulm

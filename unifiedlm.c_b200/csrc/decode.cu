@@ -259,7 +259,106 @@ __global__ void decode_embed_kernel(const int* __restrict__ tokens, const void* 
   }
 }
 
+// ---- parallel prefill: the decode state after a whole prompt ----------------------------------
+// After the training-form forward of a block over T prompt positions (z, den from ulm_address_fwd
+// with normalize = 0; kop, vop the operand copies of ulm_memory_fwd / ulm_memory_combine_fwd), the
+// block's recurrent state is what UnifiedBlock.step (model.py:96-111) leaves after those T tokens:
+//   U = w mu + sum_s lam^(T-1-s) v_s k_s^T   (k_s = r_{s-1}),   c = w + sum_s lam^(T-1-s) k_s,
+//   r_prev = r_{T-1},   buf = the last K-1 normalised inputs h, oldest first.
+// The sum over s is one carry product with a single chunk of T positions (the values scaled by
+// lam^(T-1-s), the state rows the value channels so it lands in the decoder's (D, M) layout).
+
+// c (run's update order c = (lam c + (1-lam) w) + r_prev from c = w) and r_prev; one thread per slot
+__global__ void decode_prefill_stats_kernel(const float* __restrict__ z, const float* __restrict__ den,
+                                            const float* __restrict__ w, const float* __restrict__ lam_p,
+                                            float* __restrict__ c, float* __restrict__ r_prev, int T, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (m >= M) return;
+  const float lam = *lam_p, one_minus = 1.0f - lam, wm = w[m];
+  const float* zb = z + (int64_t)b * T * M;
+  const float* db = den + (int64_t)b * T;
+  float cc = wm, rp = 0.f;
+  for (int t = 0; t < T; ++t) {
+    cc = __fadd_rn(__fadd_rn(__fmul_rn(lam, cc), __fmul_rn(one_minus, wm)), rp);
+    rp = zb[(int64_t)t * M + m] / db[t];
+  }
+  c[(int64_t)b * M + m] = cc;
+  r_prev[(int64_t)b * M + m] = rp;
+}
+
+// U[b] += w mu (the prior part of the state); buf[b][d][j] = h[b][T-kw+j][d] (0 before position 0)
+__global__ void decode_prefill_state_kernel(float* __restrict__ U, const float* __restrict__ mu,
+                                            const float* __restrict__ w, const void* __restrict__ h, int h_bf16,
+                                            float* __restrict__ buf, int B, int T, int D, int M, int kw) {
+  const int64_t nU = (int64_t)B * D * M;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nU; i += stride) {
+    const int64_t dm = i % ((int64_t)D * M);
+    U[i] = mu[dm] * w[dm % M] + U[i];
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)B * D * kw; i += stride) {
+    const int64_t b = i / ((int64_t)D * kw), rem = i - b * D * kw;
+    const int d = (int)(rem / kw), j = (int)(rem - (int64_t)d * kw);
+    const int t = T - kw + j;
+    float val = 0.f;
+    if (t >= 0) {
+      const int64_t off = ((int64_t)b * T + t) * D + d;
+      val = h_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(h)[off]) : static_cast<const float*>(h)[off];
+    }
+    buf[i] = val;
+  }
+}
+
 }  // namespace ulm
+
+extern "C" int64_t ulm_decode_prefill_work_bytes(int64_t B, int64_t T, int64_t D, int prec) {
+  if (B < 0 || T < 0 || D < 0 || (prec != ULM_PREC_BF16 && prec != ULM_PREC_FP32)) return -1;
+  return B * T * ulm_operand_ld(D) * (prec == ULM_PREC_FP32 ? 4 : 2);
+}
+
+extern "C" int ulm_decode_prefill_block(const void* kop, const void* vop, const float* g, const float* lam,
+                                        const float* z, const float* den, const void* h, int h_dtype,
+                                        const float* mu, const float* w, void* work, float* U, float* c,
+                                        float* r_prev, float* buf, int64_t B, int64_t T, int64_t D, int64_t M,
+                                        int64_t conv_size, int prec, void* stream) {
+  ULM_REQUIRE(prec == ULM_PREC_BF16 || prec == ULM_PREC_FP32, "prec must be ULM_PREC_BF16 or ULM_PREC_FP32");
+  ULM_REQUIRE(h_dtype == ULM_F32 || h_dtype == ULM_BF16, "h_dtype must be ULM_F32 or ULM_BF16");
+  ULM_REQUIRE(B > 0 && T > 0 && D > 0 && M > 0 && conv_size >= 1, "bad extents");
+  ULM_REQUIRE(B <= 65535 && T < (1 << 30) && D < (1 << 30) && M < (1 << 30), "extent too large");
+  ULM_REQUIRE(kop && vop && g && lam && z && den && h && mu && w && work && U && c && r_prev &&
+                  (buf || conv_size <= 1),
+              "null pointer argument");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int dt = op_dtype_of(prec);
+  const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D);
+  // the values scaled by lam^(T-1-s): one chunk of T positions
+  if (int rc = chunk_scale_rows(vop, work, dt, ldd, B * T, D, (int)T, g, (float)(T - 1), -1.f, st)) return rc;
+  {
+    // U[b][d][m] = sum_s vhat_s[d] k_s[m]: state rows d (A = vhat as [pos][d]), columns m (B = k)
+    Operand A{work, ldd, T * ldd, D, T, dt, true};
+    Operand Bk{kop, ldm, T * ldm, M, T, dt, true};
+    GemmShape s{(int)B, (int)D, (int)M, (int)T, CAUSAL_NONE};
+    s.carry = CARRY_FWD;
+    s.carry_C = (int)T;
+    s.carry_chunks = 1;
+    s.carry_end = 1;
+    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, U, M, D * M, g);
+    e.end_state = U;
+    e.end_ld = M;
+    e.end_bstride = D * M;
+    if (int rc = run_gemm(A, Bk, s, e, st)) return rc;
+  }
+  decode_prefill_stats_kernel<<<dim3((unsigned)cdiv(M, 256), (unsigned)B), 256, 0, st>>>(z, den, w, lam, c, r_prev,
+                                                                                       (int)T, (int)M);
+  ULM_LAUNCH_CHECK("decode_prefill_stats_kernel");
+  decode_prefill_state_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * D * M, 256), 8 * 148), 256, 0, st>>>(
+      U, mu, w, h, h_dtype == ULM_BF16, buf, (int)B, (int)T, (int)D, (int)M, (int)(conv_size - 1));
+  ULM_LAUNCH_CHECK("decode_prefill_state_kernel");
+  return ULM_OK;
+}
+
+
 
 using namespace ulm;
 

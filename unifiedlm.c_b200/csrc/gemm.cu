@@ -135,6 +135,12 @@ __device__ __forceinline__ void epilogue_math(const GemmEpilogue& e, float gl2, 
       dg_acc += v[i];  // row sum of this tile row (used when e.row_partial is set)
     }
   }
+  if (e.kind == EPI_ROW_DECAY) {
+    // one factor per row: lam^(rd_a + rd_s * row), all powers >= 0
+    const float f = fast_exp2(gl2 * (e.rd_a + e.rd_s * (float)row));
+#pragma unroll
+    for (int i = 0; i < NC; ++i) v[i] *= f;
+  }
   if (e.kind == EPI_STORE_ADD) {
 #pragma unroll
     for (int i = 0; i < NC; ++i) v[i] += p[i];
@@ -408,7 +414,9 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
   const bool active = part * PART < BN;
   const int mode = epi.staged;
   const bool f32 = epi.out_dtype == ULM_F32;
-  const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG) ? (*epi.g) * 1.4426950408889634f : 0.f;
+  const float gl2 = (epi.kind == EPI_DECAY || epi.kind == EPI_DECAY_DG || epi.kind == EPI_ROW_DECAY)
+                        ? (*epi.g) * 1.4426950408889634f
+                        : 0.f;
   uint8_t* wslots = stage + ew * (SLOTS * 4096);  // this warp's staging tiles
   uint64_t* wbar = aux_bar + ew * SLOTS;
   int n = 0;         // staged chunks of this warp so far (slot n % SLOTS)
@@ -511,6 +519,218 @@ __device__ __forceinline__ void epilogue_warps(const GemmShape& shape, const Gem
   }
 }
 
+// ---- carry products ----------------------------------------------------------------------------
+// A CTA (pair) of a carry product takes its tiles (slots t_first, t_first + t_stride, ...) in
+// groups of two: the chunk steps of the two tiles alternate, the first in accumulator 0 and the
+// second in accumulator 1, so one tile's epilogue (state write and rescale) overlaps the other
+// tile's MMAs. A last group of one tile keeps accumulator 0. f(t, chunk, acc, step, steps) is
+// called for every step in that order by all three roles; false stops the walk.
+template <typename F>
+__device__ __forceinline__ bool carry_walk(int t_first, int t_stride, int total_tiles, const GemmShape& s, F&& f) {
+  const int steps = carry_steps(s);
+  if (steps <= 0) return true;
+  for (int t0 = t_first; t0 < total_tiles; t0 += 2 * t_stride) {
+    const int t1 = t0 + t_stride;
+    const int members = t1 < total_tiles ? 2 : 1;
+    for (int st = 0; st < steps; ++st) {
+      const int chunk = s.carry == CARRY_FWD ? st : s.carry_chunks - 1 - st;
+      for (int m = 0; m < members; ++m)
+        if (!f(m ? t1 : t0, chunk, m, st, steps)) return false;
+    }
+  }
+  return true;
+}
+
+// The epilogue warps of a carry product. For every chunk step: wait for the accumulator, write
+// the state it holds to slot (b * NT + state index) of the output (staged through shared memory
+// and TMA stores, or stored directly when the layout does not allow that), or after the last
+// forward chunk with carry_end the fp32 end state (direct stores); with an aux (the other state
+// sequence, same layout) add the warp's share of <state, aux>; unless this was the tile's last step
+// multiply the accumulator by lam^C in tensor memory; hand the accumulator back. A tile's
+// <state, aux> sum, times aux_dot_scale, goes to tile_partial[part_stride * t + part_off + warp].
+template <int BM, int BN, bool PAIR, int SLOTS>
+__device__ __forceinline__ void carry_epilogue_warps(const GemmShape& shape, const GemmEpilogue& epi,
+                                                     const CUtensorMap* tma_out, const CUtensorMap* tma_aux,
+                                                     int m_blocks, int n_blocks, int tiles_per_batch,
+                                                     int total_tiles, int t_first, int t_stride, int cta_rows,
+                                                     uint32_t tmem_base, uint64_t* tfull, uint64_t* tempty,
+                                                     uint32_t leader_tempty, uint8_t* stage, uint64_t* aux_bar,
+                                                     volatile int* abort_flag, int site, int part_stride,
+                                                     int part_off) {
+  constexpr int PART = BN / (EPI_WARPS / 4) < 64 ? 64 : BN / (EPI_WARPS / 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ew = warp - 2;
+  const int quad = warp & 3;
+  const int part = ew >> 2;
+  const bool active = part * PART < BN;
+  const bool f32 = epi.out_dtype == ULM_F32;
+  const bool staged = epi.staged == EPI_MODE_WARP;
+  const bool dot = epi.aux != nullptr;
+  const float lamC = fast_exp2((*epi.g) * 1.4426950408889634f * (float)shape.carry_C);
+  const int NT = shape.carry_chunks;
+  uint8_t* wslots = stage + ew * (SLOTS * 4096);
+  uint64_t* wbar = aux_bar + ew * SLOTS;
+  const int cw = f32 ? 32 : 64;  // columns of a staged chunk
+  int n = 0;                     // staged chunks of this warp so far (slot n % SLOTS)
+  int n_issued = 0;              // aux loads issued by this warp (lane 0's count)
+  int uses[2] = {0, 0};
+  float dg_member[2] = {0.f, 0.f};
+  const bool ok = carry_walk(t_first, t_stride, total_tiles, shape,
+                             [&](int t, int chunk, int acc, int step, int steps) -> bool {
+    const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+    const uint32_t acc_phase = (uint32_t)(uses[acc]++) & 1u;
+    const int row_base = tc.mb * BM + cta_rows + quad * 32;
+    const int row = row_base + lane;
+    const int col_base = tc.nb * BN + part * PART;
+    const bool cols = active && row_base < shape.M && col_base < shape.N;
+    const bool last = step == steps - 1;
+    const bool to_end = shape.carry == CARRY_FWD && shape.carry_end && chunk == NT - 1;
+    const int slot = shape.carry == CARRY_FWD ? chunk + 1 : chunk - 1;
+    const int ob = tc.b * NT + slot;  // output (and aux) batch coordinate
+    const int nch = (cols && !to_end && staged) ? min(PART / cw, (shape.N - col_base + cw - 1) / cw) : 0;
+    if (dot && lane == 0 && nch > 0) {
+      bulk_wait_group_read<0>();  // every earlier store of this warp has read its slot
+      for (int i = 0; i < nch && i < SLOTS; ++i) {
+        epi_aux_issue<SLOTS>(tma_aux, wslots, wbar, n + i, col_base + i * cw, row_base, ob);
+        ++n_issued;
+      }
+    }
+    if (!wait_or_abort(&tfull[acc], acc_phase, abort_flag, site)) return false;
+    tc_fence_after();
+    const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + part * PART);
+    float dg_acc = 0.f;
+    if (!cols) {
+      // nothing of this tile for this warp: only its barrier arrival below
+    } else if (to_end) {
+#pragma unroll 1
+      for (int c = 0; c < PART; c += 16) {
+        float v[16];
+        tmem_ld_32x16(taddr + (uint32_t)c, v);
+        const int col0 = col_base + c;
+        if (row < shape.M) {
+          float* o = epi.end_state + (int64_t)tc.b * epi.end_bstride + (int64_t)row * epi.end_ld;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (col0 + i < shape.N) o[col0 + i] = v[i];
+        }
+      }
+    } else if (staged) {
+#pragma unroll 1
+      for (int i = 0; i < nch; ++i) {
+        const int sl = n % SLOTS;
+        const uint32_t parity = (uint32_t)(n / SLOTS) & 1u;
+        ++n;
+        uint8_t* tile = wslots + sl * 4096;
+        if (!dot) {
+          if (lane == 0) bulk_wait_group_read<SLOTS - 1>();  // the store of chunk n - SLOTS has read the slot
+          __syncwarp();
+        } else if (!wait_or_abort(&wbar[sl], parity, abort_flag, site)) {
+          return false;
+        }
+#pragma unroll 1
+        for (int h = 0; h < (f32 ? 2 : 4); ++h) {
+          float v[16];
+          const uint32_t ta = taddr + (uint32_t)(i * cw + 16 * h);
+          tmem_ld_32x16(ta, v);
+          const int u0 = f32 ? 4 * h : 2 * h;
+          if (dot) {
+            float p[16];
+            if (f32)
+              stage_read<true, 16>(tile, lane, u0, p);
+            else
+              stage_read<false, 16>(tile, lane, u0, p);
+            const int c0 = col_base + i * cw + 16 * h;
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c0 + e < shape.N) dg_acc = fmaf(p[e], v[e], dg_acc);
+          }
+          if (f32)
+            stage_write<true, 16>(tile, lane, u0, v);
+          else
+            stage_write<false, 16>(tile, lane, u0, v);
+          if (!last) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] *= lamC;
+            tmem_st_32x16(ta, v);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(tma_out, tile, col_base + i * cw, row_base, ob);
+          bulk_commit_group();
+          if (dot && i + SLOTS < nch) {
+            bulk_wait_group_read<0>();  // the store just issued has read the slot
+            epi_aux_issue<SLOTS>(tma_aux, wslots, wbar, n - 1 + SLOTS, col_base + (i + SLOTS) * cw, row_base, ob);
+            ++n_issued;
+          }
+        }
+        __syncwarp();
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < PART; c += 16) {
+        float v[16];
+        tmem_ld_32x16(taddr + (uint32_t)c, v);
+        const int col0 = col_base + c;
+        if (row < shape.M) {
+          const int64_t off = (int64_t)ob * epi.out_bstride + (int64_t)row * epi.ldo + col0;
+          const int64_t aoff = (int64_t)ob * epi.aux_bstride + (int64_t)row * epi.ld_aux + col0;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (col0 + e >= shape.N) continue;
+            if (f32) {
+              reinterpret_cast<float*>(epi.out)[off + e] = v[e];
+              if (dot) dg_acc = fmaf(reinterpret_cast<const float*>(epi.aux)[aoff + e], v[e], dg_acc);
+            } else {
+              reinterpret_cast<__nv_bfloat16*>(epi.out)[off + e] = __float2bfloat16_rn(v[e]);
+              if (dot)
+                dg_acc = fmaf(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.aux)[aoff + e]), v[e],
+                              dg_acc);
+            }
+          }
+        }
+        if (!last) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] *= lamC;
+          tmem_st_32x16(taddr + (uint32_t)c, v);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (PAIR)
+        mbar_arrive_cluster(leader_tempty + (uint32_t)(acc * sizeof(uint64_t)));
+      else
+        mbar_arrive(&tempty[acc]);
+    }
+    dg_member[acc] += dg_acc;
+    if (last && dot) {
+      float d = dg_member[acc];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      if (lane == 0)
+        epi.tile_partial[part_stride * (int64_t)t + part_off + ew] =
+            d * epi.aux_dot_scale * fast_exp2((*epi.g) * 1.4426950408889634f * epi.aux_dot_pow);
+      dg_member[acc] = 0.f;
+    }
+    return true;
+  });
+  if (lane == 0) {
+    // aux loads still in flight after an abort land before the CTA exits; stores complete
+    if (!ok && dot && staged) {
+      for (int k = max(0, n_issued - SLOTS); k < n_issued; ++k) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&wbar[k % SLOTS], (uint32_t)(k / SLOTS) & 1u) &&
+               globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+    bulk_wait_group<0>();
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // tensor-core back end
 
@@ -586,7 +806,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (epi.staged != EPI_MODE_DIRECT) {
       tma_prefetch_desc(&tma_out);
-      if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
+      if (has_tile_aux(epi.kind) || (shape.carry && epi.aux)) tma_prefetch_desc(&tma_aux);
     }
   }
   if (warp == 1) {
@@ -606,7 +826,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages issued and possibly not yet consumed (for draining on abort)
       bool ok = true;
-      const int rounded = (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
+      if (shape.carry) {
+        ok = carry_walk(blockIdx.x, gridDim.x, total_tiles, shape, [&](int t, int chunk, int, int, int) -> bool {
+          const TileCoord tc = decode_tile<TC_BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+          const int k_lo = chunk * shape.carry_C, k_hi = min(shape.K, k_lo + shape.carry_C);
+          for (int kb = k_lo / TC_BK; kb * TC_BK < k_hi; ++kb) {
+            if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM_PRODUCER_WAIT)) return false;
+            uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+            uint8_t* sb = sa + Cfg::A_BYTES;
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+            const int k0 = kb * TC_BK;
+            if (!A_MN) {
+              tma_load_3d(&tma_a, sa, &full[stage], k0, tc.mb * TC_BM, tc.b);
+            } else {
+#pragma unroll
+              for (int j = 0; j < TC_BM / 64; ++j)
+                tma_load_3d(&tma_a, sa + j * MN_LBO, &full[stage], tc.mb * TC_BM + j * 64, k0, tc.b);
+            }
+            if (!B_MN) {
+              tma_load_3d(&tma_b, sb, &full[stage], k0, tc.nb * BN, tc.b);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(&tma_b, sb + j * MN_LBO, &full[stage], tc.nb * BN + j * 64, k0, tc.b);
+            }
+            issued = min(issued + 1, STAGES);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          return true;
+        });
+      }
+      const int rounded =
+          shape.carry ? 0 : (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
       for (int tt = blockIdx.x; tt < rounded && ok; tt += gridDim.x) {
         const int t = schedule_tile(tt, gridDim.x, total_tiles, shape.balanced);
         if (t < 0) continue;
@@ -670,7 +924,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int j = 0;
       bool ok = true, issued_any = false;
-      const int rounded = (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
+      if (shape.carry) {
+        int uses[2] = {0, 0};
+        ok = carry_walk(blockIdx.x, gridDim.x, total_tiles, shape, [&](int, int chunk, int acc, int step, int) -> bool {
+          const uint32_t acc_phase = (uint32_t)(uses[acc]++) & 1u;
+          if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM_MMA_WAIT)) return false;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+          const int k_lo = chunk * shape.carry_C, k_hi = min(shape.K, k_lo + shape.carry_C);
+          for (int kb = k_lo / TC_BK, i = 0; kb * TC_BK < k_hi; ++kb, ++i) {
+            if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM_MMA_WAIT)) return false;
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+            const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+              const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
+              const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
+              umma_bf16_ss(d_tmem, ad, bd, IDESC, (step > 0 || i > 0 || kk > 0) ? 1u : 0u);
+            }
+            issued_any = true;
+            umma_commit(&empty[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          umma_commit(&tfull[acc]);
+          return true;
+        });
+      }
+      const int rounded =
+          shape.carry ? 0 : (total_tiles + (int)gridDim.x - 1) / (int)gridDim.x * (int)gridDim.x;
       for (int tt = blockIdx.x; tt < rounded && ok; tt += gridDim.x) {
         const int t = schedule_tile(tt, gridDim.x, total_tiles, shape.balanced);
         if (t < 0) continue;
@@ -719,7 +1004,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2.., TMEM lane quadrant = warp % 4) ----------------
-    epilogue_warps<TC_BM, BN, false, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
+    if (shape.carry)
+      carry_epilogue_warps<TC_BM, BN, false, Cfg::EPI_SLOTS>(
+          shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, blockIdx.x, gridDim.x,
+          0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar, abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, EPI_WARPS, 0);
+    else
+      epilogue_warps<TC_BM, BN, false, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles,
                                      blockIdx.x, gridDim.x, 0, tmem_base, tfull, tempty, 0u, epi_stage, aux_bar,
                                      abort_flag, DEVERR_GEMM_EPILOGUE_WAIT, EPI_WARPS, 0);
   }
@@ -814,7 +1104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
     if (epi.staged != EPI_MODE_DIRECT) {
       tma_prefetch_desc(&tma_out);
-      if (has_tile_aux(epi.kind)) tma_prefetch_desc(&tma_aux);
+      if (has_tile_aux(epi.kind) || (shape.carry && epi.aux)) tma_prefetch_desc(&tma_aux);
     }
   }
   if (warp == 1) {
@@ -835,7 +1125,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      const int rounded = (total_tiles + pairs - 1) / pairs * pairs;
+      // one stage: k block kb (64 k values) of the first operand pair for tile coordinate tc
+      auto load_stage = [&](const TileCoord& tc, int kb) -> bool {
+        if (!wait_or_abort(&empty[stage], phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) return false;
+        uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
+        uint8_t* sb = sa + Cfg::A_BYTES;
+        const uint32_t bar = leader_full + (uint32_t)(stage * sizeof(uint64_t));
+        if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+        const int k0 = kb * TC_BK;
+        const int row0 = tc.mb * BM + (int)rank * 128;
+        const int col0 = tc.nb * BN + (int)rank * 128;
+        if (!A_MN) {
+          tma_load_3d_pair(&tma_a, sa, bar, k0, row0, tc.b);
+        } else {
+          tma_load_3d_pair(&tma_a, sa, bar, row0, k0, tc.b);
+          tma_load_3d_pair(&tma_a, sa + MN_LBO, bar, row0 + 64, k0, tc.b);
+        }
+        if (!B_MN) {
+          tma_load_3d_pair(&tma_b, sb, bar, k0, col0, tc.b);
+        } else {
+          tma_load_3d_pair(&tma_b, sb, bar, col0, k0, tc.b);
+          tma_load_3d_pair(&tma_b, sb + MN_LBO, bar, col0 + 64, k0, tc.b);
+        }
+        issued = min(issued + 1, STAGES);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        return true;
+      };
+      if (shape.carry) {
+        ok = carry_walk(pair, pairs, total_tiles, shape, [&](int t, int chunk, int, int, int) -> bool {
+          const TileCoord tc = decode_tile<BM, BN>(t, shape, m_blocks, n_blocks, tiles_per_batch);
+          const int k_lo = chunk * shape.carry_C, k_hi = min(shape.K, k_lo + shape.carry_C);
+          for (int kb = k_lo / TC_BK; kb * TC_BK < k_hi; ++kb)
+            if (!load_stage(tc, kb)) return false;
+          return true;
+        });
+      }
+      const int rounded = shape.carry ? 0 : (total_tiles + pairs - 1) / pairs * pairs;
       for (int tt = pair; tt < rounded && ok; tt += pairs) {
         const int t = schedule_tile(tt, pairs, total_tiles, shape.balanced);
         if (t < 0) continue;
@@ -899,7 +1227,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0;
       int j = 0;
       bool ok = true, issued_any = false;
-      const int rounded = (total_tiles + pairs - 1) / pairs * pairs;
+      if (shape.carry) {
+        int uses[2] = {0, 0};
+        ok = carry_walk(pair, pairs, total_tiles, shape, [&](int, int chunk, int acc, int step, int) -> bool {
+          const uint32_t acc_phase = (uint32_t)(uses[acc]++) & 1u;
+          if (!wait_or_abort(&tempty[acc], acc_phase ^ 1u, abort_flag, DEVERR_GEMM2_WAIT)) return false;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+          const int k_lo = chunk * shape.carry_C, k_hi = min(shape.K, k_lo + shape.carry_C);
+          for (int kb = k_lo / TC_BK, i = 0; kb * TC_BK < k_hi; ++kb, ++i) {
+            if (!wait_or_abort(&full[stage], phase, abort_flag, DEVERR_GEMM2_WAIT)) return false;
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+            const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; ++kk) {
+              const uint64_t ad = smem_desc_sw128(sa + kk * A_KSTEP, A_MN ? MN_LBO : 16, SBO);
+              const uint64_t bd = smem_desc_sw128(sb + kk * B_KSTEP, B_MN ? MN_LBO : 16, SBO);
+              // the first chunk starts the state; later chunks add to the rescaled state
+              umma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (step > 0 || i > 0 || kk > 0) ? 1u : 0u);
+            }
+            issued_any = true;
+            umma_commit_pair(&empty[stage], 0x3);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          umma_commit_pair(&tfull[acc], 0x3);
+          return true;
+        });
+      }
+      const int rounded = shape.carry ? 0 : (total_tiles + pairs - 1) / pairs * pairs;
       for (int tt = pair; tt < rounded && ok; tt += pairs) {
         const int t = schedule_tile(tt, pairs, total_tiles, shape.balanced);
         if (t < 0) continue;
@@ -948,7 +1307,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- epilogue (warps 2.. of both CTAs) ----------------
-    epilogue_warps<BM, BN, true, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
+    if (shape.carry)
+      carry_epilogue_warps<BM, BN, true, Cfg::EPI_SLOTS>(
+          shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair, pairs,
+          (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0), epi_stage, aux_bar,
+          abort_flag, DEVERR_GEMM2_WAIT, 2 * EPI_WARPS, (int)rank * EPI_WARPS);
+    else
+      epilogue_warps<BM, BN, true, Cfg::EPI_SLOTS>(shape, epi, &tma_out, &tma_aux, m_blocks, n_blocks, tiles_per_batch, total_tiles, pair,
                                  pairs, (int)rank * 128, tmem_base, tfull, tempty, mapa_shared(smem_u32(tempty), 0),
                                  epi_stage, aux_bar, abort_flag, DEVERR_GEMM2_WAIT, 2 * EPI_WARPS,
                                  (int)rank * EPI_WARPS);
@@ -1020,6 +1385,64 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
   }
   };
+  if (shape.carry) {
+    // carry product: the 64 x 64 state tile stays in registers across the chunks; after each chunk
+    // it is written to its slot (or the end state), dotted with the aux states, and rescaled
+    const int NT = shape.carry_chunks, steps = carry_steps(shape);
+    const float lamC = expf(*epi.g * (float)shape.carry_C);
+    const bool dot = epi.aux != nullptr;
+    float dgp = 0.f;
+    for (int step = 0; step < steps; ++step) {
+      const int chunk = shape.carry == CARRY_FWD ? step : NT - 1 - step;
+      segment(Ab, lda, Bb, ldb, chunk * shape.carry_C, min(shape.K, (chunk + 1) * shape.carry_C));
+      const bool to_end = shape.carry == CARRY_FWD && shape.carry_end && chunk == NT - 1;
+      const int64_t ob = (int64_t)tc.b * NT + (shape.carry == CARRY_FWD ? chunk + 1 : chunk - 1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = tc.mb * BM + ty + 16 * i;
+        if (row >= shape.M) continue;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int col = tc.nb * BN + tx + 16 * jj;
+          if (col >= shape.N) continue;
+          const float v = acc[i][jj];
+          if (to_end) {
+            epi.end_state[(int64_t)tc.b * epi.end_bstride + (int64_t)row * epi.end_ld + col] = v;
+            continue;
+          }
+          const int64_t off = ob * epi.out_bstride + (int64_t)row * epi.ldo + col;
+          const int64_t aoff = ob * epi.aux_bstride + (int64_t)row * epi.ld_aux + col;
+          if (epi.out_dtype == ULM_F32) {
+            reinterpret_cast<float*>(epi.out)[off] = v;
+            if (dot) dgp = fmaf(reinterpret_cast<const float*>(epi.aux)[aoff], v, dgp);
+          } else {
+            reinterpret_cast<__nv_bfloat16*>(epi.out)[off] = __float2bfloat16_rn(v);
+            if (dot) dgp = fmaf(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.aux)[aoff]), v, dgp);
+          }
+        }
+      }
+      if (step + 1 < steps) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) acc[i][jj] *= lamC;
+      }
+    }
+    if (dot) {
+      // fixed-order block reduction, one partial per tile (slots 1..3 of the tile are zero)
+      __shared__ float cred[256];
+      cred[threadIdx.x] = dgp;
+      __syncthreads();
+      for (int stride = 128; stride > 0; stride >>= 1) {
+        if ((int)threadIdx.x < stride) cred[threadIdx.x] += cred[threadIdx.x + stride];
+        __syncthreads();
+      }
+      if (threadIdx.x < 4)
+        epi.tile_partial[4 * (int64_t)blockIdx.x + threadIdx.x] =
+            threadIdx.x == 0 ? cred[0] * epi.aux_dot_scale * expf(*epi.g * epi.aux_dot_pow) : 0.f;
+    }
+    return;
+  }
   segment(Ab, lda, Bb, ldb, tc.k_begin, tc.k_end);
   if (shape.K2 > 0)
     segment(A2 + (shape.a2_batched ? (int64_t)tc.b * bsA2 : 0), lda2, B2 + (shape.b2_batched ? (int64_t)tc.b * bsB2 : 0),
@@ -1077,6 +1500,7 @@ __global__ void __launch_bounds__(256)
         dg_acc = fmaf((float)(row - col) * p, v, dg_acc);
       }
       if (decay) v = (col <= row) ? v * expf(g * (float)(row - col)) : 0.f;
+      if (epi.kind == EPI_ROW_DECAY) v *= expf(*epi.g * (epi.rd_a + epi.rd_s * (float)row));
       if (epi.kind == EPI_STORE_ADD) {
         const int64_t ai = (int64_t)tc.b * epi.aux_bstride + (int64_t)row * epi.ld_aux + col;
         v += epi.out_dtype == ULM_F32 ? reinterpret_cast<const float*>(epi.aux)[ai]
@@ -1205,10 +1629,12 @@ void prepare_epilogue(GemmEpilogue& e, const GemmShape& s, CUtensorMap* tout, CU
   memset(tout, 0, sizeof(CUtensorMap));
   memset(taux, 0, sizeof(CUtensorMap));
   const int mode = g_epi_mode;
+  // a carry product writes one state per chunk slot: its output (and aux) hold batches * chunks
+  const int ob = s.carry ? s.batches * s.carry_chunks : s.batches;
   bool ok = mode != EPI_MODE_DIRECT && e.vec_ok && s.N >= 32 &&
-            make_epi_tmap(tout, mode, e.out, e.out_dtype, s.N, s.M, s.batches, e.ldo, e.out_bstride);
-  if (ok && has_tile_aux(e.kind))
-    ok = make_epi_tmap(taux, mode, e.aux, e.out_dtype, s.N, s.M, s.batches, e.ld_aux, e.aux_bstride);
+            make_epi_tmap(tout, mode, e.out, e.out_dtype, s.N, s.M, ob, e.ldo, e.out_bstride);
+  if (ok && (has_tile_aux(e.kind) || (s.carry && e.aux)))
+    ok = make_epi_tmap(taux, mode, e.aux, e.out_dtype, s.N, s.M, ob, e.ld_aux, e.aux_bstride);
   e.staged = ok ? mode : EPI_MODE_DIRECT;
 }
 
@@ -1370,6 +1796,17 @@ int run_gemm2(const Operand& A, const Operand& B, const Operand* A2, const Opera
   ULM_REQUIRE(e.kind != EPI_STORE_ADD || e.aux, "EPI_STORE_ADD needs the addend (in the output's type)");
   if (s.causal == CAUSAL_KLOWER || s.causal == CAUSAL_KUPPER)
     ULM_REQUIRE(s.M == s.K, "causal k range needs a square (M == K) problem");
+  if (s.carry) {
+    ULM_REQUIRE(s.carry == CARRY_FWD || s.carry == CARRY_REV, "bad carry mode");
+    ULM_REQUIRE(s.causal == CAUSAL_NONE && s.ksplit <= 1 && s.K2 == 0 && e.kind == EPI_STORE && e.g,
+                "a carry product is a plain product (no causal range, split K or second pair) with EPI_STORE and g");
+    ULM_REQUIRE(s.carry_C > 0 && s.carry_chunks >= 1 && (int64_t)s.carry_C * (s.carry_chunks - 1) < s.K &&
+                    (int64_t)s.carry_C * s.carry_chunks >= s.K,
+                "carry chunks must cover K");
+    ULM_REQUIRE(s.carry_chunks == 1 || s.carry_C % 64 == 0, "carry chunk length must be a multiple of 64");
+    ULM_REQUIRE(!s.carry_end || (s.carry == CARRY_FWD && e.end_state), "carry_end needs CARRY_FWD and end_state");
+    ULM_REQUIRE(!e.aux || e.tile_partial, "a carry aux dot needs tile_partial");
+  }
   ULM_REQUIRE(s.ksplit <= 1 || (s.causal == CAUSAL_NONE && s.ksplit == s.batches &&
                                  (int64_t)(s.ksplit - 1) * ksplit_chunk(s.K, s.ksplit) < s.K),
               "split K needs a non-causal product, batches == ksplit and no empty k range");

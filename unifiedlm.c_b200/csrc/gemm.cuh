@@ -21,7 +21,17 @@
 namespace ulm {
 
 enum { CAUSAL_NONE = 0, CAUSAL_KLOWER = 1, CAUSAL_KUPPER = 2, CAUSAL_NLOWER = 3 };
-enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RELU2 = 4, EPI_LSE = 5, EPI_CE_GRAD = 6 };
+enum { EPI_STORE = 0, EPI_DECAY = 1, EPI_DECAY_DG = 2, EPI_STORE_ADD = 3, EPI_RELU2 = 4, EPI_LSE = 5, EPI_CE_GRAD = 6,
+       EPI_ROW_DECAY = 7 };
+
+// Carry products (GemmShape.carry): the k dimension is time, cut into chunks of carry_C positions,
+// and the accumulator of an (M x N) tile is a state that runs across the chunks,
+//   forward : S_{c+1} = lam^C S_c + A_c B_c^T   for chunks c = 0, 1, ..., written as S_1, S_2, ...
+//   reverse : R_{c-1} = lam^C R_c + A_c B_c^T   for chunks c = NT-1, ..., 1, written as R_{NT-2}, ...
+// (A_c, B_c: the chunk's k range of the operands). After each chunk the epilogue writes the state
+// to slot (b * NT + state index) of the output, multiplies the accumulator by lam^C in tensor
+// memory and hands it back, so the state never leaves the SM between chunks.
+enum { CARRY_NONE = 0, CARRY_FWD = 1, CARRY_REV = 2 };
 
 struct GemmShape {
   int batches, M, N, K;
@@ -37,7 +47,20 @@ struct GemmShape {
   // a2_batched / b2_batched (set by run_gemm2) say whether they have a batch stride
   int K2;
   int a2_batched, b2_batched;
+  // carry products: CARRY_FWD / CARRY_REV, chunk length (a multiple of 64 unless there is one chunk)
+  // and chunk count (K = carry_C * carry_chunks); CARRY_FWD with carry_end also runs the last
+  // chunk, whose state goes to GemmEpilogue.end_state instead of a slot
+  int carry = 0;
+  int carry_C = 0;
+  int carry_chunks = 0;
+  int carry_end = 0;
 };
+
+// Chunk steps a carry tile runs.
+__host__ __device__ inline int carry_steps(const GemmShape& s) {
+  if (s.carry == CARRY_FWD) return s.carry_end ? s.carry_chunks : s.carry_chunks - 1;
+  return s.carry_chunks - 1;
+}
 
 __host__ __device__ inline int ksplit_chunk(int K, int ksplit) { return ((K + ksplit - 1) / ksplit + 63) / 64 * 64; }
 
@@ -75,6 +98,15 @@ struct GemmEpilogue {
   const float* row_lse = nullptr;
   const float* scale = nullptr;
   int rows_valid = 0;  // rows of the product (bound for targets / row_lse reads)
+  // EPI_ROW_DECAY: out = lam^(rd_a + rd_s * row) * acc (row = the row inside its batch row)
+  float rd_a = 0.f, rd_s = 0.f;
+  // carry products: optional tile aux (the other state sequence, same layout and type as the
+  // output) whose elementwise product with each written state is summed per warp into
+  // tile_partial (scaled by aux_dot_scale * lam^aux_dot_pow); optional fp32 end state (batch
+  // stride end_bstride, row stride end_ld) for CARRY_FWD with carry_end
+  float aux_dot_scale = 0.f, aux_dot_pow = 0.f;
+  float* end_state = nullptr;
+  int64_t end_ld = 0, end_bstride = 0;
 };
 
 // A matrix operand in global memory: element (b, row, col) of its storage order at
@@ -147,11 +179,21 @@ inline int tiles_per_batch_host(const GemmShape& s, int BM, int BN, int m_blocks
   return n;
 }
 
-// Upper bound of tile_partial entries an EPI_DECAY_DG launch over (batches, T x T) writes.
-inline int64_t decay_dg_partials(int64_t batches, int64_t T) {
-  const int64_t b = (T + 63) / 64;
-  return 4 * batches * b * b;
+// Entries of tile_partial an EPI_DECAY_DG launch over (batches, T x T) may write, for every back
+// end: 16 per 256 x 256 tile on CTA pairs, 8 per 128-row tile on single CTAs (columns of 128 or
+// 256), 4 per 64 x 64 tile of the FMA kernel.
+inline int64_t tile_partials_2d(int64_t batches, int64_t M, int64_t N) {
+  auto b = [](int64_t n, int64_t t) { return (n + t - 1) / t; };
+  int64_t e = 4 * b(M, 64) * b(N, 64);
+  e = e > 8 * b(M, 128) * b(N, 128) ? e : 8 * b(M, 128) * b(N, 128);
+  e = e > 16 * b(M, 256) * b(N, 256) ? e : 16 * b(M, 256) * b(N, 256);
+  return batches * e;
 }
+
+inline int64_t decay_dg_partials(int64_t batches, int64_t T) { return tile_partials_2d(batches, T, T); }
+
+// Entries of tile_partial a carry product with an aux dot over (batches, M x N) states may write.
+inline int64_t carry_dot_partials(int64_t batches, int64_t M, int64_t N) { return tile_partials_2d(batches, M, N); }
 
 // Host entry: validates, picks the back end from the operand types, launches on `stream`.
 int run_gemm(const Operand& A, const Operand& B, const GemmShape& s, const GemmEpilogue& e, cudaStream_t stream);

@@ -352,6 +352,414 @@ extern "C" int ulm_causal_apply(const void* P, int64_t ldp, const void* c, int64
   return run_gemm(A, Bo, s, e, static_cast<cudaStream_t>(stream));
 }
 
+// ---- the chunk-carry form of the fast read (long sequences) ----------------------------------
+// For T well above the slot and value widths the whole-sequence products cost T (M + D) flops per
+// token; the reference's chunked form costs 4 M D + 2 C (M + D). Here the chunked form runs on the
+// same GEMM engine: a carry product walks the chunks with the (M x D) state in the tensor cores'
+// accumulator (written once per chunk boundary, in the operand type), the inter-chunk read is a
+// product against those states with a per-row decay, and the intra-chunk part is the
+// whole-sequence machinery on C-long pieces (batches B * T / C). The backward runs one reverse
+// carry (the state of q dO^T from the chunks to the right), three inter-chunk products and the
+// intra-chunk products; d/dg gets three extra position-weighted sums (see chunk_read_bwd).
+namespace ulm {
+namespace {
+
+// -1: automatic; 0: always the whole-sequence form; > 0: this chunk length wherever T is a multiple
+// of it with at least two chunks (ulm_set_chunk_mode)
+int g_chunk_mode = -1;
+
+constexpr int DOT_BLOCKS = 296;  // fixed grid of the weighted dot products (deterministic partials)
+
+// Chunk length of the operator's fast read, 0 = the whole-sequence form. Automatic: C = 256 on the
+// tensor cores (the pair tiles' 256 rows: one diagonal tile per chunk) or 64 in fp32 (the FMA back
+// end's 64-row tiles), where T is a multiple of C with at least two chunks and the chunked form's
+// flops per token 4 M D + 2 C (M + D) are fewer than the whole-sequence form's T (M + D).
+int chunk_len(int64_t T, int64_t M, int64_t D, int prec) {
+  if (g_chunk_mode == 0 || M == 0 || D == 0) return 0;
+  const int64_t C = g_chunk_mode > 0 ? g_chunk_mode : (prec == ULM_PREC_FP32 ? 64 : 256);
+  if (T % C != 0 || T / C < 2) return 0;
+  if (g_chunk_mode > 0) return (int)C;
+  return (double)T * (double)(M + D) > 4.0 * (double)M * (double)D + 2.0 * (double)C * (double)(M + D) ? (int)C : 0;
+}
+
+struct ChunkFwdLayout {
+  void* Pc;    // (B, T, C) intra-chunk decayed scores, operand type
+  void* Hs;    // (B, NT, M, ldD) state entering each chunk (slot 0 = zero), operand type
+  float* Fi;   // (B, T, D) inter-chunk read, fp32
+  void* work;  // the carry's decayed values (B, T, ldD), then the intra read's addend (B, T, D)
+  int64_t bytes;
+};
+
+ChunkFwdLayout chunk_fwd_layout(void* base, int64_t B, int64_t T, int64_t M, int64_t D, int64_t C, int prec) {
+  const int64_t es = prec == ULM_PREC_FP32 ? 4 : 2, ldd = ulm_operand_ld(D), NT = T / C;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  ChunkFwdLayout L;
+  int64_t off = 0;
+  L.Pc = p + off;
+  off += align256(B * T * C * es);
+  L.Hs = p + off;
+  off += align256(B * NT * M * ldd * es);
+  L.Fi = reinterpret_cast<float*>(p + off);
+  off += align256(B * T * D * 4);
+  L.work = p + off;
+  off += align256(B * T * std::max<int64_t>(ldd * es, D * 4));
+  L.bytes = off;
+  return L;
+}
+
+struct ChunkBwdLayout {
+  void* dSc;      // (B, T, C) intra-chunk score gradient
+  void* Rs;       // (B, NT, M, ldD) reverse states (slot NT-1 = zero)
+  float* Fv;      // (B, T, D) inter-chunk part of dv, fp32
+  void* dOhat;    // (B, T, ldD) upstream gradient times lam^(position in chunk)
+  void* auxv;     // (B, T, D) the intra dv product's addend in dv's type
+  float* tiles;   // d/dg partials: score epilogue, reverse-carry dot, the two weighted sums
+  int64_t n_score, n_carry, n_tiles;
+  int64_t bytes;
+};
+
+ChunkBwdLayout chunk_bwd_layout(void* base, int64_t B, int64_t T, int64_t M, int64_t D, int64_t C, int prec) {
+  const int64_t es = prec == ULM_PREC_FP32 ? 4 : 2, ldd = ulm_operand_ld(D), NT = T / C;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  ChunkBwdLayout L;
+  int64_t off = 0;
+  L.dSc = p + off;
+  off += align256(B * T * C * es);
+  L.Rs = p + off;
+  off += align256(B * NT * M * ldd * es);
+  L.Fv = reinterpret_cast<float*>(p + off);
+  off += align256(B * T * D * 4);
+  L.dOhat = p + off;
+  off += align256(B * T * ldd * es);
+  L.auxv = p + off;
+  off += align256(B * T * D * 4);
+  L.n_score = decay_dg_partials(B * NT, C);
+  L.n_carry = carry_dot_partials(B, M, D);
+  L.n_tiles = L.n_score + L.n_carry + 2 * DOT_BLOCKS;
+  L.tiles = reinterpret_cast<float*>(p + off);
+  off += align256(L.n_tiles * 4);
+  L.bytes = off;
+  return L;
+}
+
+// dst[r][d] = lam^(a + s * (r mod C)) * src[r][d] for d < D over `rows` rows of stride ld (the row's
+// position inside its chunk is r mod C because T is a multiple of C)
+template <typename E>
+__global__ void chunk_scale_rows_kernel(const E* __restrict__ src, E* __restrict__ dst, int64_t ld, int64_t rows, int D,
+                                        int C, const float* __restrict__ g, float a, float s) {
+  pdl_enter();
+  const float gl = *g;
+  const int64_t n = rows * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / D, d = i - r * D;
+    const float f = expf(gl * (a + s * (float)(r % C)));
+    if constexpr (sizeof(E) == 4) {
+      dst[r * ld + d] = src[r * ld + d] * f;
+    } else {
+      dst[r * ld + d] = __float2bfloat16_rn(__bfloat162float(src[r * ld + d]) * f);
+    }
+  }
+}
+
+int chunk_scale_rows(const void* src, void* dst, int dt, int64_t ld, int64_t rows, int64_t D, int C, const float* g,
+                     float a, float s, cudaStream_t st) {
+  if (rows * D == 0) return ULM_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows * D, 256), 8 * 148);
+  if (dt == ULM_F32)
+    return launch_pdl(chunk_scale_rows_kernel<float>, dim3(grid), dim3(256), 0, st, static_cast<const float*>(src),
+                      static_cast<float*>(dst), ld, rows, (int)D, C, g, a, s);
+  return launch_pdl(chunk_scale_rows_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st,
+                    static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), ld, rows, (int)D, C, g,
+                    a, s);
+}
+
+// out[i] = x[i] + f[i] in x's type (the combine's residual plus the inter-chunk read)
+__global__ void add_rows_kernel(const void* __restrict__ x, int xdt, const float* __restrict__ f, void* __restrict__ out,
+                                int64_t n) {
+  pdl_enter();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (xdt == ULM_F32)
+      static_cast<float*>(out)[i] = static_cast<const float*>(x)[i] + f[i];
+    else
+      static_cast<__nv_bfloat16*>(out)[i] =
+          __float2bfloat16_rn(__bfloat162float(static_cast<const __nv_bfloat16*>(x)[i]) + f[i]);
+  }
+}
+
+// part[blockIdx.x] = sum over rows r < rows, d < D of (wa + ws * (r mod C)) * x[r][d] * y[r][d]
+// (x in its type with row stride ldx, y fp32 with row stride D); DOT_BLOCKS blocks, fixed order
+__global__ void __launch_bounds__(256)
+    weighted_dot_kernel(const void* __restrict__ x, int xdt, int64_t ldx, const float* __restrict__ y, int64_t rows,
+                        int D, int C, float wa, float ws, float* __restrict__ part) {
+  pdl_enter();
+  __shared__ float red[256];
+  float acc = 0.f;
+  const int64_t n = rows * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / D, d = i - r * D;
+    const float xv = xdt == ULM_F32 ? static_cast<const float*>(x)[r * ldx + d]
+                                    : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[r * ldx + d]);
+    acc = fmaf((wa + ws * (float)(r % C)) * xv, y[i], acc);
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    if ((int)threadIdx.x < stride) red[threadIdx.x] += red[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) part[blockIdx.x] = red[0];
+}
+
+// Forward fast read in the chunk-carry form: out = P v + lam^(i+1) q H (+ x + q wmu^T with the
+// combine's x and wmu), from the operand copies; `saved` (chunk_fwd_layout) keeps what the backward
+// reads. end_state (optional, fp32 (B, M, D)): the state after the last position,
+// sum_s lam^(T-1-s) k_s v_s^T.
+int chunk_read_fwd(const void* qop, const void* kop, const void* vop, const float* g, void* saved, void* out,
+                   int out_dtype, const void* x, const void* wmu, float* end_state, int64_t B, int64_t T, int64_t M,
+                   int64_t D, int C, int prec, cudaStream_t st) {
+  const int dt = op_dtype_of(prec);
+  const int64_t es = elem_size(dt), ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), NT = T / C;
+  ChunkFwdLayout L = chunk_fwd_layout(saved, B, T, M, D, C, prec);
+  // the carry's values: v_s lam^(C-1-j), j the position in its chunk
+  if (int rc = chunk_scale_rows(vop, L.work, dt, ldd, B * T, D, C, g, (float)(C - 1), -1.f, st)) return rc;
+  // slot 0 of every batch row: the zero state entering the first chunk
+  ULM_CUDA_TRY(cudaMemset2DAsync(L.Hs, (size_t)(NT * M * ldd * es), 0, (size_t)(M * ldd * es), (size_t)B, st));
+  {
+    // H_{n+1} = lam^C H_n + k_n^T vhat_n  (A = k as [pos][slot], B = vhat as [pos][d])
+    Operand A{kop, ldm, T * ldm, M, T, dt, true};
+    Operand Bv{L.work, ldd, T * ldd, D, T, dt, true};
+    GemmShape s{(int)B, (int)M, (int)D, (int)T, CAUSAL_NONE};
+    s.carry = CARRY_FWD;
+    s.carry_C = C;
+    s.carry_chunks = (int)NT;
+    s.carry_end = end_state ? 1 : 0;
+    GemmEpilogue e = make_epilogue(EPI_STORE, dt, L.Hs, ldd, M * ldd, g);
+    e.end_state = end_state;
+    e.end_ld = D;
+    e.end_bstride = M * D;
+    if (int rc = run_gemm(A, Bv, s, e, st)) return rc;
+  }
+  {
+    // inter-chunk read F = lam^(i+1) q H_n, batches (b, n)
+    Operand Aq{qop, ldm, C * ldm, M, C, dt, false};
+    Operand Bh{L.Hs, ldd, M * ldd, D, M, dt, true};
+    GemmShape s{(int)(B * NT), C, (int)D, (int)M, CAUSAL_NONE};
+    GemmEpilogue e = make_epilogue(EPI_ROW_DECAY, ULM_F32, L.Fi, D, C * D, g);
+    e.rd_a = 1.f;
+    e.rd_s = 1.f;
+    if (int rc = run_gemm(Aq, Bh, s, e, st)) return rc;
+  }
+  if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, L.Pc, C, g, B * NT, C, M, prec, st)) return rc;
+  // the intra read's addend in the output's type: F, plus x for the combine
+  const void* addend = L.Fi;
+  if (x) {
+    const unsigned grid = (unsigned)std::min<int64_t>(cdiv(B * T * D, 256), 8 * 148);
+    if (int rc = launch_pdl(add_rows_kernel, dim3(grid), dim3(256), 0, st, x, out_dtype, (const float*)L.Fi, L.work,
+                            B * T * D))
+      return rc;
+    addend = L.work;
+  } else if (out_dtype != ULM_F32) {
+    if (int rc = convert_rows(L.Fi, ULM_F32, D, L.work, out_dtype, D, B * T, D, st)) return rc;
+    addend = L.work;
+  }
+  // out = P v (+ q wmu^T) + addend, intra-chunk causal k range
+  Operand Ap{L.Pc, C, (int64_t)C * C, C, C, dt, false};
+  Operand Bv{vop, ldd, C * ldd, D, C, dt, true};
+  GemmShape s{(int)(B * NT), C, (int)D, C, CAUSAL_KLOWER};
+  GemmEpilogue e = make_epilogue(EPI_STORE_ADD, out_dtype, out, D, C * D, nullptr);
+  e.aux = addend;
+  e.ld_aux = D;
+  e.aux_bstride = C * D;
+  e.vec_ok = e.vec_ok && is_aligned16(addend);
+  if (wmu) {
+    Operand A2{qop, ldm, C * ldm, M, C, dt, false};
+    Operand B2{wmu, ldd, 0, D, M, dt, true};
+    s.K2 = (int)M;
+    return run_gemm2(Ap, Bv, &A2, &B2, s, e, st);
+  }
+  return run_gemm(Ap, Bv, s, e, st);
+}
+
+// Backward fast read in the chunk-carry form, for dO (doop, the operand copy of dfast or dy):
+//   dq = dS k + lam^(i+1) dO H_n^T (+ dy mw with the combine's mw)
+//   dk = dS^T q + lam^(C-j) v R_n^T,  dv = P^T dO + lam^(C-j) k R_n
+// with dS the intra-chunk score gradient and R_n = sum_{t past chunk n} lam^(t - start of chunk
+// n+1) q_t dO_t^T (the reverse carry). d/dg of the fast read in tile partials (layout in L): the
+// score epilogue's sum (t-s) P dP inside chunks, plus across chunks
+//   sum_t (i+1) dO_t . F_t  +  C lam^(C+1) sum_n <R_n, H_n>  +  sum_s (C-1-j) v_s . dv_inter_s,
+// the derivative of the lam^(i+1) read factor, of the lam^C carry and of the lam^(C-1-j) write
+// factor. dq and dk are fp32 (B,T,M); dv in dv_dtype.
+int chunk_read_bwd(const void* doop, const void* qop, const void* kop, const void* vop, const float* g,
+                   const void* saved, void* work, float* dqf, float* dk, void* dv, int dv_dtype, const void* mw,
+                   int64_t B, int64_t T, int64_t M, int64_t D, int C, int prec, cudaStream_t st, cudaStream_t side,
+                   ChunkBwdLayout* out_layout) {
+  const int dt = op_dtype_of(prec);
+  const int64_t es = elem_size(dt), ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), NT = T / C;
+  ChunkFwdLayout F = chunk_fwd_layout(const_cast<void*>(saved), B, T, M, D, C, prec);
+  ChunkBwdLayout L = chunk_bwd_layout(work, B, T, M, D, C, prec);
+  *out_layout = L;
+  ULM_CUDA_TRY(cudaMemsetAsync(L.tiles, 0, L.n_tiles * sizeof(float), st));
+  if (int rc = chunk_scale_rows(doop, L.dOhat, dt, ldd, B * T, D, C, g, 0.f, 1.f, st)) return rc;
+  ULM_CUDA_TRY(cudaMemset2DAsync(static_cast<uint8_t*>(L.Rs) + (NT - 1) * M * ldd * es, (size_t)(NT * M * ldd * es), 0,
+                                 (size_t)(M * ldd * es), (size_t)B, st));
+  float* t_score = L.tiles;
+  float* t_carry = t_score + L.n_score;
+  float* t_readA = t_carry + L.n_carry;
+  float* t_writeC = t_readA + DOT_BLOCKS;
+  const unsigned dgrid = DOT_BLOCKS;
+  if (int rc = stream_after(side, st)) return rc;
+  // ---- side stream: reverse carry and the inter-chunk dk / dv ----
+  {
+    // R_{n-1} = lam^C R_n + q_n^T dOhat_n for n = NT-1 .. 1, with C lam^(C+1) <R_n, H_n> summed
+    Operand A{qop, ldm, T * ldm, M, T, dt, true};
+    Operand Bo{L.dOhat, ldd, T * ldd, D, T, dt, true};
+    GemmShape s{(int)B, (int)M, (int)D, (int)T, CAUSAL_NONE};
+    s.carry = CARRY_REV;
+    s.carry_C = C;
+    s.carry_chunks = (int)NT;
+    GemmEpilogue e = make_epilogue(EPI_STORE, dt, L.Rs, ldd, M * ldd, g);
+    e.aux = F.Hs;
+    e.ld_aux = ldd;
+    e.aux_bstride = M * ldd;
+    e.tile_partial = t_carry;
+    e.aux_dot_scale = (float)C;
+    e.aux_dot_pow = (float)(C + 1);
+    e.vec_ok = e.vec_ok && is_aligned16(F.Hs);
+    if (int rc = run_gemm(A, Bo, s, e, side)) return rc;
+  }
+  {
+    // dv_inter = lam^(C-j) k_n R_n  (B = R_n read as [slot][d]: MN-major over d)
+    Operand Ak{kop, ldm, C * ldm, M, C, dt, false};
+    Operand Br{L.Rs, ldd, M * ldd, D, M, dt, true};
+    GemmShape s{(int)(B * NT), C, (int)D, (int)M, CAUSAL_NONE};
+    GemmEpilogue e = make_epilogue(EPI_ROW_DECAY, ULM_F32, L.Fv, D, C * D, g);
+    e.rd_a = (float)C;
+    e.rd_s = -1.f;
+    if (int rc = run_gemm(Ak, Br, s, e, side)) return rc;
+  }
+  {
+    // dk_inter = lam^(C-j) v_n R_n^T  (B = R_n as [slot][d]: K-major)
+    Operand Av{vop, ldd, C * ldd, D, C, dt, false};
+    Operand Br{L.Rs, ldd, M * ldd, D, M, dt, false};
+    GemmShape s{(int)(B * NT), C, (int)M, (int)D, CAUSAL_NONE};
+    GemmEpilogue e = make_epilogue(EPI_ROW_DECAY, ULM_F32, dk, M, C * M, g);
+    e.rd_a = (float)C;
+    e.rd_s = -1.f;
+    if (int rc = run_gemm(Av, Br, s, e, side)) return rc;
+  }
+  // sum_s (C-1-j) v_s . dv_inter_s
+  if (int rc = launch_pdl(weighted_dot_kernel, dim3(dgrid), dim3(256), 0, side, vop, dt, ldd, (const float*)L.Fv,
+                          B * T, (int)D, C, (float)(C - 1), -1.f, t_writeC))
+    return rc;
+  // the intra dv product's addend in dv's type
+  const void* addv = L.Fv;
+  if (dv_dtype != ULM_F32) {
+    if (int rc = convert_rows(L.Fv, ULM_F32, D, L.auxv, dv_dtype, D, B * T, D, side)) return rc;
+    addv = L.auxv;
+  }
+  // ---- main stream: intra score gradient, then dq ----
+  {
+    Operand A{doop, ldd, C * ldd, D, C, dt, false};
+    Operand Bo{vop, ldd, C * ldd, D, C, dt, false};
+    GemmShape s{(int)(B * NT), C, C, (int)D, CAUSAL_NLOWER};
+    GemmEpilogue e = make_epilogue(EPI_DECAY_DG, dt, L.dSc, C, (int64_t)C * C, g);
+    e.aux = F.Pc;
+    e.ld_aux = C;
+    e.aux_bstride = (int64_t)C * C;
+    e.tile_partial = t_score;
+    e.vec_ok = e.vec_ok && is_aligned16(F.Pc);
+    if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
+  }
+  if (int rc = stream_after(side, st)) return rc;  // the side stream's intra products need dS
+  {
+    // dq_inter = lam^(i+1) dO_n H_n^T  (B = H_n as [slot][d]: K-major)
+    Operand Ad{doop, ldd, C * ldd, D, C, dt, false};
+    Operand Bh{F.Hs, ldd, M * ldd, D, M, dt, false};
+    GemmShape s{(int)(B * NT), C, (int)M, (int)D, CAUSAL_NONE};
+    GemmEpilogue e = make_epilogue(EPI_ROW_DECAY, ULM_F32, dqf, M, C * M, g);
+    e.rd_a = 1.f;
+    e.rd_s = 1.f;
+    if (int rc = run_gemm(Ad, Bh, s, e, st)) return rc;
+  }
+  // sum_t (i+1) dO_t . F_t
+  if (int rc = launch_pdl(weighted_dot_kernel, dim3(dgrid), dim3(256), 0, st, doop, dt, ldd, (const float*)F.Fi,
+                          B * T, (int)D, C, 1.f, 1.f, t_readA))
+    return rc;
+  {
+    // dq = dS k (+ dy mw) + dq_inter, in place
+    Operand A{L.dSc, C, (int64_t)C * C, C, C, dt, false};
+    Operand Bk{kop, ldm, C * ldm, M, C, dt, true};
+    GemmShape s{(int)(B * NT), C, (int)M, C, CAUSAL_KLOWER};
+    GemmEpilogue e = make_epilogue(EPI_STORE_ADD, ULM_F32, dqf, M, C * M, nullptr);
+    e.aux = dqf;
+    e.ld_aux = M;
+    e.aux_bstride = C * M;
+    if (mw) {
+      Operand A2{doop, ldd, C * ldd, D, C, dt, false};
+      Operand B2{mw, ldm, 0, M, D, dt, true};
+      s.K2 = (int)D;
+      if (int rc = run_gemm2(A, Bk, &A2, &B2, s, e, st)) return rc;
+    } else if (int rc = run_gemm(A, Bk, s, e, st)) {
+      return rc;
+    }
+  }
+  {
+    // side: dk = dS^T q + dk_inter, in place
+    Operand A{L.dSc, C, (int64_t)C * C, C, C, dt, true};
+    Operand Bq{qop, ldm, C * ldm, M, C, dt, true};
+    GemmShape s{(int)(B * NT), C, (int)M, C, CAUSAL_KUPPER};
+    GemmEpilogue e = make_epilogue(EPI_STORE_ADD, ULM_F32, dk, M, C * M, nullptr);
+    e.aux = dk;
+    e.ld_aux = M;
+    e.aux_bstride = C * M;
+    if (int rc = run_gemm(A, Bq, s, e, side)) return rc;
+  }
+  {
+    // side: dv = P^T dO + dv_inter
+    Operand A{F.Pc, C, (int64_t)C * C, C, C, dt, true};
+    Operand Bo{doop, ldd, C * ldd, D, C, dt, true};
+    GemmShape s{(int)(B * NT), C, (int)D, C, CAUSAL_KUPPER};
+    GemmEpilogue e = make_epilogue(EPI_STORE_ADD, dv_dtype, dv, D, C * D, nullptr);
+    e.aux = addv;
+    e.ld_aux = D;
+    e.aux_bstride = C * D;
+    e.vec_ok = e.vec_ok && is_aligned16(addv);
+    if (int rc = run_gemm(A, Bo, s, e, side)) return rc;
+  }
+  return stream_after(st, side);  // join
+}
+
+}  // namespace
+}  // namespace ulm
+
+extern "C" int ulm_set_chunk_mode(int mode) {
+  if (mode < -1 || (mode > 0 && (mode % 64 != 0 || mode > 4096))) return -2;
+  const int old = g_chunk_mode;
+  g_chunk_mode = mode;
+  return old;
+}
+
+extern "C" int ulm_memory_chunk_len(int64_t T, int64_t M, int64_t D, int prec) {
+  if (T < 0 || M < 0 || D < 0 || (prec != ULM_PREC_BF16 && prec != ULM_PREC_FP32)) return -1;
+  return chunk_len(T, M, D, prec);
+}
+
+extern "C" int64_t ulm_memory_saved_bytes(int64_t B, int64_t T, int64_t M, int64_t D, int prec) {
+  if (B < 0 || T < 0 || M < 0 || D < 0 || (prec != ULM_PREC_BF16 && prec != ULM_PREC_FP32)) return -1;
+  const int C = chunk_len(T, M, D, prec);
+  const int64_t es = prec == ULM_PREC_FP32 ? 4 : 2;
+  if (!C) return B * T * ulm_operand_ld(T) * es;
+  return chunk_fwd_layout(nullptr, B, T, M, D, C, prec).bytes;
+}
+
+extern "C" int64_t ulm_memory_bwd_work_bytes(int64_t B, int64_t T, int64_t M, int64_t D, int prec) {
+  if (B < 0 || T < 0 || M < 0 || D < 0 || (prec != ULM_PREC_BF16 && prec != ULM_PREC_FP32)) return -1;
+  const int C = chunk_len(T, M, D, prec);
+  const int64_t es = prec == ULM_PREC_FP32 ? 4 : 2;
+  if (!C) return B * T * ulm_operand_ld(T) * es;
+  return chunk_bwd_layout(nullptr, B, T, M, D, C, prec).bytes;
+}
+
 extern "C" int ulm_memory_fwd(const float* r, const float* den, const void* v, int v_dtype, const float* g,
                               const float* w, float* q,
                               void* fast, float* c, void* qop, void* kop, void* vop, void* P, int64_t B, int64_t T,
@@ -377,6 +785,8 @@ extern "C" int ulm_memory_fwd(const float* r, const float* den, const void* v, i
   if (D == 0) return ULM_OK;
   ULM_REQUIRE(v && fast && vop && P, "null pointer argument");
   if (int rc = convert_rows(v, v_dtype, D, vop, dt, ldd, B * T, D, st)) return rc;
+  if (const int C = chunk_len(T, M, D, prec))
+    return chunk_read_fwd(qop, kop, vop, g, P, fast, v_dtype, nullptr, nullptr, nullptr, B, T, M, D, C, prec, st);
   if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, P, ldt, g, B, T, M, prec, stream)) return rc;
   return ulm_causal_apply(P, ldt, vop, ldd, fast, D, v_dtype, 0, B, T, D, prec, stream);
 }
@@ -411,6 +821,19 @@ static int memory_bwd_impl(const float* dq_out, const void* dfast, int do_dtype,
     ULM_CUDA_TRY(cudaMemsetAsync(dk, 0, B * T * M * sizeof(float), st));
   } else {
     if (int rc = convert_rows(dfast, do_dtype, D, doop, dt, ldd, B * T, D, st)) return rc;
+    if (const int C = chunk_len(T, M, D, prec)) {
+      // chunk-carry form: P and dS are the saved and work buffers of that form; the gradient of
+      // the q output joins in the statistics backward
+      ULM_REQUIRE(B <= 65535 && T < (1ll << 31) && M < (1ll << 31), "extent too large");
+      cudaStream_t side = nullptr;
+      if (int rc = side_stream(&side)) return rc;
+      ChunkBwdLayout CL;
+      if (int rc = chunk_read_bwd(doop, qop, kop, vop, g, P, dS, dqf, dk, dv, do_dtype, nullptr, B, T, M, D, C, prec,
+                                  st, side, &CL))
+        return rc;
+      return stats_bwd_run(dqf, dq_out, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
+                           CL.tiles, CL.n_tiles, st, red_st);
+    }
     // dS = D * (do v^T): gradient of the scores, same causal decay as the forward; its epilogue
     // also sums (t-s) P dP per tile, the fast read's share of d/dg
     StatsScratch sc = carve_stats_scratch(partial, B, M);
@@ -515,6 +938,8 @@ extern "C" int ulm_memory_combine_fwd(const float* r, const float* den, const vo
   combine_weight_t_kernel<<<dim3((unsigned)cdiv(M, 32), (unsigned)cdiv(D, 32)), 256, 0, st>>>(mu, w, wmu, dt, ldd,
                                                                                             (int)D, (int)M);
   ULM_LAUNCH_CHECK("combine_weight_t_kernel");
+  if (const int C = chunk_len(T, M, D, prec))
+    return chunk_read_fwd(qop, kop, vop, g, P, y, x_dtype, x, wmu, nullptr, B, T, M, D, C, prec, st);
   if (int rc = ulm_decayed_scores(qop, ldm, kop, ldm, P, ldt, g, B, T, M, prec, stream)) return rc;
   // y = x + P v (causal k range) + q (w mu)^T (all M) in one accumulator
   Operand A{P, ldt, T * ldt, T, T, dt, false};
@@ -555,6 +980,44 @@ static int combine_bwd_impl(const void* dy, int dy_dtype, const float* r, const 
   const int64_t ldm = ulm_operand_ld(M), ldd = ulm_operand_ld(D), ldt = ulm_operand_ld(T);
   // dfast = dy: its operand copy is the A operand of the score gradient, of dv and of d(q w)
   if (int rc = convert_rows(dy, dy_dtype, D, doop, dt, ldd, B * T, D, st)) return rc;
+  float* dw_part = gpart + 8 * D * M;
+  const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
+  // G = dy^T q over all B*T rows (split K), then dmu = G w and the combine's share of dw,
+  // sum_d mu G (partials, added to dw after the statistics backward)
+  auto combine_grads = [&](cudaStream_t on) -> int {
+    const int64_t rows = B * T;
+    const int S = fill_split(rows, D, M);
+    Operand A{doop, ldd, 0, D, rows, dt, true};
+    Operand Bq{qop, ldm, 0, M, rows, dt, true};
+    GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
+    s.ksplit = S;
+    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
+    if (int rc = run_gemm(A, Bq, s, e, on)) return rc;
+    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, on>>>(gpart, S, mu, w, dmu, dw_part,
+                                                                                (int)D, (int)M);
+    ULM_LAUNCH_CHECK("combine_grad_kernel");
+    return ULM_OK;
+  };
+  if (const int C = chunk_len(T, M, D, prec)) {
+    // chunk-carry form (P and dS are its saved and work buffers)
+    cudaStream_t side = nullptr;
+    if (int rc = side_stream(&side)) return rc;
+    combine_weight_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 8 * 148), 256, 0, st>>>(mu, w, mw, dt, ldm,
+                                                                                               (int)D, (int)M);
+    ULM_LAUNCH_CHECK("combine_weight_kernel");
+    if (int rc = stream_after(side, st)) return rc;
+    if (int rc = combine_grads(side)) return rc;
+    ChunkBwdLayout CL;
+    if (int rc = chunk_read_bwd(doop, qop, kop, vop, g, P, dS, dqf, dk, dv, dv_dtype, mw, B, T, M, D, C, prec, st,
+                                side, &CL))
+      return rc;  // joins the side stream
+    if (int rc = stats_bwd_run(dqf, nullptr, dk, c ? q : nullptr, c, r, den, w, g, dr, dw, dg, partial, B, T, M, 0,
+                               CL.tiles, CL.n_tiles, st, red_st))
+      return rc;
+    add_parts_kernel<<<(unsigned)cdiv(M, 256), 256, 0, red_st ? red_st : st>>>(dw_part, (int)row_blocks, M, dw);
+    ULM_LAUNCH_CHECK("add_parts_kernel");
+    return ULM_OK;
+  }
   StatsScratch sc = carve_stats_scratch(partial, B, M);
   const int64_t n_tiles = decay_dg_partials(B, T);
   ULM_CUDA_TRY(cudaMemsetAsync(sc.tiles, 0, n_tiles * sizeof(float), st));
@@ -575,23 +1038,7 @@ static int combine_bwd_impl(const void* dy, int dy_dtype, const float* r, const 
     if (int rc = run_gemm(A, Bo, s, e, st)) return rc;
   }
   if (int rc = ulm_causal_apply(P, ldt, doop, ldd, dv, D, dv_dtype, 1, B, T, D, prec, side)) return rc;
-  float* dw_part = gpart + 8 * D * M;
-  const unsigned row_blocks = (unsigned)cdiv(D, COMBINE_ROWS);
-  {
-    // G = dy^T q over all B*T rows (split K), then dmu = G w and the combine's share of dw,
-    // sum_d mu G (partials, added to dw after the statistics backward)
-    const int64_t rows = B * T;
-    const int S = fill_split(rows, D, M);
-    Operand A{doop, ldd, 0, D, rows, dt, true};
-    Operand Bq{qop, ldm, 0, M, rows, dt, true};
-    GemmShape s{S, (int)D, (int)M, (int)rows, CAUSAL_NONE};
-    s.ksplit = S;
-    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, gpart, M, D * M, nullptr);
-    if (int rc = run_gemm(A, Bq, s, e, side)) return rc;
-    combine_grad_kernel<<<dim3((unsigned)cdiv(M, 32), row_blocks), 256, 0, side>>>(gpart, S, mu, w, dmu, dw_part,
-                                                                                  (int)D, (int)M);
-    ULM_LAUNCH_CHECK("combine_grad_kernel");
-  }
+  if (int rc = combine_grads(side)) return rc;
   if (int rc = stream_after(side, st)) return rc;  // dS is ready for dk
   combine_weight_kernel<<<(unsigned)std::min<int64_t>(cdiv(D * M, 256), 8 * 148), 256, 0, st>>>(mu, w, mw, dt, ldm,
                                                                                              (int)D, (int)M);

@@ -6,3 +6,4 @@
 #include "decode.cu"
 #include "address.cu"
 #include "head.cu"
+#include "norm.cu"

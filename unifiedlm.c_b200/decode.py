@@ -22,6 +22,12 @@ import torch
 from . import _lib as L
 
 
+def rmsnorm_rows(x, weight, eps):
+    """RMSNorm of the residual stream rows in fp32, as the decode step applies it:
+    weight * (x / sqrt(mean(x^2) + eps))."""
+    return weight * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
 class BatchedDecoder:
     def __init__(self, params, batch, precision="fp32", device="cuda", norm_eps=1e-5, use_graph=True,
                  temperature=0.0, topp=0.9, seed=0):
@@ -65,6 +71,7 @@ class BatchedDecoder:
                            w=f32(torch.exp(torch.clamp(p("log_w").double(), -7.0, 12.0))),
                            lam=f32(torch.exp(-torch.exp(p("log_rate").double())).reshape(1)),
                            eps=f32(torch.exp(torch.clamp(p("log_eps").double(), -10.0, 10.0)).reshape(1)))
+            lay["g"] = torch.log(lay["lam"]).reshape(())  # log decay, for the parallel prefill's products
             lay["prior"] = torch.empty(D, M, device=self.dev, dtype=self.wdt)
             lay["U"] = torch.empty(B, D, M, device=self.dev)
             lay["c"] = torch.empty(B, M, device=self.dev)
@@ -199,6 +206,44 @@ class BatchedDecoder:
             nt = self.step_sample()
             out.append(nt.clone())
         return torch.stack(out, 1).long().cpu()
+
+    @torch.no_grad()
+    def prefill(self, prompt):
+        """Feed a whole prompt (B, P) ints in one parallel pass instead of P steps: every block runs
+        its training-form forward over the P positions (the addressing prologue, the fast memory and
+        the combine, libulm_b200.so) and its state is then set to what P token-by-token steps leave
+        (ulm_decode_prefill_block: U = w mu + sum_s lam^(P-1-s) v_s k_s^T from one carry product,
+        c, r_prev and the conv window). The last position's logits go through the decode head.
+        Returns the next tokens (greedy, int32 (B,) on the device); self.logits holds the logits."""
+        from .block import mixer_fwd_raw
+        prompt = prompt.to(self.dev)
+        B, P = prompt.shape
+        if B != self.B:
+            raise ValueError(f"prompt batch {B} != decoder batch {self.B}")
+        lib = L.lib()
+        prec = L.ULM_PREC_FP32 if self.prec == "fp32" else L.ULM_PREC_BF16
+        st = L.stream_of(self.x)
+        x = self.emb[prompt.long()].float()
+        work = torch.empty(int(lib.ulm_decode_prefill_work_bytes(B, P, self.D, prec)), device=self.dev,
+                           dtype=torch.uint8)
+        for lay in self.layers:
+            h = rmsnorm_rows(x, lay["norm"], self.norm_eps)
+            v = (h.to(self.wdt) @ lay["val_w"].t()).to(self.wdt if self.prec == "bf16" else torch.float32)
+            y, z, den, kop, vop = mixer_fwd_raw(x, h, lay["conv"][:, None, :], lay["key_w"], lay["key_b"],
+                                                lay["eps"].reshape(()), v, lay["g"], lay["w"], lay["mu"], prec)
+            with torch.cuda.device(self.dev):
+                L.check(lib.ulm_decode_prefill_block(
+                    L.ptr(kop), L.ptr(vop), L.ptr(lay["g"]), L.ptr(lay["lam"]), L.ptr(z), L.ptr(den), L.ptr(h),
+                    L.dtype_code(h.dtype), L.ptr(lay["mu"]), L.ptr(lay["w"]), L.ptr(work), L.ptr(lay["U"]),
+                    L.ptr(lay["c"]), L.ptr(lay["r_prev"]), L.ptr(lay["buf"]), B, P, self.D, self.M, self.K, prec,
+                    st))
+            x = y
+        self.x.copy_(x[:, -1])
+        with torch.cuda.device(self.dev):
+            L.check(lib.ulm_decode_head(L.ptr(self.x), L.ptr(self.final_norm), L.ptr(self.cls), L.ptr(self.emb),
+                                        self.wcode, L.ptr(self.logits), L.ptr(self.next_token),
+                                        L.ptr(self.head_work), B, self.D, self.V, self.norm_eps, st))
+        return self.next_token
 
     def state_bytes(self):
         return self.L * self.B * (self.D * self.M + 2 * self.M + self.D * max(self.K - 1, 1)) * 4

@@ -23,7 +23,8 @@ import torch
 
 from . import _lib as L
 
-CHUNK = 64  # the reference's chunk length (kernel.py:20); the products here span whole sequences
+CHUNK = 64  # the reference's chunk length (kernel.py:20); here the form and chunk length of the fast
+            # read's products follow ulm_memory_chunk_len (whole sequences up to a few thousand tokens)
 
 PRECISION = {"bf16": L.ULM_PREC_BF16, "fp32": L.ULM_PREC_FP32}
 
@@ -51,6 +52,19 @@ def operand_copy(x, opt):
     return torch.empty(B, T, operand_ld(D), device=x.device, dtype=opt)
 
 
+def saved_buffer(B, T, M, D, precision, device):
+    """The fast read's saved buffer (ulm_memory_saved_bytes): the decayed scores in the
+    whole-sequence form, the chunk-boundary states and intra-chunk scores in the chunk-carry form."""
+    n = int(L.lib().ulm_memory_saved_bytes(B, T, M, D, precision))
+    return torch.empty(n, device=device, dtype=torch.uint8)
+
+
+def bwd_work_buffer(B, T, M, D, precision, device):
+    """The operator backward's work buffer (ulm_memory_bwd_work_bytes)."""
+    n = int(L.lib().ulm_memory_bwd_work_bytes(B, T, M, D, precision))
+    return torch.empty(n, device=device, dtype=torch.uint8)
+
+
 def memory_fwd_raw(r, den, v, g, w, precision):
     """ulm_memory_fwd on fresh buffers: (q, fast, c, qop, kop, vop, P). den None: r holds the
     addresses; else r holds z and den the row denominators (r = z / den)."""
@@ -66,7 +80,7 @@ def memory_fwd_raw(r, den, v, g, w, precision):
     qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
     kop = torch.empty_like(qop)
     vop = operand_copy(v, opt)
-    P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    P = saved_buffer(B, T, M, D, precision, dev)
     with torch.cuda.device(dev):
         L.check(L.lib().ulm_memory_fwd(L.ptr(r), L.ptr(den), L.ptr(v), L.dtype_code(v.dtype), L.ptr(g), L.ptr(w),
                                        L.ptr(q), L.ptr(fast), L.ptr(c) if c.numel() else None, L.ptr(qop),
@@ -82,7 +96,8 @@ def memory_fwd_fake(r, v, precision):
     c_shape = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
     return (r.new_empty(B, T, M, dtype=torch.float32), v.new_empty(B, T, D), r.new_empty(c_shape, dtype=torch.float32),
             r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
-            r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
+            r.new_empty(B, T, operand_ld(D), dtype=opt),
+            r.new_empty(int(L.lib().ulm_memory_saved_bytes(B, T, M, D, precision)), dtype=torch.uint8))
 
 
 def memory_bwd_raw(dq_out, dfast, r, den, g, w, q, c, qop, kop, vop, P, precision):
@@ -98,7 +113,7 @@ def memory_bwd_raw(dq_out, dfast, r, den, g, w, q, c, qop, kop, vop, P, precisio
     dg = torch.empty((), device=dev, dtype=torch.float32)
     dw = torch.empty(M, device=dev, dtype=torch.float32)
     doop = operand_copy(dfast, opt)
-    dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    dS = bwd_work_buffer(B, T, M, D, precision, dev)
     dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
     dk = torch.empty_like(dqf)
     partial = torch.empty(int(L.lib().ulm_memory_stats_bwd_scratch(B, T, M)), device=dev, dtype=torch.uint8)
@@ -203,7 +218,7 @@ def combine_fwd_raw(r, den, v, g, w, mu, x, precision):
     qop = torch.empty(B, T, operand_ld(M), device=dev, dtype=opt)
     kop = torch.empty_like(qop)
     vop = operand_copy(v, opt)
-    P = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    P = saved_buffer(B, T, M, D, precision, dev)
     wmu = torch.empty(M, operand_ld(D), device=dev, dtype=opt)
     with torch.cuda.device(dev):
         L.check(lib.ulm_memory_combine_fwd(
@@ -220,7 +235,8 @@ def combine_fwd_fake(r, v, x, precision):
     keep = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
     return (x.new_empty(B, T, D), r.new_empty(keep, dtype=torch.float32), r.new_empty(keep, dtype=torch.float32),
             r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
-            r.new_empty(B, T, operand_ld(D), dtype=opt), r.new_empty(B, T, operand_ld(T), dtype=opt))
+            r.new_empty(B, T, operand_ld(D), dtype=opt),
+            r.new_empty(int(L.lib().ulm_memory_saved_bytes(B, T, M, D, precision)), dtype=torch.uint8))
 
 
 def combine_bwd_raw(dy, r, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, precision):
@@ -237,7 +253,7 @@ def combine_bwd_raw(dy, r, den, g, w, mu, q, c, qop, kop, vop, P, v_dtype, preci
     dw = torch.empty(M, device=dev, dtype=torch.float32)
     dmu = torch.empty(D, M, device=dev, dtype=torch.float32)
     doop = operand_copy(dy, opt)
-    dS = torch.empty(B, T, operand_ld(T), device=dev, dtype=opt)
+    dS = bwd_work_buffer(B, T, M, D, precision, dev)
     mw = torch.empty(D, operand_ld(M), device=dev, dtype=opt)
     dqf = torch.empty(B, T, M, device=dev, dtype=torch.float32)
     dk = torch.empty_like(dqf)
