@@ -192,7 +192,7 @@ def run_reference(args, rank):
 # dram__bytes_write.sum per launch)
 PRODUCTS_DRAM_BYTES = 801400000
 
-DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), steps=24, warmup=3)
+DECODE = dict(D=768, L=12, M=2048, V=32000, batches=(1, 16, 64, 256), prompt=1024, steps=256, warmup=3)
 
 
 def decode_params(D, L, M, V, device, seed=0):
@@ -216,40 +216,54 @@ def decode_params(D, L, M, V, device, seed=0):
 
 
 def bench_decode(dev, pk):
-    """Greedy batched decode tokens/s at the 110M shape (bf16 weights, fp32 state), per batch size.
-    The state is constant in context length, so steps after a one-token prompt cost what steps after
-    a 1024-token prompt cost."""
+    """batched greedy decode at the 110M shape, per batch size and weight
+    precision: a 1024-token prompt fed in one parallel pass (BatchedDecoder.prefill: the blocks'
+    training-form forward, then each block's state from one carry product), then 256 greedy steps
+    (one CUDA graph per step). bf16 weights with fp32 state, and the fp32 mode (run.c's arithmetic).
+    CUDA events around the prefill and around the steps."""
     from unifiedlm_c_b200.decode import BatchedDecoder
     C = DECODE
     params = decode_params(C["D"], C["L"], C["M"], C["V"], dev)
+    gen = torch.Generator(device=dev).manual_seed(5)
     out = {}
-    for B in C["batches"]:
-        dec = BatchedDecoder(params, batch=B, precision="bf16", device=dev)
-        dec.prepare_graph()
-        dec.feed(torch.ones(B, dtype=torch.int32, device=dev))
-        for _ in range(C["warmup"]):
-            dec.step_greedy()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(C["steps"]):
-            dec.step_greedy()
-        e1.record()
-        torch.cuda.synchronize()
-        secs = e0.elapsed_time(e1) / 1e3 / C["steps"]
-        state_bytes = 8 * C["D"] * C["M"] * C["L"] * B  # U read + write, fp32
-        out[B] = {"tokens_per_s": round(B / secs, 1), "ms_per_step": round(secs * 1e3, 4),
-                  "state_gbs": round(state_bytes / secs / 1e9, 1)}
-        del dec
-        torch.cuda.empty_cache()
-    top = out[max(C["batches"])]
+    for prec in ("bf16", "fp32"):
+        rows = {}
+        for B in C["batches"]:
+            dec = BatchedDecoder(params, batch=B, precision=prec, device=dev)
+            dec.prepare_graph()
+            prompt = torch.randint(0, C["V"], (B, C["prompt"]), device=dev, generator=gen)
+            prompt[:, 0] = 1
+            dec.prefill(prompt)  # warm-up (first-call set-up)
+            for _ in range(C["warmup"]):
+                dec.step_greedy()
+            dec.reset()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            torch.cuda.synchronize()
+            ev[0].record()
+            dec.prefill(prompt)
+            ev[1].record()
+            for _ in range(C["steps"]):
+                dec.step_greedy()
+            ev[2].record()
+            torch.cuda.synchronize()
+            t_pre = ev[0].elapsed_time(ev[1]) / 1e3
+            t_step = ev[1].elapsed_time(ev[2]) / 1e3 / C["steps"]
+            state_bytes = 8 * C["D"] * C["M"] * C["L"] * B  # U read + write, fp32
+            rows[B] = {"tokens_per_s": round(B / t_step, 1), "ms_per_step": round(t_step * 1e3, 4),
+                       "state_gbs": round(state_bytes / t_step / 1e9, 1),
+                       "prefill_ms": round(t_pre * 1e3, 3), "prefill_tokens_per_s": round(B * C["prompt"] / t_pre, 1)}
+            del dec
+            torch.cuda.empty_cache()
+        out[prec] = rows
+    top = out["bf16"][max(C["batches"])]
     return {"metric": "batched greedy decode tokens/s (110M shape)", "value": top["tokens_per_s"],
             "unit": "tokens/s", "batch": max(C["batches"]), "precision": "bf16 weights, fp32 state",
+            "workload": f"{C['prompt']}-token prompt (parallel prefill), then {C['steps']} greedy steps per sequence",
             "roofline": {"bound": "hbm", "achieved": top["state_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(top["state_gbs"] / pk["hbm_gbs"], 4),
                          "bytes": "8*D*M*L*B per step (fp32 state read + write)",
                          "kernel": "decode_state_kernel (plus per-step GEMMs and head)"},
-            "by_batch": out}
+            "by_batch": out["bf16"], "fp32_mode_by_batch": out["fp32"]}
 
 
 def bench_mixer(dev, W, blocks, precision, steps=5, warmup=3):
@@ -347,6 +361,166 @@ def bench_head(dev, W, steps=5, warmup=3):
             "speedup": round(out["fused"]["tokens_per_s"] / out["torch_autocast"]["tokens_per_s"], 3)}
 
 
+def zipf_tokens(B, T, V, seed):
+    """Zipf(s=1.1) ranks rejected to < V, rank -> id, BOS=1 first in every row (4)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    out = np.empty((B, T), dtype=np.int64)
+    for b in range(B):
+        row = []
+        while len(row) < T - 1:
+            draw = rng.zipf(1.1, size=4 * T)
+            row.extend(int(x) - 1 for x in draw if x <= V)
+        out[b, 0] = 1
+        out[b, 1:] = row[:T - 1]
+    return torch.from_numpy(out)
+
+
+MODELS = {
+    "c4": dict(dim=768, n_layers=12, hidden_dim=2048, vocab_size=32000, max_seq_len=1024, batch=16),
+    "c2": dict(dim=288, n_layers=6, hidden_dim=768, vocab_size=32000, max_seq_len=256, batch=64),
+}
+
+
+def bench_model(dev, name, steps, warmup, world, rank, bucket_mb=25):
+    """One UnifiedLM training step per iteration at a BASELINE model config (c4: 110M, 16 x 1024
+    tokens per GPU; c2: 15M, 64 x 256): token ids copied from pinned host memory, forward with the
+    fused head, backward, the mean of every parameter gradient over ranks (DDP: bucketed NCCL
+    all-reduces overlapping the backward), fused AdamW, and the loss read back to the host. bf16
+    tensor-core products, fp32 parameters and statistics. Synthetic Zipf(1.1) token ids with BOS=1;
+    random init with prior 4 and lam 0.95 (the same seed on every rank). Device time over the K steps
+    (CUDA events), max over ranks."""
+    import math
+    from unifiedlm_c_b200.model import ModelArgs, UnifiedLM
+    cfg = dict(MODELS[name])
+    B = cfg.pop("batch")
+    torch.manual_seed(1234)
+    model = UnifiedLM(ModelArgs(**cfg))
+    with torch.no_grad():
+        for layer in model.layers:
+            layer.log_rate.fill_(math.log(-math.log(0.95)))
+    model = model.to(dev).train()
+    model.fused_head = True
+    model.set_precision("bf16")
+    params = [p for p in model.parameters()]
+    n_params = sum(p.numel() for p in params)
+    opt = model.configure_optimizers(0.1, 6e-4, (0.9, 0.95), "cuda")
+    net = model
+    if world > 1:
+        # the reference's data parallelism (train.py:182-183): DDP's gradient buckets, each
+        # all-reduced over NCCL as soon as the backward has produced it, overlapping the rest of the
+        # backward; the buckets are the gradients' own storage (no packing copies)
+        from torch.nn.parallel import DistributedDataParallel
+        net = DistributedDataParallel(model, device_ids=[dev.index], gradient_as_bucket_view=True,
+                                      bucket_cap_mb=bucket_mb)
+    T = cfg["max_seq_len"]
+    host = [zipf_tokens(B, T + 1, cfg["vocab_size"], seed=1000 * rank + i).pin_memory() for i in range(4)]
+    dtok = torch.empty(B, T + 1, dtype=torch.int64, device=dev)
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def step(i):
+        dtok.copy_(host[i % len(host)], non_blocking=True)
+        net(dtok[:, :-1], dtok[:, 1:])
+        model.last_loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        loss_host.copy_(model.last_loss.detach(), non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    secs = torch.tensor(e0.elapsed_time(e1) / 1e3, device=dev)
+    if world > 1:
+        dist.all_reduce(secs, op=dist.ReduceOp.MAX)
+    secs = float(secs)
+    out = {"metric": f"UnifiedLM training step tokens/s ({name}: dim {cfg['dim']}, {cfg['n_layers']} layers, "
+                     f"M {cfg['hidden_dim']}, V {cfg['vocab_size']}, {B} x {T} per GPU)",
+           "value": round(world * B * T * steps / secs, 1), "unit": "tokens/s", "n_gpus": world,
+           "ms_per_step": round(secs / steps * 1e3, 3), "steps": steps, "warmup": warmup,
+           "params": n_params, "grad_allreduce_bytes": 4 * n_params if world > 1 else 0,
+           "h2d_bytes_per_step": B * (T + 1) * 8, "d2h_bytes_per_step": 4,
+           "loss": round(float(loss_host), 4),
+           "step": "token ids H2D from pinned memory, forward (fused head), backward with DDP's bucketed NCCL "
+                   "all-reduce of all fp32 gradients overlapping it (N>1), fused AdamW, loss D2H; device time "
+                   "(CUDA events), max over ranks",
+           "ddp_bucket_mb": bucket_mb if world > 1 else None}
+    del model, opt, net
+    torch.cuda.empty_cache()
+    return out
+
+
+def bench_config3(dev, reps=5, warmup=2):
+    """the fast-memory operator at D 512, M 1024, B 32, T in {512, 1024, 2048},
+    lam in {0.9, 0.99, 0.999}, bf16 products with fp32 statistics, forward and backward timed
+    separately (CUDA events, mean of `reps` launches after `warmup`). Addresses r are relu²-normalised
+    from a Gaussian K u + b with eps 1; v bf16. The automatic choice is the whole-sequence form up to
+    T = 2048; both forms are also timed at T = 2048 and at T = 8192, where the chunk-carry form wins."""
+    import math
+    import unifiedlm_c_b200._lib as L_
+    from unifiedlm_c_b200.kernel import PRECISION, memory_bwd_raw, memory_fwd_raw, operand_or_input
+    B, D, M = 32, 512, 1024  # BASELINE config 3 (T = 8192 extends it with 8 rows, same tokens per call)
+    prec = PRECISION["bf16"]
+    lib = L_.lib()
+    gen = torch.Generator(device=dev).manual_seed(3)
+    Kw = torch.randn(M, D, device=dev, generator=gen) / math.sqrt(D)
+    bias = torch.randn(M, device=dev, generator=gen) * 0.5
+    w = torch.full((M,), 4.0, device=dev)
+    out = []
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    # (T, batch rows, lam values, chunk modes): the sweep in the automatic form choice, then both
+    # forms at T = 2048 and at T = 8192 (same tokens per call) where the chunk-carry form takes over
+    cases = [(T, B, (0.9, 0.99, 0.999), [-1]) for T in (512, 1024, 2048)]
+    cases += [(2048, B, (0.99,), [1024]), (8192, 8, (0.99,), [-1, 0])]
+    for T, Bc, lams, modes_T in cases:
+        u = torch.randn(Bc, T, D, device=dev, generator=gen)
+        z = torch.relu(u @ Kw.t() + bias).square()
+        r = z / (1.0 + z.sum(-1, keepdim=True))
+        del u, z
+        v = torch.randn(Bc, T, D, device=dev, generator=gen).to(torch.bfloat16)
+        dq = torch.randn(Bc, T, M, device=dev, generator=gen) * 1e-3
+        df = (torch.randn(Bc, T, D, device=dev, generator=gen) * 1e-3).to(torch.bfloat16)
+        for lam in lams:
+            g = torch.tensor(math.log(lam), device=dev)
+            for mode in modes_T:
+                lib.ulm_set_chunk_mode(mode)
+                C = int(lib.ulm_memory_chunk_len(T, M, D, prec))
+                saved = memory_fwd_raw(r, None, v, g, w, prec)
+                q, fast, c, qop, kop, vop, P = saved
+                vop = operand_or_input(vop, v)
+                t_f = timed(lambda: memory_fwd_raw(r, None, v, g, w, prec))
+                t_b = timed(lambda: memory_bwd_raw(dq, df, r, None, g, w, q, c, qop, kop, vop, P, prec))
+                out.append({"T": T, "B": Bc, "lam": lam, "form": f"chunk {C}" if C else "whole sequence",
+                            "choice": "automatic" if mode == -1 else "forced",
+                            "fwd_ms": round(t_f * 1e3, 3), "bwd_ms": round(t_b * 1e3, 3),
+                            "fwd_tokens_per_s": round(Bc * T / t_f, 1), "bwd_tokens_per_s": round(Bc * T / t_b, 1)})
+                del saved, q, fast, c, qop, kop, vop, P
+        lib.ulm_set_chunk_mode(-1)
+        del r, v, dq, df
+        torch.cuda.empty_cache()
+    return {"metric": "fast-memory operator fwd / bwd tokens/s (42M op sweep, D 512, M 1024, B 32)",
+            "unit": "tokens/s", "precision": "bf16 products, fp32 statistics", "sweep": out}
+
+
 def runc_decode_baseline(steps=32):
     """The reference's own C decoder (run.c, built with its runomp flags into oracle/_ref/run_omp),
     greedy, at the 110M shape with seeded random weights, all host cores. Returns tokens/s or None."""
@@ -429,6 +603,12 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the batched-decode measurement")
     ap.add_argument("--no-mixer", action="store_true", help="skip the fused-combine measurement")
     ap.add_argument("--no-head", action="store_true", help="skip the fused LM-head measurement")
+    ap.add_argument("--no-model", action="store_true", help="skip the UnifiedLM training-step measurements (c4, c2)")
+    ap.add_argument("--no-config3", action="store_true", help="skip the config-3 operator sweep")
+    ap.add_argument("--model-steps", type=int, default=5, help="timed UnifiedLM training steps (after 3 warm-up)")
+    ap.add_argument("--nccl-max-ctas", type=int, default=0,
+                    help="with N>1 ranks: at most this many CTAs per NCCL collective (0: NCCL's choice)")
+    ap.add_argument("--ddp-bucket-mb", type=int, default=25, help="DDP gradient bucket size of the model steps")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one warm-up step and one step, no timing or report (for ncu launch lists)")
     ap.add_argument("--profile-block", action="store_true",
@@ -436,6 +616,11 @@ def main():
                          "of single kernels on a small case)")
     ap.add_argument("--profile-decode", action="store_true",
                     help="run a few batch-16 decode steps at the 110M shape, no report (for ncu)")
+    ap.add_argument("--profile-model", action="store_true",
+                    help="run two UnifiedLM training steps at config 4 (110M), no report (for ncu launch lists)")
+    ap.add_argument("--profile-chunk", action="store_true",
+                    help="run the config-3 operator at T=2048 (chunk-carry form), B=8, fwd + bwd twice, no report "
+                         "(for ncu captures of the carry products)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -464,9 +649,34 @@ def main():
             dec.step_greedy()
         torch.cuda.synchronize()
         return
+    if args.profile_model:
+        bench_model(dev, "c4", 1, 1, 1, 0)
+        return
+    if args.profile_chunk:
+        import math
+        from unifiedlm_c_b200.kernel import unified_memory
+        B, T, D, M = 8, 2048, 512, 1024
+        gen = torch.Generator(device=dev).manual_seed(3)
+        z = torch.relu(torch.randn(B, T, M, device=dev, generator=gen)).square()
+        r = (z / (1.0 + z.sum(-1, keepdim=True))).requires_grad_(True)
+        v = torch.randn(B, T, D, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(True)
+        g = torch.tensor(math.log(0.99), device=dev, requires_grad=True)
+        w = torch.full((M,), 4.0, device=dev, requires_grad=True)
+        for _ in range(2):
+            q, fast = unified_memory(r, v, g, w)
+            (q.sum() + fast.float().sum()).backward()
+        torch.cuda.synchronize()
+        return
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        opts = None
+        if args.nccl_max_ctas > 0:
+            # cap the SMs NCCL's kernels take, so a collective that overlaps the backward leaves the
+            # persistent one-CTA-per-SM kernels most of the machine
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.config.max_ctas = args.nccl_max_ctas
+            opts.config.min_ctas = min(args.nccl_max_ctas, 2)
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120), pg_options=opts)
     W = dict(WORKLOAD, L=1) if args.profile_block else WORKLOAD
     prec = PRECISION[args.precision]
     h, v, dq_out, dfast, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
@@ -661,6 +871,16 @@ def main():
                 "per_launch_ms": [round(s * 1e3, 4) for _, s in per],
                 "per_launch_tflops": [round(f / s / 1e12, 1) for f, s in per]}
 
+    models = None
+    if not args.no_model:
+        models = {name: bench_model(dev, name, args.model_steps, 3, world, rank, args.ddp_bucket_mb)
+                  for name in ("c4", "c2")}
+        if L_.device_error() != 0:
+            raise RuntimeError("a kernel reported a device-side error during the model steps")
+    config3 = None
+    if world == 1 and not args.no_config3:
+        config3 = bench_config3(dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -704,7 +924,7 @@ def main():
                               "the backward packs them on one GPU, after the all-reduce with N ranks; timed "
                               "from the first copy to the last read"},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
-            "mixer": mixer, "head": head, "decode": decode}
+            "mixer": mixer, "head": head, "decode": decode, "model_step": models, "config3": config3}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

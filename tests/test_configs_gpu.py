@@ -94,3 +94,26 @@ def test_config3_operator_sweep(T, lam):
     assert dg_rel < 3e-2 or dg_abs < 1e-4 * g_terms, (dg_rel, dg_abs, g_terms)
     assert max(errs.values()) < TOL["bf16"], errs
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("T", [512, 1024])
+def test_config3_operator_fp32(T):
+    """Config 3 in the fp32 mode (1e-5 for every output, dg included) at lam 0.99; T = 2048 in fp32
+    runs in the chunk-carry form (test_chunk_gpu.py)."""
+    B, D, M = 1, 512, 1024
+    r, v, lg, w, dq, df = config3_inputs(B, T, D, M, 0.99, seed=T + 7)
+    leaves = [t.clone().requires_grad_(True) for t in (r, v, lg, w)]
+    q_ref, f_ref = O.memory_dense(*leaves)
+    ((q_ref * dq).sum() + (f_ref * df).sum()).backward()
+    dev = [t.float().cuda().requires_grad_(True) for t in (r, v, lg, w)]
+    q, fast = unified_memory(*dev, precision="fp32")
+    ((q * dq.float().cuda()).sum() + (fast * df.float().cuda()).sum()).backward()
+    torch.cuda.synchronize()
+
+    def rel(a, b_):
+        return float((a.detach().double().cpu() - b_).norm() / b_.norm().clamp(min=1e-30))
+
+    errs = {"q": rel(q, q_ref.detach()), "fast": rel(fast, f_ref.detach())}
+    errs.update({n: rel(d.grad, lf.grad) for n, d, lf in zip(("dr", "dv", "dg", "dw"), dev, leaves)})
+    assert max(errs.values()) < TOL["fp32"], errs
+    assert L.device_error() == 0

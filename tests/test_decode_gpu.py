@@ -13,6 +13,7 @@ import tempfile
 import pytest
 import torch
 
+import unifiedlm_c_b200._lib as L
 from oracle import memory as O
 from unifiedlm_c_b200 import export
 from unifiedlm_c_b200.decode import BatchedDecoder
@@ -180,7 +181,17 @@ def test_prefill_matches_token_by_token(precision, P):
     """BatchedDecoder.prefill (the prompt in one parallel pass, the state from one carry product per
     block) against feeding the prompt token by token: the last position's logits within 1e-4 (fp32)
     or 2e-2 (bf16 products against bf16-weight steps), and in fp32 mode the greedy continuation
-    identical. P = 512 (fp32) and 1024 (bf16) run the blocks' fast read in the chunk-carry form."""
+    identical. P = 512 (fp32, chunks of 64) and 1024 (bf16, chunks of 256 set for the test) run the
+    blocks' fast read in the chunk-carry form."""
+    lib = L.lib()
+    lib.ulm_set_chunk_mode(256 if (precision, P) == ("bf16", 1024) else -1)
+    try:
+        _prefill_case(precision, P)
+    finally:
+        lib.ulm_set_chunk_mode(-1)
+
+
+def _prefill_case(precision, P):
     p = rand_params(7, 64, 3, 128, 512)
     B, steps = 3, 24
     prompt = torch.randint(0, 512, (B, P), generator=torch.Generator().manual_seed(P))
@@ -229,3 +240,26 @@ def test_model_step_and_forward_recurrent_use_the_decoder():
         yo = O.block_step(pb, x.double(), so)
         assert float((y.double().cpu() - yo).norm() / yo.norm()) < 1e-5
         x = yo.float()
+
+
+def test_live_runc_token_identity_c5_shape(tmp_path):
+    """BASELINE config 5's model shape (dim 768, M 2048, 12 blocks, vocab 32000), fp32 mode: 32
+    greedy tokens from BOS identical to the reference's run.c on the same model.bin."""
+    if not os.path.exists(RUNC):
+        pytest.skip("oracle/_ref/run not built (needs the reference checkout)")
+    steps = 32
+    mpath, tpath = str(tmp_path / "m.bin"), str(tmp_path / "tok.bin")
+    export.write_tokenizer_bin(tpath, [f"|{i}" for i in range(32000)])
+    ids = []
+    for seed in range(11, 16):  # first seed whose greedy run from BOS does not stop early at BOS
+        p = rand_params(seed, 768, 12, 2048, 32000)
+        export.write_model_bin(p, mpath, max_seq_len=steps)
+        text = subprocess.run([RUNC, mpath, "-z", tpath, "-t", "0", "-n", str(steps)], capture_output=True,
+                              text=True, check=True, timeout=300).stdout
+        ids = [int(x) for x in text.strip().split("|") if x]
+        if len(ids) >= 24:
+            break
+    assert len(ids) >= 24
+    dec = BatchedDecoder(p, batch=2, precision="fp32")
+    out = dec.generate(torch.ones(2, 1, dtype=torch.long), steps=steps)
+    assert out[0, :len(ids)].tolist() == ids and out[1, :len(ids)].tolist() == ids

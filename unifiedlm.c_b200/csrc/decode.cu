@@ -372,6 +372,7 @@ int decode_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int wdt,
   Operand A{X, ldx, B * ldx, K, B, wdt, false};
   Operand Bw{W, ldw, N * ldw, K, N, wdt, false};
   GemmShape s{1, (int)B, (int)N, (int)K, CAUSAL_NONE};
+  s.k_in_order = 1;  // fp32 weights: run.c's dot-product order
   GemmEpilogue e;
   e.kind = EPI_STORE;
   e.out_dtype = ULM_F32;

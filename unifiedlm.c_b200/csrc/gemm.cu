@@ -1370,6 +1370,13 @@ __global__ void __launch_bounds__(256)
       Bs[kk][nn] = val;
     }
     __syncthreads();
+    // two-level sum: each 16-deep slice in its own partial, then into the accumulator (the rounding
+    // error of a k-long dot product grows with k / 16 + 16 instead of k)
+    float part[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) part[i][jj] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float a[4], bv[4];
@@ -1380,8 +1387,17 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(a[i], bv[jj], acc[i][jj]);
+        for (int jj = 0; jj < 4; ++jj) {
+          if (shape.k_in_order)
+            acc[i][jj] = fmaf(a[i], bv[jj], acc[i][jj]);
+          else
+            part[i][jj] = fmaf(a[i], bv[jj], part[i][jj]);
+        }
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) acc[i][jj] += part[i][jj];
     __syncthreads();
   }
   };

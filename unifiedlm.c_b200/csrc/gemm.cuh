@@ -54,6 +54,9 @@ struct GemmShape {
   int carry_C = 0;
   int carry_chunks = 0;
   int carry_end = 0;
+  // fp32 FMA back end: 1 = one running sum over k in order (run.c's matmul order, for the decode
+  // steps' token identity); 0 = each 16-deep k slice summed apart, then added (smaller rounding)
+  int k_in_order = 0;
 };
 
 // Chunk steps a carry tile runs.

@@ -370,15 +370,26 @@ int g_chunk_mode = -1;
 
 constexpr int DOT_BLOCKS = 296;  // fixed grid of the weighted dot products (deterministic partials)
 
-// Chunk length of the operator's fast read, 0 = the whole-sequence form. Automatic: C = 256 on the
-// tensor cores (the pair tiles' 256 rows: one diagonal tile per chunk) or 64 in fp32 (the FMA back
-// end's 64-row tiles), where T is a multiple of C with at least two chunks and the chunked form's
-// flops per token 4 M D + 2 C (M + D) are fewer than the whole-sequence form's T (M + D).
+// Chunk length of the operator's fast read, 0 = the whole-sequence form. Automatic: on the tensor
+// cores the largest C in {1024, 512, 256} (multiples of the pair tiles' 256 rows) that divides T into
+// at least two chunks, in fp32 C = 64 (the FMA back end's 64-row tiles), used where the chunked
+// form's flops per token 4 M D + 2 C (M + D) are fewer than the whole-sequence form's T (M + D).
+// (Measured on B200, bf16, 65536 tokens per call: at D 512 / M 1024 the forms tie near T = 4096 and
+// the chunked form with C = 1024 is 16% faster at T = 8192; at D 768 / M 2048 likewise at 8192; at
+// T = 2048 the whole-sequence form is 1.5-2x faster. C = 1024 beat 512 and 256 at every T, since
+// fewer chunk boundaries mean fewer state writes and reads.)
 int chunk_len(int64_t T, int64_t M, int64_t D, int prec) {
   if (g_chunk_mode == 0 || M == 0 || D == 0) return 0;
-  const int64_t C = g_chunk_mode > 0 ? g_chunk_mode : (prec == ULM_PREC_FP32 ? 64 : 256);
-  if (T % C != 0 || T / C < 2) return 0;
-  if (g_chunk_mode > 0) return (int)C;
+  auto fits = [&](int64_t C) { return T % C == 0 && T / C >= 2; };
+  if (g_chunk_mode > 0) return fits(g_chunk_mode) ? g_chunk_mode : 0;
+  int64_t C = 0;
+  if (prec == ULM_PREC_FP32) {
+    C = fits(64) ? 64 : 0;
+  } else {
+    for (int64_t c : {1024, 512, 256})
+      if (!C && fits(c)) C = c;
+  }
+  if (!C) return 0;
   return (double)T * (double)(M + D) > 4.0 * (double)M * (double)D + 2.0 * (double)C * (double)(M + D) ? (int)C : 0;
 }
 
@@ -443,20 +454,25 @@ ChunkBwdLayout chunk_bwd_layout(void* base, int64_t B, int64_t T, int64_t M, int
 }
 
 // dst[r][d] = lam^(a + s * (r mod C)) * src[r][d] for d < D over `rows` rows of stride ld (the row's
-// position inside its chunk is r mod C because T is a multiple of C)
+// position inside its chunk is r mod C because T is a multiple of C); one warp per row, the factor
+// computed once per row, the columns strided over the lanes
 template <typename E>
-__global__ void chunk_scale_rows_kernel(const E* __restrict__ src, E* __restrict__ dst, int64_t ld, int64_t rows, int D,
-                                        int C, const float* __restrict__ g, float a, float s) {
+__global__ void __launch_bounds__(256)
+    chunk_scale_rows_kernel(const E* __restrict__ src, E* __restrict__ dst, int64_t ld, int64_t rows, int D, int C,
+                            const float* __restrict__ g, float a, float s) {
   pdl_enter();
   const float gl = *g;
-  const int64_t n = rows * D;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / D, d = i - r * D;
-    const float f = expf(gl * (a + s * (float)(r % C)));
-    if constexpr (sizeof(E) == 4) {
-      dst[r * ld + d] = src[r * ld + d] * f;
-    } else {
-      dst[r * ld + d] = __float2bfloat16_rn(__bfloat162float(src[r * ld + d]) * f);
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    const float f = expf(gl * (a + s * (float)(int)(r % C)));
+    const E* sr = src + r * ld;
+    E* dr = dst + r * ld;
+    for (int d = lane; d < D; d += 32) {
+      if constexpr (sizeof(E) == 4)
+        dr[d] = sr[d] * f;
+      else
+        dr[d] = __float2bfloat16_rn(__bfloat162float(sr[d]) * f);
     }
   }
 }
@@ -464,7 +480,7 @@ __global__ void chunk_scale_rows_kernel(const E* __restrict__ src, E* __restrict
 int chunk_scale_rows(const void* src, void* dst, int dt, int64_t ld, int64_t rows, int64_t D, int C, const float* g,
                      float a, float s, cudaStream_t st) {
   if (rows * D == 0) return ULM_OK;
-  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows * D, 256), 8 * 148);
+  const unsigned grid = (unsigned)std::min<int64_t>(cdiv(rows, 8), 16 * 148);
   if (dt == ULM_F32)
     return launch_pdl(chunk_scale_rows_kernel<float>, dim3(grid), dim3(256), 0, st, static_cast<const float*>(src),
                       static_cast<float*>(dst), ld, rows, (int)D, C, g, a, s);
@@ -487,27 +503,37 @@ __global__ void add_rows_kernel(const void* __restrict__ x, int xdt, const float
 }
 
 // part[blockIdx.x] = sum over rows r < rows, d < D of (wa + ws * (r mod C)) * x[r][d] * y[r][d]
-// (x in its type with row stride ldx, y fp32 with row stride D); DOT_BLOCKS blocks, fixed order
+// (x in its type with row stride ldx, y fp32 with row stride D); DOT_BLOCKS blocks of 8 warps, one
+// warp per row at a time, fixed order
 __global__ void __launch_bounds__(256)
     weighted_dot_kernel(const void* __restrict__ x, int xdt, int64_t ldx, const float* __restrict__ y, int64_t rows,
                         int D, int C, float wa, float ws, float* __restrict__ part) {
   pdl_enter();
-  __shared__ float red[256];
+  __shared__ float red[8];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   float acc = 0.f;
-  const int64_t n = rows * D;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / D, d = i - r * D;
-    const float xv = xdt == ULM_F32 ? static_cast<const float*>(x)[r * ldx + d]
-                                    : __bfloat162float(static_cast<const __nv_bfloat16*>(x)[r * ldx + d]);
-    acc = fmaf((wa + ws * (float)(r % C)) * xv, y[i], acc);
+  for (int64_t r = (int64_t)blockIdx.x * 8 + wp; r < rows; r += (int64_t)gridDim.x * 8) {
+    const float wgt = wa + ws * (float)(int)(r % C);
+    const float* yr = y + r * D;
+    float row = 0.f;
+    if (xdt == ULM_F32) {
+      const float* xr = static_cast<const float*>(x) + r * ldx;
+      for (int d = lane; d < D; d += 32) row = fmaf(xr[d], yr[d], row);
+    } else {
+      const __nv_bfloat16* xr = static_cast<const __nv_bfloat16*>(x) + r * ldx;
+      for (int d = lane; d < D; d += 32) row = fmaf(__bfloat162float(xr[d]), yr[d], row);
+    }
+    acc = fmaf(wgt, row, acc);
   }
-  red[threadIdx.x] = acc;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) red[wp] = acc;
   __syncthreads();
-  for (int stride = 128; stride > 0; stride >>= 1) {
-    if ((int)threadIdx.x < stride) red[threadIdx.x] += red[threadIdx.x + stride];
-    __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    part[blockIdx.x] = t;
   }
-  if (threadIdx.x == 0) part[blockIdx.x] = red[0];
 }
 
 // Forward fast read in the chunk-carry form: out = P v + lam^(i+1) q H (+ x + q wmu^T with the
