@@ -521,6 +521,57 @@ def bench_config3(dev, reps=5, warmup=2):
             "unit": "tokens/s", "precision": "bf16 products, fp32 statistics", "sweep": out}
 
 
+def chunk_sweep(dev, reps=4, warmup=2):
+    """fwd and bwd ms of unified_memory per form of the fast read (ulm_set_chunk_mode: 0 = the
+    whole-sequence form, C = chunks of C) at D 512 / M 1024 and D 768 / M 2048, T in {2048, 4096,
+    8192}, B = 65536 / T rows, bf16, lam 0.99; CUDA events, mean of `reps` calls after `warmup`."""
+    import math
+    import unifiedlm_c_b200._lib as L_
+    from unifiedlm_c_b200.kernel import PRECISION, memory_bwd_raw, memory_fwd_raw, operand_or_input
+    lib = L_.lib()
+    prec = PRECISION["bf16"]
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    for D, M in ((512, 1024), (768, 2048)):
+        for T in (2048, 4096, 8192):
+            B = 65536 // T
+            gen = torch.Generator(device=dev).manual_seed(1)
+            z = torch.relu(torch.randn(B, T, M, device=dev, generator=gen)).square()
+            r = z / (1.0 + z.sum(-1, keepdim=True))
+            del z
+            v = torch.randn(B, T, D, device=dev, generator=gen).to(torch.bfloat16)
+            dq = torch.randn(B, T, M, device=dev, generator=gen) * 1e-3
+            df = (torch.randn(B, T, D, device=dev, generator=gen) * 1e-3).to(torch.bfloat16)
+            g = torch.tensor(math.log(0.99), device=dev)
+            w = torch.full((M,), 4.0, device=dev)
+            res = {}
+            for mode in (0, 256, 512, 1024):
+                lib.ulm_set_chunk_mode(mode)
+                q, fast, c, qop, kop, vop, P = memory_fwd_raw(r, None, v, g, w, prec)
+                vop = operand_or_input(vop, v)
+                t_f = timed(lambda: memory_fwd_raw(r, None, v, g, w, prec))
+                t_b = timed(lambda: memory_bwd_raw(dq, df, r, None, g, w, q, c, qop, kop, vop, P, prec))
+                res["whole" if mode == 0 else f"chunk {mode}"] = {"fwd_ms": round(t_f, 3), "bwd_ms": round(t_b, 3)}
+                del q, fast, c, qop, kop, vop, P
+                torch.cuda.empty_cache()
+            lib.ulm_set_chunk_mode(-1)
+            print(json.dumps({"D": D, "M": M, "T": T, "B": B, "automatic": int(lib.ulm_memory_chunk_len(T, M, D, prec)),
+                              "ms": res}), flush=True)
+            del r, v, dq, df
+            torch.cuda.empty_cache()
+
+
 def runc_decode_baseline(steps=32):
     """The reference's own C decoder (run.c, built with its runomp flags into oracle/_ref/run_omp),
     greedy, at the 110M shape with seeded random weights, all host cores. Returns tokens/s or None."""
@@ -615,7 +666,12 @@ def main():
                     help="run one block of the step (fwd + bwd) twice, no timing or report (for ncu captures "
                          "of single kernels on a small case)")
     ap.add_argument("--profile-decode", action="store_true",
-                    help="run a few batch-16 decode steps at the 110M shape, no report (for ncu)")
+                    help="run a few decode steps at the 110M shape (batch --profile-batch), no report (for ncu)")
+    ap.add_argument("--profile-batch", type=int, default=16, help="batch of --profile-decode")
+    ap.add_argument("--chunk-sweep", action="store_true",
+                    help="time the fast read's two forms (whole sequence; chunks of 256 / 512 / 1024) fwd + bwd at the "
+                         "42M and 110M widths for T in {2048, 4096, 8192}, 65536 tokens per call; prints one JSON "
+                         "line per shape")
     ap.add_argument("--profile-model", action="store_true",
                     help="run two UnifiedLM training steps at config 4 (110M), no report (for ncu launch lists)")
     ap.add_argument("--profile-chunk", action="store_true",
@@ -641,13 +697,17 @@ def main():
     if args.profile_decode:
         from unifiedlm_c_b200.decode import BatchedDecoder
         C = DECODE
-        dec = BatchedDecoder(decode_params(C["D"], C["L"], C["M"], C["V"], dev), batch=16, precision="bf16",
+        Bp = args.profile_batch
+        dec = BatchedDecoder(decode_params(C["D"], C["L"], C["M"], C["V"], dev), batch=Bp, precision="bf16",
                              device=dev, use_graph=False)
         dec.reset()
-        dec.feed(torch.ones(16, dtype=torch.int32, device=dev))
+        dec.feed(torch.ones(Bp, dtype=torch.int32, device=dev))
         for _ in range(2):
             dec.step_greedy()
         torch.cuda.synchronize()
+        return
+    if args.chunk_sweep:
+        chunk_sweep(dev)
         return
     if args.profile_model:
         bench_model(dev, "c4", 1, 1, 1, 0)
@@ -918,6 +978,8 @@ def main():
                            l2="inputs larger than L2 (r is 134 MB), no flush"),
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "h2d_gbs_per_rank": round(h2d * e2e_steps / float(e2e_secs) / 1e9, 1),
+                    "h2d_gbs_all_ranks": round(world * h2d * e2e_steps / float(e2e_secs) / 1e9, 1),
                     "copies": "pinned host buffers; H2D of step i+1 during step i on its own stream "
                               "(double-buffered; forward inputs first, the step waits for the gradient inputs "
                               "before its backward); the gradients read back on another stream, per block as "

@@ -174,8 +174,9 @@ int ulm_set_pdl(int enable);
  * ulm_memory_chunk_len returns the chunk length the operator entry points use for (T, M, D, prec),
  * 0 for the whole-sequence form, -1 for bad arguments. Automatic choice (mode -1, default): for
  * ULM_PREC_BF16 the largest C in {1024, 512, 256} that divides T into at least two chunks, for
- * ULM_PREC_FP32 C = 64, where T (M + D) > 4 M D + 2 C (M + D) (fewer flops than the
- * whole-sequence form; on B200 the chunked form wins from about T = 4096 at the 42M and 110M widths).
+ * ULM_PREC_FP32 C = 64, where T (M + D) > 1.25 (4 M D + 2 C (M + D)) (the whole-sequence form's
+ * flops per token against the chunked form's, with a margin for the chunked form's extra passes;
+ * on B200 the chunked form wins at T = 8192 at the 42M and 110M widths, loses at T <= 4096).
  * ulm_set_chunk_mode: -1 automatic, 0 always the whole-sequence form, C > 0 (a multiple of 64, at
  * most 4096) that chunk length wherever T is a multiple of C with at least two chunks. Returns the
  * previous mode, or -2 (no change) for a bad mode. Buffers sized with ulm_memory_saved_bytes /

@@ -137,9 +137,12 @@ def _setup(ctx, inputs, output):
     ctx.v_dim = v.shape[-1]
     ctx.g_shape = g.shape
     ctx.mark_non_differentiable(z, den, u_op, kw, c, qop, kop, vop, P)
+    ctx.set_materialize_grads(False)  # no zero tensors for the outputs nothing differentiates
 
 
 def _backward(ctx, dq_out, dfast, *unused):
+    if dq_out is None and dfast is None:
+        return (None,) * 9
     h, conv_w, g, w, q, z, den, u_op, kw, c, qop, kop, vop, P = ctx.saved_tensors
     hd, cd, kd, bd, ed, vd = ctx.dtypes
     if dfast is None:
@@ -228,9 +231,12 @@ def _mix_setup(ctx, inputs, output):
     ctx.dtypes = (x.dtype, h.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype, v.dtype, mu.dtype)
     ctx.g_shape = g.shape
     ctx.mark_non_differentiable(z, den, u_op, kw, q, c, qop, kop, vop, P)
+    ctx.set_materialize_grads(False)  # no zero tensors for the saved outputs
 
 
 def _mix_backward(ctx, dy, *unused):
+    if dy is None:
+        return (None,) * 11
     h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P = ctx.saved_tensors
     xd, hd, cd, kd, bd, ed, vd, md = ctx.dtypes
     dh, dconv, dkw, dkb, deps, dv, dg, dw, dmu = mixer_bwd(dy.contiguous(), h, conv_w, g, w, mu, z, den, u_op, kw, q,

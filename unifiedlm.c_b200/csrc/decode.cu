@@ -366,6 +366,103 @@ namespace {
 
 int weight_dtype_ok(int dt) { return dt == ULM_F32 || dt == ULM_BF16; }
 
+}  // namespace
+
+namespace ulm {
+
+// Small-batch decode GEMM with bf16 weights: out[b][n] = sum_k x[b][k] W[n][k] for B <= GEMV_MAX_B.
+// The weights are streamed once by every warp of a grid that covers all SMs (one warp per weight
+// row at a time, 16-byte loads, fp32 accumulators), the batch's rows of x sit in shared memory in
+// fp32; a tensor-core tile of 128 rows would leave most of its rows empty and spread the weight
+// reads over only N / 128 CTAs.
+constexpr int GEMV_MAX_B = 4;
+constexpr int GEMV_WARPS = 8;
+
+template <int NB>
+__global__ void __launch_bounds__(32 * GEMV_WARPS)
+    decode_gemv_kernel(const float* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ W, int64_t ldw,
+                       float* __restrict__ out, int64_t ldo, int B, int N, int K) {
+  extern __shared__ float xs[];  // B x K
+  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+    const int b = i / K, k = i - b * K;
+    xs[i] = x[(int64_t)b * ldx + k];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  for (int n = blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5); n < N; n += gridDim.x * GEMV_WARPS) {
+    float acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+    const __nv_bfloat16* wr = W + (int64_t)n * ldw;
+    for (int k8 = lane * 8; k8 < K; k8 += 256) {
+      const uint4 pk = *reinterpret_cast<const uint4*>(wr + k8);
+      const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+      float wv[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h2;
+        memcpy(&h2, &w4[j], 4);
+        const float2 f = __bfloat1622float2(h2);
+        wv[2 * j] = f.x;
+        wv[2 * j + 1] = f.y;
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b < B) {
+          const float4 x0 = *reinterpret_cast<const float4*>(xs + b * K + k8);
+          const float4 x1 = *reinterpret_cast<const float4*>(xs + b * K + k8 + 4);
+          acc[b] = fmaf(wv[0], x0.x, acc[b]);
+          acc[b] = fmaf(wv[1], x0.y, acc[b]);
+          acc[b] = fmaf(wv[2], x0.z, acc[b]);
+          acc[b] = fmaf(wv[3], x0.w, acc[b]);
+          acc[b] = fmaf(wv[4], x1.x, acc[b]);
+          acc[b] = fmaf(wv[5], x1.y, acc[b]);
+          acc[b] = fmaf(wv[6], x1.z, acc[b]);
+          acc[b] = fmaf(wv[7], x1.w, acc[b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      float v = acc[b];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (b < B && lane == 0) out[(int64_t)b * ldo + n] = v;
+    }
+  }
+}
+
+int decode_gemv(const float* x, int64_t ldx, const __nv_bfloat16* W, int64_t ldw, float* out, int64_t ldo,
+                int64_t B, int64_t N, int64_t K, cudaStream_t st) {
+  const size_t smem = (size_t)B * K * sizeof(float);
+  const int dev = current_device();
+  const int64_t grid = std::min<int64_t>(cdiv(N, GEMV_WARPS), 4LL * (dev >= 0 ? sm_count(dev) : 148));
+  if (B <= 4) {
+    if (smem > 48 * 1024)
+      ULM_CUDA_TRY(cudaFuncSetAttribute(decode_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    decode_gemv_kernel<4><<<(unsigned)grid, 32 * GEMV_WARPS, smem, st>>>(x, ldx, W, ldw, out, ldo, (int)B, (int)N,
+                                                                        (int)K);
+  } else {
+    if (smem > 48 * 1024)
+      ULM_CUDA_TRY(
+          cudaFuncSetAttribute(decode_gemv_kernel<GEMV_MAX_B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    decode_gemv_kernel<GEMV_MAX_B><<<(unsigned)grid, 32 * GEMV_WARPS, smem, st>>>(x, ldx, W, ldw, out, ldo, (int)B,
+                                                                                 (int)N, (int)K);
+  }
+  ULM_LAUNCH_CHECK("decode_gemv_kernel");
+  return ULM_OK;
+}
+
+// Whether the small-batch path serves a bf16 decode GEMM (x fp32 rows of ldx, 16-byte weight rows).
+bool gemv_ok(int64_t B, int64_t K, int64_t ldw, int64_t ldx, const void* x, const void* W) {
+  return B <= GEMV_MAX_B && K % 8 == 0 && ldw % 8 == 0 && ldx % 4 == 0 && is_aligned16(x) && is_aligned16(W) &&
+         B * K * (int64_t)sizeof(float) <= 200 * 1024;
+}
+
+}  // namespace ulm
+
+namespace {
+
 // C[b][n] = sum_k X[b][k] W[n][k] for the decode batch; fp32 FMA or bf16 tensor cores.
 int decode_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int wdt, float* out, int64_t ldo, int64_t B,
                 int64_t N, int64_t K, cudaStream_t st) {
@@ -652,8 +749,13 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
                                                               norm_eps);
   ULM_LAUNCH_CHECK("decode_prologue_kernel");
   if (bf) {
-    if (int rc = decode_gemm(uop, ldo, key_w, D, ULM_BF16, a, M, B, M, D, st)) return rc;
-    if (int rc = decode_gemm(hop, ldo, val_w, D, ULM_BF16, v, D, B, D, D, st)) return rc;
+    if (gemv_ok(B, D, D, D, u, key_w) && gemv_ok(B, D, D, D, h, val_w)) {
+      if (int rc = decode_gemv(u, D, static_cast<const __nv_bfloat16*>(key_w), D, a, M, B, M, D, st)) return rc;
+      if (int rc = decode_gemv(h, D, static_cast<const __nv_bfloat16*>(val_w), D, v, D, B, D, D, st)) return rc;
+    } else {
+      if (int rc = decode_gemm(uop, ldo, key_w, D, ULM_BF16, a, M, B, M, D, st)) return rc;
+      if (int rc = decode_gemm(hop, ldo, val_w, D, ULM_BF16, v, D, B, D, D, st)) return rc;
+    }
   } else {
     if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
     if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
@@ -704,7 +806,9 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   decode_final_norm_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(x, norm_w, xn, bf ? xop : nullptr, ldo, (int)D,
                                                                 norm_eps);
   ULM_LAUNCH_CHECK("decode_final_norm_kernel");
-  if (bf) {
+  if (bf && gemv_ok(B, D, D, D, xn, cls_w)) {
+    if (int rc = decode_gemv(xn, D, static_cast<const __nv_bfloat16*>(cls_w), D, logits, V, B, V, D, st)) return rc;
+  } else if (bf) {
     if (int rc = decode_gemm(xop, ldo, cls_w, D, ULM_BF16, logits, V, B, V, D, st)) return rc;
   } else {
     if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) return rc;

@@ -36,7 +36,7 @@ HeadWork carve_head(void* base, int64_t N, int64_t V, int dt) {
     p += al256h(bytes);
     return q;
   };
-  const int64_t ctas = cdiv(N, HEAD_LOSS_THREADS);
+  const int64_t ctas = cdiv(N, HEAD_LOSS_THREADS / 32);  // the loss kernel's CTAs (one row per warp)
   w.part = reinterpret_cast<float*>(take(N * head_part_ld(V) * 2 * 4));
   w.tgt = reinterpret_cast<float*>(take(N * 4));
   w.row_loss = reinterpret_cast<float*>(take(ctas * 4));
@@ -48,44 +48,56 @@ HeadWork carve_head(void* base, int64_t N, int64_t V, int dt) {
 }
 
 // per row: lse = M + log(sum_j s_j exp(m_j - M)) over the column blocks that hold logits (s_j > 0),
-// the row's loss lse - target logit (when its target is not -1); per CTA partial sums in row order
+// the row's loss lse - target logit (when its target is not -1); one warp per row (its lanes read
+// the row's (max, sum) pairs side by side), per CTA partial sums of its HEAD_ROWS rows in row order
+constexpr int HEAD_ROWS = HEAD_LOSS_THREADS / 32;
 __global__ void __launch_bounds__(HEAD_LOSS_THREADS)
     head_lse_kernel(const float* __restrict__ part, int64_t part_ld, const float* __restrict__ tgt_logit,
                     const int64_t* __restrict__ targets, float* __restrict__ lse, float* __restrict__ row_loss,
                     int* __restrict__ row_count, int64_t N) {
-  __shared__ float lred[HEAD_LOSS_THREADS];
-  __shared__ int cred[HEAD_LOSS_THREADS];
-  const int64_t r = (int64_t)blockIdx.x * HEAD_LOSS_THREADS + threadIdx.x;
+  __shared__ float lred[HEAD_ROWS];
+  __shared__ int cred[HEAD_ROWS];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * HEAD_ROWS + wp;
   float loss = 0.f;
   int cnt = 0;
   if (r < N) {
-    const float* pp = part + r * part_ld * 2;
+    const float2* pp = reinterpret_cast<const float2*>(part + r * part_ld * 2);
     float M = -INFINITY;
-    for (int64_t j = 0; j < part_ld; ++j)
-      if (pp[2 * j + 1] > 0.f) M = fmaxf(M, pp[2 * j]);
+    for (int64_t j = lane; j < part_ld; j += 32) {
+      const float2 e = pp[j];
+      if (e.y > 0.f) M = fmaxf(M, e.x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float s = 0.f;
-    for (int64_t j = 0; j < part_ld; ++j)
-      if (pp[2 * j + 1] > 0.f) s += pp[2 * j + 1] * expf(pp[2 * j] - M);
+    for (int64_t j = lane; j < part_ld; j += 32) {
+      const float2 e = pp[j];
+      if (e.y > 0.f) s += e.y * expf(e.x - M);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float l = M + logf(s);
-    lse[r] = l;
+    if (lane == 0) lse[r] = l;
     if (targets[r] >= 0) {
       loss = l - tgt_logit[r];
       cnt = 1;
     }
   }
-  lred[threadIdx.x] = loss;
-  cred[threadIdx.x] = cnt;
-  __syncthreads();
-  for (int st = HEAD_LOSS_THREADS / 2; st > 0; st >>= 1) {
-    if ((int)threadIdx.x < st) {
-      lred[threadIdx.x] += lred[threadIdx.x + st];
-      cred[threadIdx.x] += cred[threadIdx.x + st];
-    }
-    __syncthreads();
+  if (lane == 0) {
+    lred[wp] = loss;
+    cred[wp] = cnt;
   }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    row_loss[blockIdx.x] = lred[0];
-    row_count[blockIdx.x] = cred[0];
+    float ls = 0.f;
+    int cs = 0;
+    for (int i = 0; i < HEAD_ROWS; ++i) {
+      ls += lred[i];
+      cs += cred[i];
+    }
+    row_loss[blockIdx.x] = ls;
+    row_count[blockIdx.x] = cs;
   }
 }
 
@@ -161,7 +173,7 @@ extern "C" int ulm_lm_head_loss_fwd(const void* h_op, int64_t ld_h, const void* 
   e.targets = targets;
   e.rows_valid = (int)N;
   if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
-  const int64_t ctas = cdiv(N, HEAD_LOSS_THREADS);
+  const int64_t ctas = cdiv(N, HEAD_ROWS);
   head_lse_kernel<<<(unsigned)ctas, HEAD_LOSS_THREADS, 0, st>>>(hw.part, pld, hw.tgt, targets, lse, hw.row_loss,
                                                                 hw.row_count, N);
   ULM_LAUNCH_CHECK("head_lse_kernel");

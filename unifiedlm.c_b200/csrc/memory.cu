@@ -372,12 +372,13 @@ constexpr int DOT_BLOCKS = 296;  // fixed grid of the weighted dot products (det
 
 // Chunk length of the operator's fast read, 0 = the whole-sequence form. Automatic: on the tensor
 // cores the largest C in {1024, 512, 256} (multiples of the pair tiles' 256 rows) that divides T into
-// at least two chunks, in fp32 C = 64 (the FMA back end's 64-row tiles), used where the chunked
-// form's flops per token 4 M D + 2 C (M + D) are fewer than the whole-sequence form's T (M + D).
-// (Measured on B200, bf16, 65536 tokens per call: at D 512 / M 1024 the forms tie near T = 4096 and
-// the chunked form with C = 1024 is 16% faster at T = 8192; at D 768 / M 2048 likewise at 8192; at
-// T = 2048 the whole-sequence form is 1.5-2x faster. C = 1024 beat 512 and 256 at every T, since
-// fewer chunk boundaries mean fewer state writes and reads.)
+// at least two chunks, in fp32 C = 64 (the FMA back end's 64-row tiles), used where the
+// whole-sequence form's flops per token T (M + D) exceed 1.25 x the chunked form's
+// 4 M D + 2 C (M + D) (the margin pays for the chunked form's extra passes: the per-row decays,
+// the state writes and reads). Measured on B200, bf16, 65536 tokens per call: the chunked form with
+// C = 1024 is 15-16% faster at T = 8192 at D 512 / M 1024 and at D 768 / M 2048, 6% slower at
+// T = 4096 (42M widths) and slower still below; C = 1024 beat 512 and 256 at every T, since fewer
+// chunk boundaries mean fewer state writes and reads.
 int chunk_len(int64_t T, int64_t M, int64_t D, int prec) {
   if (g_chunk_mode == 0 || M == 0 || D == 0) return 0;
   auto fits = [&](int64_t C) { return T % C == 0 && T / C >= 2; };
@@ -390,7 +391,9 @@ int chunk_len(int64_t T, int64_t M, int64_t D, int prec) {
       if (!C && fits(c)) C = c;
   }
   if (!C) return 0;
-  return (double)T * (double)(M + D) > 4.0 * (double)M * (double)D + 2.0 * (double)C * (double)(M + D) ? (int)C : 0;
+  const double whole = (double)T * (double)(M + D);
+  const double chunked = 4.0 * (double)M * (double)D + 2.0 * (double)C * (double)(M + D);
+  return whole > 1.25 * chunked ? (int)C : 0;
 }
 
 struct ChunkFwdLayout {

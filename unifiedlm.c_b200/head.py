@@ -92,9 +92,12 @@ def _setup(ctx, inputs, output):
     ctx.D = h.shape[1]
     ctx.dtypes = (h.dtype, weight.dtype)
     ctx.mark_non_differentiable(lse, count, h_op, w_op, work)
+    ctx.set_materialize_grads(False)  # no zero tensors for the outputs nothing differentiates
 
 
 def _backward(ctx, dloss, *unused):
+    if dloss is None:
+        return None, None, None, None
     count, h_op, w_op, targets, lse, work = ctx.saved_tensors
     dh, dw = lm_head_bwd(dloss.float().reshape(()).contiguous(), count, h_op, w_op, targets, lse, work, ctx.D,
                          ctx.precision)

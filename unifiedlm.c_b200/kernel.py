@@ -43,13 +43,26 @@ def _op_dtype(precision):
     return torch.float32 if precision == L.ULM_PREC_FP32 else torch.bfloat16
 
 
+def serves_as_operand(x, opt):
+    """Whether a (B,T,D) array can be its own tensor-core operand copy: the operand type, a row
+    stride that needs no padding, contiguous (and, checked by operand_copy on real tensors, a
+    16-byte aligned start; the fake kernels assume it, as every fresh allocation is)."""
+    return x.dtype == opt and operand_ld(x.shape[-1]) == x.shape[-1] and x.is_contiguous()
+
+
 def operand_copy(x, opt):
-    """Buffer for the tensor-core operand copy of a (B,T,D) array: x itself when it already has the
-    operand type, padded row stride and alignment (the library then skips the copy), else a new one."""
+    """Buffer for the tensor-core operand copy of a (B,T,D) array: x itself when it serves as one
+    (the library then skips the copy), else a new one."""
     B, T, D = x.shape
-    if x.dtype == opt and operand_ld(D) == D and x.is_contiguous() and x.data_ptr() % 16 == 0:
+    if serves_as_operand(x, opt) and x.data_ptr() % 16 == 0:
         return x
     return torch.empty(B, T, operand_ld(D), device=x.device, dtype=opt)
+
+
+def operand_copy_fake(x, opt):
+    """The fake-tensor counterpart of unaliased(operand_copy(x, opt), x)."""
+    B, T, D = x.shape
+    return x.new_empty(0, dtype=x.dtype) if serves_as_operand(x, opt) else x.new_empty(B, T, operand_ld(D), dtype=opt)
 
 
 def saved_buffer(B, T, M, D, precision, device):
@@ -96,7 +109,7 @@ def memory_fwd_fake(r, v, precision):
     c_shape = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
     return (r.new_empty(B, T, M, dtype=torch.float32), v.new_empty(B, T, D), r.new_empty(c_shape, dtype=torch.float32),
             r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
-            r.new_empty(B, T, operand_ld(D), dtype=opt),
+            operand_copy_fake(v, opt),
             r.new_empty(int(L.lib().ulm_memory_saved_bytes(B, T, M, D, precision)), dtype=torch.uint8))
 
 
@@ -176,9 +189,12 @@ def _setup_context(ctx, inputs, output):
     ctx.v_dim = v.shape[-1]
     ctx.g_shape = g.shape
     ctx.mark_non_differentiable(c, qop, kop, vop, P)
+    ctx.set_materialize_grads(False)  # no zero tensors for the outputs nothing differentiates
 
 
 def _backward(ctx, dq_out, dfast, *unused):
+    if dq_out is None and dfast is None:
+        return None, None, None, None, None
     r, g, w, q, c, qop, kop, vop, P = ctx.saved_tensors
     if dfast is None:
         dfast = torch.zeros(q.shape[0], q.shape[1], ctx.v_dim, device=q.device, dtype=ctx.v_dtype)
@@ -235,7 +251,7 @@ def combine_fwd_fake(r, v, x, precision):
     keep = (B, T, M) if L.lib().ulm_memory_needs_c(T, M) else (0,)
     return (x.new_empty(B, T, D), r.new_empty(keep, dtype=torch.float32), r.new_empty(keep, dtype=torch.float32),
             r.new_empty(B, T, operand_ld(M), dtype=opt), r.new_empty(B, T, operand_ld(M), dtype=opt),
-            r.new_empty(B, T, operand_ld(D), dtype=opt),
+            operand_copy_fake(v, opt),
             r.new_empty(int(L.lib().ulm_memory_saved_bytes(B, T, M, D, precision)), dtype=torch.uint8))
 
 

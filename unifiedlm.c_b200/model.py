@@ -106,7 +106,10 @@ class UnifiedBlock(nn.Module):
 
     def forward(self, x):
         h = self.norm(x)
-        v = linear(h, self.val.weight, precision=self.precision)
+        # v in bf16 with the tensor-core products (as under the reference's bf16 autocast): the fast
+        # memory rounds it to its bf16 operand copy anyway, so it is written once in that form
+        v = linear(h, self.val.weight, precision=self.precision,
+                   out_dtype=torch.bfloat16 if self.precision == "bf16" else None)
         w, g, eps = self._w(), self._g(), self._eps()
         if self.dropout.p == 0.0 or not self.training:
             return block_mixer(x, h, self.conv.weight, self.key.weight, self.key.bias, eps, v, g, w,

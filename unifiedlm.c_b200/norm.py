@@ -60,9 +60,12 @@ def _rn_setup(ctx, inputs, output):
     ctx.save_for_backward(x, weight, output[1])
     ctx.dtypes = (x.dtype, weight.dtype)
     ctx.mark_non_differentiable(output[1])
+    ctx.set_materialize_grads(False)
 
 
 def _rn_backward(ctx, dy, _drstd):
+    if dy is None:
+        return None, None, None
     x, weight, rstd = ctx.saved_tensors
     dx, dw = rms_norm_bwd(dy.contiguous(), x, weight, rstd)
     return dx.to(ctx.dtypes[0]), dw.to(ctx.dtypes[1]), None
@@ -82,15 +85,16 @@ def rms_norm(x, weight, eps):
 # ---- Linear --------------------------------------------------------------------------------------
 
 @torch.library.custom_op("ulm::linear_fwd", mutates_args=())
-def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int
+def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int, out_bf16: bool
                ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Returns (y, x_op, w_op); the operand copies are saved for the backward."""
+    """Returns (y, x_op, w_op); y in x's type or bf16 (out_bf16); the operand copies are saved for
+    the backward."""
     _require_cuda(x, weight)
     K = x.shape[-1]
     N = x.numel() // max(K, 1)
     Nout = weight.shape[0]
     opt = _op_dtype(precision)
-    y = torch.empty(*x.shape[:-1], Nout, device=x.device, dtype=x.dtype)
+    y = torch.empty(*x.shape[:-1], Nout, device=x.device, dtype=torch.bfloat16 if out_bf16 else x.dtype)
     x_op = torch.empty(N, operand_ld(K), device=x.device, dtype=opt)
     w_op = torch.empty(Nout, operand_ld(K), device=x.device, dtype=opt)
     with torch.cuda.device(x.device):
@@ -100,11 +104,12 @@ def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int
 
 
 @linear_fwd.register_fake
-def _linear_fwd_fake(x, weight, precision):
+def _linear_fwd_fake(x, weight, precision, out_bf16):
     K = x.shape[-1]
     N = x.numel() // max(K, 1)
     opt = _op_dtype(precision)
-    return (x.new_empty(*x.shape[:-1], weight.shape[0]), x.new_empty(N, operand_ld(K), dtype=opt),
+    return (x.new_empty(*x.shape[:-1], weight.shape[0], dtype=torch.bfloat16 if out_bf16 else x.dtype),
+            x.new_empty(N, operand_ld(K), dtype=opt),
             x.new_empty(weight.shape[0], operand_ld(K), dtype=opt))
 
 
@@ -131,25 +136,31 @@ def _linear_bwd_fake(dy, x_op, w_op, K, precision):
 
 
 def _lin_setup(ctx, inputs, output):
-    x, weight, precision = inputs
+    x, weight, precision, out_bf16 = inputs
     ctx.save_for_backward(output[1], output[2])
     ctx.meta = (x.shape, x.dtype, weight.dtype, precision)
     ctx.mark_non_differentiable(output[1], output[2])
+    ctx.set_materialize_grads(False)
 
 
 def _lin_backward(ctx, dy, _dx_op, _dw_op):
+    if dy is None:
+        return None, None, None, None
     x_op, w_op = ctx.saved_tensors
     shape, xdt, wdt, precision = ctx.meta
     dx, dw = linear_bwd(dy.reshape(-1, dy.shape[-1]).contiguous(), x_op, w_op, shape[-1], precision)
-    return dx.reshape(shape).to(xdt), dw.to(wdt), None
+    return dx.reshape(shape).to(xdt), dw.to(wdt), None, None
 
 
 torch.library.register_autograd("ulm::linear_fwd", _lin_backward, setup_context=_lin_setup)
 
 
-def linear(x, weight, precision="bf16"):
+def linear(x, weight, precision="bf16", out_dtype=None):
     """x W^T without bias (nn.Linear's forward for UnifiedBlock.val): x (..., K) fp32 or bf16,
-    weight (Nout, K); the result has x's type."""
+    weight (Nout, K); the result has x's type, or bf16 with out_dtype=torch.bfloat16 (the type
+    autocast gives it, and the one the fast memory's tensor-core operands use)."""
     xx = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
-    y, _, _ = torch.ops.ulm.linear_fwd(xx.contiguous(), weight.float().contiguous(), PRECISION[precision])
-    return y if y.dtype == x.dtype else y.to(x.dtype)
+    bf16 = out_dtype == torch.bfloat16
+    y, _, _ = torch.ops.ulm.linear_fwd(xx.contiguous(), weight.float().contiguous(), PRECISION[precision], bf16)
+    want = torch.bfloat16 if bf16 else x.dtype
+    return y if y.dtype == want else y.to(want)

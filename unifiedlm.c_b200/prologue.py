@@ -123,9 +123,12 @@ def _setup(ctx, inputs, output):
     ctx.precision = precision
     ctx.dtypes = (h.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype)
     ctx.mark_non_differentiable(den, u_op, kw)
+    ctx.set_materialize_grads(False)  # no zero tensors for the outputs nothing differentiates
 
 
 def _backward(ctx, dr, *unused):
+    if dr is None:
+        return None, None, None, None, None, None
     r, den, u_op, kw, h, conv_w = ctx.saved_tensors
     dh, dconv, dkw, dkb, deps = address_bwd(dr, r, den, u_op, kw, h, conv_w, ctx.precision)
     hd, cd, kd, bd, ed = ctx.dtypes
