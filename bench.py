@@ -621,9 +621,20 @@ def timed_products(ulm_lib, L_, tensors, W, prec):
         (2 * B * pairs * D, lambda: lib.ulm_causal_apply(L_.ptr(P), ldt, L_.ptr(doop), ldd, L_.ptr(dv), D,
                                                          L_.dtype_code(dv.dtype), 1, B, T, D, prec, sp)),
     ]
+    # compulsory DRAM bytes of each launch: its operands read once, its output written once (the
+    # causal score matrices P and dS hold T (T + 1) / 2 entries per row)
+    tri = B * pairs * P.element_size()
+    btm, btd = B * T * M, B * T * D
+    nbytes = [btm * qop.element_size() + btm * kop.element_size() + tri,
+              tri + btd * vop.element_size() + btd * fast.element_size(),
+              btd * doop.element_size() + btd * vop.element_size() + 2 * tri,
+              tri + btm * kop.element_size() + btm * dqf.element_size(),
+              tri + btm * qop.element_size() + btm * dk.element_size(),
+              tri + btd * doop.element_size() + btd * dv.element_size()]
+    calls = [(fl, fn, nb) for (fl, fn), nb in zip(calls, nbytes)]
     flops, secs = 0, 0.0
     per = []
-    for fl, fn in calls:
+    for fl, fn, nb in calls:
         L_.check(fn())  # warm
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         reps = 5
@@ -634,7 +645,7 @@ def timed_products(ulm_lib, L_, tensors, W, prec):
         ev[1].record(st)
         torch.cuda.synchronize()
         s = ev[0].elapsed_time(ev[1]) / 1e3 / reps
-        per.append((fl, s))
+        per.append((fl, s, nb))
         flops += fl
         secs += s
     return flops, secs, per
@@ -921,6 +932,9 @@ def main():
     flops, psecs, per = timed_products(None, L_, (qop, kop, vop, P, doop, dS, dqf, dk, dvb, fastb, g), W, prec)
     pk = peaks()
     achieved = flops / psecs / 1e12
+    # each product's own roofline time: the slower of its flops at the tensor peak and its compulsory
+    # bytes at the copy peak (dq and dk write fp32 T x M gradients, so their bytes bound them)
+    floors = [max(f / (pk["bf16_tflops"] * 1e12), nb / (pk["hbm_gbs"] * 1e9)) for f, _, nb in per]
     roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": PRODUCTS_DRAM_BYTES,
                 "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the six products of one block, "
@@ -928,8 +942,13 @@ def main():
                 "algorithmic_flops_per_block": flops,
                 "kernel": "tc2_gemm_kernel (6 causal products per block fwd+bwd)",
                 "peak_source": pk["source"],
-                "per_launch_ms": [round(s * 1e3, 4) for _, s in per],
-                "per_launch_tflops": [round(f / s / 1e12, 1) for f, s in per]}
+                "per_launch_ms": [round(s * 1e3, 4) for _, s, _ in per],
+                "per_launch_tflops": [round(f / s / 1e12, 1) for f, s, _ in per],
+                "per_launch_compulsory_mb": [round(nb / 1e6, 1) for _, _, nb in per],
+                "per_launch_floor_ms": [round(t * 1e3, 4) for t in floors],
+                "floor_frac": round(sum(floors) / psecs, 4),
+                "floor_note": "per product max(flops / bf16 peak, compulsory bytes / hbm peak); floor_frac = "
+                              "sum of those times / sum of the measured launch times"}
 
     models = None
     if not args.no_model:

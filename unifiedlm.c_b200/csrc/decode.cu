@@ -101,16 +101,20 @@ __global__ void __launch_bounds__(DEC_THREADS)
   }
 }
 
-// One warp per state row (b, d): U'[m] = ((lam U) + prior[d][m]) + v[d] r_prev[m]; x[b][d] += sum U' q.
-// prior = (1-lam) mu w, fp32 or bf16. The row is streamed once with 16-byte loads and stores.
-template <typename PriorT>
+// S warps per state row (b, d) (S in {1, 2, 4, 8}; more at small batches, so that enough loads are in
+// flight): U'[m] = ((lam U) + prior[d][m]) + v[d] r_prev[m]; x[b][d] += sum U' q. prior = (1-lam) mu w,
+// fp32 or bf16. The row is streamed once with 16-byte loads and stores; a CTA's 8 warps cover 8 / S
+// rows and the S partial dot products of a row are added in warp order through shared memory.
+template <typename PriorT, int S>
 __global__ void __launch_bounds__(DEC_THREADS)
     decode_state_kernel(float* __restrict__ U, const PriorT* __restrict__ prior, const float* __restrict__ v,
                         const float* __restrict__ r_prev, const float* __restrict__ q, const float* __restrict__ lam_p,
                         float* __restrict__ x, int D, int M) {
-  const int warps = blockDim.x >> 5;
+  __shared__ float red[DEC_THREADS / 32];
+  constexpr int warps = DEC_THREADS / 32;
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * warps + wp;  // b * D + d
+  const int sub = wp % S;
+  const int64_t row = (int64_t)blockIdx.x * (warps / S) + wp / S;  // b * D + d
   const int b = (int)(row / D);
   const int d = (int)(row - (int64_t)b * D);
   const float lam = *lam_p;
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
   const float* rp = r_prev + (int64_t)b * M;
   const float* qb = q + (int64_t)b * M;
   float acc = 0.f;
-  for (int m = lane * 4; m < M; m += 128) {
+  for (int m = (sub * 32 + lane) * 4; m < M; m += 128 * S) {
     float4 u4 = *reinterpret_cast<const float4*>(Ur + m);
     const float4 r4 = *reinterpret_cast<const float4*>(rp + m);
     const float4 q4 = *reinterpret_cast<const float4*>(qb + m);
@@ -148,7 +152,17 @@ __global__ void __launch_bounds__(DEC_THREADS)
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) x[row] += acc;
+  if constexpr (S == 1) {
+    if (lane == 0) x[row] += acc;
+    return;
+  }
+  if (lane == 0) red[wp] = acc;
+  __syncthreads();
+  if (sub == 0 && lane == 0) {
+    float t = red[wp];
+    for (int j = 1; j < S; ++j) t += red[wp + j];
+    x[row] += t;
+  }
 }
 
 // prior[d][m] = ((1 - lam) * mu[d][m]) * w[m], and the initial state U = mu * w (run.c:121-138)
@@ -763,14 +777,22 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   decode_address_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(a, key_b, w, lam, eps, c, r_prev, r_new, q, (int)M);
   ULM_LAUNCH_CHECK("decode_address_kernel");
   const int warps = DEC_THREADS / 32;
-  const unsigned blocks = (unsigned)cdiv(B * D, warps);
   ULM_REQUIRE((B * D) % warps == 0, "B*D must be a multiple of %d", warps);
-  if (bf)
-    decode_state_kernel<__nv_bfloat16><<<blocks, DEC_THREADS, 0, st>>>(
-        U, static_cast<const __nv_bfloat16*>(prior), v, r_prev, q, lam, x, (int)D, (int)M);
-  else
-    decode_state_kernel<float><<<blocks, DEC_THREADS, 0, st>>>(U, static_cast<const float*>(prior), v, r_prev, q, lam,
-                                                               x, (int)D, (int)M);
+  // warps per state row: enough rows' loads in flight to cover the SMs at small batches
+  int S = 1;
+  while (S < warps && B * D * S < 16 * 148 && (int64_t)S * 128 < M) S *= 2;
+  const unsigned blocks = (unsigned)(B * D * S / warps);
+  auto launch = [&](auto kern, const auto* pr) {
+    kern<<<blocks, DEC_THREADS, 0, st>>>(U, pr, v, r_prev, q, lam, x, (int)D, (int)M);
+  };
+  const auto* pb = static_cast<const __nv_bfloat16*>(prior);
+  const auto* pf = static_cast<const float*>(prior);
+  switch (S) {
+    case 1: bf ? launch(decode_state_kernel<__nv_bfloat16, 1>, pb) : launch(decode_state_kernel<float, 1>, pf); break;
+    case 2: bf ? launch(decode_state_kernel<__nv_bfloat16, 2>, pb) : launch(decode_state_kernel<float, 2>, pf); break;
+    case 4: bf ? launch(decode_state_kernel<__nv_bfloat16, 4>, pb) : launch(decode_state_kernel<float, 4>, pf); break;
+    default: bf ? launch(decode_state_kernel<__nv_bfloat16, 8>, pb) : launch(decode_state_kernel<float, 8>, pf); break;
+  }
   ULM_LAUNCH_CHECK("decode_state_kernel");
   copy_f32_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * M, 256), 4 * 148), 256, 0, st>>>(r_new, r_prev, B * M);
   ULM_LAUNCH_CHECK("copy_f32_kernel");

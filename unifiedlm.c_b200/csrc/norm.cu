@@ -98,6 +98,101 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
   }
 }
 
+// The same two kernels for fp32 rows with D % 4 == 0 and D <= 128 * NV: each lane keeps its
+// float4 columns (lane, lane + 32, ...) of the row in registers, so the row is read once per pass.
+template <int NV>
+__global__ void __launch_bounds__(32 * NORM_WARPS)
+    rms_norm_fwd_vec_kernel(const float* __restrict__ x, const float* __restrict__ weight, float* __restrict__ y,
+                            float* __restrict__ rstd, int64_t rows, int D, float eps) {
+  pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int D4 = D / 4;
+  for (int64_t r = (int64_t)blockIdx.x * NORM_WARPS + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * NORM_WARPS) {
+    const float4* xr = reinterpret_cast<const float4*>(x + r * D);
+    float4 v[NV];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      v[j] = i < D4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / (float)D + eps);
+    float4* yr = reinterpret_cast<float4*>(y + r * D);
+    const float4* w4 = reinterpret_cast<const float4*>(weight);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      if (i < D4) {
+        const float4 w = w4[i];
+        yr[i] = make_float4(v[j].x * rs * w.x, v[j].y * rs * w.y, v[j].z * rs * w.z, v[j].w * rs * w.w);
+      }
+    }
+    if (lane == 0 && rstd) rstd[r] = rs;
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(32 * NORM_WARPS)
+    rms_norm_bwd_vec_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ weight,
+                            const float* __restrict__ rstd, float* __restrict__ dx, float* __restrict__ part,
+                            int64_t rows, int D) {
+  pdl_enter();
+  extern __shared__ float colsum[];  // NORM_WARPS x D
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int D4 = D / 4;
+  float4* mine = reinterpret_cast<float4*>(colsum + (int64_t)warp * D);
+  const float4* w4 = reinterpret_cast<const float4*>(weight);
+  float4 acc[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t r = (int64_t)blockIdx.x * NORM_WARPS + warp; r < rows; r += (int64_t)gridDim.x * NORM_WARPS) {
+    const float rs = rstd[r];
+    const float4* gr = reinterpret_cast<const float4*>(dy + r * D);
+    const float4* xr = reinterpret_cast<const float4*>(x + r * D);
+    float4 g[NV], xh[NV];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      g[j] = i < D4 ? gr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 xv = i < D4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      xh[j] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
+      const float4 w = i < D4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      dot = fmaf(g[j].x * w.x, xh[j].x, fmaf(g[j].y * w.y, xh[j].y,
+                 fmaf(g[j].z * w.z, xh[j].z, fmaf(g[j].w * w.w, xh[j].w, dot))));
+      acc[j].x = fmaf(g[j].x, xh[j].x, acc[j].x);
+      acc[j].y = fmaf(g[j].y, xh[j].y, acc[j].y);
+      acc[j].z = fmaf(g[j].z, xh[j].z, acc[j].z);
+      acc[j].w = fmaf(g[j].w, xh[j].w, acc[j].w);
+    }
+    dot = warp_sum(dot) / (float)D;
+    float4* dr = reinterpret_cast<float4*>(dx + r * D);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = lane + 32 * j;
+      if (i < D4) {
+        const float4 w = w4[i];
+        dr[i] = make_float4(rs * (g[j].x * w.x - xh[j].x * dot), rs * (g[j].y * w.y - xh[j].y * dot),
+                            rs * (g[j].z * w.z - xh[j].z * dot), rs * (g[j].w * w.w - xh[j].w * dot));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = lane + 32 * j;
+    if (i < D4) mine[i] = acc[j];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float t = 0.f;
+    for (int w = 0; w < NORM_WARPS; ++w) t += colsum[(int64_t)w * D + i];
+    part[(int64_t)blockIdx.x * D + i] = t;
+  }
+}
+
 // out[i] = sum over p < nparts of part[p][i], in order
 __global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int64_t n, float* __restrict__ out) {
   pdl_enter();
@@ -110,7 +205,7 @@ __global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int6
 
 int norm_grid(int64_t rows) {
   const int dev = current_device();
-  const int64_t cap = 2LL * (dev >= 0 ? sm_count(dev) : 148);
+  const int64_t cap = 4LL * (dev >= 0 ? sm_count(dev) : 148);
   return (int)std::max<int64_t>(1, std::min<int64_t>(cap, cdiv(rows, NORM_WARPS)));
 }
 
@@ -128,8 +223,17 @@ extern "C" int ulm_rms_norm_fwd(const void* x, int x_dtype, const float* weight,
   if (rows == 0 || D == 0) return ULM_OK;
   ULM_REQUIRE(x && weight && y, "null pointer argument");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return launch_pdl(rms_norm_fwd_kernel, dim3((unsigned)norm_grid(rows)), dim3(32 * NORM_WARPS), 0, st, x, x_dtype,
-                    weight, y, y_dtype, rstd, rows, (int)D, eps);
+  const dim3 grid((unsigned)norm_grid(rows)), block(32 * NORM_WARPS);
+  if (x_dtype == ULM_F32 && y_dtype == ULM_F32 && D % 4 == 0 && is_aligned16(x) && is_aligned16(y) &&
+      is_aligned16(weight)) {
+    const float* xf = static_cast<const float*>(x);
+    float* yf = static_cast<float*>(y);
+    if (D <= 128 * 4)
+      return launch_pdl(rms_norm_fwd_vec_kernel<4>, grid, block, 0, st, xf, weight, yf, rstd, rows, (int)D, eps);
+    if (D <= 128 * 8)
+      return launch_pdl(rms_norm_fwd_vec_kernel<8>, grid, block, 0, st, xf, weight, yf, rstd, rows, (int)D, eps);
+  }
+  return launch_pdl(rms_norm_fwd_kernel, grid, block, 0, st, x, x_dtype, weight, y, y_dtype, rstd, rows, (int)D, eps);
 }
 
 extern "C" int64_t ulm_rms_norm_bwd_work_bytes(int64_t rows, int64_t D) {
@@ -158,9 +262,21 @@ extern "C" int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int
   if (smem > 48 * 1024)
     ULM_CUDA_TRY(cudaFuncSetAttribute(rms_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   float* part = static_cast<float*>(work);
-  if (int rc = launch_pdl(rms_norm_bwd_kernel, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, dy, dy_dtype, x,
-                          x_dtype, weight, rstd, dx, part, rows, (int)D))
+  const bool vec = x_dtype == ULM_F32 && dy_dtype == ULM_F32 && D % 4 == 0 && D <= 128 * 8 && is_aligned16(x) &&
+                   is_aligned16(dy) && is_aligned16(dx) && is_aligned16(weight);
+  if (vec) {
+    const float* xf = static_cast<const float*>(x);
+    const float* gf = static_cast<const float*>(dy);
+    auto kern = D <= 128 * 4 ? rms_norm_bwd_vec_kernel<4> : rms_norm_bwd_vec_kernel<8>;
+    if (smem > 48 * 1024)
+      ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (int rc = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, gf, xf, weight, rstd, dx, part,
+                            rows, (int)D))
+      return rc;
+  } else if (int rc = launch_pdl(rms_norm_bwd_kernel, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, dy,
+                                 dy_dtype, x, x_dtype, weight, rstd, dx, part, rows, (int)D)) {
     return rc;
+  }
   return launch_pdl(sum_rows_kernel, dim3((unsigned)cdiv(D, 256)), dim3(256), 0, st, (const float*)part, grid, D,
                     dweight);
 }
