@@ -156,8 +156,9 @@ int ulm_set_epilogue_mode(int mode);
 
 /* Library-wide choice of the slot-statistics scan kernels for T <= 1024: 1 (default) = persistent
  * clusters that walk (batch row, 32-slot block) items with the next item's tiles loading while the
- * current one is scanned; 0 = one cluster per item. Both compute the same values in the same
- * order. Returns the previous mode, or -1 (no change) for an unknown mode. */
+ * current one is scanned; 0 = one cluster per item. Both compute the same values; they add the
+ * per-warp partial sums in different groupings, so results agree to fp32 rounding. Returns the
+ * previous mode, or -1 (no change) for an unknown mode. */
 int ulm_set_scan_mode(int mode);
 
 /* Library-wide switch of programmatic dependent launch: 1 (default) lets each kernel of the library

@@ -290,8 +290,12 @@ def test_pair_and_single_cta_products_agree(kind):
                          ids=lambda s: "x".join(map(str, s)))
 def test_scan_modes_agree(shape):
     """The persistent pipelined scans (ulm_set_scan_mode(1), the default) and the one-cluster-per-item
-    scans compute the same q, c, operand copies, dr and dw bit for bit (same arithmetic in the same
-    order), with and without dq_out; dg differs only in the order its partials are added."""
+    scans compute the same q, c, operand copies, dr, dw and dg, with and without dq_out. The
+    pipelined kernels give each thread two slots of half a warp's rows and join the two halves'
+    partial sums with lam^8, the per-item kernels chain a warp's 16 rows directly, so the fp32 results
+    agree to rounding: within 1e-5 of the array's largest magnitude (measured differences are ~1e-7
+    relative), and the bf16 copy of q within one bf16 step where the fp32 q values straddle a
+    rounding boundary."""
     B, T, M = shape
     gen = torch.Generator().manual_seed(B * T + M)
     a = torch.randn(B, T, M, generator=gen) + 0.3
@@ -329,7 +333,12 @@ def test_scan_modes_agree(shape):
     names = ["q", "c", "qop", "kop", "dr", "dw", "dg", "dr0", "dw0", "dg0"]
     for name, x0, x1 in zip(names, res[0], res[1]):
         if name.startswith("dg"):
-            assert abs(float(x0) - float(x1)) <= 1e-6 * abs(float(x0)) + 1e-12, (name, float(x0), float(x1))
+            assert abs(float(x0) - float(x1)) <= 1e-5 * abs(float(x0)) + 1e-12, (name, float(x0), float(x1))
+        elif name == "kop":  # r shifted by one position: no scan arithmetic
+            assert torch.equal(x0, x1)
+        elif name == "qop":
+            assert ((x0 - x1).abs() <= x0.abs() * 2.0 ** -7).all(), (name, float((x0 - x1).abs().max()))
         else:
-            assert torch.equal(x0, x1), (name, float((x0 - x1).abs().max()))
+            err = float((x0 - x1).abs().max())
+            assert err <= 1e-5 * float(x0.abs().max()) + 1e-30, (name, err, float(x0.abs().max()))
     assert L.device_error() == 0

@@ -551,20 +551,38 @@ __device__ __forceinline__ void den_store(float* sinv, const float* den, float d
   if (i <= n) sinv[i] = den ? ((t >= 0 && t < T) ? __frcp_rn(dv) : 0.f) : 1.f;
 }
 
+// Two slots of one item as a pair of floats (8-byte stores; the bf16 operand pair packed in 4 bytes).
+template <typename T>
+__device__ __forceinline__ void store_op2(void* base, int64_t idx, float2 v);
+template <>
+__device__ __forceinline__ void store_op2<float>(void* base, int64_t idx, float2 v) {
+  *reinterpret_cast<float2*>(static_cast<float*>(base) + idx) = v;
+}
+template <>
+__device__ __forceinline__ void store_op2<__nv_bfloat16>(void* base, int64_t idx, float2 v) {
+  *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(base) + idx) = __floats2bfloat162_rn(v.x, v.y);
+}
+
+// Forward scan (kernel.py:109-136) on the TMA-staged r tile of one item per stage. Each warp owns
+// SEG consecutive rows of the CTA's R; a thread holds two adjacent slots of SEG / 2 of those rows
+// (lanes 0-15 the first half, lanes 16-31 the second), so every shared-memory load and global
+// store moves two slots. The warp's total is the second half's plus lam^(SEG/2) times the first's.
 template <int SEG, int WARPS, int STAGES, typename OpT>
-__global__ void __launch_bounds__(32 * WARPS)
+__global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 registers
     stats_fwd_pipe_kernel(const __grid_constant__ CUtensorMap map_r, const __grid_constant__ CUtensorMap map_r1,
                           const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
                           float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
                           void* __restrict__ kop, int64_t ldop, int B, int T, int M) {
   pdl_enter();
+  static_assert(SEG % 2 == 0, "two half-segments per warp");
   constexpr int R = SEG * WARPS;
+  constexpr int H = SEG / 2;
   constexpr int STAGE_FLOATS = (R + 1) * 32;
   extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t full[STAGES];
   __shared__ __align__(8) uint64_t xbar;
-  __shared__ float warp_sum[WARPS][32];
-  __shared__ float ctot[SCAN_MAX_CLUSTER][32];
+  __shared__ __align__(16) float warp_sum[WARPS][32];
+  __shared__ __align__(16) float ctot[SCAN_MAX_CLUSTER][32];
   __shared__ float sinv[2][R + 1];  // row scales of the current and the next item
   __shared__ int ok_flag;
   static_assert(32 * WARPS > R, "one thread per row scale");
@@ -572,6 +590,7 @@ __global__ void __launch_bounds__(32 * WARPS)
   const int C = (int)cluster.num_blocks();
   const int cr = (int)cluster.block_rank();
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int half = lane >> 4, s2 = (lane & 15) * 2;  // rows [half * H, half * H + H) of the warp; slots s2, s2 + 1
   const int cta_t0 = cr * R;
   const int nmb = (M + 31) / 32;
   const int n_items = B * nmb;
@@ -602,38 +621,52 @@ __global__ void __launch_bounds__(32 * WARPS)
   cluster_sync_all();
   const float gg = *g;
   const float lam = expf(gg);
+  const float lam_h = expf(gg * (float)H);
   const float lam_seg = expf(gg * (float)SEG);
   const float lam_cta = expf(gg * (float)R);
-  float w_cur = 0.f;
+  // prior masses of this thread's two slots (the current and the next item)
+  auto load_w = [&](int item) {
+    const int m0 = (item % nmb) * 32 + s2;
+    return m0 < M ? make_float2(w[m0], w[m0 + 1]) : make_float2(0.f, 0.f);  // M % 4 == 0: both or neither
+  };
+  float2 w_cur = make_float2(0.f, 0.f);
   if (k0 < n_items) {
-    const int m_first = (k0 % nmb) * 32 + lane;
-    w_cur = m_first < M ? w[m_first] : 0.f;
+    w_cur = load_w(k0);
     den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
   }
   for (int j = 0;; ++j) {
     const int item = k0 + j * G;
     if (item >= n_items) break;
     const int b = item / nmb;
-    const int m = (item % nmb) * 32 + lane;
+    const int m0 = (item % nmb) * 32 + s2;
     const float* xs = tile + (j % STAGES) * STAGE_FLOATS;
     // the next item's row scales and prior masses: loaded now, used after this item
     const int item_n = item + G;
     const bool has_next = item_n < n_items;
-    const int m_n = (item_n % nmb) * 32 + lane;
     const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
-    const float w_n = (has_next && m_n < M) ? w[m_n] : 0.f;
+    const float2 w_n = has_next ? load_w(item_n) : make_float2(0.f, 0.f);
     const uint64_t lim = ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS;
     if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, lim)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
       ok_flag = 0;
     }
     __syncthreads();
-    const float* xt = xs + (wp * SEG) * 32 + lane;  // xt[i * 32]: k of position t0 + i, r of t0 + i - 1
-    const float* si = sinv[j & 1] + wp * SEG;
-    float run = 0.f;
+    // xt[i * 32]: k of position t0 + i (the r row before it), xt[(i + 1) * 32]: r of t0 + i
+    const int rh = wp * SEG + half * H;
+    const float* xt = xs + rh * 32 + s2;
+    const float* si = sinv[j & 1] + rh;
+    float2 run = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, xt[i * 32] * si[i]);
-    warp_sum[wp][lane] = run;
+    for (int i = 0; i < H; ++i) {
+      const float2 k2 = *reinterpret_cast<const float2*>(xt + i * 32);
+      const float sv = si[i];
+      run.x = fmaf(lam, run.x, k2.x * sv);
+      run.y = fmaf(lam, run.y, k2.y * sv);
+    }
+    // the first half's total, seen by the second half's lanes of the same slots
+    const float lo_x = __shfl_sync(0xffffffffu, run.x, lane & 15);
+    const float lo_y = __shfl_sync(0xffffffffu, run.y, lane & 15);
+    if (half) *reinterpret_cast<float2*>(&warp_sum[wp][s2]) = make_float2(fmaf(lam_h, lo_x, run.x), fmaf(lam_h, lo_y, run.y));
     __syncthreads();
     __syncwarp();
     if (j > 0) cluster_wait_acquire();  // every CTA has read the previous item's totals
@@ -651,33 +684,54 @@ __global__ void __launch_bounds__(32 * WARPS)
       // armed for the next item: its totals are sent only after this CTA's cluster arrive below
       if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar, (uint32_t)cr * 128u);
     }
-    float carry = 0.f;
-    for (int jj = 0; jj < cr; ++jj) carry = fmaf(carry, lam_cta, ctot[jj][lane]);
-    for (int jj = 0; jj < wp; ++jj) carry = fmaf(carry, lam_seg, warp_sum[jj][lane]);
+    float2 carry = make_float2(0.f, 0.f);
+    // unrolled to the static bounds so that the shared-memory loads issue together
+#pragma unroll
+    for (int jj = 0; jj < SCAN_MAX_CLUSTER; ++jj)
+      if (jj < cr) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&ctot[jj][s2]);
+        carry.x = fmaf(carry.x, lam_cta, t2.x);
+        carry.y = fmaf(carry.y, lam_cta, t2.y);
+      }
+#pragma unroll
+    for (int jj = 0; jj < WARPS; ++jj)
+      if (jj < wp) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&warp_sum[jj][s2]);
+        carry.x = fmaf(carry.x, lam_seg, t2.x);
+        carry.y = fmaf(carry.y, lam_seg, t2.y);
+      }
+    if (half) {  // the second half starts after the first half's rows
+      carry.x = fmaf(lam_h, carry.x, lo_x);
+      carry.y = fmaf(lam_h, carry.y, lo_y);
+    }
     // this CTA's totals slots may be written again: every thread has read them (the CTA barrier),
     // so the arrive needs no release ordering (which would also wait for the previous item's stores)
     __syncthreads();
     cluster_arrive_relaxed();
-    if (m < M) {
-      const float wm = w_cur;
-      const int t0 = cta_t0 + wp * SEG;
+    if (m0 < M) {
+      const float2 wm = w_cur;
+      const int t0 = cta_t0 + rh;
       const int64_t row = (int64_t)b * T + t0;
-      float* qp = q ? q + row * M + m : nullptr;
-      float* cp = c ? c + row * M + m : nullptr;
-      const int64_t io = row * ldop + m;
+      float* qp = q ? q + row * M + m0 : nullptr;
+      float* cp = c ? c + row * M + m0 : nullptr;
+      const int64_t io = row * ldop + m0;
       run = carry;
-      float kk = xt[0] * si[0];
+      const float2 k0v = *reinterpret_cast<const float2*>(xt);
+      float2 kk = make_float2(k0v.x * si[0], k0v.y * si[0]);
 #pragma unroll
-      for (int i = 0; i < SEG; ++i) {
-        const float rv = xt[(i + 1) * 32] * si[i + 1];
+      for (int i = 0; i < H; ++i) {
+        const float2 r2 = *reinterpret_cast<const float2*>(xt + (i + 1) * 32);
+        const float sv = si[i + 1];
+        const float2 rv = make_float2(r2.x * sv, r2.y * sv);
         if (t0 + i < T) {
-          run = fmaf(lam, run, kk);
-          const float cc = wm + run;
-          const float qq = rv * fast_rcp(cc);
-          if (qp) qp[(int64_t)i * M] = qq;
-          if (cp) cp[(int64_t)i * M] = cc;
-          store_op<OpT>(qop, io + (int64_t)i * ldop, qq);
-          store_op<OpT>(kop, io + (int64_t)i * ldop, kk);
+          run.x = fmaf(lam, run.x, kk.x);
+          run.y = fmaf(lam, run.y, kk.y);
+          const float2 cc = make_float2(wm.x + run.x, wm.y + run.y);
+          const float2 qq = make_float2(rv.x * fast_rcp(cc.x), rv.y * fast_rcp(cc.y));
+          if (qp) *reinterpret_cast<float2*>(qp + (int64_t)i * M) = qq;
+          if (cp) *reinterpret_cast<float2*>(cp + (int64_t)i * M) = cc;
+          store_op2<OpT>(qop, io + (int64_t)i * ldop, qq);
+          store_op2<OpT>(kop, io + (int64_t)i * ldop, kk);
         }
         kk = rv;
       }
@@ -695,9 +749,12 @@ __global__ void __launch_bounds__(32 * WARPS)
   if (k0 < n_items) cluster_wait_acquire();
 }
 
-// Backward with q and c rebuilt from the r tile (the RECOMPUTE form of stats_bwd_tma_kernel).
+// Backward with q and c rebuilt from the r tile (kernel.py:139-180 and the shift-add of :232).
 // Stage layout: dqf (R rows), dk (R + 1 rows), r (R + 1 rows from position cta_t0 - 1), dq_out (R
 // rows, when given). part_dg gets one partial per CTA (its items' sum); part_dw one row per (b, rank).
+// As in the forward, a thread holds two adjacent slots of half of its warp's SEG rows; the halves are
+// joined with lam^(SEG/2): the first half's forward total carried into the second half, the second
+// half's reverse total into the first.
 template <int SEG, int WARPS, int STAGES>
 __global__ void __launch_bounds__(32 * WARPS, 2)
     stats_bwd_pipe_kernel(const __grid_constant__ CUtensorMap map_dqf, const __grid_constant__ CUtensorMap map_dqo,
@@ -706,17 +763,19 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
                           float* __restrict__ dr, float* __restrict__ part_dw, double* __restrict__ part_dg, int B,
                           int T, int M, int has_dqo, int fast_identity) {
   pdl_enter();
+  static_assert(SEG % 2 == 0, "two half-segments per warp");
   constexpr int R = SEG * WARPS;
+  constexpr int H = SEG / 2;
   constexpr int TILE = R * 32;
   extern __shared__ __align__(128) float tile[];
   __shared__ __align__(8) uint64_t full[STAGES];
   __shared__ __align__(8) uint64_t xbar_f[2];  // lower ranks' forward totals of the item have arrived
   __shared__ __align__(8) uint64_t xbar_r[2];  // higher ranks' reverse totals have arrived
-  __shared__ float warp_sum[WARPS][32];     // reverse partial sums of the current item
-  __shared__ float warp_sum_f[2][WARPS][32];  // forward partial sums, by item parity
-  __shared__ float warp_dw[WARPS][32];
-  __shared__ float ctot_f[2][SCAN_MAX_CLUSTER][32];
-  __shared__ float ctot_r[2][SCAN_MAX_CLUSTER][32];
+  __shared__ __align__(16) float warp_sum[WARPS][32];     // reverse partial sums of the current item
+  __shared__ __align__(16) float warp_sum_f[2][WARPS][32];  // forward partial sums, by item parity
+  __shared__ __align__(16) float warp_dw[WARPS][32];
+  __shared__ __align__(16) float ctot_f[2][SCAN_MAX_CLUSTER][32];
+  __shared__ __align__(16) float ctot_r[2][SCAN_MAX_CLUSTER][32];
   __shared__ double red_dg[32 * WARPS];
   __shared__ float sinv[2][R + 1];  // row scales of the current and the next item
   __shared__ int ok_flag;
@@ -725,6 +784,8 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
   const int C = (int)cluster.num_blocks();
   const int cr = (int)cluster.block_rank();
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int half = lane >> 4, s2 = (lane & 15) * 2;  // rows [half * H, half * H + H) of the warp; slots s2, s2 + 1
+  const int rh = wp * SEG + half * H;                // this thread's first row within the CTA's R
   const int cta_t0 = cr * R;
   const int nmb = (M + 31) / 32;
   const int n_items = B * nmb;
@@ -765,18 +826,24 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
   cluster_sync_all();
   const float gg = *g;
   const float lam = expf(gg);
+  const float lam_h = expf(gg * (float)H);
   const float lam_seg = expf(gg * (float)SEG);
   const float lam_cta = expf(gg * (float)R);
   const float t_mid = 0.5f * (float)(T - 1);
-  const int t0 = cta_t0 + wp * SEG;
-  const int o = (wp * SEG) * 32 + lane;
+  const int t0 = cta_t0 + rh;
+  const int o = rh * 32 + s2;
   double dg_acc = 0.0;
-  float w_cur = 0.f;
+  auto load_w = [&](int item) {
+    const int m0 = (item % nmb) * 32 + s2;
+    return m0 < M ? make_float2(w[m0], w[m0 + 1]) : make_float2(0.f, 0.f);  // M % 4 == 0: both or neither
+  };
+  float2 w_cur = make_float2(0.f, 0.f);
+  float2 lo_cur = make_float2(0.f, 0.f);  // the first half's forward total of the current item
   // Forward part of item jn: wait for its tile, rescan the write addresses k of this CTA's rows from
-  // zero (warp_sum_f) and send the CTA's total into the higher ranks' slot jn & 1. Item jn + 1's
-  // forward part runs during item jn (after its reverse totals are sent), so the forward exchange
-  // is complete by the time item jn + 1 needs it.
-  auto forward_part = [&](int jn) {
+  // zero (warp_sum_f) and send the CTA's total into the higher ranks' slot jn & 1; returns the first
+  // half's total for the second half's lanes. Item jn + 1's forward part runs during item jn (after
+  // its reverse totals are sent), so the forward exchange is complete by the time item jn + 1 needs it.
+  auto forward_part = [&](int jn) -> float2 {
     if (!mbar_wait_bounded(&full[jn % STAGES], (uint32_t)(jn / STAGES) & 1u,
                            ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
@@ -784,11 +851,18 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
     }
     __syncthreads();  // the tile and this item's row scales are visible to every thread
     const float* s_kn = tile + (jn % STAGES) * stage_floats + 2 * TILE + 32 + o;
-    const float* sin = sinv[jn & 1] + wp * SEG;
-    float run = 0.f;
+    const float* sin = sinv[jn & 1] + rh;
+    float2 run = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) run = fmaf(lam, run, s_kn[i * 32] * sin[i]);
-    warp_sum_f[jn & 1][wp][lane] = run;
+    for (int i = 0; i < H; ++i) {
+      const float2 k2 = *reinterpret_cast<const float2*>(s_kn + i * 32);
+      const float sv = sin[i];
+      run.x = fmaf(lam, run.x, k2.x * sv);
+      run.y = fmaf(lam, run.y, k2.y * sv);
+    }
+    const float2 lo = make_float2(__shfl_sync(0xffffffffu, run.x, lane & 15), __shfl_sync(0xffffffffu, run.y, lane & 15));
+    if (half)
+      *reinterpret_cast<float2*>(&warp_sum_f[jn & 1][wp][s2]) = make_float2(fmaf(lam_h, lo.x, run.x), fmaf(lam_h, lo.y, run.y));
     __syncthreads();
     if (wp == 0) {
       float tot = 0.f;
@@ -796,124 +870,192 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
       const uint32_t slot = smem_u32(&ctot_f[jn & 1][cr][lane]), xb = smem_u32(&xbar_f[jn & 1]);
       for (int jj = cr + 1; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
     }
+    return lo;
   };
   if (k0 < n_items) {
-    const int m_first = (k0 % nmb) * 32 + lane;
-    w_cur = m_first < M ? w[m_first] : 0.f;
+    w_cur = load_w(k0);
     den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
-    forward_part(0);
+    lo_cur = forward_part(0);
   }
   for (int j = 0;; ++j) {
     const int item = k0 + j * G;
     if (item >= n_items) break;
     const int b = item / nmb;
-    const int m = (item % nmb) * 32 + lane;
-    const bool valid = m < M;
+    const int m0 = (item % nmb) * 32 + s2;
+    const bool valid = m0 < M;
     const int xp = j & 1;
     const uint32_t xph = (uint32_t)(j >> 1) & 1u;
     const float* st = tile + (j % STAGES) * stage_floats;
     // the next item's row scales and prior masses: loaded now, used from its forward part on
     const int item_n = item + G;
     const bool has_next = item_n < n_items;
-    const int m_n = (item_n % nmb) * 32 + lane;
     const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
-    const float w_n = (has_next && m_n < M) ? w[m_n] : 0.f;
+    const float2 w_n = has_next ? load_w(item_n) : make_float2(0.f, 0.f);
     const float* s_dqf = st + o;
     const float* s_dk = st + TILE + o;
     const float* s_k = st + 2 * TILE + 32 + o;  // k_t = r_{t-1}
     const float* s_r = st + 2 * TILE + 64 + o;  // r_t
     const float* s_dqo = st + 3 * TILE + 64 + o;
-    const float* si = sinv[j & 1] + wp * SEG;  // si[i]: scale of k row i, si[i + 1]: of r row i
-    const float wm = w_cur;
+    const float* si = sinv[j & 1] + rh;  // si[i]: scale of k row i, si[i + 1]: of r row i
+    const float2 wm = w_cur;
 
-    // carry of the forward scan into this warp's rows: lower ranks' totals, then lower warps'
+    // carry of the forward scan into this thread's rows: lower ranks' totals, lower warps', then
+    // (second half) the first half's
     if (cr > 0 && !mbar_wait_bounded(&xbar_f[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
       ok_flag = 0;
     }
-    float n = 0.f;
-    for (int jj = 0; jj < cr; ++jj) n = fmaf(n, lam_cta, ctot_f[xp][jj][lane]);
-    for (int jj = 0; jj < wp; ++jj) n = fmaf(n, lam_seg, warp_sum_f[xp][jj][lane]);
+    float2 n = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int jj = 0; jj < SCAN_MAX_CLUSTER; ++jj)
+      if (jj < cr) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&ctot_f[xp][jj][s2]);
+        n.x = fmaf(n.x, lam_cta, t2.x);
+        n.y = fmaf(n.y, lam_cta, t2.y);
+      }
+#pragma unroll
+    for (int jj = 0; jj < WARPS; ++jj)
+      if (jj < wp) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&warp_sum_f[xp][jj][s2]);
+        n.x = fmaf(n.x, lam_seg, t2.x);
+        n.y = fmaf(n.y, lam_seg, t2.y);
+      }
+    if (half) {
+      n.x = fmaf(lam_h, n.x, lo_cur.x);
+      n.y = fmaf(lam_h, n.y, lo_cur.y);
+    }
     __syncthreads();  // every thread is past the wait on xbar_f[xp]
     if (threadIdx.x == 0 && cr > 0) mbar_arrive_expect_tx(&xbar_f[xp], (uint32_t)cr * 128u);
 
-    float dw_acc = 0.f, dg_f = 0.f;
-    float drd_v[SEG], dc_v[SEG];
+    float2 dw_acc = make_float2(0.f, 0.f);
+    float dg_f = 0.f;
+    float2 drd_v[H], dc_v[H];
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) {
+    for (int i = 0; i < H; ++i) {
       const int t = t0 + i;
-      n = fmaf(lam, n, s_k[i * 32] * si[i]);
-      float cc = wm + n;
-      float inv = fast_rcp(cc);
-      float qq = (s_r[i * 32] * si[i + 1]) * inv;
-      if (!(t < T && valid)) {
-        cc = 1.f;
-        qq = 0.f;
-        inv = 1.f;
+      const bool live = t < T && valid;
+      const float2 k2 = *reinterpret_cast<const float2*>(s_k + i * 32);
+      const float2 r2 = *reinterpret_cast<const float2*>(s_r + i * 32);
+      const float2 dqfv = *reinterpret_cast<const float2*>(s_dqf + i * 32);
+      const float2 dqov = has_dqo ? *reinterpret_cast<const float2*>(s_dqo + i * 32) : make_float2(0.f, 0.f);
+      const float sk = si[i], sr = si[i + 1];
+      n.x = fmaf(lam, n.x, k2.x * sk);
+      n.y = fmaf(lam, n.y, k2.y * sk);
+      float cx = wm.x + n.x, cy = wm.y + n.y;
+      float ix = fast_rcp(cx), iy = fast_rcp(cy);
+      float qx = (r2.x * sr) * ix, qy = (r2.y * sr) * iy;
+      if (!live) {
+        cx = cy = 1.f;
+        qx = qy = 0.f;
+        ix = iy = 1.f;
       }
-      const float dqfv = s_dqf[i * 32];
-      const float dq = dqfv + (has_dqo ? s_dqo[i * 32] : 0.f);
-      const float drd = dq * inv;
-      const float dc = -drd * qq;
-      drd_v[i] = drd;
-      dc_v[i] = dc;
-      dw_acc += dc;
-      float term = dc * (cc - wm);
-      if (fast_identity) term += qq * dqfv;
-      dg_f = fmaf((float)t - t_mid, term, dg_f);
+      const float drx = (dqfv.x + dqov.x) * ix, dry = (dqfv.y + dqov.y) * iy;
+      const float dcx = -drx * qx, dcy = -dry * qy;
+      drd_v[i] = make_float2(drx, dry);
+      dc_v[i] = make_float2(dcx, dcy);
+      dw_acc.x += dcx;
+      dw_acc.y += dcy;
+      float tx = dcx * (cx - wm.x), ty = dcy * (cy - wm.y);
+      if (fast_identity) {
+        tx += qx * dqfv.x;
+        ty += qy * dqfv.y;
+      }
+      dg_f = fmaf((float)t - t_mid, tx, dg_f);
+      dg_f = fmaf((float)t - t_mid, ty, dg_f);
     }
-    float run = 0.f;
+    // this thread's reverse sum over its rows; the warp's = the first half's + lam^H x the second's
+    float2 run = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int i = SEG - 1; i >= 0; --i) run = fmaf(lam, run, dc_v[i]);
-    warp_sum[wp][lane] = run;
-    warp_dw[wp][lane] = dw_acc;
+    for (int i = H - 1; i >= 0; --i) {
+      run.x = fmaf(lam, run.x, dc_v[i].x);
+      run.y = fmaf(lam, run.y, dc_v[i].y);
+    }
+    const int up = (lane & 15) + 16;
+    const float2 hi = make_float2(__shfl_sync(0xffffffffu, run.x, up), __shfl_sync(0xffffffffu, run.y, up));
+    const float2 dw_hi = make_float2(__shfl_sync(0xffffffffu, dw_acc.x, up), __shfl_sync(0xffffffffu, dw_acc.y, up));
+    if (!half) {
+      *reinterpret_cast<float2*>(&warp_sum[wp][s2]) = make_float2(fmaf(lam_h, hi.x, run.x), fmaf(lam_h, hi.y, run.y));
+      *reinterpret_cast<float2*>(&warp_dw[wp][s2]) = make_float2(dw_acc.x + dw_hi.x, dw_acc.y + dw_hi.y);
+    }
     __syncthreads();
     if (wp == 0) {
       float tot = 0.f;
       for (int jj = WARPS - 1; jj >= 0; --jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
       const uint32_t slot = smem_u32(&ctot_r[xp][cr][lane]), xb = smem_u32(&xbar_r[xp]);
       for (int jj = 0; jj < cr; ++jj) st_async_f32(mapa_shared(slot, jj), tot, mapa_shared(xb, jj));
-      if (valid) {
-        float s2 = 0.f;
-        for (int jj = 0; jj < WARPS; ++jj) s2 += warp_dw[jj][lane];
-        part_dw[((int64_t)b * C + cr) * M + m] = s2;
+      const int ml = (item % nmb) * 32 + lane;
+      if (ml < M) {
+        float sdw = 0.f;
+        for (int jj = 0; jj < WARPS; ++jj) sdw += warp_dw[jj][lane];
+        part_dw[((int64_t)b * C + cr) * M + ml] = sdw;
       }
     }
+    float2 lo_n = make_float2(0.f, 0.f);
     if (has_next) {
       den_store(sinv[(j + 1) & 1], den, den_n, T, cta_t0 - 1, R);  // last read in item j - 1
-      forward_part(j + 1);
+      lo_n = forward_part(j + 1);
     }
     if (cr < C - 1 && !mbar_wait_bounded(&xbar_r[xp], xph, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
       ok_flag = 0;
     }
-    float carry = 0.f;  // dkc at position t0 + SEG
-    for (int jj = C - 1; jj > cr; --jj) carry = fmaf(carry, lam_cta, ctot_r[xp][jj][lane]);
-    for (int jj = WARPS - 1; jj > wp; --jj) carry = fmaf(carry, lam_seg, warp_sum[jj][lane]);
+    // dkc just past this thread's rows: higher ranks' totals, higher warps', then (first half) the
+    // second half's
+    float2 carry = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int jj = SCAN_MAX_CLUSTER - 1; jj >= 0; --jj)
+      if (jj < C && jj > cr) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&ctot_r[xp][jj][s2]);
+        carry.x = fmaf(carry.x, lam_cta, t2.x);
+        carry.y = fmaf(carry.y, lam_cta, t2.y);
+      }
+#pragma unroll
+    for (int jj = WARPS - 1; jj >= 0; --jj)
+      if (jj > wp) {
+        const float2 t2 = *reinterpret_cast<const float2*>(&warp_sum[jj][s2]);
+        carry.x = fmaf(carry.x, lam_seg, t2.x);
+        carry.y = fmaf(carry.y, lam_seg, t2.y);
+      }
+    if (!half) {
+      carry.x = fmaf(lam_h, carry.x, hi.x);
+      carry.y = fmaf(lam_h, carry.y, hi.y);
+    }
     dg_acc += (double)dg_f;
     if (valid) {
-      const int64_t base = (int64_t)b * T * M + m;
-      const int t_end = t0 + SEG;
-      float dkt_next = (t_end < T) ? s_dk[SEG * 32] + carry : 0.f;  // the dk tile holds row t_end
+      const int64_t base = (int64_t)b * T * M + m0;
+      const int t_end = t0 + H;
+      float2 dkt_next = make_float2(0.f, 0.f);  // dk_total of the row after this thread's last one
+      if (t_end < T) {
+        const float2 d2 = *reinterpret_cast<const float2*>(s_dk + H * 32);  // the dk tile holds row t_end
+        dkt_next = make_float2(d2.x + carry.x, d2.y + carry.y);
+      }
       run = carry;
       float dg_s = 0.f;
 #pragma unroll
-      for (int i = SEG - 1; i >= 0; --i) {
+      for (int i = H - 1; i >= 0; --i) {
         const int t = t0 + i;
         if (t < T) {
-          const float dkv = s_dk[i * 32];
-          const float kv = s_k[i * 32] * si[i];
-          run = fmaf(lam, run, dc_v[i]);  // dkc_t
-          dr[base + (int64_t)t * M] = drd_v[i] + dkt_next;
-          dkt_next = dkv + run;
-          float term = -kv * run;
-          if (fast_identity) term -= kv * dkv;
-          dg_s = fmaf((float)t - t_mid, term, dg_s);
+          const float2 dkv = *reinterpret_cast<const float2*>(s_dk + i * 32);
+          const float2 k2 = *reinterpret_cast<const float2*>(s_k + i * 32);
+          const float kx = k2.x * si[i], ky = k2.y * si[i];
+          run.x = fmaf(lam, run.x, dc_v[i].x);  // dkc_t
+          run.y = fmaf(lam, run.y, dc_v[i].y);
+          *reinterpret_cast<float2*>(dr + base + (int64_t)t * M) =
+              make_float2(drd_v[i].x + dkt_next.x, drd_v[i].y + dkt_next.y);
+          dkt_next = make_float2(dkv.x + run.x, dkv.y + run.y);
+          float tx = -kx * run.x, ty = -ky * run.y;
+          if (fast_identity) {
+            tx -= kx * dkv.x;
+            ty -= ky * dkv.y;
+          }
+          dg_s = fmaf((float)t - t_mid, tx, dg_s);
+          dg_s = fmaf((float)t - t_mid, ty, dg_s);
         }
       }
       dg_acc += (double)dg_s;
     }
     w_cur = w_n;
+    lo_cur = lo_n;
     __syncthreads();  // this item's stage, sinv[j & 1], warp_sum and warp_dw are free again
     if (threadIdx.x == 0) {
       if (cr < C - 1) mbar_arrive_expect_tx(&xbar_r[xp], (uint32_t)(C - 1 - cr) * 128u);
