@@ -230,6 +230,74 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The address backward with each row held in registers: a CTA's 8 warps form two row groups of
+// four warps, each warp holding a quarter of the row (NV4 16-byte loads per lane and array), so a
+// row is read from HBM once, all its loads in flight together, and da is computed from the
+// registers. The quarter sums meet in shared memory (a named barrier per group) and are added in
+// quarter order; per element the arithmetic is addr_bwd_kernel's. Needs M % 16 == 0 and
+// M / 4 <= 128 * NV4.
+template <int NV4>
+__global__ void __launch_bounds__(256)
+    addr_bwd_rows_kernel(const float* __restrict__ dr, const float* __restrict__ r, const float* __restrict__ den,
+                         int unnormalised, void* __restrict__ da, int da_dtype, int64_t ld_da,
+                         float* __restrict__ deps_part, int64_t rows, int M, int rows_per_cta) {
+  pdl_enter();
+  __shared__ float qsum[2][4];
+  __shared__ float deps_g[2];
+  const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = wp >> 2, qt = wp & 3;  // row group, quarter of the row
+  const int Mq = M >> 2;
+  float deps_acc = 0.f;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
+  for (int rr = grp; rr < rows_per_cta; rr += 2) {
+    const int64_t row = row0 + rr;
+    if (row >= rows) break;  // the group's four warps leave together
+    const float* drr = dr + row * M + qt * Mq;
+    const float* rrow = r + row * M + qt * Mq;
+    const float dn = den[row];
+    float4 a[NV4], c[NV4];
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int m = (i * 32 + lane) * 4;
+      if (m < Mq) {
+        a[i] = *reinterpret_cast<const float4*>(drr + m);
+        c[i] = *reinterpret_cast<const float4*>(rrow + m);
+      } else {
+        a[i] = c[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i)
+      s = fmaf(a[i].x, c[i].x, fmaf(a[i].y, c[i].y, fmaf(a[i].z, c[i].z, fmaf(a[i].w, c[i].w, s))));
+    s = warp_sum(s);
+    if (lane == 0) qsum[grp][qt] = s;
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
+    s = ((qsum[grp][0] + qsum[grp][1]) + qsum[grp][2]) + qsum[grp][3];
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");  // qsum is free for the group's next row
+    const float inv = 1.0f / dn;
+    // z scale: sqrt(z) = sqrt(x * zs) with zs = den for normalised rows, 1 for z rows
+    const float zs = unnormalised ? 1.f : dn;
+    if (unnormalised) s *= inv;
+    deps_acc -= s * inv;
+#pragma unroll
+    for (int i = 0; i < NV4; ++i) {
+      const int m = (i * 32 + lane) * 4;
+      if (m < Mq) {
+        float4 o;
+        o.x = 2.f * sqrtf(c[i].x * zs) * ((a[i].x - s) * inv);
+        o.y = 2.f * sqrtf(c[i].y * zs) * ((a[i].y - s) * inv);
+        o.z = 2.f * sqrtf(c[i].z * zs) * ((a[i].z - s) * inv);
+        o.w = 2.f * sqrtf(c[i].w * zs) * ((a[i].w - s) * inv);
+        st4(da, row * ld_da + qt * Mq + m, o, da_dtype);
+      }
+    }
+  }
+  if (qt == 0 && lane == 0) deps_g[grp] = deps_acc;
+  __syncthreads();
+  if (threadIdx.x == 0) deps_part[blockIdx.x] = deps_g[0] + deps_g[1];
+}
+
 // column sums of a bf16 (rows x cols) array over chunks of rows, part[chunk][col]: a CTA covers
 // 256 columns (8 per lane, one 16-byte load per row: a warp reads 512 contiguous bytes) of one chunk;
 // warp w adds rows w, w + 8, ... of the chunk in order, then the warps' sums are added in warp order.
@@ -623,9 +691,27 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
   const int64_t rows = B * T;
   AddrBwdWork wk = carve_addr_work(work, B, T, D, M, dt);
   // da and the d eps partials, then db = column sums of da
-  if (int rc = launch_pdl(addr_bwd_kernel, dim3((unsigned)wk.ctas), dim3(256), 0, st, dr, r, den, normalized ? 0 : 1,
-                          wk.da, dt, wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA))
-    return rc;
+  {
+    const int unnorm = normalized ? 0 : 1;
+    const dim3 grid((unsigned)wk.ctas);
+    int rc;
+    // rows in registers when a quarter row fits in 8 16-byte loads per lane
+    if (M % 16 == 0 && M <= 4096) {
+      const int64_t nv = cdiv(M / 4, 128);
+      rc = nv <= 1   ? launch_pdl(addr_bwd_rows_kernel<1>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
+                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
+           : nv <= 2 ? launch_pdl(addr_bwd_rows_kernel<2>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
+                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
+           : nv <= 4 ? launch_pdl(addr_bwd_rows_kernel<4>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
+                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
+                     : launch_pdl(addr_bwd_rows_kernel<8>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
+                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
+    } else {
+      rc = launch_pdl(addr_bwd_kernel, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt, wk.ld_m, wk.deps_part,
+                      rows, (int)M, ADDR_ROWS_PER_CTA);
+    }
+    if (rc) return rc;
+  }
   // du = da K and the conv backward stay on the caller's stream (launched first); db, deps and
   // dK = da^T u run beside them on the side stream
   cudaStream_t side = nullptr;

@@ -538,6 +538,7 @@ __global__ void __launch_bounds__(32 * WARPS)
 // going with short limits, so its peers are never left waiting.
 
 constexpr uint64_t SCAN_SHORT_WAIT_NS = 10000000ull;  // waits after an error: 10 ms
+constexpr int SCAN_RING = 4;  // dealt items in flight per CTA of the forward scan
 
 // Row scales of the next item, in two steps so that the global load's latency overlaps the current
 // item: thread i (i <= n) loads den of row t_first + i early (den_prefetch) and stores the scale
@@ -567,12 +568,17 @@ __device__ __forceinline__ void store_op2<__nv_bfloat16>(void* base, int64_t idx
 // SEG consecutive rows of the CTA's R; a thread holds two adjacent slots of SEG / 2 of those rows
 // (lanes 0-15 the first half, lanes 16-31 the second), so every shared-memory load and global
 // store moves two slots. The warp's total is the second half's plus lam^(SEG/2) times the first's.
+// Items: a cluster's first STAGES items are fixed (k0, k0 + G, ...); with `tickets` the rest are
+// handed out in arrival order by rank 0 of each cluster (a global ticket, sent to every rank of the
+// cluster through shared memory), so clusters that run faster take more items; without, every
+// item is fixed (k0 + j G).
 template <int SEG, int WARPS, int STAGES, typename OpT>
 __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 registers
     stats_fwd_pipe_kernel(const __grid_constant__ CUtensorMap map_r, const __grid_constant__ CUtensorMap map_r1,
                           const float* __restrict__ den, const float* __restrict__ w, const float* __restrict__ g,
                           float* __restrict__ q, float* __restrict__ c, void* __restrict__ qop,
-                          void* __restrict__ kop, int64_t ldop, int B, int T, int M) {
+                          void* __restrict__ kop, int64_t ldop, int B, int T, int M,
+                          unsigned int* __restrict__ tickets) {
   pdl_enter();
   static_assert(SEG % 2 == 0, "two half-segments per warp");
   constexpr int R = SEG * WARPS;
@@ -585,7 +591,11 @@ __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 regi
   __shared__ __align__(16) float ctot[SCAN_MAX_CLUSTER][32];
   __shared__ float sinv[2][R + 1];  // row scales of the current and the next item
   __shared__ int ok_flag;
+  __shared__ int ring_item[SCAN_RING];  // items of iterations STAGES, STAGES + 1, ... (use u: slot u % SCAN_RING)
+  __shared__ __align__(8) uint64_t ring_bar[SCAN_RING];
+  __shared__ int dealt[SCAN_RING];  // the same items, stored by thread 0 once received: read after a CTA barrier
   static_assert(32 * WARPS > R, "one thread per row scale");
+  static_assert(SCAN_RING >= STAGES + 2, "rank 0 runs at most one item ahead of its peers");
   cg::cluster_group cluster = cg::this_cluster();
   const int C = (int)cluster.num_blocks();
   const int cr = (int)cluster.block_rank();
@@ -596,8 +606,13 @@ __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 regi
   const int n_items = B * nmb;
   const int G = (int)gridDim.x / C;
   const int k0 = (int)blockIdx.x / C;
-  auto issue = [&](int j) {
-    const int item = k0 + j * G;
+  // item of iteration j. Thread 0 stores a dealt item (use j - STAGES) at the end of iteration
+  // j - STAGES; the other threads read it only after the next CTA barrier: as the current item at the
+  // top of iteration j, as the next item after the first barrier of iteration j - 1.
+  auto item_of = [&](int j) -> int {
+    return (j < STAGES || !tickets) ? k0 + j * G : dealt[(j - STAGES) % SCAN_RING];
+  };
+  auto issue = [&](int j, int item) {
     if (item >= n_items) return;
     const int bb = item / nmb, mm0 = (item % nmb) * 32;
     float* st = tile + (j % STAGES) * STAGE_FLOATS;
@@ -609,13 +624,16 @@ __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 regi
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     mbar_init(&xbar, 1);
+    for (int s = 0; s < SCAN_RING; ++s) mbar_init(&ring_bar[s], 1);
     fence_barrier_init();
     if (cr > 0) mbar_arrive_expect_tx(&xbar, (uint32_t)cr * 128u);  // armed for the first item
+    for (int s = 0; s < SCAN_RING; ++s) mbar_arrive_expect_tx(&ring_bar[s], 4u);  // armed for uses 0 .. SCAN_RING - 1
     ok_flag = 1;
   }
   __syncthreads();
   if (threadIdx.x == 0)
-    for (int j = 0; j < STAGES; ++j) issue(j);
+    for (int j = 0; j < STAGES; ++j) issue(j, k0 + j * G);
+  bool dealt_out = false;  // rank 0, thread 0: the ticket ran past the last item
   // the barriers of every CTA are initialised before any CTA sends into them
   __syncwarp();
   cluster_sync_all();
@@ -635,22 +653,22 @@ __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 regi
     den_store(sinv[0], den, den_prefetch(den, k0 / nmb, T, cta_t0 - 1, R), T, cta_t0 - 1, R);
   }
   for (int j = 0;; ++j) {
-    const int item = k0 + j * G;
+    const int item = item_of(j);
     if (item >= n_items) break;
     const int b = item / nmb;
     const int m0 = (item % nmb) * 32 + s2;
     const float* xs = tile + (j % STAGES) * STAGE_FLOATS;
-    // the next item's row scales and prior masses: loaded now, used after this item
-    const int item_n = item + G;
-    const bool has_next = item_n < n_items;
-    const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
-    const float2 w_n = has_next ? load_w(item_n) : make_float2(0.f, 0.f);
     const uint64_t lim = ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS;
     if (!mbar_wait_bounded(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, lim)) {
       raise_device_error(DEVERR_SCAN_TMA_WAIT);
       ok_flag = 0;
     }
-    __syncthreads();
+    __syncthreads();  // also orders thread 0's store of the next item (end of the previous iteration)
+    // the next item's row scales and prior masses: loaded now, used after this item
+    const int item_n = item_of(j + 1);
+    const bool has_next = item_n < n_items;
+    const float den_n = has_next ? den_prefetch(den, item_n / nmb, T, cta_t0 - 1, R) : 0.f;
+    const float2 w_n = has_next ? load_w(item_n) : make_float2(0.f, 0.f);
     // xt[i * 32]: k of position t0 + i (the r row before it), xt[(i + 1) * 32]: r of t0 + i
     const int rh = wp * SEG + half * H;
     const float* xt = xs + rh * 32 + s2;
@@ -740,8 +758,43 @@ __global__ void __launch_bounds__(32 * WARPS, 6)  // six CTAs per SM: <= 40 regi
     w_cur = w_n;
     __syncthreads();  // the stage, sinv[j & 1] and warp_sum are free again
     if (threadIdx.x == 0) {
+      int it = k0 + (j + STAGES) * G;
+      if (tickets) {  // ring use j: the item of iteration j + STAGES
+        const int sl = j % SCAN_RING;
+        if (cr == 0) {  // rank 0 deals: the next ticket, to every rank of the cluster
+          int v = n_items;
+          if (!dealt_out) {
+            v = STAGES * G + (int)atomicAdd(&tickets[0], 1u);
+            if (v >= n_items) {
+              v = n_items;
+              dealt_out = true;
+              // the last cluster to run out resets the pair for a later launch
+              if (atomicAdd(&tickets[1], 1u) == (unsigned)(G - 1)) {
+                atomicExch(&tickets[0], 0u);
+                atomicExch(&tickets[1], 0u);
+              }
+            }
+          }
+          const uint32_t slot = smem_u32(&ring_item[sl]), rb = smem_u32(&ring_bar[sl]);
+          for (int jj = 0; jj < C; ++jj) st_async_f32(mapa_shared(slot, jj), __int_as_float(v), mapa_shared(rb, jj));
+        }
+        it = n_items;
+        if (mbar_wait_bounded(&ring_bar[sl], (uint32_t)(j / SCAN_RING) & 1u, ok_flag ? 2000000000ull : SCAN_SHORT_WAIT_NS)) {
+          it = ring_item[sl];
+          if (it != n_items && (it < STAGES * G || it > n_items)) {  // neither a dealt item nor the end mark
+            raise_device_error(DEVERR_SCAN_TMA_WAIT);
+            ok_flag = 0;
+            it = n_items;
+          }
+        } else {
+          raise_device_error(DEVERR_SCAN_TMA_WAIT);
+          ok_flag = 0;
+        }
+        dealt[sl] = it;
+        mbar_arrive_expect_tx(&ring_bar[sl], 4u);  // armed for use j + SCAN_RING
+      }
       fence_proxy_async_smem();
-      issue(j + STAGES);
+      issue(j + STAGES, it);
     }
   }
   // pairs the last arrive; no CTA leaves while a peer may still send into its shared memory
@@ -1137,6 +1190,39 @@ static int g_scan_mode = 1;
 constexpr int SCAN_PIPE_STAGES = 2;  // backward: two stages of up to 66 KB
 constexpr int SCAN_FWD_STAGES = 2;   // forward: two stages of 16.5 KB (more CTAs per SM beat a deeper ring)
 
+// Ticket pairs (next ticket, clusters done) of the forward scan's item dealing, per device. Each
+// launch takes the next pair of the ring; the last cluster of a launch resets its pair, so a pair
+// is reused only SCAN_TICKET_PAIRS launches later, long after the launch that used it has ended.
+constexpr int SCAN_TICKET_PAIRS = 4096;
+__device__ unsigned int g_scan_tickets[SCAN_TICKET_PAIRS][2];
+
+// The pair for the next launch on stream st; NULL (fixed items) while st is being captured into a
+// graph, which may be replayed on several streams at once.
+unsigned int* scan_tickets(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return nullptr;
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return nullptr;
+  static std::mutex mu;
+  static unsigned int* base[64] = {};
+  static unsigned int next[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (!base[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_scan_tickets) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    base[dev] = static_cast<unsigned int*>(p);
+  }
+  const unsigned int k = next[dev]++ % SCAN_TICKET_PAIRS;
+  return base[dev] + 2 * k;
+}
+
 // Clusters of a persistent scan that fit on the device at once (cached per device, kernel and
 // shared-memory size), at most n_items.
 template <typename K>
@@ -1363,10 +1449,11 @@ int stats_fwd_run(const float* r, const float* den, const float* w, const float*
       if (int rc = bf ? pipe_clusters(kb, 256, C, smem_p, n_items, &nc) : pipe_clusters(kf, 256, C, smem_p, n_items, &nc))
         return rc;
       const dim3 pgrid((unsigned)(nc * C));
+      unsigned int* tk = scan_tickets(st);
       return bf ? launch_cluster_smem(kb, pgrid, 256, C, smem_p, st, mr, mr1, den, w, g, q, c, qop, kop, ld_op, (int)B,
-                                      (int)T, (int)M)
+                                      (int)T, (int)M, tk)
                 : launch_cluster_smem(kf, pgrid, 256, C, smem_p, st, mr, mr1, den, w, g, q, c, qop, kop, ld_op, (int)B,
-                                      (int)T, (int)M);
+                                      (int)T, (int)M, tk);
     }
     if (tp.warps == 8)
       return bf ? launch_cluster_smem(stats_fwd_tma_kernel<16, 8, __nv_bfloat16>, grid, 256, C, smem, st, mr, mr1, den, w,
