@@ -423,7 +423,7 @@ def bench_model(dev, name, steps, warmup, world, rank, bucket_mb=25):
         net(dtok[:, :-1], dtok[:, 1:])
         model.last_loss.backward()
         opt.step()
-        opt.zero_grad(set_to_none=False)
+        opt.zero_grad(set_to_none=True)  # as train.py:287
         loss_host.copy_(model.last_loss.detach(), non_blocking=True)
 
     for i in range(warmup):

@@ -330,12 +330,14 @@ int ulm_mixer_bwd(const void* dy, int dy_dtype, const float* z, const float* den
  * the backward needs it). */
 int ulm_rms_norm_fwd(const void* x, int x_dtype, const float* weight, void* y, int y_dtype, float* rstd,
                      int64_t rows, int64_t D, float eps, void* stream);
-/* Backward of ulm_rms_norm_fwd from dy (rows, D) of dy_dtype: dx (rows, D) fp32, dweight (D,) fp32
- * (overwritten; summed over rows in a fixed order). work: ulm_rms_norm_bwd_work_bytes(rows, D)
- * bytes. D * 32 bytes must fit the backward's shared memory (D <= 6400). */
+/* Backward of ulm_rms_norm_fwd from dy (rows, D) of dy_dtype: dx (rows, D) fp32, plus dx_add
+ * (rows, D) fp32 when not NULL (the gradient the input receives along another path, such as a
+ * residual connection, added as dx is written), dweight (D,) fp32 (overwritten; summed over rows in
+ * a fixed order). work: ulm_rms_norm_bwd_work_bytes(rows, D) bytes. D * 32 bytes must fit the
+ * backward's shared memory (D <= 6400). */
 int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int x_dtype, const float* weight,
-                     const float* rstd, float* dx, float* dweight, void* work, int64_t rows, int64_t D,
-                     void* stream);
+                     const float* rstd, float* dx, const float* dx_add, float* dweight, void* work, int64_t rows,
+                     int64_t D, void* stream);
 int64_t ulm_rms_norm_bwd_work_bytes(int64_t rows, int64_t D);
 
 /* y = x W^T (nn.Linear without bias; UnifiedBlock.val, model.py:65, 81): x (N, K) of x_dtype, weight
@@ -344,11 +346,11 @@ int64_t ulm_rms_norm_bwd_work_bytes(int64_t rows, int64_t D);
  * backward reads. */
 int ulm_linear_fwd(const void* x, int x_dtype, const float* weight, void* x_op, void* w_op, void* y, int y_dtype,
                    int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
-/* Backward of ulm_linear_fwd from dy (N, Nout) of dy_dtype: dx (N, K) fp32 = dy W, dw (Nout, K)
- * fp32 = dy^T x (split over the rows, partials summed in a fixed order). work:
- * ulm_linear_bwd_work_bytes(N, K, Nout, prec) bytes. */
-int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx, float* dw,
-                   void* work, int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
+/* Backward of ulm_linear_fwd from dy (N, Nout) of dy_dtype: dx (N, K) fp32 = dy W (+ dx_add (N, K)
+ * fp32 when not NULL, added in the product's epilogue), dw (Nout, K) fp32 = dy^T x (split over the
+ * rows, partials summed in a fixed order). work: ulm_linear_bwd_work_bytes(N, K, Nout, prec) bytes. */
+int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx, const float* dx_add,
+                   float* dw, void* work, int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
 int64_t ulm_linear_bwd_work_bytes(int64_t N, int64_t K, int64_t Nout, int prec);
 
 /* ---- batched recurrent decode (model.py:88-111, 164-175; run.c:121-265) --------------------- */

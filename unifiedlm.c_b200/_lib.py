@@ -56,10 +56,10 @@ SIGNATURES = {
     "ulm_mixer_bwd": (_I, [_P, _I] + [_P] * 20 + [_I, _P, _P, _P] + [_P, _I64, _P, _I, _P, _I64, _P, _I64] +
                       [_P] * 6 + [_I64] * 4 + [_I, _P]),
     "ulm_rms_norm_fwd": (_I, [_P, _I, _P, _P, _I, _P, _I64, _I64, ctypes.c_float, _P]),
-    "ulm_rms_norm_bwd": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _P]),
+    "ulm_rms_norm_bwd": (_I, [_P, _I, _P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _P]),
     "ulm_rms_norm_bwd_work_bytes": (_I64, [_I64, _I64]),
     "ulm_linear_fwd": (_I, [_P, _I, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I, _P]),
-    "ulm_linear_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
+    "ulm_linear_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_linear_bwd_work_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "ulm_lm_head_loss_fwd": (_I, [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_lm_head_loss_bwd": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _P]),

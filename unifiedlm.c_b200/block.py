@@ -22,6 +22,8 @@ from . import _lib as L
 from .kernel import (PRECISION, _op_dtype, _require_cuda, bwd_work_buffer, combine_fwd_fake, combine_fwd_raw,
                      memory_fwd_fake, memory_fwd_raw, operand_copy, operand_ld, operand_or_input, unaliased)
 from .prologue import address_bwd_fake, address_fwd_fake, address_fwd_raw
+from .norm import (_linear_fwd_fake, _rms_norm_fwd_fake, linear_bwd_raw, linear_fwd_raw, rms_norm_bwd_raw,
+                   rms_norm_fwd_raw)
 
 _OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
              torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]
@@ -262,4 +264,112 @@ def block_mixer(x, h, conv_weight, key_weight, key_bias, eps, v, g, w, mu_weight
     y, *_ = torch.ops.ulm.mixer_fwd(xx.contiguous(), hh.contiguous(), conv_weight, key_weight, key_bias,
                                     eps.float().reshape(()), vv.contiguous(), g.float().reshape(()),
                                     w.float().contiguous(), mu_weight.float().contiguous(), PRECISION[precision])
+    return y.to(x.dtype)
+
+
+# ---- UnifiedBlock.forward as one op (model.py:76-85 without dropout) -----------------------------
+# x feeds both the norm and the residual, h both the val projection and the mixer; as one op the
+# backward adds those gradients where they are produced (the val product's epilogue adds the
+# mixer's dh, the norm backward adds the residual's dy as it writes dx) instead of in separate sums.
+
+_BLOCK_OUT = tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                   torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                   torch.Tensor, torch.Tensor]
+
+
+@torch.library.custom_op("ulm::block_fwd", mutates_args=())
+def block_fwd(x: torch.Tensor, norm_w: torch.Tensor, conv_w: torch.Tensor, key_w: torch.Tensor, key_b: torch.Tensor,
+              eps: torch.Tensor, val_w: torch.Tensor, g: torch.Tensor, w: torch.Tensor, mu: torch.Tensor,
+              norm_eps: float, precision: int) -> _BLOCK_OUT:
+    """Returns (y, h, rstd, v, x_op, wv_op, z, den, u_op, kw, q, c, qop, kop, vop, P); all but y are
+    saved for the backward (v in bf16 for bf16 products, as the reference's autocast gives it)."""
+    h, rstd = rms_norm_fwd_raw(x, norm_w, norm_eps)
+    v, x_op, wv_op = linear_fwd_raw(h, val_w, precision, precision == PRECISION["bf16"])
+    z, den, u_op, kw = address_fwd_raw(h, conv_w, key_w, key_b, eps, precision, normalize=False)
+    y, q, c, qop, kop, vop, P = combine_fwd_raw(z, den, v, g, w, mu, x, precision)
+    return y, h, rstd, v, x_op, wv_op, z, den, u_op, kw, q, c, qop, kop, unaliased(vop, v), P
+
+
+@block_fwd.register_fake
+def _block_fwd_fake(x, norm_w, conv_w, key_w, key_b, eps, val_w, g, w, mu, norm_eps, precision):
+    h, rstd = _rms_norm_fwd_fake(x, norm_w, norm_eps)
+    v, x_op, wv_op = _linear_fwd_fake(h, val_w, precision, precision == PRECISION["bf16"])
+    z, den, u_op, kw = address_fwd_fake(h, key_w, precision)
+    y, q, c, qop, kop, vop, P = combine_fwd_fake(z, v, x, precision)
+    return y, h, rstd, v, x_op, wv_op, z, den, u_op, kw, q, c, qop, kop, vop, P
+
+
+@torch.library.custom_op("ulm::block_bwd", mutates_args=())
+def block_bwd(dy: torch.Tensor, x: torch.Tensor, norm_w: torch.Tensor, rstd: torch.Tensor, h: torch.Tensor,
+              conv_w: torch.Tensor, g: torch.Tensor, w: torch.Tensor, mu: torch.Tensor, z: torch.Tensor,
+              den: torch.Tensor, u_op: torch.Tensor, kw: torch.Tensor, q: torch.Tensor, c: torch.Tensor,
+              qop: torch.Tensor, kop: torch.Tensor, vop: torch.Tensor, P: torch.Tensor, x_op: torch.Tensor,
+              wv_op: torch.Tensor, v_dtype: torch.dtype, precision: int
+              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
+                         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (dx fp32, dnorm_w, dconv_w, dkey_w, dkey_b, deps, dval_w, dg, dw, dmu), fp32."""
+    D = x.shape[-1]
+    dh_mix, dconv, dkw, dkb, deps, dv, dg, dw, dmu = mixer_bwd_raw(dy, h, conv_w, g, w, mu, z, den, u_op, kw, q, c,
+                                                                   qop, kop, vop, P, v_dtype, precision)
+    # dh = dv W_v + the mixer's dh (added in the product's epilogue)
+    dh, dval = linear_bwd_raw(dv.reshape(-1, D), x_op, wv_op, D, precision, dx_add=dh_mix.reshape(-1, D))
+    # dx = the norm's backward + the residual's dy (added as dx is written)
+    dx, dnorm = rms_norm_bwd_raw(dh.reshape(x.shape), x, norm_w, rstd, dx_add=dy.float().contiguous())
+    return dx, dnorm, dconv, dkw, dkb, deps, dval, dg, dw, dmu
+
+
+@block_bwd.register_fake
+def _block_bwd_fake(dy, x, norm_w, rstd, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, x_op, wv_op,
+                    v_dtype, precision):
+    dh, dconv, dkw, dkb, deps = address_bwd_fake(h, z, conv_w)
+    M, D = z.shape[-1], x.shape[-1]
+    f32 = torch.float32
+    return (x.new_empty(x.shape, dtype=f32), x.new_empty(D, dtype=f32), dconv, dkw, dkb, deps,
+            x.new_empty(wv_op.shape[0], D, dtype=f32), z.new_empty((), dtype=f32), z.new_empty(M, dtype=f32),
+            z.new_empty(mu.shape, dtype=f32))
+
+
+def _blk_setup(ctx, inputs, output):
+    x, norm_w, conv_w, key_w, key_b, eps, val_w, g, w, mu, norm_eps, precision = inputs
+    y, h, rstd, v, x_op, wv_op, z, den, u_op, kw, q, c, qop, kop, vop, P = output
+    ctx.save_for_backward(x, norm_w, rstd, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop,
+                          operand_or_input(vop, v), P, x_op, wv_op)
+    ctx.precision = precision
+    ctx.v_dtype = v.dtype
+    ctx.dtypes = (x.dtype, norm_w.dtype, conv_w.dtype, key_w.dtype, key_b.dtype, eps.dtype, val_w.dtype, mu.dtype)
+    ctx.g_shape = g.shape
+    ctx.mark_non_differentiable(h, rstd, v, x_op, wv_op, z, den, u_op, kw, q, c, qop, kop, vop, P)
+    ctx.set_materialize_grads(False)
+
+
+def _blk_backward(ctx, dy, *unused):
+    if dy is None:
+        return (None,) * 12
+    (x, norm_w, rstd, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, x_op,
+     wv_op) = ctx.saved_tensors
+    xd, nd, cd, kd, bd, ed, vwd, md = ctx.dtypes
+    dx, dnorm, dconv, dkw, dkb, deps, dval, dg, dw, dmu = block_bwd(
+        dy.contiguous(), x, norm_w, rstd, h, conv_w, g, w, mu, z, den, u_op, kw, q, c, qop, kop, vop, P, x_op, wv_op,
+        ctx.v_dtype, ctx.precision)
+    return (dx.to(xd), dnorm.to(nd), dconv.to(cd), dkw.to(kd), dkb.to(bd), deps.to(ed), dval.to(vwd),
+            dg.reshape(ctx.g_shape), dw, dmu.to(md), None, None)
+
+
+torch.library.register_autograd("ulm::block_fwd", _blk_backward, setup_context=_blk_setup)
+
+
+def unified_block(x, norm_weight, norm_eps, conv_weight, key_weight, key_bias, eps, val_weight, g, w, mu_weight,
+                  precision="bf16"):
+    """UnifiedBlock.forward without dropout (model.py:76-85): h = RMSNorm(x), v = val(h) (bf16 for
+    bf16 products), y = x + mu(q w) + fast with (q, fast) = unified_memory(address(h, ...), v, g, w),
+    in x's dtype."""
+    for t in (x, norm_weight, val_weight, g, w, mu_weight):
+        if not t.is_cuda:
+            raise RuntimeError("unified_block runs on CUDA tensors only (no CPU path)")
+    xx = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+    nw = norm_weight if norm_weight.dtype in (torch.float32, torch.bfloat16) else norm_weight.float()
+    y, *_ = torch.ops.ulm.block_fwd(xx.contiguous(), nw.contiguous(), conv_weight, key_weight, key_bias,
+                                    eps.float().reshape(()), val_weight.float().contiguous(), g.float().reshape(()),
+                                    w.float().contiguous(), mu_weight.float().contiguous(), float(norm_eps),
+                                    PRECISION[precision])
     return y.to(x.dtype)

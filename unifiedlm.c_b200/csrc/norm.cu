@@ -61,13 +61,13 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
   }
 }
 
-// dx (fp32) and one dweight partial row per CTA (part[blockIdx.x][D]); the CTA's warps take rows
+// dx (fp32, plus dx_add when given) and one dweight partial row per CTA (part[blockIdx.x][D]); the CTA's warps take rows
 // blockIdx.x * NORM_WARPS + warp, then every gridDim.x * NORM_WARPS rows, and keep their column sums
 // in shared memory (D floats per warp), added in warp order at the end.
 __global__ void __launch_bounds__(32 * NORM_WARPS)
     rms_norm_bwd_kernel(const void* __restrict__ dy, int dydt, const void* __restrict__ x, int xdt,
                         const float* __restrict__ weight, const float* __restrict__ rstd, float* __restrict__ dx,
-                        float* __restrict__ part, int64_t rows, int D) {
+                        const float* __restrict__ dx_add, float* __restrict__ part, int64_t rows, int D) {
   pdl_enter();
   extern __shared__ float colsum[];  // NORM_WARPS x D
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -87,7 +87,8 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
     for (int i = lane; i < D; i += 32) {
       const float g = load_as_float(dy, dydt, base + i);
       const float xh = load_as_float(x, xdt, base + i) * rs;
-      dx[base + i] = rs * (g * weight[i] - xh * dot);
+      const float d = rs * (g * weight[i] - xh * dot);
+      dx[base + i] = dx_add ? d + dx_add[base + i] : d;
     }
   }
   __syncthreads();
@@ -137,8 +138,8 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
 template <int NV>
 __global__ void __launch_bounds__(32 * NORM_WARPS)
     rms_norm_bwd_vec_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ weight,
-                            const float* __restrict__ rstd, float* __restrict__ dx, float* __restrict__ part,
-                            int64_t rows, int D) {
+                            const float* __restrict__ rstd, float* __restrict__ dx,
+                            const float* __restrict__ dx_add, float* __restrict__ part, int64_t rows, int D) {
   pdl_enter();
   extern __shared__ float colsum[];  // NORM_WARPS x D
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -175,8 +176,13 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
       const int i = lane + 32 * j;
       if (i < D4) {
         const float4 w = w4[i];
-        dr[i] = make_float4(rs * (g[j].x * w.x - xh[j].x * dot), rs * (g[j].y * w.y - xh[j].y * dot),
-                            rs * (g[j].z * w.z - xh[j].z * dot), rs * (g[j].w * w.w - xh[j].w * dot));
+        float4 d = make_float4(rs * (g[j].x * w.x - xh[j].x * dot), rs * (g[j].y * w.y - xh[j].y * dot),
+                               rs * (g[j].z * w.z - xh[j].z * dot), rs * (g[j].w * w.w - xh[j].w * dot));
+        if (dx_add) {
+          const float4 a = reinterpret_cast<const float4*>(dx_add + r * D)[i];
+          d = make_float4(d.x + a.x, d.y + a.y, d.z + a.z, d.w + a.w);
+        }
+        dr[i] = d;
       }
     }
   }
@@ -193,16 +199,8 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
   }
 }
 
-// out[i] = sum over p < nparts of part[p][i], in order
-__global__ void sum_rows_kernel(const float* __restrict__ part, int nparts, int64_t n, float* __restrict__ out) {
-  pdl_enter();
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float t = 0.f;
-  for (int p = 0; p < nparts; ++p) t += part[(int64_t)p * n + i];
-  out[i] = t;
-}
-
+// CTAs of the RMSNorm kernels: enough rows in flight, at most four CTAs per SM (each writes one
+// partial dweight row in the backward)
 int norm_grid(int64_t rows) {
   const int dev = current_device();
   const int64_t cap = 4LL * (dev >= 0 ? sm_count(dev) : 148);
@@ -242,8 +240,8 @@ extern "C" int64_t ulm_rms_norm_bwd_work_bytes(int64_t rows, int64_t D) {
 }
 
 extern "C" int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int x_dtype, const float* weight,
-                                const float* rstd, float* dx, float* dweight, void* work, int64_t rows, int64_t D,
-                                void* stream) {
+                                const float* rstd, float* dx, const float* dx_add, float* dweight, void* work,
+                                int64_t rows, int64_t D, void* stream) {
   ULM_REQUIRE(rows >= 0 && D >= 0, "negative extent");
   ULM_REQUIRE((x_dtype == ULM_F32 || x_dtype == ULM_BF16) && (dy_dtype == ULM_F32 || dy_dtype == ULM_BF16),
               "x_dtype and dy_dtype must be ULM_F32 or ULM_BF16");
@@ -263,22 +261,22 @@ extern "C" int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int
     ULM_CUDA_TRY(cudaFuncSetAttribute(rms_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   float* part = static_cast<float*>(work);
   const bool vec = x_dtype == ULM_F32 && dy_dtype == ULM_F32 && D % 4 == 0 && D <= 128 * 8 && is_aligned16(x) &&
-                   is_aligned16(dy) && is_aligned16(dx) && is_aligned16(weight);
+                   is_aligned16(dy) && is_aligned16(dx) && is_aligned16(weight) && (!dx_add || is_aligned16(dx_add));
   if (vec) {
     const float* xf = static_cast<const float*>(x);
     const float* gf = static_cast<const float*>(dy);
     auto kern = D <= 128 * 4 ? rms_norm_bwd_vec_kernel<4> : rms_norm_bwd_vec_kernel<8>;
     if (smem > 48 * 1024)
       ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (int rc = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, gf, xf, weight, rstd, dx, part,
-                            rows, (int)D))
+    if (int rc = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, gf, xf, weight, rstd, dx,
+                            dx_add, part, rows, (int)D))
       return rc;
   } else if (int rc = launch_pdl(rms_norm_bwd_kernel, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, dy,
-                                 dy_dtype, x, x_dtype, weight, rstd, dx, part, rows, (int)D)) {
+                                 dy_dtype, x, x_dtype, weight, rstd, dx, dx_add, part, rows, (int)D)) {
     return rc;
   }
-  return launch_pdl(sum_rows_kernel, dim3((unsigned)cdiv(D, 256)), dim3(256), 0, st, (const float*)part, grid, D,
-                    dweight);
+  // dweight = the CTAs' partial rows summed in a fixed order (a tree over the parts: there are many)
+  return sum_parts(static_cast<const float*>(part), grid, D, dweight, st);
 }
 
 // ---- Linear -------------------------------------------------------------------------------------
@@ -316,8 +314,9 @@ extern "C" int64_t ulm_linear_bwd_work_bytes(int64_t N, int64_t K, int64_t Nout,
   return align256(N * ulm_operand_ld(Nout) * es) + 8 * Nout * K * (int64_t)sizeof(float);
 }
 
-extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx, float* dw,
-                              void* work, int64_t N, int64_t K, int64_t Nout, int prec, void* stream) {
+extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx,
+                              const float* dx_add, float* dw, void* work, int64_t N, int64_t K, int64_t Nout, int prec,
+                              void* stream) {
   ULM_REQUIRE(prec == ULM_PREC_BF16 || prec == ULM_PREC_FP32, "prec must be ULM_PREC_BF16 or ULM_PREC_FP32");
   ULM_REQUIRE(dy_dtype == ULM_F32 || dy_dtype == ULM_BF16, "dy_dtype must be ULM_F32 or ULM_BF16");
   ULM_REQUIRE(N >= 0 && K >= 0 && Nout >= 0, "negative extent");
@@ -326,7 +325,10 @@ extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, co
   if (K == 0) return ULM_OK;
   ULM_REQUIRE(dx && dw, "null pointer argument");
   if (N == 0 || Nout == 0) {
-    if (N > 0) ULM_CUDA_TRY(cudaMemsetAsync(dx, 0, N * K * sizeof(float), st));
+    if (N > 0 && dx_add)
+      ULM_CUDA_TRY(cudaMemcpyAsync(dx, dx_add, N * K * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    else if (N > 0)
+      ULM_CUDA_TRY(cudaMemsetAsync(dx, 0, N * K * sizeof(float), st));
     if (Nout > 0) ULM_CUDA_TRY(cudaMemsetAsync(dw, 0, Nout * K * sizeof(float), st));
     return ULM_OK;
   }
@@ -341,7 +343,13 @@ extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, co
     Operand A{dy_op, ldo, N * ldo, Nout, N, dt, false};
     Operand Bw{w_op, ldk, Nout * ldk, K, Nout, dt, true};
     GemmShape s{1, (int)N, (int)K, (int)Nout, CAUSAL_NONE};
-    GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, dx, K, 0, nullptr);
+    GemmEpilogue e = make_epilogue(dx_add ? EPI_STORE_ADD : EPI_STORE, ULM_F32, dx, K, 0, nullptr);
+    if (dx_add) {  // dx = dy W + dx_add in the product's epilogue
+      e.aux = dx_add;
+      e.ld_aux = K;
+      e.aux_bstride = 0;
+      e.vec_ok = e.vec_ok && is_aligned16(dx_add);
+    }
     if (int rc = run_gemm(A, Bw, s, e, st)) return rc;
   }
   // dW[o][k] = sum_n dy[n][o] x[n][k], split K over the rows so the few output tiles fill the GPU
@@ -352,8 +360,6 @@ extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, co
   s.ksplit = S;
   GemmEpilogue e = make_epilogue(EPI_STORE, ULM_F32, S > 1 ? part : dw, K, Nout * K, nullptr);
   if (int rc = run_gemm(A, Bx, s, e, st)) return rc;
-  if (S > 1)
-    return launch_pdl(sum_rows_kernel, dim3((unsigned)cdiv(Nout * K, 256)), dim3(256), 0, st, (const float*)part, S,
-                      Nout * K, dw);
+  if (S > 1) return sum_parts(static_cast<const float*>(part), S, Nout * K, dw, st);
   return ULM_OK;
 }

@@ -13,6 +13,9 @@
 
 #include "gemm.cuh"
 
+// fixed-order sums of partial arrays (address.cu)
+int sum_parts(const float* part, int64_t nparts, int64_t n, float* out, cudaStream_t st);
+
 namespace ulm {
 
 constexpr int STATS_SEGS = 8;
@@ -1268,16 +1271,6 @@ int pipe_clusters(K kernel, int threads, int C, size_t smem, int64_t n_items, in
   return ULM_OK;
 }
 
-// dw[m] = sum over the R partial rows of part_dw[.][m], in row order.
-__global__ void stats_bwd_dw_kernel(const float* __restrict__ part_dw, float* __restrict__ dw, int R, int M) {
-  pdl_enter();
-  const int m = blockIdx.x * blockDim.x + threadIdx.x;
-  if (m < M) {
-    float s = 0.f;
-    for (int i = 0; i < R; ++i) s += part_dw[(int64_t)i * M + m];
-    dw[m] = s;
-  }
-}
 
 // dg = sum of part_dg (n1 doubles) + sum of extra (n2 floats): one block, every thread sums a fixed
 // strided subset in order, then a fixed-shape tree. Deterministic for given inputs.
@@ -1395,9 +1388,8 @@ int stats_bwd_run(const float* dqf, const float* dq_out, const float* dk, const 
     if (int rc = stream_after(red_st, st)) return rc;
     rs = red_st;
   }
-  if (int rc = launch_pdl(stats_bwd_dw_kernel, dim3((unsigned)cdiv(M, 256)), dim3(256), 0, rs, (const float*)sc.part_dw,
-                          dw, (int)dw_rows, (int)M))
-    return rc;
+  // dw = the (b, rank) partial rows summed in a fixed order (a tree when there are many)
+  if (int rc = ::sum_parts(static_cast<const float*>(sc.part_dw), dw_rows, M, dw, rs)) return rc;
   if (int rc = launch_pdl(stats_bwd_dg_kernel, dim3(1), dim3(256), 0, rs, (const double*)sc.part_dg, n_dg,
                           tile_partials, tile_partials ? n_tiles : (int64_t)0, dg))
     return rc;

@@ -6,9 +6,10 @@ state_dicts, checkpoints and the model.bin exporter interoperate unchanged; the 
 libulm_b200.so:
 
 * UnifiedBlock.forward (model.py:77-85): RMSNorm, the val projection and the whole mixing span
-  (conv -> key -> relu^2 code -> fast memory -> mu(q w) + residual) as library ops
-  (`norm.rms_norm`, `norm.linear`, `block.block_mixer`); with dropout active in training the
-  combine stays a separate product so the dropout mask can sit between it and the residual.
+  (conv -> key -> relu^2 code -> fast memory -> mu(q w) + residual) as one library op
+  (`block.unified_block`, whose backward adds the residual's and the two paths' gradients inside its
+  kernels); with dropout active in training they run as separate ops (`norm.rms_norm`,
+  `norm.linear`, `block.addressed_memory`) so the dropout mask can sit before the residual.
 * UnifiedBlock.init_state / step (model.py:88-111) and UnifiedLM.forward_recurrent (:164-175): the
   batched decode kernels (ulm_decode_*), the same state dict (buf, U, c, r_prev) kept in fp32.
 * UnifiedLM.forward with `fused_head`: output Linear + cross entropy without the logits
@@ -27,7 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib as L
-from .block import addressed_memory, block_mixer
+from .block import addressed_memory, unified_block
 from .head import lm_head_loss
 from .kernel import CHUNK
 from .norm import linear, rms_norm
@@ -105,15 +106,15 @@ class UnifiedBlock(nn.Module):
         return z / (self._eps() + z.sum(-1, keepdim=True))
 
     def forward(self, x):
-        h = self.norm(x)
-        # v in bf16 with the tensor-core products (as under the reference's bf16 autocast): the fast
-        # memory rounds it to its bf16 operand copy anyway, so it is written once in that form
-        v = linear(h, self.val.weight, precision=self.precision,
-                   out_dtype=torch.bfloat16 if self.precision == "bf16" else None)
         w, g, eps = self._w(), self._g(), self._eps()
         if self.dropout.p == 0.0 or not self.training:
-            return block_mixer(x, h, self.conv.weight, self.key.weight, self.key.bias, eps, v, g, w,
-                               self.mu.weight, precision=self.precision)
+            # norm, val, addressing, fast memory and combine as one op (v in bf16 with the
+            # tensor-core products, as under the reference's bf16 autocast)
+            return unified_block(x, self.norm.weight, self.norm.eps, self.conv.weight, self.key.weight,
+                                 self.key.bias, eps, self.val.weight, g, w, self.mu.weight, precision=self.precision)
+        h = self.norm(x)
+        v = linear(h, self.val.weight, precision=self.precision,
+                   out_dtype=torch.bfloat16 if self.precision == "bf16" else None)
         q, fast = addressed_memory(h, self.conv.weight, self.key.weight, self.key.bias, eps, v, g, w,
                                    precision=self.precision)
         return x + self.dropout(self.mu((q * w).type_as(x)) + fast.type_as(x))

@@ -12,9 +12,8 @@ from . import _lib as L
 from .kernel import PRECISION, _op_dtype, _require_cuda, operand_ld
 
 
-@torch.library.custom_op("ulm::rms_norm_fwd", mutates_args=())
-def rms_norm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
-    """Returns (y, rstd); y in promote(x, weight) type, rstd (rows,) fp32 saved for the backward."""
+def rms_norm_fwd_raw(x, weight, eps):
+    """ulm_rms_norm_fwd on fresh buffers: (y in promote(x, weight) type, rstd (rows,) fp32)."""
     _require_cuda(x, weight)
     D = x.shape[-1]
     rows = x.numel() // max(D, 1)
@@ -26,6 +25,12 @@ def rms_norm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float) -> tuple[tor
     return y, rstd
 
 
+@torch.library.custom_op("ulm::rms_norm_fwd", mutates_args=())
+def rms_norm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (y, rstd); y in promote(x, weight) type, rstd (rows,) fp32 saved for the backward."""
+    return rms_norm_fwd_raw(x, weight, eps)
+
+
 @rms_norm_fwd.register_fake
 def _rms_norm_fwd_fake(x, weight, eps):
     D = x.shape[-1]
@@ -34,10 +39,8 @@ def _rms_norm_fwd_fake(x, weight, eps):
             x.new_empty(rows, dtype=torch.float32))
 
 
-@torch.library.custom_op("ulm::rms_norm_bwd", mutates_args=())
-def rms_norm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor
-                 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Returns (dx fp32, dweight fp32)."""
+def rms_norm_bwd_raw(dy, x, weight, rstd, dx_add=None):
+    """ulm_rms_norm_bwd on fresh buffers: (dx fp32 (+ dx_add fp32 when given), dweight fp32)."""
     D = x.shape[-1]
     rows = x.numel() // max(D, 1)
     dx = torch.empty(x.shape, device=x.device, dtype=torch.float32)
@@ -45,9 +48,16 @@ def rms_norm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: 
     work = torch.empty(int(L.lib().ulm_rms_norm_bwd_work_bytes(rows, D)), device=x.device, dtype=torch.uint8)
     with torch.cuda.device(x.device):
         L.check(L.lib().ulm_rms_norm_bwd(L.ptr(dy), L.dtype_code(dy.dtype), L.ptr(x), L.dtype_code(x.dtype),
-                                         L.ptr(weight), L.ptr(rstd), L.ptr(dx), L.ptr(dw), L.ptr(work), rows, D,
-                                         L.stream_of(x)))
+                                         L.ptr(weight), L.ptr(rstd), L.ptr(dx), L.ptr(dx_add), L.ptr(dw),
+                                         L.ptr(work), rows, D, L.stream_of(x)))
     return dx, dw
+
+
+@torch.library.custom_op("ulm::rms_norm_bwd", mutates_args=())
+def rms_norm_bwd(dy: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (dx fp32, dweight fp32)."""
+    return rms_norm_bwd_raw(dy, x, weight, rstd)
 
 
 @rms_norm_bwd.register_fake
@@ -84,11 +94,8 @@ def rms_norm(x, weight, eps):
 
 # ---- Linear --------------------------------------------------------------------------------------
 
-@torch.library.custom_op("ulm::linear_fwd", mutates_args=())
-def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int, out_bf16: bool
-               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Returns (y, x_op, w_op); y in x's type or bf16 (out_bf16); the operand copies are saved for
-    the backward."""
+def linear_fwd_raw(x, weight, precision, out_bf16):
+    """ulm_linear_fwd on fresh buffers: (y, x_op, w_op)."""
     _require_cuda(x, weight)
     K = x.shape[-1]
     N = x.numel() // max(K, 1)
@@ -103,6 +110,14 @@ def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int, out_bf16: 
     return y, x_op, w_op
 
 
+@torch.library.custom_op("ulm::linear_fwd", mutates_args=())
+def linear_fwd(x: torch.Tensor, weight: torch.Tensor, precision: int, out_bf16: bool
+               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Returns (y, x_op, w_op); y in x's type or bf16 (out_bf16); the operand copies are saved for
+    the backward."""
+    return linear_fwd_raw(x, weight, precision, out_bf16)
+
+
 @linear_fwd.register_fake
 def _linear_fwd_fake(x, weight, precision, out_bf16):
     K = x.shape[-1]
@@ -113,10 +128,9 @@ def _linear_fwd_fake(x, weight, precision, out_bf16):
             x.new_empty(weight.shape[0], operand_ld(K), dtype=opt))
 
 
-@torch.library.custom_op("ulm::linear_bwd", mutates_args=())
-def linear_bwd(dy: torch.Tensor, x_op: torch.Tensor, w_op: torch.Tensor, K: int, precision: int
-               ) -> tuple[torch.Tensor, torch.Tensor]:
-    """Returns (dx fp32 (N, K), dweight fp32 (Nout, K))."""
+def linear_bwd_raw(dy, x_op, w_op, K, precision, dx_add=None):
+    """ulm_linear_bwd on fresh buffers: (dx fp32 (N, K) (+ dx_add fp32 (N, K) when given), dweight
+    fp32 (Nout, K))."""
     Nout = w_op.shape[0]
     N = x_op.shape[0]
     dx = torch.empty(N, K, device=dy.device, dtype=torch.float32)
@@ -125,8 +139,16 @@ def linear_bwd(dy: torch.Tensor, x_op: torch.Tensor, w_op: torch.Tensor, K: int,
                        dtype=torch.uint8)
     with torch.cuda.device(dy.device):
         L.check(L.lib().ulm_linear_bwd(L.ptr(dy), L.dtype_code(dy.dtype), L.ptr(x_op), L.ptr(w_op), L.ptr(dx),
-                                       L.ptr(dw), L.ptr(work), N, K, Nout, precision, L.stream_of(dy)))
+                                       L.ptr(dx_add), L.ptr(dw), L.ptr(work), N, K, Nout, precision,
+                                       L.stream_of(dy)))
     return dx, dw
+
+
+@torch.library.custom_op("ulm::linear_bwd", mutates_args=())
+def linear_bwd(dy: torch.Tensor, x_op: torch.Tensor, w_op: torch.Tensor, K: int, precision: int
+               ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns (dx fp32 (N, K), dweight fp32 (Nout, K))."""
+    return linear_bwd_raw(dy, x_op, w_op, K, precision)
 
 
 @linear_bwd.register_fake
