@@ -234,9 +234,17 @@ __global__ void __launch_bounds__(256)
 // four warps, each warp holding a quarter of the row (NV4 16-byte loads per lane and array), so a
 // row is read from HBM once, all its loads in flight together, and da is computed from the
 // registers. The quarter sums meet in shared memory (a named barrier per group) and are added in
-// quarter order; per element the arithmetic is addr_bwd_kernel's. Needs M % 16 == 0 and
-// M / 4 <= 128 * NV4.
-template <int NV4>
+// quarter order (each warp's sum is formed from NV4 independent partial sums); da per element is
+// addr_bwd_kernel's arithmetic. Needs M % 16 == 0 and M / 4 <= 128 * NV4; FULL: M / 4 == 128 * NV4.
+// named barrier of one four-warp row group (ids 1 and 2; literal ids keep the CTA at three barriers)
+__device__ __forceinline__ void group_bar(int grp) {
+  if (grp == 0)
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  else
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+}
+
+template <int NV4, bool FULL>
 __global__ void __launch_bounds__(256)
     addr_bwd_rows_kernel(const float* __restrict__ dr, const float* __restrict__ r, const float* __restrict__ den,
                          int unnormalised, void* __restrict__ da, int da_dtype, int64_t ld_da,
@@ -259,22 +267,25 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
       const int m = (i * 32 + lane) * 4;
-      if (m < Mq) {
+      if (FULL || m < Mq) {
         a[i] = *reinterpret_cast<const float4*>(drr + m);
         c[i] = *reinterpret_cast<const float4*>(rrow + m);
       } else {
         a[i] = c[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-    float s = 0.f;
+    // one partial sum per 16-byte load (independent chains), added in load order
+    float sp[NV4];
 #pragma unroll
-    for (int i = 0; i < NV4; ++i)
-      s = fmaf(a[i].x, c[i].x, fmaf(a[i].y, c[i].y, fmaf(a[i].z, c[i].z, fmaf(a[i].w, c[i].w, s))));
+    for (int i = 0; i < NV4; ++i) sp[i] = fmaf(a[i].x, c[i].x, fmaf(a[i].y, c[i].y, fmaf(a[i].z, c[i].z, a[i].w * c[i].w)));
+    float s = sp[0];
+#pragma unroll
+    for (int i = 1; i < NV4; ++i) s += sp[i];
     s = warp_sum(s);
     if (lane == 0) qsum[grp][qt] = s;
-    asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");
+    group_bar(grp);
     s = ((qsum[grp][0] + qsum[grp][1]) + qsum[grp][2]) + qsum[grp][3];
-    asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory");  // qsum is free for the group's next row
+    group_bar(grp);  // qsum is free for the group's next row
     const float inv = 1.0f / dn;
     // z scale: sqrt(z) = sqrt(x * zs) with zs = den for normalised rows, 1 for z rows
     const float zs = unnormalised ? 1.f : dn;
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < NV4; ++i) {
       const int m = (i * 32 + lane) * 4;
-      if (m < Mq) {
+      if (FULL || m < Mq) {
         float4 o;
         o.x = 2.f * sqrtf(c[i].x * zs) * ((a[i].x - s) * inv);
         o.y = 2.f * sqrtf(c[i].y * zs) * ((a[i].y - s) * inv);
@@ -698,14 +709,15 @@ extern "C" int ulm_address_bwd(const float* dr, const float* r, const float* den
     // rows in registers when a quarter row fits in 8 16-byte loads per lane
     if (M % 16 == 0 && M <= 4096) {
       const int64_t nv = cdiv(M / 4, 128);
-      rc = nv <= 1   ? launch_pdl(addr_bwd_rows_kernel<1>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
-                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
-           : nv <= 2 ? launch_pdl(addr_bwd_rows_kernel<2>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
-                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
-           : nv <= 4 ? launch_pdl(addr_bwd_rows_kernel<4>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
-                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA)
-                     : launch_pdl(addr_bwd_rows_kernel<8>, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt,
-                                  wk.ld_m, wk.deps_part, rows, (int)M, ADDR_ROWS_PER_CTA);
+      auto go = [&](auto kern) {
+        return launch_pdl(kern, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt, wk.ld_m, wk.deps_part, rows,
+                          (int)M, ADDR_ROWS_PER_CTA);
+      };
+      const bool full = M % 512 == 0 && (M / 512) == (nv <= 1 ? 1 : nv <= 2 ? 2 : nv <= 4 ? 4 : 8);
+      if (nv <= 1) rc = full ? go(addr_bwd_rows_kernel<1, true>) : go(addr_bwd_rows_kernel<1, false>);
+      else if (nv <= 2) rc = full ? go(addr_bwd_rows_kernel<2, true>) : go(addr_bwd_rows_kernel<2, false>);
+      else if (nv <= 4) rc = full ? go(addr_bwd_rows_kernel<4, true>) : go(addr_bwd_rows_kernel<4, false>);
+      else rc = full ? go(addr_bwd_rows_kernel<8, true>) : go(addr_bwd_rows_kernel<8, false>);
     } else {
       rc = launch_pdl(addr_bwd_kernel, grid, dim3(256), 0, st, dr, r, den, unnorm, wk.da, dt, wk.ld_m, wk.deps_part,
                       rows, (int)M, ADDR_ROWS_PER_CTA);

@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
                            const float* __restrict__ conv_w, float* __restrict__ buf, float* __restrict__ h,
                            float* __restrict__ u, __nv_bfloat16* __restrict__ hop, __nv_bfloat16* __restrict__ uop,
                            int64_t ld_op, int D, int K, float norm_eps) {
+  pdl_enter();
   __shared__ float red[33];
   const int b = blockIdx.x;
   const float* xb = x + (int64_t)b * D;
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
     decode_address_kernel(const float* __restrict__ a, const float* __restrict__ key_b, const float* __restrict__ w,
                           const float* __restrict__ lam_p, const float* __restrict__ eps_p, float* __restrict__ c,
                           const float* __restrict__ r_prev, float* __restrict__ r_new, float* __restrict__ q, int M) {
+  pdl_enter();
   __shared__ float red[33];
   const int b = blockIdx.x;
   const float lam = *lam_p, eps = *eps_p;
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
     decode_state_kernel(float* __restrict__ U, const PriorT* __restrict__ prior, const float* __restrict__ v,
                         const float* __restrict__ r_prev, const float* __restrict__ q, const float* __restrict__ lam_p,
                         float* __restrict__ x, int D, int M) {
+  pdl_enter();
   __shared__ float red[DEC_THREADS / 32];
   constexpr int warps = DEC_THREADS / 32;
   const int wp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -198,6 +201,7 @@ __global__ void decode_reset_kernel(const float* __restrict__ mu, const float* _
 }
 
 __global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
+  pdl_enter();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     dst[i] = src[i];
 }
@@ -206,6 +210,7 @@ __global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict
 __global__ void __launch_bounds__(DEC_THREADS)
     decode_final_norm_kernel(const float* __restrict__ x, const float* __restrict__ norm_w, float* __restrict__ xn,
                              __nv_bfloat16* __restrict__ xop, int64_t ld_op, int D, float norm_eps) {
+  pdl_enter();
   __shared__ float red[33];
   const int b = blockIdx.x;
   const float* xb = x + (int64_t)b * D;
@@ -226,6 +231,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
     decode_argmax_embed_kernel(const float* __restrict__ logits, int64_t ld_logits, int V,
                                const void* __restrict__ emb, int emb_bf16, int D, int* __restrict__ next_token,
                                float* __restrict__ x) {
+  pdl_enter();
   __shared__ float bv[DEC_THREADS];
   __shared__ int bi[DEC_THREADS];
   const int b = blockIdx.x;
@@ -264,6 +270,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
 
 __global__ void decode_embed_kernel(const int* __restrict__ tokens, const void* __restrict__ emb, int emb_bf16, int D,
                                     float* __restrict__ x) {
+  pdl_enter();
   const int b = blockIdx.x;
   const int tok = tokens[b];
   for (int i = threadIdx.x; i < D; i += blockDim.x) {
@@ -396,6 +403,7 @@ template <int NB>
 __global__ void __launch_bounds__(32 * GEMV_WARPS)
     decode_gemv_kernel(const float* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ W, int64_t ldw,
                        float* __restrict__ out, int64_t ldo, int B, int N, int K) {
+  pdl_enter();
   extern __shared__ float xs[];  // B x K
   for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
     const int b = i / K, k = i - b * K;
@@ -454,14 +462,16 @@ int decode_gemv(const float* x, int64_t ldx, const __nv_bfloat16* W, int64_t ldw
   if (B <= 4) {
     if (smem > 48 * 1024)
       ULM_CUDA_TRY(cudaFuncSetAttribute(decode_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    decode_gemv_kernel<4><<<(unsigned)grid, 32 * GEMV_WARPS, smem, st>>>(x, ldx, W, ldw, out, ldo, (int)B, (int)N,
-                                                                        (int)K);
+    if (int rc = launch_pdl(decode_gemv_kernel<4>, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, x, ldx, W,
+                            ldw, out, ldo, (int)B, (int)N, (int)K))
+      return rc;
   } else {
     if (smem > 48 * 1024)
       ULM_CUDA_TRY(
           cudaFuncSetAttribute(decode_gemv_kernel<GEMV_MAX_B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    decode_gemv_kernel<GEMV_MAX_B><<<(unsigned)grid, 32 * GEMV_WARPS, smem, st>>>(x, ldx, W, ldw, out, ldo, (int)B,
-                                                                                 (int)N, (int)K);
+    if (int rc = launch_pdl(decode_gemv_kernel<GEMV_MAX_B>, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, x,
+                            ldx, W, ldw, out, ldo, (int)B, (int)N, (int)K))
+      return rc;
   }
   ULM_LAUNCH_CHECK("decode_gemv_kernel");
   return ULM_OK;
@@ -607,6 +617,7 @@ __global__ void __launch_bounds__(SMP_THREADS)
     decode_sample_kernel(const float* __restrict__ logits, int V, float temperature, float topp,
                          unsigned long long* __restrict__ rng, int* __restrict__ next_token,
                          const void* __restrict__ emb, int emb_bf16, int D, float* __restrict__ x) {
+  pdl_enter();
   extern __shared__ float ps[];
   __shared__ float red[33];
   __shared__ uint64_t redk[33];
@@ -758,10 +769,9 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   float* q = reinterpret_cast<float*>(take(B * M * 4));
   __nv_bfloat16* hop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
   __nv_bfloat16* uop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
-  decode_prologue_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(x, norm_w, conv_w, buf, h, u, bf ? hop : nullptr,
-                                                              bf ? uop : nullptr, ldo, (int)D, (int)conv_size,
-                                                              norm_eps);
-  ULM_LAUNCH_CHECK("decode_prologue_kernel");
+  if (int rc = launch_pdl(decode_prologue_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, x, norm_w, conv_w, buf,
+                          h, u, bf ? hop : nullptr, bf ? uop : nullptr, ldo, (int)D, (int)conv_size, norm_eps))
+    return rc;
   if (bf) {
     if (gemv_ok(B, D, D, D, u, key_w) && gemv_ok(B, D, D, D, h, val_w)) {
       if (int rc = decode_gemv(u, D, static_cast<const __nv_bfloat16*>(key_w), D, a, M, B, M, D, st)) return rc;
@@ -774,8 +784,9 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
     if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
     if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
   }
-  decode_address_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(a, key_b, w, lam, eps, c, r_prev, r_new, q, (int)M);
-  ULM_LAUNCH_CHECK("decode_address_kernel");
+  if (int rc = launch_pdl(decode_address_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, a, key_b, w, lam, eps,
+                          c, r_prev, r_new, q, (int)M))
+    return rc;
   const int warps = DEC_THREADS / 32;
   ULM_REQUIRE((B * D) % warps == 0, "B*D must be a multiple of %d", warps);
   // warps per state row: enough rows' loads in flight to cover the SMs at small batches
@@ -783,19 +794,23 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   while (S < warps && B * D * S < 16 * 148 && (int64_t)S * 128 < M) S *= 2;
   const unsigned blocks = (unsigned)(B * D * S / warps);
   auto launch = [&](auto kern, const auto* pr) {
-    kern<<<blocks, DEC_THREADS, 0, st>>>(U, pr, v, r_prev, q, lam, x, (int)D, (int)M);
+    return launch_pdl(kern, dim3(blocks), dim3(DEC_THREADS), 0, st, U, pr, v, r_prev, q, lam, x, (int)D, (int)M);
   };
   const auto* pb = static_cast<const __nv_bfloat16*>(prior);
   const auto* pf = static_cast<const float*>(prior);
-  switch (S) {
-    case 1: bf ? launch(decode_state_kernel<__nv_bfloat16, 1>, pb) : launch(decode_state_kernel<float, 1>, pf); break;
-    case 2: bf ? launch(decode_state_kernel<__nv_bfloat16, 2>, pb) : launch(decode_state_kernel<float, 2>, pf); break;
-    case 4: bf ? launch(decode_state_kernel<__nv_bfloat16, 4>, pb) : launch(decode_state_kernel<float, 4>, pf); break;
-    default: bf ? launch(decode_state_kernel<__nv_bfloat16, 8>, pb) : launch(decode_state_kernel<float, 8>, pf); break;
-  }
-  ULM_LAUNCH_CHECK("decode_state_kernel");
-  copy_f32_kernel<<<(unsigned)std::min<int64_t>(cdiv(B * M, 256), 4 * 148), 256, 0, st>>>(r_new, r_prev, B * M);
-  ULM_LAUNCH_CHECK("copy_f32_kernel");
+  int rc_state;
+  if (S == 1)
+    rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 1>, pb) : launch(decode_state_kernel<float, 1>, pf);
+  else if (S == 2)
+    rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 2>, pb) : launch(decode_state_kernel<float, 2>, pf);
+  else if (S == 4)
+    rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 4>, pb) : launch(decode_state_kernel<float, 4>, pf);
+  else
+    rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 8>, pb) : launch(decode_state_kernel<float, 8>, pf);
+  if (rc_state) return rc_state;
+  if (int rc = launch_pdl(copy_f32_kernel, dim3((unsigned)std::min<int64_t>(cdiv(B * M, 256), 4 * 148)), dim3(256), 0,
+                          st, r_new, r_prev, B * M))
+    return rc;
   return ULM_OK;
 }
 
@@ -808,9 +823,9 @@ extern "C" int ulm_decode_embed(const int* tokens, const void* emb, int emb_dtyp
                                 void* stream) {
   ULM_REQUIRE(tokens && emb && x, "null pointer argument");
   ULM_REQUIRE(weight_dtype_ok(emb_dtype), "emb_dtype must be ULM_F32 or ULM_BF16");
-  decode_embed_kernel<<<(unsigned)B, 128, 0, static_cast<cudaStream_t>(stream)>>>(tokens, emb, emb_dtype == ULM_BF16,
-                                                                                  (int)D, x);
-  ULM_LAUNCH_CHECK("decode_embed_kernel");
+  if (int rc = launch_pdl(decode_embed_kernel, dim3((unsigned)B), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                          tokens, emb, emb_dtype == ULM_BF16, (int)D, x))
+    return rc;
   return ULM_OK;
 }
 
@@ -825,9 +840,9 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   const int64_t ldo = ulm_operand_ld(D);
   float* xn = static_cast<float*>(work);
   __nv_bfloat16* xop = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(work) + (B * D * 4 + 255) / 256 * 256);
-  decode_final_norm_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(x, norm_w, xn, bf ? xop : nullptr, ldo, (int)D,
-                                                                norm_eps);
-  ULM_LAUNCH_CHECK("decode_final_norm_kernel");
+  if (int rc = launch_pdl(decode_final_norm_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, x, norm_w, xn,
+                          bf ? xop : nullptr, ldo, (int)D, norm_eps))
+    return rc;
   if (bf && gemv_ok(B, D, D, D, xn, cls_w)) {
     if (int rc = decode_gemv(xn, D, static_cast<const __nv_bfloat16*>(cls_w), D, logits, V, B, V, D, st)) return rc;
   } else if (bf) {
@@ -835,8 +850,9 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   } else {
     if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) return rc;
   }
-  decode_argmax_embed_kernel<<<(unsigned)B, DEC_THREADS, 0, st>>>(logits, V, (int)V, emb, bf, (int)D, next_token, x);
-  ULM_LAUNCH_CHECK("decode_argmax_embed_kernel");
+  if (int rc = launch_pdl(decode_argmax_embed_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, logits, V, (int)V,
+                          emb, bf, (int)D, next_token, x))
+    return rc;
   return ULM_OK;
 }
 
@@ -855,9 +871,8 @@ extern "C" int ulm_decode_sample(const float* logits, int64_t B, int64_t V, floa
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)V * sizeof(float);
   ULM_CUDA_TRY(cudaFuncSetAttribute(decode_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  decode_sample_kernel<<<(unsigned)B, SMP_THREADS, smem, st>>>(logits, (int)V, temperature, topp, rng_state,
-                                                                next_token, emb, emb_dtype == ULM_BF16 ? 1 : 0,
-                                                                (int)D, x);
-  ULM_LAUNCH_CHECK("decode_sample_kernel");
+  if (int rc = launch_pdl(decode_sample_kernel, dim3((unsigned)B), dim3(SMP_THREADS), smem, st, logits, (int)V,
+                          temperature, topp, rng_state, next_token, emb, emb_dtype == ULM_BF16 ? 1 : 0, (int)D, x))
+    return rc;
   return ULM_OK;
 }
