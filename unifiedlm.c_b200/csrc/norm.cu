@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
 }
 
 template <int NV>
-__global__ void __launch_bounds__(32 * NORM_WARPS)
+__global__ void __launch_bounds__(32 * NORM_WARPS, NV <= 6 ? 2 : 1)  // two CTAs per SM up to NV = 6
     rms_norm_bwd_vec_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ weight,
                             const float* __restrict__ rstd, float* __restrict__ dx,
                             const float* __restrict__ dx_add, float* __restrict__ part, int64_t rows, int D) {
@@ -153,12 +153,14 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
     const float rs = rstd[r];
     const float4* gr = reinterpret_cast<const float4*>(dy + r * D);
     const float4* xr = reinterpret_cast<const float4*>(x + r * D);
-    float4 g[NV], xh[NV];
+    float4 g[NV], xh[NV], ad[NV];
+    const float4* ar = dx_add ? reinterpret_cast<const float4*>(dx_add + r * D) : nullptr;
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int i = lane + 32 * j;
       g[j] = i < D4 ? gr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ad[j] = (dx_add && i < D4) ? ar[i] : make_float4(0.f, 0.f, 0.f, 0.f);
       const float4 xv = i < D4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
       xh[j] = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
       const float4 w = i < D4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -178,10 +180,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS)
         const float4 w = w4[i];
         float4 d = make_float4(rs * (g[j].x * w.x - xh[j].x * dot), rs * (g[j].y * w.y - xh[j].y * dot),
                                rs * (g[j].z * w.z - xh[j].z * dot), rs * (g[j].w * w.w - xh[j].w * dot));
-        if (dx_add) {
-          const float4 a = reinterpret_cast<const float4*>(dx_add + r * D)[i];
-          d = make_float4(d.x + a.x, d.y + a.y, d.z + a.z, d.w + a.w);
-        }
+        if (dx_add) d = make_float4(d.x + ad[j].x, d.y + ad[j].y, d.z + ad[j].z, d.w + ad[j].w);
         dr[i] = d;
       }
     }
@@ -265,7 +264,12 @@ extern "C" int ulm_rms_norm_bwd(const void* dy, int dy_dtype, const void* x, int
   if (vec) {
     const float* xf = static_cast<const float*>(x);
     const float* gf = static_cast<const float*>(dy);
-    auto kern = D <= 128 * 4 ? rms_norm_bwd_vec_kernel<4> : rms_norm_bwd_vec_kernel<8>;
+    // float4s per lane: the row's D / 4 over 32 lanes, rounded up to an even count (registers)
+    const int64_t nv = cdiv(D / 4, 32);
+    auto kern = nv <= 2   ? rms_norm_bwd_vec_kernel<2>
+                : nv <= 4 ? rms_norm_bwd_vec_kernel<4>
+                : nv <= 6 ? rms_norm_bwd_vec_kernel<6>
+                          : rms_norm_bwd_vec_kernel<8>;
     if (smem > 48 * 1024)
       ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (int rc = launch_pdl(kern, dim3((unsigned)grid), dim3(32 * NORM_WARPS), smem, st, gf, xf, weight, rstd, dx,
