@@ -24,6 +24,11 @@
 namespace ulm {
 
 constexpr int DEC_THREADS = 256;
+// The per-row kernels (prologue, address, final norm, greedy pick) run one CTA per sequence: 1024
+// threads at small batches, where a few CTAs hold the GPU and each must cover its row in one round
+// of loads, 256 from 64 sequences on.
+constexpr int DEC_ROW_MAX_THREADS = 1024;
+inline int dec_row_threads(int64_t B) { return B < 64 ? DEC_ROW_MAX_THREADS : DEC_THREADS; }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
   // sum over the block, fixed order
@@ -45,7 +50,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // h = rmsnorm(x) * norm_w; u = conv over the window (buf oldest..newest, h); buf shifts.
 // Also writes bf16 copies of h and u when hop/uop are given (tensor-core GEMM operands).
-__global__ void __launch_bounds__(DEC_THREADS)
+__global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
     decode_prologue_kernel(const float* __restrict__ x, const float* __restrict__ norm_w,
                            const float* __restrict__ conv_w, float* __restrict__ buf, float* __restrict__ h,
                            float* __restrict__ u, __nv_bfloat16* __restrict__ hop, __nv_bfloat16* __restrict__ uop,
@@ -75,7 +80,7 @@ __global__ void __launch_bounds__(DEC_THREADS)
 }
 
 // r = relu(a + bias)^2 / (eps + sum), c = lam c + (1-lam) w + r_prev, q = r / c
-__global__ void __launch_bounds__(DEC_THREADS)
+__global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
     decode_address_kernel(const float* __restrict__ a, const float* __restrict__ key_b, const float* __restrict__ w,
                           const float* __restrict__ lam_p, const float* __restrict__ eps_p, float* __restrict__ c,
                           const float* __restrict__ r_prev, float* __restrict__ r_new, float* __restrict__ q, int M) {
@@ -207,7 +212,7 @@ __global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict
 }
 
 // final RMSNorm of the residual stream, fp32 and optional bf16 copy
-__global__ void __launch_bounds__(DEC_THREADS)
+__global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
     decode_final_norm_kernel(const float* __restrict__ x, const float* __restrict__ norm_w, float* __restrict__ xn,
                              __nv_bfloat16* __restrict__ xop, int64_t ld_op, int D, float norm_eps) {
   pdl_enter();
@@ -226,24 +231,40 @@ __global__ void __launch_bounds__(DEC_THREADS)
 }
 
 // greedy pick: first index of the largest logit (run.c sample_argmax), then gather the next
-// token's embedding row into x
-__global__ void __launch_bounds__(DEC_THREADS)
+// token's embedding row into x. Each thread keeps the first index of its largest value (16-byte
+// loads when the rows allow them), then a tree keeps the larger value, the smaller index on ties.
+__device__ __forceinline__ void argmax_take(float v, int i, float& best, int& idx) {
+  if (v > best || (v == best && i < idx)) {
+    best = v;
+    idx = i;
+  }
+}
+
+__global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
     decode_argmax_embed_kernel(const float* __restrict__ logits, int64_t ld_logits, int V,
                                const void* __restrict__ emb, int emb_bf16, int D, int* __restrict__ next_token,
                                float* __restrict__ x) {
   pdl_enter();
-  __shared__ float bv[DEC_THREADS];
-  __shared__ int bi[DEC_THREADS];
+  __shared__ float bv[DEC_ROW_MAX_THREADS];
+  __shared__ int bi[DEC_ROW_MAX_THREADS];
   const int b = blockIdx.x;
   const float* lg = logits + (int64_t)b * ld_logits;
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = lg[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
+  if ((reinterpret_cast<uintptr_t>(lg) & 15u) == 0) {
+    const int V4 = V / 4;
+    const float4* l4 = reinterpret_cast<const float4*>(lg);
+#pragma unroll 4
+    for (int j = threadIdx.x; j < V4; j += blockDim.x) {
+      const float4 v = l4[j];
+      argmax_take(v.x, 4 * j, best, idx);
+      argmax_take(v.y, 4 * j + 1, best, idx);
+      argmax_take(v.z, 4 * j + 2, best, idx);
+      argmax_take(v.w, 4 * j + 3, best, idx);
     }
+    for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) argmax_take(lg[i], i, best, idx);
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) argmax_take(lg[i], i, best, idx);
   }
   bv[threadIdx.x] = best;
   bi[threadIdx.x] = idx;
@@ -769,8 +790,9 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   float* q = reinterpret_cast<float*>(take(B * M * 4));
   __nv_bfloat16* hop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
   __nv_bfloat16* uop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
-  if (int rc = launch_pdl(decode_prologue_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, x, norm_w, conv_w, buf,
-                          h, u, bf ? hop : nullptr, bf ? uop : nullptr, ldo, (int)D, (int)conv_size, norm_eps))
+  if (int rc = launch_pdl(decode_prologue_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, x, norm_w,
+                          conv_w, buf, h, u, bf ? hop : nullptr, bf ? uop : nullptr, ldo, (int)D, (int)conv_size,
+                          norm_eps))
     return rc;
   if (bf) {
     if (gemv_ok(B, D, D, D, u, key_w) && gemv_ok(B, D, D, D, h, val_w)) {
@@ -784,8 +806,8 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
     if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
     if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
   }
-  if (int rc = launch_pdl(decode_address_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, a, key_b, w, lam, eps,
-                          c, r_prev, r_new, q, (int)M))
+  if (int rc = launch_pdl(decode_address_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, a, key_b, w, lam,
+                          eps, c, r_prev, r_new, q, (int)M))
     return rc;
   const int warps = DEC_THREADS / 32;
   ULM_REQUIRE((B * D) % warps == 0, "B*D must be a multiple of %d", warps);
@@ -840,7 +862,7 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   const int64_t ldo = ulm_operand_ld(D);
   float* xn = static_cast<float*>(work);
   __nv_bfloat16* xop = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(work) + (B * D * 4 + 255) / 256 * 256);
-  if (int rc = launch_pdl(decode_final_norm_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, x, norm_w, xn,
+  if (int rc = launch_pdl(decode_final_norm_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, x, norm_w, xn,
                           bf ? xop : nullptr, ldo, (int)D, norm_eps))
     return rc;
   if (bf && gemv_ok(B, D, D, D, xn, cls_w)) {
@@ -850,8 +872,8 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   } else {
     if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) return rc;
   }
-  if (int rc = launch_pdl(decode_argmax_embed_kernel, dim3((unsigned)B), dim3(DEC_THREADS), 0, st, logits, V, (int)V,
-                          emb, bf, (int)D, next_token, x))
+  if (int rc = launch_pdl(decode_argmax_embed_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, logits, V,
+                          (int)V, emb, bf, (int)D, next_token, x))
     return rc;
   return ULM_OK;
 }
