@@ -420,23 +420,38 @@ namespace ulm {
 constexpr int GEMV_MAX_B = 4;
 constexpr int GEMV_WARPS = 8;
 
+// Up to two products per launch (the key and val projections of a decode step share one): rows
+// [0, N1) of the grid's row space are W1 x1, rows [N1, N1 + N2) are W2 x2, both with K columns.
+struct GemvPair {
+  const float* x[2];
+  const __nv_bfloat16* W[2];
+  float* out[2];
+  int64_t ldo[2];
+  int N[2];
+};
+
 template <int NB>
 __global__ void __launch_bounds__(32 * GEMV_WARPS)
-    decode_gemv_kernel(const float* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ W, int64_t ldw,
-                       float* __restrict__ out, int64_t ldo, int B, int N, int K) {
+    decode_gemv_kernel(const GemvPair pr, int64_t ldx, int64_t ldw, int B, int K) {
   pdl_enter();
-  extern __shared__ float xs[];  // B x K
-  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
-    const int b = i / K, k = i - b * K;
-    xs[i] = x[(int64_t)b * ldx + k];
+  extern __shared__ float xs[];  // (products) x B x K
+  const int np = pr.N[1] > 0 ? 2 : 1;
+  for (int i = threadIdx.x; i < np * B * K; i += blockDim.x) {
+    const int p = i / (B * K), r = i - p * B * K;
+    const int b = r / K, k = r - b * K;
+    xs[i] = (p ? pr.x[1] : pr.x[0])[(int64_t)b * ldx + k];
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  for (int n = blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5); n < N; n += gridDim.x * GEMV_WARPS) {
+  const int rows = pr.N[0] + pr.N[1];
+  for (int row = blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5); row < rows; row += gridDim.x * GEMV_WARPS) {
+    const int p = row < pr.N[0] ? 0 : 1;
+    const int n = p ? row - pr.N[0] : row;
+    const float* xp = xs + p * B * K;
     float acc[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-    const __nv_bfloat16* wr = W + (int64_t)n * ldw;
+    const __nv_bfloat16* wr = (p ? pr.W[1] : pr.W[0]) + (int64_t)n * ldw;
     for (int k8 = lane * 8; k8 < K; k8 += 256) {
       const uint4 pk = *reinterpret_cast<const uint4*>(wr + k8);
       const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
@@ -452,8 +467,8 @@ __global__ void __launch_bounds__(32 * GEMV_WARPS)
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         if (b < B) {
-          const float4 x0 = *reinterpret_cast<const float4*>(xs + b * K + k8);
-          const float4 x1 = *reinterpret_cast<const float4*>(xs + b * K + k8 + 4);
+          const float4 x0 = *reinterpret_cast<const float4*>(xp + b * K + k8);
+          const float4 x1 = *reinterpret_cast<const float4*>(xp + b * K + k8 + 4);
           acc[b] = fmaf(wv[0], x0.x, acc[b]);
           acc[b] = fmaf(wv[1], x0.y, acc[b]);
           acc[b] = fmaf(wv[2], x0.z, acc[b]);
@@ -470,32 +485,34 @@ __global__ void __launch_bounds__(32 * GEMV_WARPS)
       float v = acc[b];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (b < B && lane == 0) out[(int64_t)b * ldo + n] = v;
+      if (b < B && lane == 0) (p ? pr.out[1] : pr.out[0])[(int64_t)b * (p ? pr.ldo[1] : pr.ldo[0]) + n] = v;
     }
   }
 }
 
+int decode_gemv_launch(const GemvPair& pr, int64_t ldx, int64_t ldw, int64_t B, int64_t K, cudaStream_t st) {
+  const int np = pr.N[1] > 0 ? 2 : 1;
+  const size_t smem = (size_t)np * B * K * sizeof(float);
+  const int dev = current_device();
+  const int64_t rows = (int64_t)pr.N[0] + pr.N[1];
+  const int64_t grid = std::min<int64_t>(cdiv(rows, GEMV_WARPS), 4LL * (dev >= 0 ? sm_count(dev) : 148));
+  auto kern = B <= 1 ? decode_gemv_kernel<1> : decode_gemv_kernel<GEMV_MAX_B>;
+  if (smem > 48 * 1024) ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  return launch_pdl(kern, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, pr, ldx, ldw, (int)B, (int)K);
+}
+
 int decode_gemv(const float* x, int64_t ldx, const __nv_bfloat16* W, int64_t ldw, float* out, int64_t ldo,
                 int64_t B, int64_t N, int64_t K, cudaStream_t st) {
-  const size_t smem = (size_t)B * K * sizeof(float);
-  const int dev = current_device();
-  const int64_t grid = std::min<int64_t>(cdiv(N, GEMV_WARPS), 4LL * (dev >= 0 ? sm_count(dev) : 148));
-  if (B <= 4) {
-    if (smem > 48 * 1024)
-      ULM_CUDA_TRY(cudaFuncSetAttribute(decode_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (int rc = launch_pdl(decode_gemv_kernel<4>, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, x, ldx, W,
-                            ldw, out, ldo, (int)B, (int)N, (int)K))
-      return rc;
-  } else {
-    if (smem > 48 * 1024)
-      ULM_CUDA_TRY(
-          cudaFuncSetAttribute(decode_gemv_kernel<GEMV_MAX_B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (int rc = launch_pdl(decode_gemv_kernel<GEMV_MAX_B>, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, x,
-                            ldx, W, ldw, out, ldo, (int)B, (int)N, (int)K))
-      return rc;
-  }
-  ULM_LAUNCH_CHECK("decode_gemv_kernel");
-  return ULM_OK;
+  GemvPair pr{{x, nullptr}, {W, nullptr}, {out, nullptr}, {ldo, 0}, {(int)N, 0}};
+  return decode_gemv_launch(pr, ldx, ldw, B, K, st);
+}
+
+// two products with the same K, x row stride and weight row stride in one launch
+int decode_gemv2(const float* x1, const __nv_bfloat16* W1, float* out1, int64_t ldo1, int64_t N1, const float* x2,
+                 const __nv_bfloat16* W2, float* out2, int64_t ldo2, int64_t N2, int64_t ldx, int64_t ldw, int64_t B,
+                 int64_t K, cudaStream_t st) {
+  GemvPair pr{{x1, x2}, {W1, W2}, {out1, out2}, {ldo1, ldo2}, {(int)N1, (int)N2}};
+  return decode_gemv_launch(pr, ldx, ldw, B, K, st);
 }
 
 // Whether the small-batch path serves a bf16 decode GEMM (x fp32 rows of ldx, 16-byte weight rows).
@@ -795,9 +812,11 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
                           norm_eps))
     return rc;
   if (bf) {
-    if (gemv_ok(B, D, D, D, u, key_w) && gemv_ok(B, D, D, D, h, val_w)) {
-      if (int rc = decode_gemv(u, D, static_cast<const __nv_bfloat16*>(key_w), D, a, M, B, M, D, st)) return rc;
-      if (int rc = decode_gemv(h, D, static_cast<const __nv_bfloat16*>(val_w), D, v, D, B, D, D, st)) return rc;
+    if (gemv_ok(B, D, D, D, u, key_w) && gemv_ok(B, D, D, D, h, val_w) && 2 * B * D * 4 <= 200 * 1024) {
+      // a = u K^T and v = h W_v^T in one launch
+      if (int rc = decode_gemv2(u, static_cast<const __nv_bfloat16*>(key_w), a, M, M, h,
+                                static_cast<const __nv_bfloat16*>(val_w), v, D, D, D, D, B, D, st))
+        return rc;
     } else {
       if (int rc = decode_gemm(uop, ldo, key_w, D, ULM_BF16, a, M, B, M, D, st)) return rc;
       if (int rc = decode_gemm(hop, ldo, val_w, D, ULM_BF16, v, D, B, D, D, st)) return rc;
