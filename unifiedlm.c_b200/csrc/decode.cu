@@ -497,7 +497,8 @@ int decode_gemv_launch(const GemvPair& pr, int64_t ldx, int64_t ldw, int64_t B, 
   const int64_t rows = (int64_t)pr.N[0] + pr.N[1];
   const int64_t grid = std::min<int64_t>(cdiv(rows, GEMV_WARPS), 4LL * (dev >= 0 ? sm_count(dev) : 148));
   auto kern = B <= 1 ? decode_gemv_kernel<1> : decode_gemv_kernel<GEMV_MAX_B>;
-  if (smem > 48 * 1024) ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (smem > 48 * 1024)
+    ULM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   return launch_pdl(kern, dim3((unsigned)grid), dim3(32 * GEMV_WARPS), smem, st, pr, ldx, ldw, (int)B, (int)K);
 }
 
@@ -513,6 +514,61 @@ int decode_gemv2(const float* x1, const __nv_bfloat16* W1, float* out1, int64_t 
                  int64_t K, cudaStream_t st) {
   GemvPair pr{{x1, x2}, {W1, W2}, {out1, out2}, {ldo1, ldo2}, {(int)N1, (int)N2}};
   return decode_gemv_launch(pr, ldx, ldw, B, K, st);
+}
+
+// fp32 decode GEMM for small batches in the FMA back end's in-order form (the fp32 mode's run.c
+// order): one thread per output row n walks k from 0 with one fused multiply-add per term, so the
+// results equal the tiled kernel's with k_in_order bit for bit; its weight row is read with 16-byte
+// loads, the batch's x rows sit in shared memory (read as broadcasts).
+template <int NB>
+__global__ void __launch_bounds__(128)
+    decode_gemv_f32_kernel(const float* __restrict__ x, int64_t ldx, const float* __restrict__ W, int64_t ldw,
+                           float* __restrict__ out, int64_t ldo, int B, int N, int K) {
+  pdl_enter();
+  extern __shared__ float xs[];  // B x K
+  for (int i = threadIdx.x; i < B * K; i += blockDim.x) {
+    const int b = i / K, k = i - b * K;
+    xs[i] = x[(int64_t)b * ldx + k];
+  }
+  __syncthreads();
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const float4* wr = reinterpret_cast<const float4*>(W + (int64_t)n * ldw);
+  float acc[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+#pragma unroll 4
+  for (int k4 = 0; k4 < K / 4; ++k4) {
+    const float4 w4 = wr[k4];
+    const int k = 4 * k4;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b < B) {
+        const float* xb = xs + b * K + k;
+        acc[b] = fmaf(xb[0], w4.x, acc[b]);
+        acc[b] = fmaf(xb[1], w4.y, acc[b]);
+        acc[b] = fmaf(xb[2], w4.z, acc[b]);
+        acc[b] = fmaf(xb[3], w4.w, acc[b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+    if (b < B) out[(int64_t)b * ldo + n] = acc[b];
+}
+
+// Whether the small-batch fp32 path serves a decode GEMM (K % 4 == 0, 16-byte weight rows).
+bool gemv_f32_ok(int64_t B, int64_t K, int64_t ldw, const void* W) {
+  return B <= GEMV_MAX_B && K % 4 == 0 && ldw % 4 == 0 && is_aligned16(W) &&
+         B * K * (int64_t)sizeof(float) <= 48 * 1024;
+}
+
+int decode_gemv_f32(const float* x, int64_t ldx, const float* W, int64_t ldw, float* out, int64_t ldo, int64_t B,
+                    int64_t N, int64_t K, cudaStream_t st) {
+  const size_t smem = (size_t)B * K * sizeof(float);
+  auto kern = B <= 1 ? decode_gemv_f32_kernel<1> : decode_gemv_f32_kernel<GEMV_MAX_B>;
+  return launch_pdl(kern, dim3((unsigned)cdiv(N, 128)), dim3(128), smem, st, x, ldx, W, ldw, out, ldo, (int)B, (int)N,
+                    (int)K);
 }
 
 // Whether the small-batch path serves a bf16 decode GEMM (x fp32 rows of ldx, 16-byte weight rows).
@@ -822,8 +878,15 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
       if (int rc = decode_gemm(hop, ldo, val_w, D, ULM_BF16, v, D, B, D, D, st)) return rc;
     }
   } else {
-    if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
-    if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
+    if (gemv_f32_ok(B, D, D, key_w) && gemv_f32_ok(B, D, D, val_w)) {
+      const float* kwf = static_cast<const float*>(key_w);
+      const float* vwf = static_cast<const float*>(val_w);
+      if (int rc = decode_gemv_f32(u, D, kwf, D, a, M, B, M, D, st)) return rc;
+      if (int rc = decode_gemv_f32(h, D, vwf, D, v, D, B, D, D, st)) return rc;
+    } else {
+      if (int rc = decode_gemm(u, D, key_w, D, ULM_F32, a, M, B, M, D, st)) return rc;
+      if (int rc = decode_gemm(h, D, val_w, D, ULM_F32, v, D, B, D, D, st)) return rc;
+    }
   }
   if (int rc = launch_pdl(decode_address_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, a, key_b, w, lam,
                           eps, c, r_prev, r_new, q, (int)M))
@@ -889,7 +952,11 @@ extern "C" int ulm_decode_head(float* x, const float* norm_w, const void* cls_w,
   } else if (bf) {
     if (int rc = decode_gemm(xop, ldo, cls_w, D, ULM_BF16, logits, V, B, V, D, st)) return rc;
   } else {
-    if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) return rc;
+    if (gemv_f32_ok(B, D, D, cls_w)) {
+      if (int rc = decode_gemv_f32(xn, D, static_cast<const float*>(cls_w), D, logits, V, B, V, D, st)) return rc;
+    } else if (int rc = decode_gemm(xn, D, cls_w, D, ULM_F32, logits, V, B, V, D, st)) {
+      return rc;
+    }
   }
   if (int rc = launch_pdl(decode_argmax_embed_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, logits, V,
                           (int)V, emb, bf, (int)D, next_token, x))
