@@ -980,8 +980,6 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
       n.x = fmaf(lam_h, n.x, lo_cur.x);
       n.y = fmaf(lam_h, n.y, lo_cur.y);
     }
-    __syncthreads();  // every thread is past the wait on xbar_f[xp]
-    if (threadIdx.x == 0 && cr > 0) mbar_arrive_expect_tx(&xbar_f[xp], (uint32_t)cr * 128u);
 
     float2 dw_acc = make_float2(0.f, 0.f);
     float dg_f = 0.f;
@@ -1034,6 +1032,9 @@ __global__ void __launch_bounds__(32 * WARPS, 2)
       *reinterpret_cast<float2*>(&warp_dw[wp][s2]) = make_float2(dw_acc.x + dw_hi.x, dw_acc.y + dw_hi.y);
     }
     __syncthreads();
+    // every thread is past the wait on xbar_f[xp]: armed for item j + 2, whose forward totals the
+    // lower ranks send only after this CTA's reverse totals of item j (below) have reached them
+    if (threadIdx.x == 0 && cr > 0) mbar_arrive_expect_tx(&xbar_f[xp], (uint32_t)cr * 128u);
     if (wp == 0) {
       float tot = 0.f;
       for (int jj = WARPS - 1; jj >= 0; --jj) tot = fmaf(tot, lam_seg, warp_sum[jj][lane]);
