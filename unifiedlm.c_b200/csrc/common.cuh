@@ -58,9 +58,11 @@ inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // Kernels started with launch_pdl may be scheduled while the previous kernel on their stream is
 // still finishing: their CTAs take SMs as the predecessor's CTAs leave and do their set-up
 // (barriers, tensor memory) early. Each such kernel calls pdl_enter() before its first access to
-// global memory: it waits until the predecessor grid has completed with its writes visible, then
-// lets the next kernel on the stream be scheduled the same way. Without the launch attribute both
-// instructions return at once, so every kernel calls pdl_enter() however it is launched.
+// global memory: it waits until the predecessor grid has completed with its writes visible. No
+// kernel signals its dependents early (griddepcontrol.launch_dependents): the next kernel's CTAs are
+// placed as this grid's CTAs exit (an early signal let them hold SM resources while they waited, and
+// the step got slower). Without the launch attribute the wait returns at once, so every kernel calls
+// pdl_enter() however it is launched.
 __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
