@@ -47,23 +47,29 @@ def peaks():
 
 
 def make_inputs(B, T, M, D, L, lam, prior, device, seed=0):
-    """Seeded synthetic inputs of one step and per-block weights (the reference's init scales)."""
+    """Seeded synthetic inputs of one step and per-block weights (the reference's init scales).
+
+    Every block gets its own h, v, dq_out and dfast (lists of L tensors, 235 MB per block at the
+    110M shape), as in a model where each block's inputs come from its neighbours: no block reads
+    what an earlier block left in L2."""
     import math
     gen = torch.Generator(device=device).manual_seed(seed)
     rn = lambda *s_: torch.randn(*s_, device=device, generator=gen)  # noqa: E731
-    h = rn(B, T, D)
-    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)
-    # dtypes as under the reference's bf16 autocast: the residual stream and h = norm(x) stay fp32,
-    # v = val(h) is bf16, so fast and its gradient are bf16; q and its gradient are fp32
-    v = rn(B, T, D).to(torch.bfloat16)
-    dq_out = rn(B, T, M) * 1e-3
-    dfast = (rn(B, T, D) * 1e-3).to(torch.bfloat16)
+    hs, vs, dqs, dfs = [], [], [], []
+    for _ in range(L):
+        h = rn(B, T, D)
+        hs.append(h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5))
+        # dtypes as under the reference's bf16 autocast: the residual stream and h = norm(x) stay
+        # fp32, v = val(h) is bf16, so fast and its gradient are bf16; q and its gradient are fp32
+        vs.append(rn(B, T, D).to(torch.bfloat16))
+        dqs.append(rn(B, T, M) * 1e-3)
+        dfs.append((rn(B, T, D) * 1e-3).to(torch.bfloat16))
     blocks = []
     for _ in range(L):
         blocks.append({"conv": rn(D, 1, 4) * 0.5, "key_w": rn(M, D) / math.sqrt(D), "key_b": rn(M) * 0.1,
                        "eps": torch.ones((), device=device),
                        "g": torch.tensor(math.log(lam), device=device), "w": torch.full((M,), prior, device=device)})
-    return h, v, dq_out, dfast, blocks
+    return hs, vs, dqs, dfs, blocks
 
 
 class ClockSampler:
@@ -124,7 +130,8 @@ class ClockSampler:
 
 def cpu_reference_seconds(T, M, D, lam, prior, reps, threads):
     """Seconds for one sequence x one block of the reference's CPU form of the path (prologue +
-    chunked fast memory, forward and backward, fp32)."""
+    chunked fast memory, forward and backward, fp32): the median of `reps` timed samples after one
+    untimed one."""
     import math
     from oracle import memory as O
     torch.set_num_threads(threads)
@@ -146,10 +153,12 @@ def cpu_reference_seconds(T, M, D, lam, prior, reps, threads):
         ((q * dq_out).sum() + (fast * dfast).sum()).backward()
 
     once()  # warm-up
-    t0 = time.perf_counter()
+    secs = []
     for _ in range(reps):
+        t0 = time.perf_counter()
         once()
-    return (time.perf_counter() - t0) / reps
+        secs.append(time.perf_counter() - t0)
+    return statistics.median(secs)
 
 
 def workload_config(W):
@@ -164,8 +173,9 @@ def run_reference(args, rank):
         return
     W = WORKLOAD
     threads = os.cpu_count() or 1
-    reps = 1
-    # warm-up W samples, then K timed samples; one sample = 1 sequence through 1 block
+    reps = 3
+    # warm-up W samples, then K timed steps; one step = the median of 3 samples of 1 sequence
+    # through 1 block
     for _ in range(max(args.warmup, 0)):
         cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 1, threads)
     secs = [cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], reps, threads)
@@ -176,8 +186,8 @@ def run_reference(args, rank):
             "warmup": args.warmup, "ms_per_step": per_sample * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "impl": "reference",
             "config": dict(workload_config(W), parallelism=f"dp{args.gpus}",
-                           sample="1 sequence x 1 block per timed sample on the host cores, scaled to the "
-                                  "workload's tokens"),
+                           sample="median of 3 samples of 1 sequence x 1 block per timed step on the host "
+                                  "cores, the median over the steps scaled to the workload's tokens"),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, "
                                        "prologue + chunked pure-PyTorch form (model.py:70-79, test_all.py:28-51 "
@@ -750,8 +760,8 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120), pg_options=opts)
     W = dict(WORKLOAD, L=1) if args.profile_block else WORKLOAD
     prec = PRECISION[args.precision]
-    h, v, dq_out, dfast, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
-                                              seed=rank)
+    hs, vs, dqs, dfs, blocks = make_inputs(W["B"], W["T"], W["M"], W["D"], W["L"], W["lam"], W["prior"], dev,
+                                           seed=rank)
     from unifiedlm_c_b200.dp import GradBucket
     M_, D_ = W["M"], W["D"]
     # the path's parameter gradients in one flat bucket, DP-averaged every step: by default one NCCL
@@ -764,16 +774,17 @@ def main():
     grad_shapes = [(M_, D_), (M_,), (D_, 1, 4), (), (M_,), ()] * W["L"]
     bucket = GradBucket(grad_shapes, device=dev, segments=segs)
 
-    def step(h_, v_, dq_, df_, before_bwd=None, bk=None, after_segment=None):
-        """One training step of the path, in a model's order: every block's forward, then the
-        backward from the last block to the first, the gradients packed into bucket `bk` (default
-        `bucket`) segment by segment. `before_bwd` runs between the two phases (the e2e loop makes
-        the stream wait there for the gradient inputs, which it copies last); `after_segment(s)`
-        runs once segment s is packed (and, with N ranks, its all-reduce started)."""
+    def step(hs_, vs_, dqs_, dfs_, before_bwd=None, bk=None, after_segment=None):
+        """One training step of the path, in a model's order: every block's forward (block i on
+        hs_[i], vs_[i]), then the backward from the last block to the first (on dqs_[i], dfs_[i]),
+        the gradients packed into bucket `bk` (default `bucket`) segment by segment. `before_bwd`
+        runs between the two phases (the e2e loop makes the stream wait there for the gradient
+        inputs, which it copies last); `after_segment(s)` runs once segment s is packed (and, with N
+        ranks, its all-reduce started)."""
         bk = bucket if bk is None else bk
         per_seg = len(blocks) // bk.segments
         saved = []
-        for blk in blocks:
+        for blk, h_, v_ in zip(blocks, hs_, vs_):
             saved.append(addressed_memory_fwd(h_, blk["conv"], blk["key_w"], blk["key_b"], blk["eps"], v_,
                                               blk["g"], blk["w"], prec))
         if before_bwd is not None:
@@ -784,8 +795,8 @@ def main():
             q, fast, z, den, u_op, kw, c, qop, kop, vop, P = saved[i]
             saved[i] = None
             dh, dconv, dkw, dkb, deps, dv, dg, dw = addressed_memory_bwd(
-                dq_, df_, h_, blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop,
-                operand_or_input(vop, v_), P, prec)
+                dqs_[i], dfs_[i], hs_[i], blk["conv"], blk["g"], blk["w"], q, z, den, u_op, kw, c, qop, kop,
+                operand_or_input(vop, vs_[i]), P, prec)
             grads[i] = [dkw, dkb, dconv, deps, dw, dg]
             if i % per_seg == 0:
                 bk.pack_segment(i // per_seg, [t for g6 in grads[i:i + per_seg] for t in g6])
@@ -796,8 +807,8 @@ def main():
         return bk.flat
 
     if args.profile_step or args.profile_block:
-        step(h, v, dq_out, dfast)
-        step(h, v, dq_out, dfast)
+        step(hs, vs, dqs, dfs)
+        step(hs, vs, dqs, dfs)
         torch.cuda.synchronize()
         if world > 1:
             dist.destroy_process_group()
@@ -806,14 +817,14 @@ def main():
     # the sampler starts with the warm-up so that short timed regions still see >= 1 sample under load
     with ClockSampler(local) as clocks:
         for _ in range(args.warmup):
-            step(h, v, dq_out, dfast)
+            step(hs, vs, dqs, dfs)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         ev0.record()
         for _ in range(args.steps):
-            step(h, v, dq_out, dfast)
+            step(hs, vs, dqs, dfs)
         ev1.record()
         torch.cuda.synchronize()
     if world > 1:
@@ -833,9 +844,16 @@ def main():
     # read back on another stream into one of two pinned host buffers (two device buckets). On one
     # GPU each block's gradients are read back as soon as its backward has packed them, so only the
     # first block's 6 MB remain after the last step; with N ranks the read follows the all-reduce.
-    # The timed region spans the first copy to the last read.
-    host = [t.cpu().pin_memory() for t in (h, v, dq_out, dfast)]
-    slots_in = [[torch.empty_like(t) for t in (h, v, dq_out, dfast)] for _ in range(2)]
+    # The timed region spans the first copy to the last read. The inputs copied are the step's
+    # ends, as a model's would be: the first block's h and v and the last block's upstream
+    # gradients dq_out and dfast; the other blocks read their own device-resident inputs, which in
+    # a model their neighbouring blocks write.
+    host = [t.cpu().pin_memory() for t in (hs[0], vs[0], dqs[-1], dfs[-1])]
+    slots_in = [[torch.empty_like(t, device=dev) for t in host] for _ in range(2)]
+
+    def slot_inputs(k):
+        h_, v_, dq_, df_ = slots_in[k]
+        return [h_] + hs[1:], [v_] + vs[1:], dqs[:-1] + [dq_], dfs[:-1] + [df_]
     out_buckets = [GradBucket(grad_shapes, device=dev, segments=W["L"] if world == 1 else segs) for _ in range(2)]
     host_out = [torch.empty(bucket.flat.shape, dtype=bucket.flat.dtype).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host)
@@ -884,7 +902,7 @@ def main():
                 def per_segment(s_, bk=bk, dst=host_out[k]):
                     a, b = bk.offsets[s_ * bk.per_segment], bk.offsets[(s_ + 1) * bk.per_segment]
                     read_back(bk.segment(s_), dst[a:b])
-            out = step(*slots_in[k], before_bwd=lambda k=k: main_s.wait_event(grad_ready[k]), bk=bk,
+            out = step(*slot_inputs(k), before_bwd=lambda k=k: main_s.wait_event(grad_ready[k]), bk=bk,
                        after_segment=per_segment)
             ev = torch.cuda.Event()
             ev.record(main_s)
@@ -916,6 +934,7 @@ def main():
     # roofline of the dominant kernel family (tensor-core products), CUDA events per launch
     blk0 = blocks[0]
     g, w = blk0["g"], blk0["w"]
+    h, v, dfast = hs[0], vs[0], dfs[0]
     r, _, _, _ = address_fwd(h, blk0["conv"], blk0["key_w"], blk0["key_b"], blk0["eps"], prec)
     q, fast, c, qop, kop, vop, P = memory_fwd(r, v, g, w, prec)
     vop = operand_or_input(vop, v)
@@ -963,9 +982,9 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        s = cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 2, threads)
+        s = cpu_reference_seconds(W["T"], W["M"], W["D"], W["lam"], W["prior"], 15, threads)
         cpu = {"value": W["T"] / (W["L"] * s), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd x2, prologue + chunked "
+               "sample": f"1 seq x 1 block (T={W['T']}, M={W['M']}, D={W['D']}) fwd+bwd, median of 15, prologue + chunked "
                          "pure-PyTorch form (model.py:70-79, test_all.py:28-51 restated in oracle/memory.py), "
                          "fp32, scaled to 12 blocks"}
 
@@ -994,7 +1013,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
             "config": dict(workload_config(W), parallelism=f"dp{world}", grad_allreduce_segments=segs,
-                           l2="inputs larger than L2 (r is 134 MB), no flush"),
+                           l2="every block reads its own inputs (235 MB per block); r is 134 MB; no flush"),
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "h2d_gbs_per_rank": round(h2d * e2e_steps / float(e2e_secs) / 1e9, 1),
