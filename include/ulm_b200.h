@@ -348,7 +348,9 @@ int ulm_linear_fwd(const void* x, int x_dtype, const float* weight, void* x_op, 
                    int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
 /* Backward of ulm_linear_fwd from dy (N, Nout) of dy_dtype: dx (N, K) fp32 = dy W (+ dx_add (N, K)
  * fp32 when not NULL, added in the product's epilogue), dw (Nout, K) fp32 = dy^T x (split over the
- * rows, partials summed in a fixed order). work: ulm_linear_bwd_work_bytes(N, K, Nout, prec) bytes. */
+ * rows, partials summed in a fixed order). work: ulm_linear_bwd_work_bytes(N, K, Nout, prec) bytes;
+ * dy is read in place when it is already an operand (the operand type, Nout a multiple of 8 and a
+ * 16-byte aligned start), else copied into the front of work. */
 int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, const void* w_op, float* dx, const float* dx_add,
                    float* dw, void* work, int64_t N, int64_t K, int64_t Nout, int prec, void* stream);
 int64_t ulm_linear_bwd_work_bytes(int64_t N, int64_t K, int64_t Nout, int prec);

@@ -339,9 +339,14 @@ extern "C" int ulm_linear_bwd(const void* dy, int dy_dtype, const void* x_op, co
   ULM_REQUIRE(dy && x_op && w_op && work, "null pointer argument");
   const int dt = op_dtype_of(prec);
   const int64_t ldk = ulm_operand_ld(K), ldo = ulm_operand_ld(Nout);
-  void* dy_op = work;
   float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(work) + align256(N * ldo * (dt == ULM_F32 ? 4 : 2)));
-  if (int rc = convert_rows(dy, dy_dtype, Nout, dy_op, dt, ldo, N, Nout, st)) return rc;
+  // dy is its own operand when it already has the operand type, an unpadded row stride and an
+  // aligned start (a bf16 activation gradient); otherwise it is copied into the work buffer
+  const void* dy_op = dy;
+  if (dy_dtype != dt || ldo != Nout || !is_aligned16(dy)) {
+    if (int rc = convert_rows(dy, dy_dtype, Nout, work, dt, ldo, N, Nout, st)) return rc;
+    dy_op = work;
+  }
   {
     // dx[n][k] = sum_o dy[n][o] W[o][k]: W read as [o][k] = MN-major over k
     Operand A{dy_op, ldo, N * ldo, Nout, N, dt, false};
