@@ -843,8 +843,10 @@ def main():
     # step i+1 runs on its own stream during step i (two device input slots), and the gradients are
     # read back on another stream into one of two pinned host buffers (two device buckets). On one
     # GPU each block's gradients are read back as soon as its backward has packed them, so only the
-    # first block's 6 MB remain after the last step; with N ranks the read follows the all-reduce.
-    # The timed region spans the first copy to the last read. The inputs copied are the step's
+    # first block's 6 MB remain after the last step; with N ranks the read follows the all-reduce,
+    # on rank 0 only (after the all-reduce every rank holds the same averaged gradients, so one copy
+    # is the job's result; N reads of it would only add host traffic). The timed region spans the
+    # first copy to the last read, the maximum over ranks. The inputs copied are the step's
     # ends, as a model's would be: the first block's h and v and the last block's upstream
     # gradients dq_out and dfast; the other blocks read their own device-resident inputs, which in
     # a model their neighbouring blocks write.
@@ -907,7 +909,7 @@ def main():
             ev = torch.cuda.Event()
             ev.record(main_s)
             in_free[k] = ev
-            if world > 1:
+            if world > 1 and rank == 0:
                 read_back(out, host_out[k])
             done = torch.cuda.Event()
             done.record(d2h_s)
@@ -1015,14 +1017,15 @@ def main():
             "config": dict(workload_config(W), parallelism=f"dp{world}", grad_allreduce_segments=segs,
                            l2="every block reads its own inputs (235 MB per block); r is 134 MB; no flush"),
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "d2h_bytes_per_step": d2h, "d2h_ranks": 1, "steps": e2e_steps,
                     "h2d_gbs_per_rank": round(h2d * e2e_steps / float(e2e_secs) / 1e9, 1),
                     "h2d_gbs_all_ranks": round(world * h2d * e2e_steps / float(e2e_secs) / 1e9, 1),
                     "copies": "pinned host buffers; H2D of step i+1 during step i on its own stream "
                               "(double-buffered; forward inputs first, the step waits for the gradient inputs "
                               "before its backward); the gradients read back on another stream, per block as "
-                              "the backward packs them on one GPU, after the all-reduce with N ranks; timed "
-                              "from the first copy to the last read"},
+                              "the backward packs them on one GPU, after the all-reduce and by rank 0 alone "
+                              "with N ranks (every rank holds the same averaged gradients); timed from the first "
+                              "copy to the last read, max over ranks"},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": launches,
             "mixer": mixer, "head": head, "decode": decode, "model_step": models, "config3": config3}
     if rank == 0:
