@@ -20,6 +20,7 @@
  *   kernel.py:75-101   _la_state / _la_out (apply scores)     -> ulm_causal_apply
  *   model.py:61-79     conv + UnifiedBlock.code (address)     -> ulm_address_fwd, ulm_address_bwd
  *   model.py:84-85     unified_memory + mu(q w) + residual    -> ulm_memory_combine_fwd, _bwd
+ *   model.py:72,75,84  log_eps / log_w / log_rate transforms   -> ulm_block_scalars_fwd, _bwd
  *   model.py:88-111,   UnifiedBlock.init_state / step, and
  *   run.c:121-265      run.c reset_state / forward            -> ulm_decode_* (batched)
  *   run.c:460-534      run.c sample (argmax / mult / top-p)   -> ulm_decode_head, ulm_decode_sample
@@ -220,6 +221,19 @@ int ulm_memory_bwd(const float* dq_out, const void* dfast, int do_dtype, const f
                    int prec, void* stream);
 
 /* ---- the block's combine fused into the fast memory (model.py:84-85) ------------------------- */
+
+/* The block's learned scalars from their log parameters (model.py:72, 75, 84), the reference's
+ * expressions in fp32: w (M,) = exp(clamp(log_w, -7, 12)), eps = exp(clamp(log_eps, -10, 10)) and
+ * g = -exp(log_rate) (the log decay), one launch; log_eps, log_rate, eps and g are single device
+ * floats. */
+int ulm_block_scalars_fwd(const float* log_w, const float* log_eps, const float* log_rate, float* w, float* eps,
+                          float* g, int64_t M, void* stream);
+/* Backward of ulm_block_scalars_fwd, as autograd of those expressions gives it: dlog_w = dw * w where
+ * -7 <= log_w <= 12 (else 0), dlog_eps = deps * eps where -10 <= log_eps <= 10 (else 0),
+ * dlog_rate = dg * g; w, eps and g are the forward's outputs. One launch. */
+int ulm_block_scalars_bwd(const float* log_w, const float* log_eps, const float* w, const float* eps, const float* g,
+                          const float* dw, const float* deps, const float* dg, float* dlog_w, float* dlog_eps,
+                          float* dlog_rate, int64_t M, void* stream);
 
 /* y = x + mu(q * w) + fast, (q, fast) = unified_memory(r, v, g, w): UnifiedBlock.forward's last
  * line (model.py:85, dropout off) with the combine's product mu(q w) accumulated in the same

@@ -28,6 +28,8 @@ SIGNATURES = {
     "ulm_memory_stats_bwd_scratch": (_I64, [_I64, _I64, _I64]),
     "ulm_memory_stats_bwd_noalloc": (_I, [_P] * 11 + [_I64, _I64, _I64, _P]),
     "ulm_memory_needs_c": (_I, [_I64, _I64]),
+    "ulm_block_scalars_fwd": (_I, [_P] * 6 + [_I64, _P]),
+    "ulm_block_scalars_bwd": (_I, [_P] * 11 + [_I64, _P]),
     "ulm_decayed_scores": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P]),
     "ulm_causal_apply": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I64, _I64, _I64, _I, _P]),
     "ulm_operand_ld": (_I64, [_I64]),

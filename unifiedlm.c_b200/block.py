@@ -373,3 +373,72 @@ def unified_block(x, norm_weight, norm_eps, conv_weight, key_weight, key_bias, e
                                     w.float().contiguous(), mu_weight.float().contiguous(), float(norm_eps),
                                     PRECISION[precision])
     return y.to(x.dtype)
+
+
+# ---- the block's learned scalars (model.py:72, 75, 84) ---------------------------------------------
+
+@torch.library.custom_op("ulm::block_scalars_fwd", mutates_args=())
+def block_scalars_fwd(log_w: torch.Tensor, log_eps: torch.Tensor, log_rate: torch.Tensor
+                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(w (M,), eps (), g ()) fp32 from fp32 log parameters in one launch (ulm_block_scalars_fwd)."""
+    w = torch.empty_like(log_w)
+    eps = log_eps.new_empty(())
+    g = log_rate.new_empty(())
+    with torch.cuda.device(log_w.device):
+        L.check(L.lib().ulm_block_scalars_fwd(L.ptr(log_w), L.ptr(log_eps), L.ptr(log_rate), L.ptr(w), L.ptr(eps),
+                                              L.ptr(g), log_w.numel(), L.stream_of(log_w)))
+    return w, eps, g
+
+
+@block_scalars_fwd.register_fake
+def _block_scalars_fwd_fake(log_w, log_eps, log_rate):
+    return log_w.new_empty(log_w.shape), log_eps.new_empty(()), log_rate.new_empty(())
+
+
+@torch.library.custom_op("ulm::block_scalars_bwd", mutates_args=())
+def block_scalars_bwd(log_w: torch.Tensor, log_eps: torch.Tensor, w: torch.Tensor, eps: torch.Tensor,
+                      g: torch.Tensor, dw: torch.Tensor, deps: torch.Tensor, dg: torch.Tensor
+                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dlog_w, dlog_eps, dlog_rate) in one launch (ulm_block_scalars_bwd)."""
+    dlw = torch.empty_like(log_w)
+    dle = log_eps.new_empty(())
+    dlr = g.new_empty(())
+    with torch.cuda.device(log_w.device):
+        L.check(L.lib().ulm_block_scalars_bwd(L.ptr(log_w), L.ptr(log_eps), L.ptr(w), L.ptr(eps), L.ptr(g),
+                                              L.ptr(dw), L.ptr(deps), L.ptr(dg), L.ptr(dlw), L.ptr(dle), L.ptr(dlr),
+                                              log_w.numel(), L.stream_of(log_w)))
+    return dlw, dle, dlr
+
+
+@block_scalars_bwd.register_fake
+def _block_scalars_bwd_fake(log_w, log_eps, w, eps, g, dw, deps, dg):
+    return log_w.new_empty(log_w.shape), log_eps.new_empty(()), g.new_empty(())
+
+
+def _bs_setup(ctx, inputs, output):
+    log_w, log_eps, _ = inputs
+    w, eps, g = output
+    ctx.save_for_backward(log_w, log_eps, w, eps, g)
+
+
+def _bs_backward(ctx, dw, deps, dg):
+    log_w, log_eps, w, eps, g = ctx.saved_tensors
+    dw = torch.zeros_like(w) if dw is None else dw.float().contiguous()
+    deps = torch.zeros_like(eps) if deps is None else deps.float().reshape(())
+    dg = torch.zeros_like(g) if dg is None else dg.float().reshape(())
+    return block_scalars_bwd(log_w, log_eps, w, eps, g, dw, deps, dg)
+
+
+torch.library.register_autograd("ulm::block_scalars_fwd", _bs_backward, setup_context=_bs_setup)
+
+
+def block_scalars(log_w, log_eps, log_rate):
+    """UnifiedBlock's learned scalars as the reference evaluates them (model.py:72, 75, 84):
+    w = exp(clamp(log_w, -7, 12)), eps = exp(clamp(log_eps, -10, 10)), g = -exp(log_rate), in
+    fp32, with the same gradients as autograd of those expressions; one launch each way instead of
+    one per elementwise step."""
+    for t in (log_w, log_eps, log_rate):
+        if not t.is_cuda:
+            raise RuntimeError("block_scalars runs on CUDA tensors only (no CPU path)")
+    return torch.ops.ulm.block_scalars_fwd(log_w.float().contiguous(), log_eps.float().reshape(()),
+                                           log_rate.float().reshape(()))

@@ -279,11 +279,68 @@ int check_prec(int prec) {
   return ULM_OK;
 }
 
+// The block's learned scalars from their log parameters (model.py:72, 75, 84), in fp32 as PyTorch
+// evaluates the same expressions: w = exp(clamp(log_w, -7, 12)), eps = exp(clamp(log_eps, -10, 10)),
+// g = -exp(log_rate). Thread 0 of block 0 also writes the two scalars.
+__global__ void block_scalars_fwd_kernel(const float* __restrict__ log_w, const float* __restrict__ log_eps,
+                                         const float* __restrict__ log_rate, float* __restrict__ w,
+                                         float* __restrict__ eps, float* __restrict__ g, int64_t M) {
+  pdl_enter();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < M) w[i] = expf(fminf(fmaxf(log_w[i], -7.f), 12.f));
+  if (i == 0) {
+    *eps = expf(fminf(fmaxf(*log_eps, -10.f), 10.f));
+    *g = -expf(*log_rate);
+  }
+}
+
+// Their backward, as PyTorch's autograd of the same expressions computes it: exp passes
+// grad * exp(x), clamp passes the gradient where min <= x <= max and zero elsewhere, negation
+// flips the sign (so dlog_rate = -(dg * exp(log_rate)) = dg * g).
+__global__ void block_scalars_bwd_kernel(const float* __restrict__ log_w, const float* __restrict__ log_eps,
+                                         const float* __restrict__ w, const float* __restrict__ eps,
+                                         const float* __restrict__ g, const float* __restrict__ dw,
+                                         const float* __restrict__ deps, const float* __restrict__ dg,
+                                         float* __restrict__ dlog_w, float* __restrict__ dlog_eps,
+                                         float* __restrict__ dlog_rate, int64_t M) {
+  pdl_enter();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < M) {
+    const float x = log_w[i];
+    dlog_w[i] = (x >= -7.f && x <= 12.f) ? dw[i] * w[i] : 0.f;
+  }
+  if (i == 0) {
+    const float x = *log_eps;
+    *dlog_eps = (x >= -10.f && x <= 10.f) ? (*deps) * (*eps) : 0.f;
+    *dlog_rate = (*dg) * (*g);
+  }
+}
+
 }  // namespace
 
 }  // namespace ulm
 
 using namespace ulm;
+
+extern "C" int ulm_block_scalars_fwd(const float* log_w, const float* log_eps, const float* log_rate, float* w,
+                                     float* eps, float* g, int64_t M, void* stream) {
+  ULM_REQUIRE(M >= 0 && M < (1ll << 40), "bad extent M=%lld", (long long)M);
+  ULM_REQUIRE(log_eps && log_rate && eps && g && (M == 0 || (log_w && w)), "null pointer argument");
+  const unsigned grid = (unsigned)(M > 0 ? cdiv(M, 256) : 1);
+  return launch_pdl(block_scalars_fwd_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), log_w,
+                    log_eps, log_rate, w, eps, g, M);
+}
+
+extern "C" int ulm_block_scalars_bwd(const float* log_w, const float* log_eps, const float* w, const float* eps,
+                                     const float* g, const float* dw, const float* deps, const float* dg,
+                                     float* dlog_w, float* dlog_eps, float* dlog_rate, int64_t M, void* stream) {
+  ULM_REQUIRE(M >= 0 && M < (1ll << 40), "bad extent M=%lld", (long long)M);
+  ULM_REQUIRE(log_eps && eps && g && deps && dg && dlog_eps && dlog_rate && (M == 0 || (log_w && w && dw && dlog_w)),
+              "null pointer argument");
+  const unsigned grid = (unsigned)(M > 0 ? cdiv(M, 256) : 1);
+  return launch_pdl(block_scalars_bwd_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), log_w,
+                    log_eps, w, eps, g, dw, deps, dg, dlog_w, dlog_eps, dlog_rate, M);
+}
 
 extern "C" const char* ulm_last_error(void) { return g_error_msg; }
 

@@ -28,7 +28,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib as L
-from .block import addressed_memory, unified_block
+from .block import addressed_memory, block_scalars, unified_block
 from .head import lm_head_loss
 from .kernel import CHUNK
 from .norm import linear, rms_norm
@@ -106,7 +106,8 @@ class UnifiedBlock(nn.Module):
         return z / (self._eps() + z.sum(-1, keepdim=True))
 
     def forward(self, x):
-        w, g, eps = self._w(), self._g(), self._eps()
+        # the same values and gradients as _w(), _g(), _eps(), in one launch each way
+        w, eps, g = block_scalars(self.log_w, self.log_eps, self.log_rate)
         if self.dropout.p == 0.0 or not self.training:
             # norm, val, addressing, fast memory and combine as one op (v in bf16 with the
             # tensor-core products, as under the reference's bf16 autocast)
