@@ -7,9 +7,9 @@
 //   a = K u + bias, v = W_v h               batched GEMMs (gemm.cu: fp32 FMA or tcgen05 bf16)
 //   z = relu(a)^2, r = z / (eps + sum z)    decode_address_kernel
 //   c = lam c + (1-lam) w + r_prev, q = r/c decode_address_kernel
-//   U = lam U + (1-lam) mu w + v r_prev^T   decode_state_kernel (U read once, written once)
+//   r_prev <- r (the old r_prev to work)    decode_address_kernel
+//   U = lam U + (1-lam) mu w + v r_old^T    decode_state_kernel (U read once, written once)
 //   x += U q                                decode_state_kernel
-//   r_prev <- r                             copy_f32_kernel (after the state update has used r_prev)
 // The state U (B x D x M fp32 per block) is the only large traffic: 8 D M bytes per sequence per
 // block per token; every other tensor is O(B (D + M)) or a weight shared by the whole batch.
 //
@@ -79,11 +79,13 @@ __global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
   }
 }
 
-// r = relu(a + bias)^2 / (eps + sum), c = lam c + (1-lam) w + r_prev, q = r / c
+// r = relu(a + bias)^2 / (eps + sum), c = lam c + (1-lam) w + r_prev, q = r / c; then r_prev <- r,
+// the old r_prev going to r_old for the state update (each slot is read and written by one thread,
+// so the state needs no separate copy of r after its update)
 __global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
     decode_address_kernel(const float* __restrict__ a, const float* __restrict__ key_b, const float* __restrict__ w,
                           const float* __restrict__ lam_p, const float* __restrict__ eps_p, float* __restrict__ c,
-                          const float* __restrict__ r_prev, float* __restrict__ r_new, float* __restrict__ q, int M) {
+                          float* __restrict__ r_prev, float* __restrict__ r_old, float* __restrict__ q, int M) {
   pdl_enter();
   __shared__ float red[33];
   const int b = blockIdx.x;
@@ -93,18 +95,20 @@ __global__ void __launch_bounds__(DEC_ROW_MAX_THREADS)
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
     float z = a[o + m] + key_b[m];
     z = z > 0.f ? z * z : 0.f;
-    r_new[o + m] = z;
+    r_old[o + m] = z;  // z until the second loop
     zs += z;
   }
   zs = block_sum(zs, red);
   const float denom = eps + zs;
   const float one_minus = 1.0f - lam;
   for (int m = threadIdx.x; m < M; m += blockDim.x) {
-    const float r = r_new[o + m] / denom;
-    r_new[o + m] = r;
-    const float cc = __fadd_rn(__fadd_rn(__fmul_rn(lam, c[o + m]), __fmul_rn(one_minus, w[m])), r_prev[o + m]);
+    const float r = r_old[o + m] / denom;
+    const float rp = r_prev[o + m];
+    const float cc = __fadd_rn(__fadd_rn(__fmul_rn(lam, c[o + m]), __fmul_rn(one_minus, w[m])), rp);
     c[o + m] = cc;
     q[o + m] = r / cc;
+    r_old[o + m] = rp;
+    r_prev[o + m] = r;
   }
 }
 
@@ -203,12 +207,6 @@ __global__ void decode_reset_kernel(const float* __restrict__ mu, const float* _
     r_prev[i] = 0.f;
   }
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)B * D * kw; i += stride) buf[i] = 0.f;
-}
-
-__global__ void copy_f32_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t n) {
-  pdl_enter();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = src[i];
 }
 
 // final RMSNorm of the residual stream, fp32 and optional bf16 copy
@@ -847,7 +845,7 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = weight_dtype == ULM_BF16;
   const int64_t ldo = ulm_operand_ld(D);
-  // workspace: h, u, v (B x D fp32), a, r_new, q (B x M fp32), bf16 copies of h and u (B x ldo),
+  // workspace: h, u, v (B x D fp32), a, r_old, q (B x M fp32), bf16 copies of h and u (B x ldo),
   // each piece 256-byte aligned
   char* wp = static_cast<char*>(work);
   auto take = [&](int64_t bytes) {
@@ -859,7 +857,7 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   float* u = reinterpret_cast<float*>(take(B * D * 4));
   float* v = reinterpret_cast<float*>(take(B * D * 4));
   float* a = reinterpret_cast<float*>(take(B * M * 4));
-  float* r_new = reinterpret_cast<float*>(take(B * M * 4));
+  float* r_old = reinterpret_cast<float*>(take(B * M * 4));  // the step's incoming r_prev
   float* q = reinterpret_cast<float*>(take(B * M * 4));
   __nv_bfloat16* hop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
   __nv_bfloat16* uop = reinterpret_cast<__nv_bfloat16*>(take(B * ldo * 2));
@@ -889,7 +887,7 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
     }
   }
   if (int rc = launch_pdl(decode_address_kernel, dim3((unsigned)B), dim3(dec_row_threads(B)), 0, st, a, key_b, w, lam,
-                          eps, c, r_prev, r_new, q, (int)M))
+                          eps, c, r_prev, r_old, q, (int)M))
     return rc;
   const int warps = DEC_THREADS / 32;
   ULM_REQUIRE((B * D) % warps == 0, "B*D must be a multiple of %d", warps);
@@ -898,7 +896,7 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
   while (S < warps && B * D * S < 16 * 148 && (int64_t)S * 128 < M) S *= 2;
   const unsigned blocks = (unsigned)(B * D * S / warps);
   auto launch = [&](auto kern, const auto* pr) {
-    return launch_pdl(kern, dim3(blocks), dim3(DEC_THREADS), 0, st, U, pr, v, r_prev, q, lam, x, (int)D, (int)M);
+    return launch_pdl(kern, dim3(blocks), dim3(DEC_THREADS), 0, st, U, pr, v, r_old, q, lam, x, (int)D, (int)M);
   };
   const auto* pb = static_cast<const __nv_bfloat16*>(prior);
   const auto* pf = static_cast<const float*>(prior);
@@ -911,11 +909,7 @@ extern "C" int ulm_decode_block_step(float* x, const float* norm_w, const float*
     rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 4>, pb) : launch(decode_state_kernel<float, 4>, pf);
   else
     rc_state = bf ? launch(decode_state_kernel<__nv_bfloat16, 8>, pb) : launch(decode_state_kernel<float, 8>, pf);
-  if (rc_state) return rc_state;
-  if (int rc = launch_pdl(copy_f32_kernel, dim3((unsigned)std::min<int64_t>(cdiv(B * M, 256), 4 * 148)), dim3(256), 0,
-                          st, r_new, r_prev, B * M))
-    return rc;
-  return ULM_OK;
+  return rc_state;
 }
 
 extern "C" int64_t ulm_decode_block_work_bytes(int64_t B, int64_t D, int64_t M) {
