@@ -324,7 +324,7 @@ using namespace ulm;
 
 extern "C" int ulm_block_scalars_fwd(const float* log_w, const float* log_eps, const float* log_rate, float* w,
                                      float* eps, float* g, int64_t M, void* stream) {
-  ULM_REQUIRE(M >= 0 && M < (1ll << 40), "bad extent M=%lld", (long long)M);
+  ULM_REQUIRE(M >= 0 && M < (1ll << 31), "bad extent M=%lld", (long long)M);
   ULM_REQUIRE(log_eps && log_rate && eps && g && (M == 0 || (log_w && w)), "null pointer argument");
   const unsigned grid = (unsigned)(M > 0 ? cdiv(M, 256) : 1);
   return launch_pdl(block_scalars_fwd_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream), log_w,
@@ -334,7 +334,7 @@ extern "C" int ulm_block_scalars_fwd(const float* log_w, const float* log_eps, c
 extern "C" int ulm_block_scalars_bwd(const float* log_w, const float* log_eps, const float* w, const float* eps,
                                      const float* g, const float* dw, const float* deps, const float* dg,
                                      float* dlog_w, float* dlog_eps, float* dlog_rate, int64_t M, void* stream) {
-  ULM_REQUIRE(M >= 0 && M < (1ll << 40), "bad extent M=%lld", (long long)M);
+  ULM_REQUIRE(M >= 0 && M < (1ll << 31), "bad extent M=%lld", (long long)M);
   ULM_REQUIRE(log_eps && eps && g && deps && dg && dlog_eps && dlog_rate && (M == 0 || (log_w && w && dw && dlog_w)),
               "null pointer argument");
   const unsigned grid = (unsigned)(M > 0 ? cdiv(M, 256) : 1);
